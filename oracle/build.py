@@ -1,0 +1,33 @@
+"""Build recipe for the CPU oracle (test infrastructure).
+
+Compiles oracle/nsrl_oracle.cpp into oracle/liboracle.so with g++.  Only the
+tests, the smoke check and the CPU-baseline leg of bench.py load the result.
+"""
+import os
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+SRC = [os.path.join(HERE, "nsrl_oracle.cpp")]
+HDR = [os.path.join(HERE, "nsrl_oracle.hpp")]
+OUT = os.path.join(HERE, "liboracle.so")
+
+
+def needs_build() -> bool:
+    if not os.path.exists(OUT):
+        return True
+    t = os.path.getmtime(OUT)
+    return any(os.path.getmtime(p) > t for p in SRC + HDR)
+
+
+def build(force: bool = False) -> str:
+    if force or needs_build():
+        cmd = ["g++", "-std=c++17", "-O3", "-fPIC", "-shared", "-pthread", "-Wall",
+               "-o", OUT + ".tmp"] + SRC
+        subprocess.check_call(cmd)
+        os.replace(OUT + ".tmp", OUT)
+    return OUT
+
+
+if __name__ == "__main__":
+    print(build(force="--force" in sys.argv))
