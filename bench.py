@@ -1,0 +1,356 @@
+#!/usr/bin/env python3
+"""Benchmark of the NSRL integer transformer block on B200.
+
+Workload (per GPU): one prenorm causal attention + gated-MLP block forward,
+d_model 256, 4 heads x 64, MLP hidden 1024, seq 1024, batch 64 sequences
+(65,536 tokens), Q15 Gaussian sigma 4096 activations, i8 uniform weights.
+A step is one block forward over the batch; `value` is tokens/s over all
+ranks (weak scaling: every rank runs its own 64 sequences, no collective on
+the data path).  `e2e` is the same metric through the public C-ABI call with
+the input copied from pinned host memory and the output copied back inside
+the timed region.  The L2 is flushed (256 MiB memset) before every step.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+`--impl reference` times the CPU oracle (a C++ port of the reference's Rust
+kernels) on all host threads over a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+D_MODEL, HEADS, HIDDEN, SEQ, BATCH = 256, 4, 1024, 1024, 64
+HEAD_DIM = D_MODEL // HEADS
+TOKENS = BATCH * SEQ
+METRIC = "int attention-block tokens/s @1/2/4/8 B200, %INT8/HBM roofline, bit-exact"
+WORKLOAD = "prenorm causal attention + gated-MLP block forward, d256 h4x64 ff1024 s1024 b64/gpu"
+# dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant kernel,
+# from the ncu capture summarised in profiles/ (None until captured).
+NCU_TRAFFIC = {}
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        j = json.load(open(p))
+        return j["hbm_gbs"], j["bf16_tflops"], "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms while running."""
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), "--query-gpu=" + self.FIELDS,
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx.append(float(parts[1]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[3:7]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def make_block_inputs(rank: int):
+    """Block weights (shared seed) and this rank's input batch (rank-specific seed)."""
+    from nsrl_b200 import synth as Y
+    bw = Y.BlockWeights(seed=2024, d=D_MODEL, hidden=HIDDEN)
+    chunks = []
+    rows = BATCH * SEQ
+    step = 1 << 14
+    base = Y.tensor_seed(0xB200 + rank, 99)
+    for r0 in range(0, rows, step):
+        chunks.append(Y.q15_gaussian(Y.tensor_seed(base, r0), (min(step, rows - r0), D_MODEL)))
+    return bw, np.concatenate(chunks)
+
+
+def cpu_sample(bw, x, threads: int, sequences: int):
+    """Times the oracle block (attention + MLP) over `sequences` sequences; returns tokens/s."""
+    from oracle import oracle as O
+    L = {nm: O.Linear(getattr(bw, nm), O.scales(1, bw.shift[nm], bw.out_dim(nm)))
+         for nm in ("q", "k", "v", "o", "up", "gate", "down")}
+    xs = x[:sequences * SEQ]
+    t0 = time.perf_counter()
+    y1, _ = O.prenorm_attention_block(xs, sequences, SEQ, D_MODEL, HEADS, bw.attn_gamma, 1,
+                                      L["q"], L["k"], L["v"], L["o"], threads=threads)
+    O.prenorm_mlp_block(y1, sequences * SEQ, D_MODEL, HIDDEN, bw.mlp_gamma, 1, L["up"], L["gate"], L["down"],
+                        threads=threads)
+    dt = time.perf_counter() - t0
+    return sequences * SEQ / dt, dt
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from oracle import oracle as O
+    O.use_native()
+    threads = os.cpu_count() or 1
+    bw, x = make_block_inputs(0)
+    seqs = max(1, min(BATCH, threads))
+    for _ in range(args.warmup):
+        cpu_sample(bw, x, threads, seqs)
+    rates = []
+    t_total = 0.0
+    for _ in range(args.steps):
+        r, dt = cpu_sample(bw, x, threads, seqs)
+        rates.append(r)
+        t_total += dt
+    value = seqs * SEQ * args.steps / t_total
+    sample = f"{seqs} sequences x {SEQ} tokens per step ({threads} threads, one sequence per thread)"
+    out = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * t_total / args.steps,
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int16xint8->int32/int64",
+           "data": "synthetic (seeded SplitMix64)",
+           "config": {"workload": WORKLOAD, "d_model": D_MODEL, "heads": HEADS, "head_dim": HEAD_DIM,
+                      "hidden_dim": HIDDEN, "seq_len": SEQ, "batch_per_step": seqs},
+           "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
+           "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+    return 0
+
+
+def kernel_table(core_lib):
+    import ctypes as C
+    n = core_lib.nsrl_profile_count()
+    rows = {}
+    name = C.c_char_p()
+    ms, ops, byt = C.c_float(), C.c_double(), C.c_double()
+    core_lib.nsrl_profile_entry.argtypes = [C.c_size_t, C.POINTER(C.c_char_p), C.POINTER(C.c_float),
+                                            C.POINTER(C.c_double), C.POINTER(C.c_double)]
+    for i in range(n):
+        if core_lib.nsrl_profile_entry(i, C.byref(name), C.byref(ms), C.byref(ops), C.byref(byt)) != 0:
+            raise RuntimeError("profile read failed")
+        r = rows.setdefault(name.value.decode(), {"launches": 0, "ms": 0.0, "ops": 0.0, "bytes": 0.0})
+        r["launches"] += 1
+        r["ms"] += ms.value
+        r["ops"] += ops.value
+        r["bytes"] += byt.value
+    return n, rows
+
+
+TENSOR_KERNELS = ("linear_tc", "attention_prefill")
+
+
+def roofline(rows, hbm_gbs, tflops, src):
+    name = max(rows, key=lambda k: rows[k]["ms"])
+    r = rows[name]
+    per_launch_s = r["ms"] / 1000.0 / r["launches"]
+    if name.startswith(TENSOR_KERNELS):
+        ach = r["ops"] / r["launches"] / per_launch_s / 1e12
+        out = {"kernel": name, "bound": "tensor", "achieved": ach, "peak": tflops, "unit": "TFLOP/s",
+               "frac": ach / tflops,
+               "peak_note": f"{src} dense bf16 burst = nominal int8 dense / 2 = ceiling of an i16xi8 MAC split "
+                            "into two int8 MMAs; achieved counts algorithmic integer ops (2 per MAC)"}
+    else:
+        ach = r["bytes"] / r["launches"] / per_launch_s / 1e9
+        out = {"kernel": name, "bound": "hbm", "achieved": ach, "peak": hbm_gbs, "unit": "GB/s",
+               "frac": ach / hbm_gbs, "peak_note": f"{src} HBM copy bandwidth"}
+    out["traffic"] = NCU_TRAFFIC.get(name)
+    out["algorithmic_bytes_per_launch"] = r["bytes"] / r["launches"]
+    out["algorithmic_ops_per_launch"] = r["ops"] / r["launches"]
+    out["ms_per_launch"] = r["ms"] / r["launches"]
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+
+    from nsrl_b200 import build, core
+    build.build()
+    L = core.lib()
+    bw, x_np = make_block_inputs(rank)
+    lin = {nm: core.Linear(torch.from_numpy(getattr(bw, nm)),
+                           core.make_scales(1, bw.shift[nm], bw.out_dim(nm)))
+           for nm in ("q", "k", "v", "o", "up", "gate", "down")}
+    blk = core.TransformerBlock(D_MODEL, HEADS, HIDDEN, *[lin[n] for n in ("q", "k", "v", "o", "up", "gate", "down")],
+                                torch.from_numpy(bw.attn_gamma), torch.from_numpy(bw.mlp_gamma), 1)
+    x = torch.from_numpy(x_np).cuda()
+    y = torch.empty_like(x)
+    ws = core.workspace(blk.workspace_bytes(BATCH, SEQ))
+    st = core.Status()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def step():
+        r = blk.launch(x, y, BATCH, SEQ, ws, st)
+        if r != 0:
+            raise RuntimeError(f"block launch failed: {r} {L.nsrl_last_error()}")
+
+    st.reset()
+    for _ in range(args.warmup):
+        flush.zero_()
+        step()
+    code, hs = st.fetch()
+    if code != 0:
+        raise RuntimeError(f"block rejected during warm-up (flags {hs.flags:#x})")
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    L.nsrl_profile_reset()
+    L.nsrl_profile_enable(1)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    for i in range(args.steps):
+        flush.zero_()
+        starts[i].record(stream)
+        step()
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    L.nsrl_profile_enable(0)
+    if dist:
+        dist.barrier()
+    clk = clocks.stop()
+    elapsed_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    t = torch.tensor([elapsed_ms], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    elapsed_ms = float(t.item())
+    n_launches, rows = kernel_table(L)
+    code, hs = st.fetch()
+    if code != 0:
+        raise RuntimeError(f"block rejected in the timed region (flags {hs.flags:#x})")
+
+    # ---- end to end through the public call: pinned host in, host out ----
+    e2e_steps = max(3, min(args.steps, 20))
+    xh = torch.from_numpy(x_np).pin_memory()
+    yh = torch.empty_like(xh).pin_memory()
+    sh = torch.empty(8, dtype=torch.int64).pin_memory()
+    e_s = [torch.cuda.Event(enable_timing=True) for _ in range(e2e_steps)]
+    e_e = [torch.cuda.Event(enable_timing=True) for _ in range(e2e_steps)]
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for i in range(e2e_steps):
+        flush.zero_()
+        e_s[i].record(stream)
+        x.copy_(xh, non_blocking=True)
+        st.buf.zero_()
+        step()
+        yh.copy_(y, non_blocking=True)
+        sh.copy_(st.buf, non_blocking=True)
+        e_e[i].record(stream)
+        torch.cuda.synchronize()
+        if int(sh[0]) != 0:
+            raise RuntimeError("block rejected in the end-to-end loop")
+    e2e_ms = sum(s.elapsed_time(e) for s, e in zip(e_s, e_e))
+    t = torch.tensor([e2e_ms], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.barrier()
+    e2e_ms = float(t.item())
+
+    if rank == 0:
+        hbm, tfl, src = peaks()
+        value = world * TOKENS * args.steps / (elapsed_ms / 1000.0)
+        e2e_value = world * TOKENS * e2e_steps / (e2e_ms / 1000.0)
+        total_ms = sum(r["ms"] for r in rows.values())
+        kernels = {k: {"launches": v["launches"], "ms": round(v["ms"], 4), "share": round(v["ms"] / total_ms, 4)}
+                   for k, v in sorted(rows.items(), key=lambda kv: -kv[1]["ms"])}
+        out = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+               "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
+               "scaling": "weak", "vs_baseline": None, "dtype": "int16xint8->int32/int64",
+               "data": "synthetic (seeded SplitMix64: Irwin-Hall Q15 sigma 4096, uniform i8 weights)",
+               "config": {"workload": WORKLOAD, "d_model": D_MODEL, "heads": HEADS, "head_dim": HEAD_DIM,
+                          "hidden_dim": HIDDEN, "seq_len": SEQ, "batch_per_gpu": BATCH,
+                          "global_batch": BATCH * world, "parallelism": f"dp{world} (batch-sharded replicas)",
+                          "l2": "flushed before every step (256 MiB memset, outside the timed events)"},
+               "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": int(x.numel() * 2),
+                       "d2h_bytes_per_step": int(y.numel() * 2 + 64), "steps": e2e_steps},
+               "gpu_launches": n_launches,
+               "roofline": roofline(rows, hbm, tfl, src),
+               "kernels": kernels,
+               "clocks": clk}
+        if world == 1 and not args.no_cpu_baseline:
+            from oracle import oracle as O
+            O.use_native()
+            threads = os.cpu_count() or 1
+            seqs = max(1, min(BATCH, threads))
+            rate, dt = cpu_sample(bw, x_np, threads, seqs)
+            out["cpu_baseline"] = {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port",
+                                   "sample": f"{seqs} sequences x {SEQ} tokens of the same block "
+                                             f"({dt:.1f} s, one sequence per thread)"}
+        print(json.dumps(out), flush=True)
+    if dist:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

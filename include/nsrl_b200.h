@@ -1,0 +1,178 @@
+/*
+ * nsrl_b200.h -- C ABI of the B200-native (sm_100a) NSRL integer hot path.
+ *
+ * This is the drop-in boundary for the reference's nsrl-core kernel API
+ * (crates/nsrl-core/src/lib.rs:29-90): the same operations, batched over
+ * rows / sequences, on DEVICE buffers, with the reference's arithmetic
+ * bit for bit.  Plain pointers and sizes only; `stream` is a cudaStream_t
+ * (NULL = the legacy default stream).
+ *
+ * Conventions shared by every entry point:
+ *  - Tensors are row-major and token-major: activations [rows][dim] int16
+ *    (Q15), weights [output_dim][input_dim] int8, as in linear.rs:268-271.
+ *  - The reference returns `Option::None` both for a bad shape and for an
+ *    arithmetic rejection (an i32 prefix overflow in a linear, a logit outside
+ *    i32, an all-masked softmax row, an integer rsqrt of 0).  Here shape
+ *    errors are detected on the host before any launch and returned as
+ *    NSRL_INVALID_SHAPE; arithmetic rejections are detected on the device
+ *    and recorded in a caller-owned nsrl_device_status, which
+ *    nsrl_status_fetch() turns into NSRL_CORE_REJECTED for the whole call.
+ *    Outputs of a rejected call are unspecified, as with `None`.
+ *  - Calls are asynchronous on `stream` and allocate nothing: scratch memory
+ *    is a caller-owned workspace whose size the matching *_workspace_size()
+ *    function returns (the reference's caller-owned *Workspace structs,
+ *    e.g. attention.rs:29-36).  Calls are re-entrant per stream.
+ */
+#ifndef NSRL_B200_H
+#define NSRL_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum nsrl_status {
+  NSRL_OK = 0,
+  NSRL_INVALID_SHAPE = 1,  /* validation `None` (shape / parameter rules) */
+  NSRL_CORE_REJECTED = 2,  /* arithmetic `None` detected on the device */
+  NSRL_CUDA_ERROR = 3,     /* a CUDA runtime/driver call failed */
+  NSRL_COMM_TIMEOUT = 4,   /* reserved for the data-parallel exchange */
+} nsrl_status;
+
+/* FixedScale{multiplier, right_shift} (crates/nsrl-core/src/numeric.rs:1-5). */
+typedef struct nsrl_fixed_scale {
+  int32_t multiplier;
+  uint8_t right_shift;
+  uint8_t pad[3];
+} nsrl_fixed_scale;
+
+/* LinearI16I8Params (crates/nsrl-core/src/linear.rs:6-13); the struct lives
+ * in host memory, the arrays it points to in device memory. */
+typedef struct nsrl_linear_params {
+  const int8_t* weights;          /* [output_dim][input_dim] */
+  const int32_t* bias;            /* [output_dim] or NULL */
+  const nsrl_fixed_scale* scales; /* [output_dim] */
+  size_t input_dim;
+  size_t output_dim;
+} nsrl_linear_params;
+
+/* Device-resident status written by the kernels of a call.  Reset it with
+ * nsrl_status_reset() before a call (or a group of calls); read it with
+ * nsrl_status_fetch(). */
+typedef struct nsrl_device_status {
+  unsigned long long flags;                 /* nonzero = rejected; bits name the cause */
+  unsigned long long attention_saturations; /* residual_add saturation count, attention blocks */
+  unsigned long long mlp_saturations;       /* residual_add saturation count, MLP blocks */
+  unsigned long long reserved[5];
+} nsrl_device_status;
+
+/* Clears *status on `stream`. */
+nsrl_status nsrl_status_reset(nsrl_device_status* status, void* stream);
+
+/* Synchronises `stream`, copies *status to *host_out (may be NULL) and
+ * returns NSRL_CORE_REJECTED if any flag is set, else NSRL_OK. */
+nsrl_status nsrl_status_fetch(const nsrl_device_status* status, nsrl_device_status* host_out, void* stream);
+
+/* Text of the last host-side error on this thread ("" if none). */
+const char* nsrl_last_error(void);
+
+/* ---------------------------------------------------------------- linear --
+ * y[m] = linear_i16_i8_i16_per_channel_checked(x[m], params) for m < rows.
+ * Replaces crates/nsrl-core/src/linear.rs:115-126 (generic kernel
+ * :228-324; i32 accumulator semantics :144-173) batched over rows.
+ * x: [rows][input_dim] int16, y: [rows][output_dim] int16. */
+size_t nsrl_linear_workspace_size(size_t rows, size_t input_dim, size_t output_dim);
+nsrl_status nsrl_linear_i16_i8_i16(const int16_t* x, size_t rows, const nsrl_linear_params* params, int16_t* y,
+                                   void* workspace, size_t workspace_bytes, nsrl_device_status* status,
+                                   void* stream);
+
+/* --------------------------------------------------------------- rms norm --
+ * y[r] = rms_norm_i16_q15_checked(x[r], gamma, eps) for r < rows.
+ * Replaces crates/nsrl-core/src/rms_norm.rs:68-89 batched over rows. */
+nsrl_status nsrl_rms_norm_rows(const int16_t* x, size_t rows, size_t dim, const int16_t* gamma, uint64_t eps,
+                               int16_t* y, nsrl_device_status* status, void* stream);
+
+/* ------------------------------------------------------------- attention --
+ * Causal (or full) multi-head integer self-attention over `batch`
+ * independent sequences of seq_len tokens: x and out are [batch*seq_len][d].
+ * head_dim = d / heads must be a power of four (attention.rs:1599-1602).
+ * Replaces self_attention_i16_q15_checked (attention.rs:727-877), one
+ * sequence per reference call. */
+size_t nsrl_attention_workspace_size(size_t batch, size_t seq_len, size_t d_model, size_t heads);
+nsrl_status nsrl_self_attention(const int16_t* x, size_t batch, size_t seq_len, size_t d_model, size_t heads,
+                                int causal, const nsrl_linear_params* q, const nsrl_linear_params* k,
+                                const nsrl_linear_params* v, const nsrl_linear_params* o, int16_t* out,
+                                void* workspace, size_t workspace_bytes, nsrl_device_status* status,
+                                void* stream);
+
+/* y = x + self_attention(rms_norm(x)) with saturating Q15 residual; the
+ * residual saturation count is added to status->attention_saturations.
+ * Replaces prenorm_attention_residual_block_i16_q15_checked
+ * (attention.rs:1522-1583). */
+nsrl_status nsrl_prenorm_attention_residual_block(const int16_t* x, size_t batch, size_t seq_len, size_t d_model,
+                                                  size_t heads, int causal, const int16_t* rms_gamma,
+                                                  uint64_t rms_eps, const nsrl_linear_params* q,
+                                                  const nsrl_linear_params* k, const nsrl_linear_params* v,
+                                                  const nsrl_linear_params* o, int16_t* y, void* workspace,
+                                                  size_t workspace_bytes, nsrl_device_status* status,
+                                                  void* stream);
+
+/* ------------------------------------------------------------- gated MLP --
+ * y = x + down(gated(up(n), gate(n))), n = rms_norm(x), over `rows` tokens;
+ * residual saturations are added to status->mlp_saturations.
+ * Replaces prenorm_gated_mlp_residual_block_i16_q15_checked
+ * (crates/nsrl-core/src/mlp.rs:541-594). */
+size_t nsrl_mlp_workspace_size(size_t rows, size_t d_model, size_t hidden_dim);
+nsrl_status nsrl_prenorm_gated_mlp_residual_block(const int16_t* x, size_t rows, size_t d_model,
+                                                  size_t hidden_dim, const int16_t* rms_gamma, uint64_t rms_eps,
+                                                  const nsrl_linear_params* up, const nsrl_linear_params* gate,
+                                                  const nsrl_linear_params* down, int16_t* y, void* workspace,
+                                                  size_t workspace_bytes, nsrl_device_status* status,
+                                                  void* stream);
+
+/* ---------------------------------------------------- transformer block --
+ * The attention block followed by the MLP block with the same RMS gamma and
+ * eps -- the loop body of the reference's block benchmark
+ * (crates/nsrl-demo/src/bench.rs:288-343).  x and y may not alias. */
+size_t nsrl_transformer_block_workspace_size(size_t batch, size_t seq_len, size_t d_model, size_t heads,
+                                             size_t hidden_dim);
+nsrl_status nsrl_prenorm_transformer_block(const int16_t* x, size_t batch, size_t seq_len, size_t d_model,
+                                           size_t heads, size_t hidden_dim, const int16_t* attn_gamma,
+                                           const int16_t* mlp_gamma, uint64_t rms_eps,
+                                           const nsrl_linear_params* q, const nsrl_linear_params* k,
+                                           const nsrl_linear_params* v, const nsrl_linear_params* o,
+                                           const nsrl_linear_params* up, const nsrl_linear_params* gate,
+                                           const nsrl_linear_params* down, int16_t* y, void* workspace,
+                                           size_t workspace_bytes, nsrl_device_status* status, void* stream);
+
+/* ------------------------------------------------------ KV-cache decode --
+ * For each sequence b and head h, the single query q[b][h*hd:(h+1)*hd]
+ * attends over the first lens[b] cached keys/values of that head:
+ * ctx[b][h] = attention_row_i16_q15_checked(q, K[b][:lens[b]], V[b][:lens[b]])
+ * (crates/nsrl-core/src/attention.rs:671-725, no mask).
+ * q, ctx: [batch][heads*head_dim]; k_cache, v_cache: [batch][max_len][heads*head_dim];
+ * lens: [batch] int32 in (0, max_len] (device). */
+nsrl_status nsrl_attention_decode(const int16_t* q, const int16_t* k_cache, const int16_t* v_cache,
+                                  const int32_t* lens, size_t batch, size_t heads, size_t head_dim, size_t max_len,
+                                  int16_t* ctx, nsrl_device_status* status, void* stream);
+
+/* ------------------------------------------------------------ profiling --
+ * Per-launch CUDA-event timing of the library's own kernels (no counterpart
+ * in the reference, whose only timer is a wall clock around the block loop,
+ * crates/nsrl-demo/src/bench.rs:285).  While enabled, every kernel launch of
+ * the library is bracketed by two events on its stream and recorded with its
+ * algorithmic work (integer ops) and algorithmic HBM bytes.  Reading
+ * synchronises the device. */
+void nsrl_profile_enable(int enable);
+void nsrl_profile_reset(void);
+size_t nsrl_profile_count(void);
+/* Entry i: kernel name (static string), duration in ms, algorithmic ops and bytes. */
+nsrl_status nsrl_profile_entry(size_t i, const char** name, float* ms, double* ops, double* bytes);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NSRL_B200_H */

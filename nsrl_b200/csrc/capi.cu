@@ -1,0 +1,446 @@
+// C ABI of libnsrl_b200 (include/nsrl_b200.h): host-side validation with the
+// reference's shape rules, workspace carving, and the kernel sequence of each
+// operation.  No entry point allocates device memory.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace nsrl {
+
+static thread_local char g_err[512] = "";
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+}
+
+// Attention core over int16 operands (used when the tensor-core prefill
+// kernel does not take the head dim); defined in attention.cu.
+cudaError_t launch_attention_rows_i16(const int16_t* qkv, size_t B, size_t S, size_t d, size_t H, bool causal,
+                                      int16_t* ctx, nsrl_device_status* st, cudaStream_t stream);
+
+namespace {
+
+constexpr size_t ALIGN = 256;
+size_t up(size_t v) { return (v + ALIGN - 1) & ~(ALIGN - 1); }
+
+// Bump allocator over the caller's workspace.
+struct Carver {
+  uint8_t* base;
+  size_t off = 0;
+  explicit Carver(void* b) : base(static_cast<uint8_t*>(b)) {}
+  template <class T>
+  T* take(size_t count) {
+    T* p = base ? reinterpret_cast<T*>(base + off) : nullptr;
+    off += up(count * sizeof(T));
+    return p;
+  }
+  Planes planes(size_t rows, size_t ld, bool with_l1) {
+    Planes p;
+    p.hi = take<int8_t>(rows * ld);
+    p.lo = take<uint8_t>(rows * ld);
+    p.l1 = with_l1 ? take<unsigned long long>(rows) : nullptr;
+    p.ld = ld;
+    return p;
+  }
+};
+
+bool is_power_of_four(size_t v) { return v != 0 && (v & (v - 1)) == 0 && (__builtin_ctzll(v) % 2) == 0; }
+
+// linear.rs:56-78 (LinearI16I8Params::is_valid) with the expected dims.
+bool linear_ok(const nsrl_linear_params* p, size_t in, size_t out) {
+  return p && p->input_dim == in && p->output_dim == out && in != 0 && out != 0 && p->weights && p->scales;
+}
+
+WeightSeg seg_of(const nsrl_linear_params* p) { return WeightSeg{p->weights, p->bias, p->scales, p->output_dim}; }
+
+nsrl_status cuda_fail(cudaError_t e, const char* what) {
+  set_error("%s: %s", what, cudaGetErrorString(e));
+  return NSRL_CUDA_ERROR;
+}
+
+nsrl_status shape_fail(const char* what) {
+  set_error("invalid shape: %s", what);
+  return NSRL_INVALID_SHAPE;
+}
+
+#define NSRL_TRY(call, what)                  \
+  do {                                        \
+    cudaError_t _e = (call);                  \
+    if (_e != cudaSuccess) return cuda_fail(_e, what); \
+  } while (0)
+
+bool attention_prefill_native(size_t d, size_t H, size_t S) {
+  const size_t hd = d / H;
+  return (hd == 64 || hd == 16) && S <= 32768;
+}
+
+// ---- attention workspace: xn planes + l1, qkv planes, ctx planes + l1 [, int16 fallback buffers]
+size_t attention_ws(size_t B, size_t S, size_t d, size_t H, Carver* c = nullptr) {
+  Carver local(nullptr);
+  Carver& k = c ? *c : local;
+  const size_t T = B * S;
+  const size_t start = k.off;
+  k.planes(T, d, true);
+  k.planes(T, 3 * d, false);
+  k.planes(T, d, true);
+  if (!attention_prefill_native(d, H, S)) {
+    k.take<int16_t>(T * 3 * d);
+    k.take<int16_t>(T * d);
+  }
+  return k.off - start;
+}
+
+size_t mlp_ws(size_t T, size_t d, size_t F, Carver* c = nullptr) {
+  Carver local(nullptr);
+  Carver& k = c ? *c : local;
+  const size_t start = k.off;
+  k.planes(T, d, true);
+  k.planes(T, F, true);
+  return k.off - start;
+}
+
+// Attention core: (normalised or raw) input planes -> q|k|v -> ctx -> O linear.
+nsrl_status attention_core(const Planes& xin, size_t B, size_t S, size_t d, size_t H, bool causal,
+                           const nsrl_linear_params* q, const nsrl_linear_params* k, const nsrl_linear_params* v,
+                           const nsrl_linear_params* o, Planes qkv, Planes ctx, int16_t* qkv16, int16_t* ctx16,
+                           Epi out_epi, const int16_t* skip, int16_t* out, unsigned long long* sat,
+                           nsrl_device_status* st, cudaStream_t stream) {
+  const size_t T = B * S;
+  GemmArgs g{};
+  g.a_hi = xin.hi;
+  g.a_lo = xin.lo;
+  g.a_l1 = xin.l1;
+  g.lda = xin.ld;
+  g.M = T;
+  g.K = d;
+  g.nseg = 3;
+  g.seg[0] = seg_of(q);
+  g.seg[1] = seg_of(k);
+  g.seg[2] = seg_of(v);
+  g.epi = Epi::PLANES;
+  g.yp = qkv;
+  g.st = st;
+  NSRL_TRY(launch_gemm(g, stream), "qkv projection");
+
+  NSRL_TRY(cudaMemsetAsync(ctx.l1, 0, T * sizeof(unsigned long long), stream), "memset");
+  if (attention_prefill_native(d, H, S)) {
+    NSRL_TRY(launch_attention(qkv, B, S, d, H, causal, ctx, st, stream), "attention");
+  } else {
+    NSRL_TRY(launch_join_planes(qkv, T, 3 * d, qkv16, 3 * d, stream), "join planes");
+    NSRL_TRY(launch_attention_rows_i16(qkv16, B, S, d, H, causal, ctx16, st, stream), "attention rows");
+    NSRL_TRY(launch_split_planes(ctx16, T, d, d, ctx, stream), "split planes");
+  }
+
+  GemmArgs og{};
+  og.a_hi = ctx.hi;
+  og.a_lo = ctx.lo;
+  og.a_l1 = ctx.l1;
+  og.lda = ctx.ld;
+  og.M = T;
+  og.K = d;
+  og.nseg = 1;
+  og.seg[0] = seg_of(o);
+  og.epi = out_epi;
+  og.y = out;
+  og.ldy = d;
+  og.skip = skip;
+  og.ldskip = d;
+  og.sat_counter = sat;
+  og.st = st;
+  NSRL_TRY(launch_gemm(og, stream), "output projection");
+  return NSRL_OK;
+}
+
+nsrl_status validate_attention(size_t S, size_t d, size_t H, const nsrl_linear_params* q,
+                               const nsrl_linear_params* k, const nsrl_linear_params* v,
+                               const nsrl_linear_params* o) {
+  // attention.rs:1585-1634
+  if (S == 0 || d == 0 || H == 0) return shape_fail("seq_len, d_model and heads must be nonzero");
+  if (d % H != 0) return shape_fail("d_model must be a multiple of heads");
+  if (!is_power_of_four(d / H)) return shape_fail("head_dim must be a power of four");
+  if (!linear_ok(q, d, d) || !linear_ok(k, d, d) || !linear_ok(v, d, d) || !linear_ok(o, d, d))
+    return shape_fail("q/k/v/o must be d_model x d_model linears");
+  if (d > (size_t)INT32_MAX / 3 || S > (size_t)INT32_MAX) return shape_fail("dimension too large");
+  return NSRL_OK;
+}
+
+nsrl_status validate_mlp(size_t T, size_t d, size_t F, const nsrl_linear_params* upp,
+                         const nsrl_linear_params* gatep, const nsrl_linear_params* downp) {
+  // mlp.rs:108-122 (GatedMlpI16Params::is_valid)
+  if (T == 0 || d == 0 || F == 0) return shape_fail("seq_len, d_model and hidden_dim must be nonzero");
+  if (!linear_ok(upp, d, F) || !linear_ok(gatep, d, F) || !linear_ok(downp, F, d))
+    return shape_fail("up/gate must be d_model -> hidden, down hidden -> d_model");
+  return NSRL_OK;
+}
+
+nsrl_status mlp_block(const int16_t* x, size_t T, size_t d, size_t F, const int16_t* gamma, uint64_t eps,
+                      const nsrl_linear_params* upp, const nsrl_linear_params* gatep,
+                      const nsrl_linear_params* downp, int16_t* y, Carver& c, nsrl_device_status* st,
+                      cudaStream_t stream) {
+  Planes xn = c.planes(T, d, true);
+  Planes gated = c.planes(T, F, true);
+  NSRL_TRY(launch_rms_norm(x, T, d, gamma, eps, nullptr, xn, st, stream), "rms norm");
+  NSRL_TRY(cudaMemsetAsync(gated.l1, 0, T * sizeof(unsigned long long), stream), "memset");
+  GemmArgs g{};
+  g.a_hi = xn.hi;
+  g.a_lo = xn.lo;
+  g.a_l1 = xn.l1;
+  g.lda = d;
+  g.M = T;
+  g.K = d;
+  g.nseg = 2;
+  g.seg[0] = seg_of(upp);
+  g.seg[1] = seg_of(gatep);
+  g.epi = Epi::GATED;
+  g.yp = gated;
+  g.st = st;
+  NSRL_TRY(launch_gemm(g, stream), "up/gate projection");
+  GemmArgs dg{};
+  dg.a_hi = gated.hi;
+  dg.a_lo = gated.lo;
+  dg.a_l1 = gated.l1;
+  dg.lda = F;
+  dg.M = T;
+  dg.K = F;
+  dg.nseg = 1;
+  dg.seg[0] = seg_of(downp);
+  dg.epi = Epi::RESID;
+  dg.y = y;
+  dg.ldy = d;
+  dg.skip = x;
+  dg.ldskip = d;
+  dg.sat_counter = &st->mlp_saturations;
+  dg.st = st;
+  NSRL_TRY(launch_gemm(dg, stream), "down projection");
+  return NSRL_OK;
+}
+
+nsrl_status attention_block(const int16_t* x, size_t B, size_t S, size_t d, size_t H, bool causal,
+                            const int16_t* gamma, uint64_t eps, const nsrl_linear_params* q,
+                            const nsrl_linear_params* k, const nsrl_linear_params* v, const nsrl_linear_params* o,
+                            int16_t* y, Carver& c, nsrl_device_status* st, cudaStream_t stream) {
+  const size_t T = B * S;
+  Planes xn = c.planes(T, d, true);
+  Planes qkv = c.planes(T, 3 * d, false);
+  Planes ctx = c.planes(T, d, true);
+  int16_t *qkv16 = nullptr, *ctx16 = nullptr;
+  if (!attention_prefill_native(d, H, S)) {
+    qkv16 = c.take<int16_t>(T * 3 * d);
+    ctx16 = c.take<int16_t>(T * d);
+  }
+  NSRL_TRY(launch_rms_norm(x, T, d, gamma, eps, nullptr, xn, st, stream), "rms norm");
+  return attention_core(xn, B, S, d, H, causal, q, k, v, o, qkv, ctx, qkv16, ctx16, Epi::RESID, x, y,
+                        &st->attention_saturations, st, stream);
+}
+
+}  // namespace
+}  // namespace nsrl
+
+using namespace nsrl;
+
+extern "C" {
+
+const char* nsrl_last_error(void) { return g_err; }
+
+nsrl_status nsrl_status_reset(nsrl_device_status* status, void* stream) {
+  if (!status) return shape_fail("status is NULL");
+  NSRL_TRY(cudaMemsetAsync(status, 0, sizeof(nsrl_device_status), (cudaStream_t)stream), "status reset");
+  return NSRL_OK;
+}
+
+nsrl_status nsrl_status_fetch(const nsrl_device_status* status, nsrl_device_status* host_out, void* stream) {
+  if (!status) return shape_fail("status is NULL");
+  nsrl_device_status h;
+  NSRL_TRY(cudaMemcpyAsync(&h, status, sizeof(h), cudaMemcpyDeviceToHost, (cudaStream_t)stream), "status fetch");
+  NSRL_TRY(cudaStreamSynchronize((cudaStream_t)stream), "status fetch");
+  if (host_out) *host_out = h;
+  if (h.flags) {
+    set_error("core rejected (flags 0x%llx)", h.flags);
+    return NSRL_CORE_REJECTED;
+  }
+  return NSRL_OK;
+}
+
+size_t nsrl_linear_workspace_size(size_t rows, size_t input_dim, size_t output_dim) {
+  (void)output_dim;
+  Carver c(nullptr);
+  c.planes(rows, input_dim, true);
+  return c.off;
+}
+
+nsrl_status nsrl_linear_i16_i8_i16(const int16_t* x, size_t rows, const nsrl_linear_params* params, int16_t* y,
+                                   void* workspace, size_t workspace_bytes, nsrl_device_status* status,
+                                   void* stream) {
+  if (!params || params->input_dim == 0 || params->output_dim == 0 || !params->weights || !params->scales)
+    return shape_fail("linear params");
+  if (!status) return shape_fail("status is NULL");
+  if (rows == 0) return NSRL_OK;
+  if (!x || !y) return shape_fail("x / y is NULL");
+  const size_t K = params->input_dim, N = params->output_dim;
+  if (K > (size_t)INT32_MAX || N > (size_t)INT32_MAX || rows > (size_t)INT32_MAX)
+    return shape_fail("dimension too large");
+  if (workspace_bytes < nsrl_linear_workspace_size(rows, K, N) || !workspace) return shape_fail("workspace too small");
+  cudaStream_t s = (cudaStream_t)stream;
+  Carver c(workspace);
+  Planes xp = c.planes(rows, K, true);
+  NSRL_TRY(launch_split_planes(x, rows, K, K, xp, s), "split planes");
+  GemmArgs g{};
+  g.a_hi = xp.hi;
+  g.a_lo = xp.lo;
+  g.a_l1 = xp.l1;
+  g.lda = K;
+  g.M = rows;
+  g.K = K;
+  g.nseg = 1;
+  g.seg[0] = seg_of(params);
+  g.epi = Epi::I16;
+  g.y = y;
+  g.ldy = N;
+  g.st = status;
+  NSRL_TRY(launch_gemm(g, s), "linear");
+  return NSRL_OK;
+}
+
+nsrl_status nsrl_rms_norm_rows(const int16_t* x, size_t rows, size_t dim, const int16_t* gamma, uint64_t eps,
+                               int16_t* y, nsrl_device_status* status, void* stream) {
+  if (dim == 0) return shape_fail("rms norm dim is zero");  // rms_norm.rs:74-76
+  if (!status || !gamma) return shape_fail("status / gamma is NULL");
+  if (rows == 0) return NSRL_OK;
+  Planes none{nullptr, nullptr, nullptr, 0};
+  NSRL_TRY(launch_rms_norm(x, rows, dim, gamma, eps, y, none, status, (cudaStream_t)stream), "rms norm");
+  return NSRL_OK;
+}
+
+size_t nsrl_attention_workspace_size(size_t batch, size_t seq_len, size_t d_model, size_t heads) {
+  if (heads == 0) return 0;
+  return attention_ws(batch, seq_len, d_model, heads);
+}
+
+nsrl_status nsrl_self_attention(const int16_t* x, size_t batch, size_t seq_len, size_t d_model, size_t heads,
+                                int causal, const nsrl_linear_params* q, const nsrl_linear_params* k,
+                                const nsrl_linear_params* v, const nsrl_linear_params* o, int16_t* out,
+                                void* workspace, size_t workspace_bytes, nsrl_device_status* status,
+                                void* stream) {
+  nsrl_status r = validate_attention(seq_len, d_model, heads, q, k, v, o);
+  if (r != NSRL_OK) return r;
+  if (!status) return shape_fail("status is NULL");
+  if (batch == 0) return NSRL_OK;
+  if (!workspace || workspace_bytes < attention_ws(batch, seq_len, d_model, heads))
+    return shape_fail("workspace too small");
+  cudaStream_t s = (cudaStream_t)stream;
+  const size_t T = batch * seq_len;
+  Carver c(workspace);
+  Planes xp = c.planes(T, d_model, true);
+  Planes qkv = c.planes(T, 3 * d_model, false);
+  Planes ctx = c.planes(T, d_model, true);
+  int16_t *qkv16 = nullptr, *ctx16 = nullptr;
+  if (!attention_prefill_native(d_model, heads, seq_len)) {
+    qkv16 = c.take<int16_t>(T * 3 * d_model);
+    ctx16 = c.take<int16_t>(T * d_model);
+  }
+  NSRL_TRY(launch_split_planes(x, T, d_model, d_model, xp, s), "split planes");
+  return attention_core(xp, batch, seq_len, d_model, heads, causal != 0, q, k, v, o, qkv, ctx, qkv16, ctx16,
+                        Epi::I16, nullptr, out, nullptr, status, s);
+}
+
+nsrl_status nsrl_prenorm_attention_residual_block(const int16_t* x, size_t batch, size_t seq_len, size_t d_model,
+                                                  size_t heads, int causal, const int16_t* rms_gamma,
+                                                  uint64_t rms_eps, const nsrl_linear_params* q,
+                                                  const nsrl_linear_params* k, const nsrl_linear_params* v,
+                                                  const nsrl_linear_params* o, int16_t* y, void* workspace,
+                                                  size_t workspace_bytes, nsrl_device_status* status,
+                                                  void* stream) {
+  nsrl_status r = validate_attention(seq_len, d_model, heads, q, k, v, o);
+  if (r != NSRL_OK) return r;
+  if (!status || !rms_gamma) return shape_fail("status / gamma is NULL");
+  if (batch == 0) return NSRL_OK;
+  if (!workspace || workspace_bytes < attention_ws(batch, seq_len, d_model, heads))
+    return shape_fail("workspace too small");
+  Carver c(workspace);
+  return attention_block(x, batch, seq_len, d_model, heads, causal != 0, rms_gamma, rms_eps, q, k, v, o, y, c,
+                         status, (cudaStream_t)stream);
+}
+
+size_t nsrl_mlp_workspace_size(size_t rows, size_t d_model, size_t hidden_dim) {
+  return mlp_ws(rows, d_model, hidden_dim);
+}
+
+nsrl_status nsrl_prenorm_gated_mlp_residual_block(const int16_t* x, size_t rows, size_t d_model,
+                                                  size_t hidden_dim, const int16_t* rms_gamma, uint64_t rms_eps,
+                                                  const nsrl_linear_params* up, const nsrl_linear_params* gate,
+                                                  const nsrl_linear_params* down, int16_t* y, void* workspace,
+                                                  size_t workspace_bytes, nsrl_device_status* status,
+                                                  void* stream) {
+  nsrl_status r = validate_mlp(rows, d_model, hidden_dim, up, gate, down);
+  if (r != NSRL_OK) return r;
+  if (!status || !rms_gamma) return shape_fail("status / gamma is NULL");
+  if (!workspace || workspace_bytes < mlp_ws(rows, d_model, hidden_dim)) return shape_fail("workspace too small");
+  Carver c(workspace);
+  return mlp_block(x, rows, d_model, hidden_dim, rms_gamma, rms_eps, up, gate, down, y, c, status,
+                   (cudaStream_t)stream);
+}
+
+size_t nsrl_transformer_block_workspace_size(size_t batch, size_t seq_len, size_t d_model, size_t heads,
+                                             size_t hidden_dim) {
+  if (heads == 0) return 0;
+  const size_t T = batch * seq_len;
+  size_t a = attention_ws(batch, seq_len, d_model, heads);
+  size_t m = mlp_ws(T, d_model, hidden_dim);
+  return up(T * d_model * sizeof(int16_t)) + (a > m ? a : m);
+}
+
+nsrl_status nsrl_prenorm_transformer_block(const int16_t* x, size_t batch, size_t seq_len, size_t d_model,
+                                           size_t heads, size_t hidden_dim, const int16_t* attn_gamma,
+                                           const int16_t* mlp_gamma, uint64_t rms_eps,
+                                           const nsrl_linear_params* q, const nsrl_linear_params* k,
+                                           const nsrl_linear_params* v, const nsrl_linear_params* o,
+                                           const nsrl_linear_params* up_p, const nsrl_linear_params* gate,
+                                           const nsrl_linear_params* down, int16_t* y, void* workspace,
+                                           size_t workspace_bytes, nsrl_device_status* status, void* stream) {
+  nsrl_status r = validate_attention(seq_len, d_model, heads, q, k, v, o);
+  if (r != NSRL_OK) return r;
+  r = validate_mlp(seq_len, d_model, hidden_dim, up_p, gate, down);
+  if (r != NSRL_OK) return r;
+  if (!status || !attn_gamma || !mlp_gamma) return shape_fail("status / gamma is NULL");
+  if (batch == 0) return NSRL_OK;
+  if (x == y) return shape_fail("x and y may not alias");
+  if (!workspace ||
+      workspace_bytes < nsrl_transformer_block_workspace_size(batch, seq_len, d_model, heads, hidden_dim))
+    return shape_fail("workspace too small");
+  const size_t T = batch * seq_len;
+  cudaStream_t s = (cudaStream_t)stream;
+  Carver c(workspace);
+  int16_t* h = c.take<int16_t>(T * d_model);
+  const size_t mark = c.off;
+  r = attention_block(x, batch, seq_len, d_model, heads, true, attn_gamma, rms_eps, q, k, v, o, h, c, status, s);
+  if (r != NSRL_OK) return r;
+  c.off = mark;  // the MLP block reuses the attention scratch
+  return mlp_block(h, T, d_model, hidden_dim, mlp_gamma, rms_eps, up_p, gate, down, y, c, status, s);
+}
+
+nsrl_status nsrl_attention_decode(const int16_t* q, const int16_t* k_cache, const int16_t* v_cache,
+                                  const int32_t* lens, size_t batch, size_t heads, size_t head_dim, size_t max_len,
+                                  int16_t* ctx, nsrl_device_status* status, void* stream) {
+  // attention.rs:682-708
+  if (heads == 0 || head_dim == 0 || max_len == 0) return shape_fail("heads, head_dim and max_len must be nonzero");
+  if (!is_power_of_four(head_dim)) return shape_fail("head_dim must be a power of four");
+  if (!status || !lens) return shape_fail("status / lens is NULL");
+  if (max_len > 50000) return shape_fail("max_len above the shared-memory logit buffer (50000)");
+  if (batch == 0) return NSRL_OK;
+  const size_t d = heads * head_dim;
+  const bool vec = head_dim >= 8 && (reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k_cache) |
+                                     reinterpret_cast<uintptr_t>(v_cache)) % 16 == 0 && d % 8 == 0;
+  if (!vec && head_dim >= 8) return shape_fail("q / cache pointers must be 16-byte aligned");
+  NSRL_TRY(launch_decode_attention(q, k_cache, v_cache, lens, batch, heads, head_dim, max_len, ctx, status,
+                                   (cudaStream_t)stream),
+           "decode attention");
+  return NSRL_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,240 @@
+// Shared device code for the NSRL integer hot path on B200 (sm_100a):
+// the integer numeric rules of the reference's nsrl-core, the device status
+// word, and thin inline-PTX wrappers for mbarrier, TMA and tcgen05.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/nsrl_b200.h"
+#include "nsrl_luts.h"
+
+// Device copies of the three integer tables (one per translation unit).
+static __device__ const int16_t d_rsqrt_lut[128] = {NSRL_RSQRT_LUT_VALUES};
+static __device__ const int16_t d_exp2_lut[256] = {NSRL_EXP2_LUT_VALUES};
+static __device__ const uint32_t d_recip_lut[128] = {NSRL_RECIP_LUT_VALUES};
+#define NSRL_RECIP_LUT_DEV(i) d_recip_lut[(i)]
+
+// ----------------------------------------------------------------------------
+// Status word.  Kernels never trap: a condition under which the reference
+// returns `None` sets a bit in nsrl_device_status.flags (atomicOr) and the
+// host reports NSRL_CORE_REJECTED for the whole call.
+// ----------------------------------------------------------------------------
+#define NSRL_FLAG_LINEAR_OVERFLOW 0x1ull   // an i32 prefix of a linear dot overflowed
+#define NSRL_FLAG_LOGIT_RANGE 0x2ull       // (q.k) >> shift left the i32 range
+#define NSRL_FLAG_ALL_MASKED 0x4ull        // a softmax row had no unmasked logit
+#define NSRL_FLAG_RMS_ZERO 0x8ull          // mean square + eps == 0 (integer rsqrt of 0)
+#define NSRL_FLAG_BAD_LENGTH 0x10ull       // a KV-cache length outside (0, Lmax]
+#define NSRL_FLAG_WAIT_TIMEOUT 0x100ull    // a bounded device wait gave up (internal error)
+
+__device__ __forceinline__ void nsrl_flag(nsrl_device_status* st, unsigned long long bits) {
+  atomicOr(reinterpret_cast<unsigned long long*>(&st->flags), bits);
+}
+
+// ----------------------------------------------------------------------------
+// Integer numerics (crates/nsrl-core/src/numeric.rs).
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ int16_t sat_i16(long long v) {
+  return (int16_t)(v < -32768 ? -32768 : (v > 32767 ? 32767 : v));
+}
+__device__ __forceinline__ int8_t sat_i8(long long v) {
+  return (int8_t)(v < -128 ? -128 : (v > 127 ? 127 : v));
+}
+__device__ __forceinline__ int16_t sat_i16_i32(int v) { return (int16_t)max(-32768, min(32767, v)); }
+
+// numeric.rs:47-57: (v saturating+ 2^(s-1)) >> s, s clamped to 62, s = 0 is identity.
+__device__ __forceinline__ long long rhu64(long long v, uint32_t s) {
+  if (s == 0) return v;
+  s = s > 62 ? 62 : s;
+  long long bias = 1ll << (s - 1);
+  long long r = (v > LLONG_MAX - bias) ? LLONG_MAX : v + bias;
+  return r >> s;
+}
+
+// numeric.rs:59-70: identity scale saturates; otherwise i64 multiply, rhu, saturate.
+__device__ __forceinline__ int16_t requant_i32(int acc, int mult, uint32_t shift) {
+  if (mult == 1 && shift == 0) return sat_i16_i32(acc);
+  return sat_i16(rhu64((long long)acc * (long long)mult, shift));
+}
+
+// mlp.rs:150-170: hard-SiLU gate and the gated activation.
+__device__ __forceinline__ int16_t gated_act(int16_t up, int16_t gate) {
+  int g = ((int)gate >> 2) + 16384;
+  g = max(0, min(32767, g));
+  int16_t silu = sat_i16(rhu64((long long)gate * g, 15));
+  return sat_i16(rhu64((long long)up * silu, 15));
+}
+
+// attention.rs:142-158 with the table in shared memory.
+__device__ __forceinline__ int exp2_neg_q15(const int16_t* lut, long long delta) {
+  if (delta >= 0) return 32767;
+  long long mag = -delta;
+  long long ish = mag >> 8;
+  if (ish >= 15) return 0;
+  return (int)lut[mag & 255] >> (int)ish;
+}
+
+// lut.rs:16-40 + attention.rs:181-193: Q31 reciprocal of a positive sum.
+__device__ __forceinline__ uint32_t recip_sum_q31(unsigned long long sum) {
+  int msb = 63 - __clzll((long long)sum);
+  unsigned long long base;
+  if (msb >= 7) {
+    int sh = msb - 7;
+    uint32_t mant = (uint32_t)(sum >> sh) & 255u;
+    base = NSRL_RECIP_LUT_DEV(mant - 128);
+    base = sh >= 63 ? 0ull : (base >> sh);
+  } else {
+    int sh = 7 - msb;
+    uint32_t mant = (uint32_t)(sum << sh) & 255u;
+    base = NSRL_RECIP_LUT_DEV(mant - 128);
+    base = base << sh;
+  }
+  return (uint32_t)(base > 0xFFFFFFFFull ? 0xFFFFFFFFull : base);
+}
+
+// ----------------------------------------------------------------------------
+// Small PTX helpers.
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Every wait is bounded in time: after NSRL_WAIT_NS nanoseconds the waiter
+// records NSRL_FLAG_WAIT_TIMEOUT and returns false so that the kernel can
+// unwind (the host then reports the call as failed).
+#define NSRL_WAIT_NS 2000000000ull
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, nsrl_device_status* st) {
+  const unsigned long long t0 = global_ns();
+  for (uint32_t i = 0;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 255u && global_ns() - t0 > NSRL_WAIT_NS) {
+      nsrl_flag(st, NSRL_FLAG_WAIT_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+// True once any bounded wait of the call has timed out (read by one thread,
+// broadcast by the caller); later CTAs then skip their work.
+__device__ __forceinline__ bool timed_out(const nsrl_device_status* st) {
+  return (*reinterpret_cast<const volatile unsigned long long*>(&st->flags) & NSRL_FLAG_WAIT_TIMEOUT) != 0;
+}
+
+// 2-D tiled TMA load (no multicast) into shared memory, completing on `bar`.
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int c0,
+                                            int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// ---- tcgen05 ----------------------------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot_smem)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::i8, s32 accumulate.
+__device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive once on `bar` when all previously issued tcgen05.mma of this thread complete.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// 32 lanes x 32 consecutive 32-bit columns: thread i of the warp gets lane
+// (base lane + i), columns [col, col + 32).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor for a K-major operand tile stored with the
+// 128-byte swizzle (rows of 128 bytes, 8-row atoms of 1024 bytes, tile base
+// 1024-byte aligned).  SBO = 1024 B between 8-row groups; LBO is unused for
+// swizzled K-major layouts; version field = 1 (sm_100).
+__device__ __forceinline__ uint64_t sdesc_k128(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor: kind::i8, D = s32, K-major A and B, shape M x N.
+// a_signed / b_signed select s8 (1) or u8 (0) per operand.
+__host__ __device__ constexpr uint32_t idesc_i8(uint32_t M, uint32_t N, uint32_t a_signed, uint32_t b_signed) {
+  return (2u << 4) | (a_signed << 7) | (b_signed << 10) | ((N >> 3) << 17) | ((M >> 4) << 24);
+}
+
+// Byte offset of element (row r, byte c) in a 128-byte-swizzled tile whose
+// base is 1024-byte aligned (the layout TMA writes with SWIZZLE_128B).
+__device__ __forceinline__ uint32_t swz128(uint32_t r, uint32_t c) {
+  return r * 128u + ((((c >> 4) ^ (r & 7u)) << 4) | (c & 15u));
+}

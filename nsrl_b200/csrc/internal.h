@@ -1,0 +1,101 @@
+// Host-side declarations shared by the translation units of libnsrl_b200.
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/nsrl_b200.h"
+
+namespace nsrl {
+
+// An activation tensor [rows][ld] stored as two byte planes: hi = x >> 8
+// (int8) and lo = x & 255 (uint8), so that x = 256 * hi + lo.  Tensor-core
+// kernels consume and produce activations in this form; `l1` (optional,
+// [rows] uint64) receives sum_k |x[row][k]| for the i32 prefix bound.
+struct Planes {
+  int8_t* hi;
+  uint8_t* lo;
+  unsigned long long* l1;
+  size_t ld;
+};
+
+// One weight matrix [rows][K] with its bias / scales (device pointers).
+struct WeightSeg {
+  const int8_t* w;
+  const int32_t* bias;
+  const nsrl_fixed_scale* scales;
+  size_t rows;
+};
+
+enum class Epi : int {
+  I16 = 0,     // y = requant(acc) as int16
+  PLANES = 1,  // y = requant(acc) as byte planes (+ row L1)
+  RESID = 2,   // y = skip (+sat) requant(acc) as int16, saturations counted
+  GATED = 3,   // y = gated_act(requant(up), requant(gate)) as byte planes (+ row L1)
+};
+
+struct GemmArgs {
+  const int8_t* a_hi;
+  const uint8_t* a_lo;
+  const unsigned long long* a_l1;  // row L1 of A (needed when the i32 prefix bound can fail)
+  size_t lda;
+  size_t M, K;
+  int nseg;  // 1 = plain, 3 = concatenated along N (Q|K|V), 2 = gated (up, gate)
+  WeightSeg seg[3];
+  Epi epi;
+  int16_t* y;
+  size_t ldy;
+  Planes yp;
+  const int16_t* skip;
+  size_t ldskip;
+  unsigned long long* sat_counter;
+  nsrl_device_status* st;
+};
+
+// Launches the linear on `stream` (tcgen05 path when the shape allows TMA,
+// SIMT otherwise), then the exact i32-prefix check where the bound requires it.
+cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t stream);
+
+// x [rows][K] int16 -> planes (+ row L1).
+cudaError_t launch_split_planes(const int16_t* x, size_t rows, size_t K, size_t ldx, Planes out,
+                                cudaStream_t stream);
+
+// RMS norm rows; writes int16 output and/or planes (+ row L1).
+cudaError_t launch_rms_norm(const int16_t* x, size_t rows, size_t d, const int16_t* gamma, uint64_t eps,
+                            int16_t* y_i16, Planes y_planes, nsrl_device_status* st, cudaStream_t stream);
+
+// Causal / full self-attention core on projected q|k|v planes [B*S][3d]
+// (q at column 0, k at d, v at 2d); writes ctx planes [B*S][d] (+ row L1,
+// which must be zeroed by the caller).
+cudaError_t launch_attention(const Planes& qkv, size_t B, size_t S, size_t d, size_t H, bool causal, Planes ctx,
+                             nsrl_device_status* st, cudaStream_t stream);
+
+// KV-cache decode attention (int16 operands).
+cudaError_t launch_decode_attention(const int16_t* q, const int16_t* kc, const int16_t* vc, const int32_t* lens,
+                                    size_t B, size_t H, size_t hd, size_t Lmax, int16_t* ctx,
+                                    nsrl_device_status* st, cudaStream_t stream);
+
+// Planes -> int16.
+cudaError_t launch_join_planes(Planes in, size_t rows, size_t cols, int16_t* y, size_t ldy, cudaStream_t stream);
+
+// While nsrl_profile_enable(1) is in force, brackets the kernel launched in
+// its scope with CUDA events on `s` and records the launch with its
+// algorithmic integer ops and HBM bytes.
+class ProfScope {
+ public:
+  ProfScope(const char* name, cudaStream_t s, double ops, double bytes);
+  ~ProfScope();
+  ProfScope(const ProfScope&) = delete;
+  ProfScope& operator=(const ProfScope&) = delete;
+
+ private:
+  const char* name_;
+  cudaStream_t stream_;
+  double ops_, bytes_;
+  cudaEvent_t ev_;
+};
+
+void set_error(const char* fmt, ...);
+bool tma_supported();
+
+}  // namespace nsrl

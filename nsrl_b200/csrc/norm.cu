@@ -1,0 +1,122 @@
+// Integer RMS norm rows (crates/nsrl-core/src/rms_norm.rs:12-89).
+//
+// One warp per row: sum of squares in u64, mean = floor(sum / d) + eps,
+// inverse RMS in Q30 from the 8-bit rsqrt table with the odd-exponent
+// 1/sqrt(2) correction (rms_norm.rs:47-66), then y = sat(rhu(x * g * inv, 30)).
+// |x * g| <= 2^30 and inv < 2^30, so the i64 product of rms_norm.rs:84 never
+// overflows and needs no check.  The output is written as int16 and/or as
+// byte planes with the row's L1 norm (the operand format of the tensor-core
+// linears).
+#include "common.cuh"
+#include "internal.h"
+
+namespace nsrl {
+namespace {
+
+// rms_norm.rs:47-66 for value > 0.  The normalised exponent + 7 equals the
+// index of the most significant bit, so the shift is always to the right.
+__device__ __forceinline__ long long rsqrt_q30(unsigned long long v) {
+  const int msb = 63 - __clzll((long long)v);
+  const uint32_t mant = msb >= 7 ? (uint32_t)(v >> (msb - 7)) : (uint32_t)(v << (7 - msb));
+  long long inv = (long long)d_rsqrt_lut[(mant & 255u) - 128] << 15;
+  if (msb & 1) inv = rhu64(inv * 23170ll, 15);
+  const int half = msb / 2;
+  return half >= 63 ? 0 : (inv >> half);
+}
+
+template <bool VEC>
+__global__ void rms_norm_kernel(const int16_t* __restrict__ x, long long rows, int d, const int16_t* __restrict__ g,
+                                unsigned long long eps, int16_t* __restrict__ y, int8_t* __restrict__ yh,
+                                uint8_t* __restrict__ yl, unsigned long long* __restrict__ yl1, long long ldp,
+                                nsrl_device_status* st) {
+  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+  for (long long r = (long long)blockIdx.x * warps + (threadIdx.x >> 5); r < rows; r += (long long)gridDim.x * warps) {
+    const int16_t* xr = x + r * d;
+    unsigned long long ss = 0;
+    if (VEC) {
+      for (int k8 = lane; k8 < d / 8; k8 += 32) {
+        uint4 v = reinterpret_cast<const uint4*>(xr)[k8];
+        const int16_t* e = reinterpret_cast<const int16_t*>(&v);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ss += (unsigned long long)((int)e[j] * (int)e[j]);
+      }
+    } else {
+      for (int k = lane; k < d; k += 32) ss += (unsigned long long)((int)xr[k] * (int)xr[k]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const unsigned long long mean = ss / (unsigned long long)d;
+    const unsigned long long v = mean + eps;
+    long long inv = 0;
+    if (v < mean || v == 0) {  // u64 overflow of mean + eps, or rsqrt(0): the reference returns None
+      if (lane == 0) nsrl_flag(st, NSRL_FLAG_RMS_ZERO);
+    } else {
+      inv = rsqrt_q30(v);
+    }
+    unsigned long long l1 = 0;
+    if (VEC) {
+      for (int k8 = lane; k8 < d / 8; k8 += 32) {
+        uint4 xv = reinterpret_cast<const uint4*>(xr)[k8];
+        uint4 gv = reinterpret_cast<const uint4*>(g)[k8];
+        const int16_t* xe = reinterpret_cast<const int16_t*>(&xv);
+        const int16_t* ge = reinterpret_cast<const int16_t*>(&gv);
+        int16_t out[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          out[j] = sat_i16(rhu64((long long)((int)xe[j] * (int)ge[j]) * inv, 30));
+          l1 += (unsigned long long)abs((int)out[j]);
+        }
+        if (y) reinterpret_cast<uint4*>(y + r * d)[k8] = *reinterpret_cast<uint4*>(out);
+        if (yh) {
+          uint32_t h0 = 0, h1 = 0, l0 = 0, l1w = 0;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            h0 |= (uint32_t)((out[j] >> 8) & 255) << (8 * j);
+            l0 |= (uint32_t)(out[j] & 255) << (8 * j);
+            h1 |= (uint32_t)((out[4 + j] >> 8) & 255) << (8 * j);
+            l1w |= (uint32_t)(out[4 + j] & 255) << (8 * j);
+          }
+          reinterpret_cast<uint2*>(yh + r * ldp)[k8] = make_uint2(h0, h1);
+          reinterpret_cast<uint2*>(yl + r * ldp)[k8] = make_uint2(l0, l1w);
+        }
+      }
+    } else {
+      for (int k = lane; k < d; k += 32) {
+        int16_t o = sat_i16(rhu64((long long)((int)xr[k] * (int)g[k]) * inv, 30));
+        l1 += (unsigned long long)abs((int)o);
+        if (y) y[r * d + k] = o;
+        if (yh) {
+          yh[r * ldp + k] = (int8_t)(o >> 8);
+          yl[r * ldp + k] = (uint8_t)(o & 255);
+        }
+      }
+    }
+    if (yl1) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+      if (lane == 0) yl1[r] = l1;
+    }
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_rms_norm(const int16_t* x, size_t rows, size_t d, const int16_t* gamma, uint64_t eps,
+                            int16_t* y_i16, Planes yp, nsrl_device_status* st, cudaStream_t stream) {
+  if (rows == 0) return cudaSuccess;
+  const unsigned blocks = (unsigned)std::min<size_t>((rows + 7) / 8, 148 * 16);
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  const bool vec = d % 8 == 0 && al16(x) && al16(gamma) && (!y_i16 || al16(y_i16)) &&
+                   (!yp.hi || ((reinterpret_cast<uintptr_t>(yp.hi) | reinterpret_cast<uintptr_t>(yp.lo)) % 8 == 0 &&
+                               yp.ld % 8 == 0));
+  ProfScope prof("rms_norm", stream, 0.0, 4.0 * rows * d + (yp.l1 ? 8.0 * rows : 0.0));
+  if (vec)
+    rms_norm_kernel<true><<<blocks, 256, 0, stream>>>(x, (long long)rows, (int)d, gamma, eps, y_i16, yp.hi, yp.lo,
+                                                      yp.l1, (long long)yp.ld, st);
+  else
+    rms_norm_kernel<false><<<blocks, 256, 0, stream>>>(x, (long long)rows, (int)d, gamma, eps, y_i16, yp.hi, yp.lo,
+                                                       yp.l1, (long long)yp.ld, st);
+  return cudaGetLastError();
+}
+
+}  // namespace nsrl

@@ -31,3 +31,19 @@ def build(force: bool = False) -> str:
 
 if __name__ == "__main__":
     print(build(force="--force" in sys.argv))
+
+
+NATIVE_OUT = os.path.join(HERE, "liboracle_native.so")
+
+
+def build_native() -> str:
+    """Same sources with -march=native for timing the CPU baseline on the host it runs on."""
+    if not os.path.exists(NATIVE_OUT) or os.path.getmtime(NATIVE_OUT) < max(os.path.getmtime(p) for p in SRC + HDR):
+        cmd = ["g++", "-std=c++17", "-O3", "-march=native", "-fPIC", "-shared", "-pthread",
+               "-o", NATIVE_OUT + ".tmp"] + SRC
+        try:
+            subprocess.check_call(cmd)
+        except (subprocess.CalledProcessError, OSError):
+            return build()
+        os.replace(NATIVE_OUT + ".tmp", NATIVE_OUT)
+    return NATIVE_OUT

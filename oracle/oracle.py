@@ -43,10 +43,19 @@ def scales(mult, shift, n=None):
     return a
 
 
+def use_native():
+    """Load the -march=native build (CPU-baseline timing); call before the first lib()."""
+    global _native
+    _native = True
+
+
+_native = False
+
+
 def lib():
     global _lib
     if _lib is None:
-        path = _build.build()
+        path = _build.build_native() if _native else _build.build()
         _lib = C.CDLL(path)
         _lib.orc_init()
         _lib.orc_rhu.restype = C.c_int64

@@ -1,0 +1,81 @@
+"""CPU-side checks of the C ABI: the library builds, loads without a GPU and
+exports every entry point include/nsrl_b200.h declares; host-side shape
+validation answers like the reference's `None` without touching a device."""
+import ctypes as C
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "nsrl_b200.h")
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from nsrl_b200 import build
+    path = build.build()
+    return C.CDLL(path)
+
+
+def declared():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:[\w\s\*]+?)\b(nsrl_[a-z0-9_]+)\s*\(", text, re.M)))
+
+
+def test_header_declares_entry_points():
+    names = declared()
+    for n in ("nsrl_linear_i16_i8_i16", "nsrl_rms_norm_rows", "nsrl_self_attention",
+              "nsrl_prenorm_attention_residual_block", "nsrl_prenorm_gated_mlp_residual_block",
+              "nsrl_prenorm_transformer_block", "nsrl_attention_decode", "nsrl_status_fetch"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol(lib):
+    missing = [n for n in declared() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_workspace_sizes_are_consistent(lib):
+    lib.nsrl_linear_workspace_size.restype = C.c_size_t
+    lib.nsrl_linear_workspace_size.argtypes = [C.c_size_t] * 3
+    lib.nsrl_transformer_block_workspace_size.restype = C.c_size_t
+    lib.nsrl_transformer_block_workspace_size.argtypes = [C.c_size_t] * 5
+    lib.nsrl_attention_workspace_size.restype = C.c_size_t
+    lib.nsrl_attention_workspace_size.argtypes = [C.c_size_t] * 4
+    # planes (2 bytes / element) + 8 bytes of row L1, each 256-byte aligned
+    assert lib.nsrl_linear_workspace_size(4096, 1024, 1024) == 2 * 4096 * 1024 + 4096 * 8
+    T, d, H, F = 64 * 1024, 256, 4, 1024
+    a = lib.nsrl_attention_workspace_size(64, 1024, d, H)
+    assert a == T * d * 2 + T * 8 + T * 3 * d * 2 + T * d * 2 + T * 8
+    assert lib.nsrl_transformer_block_workspace_size(64, 1024, d, H, F) >= a + T * d * 2
+
+
+class LinearParamsC(C.Structure):
+    _fields_ = [("weights", C.c_void_p), ("bias", C.c_void_p), ("scales", C.c_void_p),
+                ("input_dim", C.c_size_t), ("output_dim", C.c_size_t)]
+
+
+def test_shape_validation_matches_reference_none(lib):
+    """Shape errors are caught on the host (NSRL_INVALID_SHAPE = 1) before any launch."""
+    f = lib.nsrl_self_attention
+    lp = C.POINTER(LinearParamsC)
+    f.argtypes = [C.c_void_p, C.c_size_t, C.c_size_t, C.c_size_t, C.c_size_t, C.c_int, lp, lp, lp, lp, C.c_void_p,
+                  C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p]
+    dummy = C.c_void_p(16)
+    good = LinearParamsC(16, None, 16, 128, 128)
+    # head_dim 32 (128 / 4) is not a power of four: attention.rs:1599-1602
+    r = f(dummy, 1, 8, 128, 4, 1, C.byref(good), C.byref(good), C.byref(good), C.byref(good), dummy, dummy, 1 << 30,
+          dummy, None)
+    assert r == 1
+    # seq_len 0: attention.rs:1591-1593
+    r = f(dummy, 1, 0, 128, 2, 1, C.byref(good), C.byref(good), C.byref(good), C.byref(good), dummy, dummy, 1 << 30,
+          dummy, None)
+    assert r == 1
+    # q with the wrong output dim
+    bad = LinearParamsC(16, None, 16, 128, 64)
+    r = f(dummy, 1, 8, 128, 2, 1, C.byref(bad), C.byref(good), C.byref(good), C.byref(good), dummy, dummy, 1 << 30,
+          dummy, None)
+    assert r == 1
+    lib.nsrl_last_error.restype = C.c_char_p
+    assert b"invalid shape" in lib.nsrl_last_error()
