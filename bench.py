@@ -110,7 +110,7 @@ def make_block_inputs(rank: int):
     bw = Y.BlockWeights(seed=2024, d=D_MODEL, hidden=HIDDEN)
     chunks = []
     rows = BATCH * SEQ
-    step = 1 << 14
+    step = 1 << 12
     base = Y.tensor_seed(0xB200 + rank, 99)
     for r0 in range(0, rows, step):
         chunks.append(Y.q15_gaussian(Y.tensor_seed(base, r0), (min(step, rows - r0), D_MODEL)))

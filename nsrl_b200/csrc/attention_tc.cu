@@ -1,0 +1,458 @@
+// Integer causal self-attention on the B200 tensor cores (tcgen05, kind::i8),
+// head_dim 64.
+//
+// Reference: crates/nsrl-core/src/attention.rs:742-877 (full attention),
+// :261-293 (base-2 softmax), :117-140 (QK dot), :596-668 (AV).
+//
+// One CTA per (128-query tile, head, sequence); 10 warps:
+//   warp 0      TMA producer: Q planes once, then per 64-key tile the K planes
+//               (and in the last pass the transposed V planes)
+//   warp 1      TMEM allocator + single-thread MMA issuer
+//   warps 2..9  softmax: warp w owns query rows 32*(w%4) .. +31 (its TMEM lane
+//               quarter) and key columns [32*c, 32*c+32) of each key tile,
+//               c = (w-2)/4
+// q.k = 65536*(qh.kh) + 256*(qh.kl + ql.kh) + ql.kl: each S tile (128 x 64)
+// is three s32 TMEM accumulators (hh, mid, ll), recombined in i64 by the
+// softmax warps.  The probabilities are rounded to Q15 with the reciprocal of
+// the complete row sum before the AV product (attention.rs:285-290), so the
+// keys are swept three times: row max, row sum, then P and O = P V.  P is
+// written to shared memory as byte planes (ph <= 127, pl) in the MMA's
+// K-major layout; O = P V uses three more s32 accumulators (65536*hh +
+// 256*mid + ll), exact for up to 16384 keys.
+//
+// TMEM (512 columns): S hh/mid/ll at [0,192), O hh/mid/ll at [256,448).
+// Operand tiles use the 64-byte swizzle (rows of 64 bytes), as TMA writes it.
+#include "common.cuh"
+#include "internal.h"
+
+namespace nsrl {
+namespace {
+
+constexpr int QT = 128, KT = 64, HD = 64;
+constexpr int ST = 4;                 // K / V^T stage ring
+constexpr int PLANE_Q = QT * HD;      // 8 KB per plane
+constexpr int PLANE_K = KT * HD;      // 4 KB
+constexpr int PLANE_V = HD * KT;      // 4 KB
+constexpr int STAGE_BYTES = 2 * PLANE_K + 2 * PLANE_V;
+constexpr int PLANE_P = QT * KT;      // 8 KB
+constexpr int SOFTMAX_WARPS = 8;
+constexpr int THREADS = 64 + 32 * SOFTMAX_WARPS;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t S_HH = 0, S_MID = 64, S_LL = 128, O_HH = 256, O_MID = 320, O_LL = 384;
+
+constexpr int OFF_Q = 0;
+constexpr int OFF_STAGE = OFF_Q + 2 * PLANE_Q;
+constexpr int OFF_P = OFF_STAGE + ST * STAGE_BYTES;
+constexpr int OFF_X = OFF_P + 2 * 2 * PLANE_P;  // row-statistics exchange
+constexpr int X_BYTES = 2 * QT * 8 * 3;
+constexpr int OFF_LUT = OFF_X + X_BYTES;
+constexpr int OFF_BAR = OFF_LUT + 512;
+constexpr size_t SMEM_BYTES = OFF_BAR + 256 + 1024;
+
+struct Maps {
+  CUtensorMap q_hi, q_lo, k_hi, k_lo, vt_hi, vt_lo;  // q: 128-row boxes, k: 64-row boxes
+};
+
+struct Args {
+  int S, d, H, causal, shift;
+  int8_t* ctx_hi;
+  uint8_t* ctx_lo;
+  unsigned long long* ctx_l1;
+  long long ldc;
+  nsrl_device_status* st;
+};
+
+// Shared-memory descriptor, K-major, 64-byte swizzle: 8-row atoms of 512 B.
+__device__ __forceinline__ uint64_t sdesc_k64(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(512 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)4 << 61);
+}
+
+// Byte offset of 16-byte chunk c (0..3) of row r in a 64-byte-swizzled tile.
+__device__ __forceinline__ uint32_t swz64_chunk(uint32_t r, uint32_t c) { return r * 64u + ((c ^ ((r >> 1) & 3u)) << 4); }
+
+struct Ctl {
+  uint64_t q_full, full[ST], empty[ST], s_full, s_empty, p_full[2], p_empty[2], o_full;
+  uint32_t tslot, abort;
+};
+
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, Ctl* c, nsrl_device_status* st) {
+  if (*reinterpret_cast<volatile uint32_t*>(&c->abort)) return false;
+  if (mbar_wait(bar, parity, st)) return true;
+  *reinterpret_cast<volatile uint32_t*>(&c->abort) = 1u;
+  return false;
+}
+
+__device__ __forceinline__ void named_sync_softmax() { asm volatile("bar.sync 1, %0;" ::"n"(32 * SOFTMAX_WARPS)); }
+
+__global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_constant__ Maps maps, const Args a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Ctl* ctl = reinterpret_cast<Ctl*>(sm + OFF_BAR);
+  int16_t* lut = reinterpret_cast<int16_t*>(sm + OFF_LUT);
+  long long* xmax = reinterpret_cast<long long*>(sm + OFF_X);  // [2][QT]
+  long long* xmin = xmax + 2 * QT;                             // [2][QT]
+  unsigned long long* xsum = reinterpret_cast<unsigned long long*>(xmin + 2 * QT);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q0 = blockIdx.x * QT, h = blockIdx.y, b = blockIdx.z;
+  const int S = a.S;
+  const int kend = a.causal ? min(S, q0 + QT) : S;
+  const int ntiles = (kend + KT - 1) / KT;
+
+  if (threadIdx.x == 0) ctl->abort = timed_out(a.st) ? 1u : 0u;
+  for (int i = threadIdx.x; i < 256; i += THREADS) lut[i] = d_exp2_lut[i];
+  __syncthreads();
+  if (ctl->abort) return;
+
+  if (warp == 0 && lane == 0) {
+    mbar_init(&ctl->q_full, 1);
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(&ctl->full[s], 1);
+      mbar_init(&ctl->empty[s], 1);
+    }
+    mbar_init(&ctl->s_full, 1);
+    mbar_init(&ctl->s_empty, SOFTMAX_WARPS);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&ctl->p_full[i], SOFTMAX_WARPS);
+      mbar_init(&ctl->p_empty[i], 1);
+    }
+    mbar_init(&ctl->o_full, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&ctl->tslot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl->tslot;
+  const int row0 = b * S;  // first token row of this sequence
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&ctl->q_full, 2 * PLANE_Q);
+      tma_load_2d(sm + OFF_Q, &maps.q_hi, &ctl->q_full, h * HD, row0 + q0);
+      tma_load_2d(sm + OFF_Q + PLANE_Q, &maps.q_lo, &ctl->q_full, h * HD, row0 + q0);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int pass = 0; pass < 3 && ok; ++pass) {
+        for (int j = 0; j < ntiles; ++j, ++it) {
+          const int s = it % ST;
+          if (it >= ST && !wait_bar(&ctl->empty[s], ((it / ST) - 1) & 1, ctl, a.st)) {
+            ok = false;
+            break;
+          }
+          uint8_t* stg = sm + OFF_STAGE + s * STAGE_BYTES;
+          mbar_arrive_expect_tx(&ctl->full[s], pass == 2 ? STAGE_BYTES : 2 * PLANE_K);
+          tma_load_2d(stg, &maps.k_hi, &ctl->full[s], a.d + h * HD, row0 + j * KT);
+          tma_load_2d(stg + PLANE_K, &maps.k_lo, &ctl->full[s], a.d + h * HD, row0 + j * KT);
+          if (pass == 2) {
+            const int vrow = (b * a.H + h) * HD;
+            tma_load_2d(stg + 2 * PLANE_K, &maps.vt_hi, &ctl->full[s], j * KT, vrow);
+            tma_load_2d(stg + 2 * PLANE_K + PLANE_V, &maps.vt_lo, &ctl->full[s], j * KT, vrow);
+          }
+        }
+      }
+      mbar_wait(&ctl->q_full, 0, a.st);
+      for (uint32_t k = (it > ST ? it - ST : 0); k < it; ++k) mbar_wait(&ctl->full[k % ST], (k / ST) & 1, a.st);
+    }
+  } else if (warp == 1) {
+    // ----------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t id_ss = idesc_i8(QT, KT, 1, 1), id_su = idesc_i8(QT, KT, 1, 0);
+      const uint32_t id_us = idesc_i8(QT, KT, 0, 1), id_uu = idesc_i8(QT, KT, 0, 0);
+      const uint32_t qh = smem_u32(sm + OFF_Q), ql = qh + PLANE_Q;
+      uint32_t u = 0;  // uses of the S accumulators
+      wait_bar(&ctl->q_full, 0, ctl, a.st);
+      auto issue_s = [&](int s) {
+        if (u > 0) wait_bar(&ctl->s_empty, (u - 1) & 1, ctl, a.st);
+        tc_fence_after();
+        const uint32_t kh = smem_u32(sm + OFF_STAGE + s * STAGE_BYTES), kl = kh + PLANE_K;
+#pragma unroll
+        for (int ks = 0; ks < HD / 32; ++ks) {
+          const uint64_t aqh = sdesc_k64(qh + 32 * ks), aql = sdesc_k64(ql + 32 * ks);
+          const uint64_t bkh = sdesc_k64(kh + 32 * ks), bkl = sdesc_k64(kl + 32 * ks);
+          const uint32_t acc = ks > 0 ? 1u : 0u;
+          umma_i8(tmem + S_HH, aqh, bkh, id_ss, acc);
+          umma_i8(tmem + S_MID, aqh, bkl, id_su, acc);
+          umma_i8(tmem + S_MID, aql, bkh, id_us, 1u);
+          umma_i8(tmem + S_LL, aql, bkl, id_uu, acc);
+        }
+        umma_commit(&ctl->s_full);
+        ++u;
+      };
+      uint32_t it = 0;
+      for (int pass = 0; pass < 2; ++pass) {
+        for (int j = 0; j < ntiles; ++j, ++it) {
+          const int s = it % ST;
+          wait_bar(&ctl->full[s], (it / ST) & 1, ctl, a.st);
+          issue_s(s);
+          umma_commit(&ctl->empty[s]);
+        }
+      }
+      // pass 2: S(j+1) is issued before O += P(j) V(j) so that the softmax
+      // warps can work on tile j+1 while the tensor core does the AV product.
+      const uint32_t base = it;
+      wait_bar(&ctl->full[base % ST], (base / ST) & 1, ctl, a.st);
+      issue_s(base % ST);
+      for (int j = 0; j < ntiles; ++j) {
+        if (j + 1 < ntiles) {
+          const uint32_t n1 = base + j + 1;
+          wait_bar(&ctl->full[n1 % ST], (n1 / ST) & 1, ctl, a.st);
+          issue_s(n1 % ST);
+        }
+        const int pb = j & 1;
+        wait_bar(&ctl->p_full[pb], (j >> 1) & 1, ctl, a.st);
+        tc_fence_after();
+        const uint32_t s = (base + j) % ST;
+        const uint32_t vh = smem_u32(sm + OFF_STAGE + s * STAGE_BYTES + 2 * PLANE_K), vl = vh + PLANE_V;
+        const uint32_t ph = smem_u32(sm + OFF_P + pb * 2 * PLANE_P), pl = ph + PLANE_P;
+#pragma unroll
+        for (int ks = 0; ks < KT / 32; ++ks) {
+          const uint64_t aph = sdesc_k64(ph + 32 * ks), apl = sdesc_k64(pl + 32 * ks);
+          const uint64_t bvh = sdesc_k64(vh + 32 * ks), bvl = sdesc_k64(vl + 32 * ks);
+          const uint32_t acc = (j > 0 || ks > 0) ? 1u : 0u;
+          umma_i8(tmem + O_HH, aph, bvh, id_us, acc);
+          umma_i8(tmem + O_MID, aph, bvl, id_uu, acc);
+          umma_i8(tmem + O_MID, apl, bvh, id_us, 1u);
+          umma_i8(tmem + O_LL, apl, bvl, id_uu, acc);
+        }
+        umma_commit(&ctl->p_empty[pb]);
+        umma_commit(&ctl->empty[s]);
+      }
+      umma_commit(&ctl->o_full);
+      // every MMA of this CTA completes before TMEM is released
+      mbar_wait(&ctl->o_full, 0, a.st);
+    }
+  } else {
+    // -------------------------------------------------------------- softmax
+    const int q = warp & 3, ch = (warp - 2) >> 2;
+    const int row = q * 32 + lane;
+    const int qi = q0 + row;
+    const bool row_live = qi < S;
+    const int last_key = row_live ? (a.causal ? min(qi, S - 1) : S - 1) : -1;
+    const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16);
+    const int shift = a.shift;
+    long long rawmax = LLONG_MIN, rawmin = LLONG_MAX;
+    long long lgmax = 0;
+    unsigned long long rsum = 0;
+    uint32_t inv = 0;
+    uint32_t u = 0;
+    bool range_bad = false, masked_bad = false;
+    for (int pass = 0; pass < 3; ++pass) {
+      for (int j = 0; j < ntiles; ++j, ++u) {
+        uint32_t hh[32], mid[32], ll[32];
+        wait_bar(&ctl->s_full, u & 1, ctl, a.st);
+        tc_fence_after();
+        tmem_ld32(trow + S_HH + 32 * ch, hh);
+        tmem_ld32(trow + S_MID + 32 * ch, mid);
+        tmem_ld32(trow + S_LL + 32 * ch, ll);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ctl->s_empty);
+        const int key0 = j * KT + 32 * ch;
+        const int nlive = max(0, min(32, last_key - key0 + 1));
+        if (pass == 0) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            if (i < nlive) {
+              const long long raw =
+                  (long long)(int)hh[i] * 65536 + (long long)(int)mid[i] * 256 + (long long)(int)ll[i];
+              rawmax = max(rawmax, raw);
+              rawmin = min(rawmin, raw);
+            }
+          }
+        } else {
+          uint32_t pw[16];
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            int w2[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              int w = 0;
+              if (i + e < nlive) {
+                const long long raw = (long long)(int)hh[i + e] * 65536 + (long long)(int)mid[i + e] * 256 +
+                                      (long long)(int)ll[i + e];
+                const long long lg = raw >> shift;
+                const long long delta = lg - lgmax;  // <= 0
+                if (delta > -15 * 256 && lg != (long long)INT_MIN) {
+                  const int mag = (int)(-delta);
+                  w = (int)lut[mag & 255] >> (mag >> 8);
+                }
+              }
+              w2[e] = w;
+            }
+            if (pass == 1) {
+              rsum += (unsigned)(w2[0] + w2[1]);
+            } else {
+              // p = sat_i16(rhu(w * inv, 16)); w * inv < 2^47
+              const int p0 = (int)min(32767ull, ((unsigned long long)w2[0] * inv + 32768ull) >> 16);
+              const int p1 = (int)min(32767ull, ((unsigned long long)w2[1] * inv + 32768ull) >> 16);
+              pw[i / 2] = (uint32_t)p0 | ((uint32_t)p1 << 16);
+            }
+          }
+          if (pass == 2) {
+            const int pb = j & 1;
+            if (j >= 2) wait_bar(&ctl->p_empty[pb], ((j >> 1) - 1) & 1, ctl, a.st);
+            uint8_t* ph = sm + OFF_P + pb * 2 * PLANE_P;
+            uint8_t* pl = ph + PLANE_P;
+#pragma unroll
+            for (int c2 = 0; c2 < 2; ++c2) {
+              uint32_t hw[4], lw[4];
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const uint32_t x0 = pw[8 * c2 + 2 * k], x1 = pw[8 * c2 + 2 * k + 1];
+                hw[k] = __byte_perm(x0, x1, 0x7531);
+                lw[k] = __byte_perm(x0, x1, 0x6420);
+              }
+              const uint32_t off = swz64_chunk((uint32_t)row, (uint32_t)(2 * ch + c2));
+              *reinterpret_cast<uint4*>(ph + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+              *reinterpret_cast<uint4*>(pl + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&ctl->p_full[pb]);
+          }
+        }
+      }
+      if (pass == 0) {
+        xmax[ch * QT + row] = rawmax;
+        xmin[ch * QT + row] = rawmin;
+        named_sync_softmax();
+        rawmax = max(rawmax, xmax[(1 - ch) * QT + row]);
+        rawmin = min(rawmin, xmin[(1 - ch) * QT + row]);
+        if (row_live) {
+          lgmax = rawmax >> shift;
+          const long long lgmin = rawmin >> shift;
+          if (lgmax > INT_MAX || lgmin < INT_MIN) range_bad = true;
+          if (lgmax <= (long long)INT_MIN) masked_bad = true;  // every live logit masked or out of range
+        }
+      } else if (pass == 1) {
+        xsum[ch * QT + row] = rsum;
+        named_sync_softmax();
+        rsum += xsum[(1 - ch) * QT + row];
+        inv = (row_live && rsum) ? recip_sum_q31(rsum) : 0u;
+      }
+    }
+    if (range_bad) nsrl_flag(a.st, NSRL_FLAG_LOGIT_RANGE);
+    if (masked_bad) nsrl_flag(a.st, NSRL_FLAG_ALL_MASKED);
+    // ---- context: sat(rhu(65536*hh + 256*mid + ll, 15)) as byte planes ----
+    wait_bar(&ctl->o_full, 0, ctl, a.st);
+    tc_fence_after();
+    uint32_t oh[32], om[32], ol[32];
+    tmem_ld32(trow + O_HH + 32 * ch, oh);
+    tmem_ld32(trow + O_MID + 32 * ch, om);
+    tmem_ld32(trow + O_LL + 32 * ch, ol);
+    tmem_wait_ld();
+    if (row_live) {
+      uint32_t hw[8], lw[8];
+      unsigned long long l1 = 0;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        uint32_t hv = 0, lv = 0;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int i = 4 * k + e;
+          const long long tot = (long long)(int)oh[i] * 65536 + (long long)(int)om[i] * 256 + (long long)(int)ol[i];
+          const int v = (int)sat_i16(rhu64(tot, 15));
+          l1 += (unsigned long long)abs(v);
+          hv |= (uint32_t)((v >> 8) & 255) << (8 * e);
+          lv |= (uint32_t)(v & 255) << (8 * e);
+        }
+        hw[k] = hv;
+        lw[k] = lv;
+      }
+      const long long off = (long long)(row0 + qi) * a.ldc + h * HD + 32 * ch;
+      uint4* dh = reinterpret_cast<uint4*>(a.ctx_hi + off);
+      uint4* dl = reinterpret_cast<uint4*>(a.ctx_lo + off);
+      dh[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+      dh[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+      dl[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+      dl[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
+      if (a.ctx_l1) atomicAdd(&a.ctx_l1[row0 + qi], l1);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// 2-D uint8 map [rows][inner] (row stride ld bytes), box [box_rows][64 bytes], 64-byte swizzle.
+bool make_map64(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t rows, uint64_t ld, uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {ld};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t es[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+bool attention_tc_supported(size_t S, size_t d, size_t H) {
+  return H != 0 && d / H == (size_t)HD && d % H == 0 && S % 16 == 0 && S <= 16384 && (3 * d) % 16 == 0;
+}
+
+cudaError_t launch_attention_tc(const Planes& qkv, const VtPlanes& vt, size_t B, size_t S, size_t d, size_t H,
+                                bool causal, Planes ctx, nsrl_device_status* st, cudaStream_t stream) {
+  if (!attention_tc_supported(S, d, H) || encode_fn() == nullptr) return cudaErrorNotSupported;
+  const size_t T = B * S;
+  Maps m;
+  const bool ok = make_map64(&m.q_hi, qkv.hi, 3 * d, T, qkv.ld, QT) && make_map64(&m.q_lo, qkv.lo, 3 * d, T, qkv.ld, QT) &&
+                  make_map64(&m.k_hi, qkv.hi, 3 * d, T, qkv.ld, KT) && make_map64(&m.k_lo, qkv.lo, 3 * d, T, qkv.ld, KT) &&
+                  make_map64(&m.vt_hi, vt.hi, S, B * H * HD, S, HD) && make_map64(&m.vt_lo, vt.lo, S, B * H * HD, S, HD);
+  if (!ok) return cudaErrorNotSupported;
+  Args a{};
+  a.S = (int)S;
+  a.d = (int)d;
+  a.H = (int)H;
+  a.causal = causal ? 1 : 0;
+  a.shift = 3;  // log4(64)
+  a.ctx_hi = ctx.hi;
+  a.ctx_lo = ctx.lo;
+  a.ctx_l1 = ctx.l1;
+  a.ldc = (long long)ctx.ld;
+  a.st = st;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  dim3 grid((unsigned)((S + QT - 1) / QT), (unsigned)H, (unsigned)B);
+  const double pairs = causal ? (double)S * (S + 1) / 2.0 : (double)S * S;
+  ProfScope prof("attention_tc_hd64", stream, 4.0 * HD * (double)H * (double)B * pairs, 8.0 * (double)T * (double)d);
+  attention_tc_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(m, a);
+  return cudaGetLastError();
+}
+
+}  // namespace nsrl

@@ -80,6 +80,16 @@ bool attention_prefill_native(size_t d, size_t H, size_t S) {
   return (hd == 64 || hd == 16) && S <= 32768;
 }
 
+// Transposed V planes for the tensor-core attention (empty when it does not apply).
+VtPlanes carve_vt(Carver& c, size_t B, size_t S, size_t d, size_t H) {
+  VtPlanes vt{nullptr, nullptr, (int)S, (int)H, (int)(d / H)};
+  if (attention_tc_supported(S, d, H)) {
+    vt.hi = c.take<int8_t>(B * S * d);
+    vt.lo = c.take<uint8_t>(B * S * d);
+  }
+  return vt;
+}
+
 // ---- attention workspace: xn planes + l1, qkv planes, ctx planes + l1 [, int16 fallback buffers]
 size_t attention_ws(size_t B, size_t S, size_t d, size_t H, Carver* c = nullptr) {
   Carver local(nullptr);
@@ -89,6 +99,10 @@ size_t attention_ws(size_t B, size_t S, size_t d, size_t H, Carver* c = nullptr)
   k.planes(T, d, true);
   k.planes(T, 3 * d, false);
   k.planes(T, d, true);
+  if (attention_tc_supported(S, d, H)) {
+    k.take<int8_t>(T * d);
+    k.take<uint8_t>(T * d);
+  }
   if (!attention_prefill_native(d, H, S)) {
     k.take<int16_t>(T * 3 * d);
     k.take<int16_t>(T * d);
@@ -108,10 +122,11 @@ size_t mlp_ws(size_t T, size_t d, size_t F, Carver* c = nullptr) {
 // Attention core: (normalised or raw) input planes -> q|k|v -> ctx -> O linear.
 nsrl_status attention_core(const Planes& xin, size_t B, size_t S, size_t d, size_t H, bool causal,
                            const nsrl_linear_params* q, const nsrl_linear_params* k, const nsrl_linear_params* v,
-                           const nsrl_linear_params* o, Planes qkv, Planes ctx, int16_t* qkv16, int16_t* ctx16,
-                           Epi out_epi, const int16_t* skip, int16_t* out, unsigned long long* sat,
+                           const nsrl_linear_params* o, Planes qkv, Planes ctx, VtPlanes vt, int16_t* qkv16,
+                           int16_t* ctx16, Epi out_epi, const int16_t* skip, int16_t* out, unsigned long long* sat,
                            nsrl_device_status* st, cudaStream_t stream) {
   const size_t T = B * S;
+  const bool tc = vt.hi != nullptr && tma_supported();
   GemmArgs g{};
   g.a_hi = xin.hi;
   g.a_lo = xin.lo;
@@ -123,13 +138,16 @@ nsrl_status attention_core(const Planes& xin, size_t B, size_t S, size_t d, size
   g.seg[0] = seg_of(q);
   g.seg[1] = seg_of(k);
   g.seg[2] = seg_of(v);
-  g.epi = Epi::PLANES;
+  g.epi = tc ? Epi::QKV_VT : Epi::PLANES;
   g.yp = qkv;
+  g.vt = vt;
   g.st = st;
   NSRL_TRY(launch_gemm(g, stream), "qkv projection");
 
   NSRL_TRY(cudaMemsetAsync(ctx.l1, 0, T * sizeof(unsigned long long), stream), "memset");
-  if (attention_prefill_native(d, H, S)) {
+  if (tc) {
+    NSRL_TRY(launch_attention_tc(qkv, vt, B, S, d, H, causal, ctx, st, stream), "attention");
+  } else if (attention_prefill_native(d, H, S)) {
     NSRL_TRY(launch_attention(qkv, B, S, d, H, causal, ctx, st, stream), "attention");
   } else {
     NSRL_TRY(launch_join_planes(qkv, T, 3 * d, qkv16, 3 * d, stream), "join planes");
@@ -229,13 +247,14 @@ nsrl_status attention_block(const int16_t* x, size_t B, size_t S, size_t d, size
   Planes xn = c.planes(T, d, true);
   Planes qkv = c.planes(T, 3 * d, false);
   Planes ctx = c.planes(T, d, true);
+  VtPlanes vt = carve_vt(c, B, S, d, H);
   int16_t *qkv16 = nullptr, *ctx16 = nullptr;
   if (!attention_prefill_native(d, H, S)) {
     qkv16 = c.take<int16_t>(T * 3 * d);
     ctx16 = c.take<int16_t>(T * d);
   }
   NSRL_TRY(launch_rms_norm(x, T, d, gamma, eps, nullptr, xn, st, stream), "rms norm");
-  return attention_core(xn, B, S, d, H, causal, q, k, v, o, qkv, ctx, qkv16, ctx16, Epi::RESID, x, y,
+  return attention_core(xn, B, S, d, H, causal, q, k, v, o, qkv, ctx, vt, qkv16, ctx16, Epi::RESID, x, y,
                         &st->attention_saturations, st, stream);
 }
 
@@ -339,13 +358,14 @@ nsrl_status nsrl_self_attention(const int16_t* x, size_t batch, size_t seq_len, 
   Planes xp = c.planes(T, d_model, true);
   Planes qkv = c.planes(T, 3 * d_model, false);
   Planes ctx = c.planes(T, d_model, true);
+  VtPlanes vt = carve_vt(c, batch, seq_len, d_model, heads);
   int16_t *qkv16 = nullptr, *ctx16 = nullptr;
   if (!attention_prefill_native(d_model, heads, seq_len)) {
     qkv16 = c.take<int16_t>(T * 3 * d_model);
     ctx16 = c.take<int16_t>(T * d_model);
   }
   NSRL_TRY(launch_split_planes(x, T, d_model, d_model, xp, s), "split planes");
-  return attention_core(xp, batch, seq_len, d_model, heads, causal != 0, q, k, v, o, qkv, ctx, qkv16, ctx16,
+  return attention_core(xp, batch, seq_len, d_model, heads, causal != 0, q, k, v, o, qkv, ctx, vt, qkv16, ctx16,
                         Epi::I16, nullptr, out, nullptr, status, s);
 }
 

@@ -32,6 +32,15 @@ enum class Epi : int {
   PLANES = 1,  // y = requant(acc) as byte planes (+ row L1)
   RESID = 2,   // y = skip (+sat) requant(acc) as int16, saturations counted
   GATED = 3,   // y = gated_act(requant(up), requant(gate)) as byte planes (+ row L1)
+  QKV_VT = 4,  // Q|K|V projection: q, k as byte planes [T][3d]; v transposed per head
+               // into byte planes [B][H][hd][S] (the AV operand of the attention)
+};
+
+// Per-head transposed V planes: row (b * H + h) * hd + dim, column = position.
+struct VtPlanes {
+  int8_t* hi;
+  uint8_t* lo;
+  int S, H, hd;
 };
 
 struct GemmArgs {
@@ -49,6 +58,7 @@ struct GemmArgs {
   const int16_t* skip;
   size_t ldskip;
   unsigned long long* sat_counter;
+  VtPlanes vt;
   nsrl_device_status* st;
 };
 
@@ -69,6 +79,15 @@ cudaError_t launch_rms_norm(const int16_t* x, size_t rows, size_t d, const int16
 // which must be zeroed by the caller).
 cudaError_t launch_attention(const Planes& qkv, size_t B, size_t S, size_t d, size_t H, bool causal, Planes ctx,
                              nsrl_device_status* st, cudaStream_t stream);
+
+// Tensor-core (tcgen05) attention core for head_dim 64: q, k from the q|k|v
+// planes, v from the transposed planes of Epi::QKV_VT.  Returns
+// cudaErrorNotSupported when the shape is outside what it takes.
+cudaError_t launch_attention_tc(const Planes& qkv, const VtPlanes& vt, size_t B, size_t S, size_t d, size_t H,
+                                bool causal, Planes ctx, nsrl_device_status* st, cudaStream_t stream);
+// Shape rule of the tensor-core attention (head_dim 64, seq_len % 16 == 0,
+// seq_len <= 16384); the workspace reserves the transposed V planes for it.
+bool attention_tc_supported(size_t S, size_t d, size_t H);
 
 // KV-cache decode attention (int16 operands).
 cudaError_t launch_decode_attention(const int16_t* q, const int16_t* kc, const int16_t* vc, const int32_t* lens,

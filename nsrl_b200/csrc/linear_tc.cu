@@ -7,18 +7,25 @@
 // Exactness on int8 tensor cores: x is held as byte planes x = 256*hi + lo
 // (hi signed, lo unsigned).  Two MMAs share the weight tile: hi x W (s8.s8)
 // and lo x W (u8.s8), each into its own s32 TMEM accumulator; both partial
-// sums are exact (|hi*w| <= 16256, |lo*w| <= 32385 per product), and the
-// epilogue recombines 256*acc_hi + acc_lo + bias in i64.  A final sum outside
-// i32 is flagged here; an overflow of an intermediate prefix can only happen
-// when |bias| + 127 * sum_k |x[m][k]| > i32::MAX, and those rows (if any) are
-// re-scanned in reference order by prefix_check_kernel.
+// sums are exact (|hi*w| <= 16256, |lo*w| <= 32385 per product).  The true
+// sum 256*acc_hi + acc_lo + bias fits i32 whenever no i32 prefix of the
+// reference's accumulation overflows, so the epilogue recombines it with
+// wrapping i32 arithmetic (exact in that case).  A prefix can only overflow
+// when |bias| + 127 * sum_k |x[m][k]| > i32::MAX; only then does
+// prefix_check_kernel rescan those rows in reference order and reject the
+// call (linear.rs:144-173, :282-296).
 //
-// Kernel shape: one 128 x 128 output tile per CTA, 6 warps:
-//   warp 0      TMA producer (A hi/lo planes + W tile per 128-wide K block)
+// Persistent kernel, one CTA per SM, 10 warps:
+//   warp 0      TMA producer: A hi/lo planes + W tile per 128-wide K block,
+//               through a 4-stage shared-memory ring
 //   warp 1      TMEM allocator + single-thread MMA issuer
-//   warps 2..5  epilogue (TMEM -> registers -> requant -> global)
-// Operand tiles use the 128-byte swizzle, K-major, one 128-byte row per
-// tile row, as written by TMA.
+//   warps 2..9  epilogue: TMEM -> registers -> requant -> global; two warps
+//               per TMEM lane quarter, 64 columns each
+// The two accumulator pairs (hi, lo) of a 128 x 128 tile take 256 TMEM
+// columns; two tiles are in flight (512 columns) so that the epilogue of
+// tile i overlaps the MMAs of tile i+1.  Operand tiles are K-major with the
+// 128-byte swizzle, one 128-byte row per tile row, as written by TMA.
+#include <algorithm>
 #include <cstdio>
 
 #include "common.cuh"
@@ -31,7 +38,12 @@ constexpr int BM = 128, BN = 128, BK = 128;
 constexpr int TILE_A = BM * BK;                   // one plane, 16 KB
 constexpr int TILE_B = BN * BK;                   // 16 KB
 constexpr int STAGE_BYTES = 2 * TILE_A + TILE_B;  // 48 KB
-constexpr uint32_t TMEM_COLS = 256;               // acc_hi: cols [0,128), acc_lo: [128,256)
+constexpr int STAGES = 4;
+constexpr int ACC_COLS = 2 * BN;                  // acc_hi: [0,128), acc_lo: [128,256)
+constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;      // two tiles in flight
+constexpr int EPI_WARPS = 8;
+constexpr int THREADS = 64 + 32 * EPI_WARPS;      // 320
+constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE_BYTES + 1024 + 256;
 
 struct TcMaps {
   CUtensorMap a_hi, a_lo, b[3];
@@ -40,6 +52,7 @@ struct TcMaps {
 struct TcParams {
   int M, K, N;  // N = output columns (GATED: hidden channels)
   int nseg, seg_rows;
+  int tiles_n, tiles;
   const int32_t* bias[3];
   const nsrl_fixed_scale* scales[3];
   int16_t* y;
@@ -51,84 +64,123 @@ struct TcParams {
   const int16_t* skip;
   long long ldskip;
   unsigned long long* sat;
+  int8_t* vth;
+  uint8_t* vtl;
+  int vt_S, vt_H, vt_hd, vt_col0;  // QKV_VT: output columns >= vt_col0 go to the transposed planes
   nsrl_device_status* st;
 };
 
-// Combine the two partial sums of one output, apply bias and the scale.
-__device__ __forceinline__ int16_t finish(int hi, int lo, const int32_t* bias, const nsrl_fixed_scale* sc, int n,
-                                          bool& overflow) {
-  long long acc = (long long)hi * 256 + (long long)lo + (bias ? (long long)bias[n] : 0ll);
-  if (acc < INT_MIN || acc > INT_MAX) overflow = true;
-  nsrl_fixed_scale s = sc[n];
-  return requant_i32((int)acc, s.multiplier, s.right_shift);
+// requantize_i32_to_i16 (numeric.rs:59-70) with the i32 fast paths of a
+// multiplier of 1: rhu(acc, s) = (acc >> s) + bit (s - 1) of acc, s in 1..31.
+__device__ __forceinline__ int requant_fast(int acc, int mult, uint32_t shift) {
+  if (mult == 1) {
+    if (shift == 0) return max(-32768, min(32767, acc));
+    if (shift < 32) {
+      const int r = (acc >> shift) + ((acc >> (shift - 1)) & 1);
+      return max(-32768, min(32767, r));
+    }
+  }
+  return (int)sat_i16(rhu64((long long)acc * (long long)mult, shift));
 }
 
-__device__ __forceinline__ void store_i16x32(int16_t* dst, const int16_t (&v)[32], int nvalid, bool vec_ok) {
+__device__ __forceinline__ uint32_t pack2(int a, int b) { return (uint32_t)(a & 0xFFFF) | ((uint32_t)b << 16); }
+
+// Requantised outputs of 32 consecutive columns as 16 packed int16 pairs.
+__device__ __forceinline__ void finish32(const uint32_t (&h)[32], const uint32_t (&l)[32], const int32_t* bias,
+                                         const nsrl_fixed_scale* sc, int n0, int nvalid, uint32_t (&o)[16]) {
+#pragma unroll
+  for (int i = 0; i < 32; i += 2) {
+    int v[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int n = n0 + i + j;
+      int r = 0;
+      if (i + j < nvalid) {
+        // wrapping u32 arithmetic: exact whenever the true i32 sum fits
+        const int acc = (int)(h[i + j] * 256u + l[i + j] + (bias ? (uint32_t)bias[n] : 0u));
+        const nsrl_fixed_scale s = sc[n];
+        r = requant_fast(acc, s.multiplier, s.right_shift);
+      }
+      v[j] = r;
+    }
+    o[i / 2] = pack2(v[0], v[1]);
+  }
+}
+
+__device__ __forceinline__ void store32_i16(int16_t* dst, const uint32_t (&o)[16], int nvalid, bool vec_ok) {
   if (vec_ok && nvalid == 32) {
     uint4* d = reinterpret_cast<uint4*>(dst);
-    const uint4* s = reinterpret_cast<const uint4*>(v);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) d[i] = s[i];
+    for (int i = 0; i < 4; ++i) d[i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
   } else {
-    for (int i = 0; i < nvalid; ++i) dst[i] = v[i];
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (i < nvalid) dst[i] = (int16_t)(o[i / 2] >> (16 * (i & 1)));
   }
 }
 
-__device__ __forceinline__ void store_planes32(int8_t* dh, uint8_t* dl, const int16_t* v, int nvalid, bool vec_ok,
-                                               unsigned long long& l1) {
+// Splits 32 packed int16 values into hi / lo byte planes (+ L1 of the values).
+__device__ __forceinline__ void store32_planes(int8_t* dh, uint8_t* dl, const uint32_t (&o)[16], int nvalid,
+                                               bool vec_ok, unsigned long long& l1) {
   uint32_t hw[8], lw[8];
+  unsigned acc = 0;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    uint32_t h = 0, l = 0;
+    const uint32_t a = o[2 * i], b = o[2 * i + 1];  // values 4i..4i+3 as int16 pairs
+    // hi bytes: byte 1 of each int16, lo bytes: byte 0
+    hw[i] = __byte_perm(a, b, 0x7531);
+    lw[i] = __byte_perm(a, b, 0x6420);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      int x = v[4 * i + j];
-      h |= (uint32_t)((x >> 8) & 255) << (8 * j);
-      l |= (uint32_t)(x & 255) << (8 * j);
+      const int v = (int16_t)(((j < 2) ? a : b) >> (16 * (j & 1)));
+      if (4 * i + j < nvalid) acc += (unsigned)abs(v);
     }
-    hw[i] = h;
-    lw[i] = l;
   }
-  for (int i = 0; i < nvalid; ++i) l1 += (unsigned long long)abs((int)v[i]);
+  l1 += acc;
   if (vec_ok && nvalid == 32) {
-    uint4* a = reinterpret_cast<uint4*>(dh);
-    uint4* b = reinterpret_cast<uint4*>(dl);
-    a[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-    a[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
-    b[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-    b[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
+    uint4* ah = reinterpret_cast<uint4*>(dh);
+    uint4* al = reinterpret_cast<uint4*>(dl);
+    ah[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    ah[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+    al[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    al[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
   } else {
-    for (int i = 0; i < nvalid; ++i) {
-      dh[i] = (int8_t)(v[i] >> 8);
-      dl[i] = (uint8_t)(v[i] & 255);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      if (i < nvalid) {
+        const int v = (int16_t)(o[i / 2] >> (16 * (i & 1)));
+        dh[i] = (int8_t)(v >> 8);
+        dl[i] = (uint8_t)(v & 255);
+      }
     }
   }
 }
 
-template <int EPI, int STAGES>
-__global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__ TcMaps maps, const TcParams p) {
+template <int EPI>
+__global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_constant__ TcMaps maps, const TcParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
   uint64_t* empty = full + STAGES;
-  uint64_t* accf = empty + STAGES;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(accf + 1);
+  uint64_t* acc_full = empty + STAGES;  // [2]: MMA -> epilogue
+  uint64_t* acc_empty = acc_full + 2;   // [2]: epilogue -> MMA
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   uint32_t* skip_flag = tslot + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) *skip_flag = timed_out(p.st) ? 1u : 0u;
   __syncthreads();
   if (*skip_flag) return;  // a wait of this call already timed out: do nothing
-  const int m0 = blockIdx.y * BM;
-  const int nt = blockIdx.x;
-  const int nkb = (p.K + BK - 1) / BK;
 
   if (warp == 0 && lane == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accf, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], EPI_WARPS);
+    }
     fence_barrier_init();
     prefetch_tmap(&maps.a_hi);
     prefetch_tmap(&maps.a_lo);
@@ -141,145 +193,199 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
-
-  // Which weight rows feed this N tile.
-  int seg = 0, brow = nt * BN;
-  if (EPI == (int)Epi::GATED) {
-    brow = nt * (BN / 2);
-  } else if (p.nseg == 3) {
-    seg = (nt * BN) / p.seg_rows;
-    brow = (nt * BN) % p.seg_rows;
-  }
+  const int nkb = (p.K + BK - 1) / BK;
 
   if (warp == 0) {
     if (lane == 0) {
-      int issued = 0;
-      for (int kb = 0; kb < nkb; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (kb / STAGES) & 1;
-        if (kb >= STAGES && !mbar_wait(&empty[s], ph ^ 1, p.st)) break;
-        mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
-        uint8_t* sa = smem + s * STAGE_BYTES;
-        tma_load_2d(sa, &maps.a_hi, &full[s], kb * BK, m0);
-        tma_load_2d(sa + TILE_A, &maps.a_lo, &full[s], kb * BK, m0);
+      uint32_t it = 0;  // global k-block counter over all tiles of this CTA
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
+        const int m0 = (t / p.tiles_n) * BM, nt = t % p.tiles_n;
+        int seg = 0, brow = nt * BN;
         if (EPI == (int)Epi::GATED) {
-          tma_load_2d(sa + 2 * TILE_A, &maps.b[0], &full[s], kb * BK, brow);
-          tma_load_2d(sa + 2 * TILE_A + TILE_B / 2, &maps.b[1], &full[s], kb * BK, brow);
-        } else {
-          tma_load_2d(sa + 2 * TILE_A, &maps.b[seg], &full[s], kb * BK, brow);
+          brow = nt * (BN / 2);
+        } else if (p.nseg == 3) {
+          seg = (nt * BN) / p.seg_rows;
+          brow = (nt * BN) % p.seg_rows;
         }
-        issued = kb + 1;
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (it >= STAGES && !mbar_wait(&empty[s], ph ^ 1, p.st)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+          uint8_t* sa = smem + s * STAGE_BYTES;
+          tma_load_2d(sa, &maps.a_hi, &full[s], kb * BK, m0);
+          tma_load_2d(sa + TILE_A, &maps.a_lo, &full[s], kb * BK, m0);
+          if (EPI == (int)Epi::GATED) {
+            tma_load_2d(sa + 2 * TILE_A, &maps.b[0], &full[s], kb * BK, brow);
+            tma_load_2d(sa + 2 * TILE_A + TILE_B / 2, &maps.b[1], &full[s], kb * BK, brow);
+          } else {
+            tma_load_2d(sa + 2 * TILE_A, &maps.b[seg], &full[s], kb * BK, brow);
+          }
+        }
       }
-      // Drain: the loads still in flight must land before the CTA can exit.
-      for (int kb = (issued > STAGES ? issued - STAGES : 0); kb < issued; ++kb)
-        mbar_wait(&full[kb % STAGES], (kb / STAGES) & 1, p.st);
+      // Drain: the last loads in flight must land before the CTA exits.
+      for (uint32_t j = (it > STAGES ? it - STAGES : 0); j < it; ++j)
+        mbar_wait(&full[j % STAGES], (j / STAGES) & 1, p.st);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t id_hi = idesc_i8(BM, BN, 1, 1);  // s8 x s8
       const uint32_t id_lo = idesc_i8(BM, BN, 0, 1);  // u8 x s8
-      for (int kb = 0; kb < nkb; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (kb / STAGES) & 1;
-        if (!mbar_wait(&full[s], ph, p.st)) break;
+      uint32_t it = 0, local = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x, ++local) {
+        const uint32_t buf = local & 1, use = local >> 1;
+        if (use > 0 && !mbar_wait(&acc_empty[buf], (use - 1) & 1, p.st)) break;
         tc_fence_after();
-        const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
+        const uint32_t d = tmem + buf * ACC_COLS;
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&full[s], ph, p.st)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
 #pragma unroll
-        for (int j = 0; j < BK / 32; ++j) {
-          const uint64_t ah = sdesc_k128(base + 32 * j);
-          const uint64_t al = sdesc_k128(base + TILE_A + 32 * j);
-          const uint64_t bd = sdesc_k128(base + 2 * TILE_A + 32 * j);
-          const uint32_t acc = (kb > 0 || j > 0) ? 1u : 0u;
-          umma_i8(tmem, ah, bd, id_hi, acc);
-          umma_i8(tmem + BN, al, bd, id_lo, acc);
+          for (int j = 0; j < BK / 32; ++j) {
+            const uint64_t ah = sdesc_k128(base + 32 * j);
+            const uint64_t al = sdesc_k128(base + TILE_A + 32 * j);
+            const uint64_t bd = sdesc_k128(base + 2 * TILE_A + 32 * j);
+            const uint32_t acc = (kb > 0 || j > 0) ? 1u : 0u;
+            umma_i8(d, ah, bd, id_hi, acc);
+            umma_i8(d + BN, al, bd, id_lo, acc);
+          }
+          umma_commit(&empty[s]);
         }
-        umma_commit(&empty[s]);
+        umma_commit(&acc_full[buf]);
       }
-      umma_commit(accf);
     }
   } else {
-    // Epilogue: warp w reads TMEM lanes [32*(w%4), 32*(w%4)+32).
-    const bool ok = mbar_wait(accf, 0, p.st);
-    tc_fence_after();
+    // Epilogue: warp w reads TMEM lanes [32*(w%4), 32*(w%4)+32); warps
+    // 2..5 take columns [0, 64) of the tile, warps 6..9 columns [64, 128).
     const int q = warp & 3;
-    const int r = m0 + q * 32 + lane;
-    const bool row_ok = ok && r < p.M;
-    const uint32_t lrow = tmem + ((uint32_t)(q * 32) << 16);
-    bool overflow = false;
-    unsigned long long l1 = 0, sat = 0;
-    if (EPI == (int)Epi::GATED) {
-      const int f0 = nt * (BN / 2);
-#pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
-        uint32_t h[32], l[32];
-        int16_t up[32], out[32];
-        tmem_ld32(lrow + 32 * c, h);
-        tmem_ld32(lrow + BN + 32 * c, l);
-        tmem_wait_ld();
-        const int fb = f0 + 32 * c;
+    const int chalf = (warp - 2) >> 2;
+    uint32_t local = 0;
+    unsigned long long sat = 0;
+    for (int t = blockIdx.x; t < p.tiles; t += gridDim.x, ++local) {
+      const uint32_t buf = local & 1, use = local >> 1;
+      if (!mbar_wait(&acc_full[buf], use & 1, p.st)) break;
+      tc_fence_after();
+      const int m0 = (t / p.tiles_n) * BM, nt = t % p.tiles_n;
+      const int r = m0 + q * 32 + lane;
+      const bool row_ok = r < p.M;
+      const uint32_t lrow = tmem + buf * ACC_COLS + ((uint32_t)(q * 32) << 16);
+      unsigned long long l1 = 0;
+      if (EPI == (int)Epi::GATED) {
+        // tile columns [0,64): up channels f0..f0+63, [64,128): gate channels
+        const int fb = nt * (BN / 2) + 32 * chalf;
         const int nvalid = max(0, min(32, p.N - fb));
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          up[i] = i < nvalid ? finish((int)h[i], (int)l[i], p.bias[0], p.scales[0], fb + i, overflow) : 0;
-        tmem_ld32(lrow + 64 + 32 * c, h);
-        tmem_ld32(lrow + BN + 64 + 32 * c, l);
+        uint32_t h[32], l[32], up[16], gt[16];
+        tmem_ld32(lrow + 32 * chalf, h);
+        tmem_ld32(lrow + BN + 32 * chalf, l);
         tmem_wait_ld();
+        finish32(h, l, p.bias[0], p.scales[0], fb, nvalid, up);
+        tmem_ld32(lrow + 64 + 32 * chalf, h);
+        tmem_ld32(lrow + BN + 64 + 32 * chalf, l);
+        tmem_wait_ld();
+        tc_fence_before();
+        if (lane == 0) mbar_arrive(&acc_empty[buf]);
+        finish32(h, l, p.bias[1], p.scales[1], fb, nvalid, gt);
+        uint32_t o[16];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          int16_t g = i < nvalid ? finish((int)h[i], (int)l[i], p.bias[1], p.scales[1], fb + i, overflow) : 0;
-          out[i] = gated_act(up[i], g);
+        for (int i = 0; i < 16; ++i) {
+          const int a = gated_act((int16_t)(up[i] & 0xFFFF), (int16_t)(gt[i] & 0xFFFF));
+          const int b = gated_act((int16_t)(up[i] >> 16), (int16_t)(gt[i] >> 16));
+          o[i] = pack2(a, b);
         }
         if (row_ok && nvalid > 0) {
-          const long long o = (long long)r * p.ldp + fb;
-          store_planes32(p.yh + o, p.yl + o, out, nvalid, ((p.ldp | fb) & 15) == 0, l1);
+          const long long off = (long long)r * p.ldp + fb;
+          store32_planes(p.yh + off, p.yl + off, o, nvalid, ((p.ldp | fb) & 15) == 0, l1);
         }
-      }
-    } else {
-      const int nb = nt * BN;
-      const int sseg = (p.nseg == 3) ? nb / p.seg_rows : 0;
-      const int nloc0 = (p.nseg == 3) ? nb % p.seg_rows : nb;
-      const int32_t* bias = p.bias[sseg];
-      const nsrl_fixed_scale* sc = p.scales[sseg];
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t h[32], l[32];
-        int16_t out[32];
-        tmem_ld32(lrow + 32 * c, h);
-        tmem_ld32(lrow + BN + 32 * c, l);
+      } else {
+        const int nb = nt * BN;
+        const int sseg = (p.nseg == 3) ? nb / p.seg_rows : 0;
+        const int nloc0 = (p.nseg == 3) ? nb % p.seg_rows : nb;
+        const int32_t* bias = p.bias[sseg];
+        const nsrl_fixed_scale* sc = p.scales[sseg];
+        uint32_t h[2][32], l[2][32];
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          tmem_ld32(lrow + 64 * chalf + 32 * c, h[c]);
+          tmem_ld32(lrow + BN + 64 * chalf + 32 * c, l[c]);
+        }
         tmem_wait_ld();
-        const int n = nb + 32 * c;
-        const int nvalid = max(0, min(32, p.N - n));
+        tc_fence_before();
+        if (lane == 0) mbar_arrive(&acc_empty[buf]);
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          out[i] = i < nvalid ? finish((int)h[i], (int)l[i], bias, sc, nloc0 + 32 * c + i, overflow) : 0;
-        if (!row_ok || nvalid == 0) continue;
-        if (EPI == (int)Epi::I16) {
-          store_i16x32(p.y + (long long)r * p.ldy + n, out, nvalid, ((p.ldy | n) & 7) == 0);
-        } else if (EPI == (int)Epi::RESID) {
-          const int16_t* sk = p.skip + (long long)r * p.ldskip + n;
-          int16_t res[32];
-          const bool vec = ((p.ldskip | p.ldy | n) & 7) == 0 && nvalid == 32;
-          if (vec) {
+        for (int c = 0; c < 2; ++c) {
+          const int cn = 64 * chalf + 32 * c;
+          const int n = nb + cn;
+          const int nvalid = max(0, min(32, p.N - n));
+          uint32_t o[16];
+          finish32(h[c], l[c], bias, sc, nloc0 + cn, nvalid, o);
+          if (!row_ok || nvalid == 0) continue;
+          if (EPI == (int)Epi::I16) {
+            store32_i16(p.y + (long long)r * p.ldy + n, o, nvalid, ((p.ldy | n) & 7) == 0);
+          } else if (EPI == (int)Epi::RESID) {
+            const int16_t* sk = p.skip + (long long)r * p.ldskip + n;
+            const bool vec = ((p.ldskip | p.ldy | n) & 7) == 0 && nvalid == 32;
+            uint32_t s16[16];
+            if (vec) {
 #pragma unroll
-            for (int i = 0; i < 4; ++i) reinterpret_cast<uint4*>(res)[i] = reinterpret_cast<const uint4*>(sk)[i];
+              for (int i = 0; i < 4; ++i) {
+                const uint4 u = reinterpret_cast<const uint4*>(sk)[i];
+                s16[4 * i] = u.x;
+                s16[4 * i + 1] = u.y;
+                s16[4 * i + 2] = u.z;
+                s16[4 * i + 3] = u.w;
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const int a = (2 * i < nvalid) ? (int)sk[2 * i] : 0;
+                const int b = (2 * i + 1 < nvalid) ? (int)sk[2 * i + 1] : 0;
+                s16[i] = pack2(a, b);
+              }
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int a = (int)(int16_t)(s16[i] & 0xFFFF) + (int)(int16_t)(o[i] & 0xFFFF);
+              const int b = (int)(int16_t)(s16[i] >> 16) + (int)(int16_t)(o[i] >> 16);
+              if (2 * i < nvalid && (a < -32768 || a > 32767)) ++sat;
+              if (2 * i + 1 < nvalid && (b < -32768 || b > 32767)) ++sat;
+              o[i] = pack2(max(-32768, min(32767, a)), max(-32768, min(32767, b)));
+            }
+            store32_i16(p.y + (long long)r * p.ldy + n, o, nvalid, vec);
+          } else if (EPI == (int)Epi::QKV_VT && n >= p.vt_col0) {
+            // v columns: byte stores into [b][h][dim][s]; the 32 lanes of the
+            // warp hold 32 consecutive positions, so each store instruction
+            // writes one contiguous 32-byte run per plane.
+            const int b = r / p.vt_S, spos = r % p.vt_S;
+            const int c0 = n - p.vt_col0;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              if (i < nvalid) {
+                const int c = c0 + i, hh = c / p.vt_hd, dd = c % p.vt_hd;
+                const long long off = ((long long)(b * p.vt_H + hh) * p.vt_hd + dd) * p.vt_S + spos;
+                const int v = (int16_t)(o[i / 2] >> (16 * (i & 1)));
+                p.vth[off] = (int8_t)(v >> 8);
+                p.vtl[off] = (uint8_t)(v & 255);
+              }
+            }
           } else {
-            for (int i = 0; i < nvalid; ++i) res[i] = sk[i];
+            const long long off = (long long)r * p.ldp + n;
+            store32_planes(p.yh + off, p.yl + off, o, nvalid, ((p.ldp | n) & 15) == 0, l1);
           }
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            int w = (int)res[i] + (int)out[i];
-            if (i < nvalid && (w < -32768 || w > 32767)) ++sat;
-            res[i] = sat_i16_i32(w);
-          }
-          store_i16x32(p.y + (long long)r * p.ldy + n, res, nvalid, vec);
-        } else {
-          const long long o = (long long)r * p.ldp + n;
-          store_planes32(p.yh + o, p.yl + o, out, nvalid, ((p.ldp | n) & 15) == 0, l1);
         }
       }
+      if ((EPI == (int)Epi::PLANES || EPI == (int)Epi::GATED) && p.yl1 && row_ok && l1) atomicAdd(&p.yl1[r], l1);
     }
-    if (overflow && row_ok) nsrl_flag(p.st, NSRL_FLAG_LINEAR_OVERFLOW);
-    if ((EPI == (int)Epi::PLANES || EPI == (int)Epi::GATED) && p.yl1 && row_ok) atomicAdd(&p.yl1[r], l1);
     if (EPI == (int)Epi::RESID) {
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) sat += __shfl_xor_sync(0xffffffffu, sat, o);
@@ -307,6 +413,12 @@ struct SimtParams {
   TcParams tp;
 };
 
+__device__ __forceinline__ int16_t finish1(int hi, int lo, const int32_t* bias, const nsrl_fixed_scale* sc, int n) {
+  const int acc = (int)((uint32_t)hi * 256u + (uint32_t)lo + (bias ? (uint32_t)bias[n] : 0u));
+  const nsrl_fixed_scale s = sc[n];
+  return (int16_t)requant_fast(acc, s.multiplier, s.right_shift);
+}
+
 __device__ __forceinline__ void simt_dot(const SimtParams& s, int m, int sg, int nl, int& hi, int& lo) {
   const int8_t* ah = s.a_hi + (long long)m * s.lda;
   const uint8_t* al = s.a_lo + (long long)m * s.lda;
@@ -325,29 +437,32 @@ __global__ void gemm_simt_kernel(const SimtParams s) {
   if (idx >= (long long)s.M * s.N) return;
   const int m = (int)(idx / s.N), n = (int)(idx % s.N);
   const TcParams& p = s.tp;
-  bool overflow = false;
   int16_t v;
   if (s.epi == (int)Epi::GATED) {
     int h, l;
     simt_dot(s, m, 0, n, h, l);
-    int16_t up = finish(h, l, p.bias[0], p.scales[0], n, overflow);
+    int16_t up = finish1(h, l, p.bias[0], p.scales[0], n);
     simt_dot(s, m, 1, n, h, l);
-    int16_t g = finish(h, l, p.bias[1], p.scales[1], n, overflow);
+    int16_t g = finish1(h, l, p.bias[1], p.scales[1], n);
     v = gated_act(up, g);
   } else {
     const int sg = s.nseg == 3 ? n / s.seg_rows : 0;
     const int nl = s.nseg == 3 ? n % s.seg_rows : n;
     int h, l;
     simt_dot(s, m, sg, nl, h, l);
-    v = finish(h, l, p.bias[sg], p.scales[sg], nl, overflow);
+    v = finish1(h, l, p.bias[sg], p.scales[sg], nl);
   }
-  if (overflow) nsrl_flag(p.st, NSRL_FLAG_LINEAR_OVERFLOW);
   if (s.epi == (int)Epi::I16) {
     p.y[(long long)m * p.ldy + n] = v;
   } else if (s.epi == (int)Epi::RESID) {
     int w = (int)p.skip[(long long)m * p.ldskip + n] + (int)v;
     if (w < -32768 || w > 32767) atomicAdd(p.sat, 1ull);
     p.y[(long long)m * p.ldy + n] = sat_i16_i32(w);
+  } else if (s.epi == (int)Epi::QKV_VT && n >= p.vt_col0) {
+    const int b = m / p.vt_S, spos = m % p.vt_S, c = n - p.vt_col0;
+    const long long off = ((long long)(b * p.vt_H + c / p.vt_hd) * p.vt_hd + c % p.vt_hd) * p.vt_S + spos;
+    p.vth[off] = (int8_t)(v >> 8);
+    p.vtl[off] = (uint8_t)(v & 255);
   } else {
     p.yh[(long long)m * p.ldp + n] = (int8_t)(v >> 8);
     p.yl[(long long)m * p.ldp + n] = (uint8_t)(v & 255);
@@ -503,33 +618,44 @@ bool make_map(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t rows, ui
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int EPI, int STAGES>
-cudaError_t launch_tc(const TcMaps& maps, const TcParams& p, dim3 grid, cudaStream_t stream) {
-  const size_t smem = (size_t)STAGES * STAGE_BYTES + 1024 + 256;
+template <int EPI>
+cudaError_t launch_tc(const TcMaps& maps, const TcParams& p, int grid, cudaStream_t stream) {
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<EPI, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
+    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)SMEM_BYTES);
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  gemm_tc_kernel<EPI, STAGES><<<grid, 192, smem, stream>>>(maps, p);
+  gemm_tc_kernel<EPI><<<grid, THREADS, SMEM_BYTES, stream>>>(maps, p);
   return cudaGetLastError();
 }
 
-template <int STAGES>
-cudaError_t launch_tc_epi(Epi epi, const TcMaps& maps, const TcParams& p, dim3 grid, cudaStream_t stream) {
+cudaError_t launch_tc_epi(Epi epi, const TcMaps& maps, const TcParams& p, int grid, cudaStream_t stream) {
   switch (epi) {
     case Epi::I16:
-      return launch_tc<(int)Epi::I16, STAGES>(maps, p, grid, stream);
+      return launch_tc<(int)Epi::I16>(maps, p, grid, stream);
     case Epi::PLANES:
-      return launch_tc<(int)Epi::PLANES, STAGES>(maps, p, grid, stream);
+      return launch_tc<(int)Epi::PLANES>(maps, p, grid, stream);
     case Epi::RESID:
-      return launch_tc<(int)Epi::RESID, STAGES>(maps, p, grid, stream);
+      return launch_tc<(int)Epi::RESID>(maps, p, grid, stream);
     case Epi::GATED:
-      return launch_tc<(int)Epi::GATED, STAGES>(maps, p, grid, stream);
+      return launch_tc<(int)Epi::GATED>(maps, p, grid, stream);
+    case Epi::QKV_VT:
+      return launch_tc<(int)Epi::QKV_VT>(maps, p, grid, stream);
   }
   return cudaErrorInvalidValue;
+}
+
+int sm_count() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
@@ -566,6 +692,12 @@ cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t stream) {
   p.skip = a.skip;
   p.ldskip = (long long)a.ldskip;
   p.sat = a.sat_counter;
+  p.vth = a.vt.hi;
+  p.vtl = a.vt.lo;
+  p.vt_S = a.vt.S;
+  p.vt_H = a.vt.H;
+  p.vt_hd = a.vt.hd;
+  p.vt_col0 = a.epi == Epi::QKV_VT ? 2 * (int)a.seg[0].rows : INT_MAX;
   p.st = a.st;
 
   bool tc = tma_supported() && (a.K % 16) == 0 && (a.lda % 16) == 0 && aligned16(a.a_hi) && aligned16(a.a_lo);
@@ -578,8 +710,9 @@ cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t stream) {
   double out_bytes = 2.0 * Mx * Nx;
   if (a.epi == Epi::RESID) out_bytes *= 2.0;  // skip read + output write
   if (a.epi == Epi::PLANES || a.epi == Epi::GATED) out_bytes += a.yp.l1 ? 8.0 * Mx : 0.0;
-  static const char* names[2][4] = {{"linear_simt_i16", "linear_simt_planes", "linear_simt_resid", "linear_simt_gated"},
-                                    {"linear_tc_i16", "linear_tc_planes", "linear_tc_resid", "linear_tc_gated"}};
+  static const char* names[2][5] = {
+      {"linear_simt_i16", "linear_simt_planes", "linear_simt_resid", "linear_simt_gated", "linear_simt_qkv"},
+      {"linear_tc_i16", "linear_tc_planes", "linear_tc_resid", "linear_tc_gated", "linear_tc_qkv"}};
   cudaError_t err = cudaSuccess;
   if (tc) {
     TcMaps maps;
@@ -590,11 +723,11 @@ cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t stream) {
     if (!ok) {
       tc = false;
     } else {
-      const int ntn = gated ? (N + BN / 2 - 1) / (BN / 2) : (N + BN - 1) / BN;
-      dim3 grid(ntn, (unsigned)((a.M + BM - 1) / BM));
+      p.tiles_n = gated ? (N + BN / 2 - 1) / (BN / 2) : (N + BN - 1) / BN;
+      p.tiles = p.tiles_n * (int)((a.M + BM - 1) / BM);
+      const int grid = std::min(p.tiles, sm_count());
       ProfScope prof(names[1][(int)a.epi], stream, 2.0 * Mx * nw * Kx, 2.0 * Mx * Kx + nw * Kx + out_bytes);
-      err = (a.K <= 2 * BK) ? launch_tc_epi<2>(a.epi, maps, p, grid, stream)
-                            : launch_tc_epi<4>(a.epi, maps, p, grid, stream);
+      err = launch_tc_epi(a.epi, maps, p, grid, stream);
     }
   }
   if (!tc) {

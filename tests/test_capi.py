@@ -47,7 +47,8 @@ def test_workspace_sizes_are_consistent(lib):
     assert lib.nsrl_linear_workspace_size(4096, 1024, 1024) == 2 * 4096 * 1024 + 4096 * 8
     T, d, H, F = 64 * 1024, 256, 4, 1024
     a = lib.nsrl_attention_workspace_size(64, 1024, d, H)
-    assert a == T * d * 2 + T * 8 + T * 3 * d * 2 + T * d * 2 + T * 8
+    # + transposed V planes (2 bytes / element) for the tensor-core attention (head_dim 64)
+    assert a == T * d * 2 + T * 8 + T * 3 * d * 2 + T * d * 2 + T * 8 + T * d * 2
     assert lib.nsrl_transformer_block_workspace_size(64, 1024, d, H, F) >= a + T * d * 2
 
 

@@ -133,6 +133,11 @@ def attn_weights(core, d, seed, qk_extra=7, qk_shift=None):
     (1, 40, 16, 4, True, 2),       # head_dim 4: row-kernel path
     (1, 24, 256, 1, True, 9),      # head_dim 256: row-kernel path
     (1, 1, 64, 1, True, 7),        # one token
+    (2, 48, 128, 2, True, 7),      # tensor-core path: one partial key tile
+    (1, 144, 256, 4, True, 7),     # tensor-core path: ragged query and key tiles
+    (2, 128, 128, 2, False, 5),    # tensor-core path, full attention
+    (1, 1024, 256, 4, True, 7),    # tensor-core path at the benchmark length
+    (1, 320, 64, 1, True, 0),      # tensor-core path, peaked softmax, one head
 ])
 def test_self_attention_parity(core, B, S, d, H, causal, qk_extra):
     P = attn_weights(core, d, 100 + d + H, qk_extra)
