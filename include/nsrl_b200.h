@@ -88,6 +88,22 @@ nsrl_status nsrl_linear_i16_i8_i16(const int16_t* x, size_t rows, const nsrl_lin
                                    void* workspace, size_t workspace_bytes, nsrl_device_status* status,
                                    void* stream);
 
+/* The same linear for callers that cannot allocate device memory.  No
+ * counterpart in the reference.  It takes no workspace: it uses a static
+ * device scratch array of nsrl_linear_noalloc_scratch_bytes() (16 MiB) that
+ * every GPU loading the library holds until exit.  Callers that need it:
+ * shims that keep nsrl-core's workspace-free slice signature, and host paths
+ * that must not call cudaMalloc / cudaFree (those can synchronise the device,
+ * or fail under a memory budget owned by another allocator).  Shapes whose
+ * nsrl_linear_workspace_size() exceeds the scratch are rejected with
+ * NSRL_INVALID_SHAPE and a message.  The first call on a device looks up the
+ * scratch address (cudaGetSymbolAddress) and should come before any stream
+ * capture.  All calls share the scratch: calls that overlap on the GPU race
+ * and must be serialised by the caller. */
+size_t nsrl_linear_noalloc_scratch_bytes(void);
+nsrl_status nsrl_linear_i16_i8_i16_noalloc(const int16_t* x, size_t rows, const nsrl_linear_params* params,
+                                           int16_t* y, nsrl_device_status* status, void* stream);
+
 /* --------------------------------------------------------------- rms norm --
  * y[r] = rms_norm_i16_q15_checked(x[r], gamma, eps) for r < rows.
  * Replaces crates/nsrl-core/src/rms_norm.rs:68-89 batched over rows. */
