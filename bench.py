@@ -182,7 +182,7 @@ def kernel_table(core_lib):
     return n, rows
 
 
-TENSOR_KERNELS = ("linear_tc", "attention_prefill")
+TENSOR_KERNELS = ("linear_tc", "attention_prefill", "attention_tc")
 
 
 def roofline(rows, hbm_gbs, tflops, src):

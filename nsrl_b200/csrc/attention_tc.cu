@@ -4,13 +4,13 @@
 // Reference: crates/nsrl-core/src/attention.rs:742-877 (full attention),
 // :261-293 (base-2 softmax), :117-140 (QK dot), :596-668 (AV).
 //
-// One CTA per (128-query tile, head, sequence); 10 warps:
+// One CTA per (128-query tile, head, sequence); 18 warps:
 //   warp 0      TMA producer: Q planes once, then per 64-key tile the K planes
 //               (and in the last pass the transposed V planes)
 //   warp 1      TMEM allocator + single-thread MMA issuer
-//   warps 2..9  softmax: warp w owns query rows 32*(w%4) .. +31 (its TMEM lane
-//               quarter) and key columns [32*c, 32*c+32) of each key tile,
-//               c = (w-2)/4
+//   warps 2..17 softmax: warp w owns query rows 32*(w%4) .. +31 (its TMEM lane
+//               quarter) and key columns [16*g, 16*g+16) of each key tile,
+//               g = (w-2)/4
 // q.k = 65536*(qh.kh) + 256*(qh.kl + ql.kh) + ql.kl: each S tile (128 x 64)
 // is three s32 TMEM accumulators (hh, mid, ll), recombined in i64 by the
 // softmax warps.  The probabilities are rounded to Q15 with the reciprocal of
@@ -35,16 +35,19 @@ constexpr int PLANE_K = KT * HD;      // 4 KB
 constexpr int PLANE_V = HD * KT;      // 4 KB
 constexpr int STAGE_BYTES = 2 * PLANE_K + 2 * PLANE_V;
 constexpr int PLANE_P = QT * KT;      // 8 KB
-constexpr int SOFTMAX_WARPS = 8;
+constexpr int SOFTMAX_WARPS = 16;
 constexpr int THREADS = 64 + 32 * SOFTMAX_WARPS;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t S_HH = 0, S_MID = 64, S_LL = 128, O_HH = 256, O_MID = 320, O_LL = 384;
+// Bound on |256 * mid + ll| of one 64-dim dot product: |mid| <= 64 * 2 * 128 * 255,
+// 0 <= ll <= 64 * 255 * 255.
+constexpr long long B_MID = 64LL * 2 * 128 * 255 * 256 + 64LL * 255 * 255;
 
 constexpr int OFF_Q = 0;
 constexpr int OFF_STAGE = OFF_Q + 2 * PLANE_Q;
 constexpr int OFF_P = OFF_STAGE + ST * STAGE_BYTES;
 constexpr int OFF_X = OFF_P + 2 * 2 * PLANE_P;  // row-statistics exchange
-constexpr int X_BYTES = 2 * QT * 8 * 3;
+constexpr int X_BYTES = 4 * QT * 8 * 3;
 constexpr int OFF_LUT = OFF_X + X_BYTES;
 constexpr int OFF_BAR = OFF_LUT + 512;
 constexpr size_t SMEM_BYTES = OFF_BAR + 256 + 1024;
@@ -90,9 +93,9 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Ctl* ctl = reinterpret_cast<Ctl*>(sm + OFF_BAR);
   int16_t* lut = reinterpret_cast<int16_t*>(sm + OFF_LUT);
-  long long* xmax = reinterpret_cast<long long*>(sm + OFF_X);  // [2][QT]
-  long long* xmin = xmax + 2 * QT;                             // [2][QT]
-  unsigned long long* xsum = reinterpret_cast<unsigned long long*>(xmin + 2 * QT);
+  long long* xmax = reinterpret_cast<long long*>(sm + OFF_X);  // [4][QT]
+  long long* xmin = xmax + 4 * QT;                             // [4][QT]
+  unsigned long long* xsum = reinterpret_cast<unsigned long long*>(xmin + 4 * QT);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q0 = blockIdx.x * QT, h = blockIdx.y, b = blockIdx.z;
@@ -229,112 +232,159 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
     }
   } else {
     // -------------------------------------------------------------- softmax
-    const int q = warp & 3, ch = (warp - 2) >> 2;
+    // Warp w owns query rows 32*(w%4)..+31 and key columns [16*g, 16*g+16)
+    // of each 64-key tile, g = (w-2)/4.
+    const int q = warp & 3, g = (warp - 2) >> 2;
     const int row = q * 32 + lane;
     const int qi = q0 + row;
     const bool row_live = qi < S;
     const int last_key = row_live ? (a.causal ? min(qi, S - 1) : S - 1) : -1;
     const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16);
-    const int shift = a.shift;
-    long long rawmax = LLONG_MIN, rawmin = LLONG_MAX;
-    long long lgmax = 0;
+    // Pass 0 keeps the row max / min of the raw dot product.  With head_dim 64
+    // |256*mid + ll| <= B_MID (< 2^30), so raw = 65536*hh + 256*mid + ll is
+    // an exact i32 whenever |hh| <= 16384; other elements take an i64 path.
+    int mx32 = INT_MIN, mn32 = INT_MAX;
+    long long mx64 = LLONG_MIN, mn64 = LLONG_MAX;
+    // Per-row constants of passes 1 and 2 (see the element loop).
+    uint32_t rawmax_lo = 0, cround = 0;
+    int hh_floor = INT_MAX;
+    bool slow_row = false;
+    long long rawmax = 0, lgmax = 0;
     unsigned long long rsum = 0;
     uint32_t inv = 0;
     uint32_t u = 0;
     bool range_bad = false, masked_bad = false;
     for (int pass = 0; pass < 3; ++pass) {
       for (int j = 0; j < ntiles; ++j, ++u) {
-        uint32_t hh[32], mid[32], ll[32];
+        uint32_t hh[16], mid[16], ll[16];
         wait_bar(&ctl->s_full, u & 1, ctl, a.st);
         tc_fence_after();
-        tmem_ld32(trow + S_HH + 32 * ch, hh);
-        tmem_ld32(trow + S_MID + 32 * ch, mid);
-        tmem_ld32(trow + S_LL + 32 * ch, ll);
+        tmem_ld16(trow + S_HH + 16 * g, hh);
+        tmem_ld16(trow + S_MID + 16 * g, mid);
+        tmem_ld16(trow + S_LL + 16 * g, ll);
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&ctl->s_empty);
-        const int key0 = j * KT + 32 * ch;
-        const int nlive = max(0, min(32, last_key - key0 + 1));
+        const int key0 = j * KT + 16 * g;
+        const int nlive = max(0, min(16, last_key - key0 + 1));
         if (pass == 0) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
+          for (int i = 0; i < 16; ++i) {
+            if (i < nlive) {
+              const int h = (int)hh[i];
+              if ((unsigned)(h + 16384) <= 32768u) {
+                const int r32 = (int)((uint32_t)h * 65536u + mid[i] * 256u + ll[i]);
+                mx32 = max(mx32, r32);
+                mn32 = min(mn32, r32);
+              } else {
+                const long long raw = (long long)h * 65536 + (long long)(int)mid[i] * 256 + (long long)(int)ll[i];
+                mx64 = max(mx64, raw);
+                mn64 = min(mn64, raw);
+              }
+            }
+          }
+          continue;
+        }
+        int w[16];
+        if (!slow_row) {
+          // w != 0 needs mag = lgmax - lg < 3840, i.e. raw > rawmax - 30720;
+          // that needs hh > hh_floor, and then rawmax - raw < 2^32, so the
+          // difference is exact in u32.  mag = (diff + cround) >> 3.
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            int wi = 0;
+            if (i < nlive && (int)hh[i] > hh_floor) {
+              const uint32_t raw_lo = hh[i] * 65536u + mid[i] * 256u + ll[i];
+              const uint32_t diff = rawmax_lo - raw_lo;
+              if (diff < 30720u - cround) {
+                const uint32_t mag = (diff + cround) >> 3;
+                wi = (int)lut[mag & 255u] >> (mag >> 8);
+              }
+            }
+            w[i] = wi;
+          }
+        } else {
+          // Rows whose max logit lies within 15 * 256 of i32::MIN: exact i64
+          // path, with logits equal to MASKED_LOGIT excluded (attention.rs:266-276).
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            int wi = 0;
             if (i < nlive) {
               const long long raw =
                   (long long)(int)hh[i] * 65536 + (long long)(int)mid[i] * 256 + (long long)(int)ll[i];
-              rawmax = max(rawmax, raw);
-              rawmin = min(rawmin, raw);
-            }
-          }
-        } else {
-          uint32_t pw[16];
-#pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            int w2[2];
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              int w = 0;
-              if (i + e < nlive) {
-                const long long raw = (long long)(int)hh[i + e] * 65536 + (long long)(int)mid[i + e] * 256 +
-                                      (long long)(int)ll[i + e];
-                const long long lg = raw >> shift;
-                const long long delta = lg - lgmax;  // <= 0
-                if (delta > -15 * 256 && lg != (long long)INT_MIN) {
-                  const int mag = (int)(-delta);
-                  w = (int)lut[mag & 255] >> (mag >> 8);
-                }
+              const long long lg = raw >> 3;
+              const long long delta = lg - lgmax;
+              if (delta > -15 * 256 && lg != (long long)INT_MIN) {
+                const int mag = (int)(-delta);
+                wi = (int)lut[mag & 255] >> (mag >> 8);
               }
-              w2[e] = w;
             }
-            if (pass == 1) {
-              rsum += (unsigned)(w2[0] + w2[1]);
-            } else {
-              // p = sat_i16(rhu(w * inv, 16)); w * inv < 2^47
-              const int p0 = (int)min(32767ull, ((unsigned long long)w2[0] * inv + 32768ull) >> 16);
-              const int p1 = (int)min(32767ull, ((unsigned long long)w2[1] * inv + 32768ull) >> 16);
-              pw[i / 2] = (uint32_t)p0 | ((uint32_t)p1 << 16);
-            }
-          }
-          if (pass == 2) {
-            const int pb = j & 1;
-            if (j >= 2) wait_bar(&ctl->p_empty[pb], ((j >> 1) - 1) & 1, ctl, a.st);
-            uint8_t* ph = sm + OFF_P + pb * 2 * PLANE_P;
-            uint8_t* pl = ph + PLANE_P;
-#pragma unroll
-            for (int c2 = 0; c2 < 2; ++c2) {
-              uint32_t hw[4], lw[4];
-#pragma unroll
-              for (int k = 0; k < 4; ++k) {
-                const uint32_t x0 = pw[8 * c2 + 2 * k], x1 = pw[8 * c2 + 2 * k + 1];
-                hw[k] = __byte_perm(x0, x1, 0x7531);
-                lw[k] = __byte_perm(x0, x1, 0x6420);
-              }
-              const uint32_t off = swz64_chunk((uint32_t)row, (uint32_t)(2 * ch + c2));
-              *reinterpret_cast<uint4*>(ph + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-              *reinterpret_cast<uint4*>(pl + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-            }
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&ctl->p_full[pb]);
+            w[i] = wi;
           }
         }
+        if (pass == 1) {
+          unsigned s = 0;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) s += (unsigned)w[i];
+          rsum += s;
+          continue;
+        }
+        // pass 2: p = sat_i16(rhu(w * inv, 16)), w * inv < 2^47
+        uint32_t pw[8];
+#pragma unroll
+        for (int i = 0; i < 16; i += 2) {
+          const uint32_t p0 = (uint32_t)min(32767ull, ((unsigned long long)(uint32_t)w[i] * inv + 32768ull) >> 16);
+          const uint32_t p1 =
+              (uint32_t)min(32767ull, ((unsigned long long)(uint32_t)w[i + 1] * inv + 32768ull) >> 16);
+          pw[i / 2] = p0 | (p1 << 16);
+        }
+        const int pb = j & 1;
+        if (j >= 2) wait_bar(&ctl->p_empty[pb], ((j >> 1) - 1) & 1, ctl, a.st);
+        uint8_t* ph = sm + OFF_P + pb * 2 * PLANE_P;
+        uint8_t* pl = ph + PLANE_P;
+        uint32_t hw[4], lw[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          hw[k] = __byte_perm(pw[2 * k], pw[2 * k + 1], 0x7531);
+          lw[k] = __byte_perm(pw[2 * k], pw[2 * k + 1], 0x6420);
+        }
+        const uint32_t off = swz64_chunk((uint32_t)row, (uint32_t)g);
+        *reinterpret_cast<uint4*>(ph + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        *reinterpret_cast<uint4*>(pl + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ctl->p_full[pb]);
       }
       if (pass == 0) {
-        xmax[ch * QT + row] = rawmax;
-        xmin[ch * QT + row] = rawmin;
+        long long rmx = max((long long)mx32 == INT_MIN && mx64 != LLONG_MIN ? LLONG_MIN : (long long)mx32, mx64);
+        long long rmn = min((long long)mn32 == INT_MAX && mn64 != LLONG_MAX ? LLONG_MAX : (long long)mn32, mn64);
+        xmax[g * QT + row] = rmx;
+        xmin[g * QT + row] = rmn;
         named_sync_softmax();
-        rawmax = max(rawmax, xmax[(1 - ch) * QT + row]);
-        rawmin = min(rawmin, xmin[(1 - ch) * QT + row]);
+#pragma unroll
+        for (int o = 1; o < 4; ++o) {
+          rmx = max(rmx, xmax[((g + o) & 3) * QT + row]);
+          rmn = min(rmn, xmin[((g + o) & 3) * QT + row]);
+        }
         if (row_live) {
-          lgmax = rawmax >> shift;
-          const long long lgmin = rawmin >> shift;
+          rawmax = rmx;
+          lgmax = rawmax >> 3;
+          const long long lgmin = rmn >> 3;
           if (lgmax > INT_MAX || lgmin < INT_MIN) range_bad = true;
           if (lgmax <= (long long)INT_MIN) masked_bad = true;  // every live logit masked or out of range
+          slow_row = lgmax < (long long)INT_MIN + 15 * 256;
+          rawmax_lo = (uint32_t)rawmax;
+          cround = 7u - (uint32_t)(rawmax & 7);
+          // candidates for w != 0: 65536*hh + B_MID > rawmax - 30720
+          const long long fl = (rawmax - 30720 - B_MID) >> 16;
+          hh_floor = (int)max((long long)INT_MIN, min((long long)INT_MAX, fl));
         }
       } else if (pass == 1) {
-        xsum[ch * QT + row] = rsum;
+        xsum[g * QT + row] = rsum;
         named_sync_softmax();
-        rsum += xsum[(1 - ch) * QT + row];
+#pragma unroll
+        for (int o = 1; o < 4; ++o) rsum += xsum[((g + o) & 3) * QT + row];
         inv = (row_live && rsum) ? recip_sum_q31(rsum) : 0u;
       }
     }
@@ -343,16 +393,16 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
     // ---- context: sat(rhu(65536*hh + 256*mid + ll, 15)) as byte planes ----
     wait_bar(&ctl->o_full, 0, ctl, a.st);
     tc_fence_after();
-    uint32_t oh[32], om[32], ol[32];
-    tmem_ld32(trow + O_HH + 32 * ch, oh);
-    tmem_ld32(trow + O_MID + 32 * ch, om);
-    tmem_ld32(trow + O_LL + 32 * ch, ol);
+    uint32_t oh[16], om[16], ol[16];
+    tmem_ld16(trow + O_HH + 16 * g, oh);
+    tmem_ld16(trow + O_MID + 16 * g, om);
+    tmem_ld16(trow + O_LL + 16 * g, ol);
     tmem_wait_ld();
     if (row_live) {
-      uint32_t hw[8], lw[8];
+      uint32_t hw[4], lw[4];
       unsigned long long l1 = 0;
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
+      for (int k = 0; k < 4; ++k) {
         uint32_t hv = 0, lv = 0;
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -366,13 +416,9 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
         hw[k] = hv;
         lw[k] = lv;
       }
-      const long long off = (long long)(row0 + qi) * a.ldc + h * HD + 32 * ch;
-      uint4* dh = reinterpret_cast<uint4*>(a.ctx_hi + off);
-      uint4* dl = reinterpret_cast<uint4*>(a.ctx_lo + off);
-      dh[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-      dh[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
-      dl[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-      dl[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
+      const long long off = (long long)(row0 + qi) * a.ldc + h * HD + 16 * g;
+      *reinterpret_cast<uint4*>(a.ctx_hi + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+      *reinterpret_cast<uint4*>(a.ctx_lo + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
       if (a.ctx_l1) atomicAdd(&a.ctx_l1[row0 + qi], l1);
     }
   }

@@ -57,12 +57,13 @@ __device__ __forceinline__ int16_t requant_i32(int acc, int mult, uint32_t shift
   return sat_i16(rhu64((long long)acc * (long long)mult, shift));
 }
 
-// mlp.rs:150-170: hard-SiLU gate and the gated activation.
+// mlp.rs:150-170: hard-SiLU gate and the gated activation.  Both products are
+// below 2^30 in magnitude, so rhu(v, 15) = (v + 2^14) >> 15 in i32 is exact.
 __device__ __forceinline__ int16_t gated_act(int16_t up, int16_t gate) {
   int g = ((int)gate >> 2) + 16384;
   g = max(0, min(32767, g));
-  int16_t silu = sat_i16(rhu64((long long)gate * g, 15));
-  return sat_i16(rhu64((long long)up * silu, 15));
+  const int silu = max(-32768, min(32767, ((int)gate * g + 16384) >> 15));
+  return (int16_t)max(-32768, min(32767, ((int)up * silu + 16384) >> 15));
 }
 
 // attention.rs:142-158 with the table in shared memory.
@@ -214,6 +215,17 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
         "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
         "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+
+// 32 lanes x 16 consecutive 32-bit columns.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr)
       : "memory");
 }

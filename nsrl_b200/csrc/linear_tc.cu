@@ -15,12 +15,12 @@
 // prefix_check_kernel rescan those rows in reference order and reject the
 // call (linear.rs:144-173, :282-296).
 //
-// Persistent kernel, one CTA per SM, 10 warps:
+// Persistent kernel, one CTA per SM, 18 warps:
 //   warp 0      TMA producer: A hi/lo planes + W tile per 128-wide K block,
 //               through a 4-stage shared-memory ring
 //   warp 1      TMEM allocator + single-thread MMA issuer
-//   warps 2..9  epilogue: TMEM -> registers -> requant -> global; two warps
-//               per TMEM lane quarter, 64 columns each
+//   warps 2..17 epilogue: TMEM -> registers -> requant -> global; four
+//               warps per TMEM lane quarter, 32 columns each
 // The two accumulator pairs (hi, lo) of a 128 x 128 tile take 256 TMEM
 // columns; two tiles are in flight (512 columns) so that the epilogue of
 // tile i overlaps the MMAs of tile i+1.  Operand tiles are K-major with the
@@ -41,8 +41,8 @@ constexpr int STAGE_BYTES = 2 * TILE_A + TILE_B;  // 48 KB
 constexpr int STAGES = 4;
 constexpr int ACC_COLS = 2 * BN;                  // acc_hi: [0,128), acc_lo: [128,256)
 constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;      // two tiles in flight
-constexpr int EPI_WARPS = 8;
-constexpr int THREADS = 64 + 32 * EPI_WARPS;      // 320
+constexpr int EPI_WARPS = 16;
+constexpr int THREADS = 64 + 32 * EPI_WARPS;      // 576
 constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE_BYTES + 1024 + 256;
 
 struct TcMaps {
@@ -85,25 +85,100 @@ __device__ __forceinline__ int requant_fast(int acc, int mult, uint32_t shift) {
 
 __device__ __forceinline__ uint32_t pack2(int a, int b) { return (uint32_t)(a & 0xFFFF) | ((uint32_t)b << 16); }
 
-// Requantised outputs of 32 consecutive columns as 16 packed int16 pairs.
-__device__ __forceinline__ void finish32(const uint32_t (&h)[32], const uint32_t (&l)[32], const int32_t* bias,
-                                         const nsrl_fixed_scale* sc, int n0, int nvalid, uint32_t (&o)[16]) {
+// Per-lane copy of the scale (and bias) of column `lane` of a chunk, plus a
+// warp-uniform flag for the common case: every valid column has multiplier 1,
+// one shared right shift and no bias.  Lanes past the valid columns hold an
+// identity scale.
+struct ColScale {
+  int mult, shift, bias;
+  int ushift;
+  bool uniform;
+};
+
+__device__ __forceinline__ ColScale load_scales(const nsrl_fixed_scale* sc, const int32_t* bias, int n, bool valid) {
+  ColScale c;
+  c.mult = 1;
+  c.shift = 0;
+  c.bias = 0;
+  if (valid) {
+    const nsrl_fixed_scale s = sc[n];
+    c.mult = s.multiplier;
+    c.shift = s.right_shift;
+    c.bias = bias ? bias[n] : 0;
+  }
+  c.ushift = __shfl_sync(0xffffffffu, c.shift, 0);
+  c.uniform = __all_sync(0xffffffffu, !valid || (c.mult == 1 && c.shift == c.ushift && c.bias == 0)) != 0;
+  return c;
+}
+
+// requantize_i32_to_i16 of W columns: acc = 256*hi + lo (+ bias), wrapping
+// u32 arithmetic (exact whenever the true i32 sum fits).
+template <int W>
+__device__ __forceinline__ void requant_cols(const uint32_t (&h)[W], const uint32_t (&l)[W], const ColScale& c,
+                                             int (&v)[W]) {
+  if (c.uniform) {
+    const uint32_t s = (uint32_t)c.ushift;
+    if (s == 0) {
 #pragma unroll
-  for (int i = 0; i < 32; i += 2) {
-    int v[2];
+      for (int i = 0; i < W; ++i) v[i] = max(-32768, min(32767, (int)(h[i] * 256u + l[i])));
+    } else if (s < 32) {
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const int n = n0 + i + j;
-      int r = 0;
-      if (i + j < nvalid) {
-        // wrapping u32 arithmetic: exact whenever the true i32 sum fits
-        const int acc = (int)(h[i + j] * 256u + l[i + j] + (bias ? (uint32_t)bias[n] : 0u));
-        const nsrl_fixed_scale s = sc[n];
-        r = requant_fast(acc, s.multiplier, s.right_shift);
+      for (int i = 0; i < W; ++i) {
+        const int acc = (int)(h[i] * 256u + l[i]);
+        v[i] = max(-32768, min(32767, (acc >> s) + ((acc >> (s - 1)) & 1)));
       }
-      v[j] = r;
+    } else {
+#pragma unroll
+      for (int i = 0; i < W; ++i) v[i] = (int)sat_i16(rhu64((long long)(int)(h[i] * 256u + l[i]), s));
     }
-    o[i / 2] = pack2(v[0], v[1]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < W; ++i) {
+      const int mult = __shfl_sync(0xffffffffu, c.mult, i);
+      const int shift = __shfl_sync(0xffffffffu, c.shift, i);
+      const int b = __shfl_sync(0xffffffffu, c.bias, i);
+      v[i] = requant_fast((int)(h[i] * 256u + l[i] + (uint32_t)b), mult, (uint32_t)shift);
+    }
+  }
+}
+__device__ __forceinline__ void requant32(const uint32_t (&h)[32], const uint32_t (&l)[32], const ColScale& c,
+                                          int (&v)[32]) {
+  requant_cols<32>(h, l, c, v);
+}
+__device__ __forceinline__ void requant16(const uint32_t (&h)[16], const uint32_t (&l)[16], const ColScale& c,
+                                          int (&v)[16]) {
+  requant_cols<16>(h, l, c, v);
+}
+
+// Splits 16 packed int16 values into hi / lo byte planes (+ L1 of the values).
+__device__ __forceinline__ void store16_planes(int8_t* dh, uint8_t* dl, const uint32_t (&o)[8], int nvalid,
+                                               bool vec_ok, unsigned long long& l1) {
+  uint32_t hw[4], lw[4];
+  unsigned acc = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t a = o[2 * i], b = o[2 * i + 1];
+    hw[i] = __byte_perm(a, b, 0x7531);
+    lw[i] = __byte_perm(a, b, 0x6420);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int v = (int16_t)(((j < 2) ? a : b) >> (16 * (j & 1)));
+      if (4 * i + j < nvalid) acc += (unsigned)abs(v);
+    }
+  }
+  l1 += acc;
+  if (vec_ok && nvalid == 16) {
+    *reinterpret_cast<uint4*>(dh) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    *reinterpret_cast<uint4*>(dl) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      if (i < nvalid) {
+        const int v = (int16_t)(o[i / 2] >> (16 * (i & 1)));
+        dh[i] = (int8_t)(v >> 8);
+        dl[i] = (uint8_t)(v & 255);
+      }
+    }
   }
 }
 
@@ -266,102 +341,103 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
       }
     }
   } else {
-    // Epilogue: warp w reads TMEM lanes [32*(w%4), 32*(w%4)+32); warps
-    // 2..5 take columns [0, 64) of the tile, warps 6..9 columns [64, 128).
+    // Epilogue: warp w reads TMEM lanes [32*(w%4), 32*(w%4)+32) and owns
+    // column group cg = (w-2)/4 of the tile: columns [32*cg, 32*cg+32), or
+    // for the gated form up channels [16*cg, +16) with their gate channels.
     const int q = warp & 3;
-    const int chalf = (warp - 2) >> 2;
+    const int cg = (warp - 2) >> 2;
     uint32_t local = 0;
     unsigned long long sat = 0;
     for (int t = blockIdx.x; t < p.tiles; t += gridDim.x, ++local) {
       const uint32_t buf = local & 1, use = local >> 1;
-      if (!mbar_wait(&acc_full[buf], use & 1, p.st)) break;
-      tc_fence_after();
       const int m0 = (t / p.tiles_n) * BM, nt = t % p.tiles_n;
       const int r = m0 + q * 32 + lane;
       const bool row_ok = r < p.M;
       const uint32_t lrow = tmem + buf * ACC_COLS + ((uint32_t)(q * 32) << 16);
       unsigned long long l1 = 0;
       if (EPI == (int)Epi::GATED) {
-        // tile columns [0,64): up channels f0..f0+63, [64,128): gate channels
-        const int fb = nt * (BN / 2) + 32 * chalf;
-        const int nvalid = max(0, min(32, p.N - fb));
-        uint32_t h[32], l[32], up[16], gt[16];
-        tmem_ld32(lrow + 32 * chalf, h);
-        tmem_ld32(lrow + BN + 32 * chalf, l);
-        tmem_wait_ld();
-        finish32(h, l, p.bias[0], p.scales[0], fb, nvalid, up);
-        tmem_ld32(lrow + 64 + 32 * chalf, h);
-        tmem_ld32(lrow + BN + 64 + 32 * chalf, l);
+        const int fb = nt * (BN / 2) + 16 * cg;
+        const int nvalid = max(0, min(16, p.N - fb));
+        const ColScale su = load_scales(p.scales[0], p.bias[0], fb + (lane & 15), (lane & 15) < nvalid);
+        const ColScale sg = load_scales(p.scales[1], p.bias[1], fb + (lane & 15), (lane & 15) < nvalid);
+        uint32_t hu[16], lu[16], hg[16], lg[16];
+        if (!mbar_wait(&acc_full[buf], use & 1, p.st)) break;
+        tc_fence_after();
+        tmem_ld16(lrow + 16 * cg, hu);
+        tmem_ld16(lrow + BN + 16 * cg, lu);
+        tmem_ld16(lrow + 64 + 16 * cg, hg);
+        tmem_ld16(lrow + BN + 64 + 16 * cg, lg);
         tmem_wait_ld();
         tc_fence_before();
         if (lane == 0) mbar_arrive(&acc_empty[buf]);
-        finish32(h, l, p.bias[1], p.scales[1], fb, nvalid, gt);
-        uint32_t o[16];
+        int up[16], gt[16];
+        requant16(hu, lu, su, up);
+        requant16(hg, lg, sg, gt);
+        uint32_t o[8];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int a = gated_act((int16_t)(up[i] & 0xFFFF), (int16_t)(gt[i] & 0xFFFF));
-          const int b = gated_act((int16_t)(up[i] >> 16), (int16_t)(gt[i] >> 16));
-          o[i] = pack2(a, b);
-        }
+        for (int i = 0; i < 8; ++i)
+          o[i] = pack2(gated_act((int16_t)up[2 * i], (int16_t)gt[2 * i]),
+                       gated_act((int16_t)up[2 * i + 1], (int16_t)gt[2 * i + 1]));
         if (row_ok && nvalid > 0) {
           const long long off = (long long)r * p.ldp + fb;
-          store32_planes(p.yh + off, p.yl + off, o, nvalid, ((p.ldp | fb) & 15) == 0, l1);
+          store16_planes(p.yh + off, p.yl + off, o, nvalid, ((p.ldp | fb) & 15) == 0, l1);
         }
       } else {
         const int nb = nt * BN;
         const int sseg = (p.nseg == 3) ? nb / p.seg_rows : 0;
-        const int nloc0 = (p.nseg == 3) ? nb % p.seg_rows : nb;
-        const int32_t* bias = p.bias[sseg];
-        const nsrl_fixed_scale* sc = p.scales[sseg];
-        uint32_t h[2][32], l[2][32];
+        const int nloc = ((p.nseg == 3) ? nb % p.seg_rows : nb) + 32 * cg;
+        const int n = nb + 32 * cg;
+        const int nvalid = max(0, min(32, p.N - n));
+        const ColScale sc = load_scales(p.scales[sseg], p.bias[sseg], nloc + lane, lane < nvalid);
+        // The residual rows do not depend on the accumulator: fetch them first.
+        uint32_t s16[16];
+        const bool vec_skip = EPI == (int)Epi::RESID && ((p.ldskip | p.ldy | n) & 7) == 0 && nvalid == 32;
+        if (EPI == (int)Epi::RESID && row_ok && nvalid > 0) {
+          const int16_t* sk = p.skip + (long long)r * p.ldskip + n;
+          if (vec_skip) {
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          tmem_ld32(lrow + 64 * chalf + 32 * c, h[c]);
-          tmem_ld32(lrow + BN + 64 * chalf + 32 * c, l[c]);
+            for (int i = 0; i < 4; ++i) {
+              const uint4 v = reinterpret_cast<const uint4*>(sk)[i];
+              s16[4 * i] = v.x;
+              s16[4 * i + 1] = v.y;
+              s16[4 * i + 2] = v.z;
+              s16[4 * i + 3] = v.w;
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int a = (2 * i < nvalid) ? (int)sk[2 * i] : 0;
+              const int b = (2 * i + 1 < nvalid) ? (int)sk[2 * i + 1] : 0;
+              s16[i] = pack2(a, b);
+            }
+          }
         }
+        uint32_t h[32], l[32];
+        if (!mbar_wait(&acc_full[buf], use & 1, p.st)) break;
+        tc_fence_after();
+        tmem_ld32(lrow + 32 * cg, h);
+        tmem_ld32(lrow + BN + 32 * cg, l);
         tmem_wait_ld();
         tc_fence_before();
         if (lane == 0) mbar_arrive(&acc_empty[buf]);
+        int v[32];
+        requant32(h, l, sc, v);
+        uint32_t o[16];
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          const int cn = 64 * chalf + 32 * c;
-          const int n = nb + cn;
-          const int nvalid = max(0, min(32, p.N - n));
-          uint32_t o[16];
-          finish32(h[c], l[c], bias, sc, nloc0 + cn, nvalid, o);
-          if (!row_ok || nvalid == 0) continue;
+        for (int i = 0; i < 16; ++i) o[i] = pack2(v[2 * i], v[2 * i + 1]);
+        if (row_ok && nvalid > 0) {
           if (EPI == (int)Epi::I16) {
             store32_i16(p.y + (long long)r * p.ldy + n, o, nvalid, ((p.ldy | n) & 7) == 0);
           } else if (EPI == (int)Epi::RESID) {
-            const int16_t* sk = p.skip + (long long)r * p.ldskip + n;
-            const bool vec = ((p.ldskip | p.ldy | n) & 7) == 0 && nvalid == 32;
-            uint32_t s16[16];
-            if (vec) {
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const uint4 u = reinterpret_cast<const uint4*>(sk)[i];
-                s16[4 * i] = u.x;
-                s16[4 * i + 1] = u.y;
-                s16[4 * i + 2] = u.z;
-                s16[4 * i + 3] = u.w;
-              }
-            } else {
-#pragma unroll
-              for (int i = 0; i < 16; ++i) {
-                const int a = (2 * i < nvalid) ? (int)sk[2 * i] : 0;
-                const int b = (2 * i + 1 < nvalid) ? (int)sk[2 * i + 1] : 0;
-                s16[i] = pack2(a, b);
-              }
-            }
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
-              const int a = (int)(int16_t)(s16[i] & 0xFFFF) + (int)(int16_t)(o[i] & 0xFFFF);
-              const int b = (int)(int16_t)(s16[i] >> 16) + (int)(int16_t)(o[i] >> 16);
+              const int a = (int)(int16_t)(s16[i] & 0xFFFF) + v[2 * i];
+              const int b = (int)(int16_t)(s16[i] >> 16) + v[2 * i + 1];
               if (2 * i < nvalid && (a < -32768 || a > 32767)) ++sat;
               if (2 * i + 1 < nvalid && (b < -32768 || b > 32767)) ++sat;
               o[i] = pack2(max(-32768, min(32767, a)), max(-32768, min(32767, b)));
             }
-            store32_i16(p.y + (long long)r * p.ldy + n, o, nvalid, vec);
+            store32_i16(p.y + (long long)r * p.ldy + n, o, nvalid, vec_skip);
           } else if (EPI == (int)Epi::QKV_VT && n >= p.vt_col0) {
             // v columns: byte stores into [b][h][dim][s]; the 32 lanes of the
             // warp hold 32 consecutive positions, so each store instruction
@@ -373,9 +449,8 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
               if (i < nvalid) {
                 const int c = c0 + i, hh = c / p.vt_hd, dd = c % p.vt_hd;
                 const long long off = ((long long)(b * p.vt_H + hh) * p.vt_hd + dd) * p.vt_S + spos;
-                const int v = (int16_t)(o[i / 2] >> (16 * (i & 1)));
-                p.vth[off] = (int8_t)(v >> 8);
-                p.vtl[off] = (uint8_t)(v & 255);
+                p.vth[off] = (int8_t)(v[i] >> 8);
+                p.vtl[off] = (uint8_t)(v[i] & 255);
               }
             }
           } else {
