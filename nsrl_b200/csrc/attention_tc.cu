@@ -20,7 +20,9 @@
 // K-major layout; O = P V uses three more s32 accumulators (65536*hh +
 // 256*mid + ll), exact for up to 16384 keys.
 //
-// TMEM (512 columns): S hh/mid/ll at [0,192), O hh/mid/ll at [256,448).
+// TMEM (512 columns): S hh/mid/ll at [0,192) and, in the max and sum passes,
+// a second S buffer at [256,448); O hh/mid/ll at [256,448) in the last pass
+// (the second S buffer is no longer used by then).
 // Operand tiles use the 64-byte swizzle (rows of 64 bytes), as TMA writes it.
 #include "common.cuh"
 #include "internal.h"
@@ -39,6 +41,7 @@ constexpr int SOFTMAX_WARPS = 16;
 constexpr int THREADS = 64 + 32 * SOFTMAX_WARPS;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t S_HH = 0, S_MID = 64, S_LL = 128, O_HH = 256, O_MID = 320, O_LL = 384;
+constexpr uint32_t S_BUF1 = 256;  // column offset of the second S buffer
 // Bound on |256 * mid + ll| of one 64-dim dot product: |mid| <= 64 * 2 * 128 * 255,
 // 0 <= ll <= 64 * 255 * 255.
 constexpr long long B_MID = 64LL * 2 * 128 * 255 * 256 + 64LL * 255 * 255;
@@ -75,7 +78,7 @@ __device__ __forceinline__ uint64_t sdesc_k64(uint32_t saddr) {
 __device__ __forceinline__ uint32_t swz64_chunk(uint32_t r, uint32_t c) { return r * 64u + ((c ^ ((r >> 1) & 3u)) << 4); }
 
 struct Ctl {
-  uint64_t q_full, full[ST], empty[ST], s_full, s_empty, p_full[2], p_empty[2], o_full;
+  uint64_t q_full, full[ST], empty[ST], s_full[2], s_empty[2], p_full[2], p_empty[2], o_full;
   uint32_t tslot, abort;
 };
 
@@ -87,6 +90,51 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, Ctl* c,
 }
 
 __device__ __forceinline__ void named_sync_softmax() { asm volatile("bar.sync 1, %0;" ::"n"(32 * SOFTMAX_WARPS)); }
+
+// Pass-0 update of one warp's 16 scores.  raw = 65536*hh + 256*mid + ll is an
+// exact i32 when |hh| <= 16384 (|256*mid + ll| <= B_MID < 2^30); then the
+// logit raw >> 3 is inside i32 too and only the max matters.  Larger |hh|
+// take the i64 path, which also keeps the min for the i32 range check.
+template <bool FULL>
+__device__ __forceinline__ void scores_max(const uint32_t (&hh)[16], const uint32_t (&mid)[16],
+                                           const uint32_t (&ll)[16], int nlive, int& mx32, long long& mx64,
+                                           long long& mn64) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    if (FULL || i < nlive) {
+      const int h = (int)hh[i];
+      if ((unsigned)(h + 16384) <= 32768u) {
+        mx32 = max(mx32, (int)((uint32_t)h * 65536u + mid[i] * 256u + ll[i]));
+      } else {
+        const long long raw = (long long)h * 65536 + (long long)(int)mid[i] * 256 + (long long)(int)ll[i];
+        mx64 = max(mx64, raw);
+        mn64 = min(mn64, raw);
+      }
+    }
+  }
+}
+
+// Base-2 weights w = LUT(lg - lgmax) (attention.rs:142-158) of 16 scores.  w
+// != 0 needs mag = lgmax - lg < 3840, i.e. raw > rawmax - 30720; that needs
+// hh > hh_floor, and then rawmax - raw < 2^32 is exact in u32, with
+// mag = (diff + cround) >> 3.
+template <bool FULL>
+__device__ __forceinline__ void scores_weight(const uint32_t (&hh)[16], const uint32_t (&mid)[16],
+                                              const uint32_t (&ll)[16], int nlive, int hh_floor, uint32_t rawmax_lo,
+                                              uint32_t cround, const int16_t* lut, int (&w)[16]) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    int wi = 0;
+    if ((FULL || i < nlive) && (int)hh[i] > hh_floor) {
+      const uint32_t diff = rawmax_lo - (hh[i] * 65536u + mid[i] * 256u + ll[i]);
+      if (diff < 30720u - cround) {
+        const uint32_t mag = (diff + cround) >> 3;
+        wi = (int)lut[mag & 255u] >> (mag >> 8);
+      }
+    }
+    w[i] = wi;
+  }
+}
 
 __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_constant__ Maps maps, const Args a) {
   extern __shared__ uint8_t smem_raw[];
@@ -114,8 +162,10 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
       mbar_init(&ctl->full[s], 1);
       mbar_init(&ctl->empty[s], 1);
     }
-    mbar_init(&ctl->s_full, 1);
-    mbar_init(&ctl->s_empty, SOFTMAX_WARPS);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&ctl->s_full[i], 1);
+      mbar_init(&ctl->s_empty[i], SOFTMAX_WARPS);
+    }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&ctl->p_full[i], SOFTMAX_WARPS);
       mbar_init(&ctl->p_empty[i], 1);
@@ -168,31 +218,36 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
       const uint32_t id_ss = idesc_i8(QT, KT, 1, 1), id_su = idesc_i8(QT, KT, 1, 0);
       const uint32_t id_us = idesc_i8(QT, KT, 0, 1), id_uu = idesc_i8(QT, KT, 0, 0);
       const uint32_t qh = smem_u32(sm + OFF_Q), ql = qh + PLANE_Q;
-      uint32_t u = 0;  // uses of the S accumulators
+      uint32_t use0 = 0, use1 = 0;  // uses of each S buffer
       wait_bar(&ctl->q_full, 0, ctl, a.st);
-      auto issue_s = [&](int s) {
-        if (u > 0) wait_bar(&ctl->s_empty, (u - 1) & 1, ctl, a.st);
+      auto issue_s = [&](int s, int sb) {
+        const uint32_t n = sb ? use1 : use0;
+        if (n > 0) wait_bar(&ctl->s_empty[sb], (n - 1) & 1, ctl, a.st);
         tc_fence_after();
         const uint32_t kh = smem_u32(sm + OFF_STAGE + s * STAGE_BYTES), kl = kh + PLANE_K;
+        const uint32_t d = tmem + (uint32_t)sb * S_BUF1;
 #pragma unroll
         for (int ks = 0; ks < HD / 32; ++ks) {
           const uint64_t aqh = sdesc_k64(qh + 32 * ks), aql = sdesc_k64(ql + 32 * ks);
           const uint64_t bkh = sdesc_k64(kh + 32 * ks), bkl = sdesc_k64(kl + 32 * ks);
           const uint32_t acc = ks > 0 ? 1u : 0u;
-          umma_i8(tmem + S_HH, aqh, bkh, id_ss, acc);
-          umma_i8(tmem + S_MID, aqh, bkl, id_su, acc);
-          umma_i8(tmem + S_MID, aql, bkh, id_us, 1u);
-          umma_i8(tmem + S_LL, aql, bkl, id_uu, acc);
+          umma_i8(d + S_HH, aqh, bkh, id_ss, acc);
+          umma_i8(d + S_MID, aqh, bkl, id_su, acc);
+          umma_i8(d + S_MID, aql, bkh, id_us, 1u);
+          umma_i8(d + S_LL, aql, bkl, id_uu, acc);
         }
-        umma_commit(&ctl->s_full);
-        ++u;
+        umma_commit(&ctl->s_full[sb]);
+        if (sb)
+          ++use1;
+        else
+          ++use0;
       };
       uint32_t it = 0;
       for (int pass = 0; pass < 2; ++pass) {
         for (int j = 0; j < ntiles; ++j, ++it) {
           const int s = it % ST;
           wait_bar(&ctl->full[s], (it / ST) & 1, ctl, a.st);
-          issue_s(s);
+          issue_s(s, (int)(it & 1));
           umma_commit(&ctl->empty[s]);
         }
       }
@@ -200,12 +255,12 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
       // warps can work on tile j+1 while the tensor core does the AV product.
       const uint32_t base = it;
       wait_bar(&ctl->full[base % ST], (base / ST) & 1, ctl, a.st);
-      issue_s(base % ST);
+      issue_s(base % ST, 0);
       for (int j = 0; j < ntiles; ++j) {
         if (j + 1 < ntiles) {
           const uint32_t n1 = base + j + 1;
           wait_bar(&ctl->full[n1 % ST], (n1 / ST) & 1, ctl, a.st);
-          issue_s(n1 % ST);
+          issue_s(n1 % ST, 0);
         }
         const int pb = j & 1;
         wait_bar(&ctl->p_full[pb], (j >> 1) & 1, ctl, a.st);
@@ -243,7 +298,7 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
     // Pass 0 keeps the row max / min of the raw dot product.  With head_dim 64
     // |256*mid + ll| <= B_MID (< 2^30), so raw = 65536*hh + 256*mid + ll is
     // an exact i32 whenever |hh| <= 16384; other elements take an i64 path.
-    int mx32 = INT_MIN, mn32 = INT_MAX;
+    int mx32 = INT_MIN;
     long long mx64 = LLONG_MIN, mn64 = LLONG_MAX;
     // Per-row constants of passes 1 and 2 (see the element loop).
     uint32_t rawmax_lo = 0, cround = 0;
@@ -252,58 +307,43 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
     long long rawmax = 0, lgmax = 0;
     unsigned long long rsum = 0;
     uint32_t inv = 0;
-    uint32_t u = 0;
+    uint32_t use0 = 0, use1 = 0;  // uses of each S buffer, in the MMA issuer's order
+    uint32_t it = 0;            // items of the max and sum passes
     bool range_bad = false, masked_bad = false;
     for (int pass = 0; pass < 3; ++pass) {
-      for (int j = 0; j < ntiles; ++j, ++u) {
+      for (int j = 0; j < ntiles; ++j) {
+        const int sb = pass < 2 ? (int)(it++ & 1) : 0;
         uint32_t hh[16], mid[16], ll[16];
-        wait_bar(&ctl->s_full, u & 1, ctl, a.st);
+        wait_bar(&ctl->s_full[sb], (sb ? use1 : use0) & 1, ctl, a.st);
+        if (sb)
+          ++use1;
+        else
+          ++use0;
         tc_fence_after();
-        tmem_ld16(trow + S_HH + 16 * g, hh);
-        tmem_ld16(trow + S_MID + 16 * g, mid);
-        tmem_ld16(trow + S_LL + 16 * g, ll);
+        const uint32_t tb = trow + (uint32_t)sb * S_BUF1 + 16 * g;
+        tmem_ld16(tb + S_HH, hh);
+        tmem_ld16(tb + S_MID, mid);
+        tmem_ld16(tb + S_LL, ll);
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&ctl->s_empty);
+        if (lane == 0) mbar_arrive(&ctl->s_empty[sb]);
         const int key0 = j * KT + 16 * g;
         const int nlive = max(0, min(16, last_key - key0 + 1));
+        const bool full = __all_sync(0xffffffffu, nlive == 16) != 0;
         if (pass == 0) {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            if (i < nlive) {
-              const int h = (int)hh[i];
-              if ((unsigned)(h + 16384) <= 32768u) {
-                const int r32 = (int)((uint32_t)h * 65536u + mid[i] * 256u + ll[i]);
-                mx32 = max(mx32, r32);
-                mn32 = min(mn32, r32);
-              } else {
-                const long long raw = (long long)h * 65536 + (long long)(int)mid[i] * 256 + (long long)(int)ll[i];
-                mx64 = max(mx64, raw);
-                mn64 = min(mn64, raw);
-              }
-            }
-          }
+          if (full)
+            scores_max<true>(hh, mid, ll, nlive, mx32, mx64, mn64);
+          else
+            scores_max<false>(hh, mid, ll, nlive, mx32, mx64, mn64);
           continue;
         }
         int w[16];
         if (!slow_row) {
-          // w != 0 needs mag = lgmax - lg < 3840, i.e. raw > rawmax - 30720;
-          // that needs hh > hh_floor, and then rawmax - raw < 2^32, so the
-          // difference is exact in u32.  mag = (diff + cround) >> 3.
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            int wi = 0;
-            if (i < nlive && (int)hh[i] > hh_floor) {
-              const uint32_t raw_lo = hh[i] * 65536u + mid[i] * 256u + ll[i];
-              const uint32_t diff = rawmax_lo - raw_lo;
-              if (diff < 30720u - cround) {
-                const uint32_t mag = (diff + cround) >> 3;
-                wi = (int)lut[mag & 255u] >> (mag >> 8);
-              }
-            }
-            w[i] = wi;
-          }
+          if (full)
+            scores_weight<true>(hh, mid, ll, nlive, hh_floor, rawmax_lo, cround, lut, w);
+          else
+            scores_weight<false>(hh, mid, ll, nlive, hh_floor, rawmax_lo, cround, lut, w);
         } else {
           // Rows whose max logit lies within 15 * 256 of i32::MIN: exact i64
           // path, with logits equal to MASKED_LOGIT excluded (attention.rs:266-276).
@@ -357,8 +397,9 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
         if (lane == 0) mbar_arrive(&ctl->p_full[pb]);
       }
       if (pass == 0) {
-        long long rmx = max((long long)mx32 == INT_MIN && mx64 != LLONG_MIN ? LLONG_MIN : (long long)mx32, mx64);
-        long long rmn = min((long long)mn32 == INT_MAX && mn64 != LLONG_MAX ? LLONG_MAX : (long long)mn32, mn64);
+        // INT_MIN is never an exact-i32 raw value (> -2^30 - B_MID), so it marks "none".
+        long long rmx = max(mx32 == INT_MIN ? LLONG_MIN : (long long)mx32, mx64);
+        long long rmn = mn64;
         xmax[g * QT + row] = rmx;
         xmin[g * QT + row] = rmn;
         named_sync_softmax();
@@ -370,8 +411,7 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
         if (row_live) {
           rawmax = rmx;
           lgmax = rawmax >> 3;
-          const long long lgmin = rmn >> 3;
-          if (lgmax > INT_MAX || lgmin < INT_MIN) range_bad = true;
+          if (lgmax > INT_MAX || (rmn != LLONG_MAX && (rmn >> 3) < INT_MIN)) range_bad = true;
           if (lgmax <= (long long)INT_MIN) masked_bad = true;  // every live logit masked or out of range
           slow_row = lgmax < (long long)INT_MIN + 15 * 256;
           rawmax_lo = (uint32_t)rawmax;

@@ -57,6 +57,14 @@ bool linear_ok(const nsrl_linear_params* p, size_t in, size_t out) {
   return p && p->input_dim == in && p->output_dim == out && in != 0 && out != 0 && p->weights && p->scales;
 }
 
+// True when a linear with these inputs may need the exact i32 prefix check
+// (linear.rs:144-173), which reads the row L1 norms of its input.
+bool needs_l1(size_t K, const nsrl_linear_params* a, const nsrl_linear_params* b = nullptr,
+              const nsrl_linear_params* c = nullptr) {
+  const bool bias = (a && a->bias) || (b && b->bias) || (c && c->bias);
+  return bias || (unsigned long long)K * 127ull * 32767ull > 2147483647ull;
+}
+
 WeightSeg seg_of(const nsrl_linear_params* p) { return WeightSeg{p->weights, p->bias, p->scales, p->output_dim}; }
 
 nsrl_status cuda_fail(cudaError_t e, const char* what) {
@@ -144,7 +152,8 @@ nsrl_status attention_core(const Planes& xin, size_t B, size_t S, size_t d, size
   g.st = st;
   NSRL_TRY(launch_gemm(g, stream), "qkv projection");
 
-  NSRL_TRY(cudaMemsetAsync(ctx.l1, 0, T * sizeof(unsigned long long), stream), "memset");
+  if (!needs_l1(d, o)) ctx.l1 = nullptr;
+  if (ctx.l1) NSRL_TRY(cudaMemsetAsync(ctx.l1, 0, T * sizeof(unsigned long long), stream), "memset");
   if (tc) {
     NSRL_TRY(launch_attention_tc(qkv, vt, B, S, d, H, causal, ctx, st, stream), "attention");
   } else if (attention_prefill_native(d, H, S)) {
@@ -203,8 +212,10 @@ nsrl_status mlp_block(const int16_t* x, size_t T, size_t d, size_t F, const int1
                       cudaStream_t stream) {
   Planes xn = c.planes(T, d, true);
   Planes gated = c.planes(T, F, true);
+  if (!needs_l1(d, upp, gatep)) xn.l1 = nullptr;
+  if (!needs_l1(F, downp)) gated.l1 = nullptr;
   NSRL_TRY(launch_rms_norm(x, T, d, gamma, eps, nullptr, xn, st, stream), "rms norm");
-  NSRL_TRY(cudaMemsetAsync(gated.l1, 0, T * sizeof(unsigned long long), stream), "memset");
+  if (gated.l1) NSRL_TRY(cudaMemsetAsync(gated.l1, 0, T * sizeof(unsigned long long), stream), "memset");
   GemmArgs g{};
   g.a_hi = xn.hi;
   g.a_lo = xn.lo;
@@ -253,6 +264,7 @@ nsrl_status attention_block(const int16_t* x, size_t B, size_t S, size_t d, size
     qkv16 = c.take<int16_t>(T * 3 * d);
     ctx16 = c.take<int16_t>(T * d);
   }
+  if (!needs_l1(d, q, k, v)) xn.l1 = nullptr;
   NSRL_TRY(launch_rms_norm(x, T, d, gamma, eps, nullptr, xn, st, stream), "rms norm");
   return attention_core(xn, B, S, d, H, causal, q, k, v, o, qkv, ctx, vt, qkv16, ctx16, Epi::RESID, x, y,
                         &st->attention_saturations, st, stream);

@@ -24,28 +24,45 @@ __device__ __forceinline__ long long rsqrt_q30(unsigned long long v) {
   return half >= 63 ? 0 : (inv >> half);
 }
 
+// floor(ss / d) from a double reciprocal, corrected to the exact quotient
+// (ss < 2^53, so the double product is within one of it).
+__device__ __forceinline__ unsigned long long div_exact(unsigned long long ss, unsigned d, double rd) {
+  unsigned long long q = (unsigned long long)((double)ss * rd);
+  if (q * d > ss) --q;
+  if ((q + 1) * d <= ss) ++q;
+  return q;
+}
+
+// sat_i16(rhu(x * g * inv, 30)): |x * g| <= 2^30 and 0 <= inv < 2^30, so the
+// product fits i64 with no saturation and rhu is (v + 2^29) >> 30.
+__device__ __forceinline__ int16_t rms_scale(int x, int g, long long inv) {
+  const long long v = (long long)(x * g) * inv + (1ll << 29);
+  return (int16_t)max(-32768ll, min(32767ll, v >> 30));
+}
+
 template <bool VEC>
-__global__ void rms_norm_kernel(const int16_t* __restrict__ x, long long rows, int d, const int16_t* __restrict__ g,
-                                unsigned long long eps, int16_t* __restrict__ y, int8_t* __restrict__ yh,
-                                uint8_t* __restrict__ yl, unsigned long long* __restrict__ yl1, long long ldp,
-                                nsrl_device_status* st) {
+__global__ void rms_norm_kernel(const int16_t* __restrict__ x, long long rows, int d, double rd,
+                                const int16_t* __restrict__ g, unsigned long long eps, int16_t* __restrict__ y,
+                                int8_t* __restrict__ yh, uint8_t* __restrict__ yl, unsigned long long* __restrict__ yl1,
+                                long long ldp, nsrl_device_status* st) {
   const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
   for (long long r = (long long)blockIdx.x * warps + (threadIdx.x >> 5); r < rows; r += (long long)gridDim.x * warps) {
     const int16_t* xr = x + r * d;
     unsigned long long ss = 0;
     if (VEC) {
       for (int k8 = lane; k8 < d / 8; k8 += 32) {
-        uint4 v = reinterpret_cast<const uint4*>(xr)[k8];
+        const uint4 v = reinterpret_cast<const uint4*>(xr)[k8];
         const int16_t* e = reinterpret_cast<const int16_t*>(&v);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) ss += (unsigned long long)((int)e[j] * (int)e[j]);
+        for (int j = 0; j < 8; j += 2)  // a pair of squares is at most 2^31
+          ss += (unsigned long long)((unsigned)((int)e[j] * (int)e[j]) + (unsigned)((int)e[j + 1] * (int)e[j + 1]));
       }
     } else {
       for (int k = lane; k < d; k += 32) ss += (unsigned long long)((int)xr[k] * (int)xr[k]);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const unsigned long long mean = ss / (unsigned long long)d;
+    const unsigned long long mean = div_exact(ss, (unsigned)d, rd);
     const unsigned long long v = mean + eps;
     long long inv = 0;
     if (v < mean || v == 0) {  // u64 overflow of mean + eps, or rsqrt(0): the reference returns None
@@ -53,38 +70,33 @@ __global__ void rms_norm_kernel(const int16_t* __restrict__ x, long long rows, i
     } else {
       inv = rsqrt_q30(v);
     }
-    unsigned long long l1 = 0;
+    unsigned l1 = 0;  // per lane: at most d / 32 * 32768
     if (VEC) {
       for (int k8 = lane; k8 < d / 8; k8 += 32) {
-        uint4 xv = reinterpret_cast<const uint4*>(xr)[k8];
-        uint4 gv = reinterpret_cast<const uint4*>(g)[k8];
+        const uint4 xv = reinterpret_cast<const uint4*>(xr)[k8];
+        const uint4 gv = reinterpret_cast<const uint4*>(g)[k8];
         const int16_t* xe = reinterpret_cast<const int16_t*>(&xv);
         const int16_t* ge = reinterpret_cast<const int16_t*>(&gv);
-        int16_t out[8];
+        uint32_t pk[4];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          out[j] = sat_i16(rhu64((long long)((int)xe[j] * (int)ge[j]) * inv, 30));
-          l1 += (unsigned long long)abs((int)out[j]);
+        for (int j = 0; j < 8; j += 2) {
+          const int o0 = rms_scale(xe[j], ge[j], inv), o1 = rms_scale(xe[j + 1], ge[j + 1], inv);
+          if (yl1) l1 += (unsigned)(abs(o0) + abs(o1));
+          pk[j / 2] = (uint32_t)(o0 & 0xFFFF) | ((uint32_t)o1 << 16);
         }
-        if (y) reinterpret_cast<uint4*>(y + r * d)[k8] = *reinterpret_cast<uint4*>(out);
+        if (y) reinterpret_cast<uint4*>(y + r * d)[k8] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         if (yh) {
-          uint32_t h0 = 0, h1 = 0, l0 = 0, l1w = 0;
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            h0 |= (uint32_t)((out[j] >> 8) & 255) << (8 * j);
-            l0 |= (uint32_t)(out[j] & 255) << (8 * j);
-            h1 |= (uint32_t)((out[4 + j] >> 8) & 255) << (8 * j);
-            l1w |= (uint32_t)(out[4 + j] & 255) << (8 * j);
-          }
-          reinterpret_cast<uint2*>(yh + r * ldp)[k8] = make_uint2(h0, h1);
-          reinterpret_cast<uint2*>(yl + r * ldp)[k8] = make_uint2(l0, l1w);
+          reinterpret_cast<uint2*>(yh + r * ldp)[k8] =
+              make_uint2(__byte_perm(pk[0], pk[1], 0x7531), __byte_perm(pk[2], pk[3], 0x7531));
+          reinterpret_cast<uint2*>(yl + r * ldp)[k8] =
+              make_uint2(__byte_perm(pk[0], pk[1], 0x6420), __byte_perm(pk[2], pk[3], 0x6420));
         }
       }
     } else {
       for (int k = lane; k < d; k += 32) {
-        int16_t o = sat_i16(rhu64((long long)((int)xr[k] * (int)g[k]) * inv, 30));
-        l1 += (unsigned long long)abs((int)o);
-        if (y) y[r * d + k] = o;
+        const int o = rms_scale(xr[k], g[k], inv);
+        l1 += (unsigned)abs(o);
+        if (y) y[r * d + k] = (int16_t)o;
         if (yh) {
           yh[r * ldp + k] = (int8_t)(o >> 8);
           yl[r * ldp + k] = (uint8_t)(o & 255);
@@ -92,9 +104,10 @@ __global__ void rms_norm_kernel(const int16_t* __restrict__ x, long long rows, i
       }
     }
     if (yl1) {
+      unsigned long long l1w = l1;
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) l1 += __shfl_xor_sync(0xffffffffu, l1, o);
-      if (lane == 0) yl1[r] = l1;
+      for (int o = 16; o > 0; o >>= 1) l1w += __shfl_xor_sync(0xffffffffu, l1w, o);
+      if (lane == 0) yl1[r] = l1w;
     }
   }
 }
@@ -111,11 +124,11 @@ cudaError_t launch_rms_norm(const int16_t* x, size_t rows, size_t d, const int16
                                yp.ld % 8 == 0));
   ProfScope prof("rms_norm", stream, 0.0, 4.0 * rows * d + (yp.l1 ? 8.0 * rows : 0.0));
   if (vec)
-    rms_norm_kernel<true><<<blocks, 256, 0, stream>>>(x, (long long)rows, (int)d, gamma, eps, y_i16, yp.hi, yp.lo,
-                                                      yp.l1, (long long)yp.ld, st);
+    rms_norm_kernel<true><<<blocks, 256, 0, stream>>>(x, (long long)rows, (int)d, 1.0 / (double)d, gamma, eps, y_i16,
+                                                      yp.hi, yp.lo, yp.l1, (long long)yp.ld, st);
   else
-    rms_norm_kernel<false><<<blocks, 256, 0, stream>>>(x, (long long)rows, (int)d, gamma, eps, y_i16, yp.hi, yp.lo,
-                                                       yp.l1, (long long)yp.ld, st);
+    rms_norm_kernel<false><<<blocks, 256, 0, stream>>>(x, (long long)rows, (int)d, 1.0 / (double)d, gamma, eps,
+                                                       y_i16, yp.hi, yp.lo, yp.l1, (long long)yp.ld, st);
   return cudaGetLastError();
 }
 
