@@ -174,6 +174,32 @@ nsrl_status nsrl_attention_decode(const int16_t* q, const int16_t* k_cache, cons
                                   const int32_t* lens, size_t batch, size_t heads, size_t head_dim, size_t max_len,
                                   int16_t* ctx, nsrl_device_status* status, void* stream);
 
+/* ----------------------------------------------- training-step exchange --
+ * acc[n][k] += scaled_grad[r][n] * x[r][k] for r < rows, checked i64 adds in
+ * row order (zero terms skipped), *sample_count += rows: one call of the
+ * reference per row.  Replaces accumulate_linear_weight_gradient_i64_prescaled
+ * (crates/nsrl-train-core/src/lib.rs:344-384).  x: [rows][input_dim] int16,
+ * scaled_grad: [rows][output_dim] int32, accumulators: [output_dim][input_dim]
+ * int64, sample_count: one device uint64.  An overflow rejects the call. */
+size_t nsrl_accumulate_workspace_size(size_t input_dim, size_t output_dim);
+nsrl_status nsrl_accumulate_linear_weight_gradient_i64(const int16_t* x, const int32_t* scaled_grad, size_t rows,
+                                                       size_t input_dim, size_t output_dim, long long* accumulators,
+                                                       unsigned long long* sample_count, void* workspace,
+                                                       size_t workspace_bytes, nsrl_device_status* status,
+                                                       void* stream);
+
+/* Averages the accumulators over *sample_count (round half away from zero),
+ * scales by learning_rate, adds the carried residual, rounds with
+ * learning_rate_shift, subtracts from the i8 weights with saturation and
+ * clears the accumulators and the count.  stats (3 device uint64):
+ * {gradient saturations, zero deltas, sum |weight delta|}.  Replaces
+ * apply_linear_weight_gradient_i64_to_i8 (crates/nsrl-train-core/src/lib.rs:386-465). */
+nsrl_status nsrl_apply_linear_weight_gradient_i64_to_i8(long long* accumulators, long long* residuals, int8_t* weights,
+                                                        size_t len, unsigned long long* sample_count,
+                                                        int32_t learning_rate, uint8_t learning_rate_shift,
+                                                        int carry_residual, unsigned long long* stats,
+                                                        nsrl_device_status* status, void* stream);
+
 /* ------------------------------------------------------------ profiling --
  * Per-launch CUDA-event timing of the library's own kernels (no counterpart
  * in the reference, whose only timer is a wall clock around the block loop,

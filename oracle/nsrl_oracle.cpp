@@ -649,3 +649,105 @@ int orc_bench1m(uint64_t* model_hash, uint64_t* input_hash, uint64_t* output_has
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------ training exchange ---
+// crates/nsrl-train-core/src/lib.rs:1732-1757 (round half away from zero)
+static bool round_ratio_i64(int64_t num, int64_t den, int64_t* out) {
+  if (den <= 0) return false;
+  int64_t half = den / 2;
+  if (num >= 0) {
+    int64_t t;
+    if (__builtin_add_overflow(num, half, &t)) return false;
+    *out = t / den;
+  } else {
+    if (num == INT64_MIN) return false;
+    int64_t t;
+    if (__builtin_add_overflow(-num, half, &t)) return false;
+    *out = -(t / den);
+  }
+  return true;
+}
+
+extern "C" {
+
+// crates/nsrl-train-core/src/lib.rs:344-384, one call per row r:
+// acc[n][k] += g[r][n] * x[r][k] (checked i64, zeros skipped), count += 1.
+int orc_accumulate_linear_gradient_i64(const int16_t* x, const int32_t* g, size_t rows, size_t K, size_t N,
+                                       int64_t* acc, uint64_t* count) {
+  if (K == 0 || N == 0) return 1;
+  for (size_t r = 0; r < rows; ++r) {
+    const int16_t* xr = x + r * K;
+    const int32_t* gr = g + r * N;
+    for (size_t n = 0; n < N; ++n) {
+      if (gr[n] == 0) continue;
+      for (size_t k = 0; k < K; ++k) {
+        if (xr[k] == 0) continue;
+        int64_t prod = (int64_t)gr[n] * (int64_t)xr[k];
+        if (__builtin_add_overflow(acc[n * K + k], prod, &acc[n * K + k])) return 2;
+      }
+    }
+    *count += 1;
+  }
+  return 0;
+}
+
+// crates/nsrl-train-core/src/lib.rs:386-465.  stats = {saturations, zero deltas, |delta| sum}.
+int orc_apply_linear_gradient_i64_to_i8(int64_t* acc, int64_t* residuals, int8_t* weights, size_t len,
+                                        uint64_t* count, int32_t lr, uint8_t shift, int carry, uint64_t* stats) {
+  stats[0] = stats[1] = stats[2] = 0;
+  if (lr <= 0 || shift > MAX_RIGHT_SHIFT) return 1;
+  if (*count == 0) return 0;
+  if (*count > (uint64_t)INT64_MAX) return 1;
+  const int64_t den = (int64_t)*count;
+  for (size_t i = 0; i < len; ++i) {
+    if (acc[i] == 0) continue;
+    int64_t avg;
+    if (!round_ratio_i64(acc[i], den, &avg)) return 2;
+    int64_t product;
+    if (__builtin_mul_overflow(avg, (int64_t)lr, &product)) return 2;
+    if (carry && __builtin_add_overflow(product, residuals[i], &product)) return 2;
+    int64_t scaled = rhu(product, shift);
+    int64_t next_res = 0;
+    if (carry && shift != 0) {
+      __int128 applied = (__int128)scaled << shift;
+      __int128 res = (__int128)product - applied;
+      if (res < INT64_MIN || res > INT64_MAX) return 2;
+      next_res = (int64_t)res;
+    }
+    int64_t delta = -scaled;
+    if (delta == 0) stats[1] += 1;
+    int8_t prev = weights[i];
+    int64_t unclamped;
+    if (__builtin_add_overflow((int64_t)prev, delta, &unclamped)) return 2;
+    int8_t clamped = saturate_i8(unclamped);
+    if ((int64_t)clamped != unclamped) {
+      stats[0] += 1;
+      residuals[i] = 0;
+    } else {
+      residuals[i] = next_res;
+    }
+    int64_t applied_delta = (int64_t)clamped - (int64_t)prev;
+    stats[2] += (uint64_t)(applied_delta < 0 ? -applied_delta : applied_delta);
+    weights[i] = clamped;
+  }
+  for (size_t i = 0; i < len; ++i) acc[i] = 0;
+  *count = 0;
+  return 0;
+}
+
+// crates/nsrl-train/src/lib.rs:7443-7471: merge worker results in worker
+// order with checked adds.  parts: [workers][len].
+int orc_merge_i64(const int64_t* parts, size_t workers, size_t len, const uint64_t* counts, int64_t* out,
+                  uint64_t* count_out) {
+  uint64_t c = 0;
+  for (size_t i = 0; i < len; ++i) out[i] = 0;
+  for (size_t w = 0; w < workers; ++w) {
+    if (__builtin_add_overflow(c, counts[w], &c)) return 2;
+    for (size_t i = 0; i < len; ++i)
+      if (__builtin_add_overflow(out[i], parts[w * len + i], &out[i])) return 2;
+  }
+  *count_out = c;
+  return 0;
+}
+
+}  // extern "C"

@@ -243,3 +243,43 @@ def bench1m():
     if lib().orc_bench1m(C.byref(mh), C.byref(ih), C.byref(oh), C.byref(s)):
         return None
     return dict(model_hash=mh.value, input_hash=ih.value, output_hash=oh.value, saturations=s.value)
+
+
+# ------------------------------------------------------ training exchange ---
+def accumulate_linear_gradient_i64(x, g, acc, count):
+    """train-core lib.rs:344-384 for each row; returns (acc, count) or None on overflow."""
+    x = _c(x, np.int16)
+    g = _c(g, np.int32)
+    acc = np.array(acc, dtype=np.int64, copy=True)
+    N, K = acc.shape
+    rows = x.size // K
+    c = C.c_uint64(count)
+    if lib().orc_accumulate_linear_gradient_i64(_p(x), _p(g), C.c_size_t(rows), C.c_size_t(K), C.c_size_t(N),
+                                                _p(acc), C.byref(c)):
+        return None
+    return acc, c.value
+
+
+def apply_linear_gradient_i64_to_i8(acc, residuals, weights, count, lr, shift, carry):
+    """train-core lib.rs:386-465; returns (acc, residuals, weights, count, stats) or None."""
+    acc = np.array(acc, dtype=np.int64, copy=True).ravel()
+    res = np.array(residuals, dtype=np.int64, copy=True).ravel()
+    w = np.array(weights, dtype=np.int8, copy=True).ravel()
+    c = C.c_uint64(count)
+    stats = np.zeros(3, np.uint64)
+    if lib().orc_apply_linear_gradient_i64_to_i8(_p(acc), _p(res), _p(w), C.c_size_t(w.size), C.byref(c),
+                                                 C.c_int32(lr), C.c_uint8(shift), C.c_int(int(carry)), _p(stats)):
+        return None
+    return acc, res, w, c.value, [int(s) for s in stats]
+
+
+def merge_i64(parts, counts):
+    """nsrl-train lib.rs:7443-7471: ordered checked merge of worker accumulators."""
+    parts = _c(parts, np.int64)
+    counts = _c(counts, np.uint64)
+    W, L = parts.shape
+    out = np.zeros(L, np.int64)
+    c = C.c_uint64()
+    if lib().orc_merge_i64(_p(parts), C.c_size_t(W), C.c_size_t(L), _p(counts), _p(out), C.byref(c)):
+        return None
+    return out, c.value

@@ -184,3 +184,35 @@ def test_oracle_batched_block_is_per_sequence(threads):
     y, sat = O.prenorm_attention_block(x, B, S, d, H, g, 1, *lins, threads=threads)
     parts = [O.prenorm_attention_block(x[b * S:(b + 1) * S], 1, S, d, H, g, 1, *lins)[0] for b in range(B)]
     assert np.array_equal(y, np.concatenate(parts))
+
+
+def test_i64_gradient_average_then_update():  # crates/nsrl-train-core/src/lib.rs:1896-1927
+    acc = np.zeros((2, 2), np.int64)
+    x = np.array([[4096, 8192]], np.int16)
+    g = np.array([[1024, 2048]], np.int32)
+    acc, c = O.accumulate_linear_gradient_i64(x, g, acc, 0)
+    acc, c = O.accumulate_linear_gradient_i64(x, g, acc, c)
+    assert c == 2
+    acc2, res, w, c2, st = O.apply_linear_gradient_i64_to_i8(acc, np.zeros(4), np.full(4, 10), c, 1, 22, False)
+    assert list(w) == [9, 8, 8, 6]
+    assert st == [0, 0, 9]
+    assert c2 == 0 and not acc2.any()
+
+
+def test_i64_gradient_carries_residuals():  # crates/nsrl-train-core/src/lib.rs:1929-1966
+    acc, c = O.accumulate_linear_gradient_i64(np.array([[1]], np.int16), np.array([[1]], np.int32),
+                                              np.zeros((1, 1), np.int64), 0)
+    acc, res, w, c, st = O.apply_linear_gradient_i64_to_i8(acc, [0], [10], c, 1, 2, True)
+    assert list(w) == [10] and st[1] == 1 and st[2] == 0 and list(res) == [1]
+    acc, c = O.accumulate_linear_gradient_i64(np.array([[1]], np.int16), np.array([[1]], np.int32),
+                                              acc.reshape(1, 1), c)
+    acc, res, w, c, st = O.apply_linear_gradient_i64_to_i8(acc, res, w, c, 1, 2, True)
+    assert list(w) == [9] and st[1] == 0 and st[2] == 1 and list(res) == [-2]
+
+
+def test_ordered_merge_rejects_prefix_overflow():
+    big = 2**62
+    parts = np.array([[big], [big], [-big]], np.int64)
+    assert O.merge_i64(parts, [1, 1, 1]) is None  # big + big overflows before the third worker
+    out, c = O.merge_i64(np.array([[big], [-big], [big]], np.int64), [1, 2, 3])
+    assert out[0] == big and c == 6
