@@ -184,6 +184,147 @@ def kernel_table(core_lib):
 
 TENSOR_KERNELS = ("linear_tc", "attention_prefill", "attention_tc")
 
+# Config 5 (decode) and config 2 (linear sweep), measured after the headline.
+DEC_LAYERS, DEC_D, DEC_H, DEC_F, DEC_B, DEC_PREFIX = 4, 512, 8, 2048, 256, 8192
+SWEEP_M, SWEEP_KN = (4096, 16384, 65536), (256, 1024, 4096)
+
+
+def run_decode(core, torch, steps, warmup, hbm, flush):
+    """4-layer KV-cache decode steps: per layer the prenorm attention decode block then the
+    prenorm gated-MLP block over the batch's new tokens; the caches hold DEC_PREFIX + t rows."""
+    from nsrl_b200 import synth as Y
+    L = core.lib()
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    lmax = DEC_PREFIX + warmup + steps + 1
+    layers = []
+    for li in range(DEC_LAYERS):
+        bw = Y.BlockWeights(seed=77 + li, d=DEC_D, hidden=DEC_F)
+        lin = {nm: core.Linear(torch.from_numpy(getattr(bw, nm)), core.make_scales(1, bw.shift[nm], bw.out_dim(nm)))
+               for nm in ("q", "k", "v", "o", "up", "gate", "down")}
+        caches = []
+        for _ in range(2):  # K and V: Q15 Gaussian sigma 4096 (K narrower so that the softmax stays live)
+            c = torch.empty((DEC_B, lmax, DEC_D), dtype=torch.int16, device="cuda")
+            c.copy_((torch.randn(c.shape, generator=gen, device="cuda") * 4096).clamp_(-32768, 32767).to(torch.int16))
+            caches.append(c)
+        caches[0] >>= 5
+        layers.append((lin, caches, torch.from_numpy(bw.attn_gamma).cuda(), torch.from_numpy(bw.mlp_gamma).cuda()))
+    x0 = (torch.randn((DEC_B, DEC_D), generator=gen, device="cuda") * 4096).clamp_(-32768, 32767).to(torch.int16)
+    pos = torch.full((DEC_B,), DEC_PREFIX, dtype=torch.int32, device="cuda")
+    ws = core.workspace(max(L.nsrl_decode_block_workspace_size(DEC_B, DEC_D, DEC_H),
+                            L.nsrl_mlp_workspace_size(DEC_B, DEC_D, DEC_F)))
+    st = core.Status()
+    h = torch.empty_like(x0)
+    y = torch.empty_like(x0)
+    lp = {}
+
+    def step(x):
+        for lin, (kc, vc), ga, gm in layers:
+            ps = [lin[n].c() for n in ("q", "k", "v", "o")]
+            r = L.nsrl_prenorm_attention_decode_block(
+                core._ptr(x), DEC_B, DEC_D, DEC_H, core._ptr(ga), 1, *[core.C.byref(p) for p in ps], core._ptr(kc),
+                core._ptr(vc), core._ptr(pos), lmax, core._ptr(h), core._ptr(ws), ws.numel(), core._ptr(st.buf),
+                core._stream())
+            if r != 0:
+                raise RuntimeError(L.nsrl_last_error())
+            pm = [lin[n].c() for n in ("up", "gate", "down")]
+            r = L.nsrl_prenorm_gated_mlp_residual_block(core._ptr(h), DEC_B, DEC_D, DEC_F, core._ptr(gm), 1,
+                                                        *[core.C.byref(p) for p in pm], core._ptr(y), core._ptr(ws),
+                                                        ws.numel(), core._ptr(st.buf), core._stream())
+            if r != 0:
+                raise RuntimeError(L.nsrl_last_error())
+            x = y.clone()
+        pos.add_(1)
+        return x
+
+    st.reset()
+    x = x0
+    for _ in range(warmup):
+        x = step(x)
+    torch.cuda.synchronize()
+    ctx_rows = DEC_PREFIX + warmup  # keys attended at the first timed step = this + 1
+    L.nsrl_profile_reset()
+    L.nsrl_profile_enable(1)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        x = step(x)
+    e1.record()
+    torch.cuda.synchronize()
+    L.nsrl_profile_enable(0)
+    ms = e0.elapsed_time(e1)
+    code, hs = st.fetch()
+    if code != 0:
+        raise RuntimeError(f"decode rejected (flags {hs.flags:#x})")
+    _, rows = kernel_table(L)
+    dec = rows["attention_decode"]
+    # algorithmic bytes of the timed decode-attention launches: every cached K and V
+    # row once (positions + 1 keys), plus q in and the context out
+    keys = sum(DEC_B * (ctx_rows + t + 1) for t in range(steps)) * DEC_LAYERS
+    dbytes = 2.0 * 2 * DEC_D * keys + 2.0 * 2 * DEC_D * DEC_B * steps * DEC_LAYERS
+    ach = dbytes / (dec["ms"] / 1000.0) / 1e9
+    return {"workload": f"{DEC_LAYERS}-layer decode step, d{DEC_D} h{DEC_H}x{DEC_D // DEC_H} ff{DEC_F}, "
+                        f"batch {DEC_B}, KV prefix {DEC_PREFIX} (+t), i16 cache",
+            "value": DEC_B * steps / (ms / 1000.0), "unit": "tokens/s", "steps": steps, "warmup": warmup,
+            "ms_per_step": ms / steps,
+            "roofline": {"kernel": "attention_decode", "bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s",
+                         "frac": ach / hbm, "ms_per_launch": dec["ms"] / dec["launches"],
+                         "algorithmic_bytes_per_launch": dbytes / dec["launches"]},
+            "kernel_share": {k: round(v["ms"] / sum(r["ms"] for r in rows.values()), 4) for k, v in rows.items()}}
+
+
+def run_sweep(core, torch, hbm, tflops, flush, reps=5):
+    """Config 2: the i16 x i8 linear over M x K (K = N) through nsrl_linear_i16_i8_i16."""
+    from nsrl_b200 import synth as Y
+    L = core.lib()
+    out = []
+    gen = torch.Generator(device="cuda").manual_seed(9)
+    for K in SWEEP_KN:
+        N = K
+        w = torch.from_numpy(Y.i8_uniform(K, (N, K)))
+        lin = core.Linear(w, core.make_scales(1, Y.shift_for(K), N))
+        for M in SWEEP_M:
+            x = (torch.randn((M, K), generator=gen, device="cuda") * 4096).clamp_(-32768, 32767).to(torch.int16)
+            y = torch.empty((M, N), dtype=torch.int16, device="cuda")
+            ws = core.workspace(L.nsrl_linear_workspace_size(M, K, N))
+            st = core.Status()
+            p = lin.c()
+
+            def call():
+                r = L.nsrl_linear_i16_i8_i16(core._ptr(x), M, core.C.byref(p), core._ptr(y), core._ptr(ws),
+                                             ws.numel(), core._ptr(st.buf), core._stream())
+                if r != 0:
+                    raise RuntimeError(L.nsrl_last_error())
+
+            for _ in range(2):
+                call()
+            L.nsrl_profile_reset()
+            L.nsrl_profile_enable(1)
+            tot = 0.0
+            for _ in range(reps):
+                flush.zero_()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                call()
+                b.record()
+                torch.cuda.synchronize()
+                tot += a.elapsed_time(b)
+            L.nsrl_profile_enable(0)
+            _, rows = kernel_table(L)
+            code, _ = st.fetch()
+            if code != 0:
+                raise RuntimeError("linear rejected in the sweep")
+            gk = [v for k, v in rows.items() if k.startswith("linear_tc")][0]
+            ops = 2.0 * M * N * K
+            byts = 2.0 * M * K + N * K + 2.0 * M * N
+            t_gemm = gk["ms"] / gk["launches"] / 1000.0
+            t_call = tot / reps / 1000.0
+            roof_s = max(ops / (tflops * 1e12), byts / (hbm * 1e9))
+            out.append({"M": M, "K": K, "N": N, "bound": "tensor" if ops / (tflops * 1e12) > byts / (hbm * 1e9)
+                        else "hbm", "ms_call": round(t_call * 1e3, 4), "ms_gemm": round(t_gemm * 1e3, 4),
+                        "tops_call": ops / t_call / 1e12, "frac_call": roof_s / t_call, "frac_gemm": roof_s / t_gemm})
+            del x, y
+    return out
+
 
 def roofline(rows, hbm_gbs, tflops, src):
     name = max(rows, key=lambda k: rows[k]["ms"])
@@ -213,6 +354,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="skip the decode and linear-sweep measurements")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -226,7 +368,8 @@ def main():
     if world > 1:
         import datetime
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
 
     from nsrl_b200 import build, core
     build.build()
@@ -337,6 +480,9 @@ def main():
                "roofline": roofline(rows, hbm, tfl, src),
                "kernels": kernels,
                "clocks": clk}
+        if not args.no_extras and world == 1:
+            out["decode"] = run_decode(core, torch, steps=8, warmup=2, hbm=hbm, flush=flush)
+            out["linear_sweep"] = run_sweep(core, torch, hbm, tfl, flush)
         if world == 1 and not args.no_cpu_baseline:
             from oracle import oracle as O
             O.use_native()

@@ -174,6 +174,25 @@ nsrl_status nsrl_attention_decode(const int16_t* q, const int16_t* k_cache, cons
                                   const int32_t* lens, size_t batch, size_t heads, size_t head_dim, size_t max_len,
                                   int16_t* ctx, nsrl_device_status* status, void* stream);
 
+/* One decode step of a prenorm attention block over a KV cache.  Sequence b
+ * has positions[b] cached tokens (device int32); its new token x[b] is
+ * normalised, projected, its k and v are written to cache row positions[b],
+ * and its query attends over rows 0..positions[b] -- the last row of the
+ * causal forward (attention.rs:790, effective_len = token + 1) with earlier
+ * keys and values read from the cache instead of recomputed (the reference
+ * recomputes, crates/nsrl-train/src/lib.rs:118-130).  y[b] = x[b] +
+ * O(context), saturations into status->attention_saturations.  The caller
+ * advances positions after every layer of the step.  x, y: [batch][d_model];
+ * caches: [batch][max_len][d_model] int16, 16-byte aligned. */
+size_t nsrl_decode_block_workspace_size(size_t batch, size_t d_model, size_t heads);
+nsrl_status nsrl_prenorm_attention_decode_block(const int16_t* x, size_t batch, size_t d_model, size_t heads,
+                                                const int16_t* rms_gamma, uint64_t rms_eps,
+                                                const nsrl_linear_params* q, const nsrl_linear_params* k,
+                                                const nsrl_linear_params* v, const nsrl_linear_params* o,
+                                                int16_t* k_cache, int16_t* v_cache, const int32_t* positions,
+                                                size_t max_len, int16_t* y, void* workspace, size_t workspace_bytes,
+                                                nsrl_device_status* status, void* stream);
+
 /* ----------------------------------------------- training-step exchange --
  * acc[n][k] += scaled_grad[r][n] * x[r][k] for r < rows, checked i64 adds in
  * row order (zero terms skipped), *sample_count += rows: one call of the

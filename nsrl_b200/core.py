@@ -271,6 +271,30 @@ class TransformerBlock:
 
 
 # ----------------------------------------------------------------- decode ---
+def prenorm_attention_decode_block(x, heads, rms_gamma, rms_eps, q, k, v, o, k_cache, v_cache, positions):
+    """One decode step of the prenorm attention block (see nsrl_prenorm_attention_decode_block):
+    x [B, d]; caches [B, Lmax, d] (row positions[b] is written); returns (y, saturations) or None."""
+    L = lib()
+    if not getattr(L, "_decode_bound", False):
+        vp, sz, lp = C.c_void_p, C.c_size_t, C.POINTER(LinearParamsC)
+        L.nsrl_decode_block_workspace_size.restype = sz
+        L.nsrl_decode_block_workspace_size.argtypes = [sz, sz, sz]
+        L.nsrl_prenorm_attention_decode_block.argtypes = [vp, sz, sz, sz, vp, C.c_uint64, lp, lp, lp, lp, vp, vp, vp,
+                                                          sz, vp, vp, sz, vp, vp]
+        L._decode_bound = True
+    x = _i16(x)
+    g = _i16(rms_gamma)
+    B, d = x.shape
+    y = torch.empty_like(x)
+    pos = positions.to(x.device, torch.int32).contiguous()
+    ws = workspace(L.nsrl_decode_block_workspace_size(B, d, heads))
+    st = Status()
+    ps = [l.c() for l in (q, k, v, o)]
+    h = _run(lambda: L.nsrl_prenorm_attention_decode_block(
+        _ptr(x), B, d, heads, _ptr(g), rms_eps, *[C.byref(p) for p in ps], _ptr(k_cache), _ptr(v_cache), _ptr(pos),
+        k_cache.shape[1], _ptr(y), _ptr(ws), ws.numel(), _ptr(st.buf), _stream()), st)
+    return None if h is None else (y, h.attention_saturations)
+
 def attention_decode(q, k_cache, v_cache, lens, heads, head_dim):
     """attention.rs:671-725 for every (sequence, head): q [B, H*hd], caches [B, Lmax, H*hd], lens [B] int32."""
     q = _i16(q)

@@ -323,6 +323,7 @@ struct RowArgs {
   long long kv_seq;      // stride between sequences of k/v (elements)
   int rows_per_seq;      // query rows per sequence (1 for decode)
   int mode;              // 0: decode (lens), 1: causal prefill, 2: full prefill
+  int len_offset;        // decode: keys attended = lens[b] + len_offset
   const int32_t* lens;
   int Lmax;
   int hd, shift;
@@ -348,7 +349,7 @@ __global__ void __launch_bounds__(256) attention_rows_kernel(const RowArgs a) {
   const int tq = (int)(row % a.rows_per_seq);
   int L;
   if (a.mode == 0)
-    L = a.lens[b];
+    L = a.lens[b] + a.len_offset;
   else if (a.mode == 1)
     L = tq + 1;
   else
@@ -585,9 +586,37 @@ cudaError_t launch_attention_rows_i16(const int16_t* qkv, size_t B, size_t S, si
   return launch_rows(a, (long long)(B * S), (int)H, stream);
 }
 
+__global__ void kv_append_kernel(const int8_t* __restrict__ hi, const uint8_t* __restrict__ lo, long long ld, int d,
+                                 const int32_t* __restrict__ pos, int Lmax, int16_t* __restrict__ q16,
+                                 int16_t* __restrict__ kc, int16_t* __restrict__ vc, nsrl_device_status* st) {
+  const int b = blockIdx.x;
+  const int p = pos[b];
+  const bool ok = p >= 0 && p < Lmax;
+  if (!ok) {
+    if (threadIdx.x == 0) nsrl_flag(st, NSRL_FLAG_BAD_LENGTH);
+    return;
+  }
+  const long long row = (long long)b * ld;
+  const long long crow = ((long long)b * Lmax + p) * d;
+  for (int c = threadIdx.x; c < d; c += blockDim.x) {
+    q16[(long long)b * d + c] = (int16_t)((int)hi[row + c] * 256 + (int)lo[row + c]);
+    kc[crow + c] = (int16_t)((int)hi[row + d + c] * 256 + (int)lo[row + d + c]);
+    vc[crow + c] = (int16_t)((int)hi[row + 2 * d + c] * 256 + (int)lo[row + 2 * d + c]);
+  }
+}
+
+cudaError_t launch_kv_append(const Planes& qkv, size_t B, size_t d, const int32_t* pos, size_t Lmax, int16_t* q16,
+                             int16_t* k_cache, int16_t* v_cache, nsrl_device_status* st, cudaStream_t stream) {
+  if (B == 0) return cudaSuccess;
+  ProfScope prof("kv_append", stream, 0.0, 6.0 * (double)(B * d) + 6.0 * (double)(B * d));
+  kv_append_kernel<<<(unsigned)B, 256, 0, stream>>>(qkv.hi, qkv.lo, (long long)qkv.ld, (int)d, pos, (int)Lmax, q16,
+                                                     k_cache, v_cache, st);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_decode_attention(const int16_t* q, const int16_t* kc, const int16_t* vc, const int32_t* lens,
                                     size_t B, size_t H, size_t hd, size_t Lmax, int16_t* ctx,
-                                    nsrl_device_status* st, cudaStream_t stream) {
+                                    nsrl_device_status* st, cudaStream_t stream, int len_offset) {
   const size_t d = H * hd;
   RowArgs a{};
   a.q = q;
@@ -598,6 +627,7 @@ cudaError_t launch_decode_attention(const int16_t* q, const int16_t* kc, const i
   a.kv_seq = (long long)(Lmax * d);
   a.rows_per_seq = 1;
   a.mode = 0;
+  a.len_offset = len_offset;
   a.lens = lens;
   a.Lmax = (int)Lmax;
   a.hd = (int)hd;

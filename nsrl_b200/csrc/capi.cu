@@ -456,6 +456,83 @@ nsrl_status nsrl_prenorm_transformer_block(const int16_t* x, size_t batch, size_
   return mlp_block(h, T, d_model, hidden_dim, mlp_gamma, rms_eps, up_p, gate, down, y, c, status, s);
 }
 
+size_t nsrl_decode_block_workspace_size(size_t batch, size_t d_model, size_t heads) {
+  (void)heads;
+  Carver c(nullptr);
+  c.planes(batch, d_model, true);
+  c.planes(batch, 3 * d_model, false);
+  c.take<int16_t>(batch * d_model);
+  c.take<int16_t>(batch * d_model);
+  c.planes(batch, d_model, true);
+  return c.off;
+}
+
+nsrl_status nsrl_prenorm_attention_decode_block(const int16_t* x, size_t batch, size_t d_model, size_t heads,
+                                                const int16_t* rms_gamma, uint64_t rms_eps,
+                                                const nsrl_linear_params* q, const nsrl_linear_params* k,
+                                                const nsrl_linear_params* v, const nsrl_linear_params* o,
+                                                int16_t* k_cache, int16_t* v_cache, const int32_t* positions,
+                                                size_t max_len, int16_t* y, void* workspace, size_t workspace_bytes,
+                                                nsrl_device_status* status, void* stream) {
+  nsrl_status r = validate_attention(1, d_model, heads, q, k, v, o);
+  if (r != NSRL_OK) return r;
+  if (!status || !rms_gamma || !positions || !k_cache || !v_cache) return shape_fail("NULL argument");
+  if (max_len == 0 || max_len > 50000) return shape_fail("max_len must be in 1..50000");
+  if (batch == 0) return NSRL_OK;
+  if (((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 15) != 0 || d_model % 8 != 0)
+    return shape_fail("caches must be 16-byte aligned and d_model a multiple of 8");
+  if (!workspace || workspace_bytes < nsrl_decode_block_workspace_size(batch, d_model, heads))
+    return shape_fail("workspace too small");
+  cudaStream_t s = (cudaStream_t)stream;
+  const size_t d = d_model, hd = d / heads;
+  Carver c(workspace);
+  Planes xn = c.planes(batch, d, true);
+  Planes qkv = c.planes(batch, 3 * d, false);
+  int16_t* q16 = c.take<int16_t>(batch * d);
+  int16_t* ctx16 = c.take<int16_t>(batch * d);
+  Planes ctx = c.planes(batch, d, true);
+  if (!needs_l1(d, q, k, v)) xn.l1 = nullptr;
+  if (!needs_l1(d, o)) ctx.l1 = nullptr;
+  NSRL_TRY(launch_rms_norm(x, batch, d, rms_gamma, rms_eps, nullptr, xn, status, s), "rms norm");
+  GemmArgs g{};
+  g.a_hi = xn.hi;
+  g.a_lo = xn.lo;
+  g.a_l1 = xn.l1;
+  g.lda = d;
+  g.M = batch;
+  g.K = d;
+  g.nseg = 3;
+  g.seg[0] = seg_of(q);
+  g.seg[1] = seg_of(k);
+  g.seg[2] = seg_of(v);
+  g.epi = Epi::PLANES;
+  g.yp = qkv;
+  g.st = status;
+  NSRL_TRY(launch_gemm(g, s), "qkv projection");
+  NSRL_TRY(launch_kv_append(qkv, batch, d, positions, max_len, q16, k_cache, v_cache, status, s), "kv append");
+  NSRL_TRY(launch_decode_attention(q16, k_cache, v_cache, positions, batch, heads, hd, max_len, ctx16, status, s, 1),
+           "decode attention");
+  NSRL_TRY(launch_split_planes(ctx16, batch, d, d, ctx, s), "split planes");
+  GemmArgs og{};
+  og.a_hi = ctx.hi;
+  og.a_lo = ctx.lo;
+  og.a_l1 = ctx.l1;
+  og.lda = d;
+  og.M = batch;
+  og.K = d;
+  og.nseg = 1;
+  og.seg[0] = seg_of(o);
+  og.epi = Epi::RESID;
+  og.y = y;
+  og.ldy = d;
+  og.skip = x;
+  og.ldskip = d;
+  og.sat_counter = &status->attention_saturations;
+  og.st = status;
+  NSRL_TRY(launch_gemm(og, s), "output projection");
+  return NSRL_OK;
+}
+
 nsrl_status nsrl_attention_decode(const int16_t* q, const int16_t* k_cache, const int16_t* v_cache,
                                   const int32_t* lens, size_t batch, size_t heads, size_t head_dim, size_t max_len,
                                   int16_t* ctx, nsrl_device_status* status, void* stream) {

@@ -246,3 +246,33 @@ def test_decode_rejects_bad_length(core):
     kc = np.ones((B, Lmax, hd), np.int16)
     lens = np.array([4, 0], np.int32)
     assert core.attention_decode(dev(q), dev(kc), dev(kc), dev(lens), H, hd) is None
+
+
+@pytest.mark.parametrize("B,d,H,Lmax", [(3, 128, 2, 100), (5, 256, 4, 300), (2, 64, 4, 20)])
+def test_decode_block_parity(core, B, d, H, Lmax):
+    """One decode step == last causal row with cached keys/values (attention.rs:671-725, :742-877)."""
+    P = attn_weights(core, d, 55 + d)
+    hd = d // H
+    x = Y.q15_gaussian(3, (B, d))
+    gamma = np.full(d, 4096, np.int16)
+    kc = Y.q15_gaussian(4, (B, Lmax, d), sigma_shift=15)
+    vc = Y.q15_gaussian(5, (B, Lmax, d))
+    pos = (np.arange(B) * 17 % (Lmax - 1)).astype(np.int32)
+    pos[0] = Lmax - 1
+    # oracle: rms -> q, k, v -> cache row pos -> attention over pos + 1 keys -> o -> residual
+    xn = O.rms_norm_rows(x, gamma, 1)
+    q = O.linear(xn, P["q"][0])
+    k = O.linear(xn, P["k"][0])
+    v = O.linear(xn, P["v"][0])
+    kc_ref, vc_ref = kc.copy(), vc.copy()
+    kc_ref[np.arange(B), pos] = k
+    vc_ref[np.arange(B), pos] = v
+    ctx = O.decode_attention(q, kc_ref, vc_ref, pos + 1, B, H, hd, Lmax, threads=4)
+    att = O.linear(ctx, P["o"][0])
+    y_ref, sat_ref = O.residual_add(x, att)
+    kcg, vcg = dev(kc), dev(vc)
+    got = core.prenorm_attention_decode_block(dev(x), H, dev(gamma), 1, *[P[n][1] for n in "qkvo"], kcg, vcg,
+                                              dev(pos))
+    assert got is not None
+    assert np.array_equal(host(got[0]), y_ref) and got[1] == sat_ref
+    assert np.array_equal(host(kcg), kc_ref) and np.array_equal(host(vcg), vc_ref)
