@@ -203,7 +203,7 @@ def run_decode(core, torch, steps, warmup, hbm, flush):
                for nm in ("q", "k", "v", "o", "up", "gate", "down")}
         caches = []
         for _ in range(2):  # K and V: Q15 Gaussian sigma 4096 (K narrower so that the softmax stays live)
-            c = torch.empty((DEC_B, lmax, DEC_D), dtype=torch.int16, device="cuda")
+            c = torch.empty((DEC_B, DEC_H, lmax, DEC_D // DEC_H), dtype=torch.int16, device="cuda")  # head-major
             c.copy_((torch.randn(c.shape, generator=gen, device="cuda") * 4096).clamp_(-32768, 32767).to(torch.int16))
             caches.append(c)
         caches[0] >>= 5

@@ -183,7 +183,8 @@ nsrl_status nsrl_attention_decode(const int16_t* q, const int16_t* k_cache, cons
  * recomputes, crates/nsrl-train/src/lib.rs:118-130).  y[b] = x[b] +
  * O(context), saturations into status->attention_saturations.  The caller
  * advances positions after every layer of the step.  x, y: [batch][d_model];
- * caches: [batch][max_len][d_model] int16, 16-byte aligned. */
+ * caches: head-major [batch][heads][max_len][64] int16, 16-byte aligned, so
+ * that each head's keys and values stream contiguously (head_dim 64). */
 size_t nsrl_decode_block_workspace_size(size_t batch, size_t d_model, size_t heads);
 nsrl_status nsrl_prenorm_attention_decode_block(const int16_t* x, size_t batch, size_t d_model, size_t heads,
                                                 const int16_t* rms_gamma, uint64_t rms_eps,

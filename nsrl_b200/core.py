@@ -273,7 +273,8 @@ class TransformerBlock:
 # ----------------------------------------------------------------- decode ---
 def prenorm_attention_decode_block(x, heads, rms_gamma, rms_eps, q, k, v, o, k_cache, v_cache, positions):
     """One decode step of the prenorm attention block (see nsrl_prenorm_attention_decode_block):
-    x [B, d]; caches [B, Lmax, d] (row positions[b] is written); returns (y, saturations) or None."""
+    x [B, d]; head-major caches [B, H, Lmax, 64] (row positions[b] of every head is written);
+    returns (y, saturations) or None."""
     L = lib()
     if not getattr(L, "_decode_bound", False):
         vp, sz, lp = C.c_void_p, C.c_size_t, C.POINTER(LinearParamsC)
@@ -292,7 +293,7 @@ def prenorm_attention_decode_block(x, heads, rms_gamma, rms_eps, q, k, v, o, k_c
     ps = [l.c() for l in (q, k, v, o)]
     h = _run(lambda: L.nsrl_prenorm_attention_decode_block(
         _ptr(x), B, d, heads, _ptr(g), rms_eps, *[C.byref(p) for p in ps], _ptr(k_cache), _ptr(v_cache), _ptr(pos),
-        k_cache.shape[1], _ptr(y), _ptr(ws), ws.numel(), _ptr(st.buf), _stream()), st)
+        k_cache.shape[2], _ptr(y), _ptr(ws), ws.numel(), _ptr(st.buf), _stream()), st)
     return None if h is None else (y, h.attention_saturations)
 
 def attention_decode(q, k_cache, v_cache, lens, heads, head_dim):

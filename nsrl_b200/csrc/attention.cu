@@ -587,7 +587,7 @@ cudaError_t launch_attention_rows_i16(const int16_t* qkv, size_t B, size_t S, si
 }
 
 __global__ void kv_append_kernel(const int8_t* __restrict__ hi, const uint8_t* __restrict__ lo, long long ld, int d,
-                                 const int32_t* __restrict__ pos, int Lmax, int16_t* __restrict__ q16,
+                                 int hd, const int32_t* __restrict__ pos, int Lmax, int16_t* __restrict__ q16,
                                  int16_t* __restrict__ kc, int16_t* __restrict__ vc, nsrl_device_status* st) {
   const int b = blockIdx.x;
   const int p = pos[b];
@@ -597,26 +597,36 @@ __global__ void kv_append_kernel(const int8_t* __restrict__ hi, const uint8_t* _
     return;
   }
   const long long row = (long long)b * ld;
-  const long long crow = ((long long)b * Lmax + p) * d;
+  const int H = d / hd;
   for (int c = threadIdx.x; c < d; c += blockDim.x) {
+    // cache [B][H][Lmax][hd]: head c / hd, dim c % hd
+    const long long off = (((long long)b * H + c / hd) * Lmax + p) * hd + c % hd;
     q16[(long long)b * d + c] = (int16_t)((int)hi[row + c] * 256 + (int)lo[row + c]);
-    kc[crow + c] = (int16_t)((int)hi[row + d + c] * 256 + (int)lo[row + d + c]);
-    vc[crow + c] = (int16_t)((int)hi[row + 2 * d + c] * 256 + (int)lo[row + 2 * d + c]);
+    kc[off] = (int16_t)((int)hi[row + d + c] * 256 + (int)lo[row + d + c]);
+    vc[off] = (int16_t)((int)hi[row + 2 * d + c] * 256 + (int)lo[row + 2 * d + c]);
   }
 }
 
-cudaError_t launch_kv_append(const Planes& qkv, size_t B, size_t d, const int32_t* pos, size_t Lmax, int16_t* q16,
-                             int16_t* k_cache, int16_t* v_cache, nsrl_device_status* st, cudaStream_t stream) {
+cudaError_t launch_kv_append(const Planes& qkv, size_t B, size_t d, size_t hd, const int32_t* pos, size_t Lmax,
+                             int16_t* q16, int16_t* k_cache, int16_t* v_cache, nsrl_device_status* st,
+                             cudaStream_t stream) {
   if (B == 0) return cudaSuccess;
   ProfScope prof("kv_append", stream, 0.0, 6.0 * (double)(B * d) + 6.0 * (double)(B * d));
-  kv_append_kernel<<<(unsigned)B, 256, 0, stream>>>(qkv.hi, qkv.lo, (long long)qkv.ld, (int)d, pos, (int)Lmax, q16,
-                                                     k_cache, v_cache, st);
+  kv_append_kernel<<<(unsigned)B, 256, 0, stream>>>(qkv.hi, qkv.lo, (long long)qkv.ld, (int)d, (int)hd, pos, (int)Lmax,
+                                                     q16, k_cache, v_cache, st);
   return cudaGetLastError();
 }
 
+cudaError_t launch_decode_tma(const int16_t* q, const int16_t* kc, const int16_t* vc, const int32_t* lens,
+                              size_t B, size_t H, size_t hd, size_t Lmax, int16_t* ctx, nsrl_device_status* st,
+                              cudaStream_t stream, int len_offset, bool head_major);
+
 cudaError_t launch_decode_attention(const int16_t* q, const int16_t* kc, const int16_t* vc, const int32_t* lens,
                                     size_t B, size_t H, size_t hd, size_t Lmax, int16_t* ctx,
-                                    nsrl_device_status* st, cudaStream_t stream, int len_offset) {
+                                    nsrl_device_status* st, cudaStream_t stream, int len_offset, bool head_major) {
+  if (B == 0) return cudaSuccess;
+  const cudaError_t e = launch_decode_tma(q, kc, vc, lens, B, H, hd, Lmax, ctx, st, stream, len_offset, head_major);
+  if (e != cudaErrorNotSupported || head_major) return e;
   const size_t d = H * hd;
   RowArgs a{};
   a.q = q;

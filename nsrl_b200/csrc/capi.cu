@@ -476,8 +476,9 @@ nsrl_status nsrl_prenorm_attention_decode_block(const int16_t* x, size_t batch, 
                                                 nsrl_device_status* status, void* stream) {
   nsrl_status r = validate_attention(1, d_model, heads, q, k, v, o);
   if (r != NSRL_OK) return r;
+  if (d_model / heads != 64) return shape_fail("the decode block takes head_dim 64");
   if (!status || !rms_gamma || !positions || !k_cache || !v_cache) return shape_fail("NULL argument");
-  if (max_len == 0 || max_len > 50000) return shape_fail("max_len must be in 1..50000");
+  if (max_len == 0 || max_len > 24576) return shape_fail("max_len must be in 1..24576");
   if (batch == 0) return NSRL_OK;
   if (((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 15) != 0 || d_model % 8 != 0)
     return shape_fail("caches must be 16-byte aligned and d_model a multiple of 8");
@@ -509,8 +510,9 @@ nsrl_status nsrl_prenorm_attention_decode_block(const int16_t* x, size_t batch, 
   g.yp = qkv;
   g.st = status;
   NSRL_TRY(launch_gemm(g, s), "qkv projection");
-  NSRL_TRY(launch_kv_append(qkv, batch, d, positions, max_len, q16, k_cache, v_cache, status, s), "kv append");
-  NSRL_TRY(launch_decode_attention(q16, k_cache, v_cache, positions, batch, heads, hd, max_len, ctx16, status, s, 1),
+  NSRL_TRY(launch_kv_append(qkv, batch, d, hd, positions, max_len, q16, k_cache, v_cache, status, s), "kv append");
+  NSRL_TRY(launch_decode_attention(q16, k_cache, v_cache, positions, batch, heads, hd, max_len, ctx16, status, s, 1,
+                                   true),
            "decode attention");
   NSRL_TRY(launch_split_planes(ctx16, batch, d, d, ctx, s), "split planes");
   GemmArgs og{};

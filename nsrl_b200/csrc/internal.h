@@ -90,14 +90,18 @@ cudaError_t launch_attention_tc(const Planes& qkv, const VtPlanes& vt, size_t B,
 bool attention_tc_supported(size_t S, size_t d, size_t H);
 
 // KV-cache decode attention (int16 operands).
+// Caches are [B][Lmax][H*hd] (the reference's row layout) or, head_major,
+// [B][H][Lmax][hd] (each head's keys contiguous; head_dim 64 only).
 cudaError_t launch_decode_attention(const int16_t* q, const int16_t* kc, const int16_t* vc, const int32_t* lens,
                                     size_t B, size_t H, size_t hd, size_t Lmax, int16_t* ctx,
-                                    nsrl_device_status* st, cudaStream_t stream, int len_offset = 0);
+                                    nsrl_device_status* st, cudaStream_t stream, int len_offset = 0,
+                                    bool head_major = false);
 
-// Decode step support: q planes -> int16 q, k/v planes -> KV cache row pos[b]
-// of sequence b (pos[b] < Lmax, else NSRL_FLAG_BAD_LENGTH).
-cudaError_t launch_kv_append(const Planes& qkv, size_t B, size_t d, const int32_t* pos, size_t Lmax, int16_t* q16,
-                             int16_t* k_cache, int16_t* v_cache, nsrl_device_status* st, cudaStream_t stream);
+// Decode step support: q planes -> int16 q, k/v planes -> row pos[b] of the
+// head-major KV caches of sequence b (pos[b] < Lmax, else NSRL_FLAG_BAD_LENGTH).
+cudaError_t launch_kv_append(const Planes& qkv, size_t B, size_t d, size_t hd, const int32_t* pos, size_t Lmax,
+                             int16_t* q16, int16_t* k_cache, int16_t* v_cache, nsrl_device_status* st,
+                             cudaStream_t stream);
 
 // Planes -> int16.
 cudaError_t launch_join_planes(Planes in, size_t rows, size_t cols, int16_t* y, size_t ldy, cudaStream_t stream);
