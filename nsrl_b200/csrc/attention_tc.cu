@@ -61,6 +61,8 @@ struct Maps {
 
 struct Args {
   int S, d, H, causal, shift;
+  int16_t* wscr;     // WS: per-CTA scratch of the sum pass's weights w, [128 rows][wstride]
+  long long wstride; // S rounded up to a multiple of 64
   int8_t* ctx_hi;
   uint8_t* ctx_lo;
   unsigned long long* ctx_l1;
@@ -136,6 +138,9 @@ __device__ __forceinline__ void scores_weight(const uint32_t (&hh)[16], const ui
   }
 }
 
+// WS: the sum pass stores its weights w (int16) in global scratch and the
+// last pass reads them back instead of recomputing S (no K tiles, no QK MMAs).
+template <bool WS>
 __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_constant__ Maps maps, const Args a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -199,9 +204,12 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
             break;
           }
           uint8_t* stg = sm + OFF_STAGE + s * STAGE_BYTES;
-          mbar_arrive_expect_tx(&ctl->full[s], pass == 2 ? STAGE_BYTES : 2 * PLANE_K);
-          tma_load_2d(stg, &maps.k_hi, &ctl->full[s], a.d + h * HD, row0 + j * KT);
-          tma_load_2d(stg + PLANE_K, &maps.k_lo, &ctl->full[s], a.d + h * HD, row0 + j * KT);
+          const bool kload = !(WS && pass == 2);
+          mbar_arrive_expect_tx(&ctl->full[s], (kload ? 2 * PLANE_K : 0) + (pass == 2 ? 2 * PLANE_V : 0));
+          if (kload) {
+            tma_load_2d(stg, &maps.k_hi, &ctl->full[s], a.d + h * HD, row0 + j * KT);
+            tma_load_2d(stg + PLANE_K, &maps.k_lo, &ctl->full[s], a.d + h * HD, row0 + j * KT);
+          }
           if (pass == 2) {
             const int vrow = (b * a.H + h) * HD;
             tma_load_2d(stg + 2 * PLANE_K, &maps.vt_hi, &ctl->full[s], j * KT, vrow);
@@ -254,14 +262,17 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
       // pass 2: S(j+1) is issued before O += P(j) V(j) so that the softmax
       // warps can work on tile j+1 while the tensor core does the AV product.
       const uint32_t base = it;
-      wait_bar(&ctl->full[base % ST], (base / ST) & 1, ctl, a.st);
-      issue_s(base % ST, 0);
+      if (!WS) {
+        wait_bar(&ctl->full[base % ST], (base / ST) & 1, ctl, a.st);
+        issue_s(base % ST, 0);
+      }
       for (int j = 0; j < ntiles; ++j) {
-        if (j + 1 < ntiles) {
+        if (!WS && j + 1 < ntiles) {
           const uint32_t n1 = base + j + 1;
           wait_bar(&ctl->full[n1 % ST], (n1 / ST) & 1, ctl, a.st);
           issue_s(n1 % ST, 0);
         }
+        if (WS) wait_bar(&ctl->full[(base + j) % ST], ((base + j) / ST) & 1, ctl, a.st);
         const int pb = j & 1;
         wait_bar(&ctl->p_full[pb], (j >> 1) & 1, ctl, a.st);
         tc_fence_after();
@@ -310,8 +321,25 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
     uint32_t use0 = 0, use1 = 0;  // uses of each S buffer, in the MMA issuer's order
     uint32_t it = 0;            // items of the max and sum passes
     bool range_bad = false, masked_bad = false;
+    // WS: this thread's row of the weight scratch
+    int16_t* wrow = WS ? a.wscr + ((((long long)b * a.H + h) * gridDim.x + blockIdx.x) * QT + row) * a.wstride
+                       : nullptr;
     for (int pass = 0; pass < 3; ++pass) {
       for (int j = 0; j < ntiles; ++j) {
+        const int key0 = j * KT + 16 * g;
+        const int nlive = max(0, min(16, last_key - key0 + 1));
+        int w[16];
+        if (WS && pass == 2) {
+          // weights of the sum pass (0 beyond the live keys)
+          const uint4* src = reinterpret_cast<const uint4*>(wrow + key0);
+          const uint4 u0 = src[0], u1 = src[1];
+          const uint32_t wv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            w[2 * i] = (int)(wv[i] & 0xFFFF);
+            w[2 * i + 1] = (int)(wv[i] >> 16);
+          }
+        } else {
         const int sb = pass < 2 ? (int)(it++ & 1) : 0;
         uint32_t hh[16], mid[16], ll[16];
         wait_bar(&ctl->s_full[sb], (sb ? use1 : use0) & 1, ctl, a.st);
@@ -328,8 +356,6 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&ctl->s_empty[sb]);
-        const int key0 = j * KT + 16 * g;
-        const int nlive = max(0, min(16, last_key - key0 + 1));
         const bool full = __all_sync(0xffffffffu, nlive == 16) != 0;
         if (pass == 0) {
           if (full)
@@ -338,7 +364,6 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
             scores_max<false>(hh, mid, ll, nlive, mx32, mx64, mn64);
           continue;
         }
-        int w[16];
         if (!slow_row) {
           if (full)
             scores_weight<true>(hh, mid, ll, nlive, hh_floor, rawmax_lo, cround, lut, w);
@@ -362,6 +387,14 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
             }
             w[i] = wi;
           }
+        }
+        if (WS && pass == 1) {
+          uint4* dst = reinterpret_cast<uint4*>(wrow + key0);
+          dst[0] = make_uint4((uint32_t)w[0] | ((uint32_t)w[1] << 16), (uint32_t)w[2] | ((uint32_t)w[3] << 16),
+                              (uint32_t)w[4] | ((uint32_t)w[5] << 16), (uint32_t)w[6] | ((uint32_t)w[7] << 16));
+          dst[1] = make_uint4((uint32_t)w[8] | ((uint32_t)w[9] << 16), (uint32_t)w[10] | ((uint32_t)w[11] << 16),
+                              (uint32_t)w[12] | ((uint32_t)w[13] << 16), (uint32_t)w[14] | ((uint32_t)w[15] << 16));
+        }
         }
         if (pass == 1) {
           unsigned s = 0;
@@ -507,8 +540,18 @@ bool attention_tc_supported(size_t S, size_t d, size_t H) {
   return H != 0 && d / H == (size_t)HD && d % H == 0 && S % 16 == 0 && S <= 16384 && (3 * d) % 16 == 0;
 }
 
+size_t attention_tc_wstride(size_t S) { return (S + KT - 1) / KT * KT; }
+
+size_t attention_tc_scratch_bytes(size_t B, size_t S, size_t d, size_t H) {
+  if (!attention_tc_supported(S, d, H)) return 0;
+  const size_t nq = (S + QT - 1) / QT;
+  const size_t bytes = B * H * nq * QT * attention_tc_wstride(S) * sizeof(int16_t);
+  return bytes <= ((size_t)4 << 30) ? bytes : 0;  // beyond 4 GiB the last pass recomputes S instead
+}
+
 cudaError_t launch_attention_tc(const Planes& qkv, const VtPlanes& vt, size_t B, size_t S, size_t d, size_t H,
-                                bool causal, Planes ctx, nsrl_device_status* st, cudaStream_t stream) {
+                                bool causal, Planes ctx, int16_t* wscr, nsrl_device_status* st,
+                                cudaStream_t stream) {
   if (!attention_tc_supported(S, d, H) || encode_fn() == nullptr) return cudaErrorNotSupported;
   const size_t T = B * S;
   Maps m;
@@ -529,15 +572,23 @@ cudaError_t launch_attention_tc(const Planes& qkv, const VtPlanes& vt, size_t B,
   a.st = st;
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(attention_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)SMEM_BYTES);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(attention_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)SMEM_BYTES);
     if (e != cudaSuccess) return e;
     configured = true;
   }
+  a.wscr = wscr;
+  a.wstride = (long long)attention_tc_wstride(S);
   dim3 grid((unsigned)((S + QT - 1) / QT), (unsigned)H, (unsigned)B);
   const double pairs = causal ? (double)S * (S + 1) / 2.0 : (double)S * S;
   ProfScope prof("attention_tc_hd64", stream, 4.0 * HD * (double)H * (double)B * pairs, 8.0 * (double)T * (double)d);
-  attention_tc_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(m, a);
+  if (wscr)
+    attention_tc_kernel<true><<<grid, THREADS, SMEM_BYTES, stream>>>(m, a);
+  else
+    attention_tc_kernel<false><<<grid, THREADS, SMEM_BYTES, stream>>>(m, a);
   return cudaGetLastError();
 }
 

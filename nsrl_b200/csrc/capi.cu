@@ -90,10 +90,12 @@ bool attention_prefill_native(size_t d, size_t H, size_t S) {
 
 // Transposed V planes for the tensor-core attention (empty when it does not apply).
 VtPlanes carve_vt(Carver& c, size_t B, size_t S, size_t d, size_t H) {
-  VtPlanes vt{nullptr, nullptr, (int)S, (int)H, (int)(d / H)};
+  VtPlanes vt{nullptr, nullptr, (int)S, (int)H, (int)(d / H), nullptr};
   if (attention_tc_supported(S, d, H)) {
     vt.hi = c.take<int8_t>(B * S * d);
     vt.lo = c.take<uint8_t>(B * S * d);
+    const size_t ws = attention_tc_scratch_bytes(B, S, d, H);
+    if (ws) vt.wscr = c.take<int16_t>(ws / sizeof(int16_t));
   }
   return vt;
 }
@@ -110,6 +112,8 @@ size_t attention_ws(size_t B, size_t S, size_t d, size_t H, Carver* c = nullptr)
   if (attention_tc_supported(S, d, H)) {
     k.take<int8_t>(T * d);
     k.take<uint8_t>(T * d);
+    const size_t ws = attention_tc_scratch_bytes(B, S, d, H);
+    if (ws) k.take<int16_t>(ws / sizeof(int16_t));
   }
   if (!attention_prefill_native(d, H, S)) {
     k.take<int16_t>(T * 3 * d);
@@ -155,7 +159,7 @@ nsrl_status attention_core(const Planes& xin, size_t B, size_t S, size_t d, size
   if (!needs_l1(d, o)) ctx.l1 = nullptr;
   if (ctx.l1) NSRL_TRY(cudaMemsetAsync(ctx.l1, 0, T * sizeof(unsigned long long), stream), "memset");
   if (tc) {
-    NSRL_TRY(launch_attention_tc(qkv, vt, B, S, d, H, causal, ctx, st, stream), "attention");
+    NSRL_TRY(launch_attention_tc(qkv, vt, B, S, d, H, causal, ctx, vt.wscr, st, stream), "attention");
   } else if (attention_prefill_native(d, H, S)) {
     NSRL_TRY(launch_attention(qkv, B, S, d, H, causal, ctx, st, stream), "attention");
   } else {

@@ -41,6 +41,7 @@ struct VtPlanes {
   int8_t* hi;
   uint8_t* lo;
   int S, H, hd;
+  int16_t* wscr;  // weight scratch of the tensor-core attention (may be null)
 };
 
 struct GemmArgs {
@@ -83,8 +84,13 @@ cudaError_t launch_attention(const Planes& qkv, size_t B, size_t S, size_t d, si
 // Tensor-core (tcgen05) attention core for head_dim 64: q, k from the q|k|v
 // planes, v from the transposed planes of Epi::QKV_VT.  Returns
 // cudaErrorNotSupported when the shape is outside what it takes.
+// wscr (optional, attention_tc_scratch_bytes): weights of the sum pass, so
+// that the last pass does not recompute Q K^T.
 cudaError_t launch_attention_tc(const Planes& qkv, const VtPlanes& vt, size_t B, size_t S, size_t d, size_t H,
-                                bool causal, Planes ctx, nsrl_device_status* st, cudaStream_t stream);
+                                bool causal, Planes ctx, int16_t* wscr, nsrl_device_status* st,
+                                cudaStream_t stream);
+size_t attention_tc_wstride(size_t S);
+size_t attention_tc_scratch_bytes(size_t B, size_t S, size_t d, size_t H);
 // Shape rule of the tensor-core attention (head_dim 64, seq_len % 16 == 0,
 // seq_len <= 16384); the workspace reserves the transposed V planes for it.
 bool attention_tc_supported(size_t S, size_t d, size_t H);

@@ -48,7 +48,9 @@ def test_workspace_sizes_are_consistent(lib):
     T, d, H, F = 64 * 1024, 256, 4, 1024
     a = lib.nsrl_attention_workspace_size(64, 1024, d, H)
     # + transposed V planes (2 bytes / element) for the tensor-core attention (head_dim 64)
-    assert a == T * d * 2 + T * 8 + T * 3 * d * 2 + T * d * 2 + T * 8 + T * d * 2
+    # + its weight scratch: 128-row query tiles x 64-key-padded rows of int16 per (sequence, head)
+    S, B = 1024, 64
+    assert a == T * d * 2 + T * 8 + T * 3 * d * 2 + T * d * 2 + T * 8 + T * d * 2 + B * H * S * S * 2
     assert lib.nsrl_transformer_block_workspace_size(64, 1024, d, H, F) >= a + T * d * 2
 
 
