@@ -189,9 +189,10 @@ DEC_LAYERS, DEC_D, DEC_H, DEC_F, DEC_B, DEC_PREFIX = 4, 512, 8, 2048, 256, 8192
 SWEEP_M, SWEEP_KN = (4096, 16384, 65536), (256, 1024, 4096)
 
 
-def run_decode(core, torch, steps, warmup, hbm, flush):
+def run_decode(core, torch, steps, warmup, hbm, flush, batch=DEC_B):
     """4-layer KV-cache decode steps: per layer the prenorm attention decode block then the
     prenorm gated-MLP block over the batch's new tokens; the caches hold DEC_PREFIX + t rows."""
+    DEC_B = batch
     from nsrl_b200 import synth as Y
     L = core.lib()
     gen = torch.Generator(device="cuda").manual_seed(5)
@@ -347,6 +348,22 @@ def roofline(rows, hbm_gbs, tflops, src):
     return out
 
 
+def run_secondary(args):
+    """One secondary measurement alone on cuda:0 (its JSON object on one line)."""
+    import torch
+    from nsrl_b200 import build, core
+    build.build()
+    hbm, tfl, _ = peaks()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    if args.case == "decode":
+        out = run_decode(core, torch, steps=args.steps, warmup=args.warmup, hbm=hbm, flush=flush,
+                         batch=args.decode_batch)
+    else:
+        out = run_sweep(core, torch, hbm, tfl, flush)
+    print(json.dumps(out), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -355,9 +372,14 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip the decode and linear-sweep measurements")
+    ap.add_argument("--case", default="block", choices=["block", "decode", "sweep"],
+                    help="decode / sweep: run only that secondary measurement (a small case for profiling)")
+    ap.add_argument("--decode-batch", type=int, default=DEC_B)
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.case != "block":
+        return run_secondary(args)
 
     import torch
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -57,13 +57,22 @@ __device__ __forceinline__ int16_t requant_i32(int acc, int mult, uint32_t shift
   return sat_i16(rhu64((long long)acc * (long long)mult, shift));
 }
 
-// mlp.rs:150-170: hard-SiLU gate and the gated activation.  Both products are
-// below 2^30 in magnitude, so rhu(v, 15) = (v + 2^14) >> 15 in i32 is exact.
+// Saturating i32 -> i16 (one cvt.sat), returned sign-extended.
+__device__ __forceinline__ int sat16(int v) {
+  short r;
+  asm("cvt.sat.s16.s32 %0, %1;" : "=h"(r) : "r"(v));
+  return (int)r;
+}
+
+// mlp.rs:150-170: hard-SiLU gate and the gated activation.  For an i16 gate
+// g, (g >> 2) + 16384 lies in [8192, 24575], so the clamp to [0, 32767] never
+// acts; |g * gate| and |up * silu| stay below 32768 * 24575 < 2^30, so
+// rhu(v, 15) = (v + 2^14) >> 15 in i32 is exact and both results lie within
+// +-24575: neither saturation acts either.
 __device__ __forceinline__ int16_t gated_act(int16_t up, int16_t gate) {
-  int g = ((int)gate >> 2) + 16384;
-  g = max(0, min(32767, g));
-  const int silu = max(-32768, min(32767, ((int)gate * g + 16384) >> 15));
-  return (int16_t)max(-32768, min(32767, ((int)up * silu + 16384) >> 15));
+  const int gv = ((int)gate >> 2) + 16384;
+  const int silu = ((int)gate * gv + 16384) >> 15;
+  return (int16_t)(((int)up * silu + 16384) >> 15);
 }
 
 // attention.rs:142-158 with the table in shared memory.

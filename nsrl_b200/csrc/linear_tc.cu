@@ -67,6 +67,7 @@ struct TcParams {
   int8_t* vth;
   uint8_t* vtl;
   int vt_S, vt_H, vt_hd, vt_col0;  // QKV_VT: output columns >= vt_col0 go to the transposed planes
+  bool small_acc;                   // K * 127 * 32767 < 2^30: every accumulator is below 2^30
   nsrl_device_status* st;
 };
 
@@ -113,19 +114,25 @@ __device__ __forceinline__ ColScale load_scales(const nsrl_fixed_scale* sc, cons
 
 // requantize_i32_to_i16 of W columns: acc = 256*hi + lo (+ bias), wrapping
 // u32 arithmetic (exact whenever the true i32 sum fits).
+// `small`: |acc| < 2^30 (K * 127 * 32767 < 2^30, no bias), so acc + 2^(s-1)
+// cannot overflow and rhu is one add and one shift.
 template <int W>
 __device__ __forceinline__ void requant_cols(const uint32_t (&h)[W], const uint32_t (&l)[W], const ColScale& c,
-                                             int (&v)[W]) {
+                                             int (&v)[W], bool small) {
   if (c.uniform) {
     const uint32_t s = (uint32_t)c.ushift;
     if (s == 0) {
 #pragma unroll
-      for (int i = 0; i < W; ++i) v[i] = max(-32768, min(32767, (int)(h[i] * 256u + l[i])));
+      for (int i = 0; i < W; ++i) v[i] = sat16((int)(h[i] * 256u + l[i]));
+    } else if (s < 32 && small) {
+      const int half = 1 << (s - 1);
+#pragma unroll
+      for (int i = 0; i < W; ++i) v[i] = sat16(((int)(h[i] * 256u + l[i]) + half) >> s);
     } else if (s < 32) {
 #pragma unroll
       for (int i = 0; i < W; ++i) {
         const int acc = (int)(h[i] * 256u + l[i]);
-        v[i] = max(-32768, min(32767, (acc >> s) + ((acc >> (s - 1)) & 1)));
+        v[i] = sat16((acc >> s) + ((acc >> (s - 1)) & 1));
       }
     } else {
 #pragma unroll
@@ -142,12 +149,12 @@ __device__ __forceinline__ void requant_cols(const uint32_t (&h)[W], const uint3
   }
 }
 __device__ __forceinline__ void requant32(const uint32_t (&h)[32], const uint32_t (&l)[32], const ColScale& c,
-                                          int (&v)[32]) {
-  requant_cols<32>(h, l, c, v);
+                                          int (&v)[32], bool small) {
+  requant_cols<32>(h, l, c, v, small);
 }
 __device__ __forceinline__ void requant16(const uint32_t (&h)[16], const uint32_t (&l)[16], const ColScale& c,
-                                          int (&v)[16]) {
-  requant_cols<16>(h, l, c, v);
+                                          int (&v)[16], bool small) {
+  requant_cols<16>(h, l, c, v, small);
 }
 
 // Splits 16 packed int16 values into hi / lo byte planes (+ L1 of the values).
@@ -371,8 +378,8 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
         tc_fence_before();
         if (lane == 0) mbar_arrive(&acc_empty[buf]);
         int up[16], gt[16];
-        requant16(hu, lu, su, up);
-        requant16(hg, lg, sg, gt);
+        requant16(hu, lu, su, up, p.small_acc);
+        requant16(hg, lg, sg, gt, p.small_acc);
         uint32_t o[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i)
@@ -421,7 +428,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
         tc_fence_before();
         if (lane == 0) mbar_arrive(&acc_empty[buf]);
         int v[32];
-        requant32(h, l, sc, v);
+        requant32(h, l, sc, v, p.small_acc);
         uint32_t o[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) o[i] = pack2(v[2 * i], v[2 * i + 1]);
@@ -433,9 +440,10 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
             for (int i = 0; i < 16; ++i) {
               const int a = (int)(int16_t)(s16[i] & 0xFFFF) + v[2 * i];
               const int b = (int)(int16_t)(s16[i] >> 16) + v[2 * i + 1];
-              if (2 * i < nvalid && (a < -32768 || a > 32767)) ++sat;
-              if (2 * i + 1 < nvalid && (b < -32768 || b > 32767)) ++sat;
-              o[i] = pack2(max(-32768, min(32767, a)), max(-32768, min(32767, b)));
+              const int sa = sat16(a), sb = sat16(b);
+              if (2 * i < nvalid && sa != a) ++sat;
+              if (2 * i + 1 < nvalid && sb != b) ++sat;
+              o[i] = pack2(sa, sb);
             }
             store32_i16(p.y + (long long)r * p.ldy + n, o, nvalid, vec_skip);
           } else if (EPI == (int)Epi::QKV_VT && n >= p.vt_col0) {
@@ -773,6 +781,7 @@ cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t stream) {
   p.vt_H = a.vt.H;
   p.vt_hd = a.vt.hd;
   p.vt_col0 = a.epi == Epi::QKV_VT ? 2 * (int)a.seg[0].rows : INT_MAX;
+  p.small_acc = (unsigned long long)a.K * 127ull * 32767ull < (1ull << 30);
   p.st = a.st;
 
   bool tc = tma_supported() && (a.K % 16) == 0 && (a.lda % 16) == 0 && aligned16(a.a_hi) && aligned16(a.a_lo);
