@@ -751,3 +751,623 @@ int orc_merge_i64(const int64_t* parts, size_t workers, size_t len, const uint64
 }
 
 }  // extern "C"
+
+// ============================================================ training step ==
+// Rows of the integer training step: backward-input linears, gated-MLP and
+// RMS-norm backward, softmax-attention backward, i64 weight-gradient
+// accumulation, the byte-vocabulary output head and the map-reduce worker
+// loop of the reference's mini transformer.
+namespace orc {
+
+static const FixedScale IDENTITY_SCALE = {1, 0, {0, 0, 0}};
+static const FixedScale OUTPUT_SCALE = {1, 8, {0, 0, 0}};  // nsrl-train-core/src/lib.rs:84-87
+constexpr uint8_t FANIN_SHIFT = 1;                            // nsrl-train-core/src/lib.rs:48
+constexpr int64_t LN2_Q15 = 22713;                            // nsrl-train/src/lib.rs:117
+constexpr uint64_t TRAIN_RMS_EPS = 1;                         // nsrl-train/src/lib.rs:104
+constexpr size_t VOCAB = 256;
+
+static bool scale_ok(FixedScale s) { return s.multiplier >= 0 && s.right_shift <= MAX_RIGHT_SHIFT; }
+
+// linear.rs:735-742 then the i32 conversion of :573-592
+static bool prescale_grad(int16_t g, FixedScale s, int32_t* out) {
+  if (!scale_ok(s)) return false;
+  int64_t wide = rhu((int64_t)g * (int64_t)s.multiplier, s.right_shift);
+  if (wide < INT32_MIN || wide > INT32_MAX) return false;
+  *out = (int32_t)wide;
+  return true;
+}
+
+// linear.rs:744-751
+static bool requantize_i64_to_i16(int64_t acc, FixedScale s, int16_t* out) {
+  if (!scale_ok(s)) return false;
+  int64_t wide;
+  if (__builtin_mul_overflow(acc, (int64_t)s.multiplier, &wide)) return false;
+  *out = saturate_i16(rhu(wide, s.right_shift));
+  return true;
+}
+
+// linear.rs:548-640: dx[k] = requant_i64(sum_n g'[n] * W[n][k]) for one row,
+// g' the grad prescaled by the forward scales.  gin = null: identity scales.
+static bool linear_backward_input_row(const int16_t* g, const LinearParams& p, const FixedScale* gin,
+                                      int16_t* dx) {
+  const size_t K = p.input_dim, N = p.output_dim;
+  if (K == 0 || N == 0) return false;
+  std::vector<int32_t> gs(N);
+  for (size_t n = 0; n < N; ++n)
+    if (!prescale_grad(g[n], p.scales[n], &gs[n])) return false;
+  for (size_t k = 0; k < K; ++k) {
+    int64_t acc = 0;
+    for (size_t n = 0; n < N; ++n) {
+      int64_t prod = (int64_t)gs[n] * (int64_t)p.weights[n * K + k];
+      if (__builtin_add_overflow(acc, prod, &acc)) return false;
+    }
+    if (!requantize_i64_to_i16(acc, gin ? gin[k] : IDENTITY_SCALE, &dx[k])) return false;
+  }
+  return true;
+}
+
+// mlp.rs:162-164
+static int16_t hard_silu_derivative_q15(int16_t v) { return (int16_t)(((int32_t)v >> 1) + HARD_SILU_GATE_BIAS_Q15); }
+
+// mlp.rs:172-194
+static void gated_activation_backward(int16_t up, int16_t gate, int16_t g, int16_t* gu, int16_t* gg) {
+  const int64_t silu = hard_silu_q15(gate);
+  const int64_t grad_up = rhu((int64_t)g * silu, 15);
+  const int64_t grad_silu = rhu((int64_t)g * (int64_t)up, 15);
+  const int64_t grad_gate = rhu(grad_silu * (int64_t)hard_silu_derivative_q15(gate), 15);
+  *gu = saturate_i16(grad_up);
+  *gg = saturate_i16(grad_gate);
+}
+
+// mlp.rs:256-357 (with identity grad-input scales, as the mini transformer
+// passes them): per token down^T, the product rule, up^T and gate^T, and the
+// saturating sum of the two input gradients (mlp.rs:712-727).
+static bool gated_mlp_backward_input_rows(const int16_t* grad_out, size_t T, size_t d, size_t F,
+                                          const LinearParams* lp, const int16_t* up, const int16_t* gate,
+                                          int16_t* grad_up, int16_t* grad_gate, int16_t* grad_in, uint64_t* sat) {
+  std::vector<int16_t> gg(F), gui(d), ggi(d);
+  for (size_t t = 0; t < T; ++t) {
+    if (!linear_backward_input_row(grad_out + t * d, lp[2], nullptr, gg.data())) return false;
+    for (size_t f = 0; f < F; ++f)
+      gated_activation_backward(up[t * F + f], gate[t * F + f], gg[f], &grad_up[t * F + f], &grad_gate[t * F + f]);
+    if (!linear_backward_input_row(grad_up + t * F, lp[0], nullptr, gui.data())) return false;
+    if (!linear_backward_input_row(grad_gate + t * F, lp[1], nullptr, ggi.data())) return false;
+    for (size_t i = 0; i < d; ++i) {
+      int32_t w = (int32_t)gui[i] + (int32_t)ggi[i];
+      if (w < -32768 || w > 32767) ++*sat;
+      grad_in[t * d + i] = saturate_i16(w);
+    }
+  }
+  return true;
+}
+
+// rms_norm.rs:172-179: (num + den / 2).div_euclid(den)
+static int64_t round_ratio_rhu(int64_t num, int64_t den) {
+  __int128 t = (__int128)num + den / 2;
+  __int128 q = t / den;
+  if (t % den < 0) q -= 1;
+  return (int64_t)q;
+}
+
+// rms_norm.rs:96-170 for one row; gamma gradients added into gw (i64).
+static bool rms_norm_backward_row(const int16_t* x, const int16_t* w, const int16_t* go, size_t d, uint64_t eps,
+                                  int16_t* gi, int64_t* gw, uint64_t* sat) {
+  if (d == 0) return false;
+  uint64_t sum = 0;
+  for (size_t i = 0; i < d; ++i) sum += (uint64_t)((int64_t)x[i] * (int64_t)x[i]);
+  uint64_t mean = sum / d, v;
+  if (__builtin_add_overflow(mean, eps, &v)) return false;
+  int64_t inv;
+  if (!integer_rsqrt_q30(v, &inv)) return false;
+  std::vector<int32_t> normalized(d), scaled(d);
+  int64_t dot = 0;
+  for (size_t i = 0; i < d; ++i) {
+    int64_t t;
+    if (__builtin_mul_overflow((int64_t)x[i], inv, &t)) return false;
+    int64_t nm = rhu(t, 15);
+    if (nm < INT32_MIN || nm > INT32_MAX) return false;
+    normalized[i] = (int32_t)nm;
+    int64_t xw = (int64_t)x[i] * (int64_t)w[i], pr;
+    if (__builtin_mul_overflow(xw, inv, &pr)) return false;
+    const int64_t projected = rhu(pr, RMSNORM_INV_RMS_SHIFT);
+    const bool active = projected >= -32768 && projected <= 32767;
+    int32_t sg = 0;
+    if (active) {
+      int64_t s = rhu((int64_t)go[i] * (int64_t)w[i], 15);
+      if (s < INT32_MIN || s > INT32_MAX) return false;
+      sg = (int32_t)s;
+    }
+    scaled[i] = sg;
+    int64_t prod;
+    if (__builtin_mul_overflow((int64_t)sg, (int64_t)nm, &prod)) return false;
+    if (__builtin_add_overflow(dot, prod, &dot)) return false;
+    int64_t gg = 0;
+    if (active) {
+      int64_t q;
+      if (__builtin_mul_overflow((int64_t)go[i], nm, &q)) return false;
+      gg = rhu(q, 15);
+    }
+    if (__builtin_add_overflow(gw[i], gg, &gw[i])) return false;
+  }
+  const int64_t mean_dot = round_ratio_rhu(dot, (int64_t)d << 15);
+  for (size_t i = 0; i < d; ++i) {
+    int64_t c;
+    if (__builtin_mul_overflow((int64_t)normalized[i], mean_dot, &c)) return false;
+    const int64_t cross = rhu(c, 15);
+    int64_t corr;
+    if (__builtin_sub_overflow((int64_t)scaled[i], cross, &corr)) return false;
+    int64_t wide;
+    if (__builtin_mul_overflow(corr, inv, &wide)) return false;
+    const int64_t g = rhu(wide, RMSNORM_INV_RMS_SHIFT);
+    const int16_t cl = saturate_i16(g);
+    if ((int64_t)cl != g) ++*sat;
+    gi[i] = cl;
+  }
+  return true;
+}
+
+// nsrl-train/src/lib.rs:15353-15418: P[h][q][k] of a causal sequence, 0 above the diagonal.
+static bool attention_probabilities(const int16_t* q, const int16_t* k, size_t S, size_t d, size_t H, int16_t* P) {
+  const size_t hd = d / H;
+  const int shift = sqrt_power_of_four_shift(hd);
+  if (shift < 0) return false;
+  std::vector<int32_t> logits(S);
+  for (size_t h = 0; h < H; ++h)
+    for (size_t t = 0; t < S; ++t) {
+      int16_t* row = P + (h * S + t) * S;
+      for (size_t j = 0; j <= t; ++j)
+        if (!qk_dot(q + t * d + h * hd, k + j * d + h * hd, hd, shift, &logits[j])) return false;
+      if (!base2_softmax(logits.data(), t + 1, row, nullptr)) return false;
+      for (size_t j = t + 1; j < S; ++j) row[j] = 0;
+    }
+  return true;
+}
+
+// nsrl-train/src/lib.rs:16623-16900: gradients of the causal base-2 softmax
+// attention of one sequence.  dC = grad of the context [S][d].
+static bool attention_backward(const int16_t* q, const int16_t* k, const int16_t* v, const int16_t* P,
+                               const int16_t* dC, size_t S, size_t d, size_t H, int16_t* dq, int16_t* dk,
+                               int16_t* dv) {
+  const size_t hd = d / H;
+  const int shift = sqrt_power_of_four_shift(hd);
+  if (shift < 0) return false;
+  std::vector<int16_t> dP(H * S * S, 0), dL(H * S * S, 0);
+  for (size_t h = 0; h < H; ++h) {
+    const size_t o = h * hd;
+    // probability gradient (:16623-16677)
+    for (size_t t = 0; t < S; ++t)
+      for (size_t j = 0; j <= t; ++j) {
+        int64_t acc = 0;
+        for (size_t c = 0; c < hd; ++c) acc += (int64_t)dC[t * d + o + c] * (int64_t)v[j * d + o + c];
+        dP[(h * S + t) * S + j] = saturate_i16(rhu(acc, Q15_SHIFT));
+      }
+    // logit gradient (:16679-16747)
+    for (size_t t = 0; t < S; ++t) {
+      const int16_t* pr = P + (h * S + t) * S;
+      const int16_t* gp = &dP[(h * S + t) * S];
+      int64_t wsum = 0;
+      for (size_t j = 0; j <= t; ++j) {
+        if (pr[j] < 0) return false;
+        wsum += (int64_t)gp[j] * (int64_t)pr[j];
+      }
+      const int64_t wq = rhu(wsum, Q15_SHIFT);
+      for (size_t j = 0; j <= t; ++j) {
+        const int64_t centered = (int64_t)gp[j] - wq;
+        int64_t prod;
+        if (__builtin_mul_overflow((int64_t)pr[j] * centered, LN2_Q15, &prod)) return false;
+        dL[(h * S + t) * S + j] = saturate_i16(rhu(prod, 2 * Q15_SHIFT));
+      }
+    }
+    // q / k gradients (:16749-16839)
+    for (size_t t = 0; t < S; ++t)
+      for (size_t c = 0; c < hd; ++c) {
+        int64_t acc = 0;
+        for (size_t j = 0; j <= t; ++j) acc += (int64_t)dL[(h * S + t) * S + j] * (int64_t)k[j * d + o + c];
+        dq[t * d + o + c] = saturate_i16(rhu(acc, (uint8_t)shift));
+      }
+    for (size_t j = 0; j < S; ++j)
+      for (size_t c = 0; c < hd; ++c) {
+        int64_t acc = 0;
+        for (size_t t = j; t < S; ++t) acc += (int64_t)dL[(h * S + t) * S + j] * (int64_t)q[t * d + o + c];
+        dk[j * d + o + c] = saturate_i16(rhu(acc, (uint8_t)shift));
+      }
+    // value gradient (:16841-16900)
+    for (size_t j = 0; j < S; ++j)
+      for (size_t c = 0; c < hd; ++c) {
+        int64_t acc = 0;
+        for (size_t t = 0; t < S; ++t) {
+          const int16_t p = P[(h * S + t) * S + j];
+          if (p < 0) return false;
+          acc += (int64_t)p * (int64_t)dC[t * d + o + c];
+        }
+        dv[j * d + o + c] = saturate_i16(rhu(acc, Q15_SHIFT));
+      }
+  }
+  return true;
+}
+
+// nsrl-train-core/src/lib.rs:344-384 for one row, with the prescale of
+// linear.rs:573-592 in front (the wrappers at nsrl-train/src/lib.rs:13783-14055).
+static bool accumulate_row(const int16_t* x, const int16_t* g, const LinearParams& p, int64_t* acc,
+                           uint64_t* count) {
+  const size_t K = p.input_dim, N = p.output_dim;
+  for (size_t n = 0; n < N; ++n) {
+    int32_t gs;
+    if (!prescale_grad(g[n], p.scales[n], &gs)) return false;
+    if (gs == 0) continue;
+    for (size_t kk = 0; kk < K; ++kk) {
+      if (x[kk] == 0) continue;
+      if (__builtin_add_overflow(acc[n * K + kk], (int64_t)gs * (int64_t)x[kk], &acc[n * K + kk])) return false;
+    }
+  }
+  *count += 1;
+  return true;
+}
+
+}  // namespace orc
+
+// ---------------------------------------------------------------------------
+// C ABI of the training restatement.
+// ---------------------------------------------------------------------------
+extern "C" {
+
+// linear.rs:548-640 over rows.  gin: grad-input scales [K] or null (identity).
+int orc_linear_backward_input(const int16_t* g, size_t M, const LinearParams* p, const FixedScale* gin,
+                              int16_t* dx) {
+  for (size_t m = 0; m < M; ++m)
+    if (!linear_backward_input_row(g + m * p->output_dim, *p, gin, dx + m * p->input_dim)) return 1;
+  return 0;
+}
+
+void orc_gated_activation_backward(int16_t up, int16_t gate, int16_t g, int16_t* gu, int16_t* gg) {
+  gated_activation_backward(up, gate, g, gu, gg);
+}
+
+// mlp.rs:256-357; lp = {up, gate, down}.
+int orc_gated_mlp_backward_input(const int16_t* grad_out, size_t T, size_t d, size_t F, const LinearParams* lp,
+                                 const int16_t* up, const int16_t* gate, int16_t* grad_up, int16_t* grad_gate,
+                                 int16_t* grad_in, uint64_t* sat) {
+  *sat = 0;
+  return gated_mlp_backward_input_rows(grad_out, T, d, F, lp, up, gate, grad_up, grad_gate, grad_in, sat) ? 0 : 1;
+}
+
+// rms_norm.rs:96-170 over rows (nsrl-train/src/lib.rs:15030-15077).
+int orc_rms_norm_backward_rows(const int16_t* x, size_t T, size_t d, const int16_t* w, const int16_t* go,
+                               uint64_t eps, int16_t* gi, int64_t* gw, uint64_t* sat) {
+  *sat = 0;
+  for (size_t t = 0; t < T; ++t)
+    if (!rms_norm_backward_row(x + t * d, w, go + t * d, d, eps, gi + t * d, gw, sat)) return 1;
+  return 0;
+}
+
+int orc_attention_probabilities(const int16_t* q, const int16_t* k, size_t B, size_t S, size_t d, size_t H,
+                                int16_t* P) {
+  for (size_t b = 0; b < B; ++b)
+    if (!attention_probabilities(q + b * S * d, k + b * S * d, S, d, H, P + b * H * S * S)) return 1;
+  return 0;
+}
+
+int orc_attention_backward(const int16_t* q, const int16_t* k, const int16_t* v, const int16_t* P,
+                           const int16_t* dC, size_t B, size_t S, size_t d, size_t H, int16_t* dq, int16_t* dk,
+                           int16_t* dv) {
+  for (size_t b = 0; b < B; ++b) {
+    const size_t o = b * S * d;
+    if (!attention_backward(q + o, k + o, v + o, P + b * H * S * S, dC + o, S, d, H, dq + o, dk + o, dv + o))
+      return 1;
+  }
+  return 0;
+}
+
+}  // extern "C"
+
+// ------------------------------------------------- mini-transformer step ---
+namespace orc {
+
+struct TrainLayer {  // one block: RMS gammas (both null: RMS disabled) and q, k, v, o, up, gate, down
+  const int16_t* attn_gamma;
+  const int16_t* mlp_gamma;
+  LinearParams lin[7];
+};
+
+struct TrainModel {
+  size_t d, H, F, layers, S;
+  const int16_t* embeddings;  // [256][d]
+  const int16_t* positions;   // [S][d], or null for the position-free policy
+  const TrainLayer* layer;
+  LinearParams head;          // [256][d]
+};
+
+// Offsets of the i64 gradient arena: head, per layer (q k v o up gate down
+// rms_attention rms_mlp), token embeddings, position embeddings.
+struct Arena {
+  size_t head, layer0, per_layer, emb, pos, total;
+  size_t lin[7], rms_a, rms_m;  // offsets inside a layer
+  Arena(const TrainModel& m) {
+    const size_t d = m.d, F = m.F;
+    head = 0;
+    layer0 = VOCAB * d;
+    size_t o = 0;
+    for (int i = 0; i < 4; ++i) lin[i] = o, o += d * d;
+    for (int i = 4; i < 7; ++i) lin[i] = o, o += F * d;
+    rms_a = o, o += d;
+    rms_m = o, o += d;
+    per_layer = o;
+    emb = layer0 + m.layers * per_layer;
+    pos = emb + VOCAB * d;
+    total = pos + m.S * d;
+  }
+  // counts: [0] head, [1 + 9 l + i] layer l item i, [1 + 9 L] embeddings
+};
+
+struct BlockCache {
+  std::vector<int16_t> in, an, q, k, v, ctx, P, ares, mn, up, gate, gated, out;
+};
+
+static bool sat_add_rows(const int16_t* a, const int16_t* b, int16_t* out, size_t n, uint64_t* sat) {
+  return residual_add(a, b, out, n, sat);
+}
+
+// nsrl-train/src/lib.rs:15079-15300 (base-2 softmax attention kind)
+static bool block_forward_cache(const TrainModel& m, const TrainLayer& L, const int16_t* x, BlockCache& c,
+                                uint64_t* res_sat) {
+  const size_t S = m.S, d = m.d, F = m.F, H = m.H, T = S * d;
+  c.in.assign(x, x + T);
+  c.an.resize(T);
+  if (L.attn_gamma) {
+    for (size_t t = 0; t < S; ++t)
+      if (!rms_norm_row(x + t * d, L.attn_gamma, d, TRAIN_RMS_EPS, &c.an[t * d])) return false;
+  } else {
+    c.an = c.in;
+  }
+  if (!attention_shapes_valid(S, d, H, L.lin)) return false;
+  c.q.resize(T), c.k.resize(T), c.v.resize(T), c.ctx.resize(T);
+  std::vector<int16_t> aout(T), probs(S);
+  std::vector<int32_t> logits(S);
+  for (size_t t = 0; t < S; ++t) {
+    if (!linear_row(&c.an[t * d], L.lin[0], &c.q[t * d])) return false;
+    if (!linear_row(&c.an[t * d], L.lin[1], &c.k[t * d])) return false;
+    if (!linear_row(&c.an[t * d], L.lin[2], &c.v[t * d])) return false;
+  }
+  const size_t hd = d / H;
+  const int shift = sqrt_power_of_four_shift(hd);
+  for (size_t t = 0; t < S; ++t)
+    for (size_t h = 0; h < H; ++h) {
+      const size_t off = h * hd;
+      for (size_t j = 0; j <= t; ++j)
+        if (!qk_dot(&c.q[t * d + off], &c.k[j * d + off], hd, shift, &logits[j])) return false;
+      if (!base2_softmax(logits.data(), t + 1, probs.data(), nullptr)) return false;
+      for (size_t cc = 0; cc < hd; ++cc) {
+        int64_t acc = 0;
+        for (size_t j = 0; j <= t; ++j) acc += (int64_t)probs[j] * (int64_t)c.v[j * d + off + cc];
+        c.ctx[t * d + off + cc] = saturate_i16(rhu(acc, Q15_SHIFT));
+      }
+    }
+  for (size_t t = 0; t < S; ++t)
+    if (!linear_row(&c.ctx[t * d], L.lin[3], &aout[t * d])) return false;
+  c.P.resize(H * S * S);
+  if (!attention_probabilities(c.q.data(), c.k.data(), S, d, H, c.P.data())) return false;
+  c.ares.resize(T);
+  sat_add_rows(x, aout.data(), c.ares.data(), T, res_sat);
+  c.mn.resize(T);
+  if (L.mlp_gamma) {
+    for (size_t t = 0; t < S; ++t)
+      if (!rms_norm_row(&c.ares[t * d], L.mlp_gamma, d, TRAIN_RMS_EPS, &c.mn[t * d])) return false;
+  } else {
+    c.mn = c.ares;
+  }
+  c.up.resize(S * F), c.gate.resize(S * F), c.gated.resize(S * F);
+  std::vector<int16_t> mout(T);
+  for (size_t t = 0; t < S; ++t) {
+    if (!linear_row(&c.mn[t * d], L.lin[4], &c.up[t * F])) return false;
+    if (!linear_row(&c.mn[t * d], L.lin[5], &c.gate[t * F])) return false;
+    for (size_t f = 0; f < F; ++f) c.gated[t * F + f] = gated_activation(c.up[t * F + f], c.gate[t * F + f]);
+    if (!linear_row(&c.gated[t * F], L.lin[6], &mout[t * d])) return false;
+  }
+  c.out.resize(T);
+  sat_add_rows(c.ares.data(), mout.data(), c.out.data(), T, res_sat);
+  return true;
+}
+
+struct WindowStats {
+  uint64_t accepted, mlp_sat, attn_sat, res_sat;
+};
+
+// nsrl-train/src/lib.rs:15623-15775 with the attention update of
+// :15777-16075 in its accumulate form and the accumulations of :13783-14055.
+static bool block_backward_accumulate(const TrainModel& m, const TrainLayer& L, const BlockCache& c,
+                                      const int16_t* G, int64_t* acc, uint64_t* cnt, const Arena& ar,
+                                      std::vector<int16_t>& grad_in, WindowStats& ws) {
+  const size_t S = m.S, d = m.d, F = m.F, H = m.H, T = S * d;
+  const LinearParams mlp_lp[3] = {L.lin[4], L.lin[5], L.lin[6]};
+  std::vector<int16_t> gup(S * F), ggate(S * F), gmi(T), gmr(T), gao(T);
+  uint64_t sat_m = 0, sat_mr = 0, sat_res = 0, sat_a = 0, sat_ar = 0, sat_in = 0;
+  if (!gated_mlp_backward_input_rows(G, S, d, F, mlp_lp, c.up.data(), c.gate.data(), gup.data(), ggate.data(),
+                                     gmi.data(), &sat_m))
+    return false;
+  if (L.mlp_gamma) {
+    for (size_t t = 0; t < S; ++t)
+      if (!rms_norm_backward_row(&c.ares[t * d], L.mlp_gamma, &gmi[t * d], d, TRAIN_RMS_EPS, &gmr[t * d],
+                                 acc + ar.rms_m, &sat_mr))
+        return false;
+    cnt[8] += S;
+  } else {
+    gmr = gmi;
+  }
+  sat_add_rows(G, gmr.data(), gao.data(), T, &sat_res);
+  // gated-MLP weight gradients: rows whose output gradient is all zero are skipped (:13828-13831)
+  for (size_t t = 0; t < S; ++t) {
+    bool any = false;
+    for (size_t i = 0; i < d; ++i) any |= G[t * d + i] != 0;
+    if (!any) continue;
+    if (!accumulate_row(&c.gated[t * F], &G[t * d], L.lin[6], acc + ar.lin[6], &cnt[6])) return false;
+    if (!accumulate_row(&c.mn[t * d], &gup[t * F], L.lin[4], acc + ar.lin[4], &cnt[4])) return false;
+    if (!accumulate_row(&c.mn[t * d], &ggate[t * F], L.lin[5], acc + ar.lin[5], &cnt[5])) return false;
+  }
+  // attention update (accumulate form)
+  std::vector<int16_t> gctx(T), dq(T), dk(T), dv(T), gni(T), gq(d), gk(d), gv(d);
+  for (size_t t = 0; t < S; ++t)
+    if (!linear_backward_input_row(&gao[t * d], L.lin[3], nullptr, &gctx[t * d])) return false;
+  if (!attention_backward(c.q.data(), c.k.data(), c.v.data(), c.P.data(), gctx.data(), S, d, H, dq.data(),
+                          dk.data(), dv.data()))
+    return false;
+  for (size_t t = 0; t < S; ++t) {
+    if (!linear_backward_input_row(&dq[t * d], L.lin[0], nullptr, gq.data())) return false;
+    if (!linear_backward_input_row(&dk[t * d], L.lin[1], nullptr, gk.data())) return false;
+    if (!linear_backward_input_row(&dv[t * d], L.lin[2], nullptr, gv.data())) return false;
+    for (size_t i = 0; i < d; ++i) {
+      const int64_t s = rhu((int64_t)gq[i] + (int64_t)gk[i] + (int64_t)gv[i], FANIN_SHIFT);
+      if (s < -32768 || s > 32767) ++sat_a;
+      gni[t * d + i] = saturate_i16(s);
+    }
+  }
+  for (size_t t = 0; t < S; ++t) {
+    if (!accumulate_row(&c.an[t * d], &dq[t * d], L.lin[0], acc + ar.lin[0], &cnt[0])) return false;
+    if (!accumulate_row(&c.an[t * d], &dk[t * d], L.lin[1], acc + ar.lin[1], &cnt[1])) return false;
+    if (!accumulate_row(&c.an[t * d], &dv[t * d], L.lin[2], acc + ar.lin[2], &cnt[2])) return false;
+    if (!accumulate_row(&c.ctx[t * d], &gao[t * d], L.lin[3], acc + ar.lin[3], &cnt[3])) return false;
+  }
+  std::vector<int16_t> gai(T);
+  if (L.attn_gamma) {
+    for (size_t t = 0; t < S; ++t)
+      if (!rms_norm_backward_row(&c.in[t * d], L.attn_gamma, &gni[t * d], d, TRAIN_RMS_EPS, &gai[t * d],
+                                 acc + ar.rms_a, &sat_ar))
+        return false;
+    cnt[7] += S;
+  } else {
+    gai = gni;
+  }
+  grad_in.resize(T);
+  sat_add_rows(gao.data(), gai.data(), grad_in.data(), T, &sat_in);
+  ws.mlp_sat += sat_m + sat_mr;
+  ws.attn_sat += sat_a;
+  ws.res_sat += sat_res + sat_in + sat_ar;
+  return true;
+}
+
+// nsrl-train/src/lib.rs:7051-7399: forward, output head, softmax gradient and
+// the backward of every layer for one window, accumulated into `acc`/`cnt`.
+static bool train_window(const TrainModel& m, const uint8_t* ctx, uint8_t target, const int16_t* freq_w,
+                         int64_t* acc, uint64_t* cnt, WindowStats& ws) {
+  const Arena ar(m);
+  const size_t S = m.S, d = m.d, T = S * d;
+  // embeddings (:14862-14897)
+  std::vector<int16_t> x(T);
+  for (size_t t = 0; t < S; ++t)
+    for (size_t i = 0; i < d; ++i) {
+      int64_t v = m.embeddings[(size_t)ctx[t] * d + i];
+      if (m.positions) v += m.positions[t * d + i];
+      x[t * d + i] = saturate_i16(v);
+    }
+  std::vector<BlockCache> caches(m.layers);
+  uint64_t fwd_res = 0;
+  const int16_t* cur = x.data();
+  for (size_t l = 0; l < m.layers; ++l) {
+    if (!block_forward_cache(m, m.layer[l], cur, caches[l], &fwd_res)) return false;
+    cur = caches[l].out.data();
+  }
+  // output head on the last position (:17455-17488)
+  const int16_t* feat = cur + (S - 1) * d;
+  int16_t logits16[VOCAB], probs[VOCAB];
+  int32_t logits[VOCAB];
+  if (!linear_row(feat, m.head, logits16)) return false;
+  for (size_t i = 0; i < VOCAB; ++i) logits[i] = logits16[i];
+  if (!base2_softmax(logits, VOCAB, probs, nullptr)) return false;
+  // softmax gradient, frequency weight, i16 conversion (:18845-18949)
+  int16_t grad[VOCAB];
+  const int16_t fw = freq_w ? freq_w[target] : 32767;
+  for (size_t i = 0; i < VOCAB; ++i) {
+    int64_t g = (int64_t)probs[i] - (i == target ? 32767 : 0);
+    if (fw != 32767) g = (int32_t)rhu(g * (int64_t)fw, Q15_SHIFT);
+    grad[i] = saturate_i16(g);
+  }
+  std::vector<int16_t> G(T, 0);
+  if (!linear_backward_input_row(grad, m.head, nullptr, &G[(S - 1) * d])) return false;
+  if (!accumulate_row(feat, grad, m.head, acc + ar.head, &cnt[0])) return false;
+  std::vector<int16_t> gin;
+  for (size_t l = m.layers; l-- > 0;) {
+    if (!block_backward_accumulate(m, m.layer[l], caches[l], G.data(), acc + ar.layer0 + l * ar.per_layer,
+                                   cnt + 1 + 9 * l, ar, gin, ws))
+      return false;
+    G.swap(gin);
+  }
+  // embedding gradients (:14336-14405)
+  const size_t ce = 1 + 9 * m.layers;
+  for (size_t t = 0; t < S; ++t)
+    for (size_t i = 0; i < d; ++i) {
+      const int64_t g = G[t * d + i];
+      if (g == 0) continue;
+      if (__builtin_add_overflow(acc[ar.emb + (size_t)ctx[t] * d + i], g, &acc[ar.emb + (size_t)ctx[t] * d + i]))
+        return false;
+      if (m.positions && __builtin_add_overflow(acc[ar.pos + t * d + i], g, &acc[ar.pos + t * d + i])) return false;
+    }
+  cnt[ce] += 1;
+  ws.accepted += 1;
+  ws.res_sat += 2 * fwd_res;
+  return true;
+}
+
+}  // namespace orc
+
+extern "C" {
+
+size_t orc_train_arena_len(const TrainModel* m) { return Arena(*m).total; }
+
+// nsrl-train/src/lib.rs:6970-7050 + 7401-7471: windows split into `workers`
+// contiguous chunks, each run into private accumulators, merged in worker
+// order with checked adds.  stats = {accepted, mlp_sat, attention_sat, residual_sat}.
+// Returns 0, or 2 when any window (or the merge) is rejected: the whole batch is.
+int orc_train_windows(const TrainModel* m, const uint8_t* contexts, const uint8_t* targets, const int16_t* freq_w,
+                      size_t W, int64_t* acc, uint64_t* counts, uint64_t* stats, int workers) {
+  const Arena ar(*m);
+  const size_t nc = 2 + 9 * m->layers;
+  if (W == 0) return 1;
+  const size_t nw = (size_t)std::max(1, std::min<int>(workers, (int)W));
+  const size_t chunk = (W + nw - 1) / nw;
+  std::vector<std::vector<int64_t>> pacc(nw, std::vector<int64_t>(ar.total, 0));
+  std::vector<std::vector<uint64_t>> pcnt(nw, std::vector<uint64_t>(nc, 0));
+  std::vector<WindowStats> pst(nw, WindowStats{0, 0, 0, 0});
+  std::vector<int> pok(nw, 1);
+  auto run = [&](size_t w) {
+    for (size_t i = w * chunk; i < std::min(W, (w + 1) * chunk); ++i)
+      if (!train_window(*m, contexts + i * m->S, targets[i], freq_w, pacc[w].data(), pcnt[w].data(), pst[w])) {
+        pok[w] = 0;
+        return;
+      }
+  };
+  if (nw == 1) {
+    run(0);
+  } else {
+    std::vector<std::thread> pool;
+    for (size_t w = 0; w < nw; ++w) pool.emplace_back(run, w);
+    for (auto& t : pool) t.join();
+  }
+  for (size_t w = 0; w < nw; ++w)
+    if (!pok[w]) return 2;
+  for (size_t i = 0; i < ar.total; ++i) acc[i] = 0;
+  for (size_t c = 0; c < nc; ++c) counts[c] = 0;
+  for (int s = 0; s < 4; ++s) stats[s] = 0;
+  for (size_t w = 0; w < nw; ++w) {
+    for (size_t i = 0; i < ar.total; ++i)
+      if (__builtin_add_overflow(acc[i], pacc[w][i], &acc[i])) return 2;
+    for (size_t c = 0; c < nc; ++c) counts[c] += pcnt[w][c];
+    stats[0] += pst[w].accepted;
+    stats[1] += pst[w].mlp_sat;
+    stats[2] += pst[w].attn_sat;
+    stats[3] += pst[w].res_sat;
+  }
+  return 0;
+}
+
+// One block forward with its caches, for tests of the forward half:
+// out = block output, P = probabilities [H][S][S].
+int orc_train_block_forward(const TrainModel* m, size_t layer, const int16_t* x, int16_t* out, int16_t* P,
+                            uint64_t* res_sat) {
+  BlockCache c;
+  *res_sat = 0;
+  if (!block_forward_cache(*m, m->layer[layer], x, c, res_sat)) return 1;
+  memcpy(out, c.out.data(), c.out.size() * 2);
+  memcpy(P, c.P.data(), c.P.size() * 2);
+  return 0;
+}
+
+}  // extern "C"

@@ -283,3 +283,156 @@ def merge_i64(parts, counts):
     if lib().orc_merge_i64(_p(parts), C.c_size_t(W), C.c_size_t(L), _p(counts), _p(out), C.byref(c)):
         return None
     return out, c.value
+
+
+# ----------------------------------------------------------- training step --
+class _TrainLayer(C.Structure):
+    _fields_ = [("attn_gamma", C.c_void_p), ("mlp_gamma", C.c_void_p), ("lin", LinearParams * 7)]
+
+
+class _TrainModel(C.Structure):
+    _fields_ = [("d", C.c_size_t), ("H", C.c_size_t), ("F", C.c_size_t), ("layers", C.c_size_t),
+                ("S", C.c_size_t), ("embeddings", C.c_void_p), ("positions", C.c_void_p),
+                ("layer", C.c_void_p), ("head", LinearParams)]
+
+
+LAYER_LINEARS = ("q", "k", "v", "o", "up", "gate", "down")
+
+
+class TrainModel:
+    """The mini transformer of crates/nsrl-train (embeddings, stacked blocks, byte head).
+
+    layers: list of dicts with Linear entries q k v o up gate down and optional
+    int16 attn_gamma / mlp_gamma (RMS norm enabled when present)."""
+
+    def __init__(self, embeddings, positions, layers, head, d, H, F, S):
+        self.embeddings = _c(embeddings, np.int16)
+        self.positions = None if positions is None else _c(positions, np.int16)
+        self.layers = layers
+        self.head = head
+        self.d, self.H, self.F, self.S = d, H, F, S
+        for ly in layers:
+            for g in ("attn_gamma", "mlp_gamma"):
+                if ly.get(g) is not None:
+                    ly[g] = _c(ly[g], np.int16)
+
+    def struct(self):
+        arr = (_TrainLayer * len(self.layers))()
+        for i, ly in enumerate(self.layers):
+            arr[i].attn_gamma = None if ly.get("attn_gamma") is None else ly["attn_gamma"].ctypes.data
+            arr[i].mlp_gamma = None if ly.get("mlp_gamma") is None else ly["mlp_gamma"].ctypes.data
+            for j, nm in enumerate(LAYER_LINEARS):
+                arr[i].lin[j] = ly[nm].struct()
+        self._keep = arr
+        return _TrainModel(self.d, self.H, self.F, len(self.layers), self.S, self.embeddings.ctypes.data,
+                           None if self.positions is None else self.positions.ctypes.data,
+                           C.cast(arr, C.c_void_p), self.head.struct())
+
+    def arena_layout(self):
+        """Offsets of the i64 gradient arena, in the order the CUDA path uses too."""
+        d, F, L, S = self.d, self.F, len(self.layers), self.S
+        lay = {"head": (0, 256 * d)}
+        off = 256 * d
+        for li in range(L):
+            for nm, n in zip(LAYER_LINEARS + ("rms_attn", "rms_mlp"), [d * d] * 4 + [F * d] * 3 + [d, d]):
+                lay[(li, nm)] = (off, n)
+                off += n
+        lay["emb"] = (off, 256 * d)
+        off += 256 * d
+        lay["pos"] = (off, S * d)
+        off += S * d
+        lay["total"] = off
+        return lay
+
+
+def train_windows(model: TrainModel, contexts, targets, freq_w=None, workers=1):
+    """nsrl-train/src/lib.rs:6970-7471 over W windows: returns (acc i64, counts u64, stats) or None."""
+    L = lib()
+    ms = model.struct()
+    n = model.arena_layout()["total"]
+    acc = np.zeros(n, np.int64)
+    counts = np.zeros(2 + 9 * len(model.layers), np.uint64)
+    stats = np.zeros(4, np.uint64)
+    ctx = _c(contexts, np.uint8)
+    tg = _c(targets, np.uint8)
+    fw = None if freq_w is None else _c(freq_w, np.int16)
+    r = L.orc_train_windows(C.byref(ms), _p(ctx), _p(tg), _p(fw), C.c_size_t(len(tg)), _p(acc), _p(counts),
+                            _p(stats), C.c_int(workers))
+    if r != 0:
+        return None
+    return acc, counts, {"accepted": int(stats[0]), "mlp_saturation_count": int(stats[1]),
+                         "attention_saturation_count": int(stats[2]), "residual_saturation_count": int(stats[3])}
+
+
+def train_block_forward(model: TrainModel, layer, x):
+    L = lib()
+    ms = model.struct()
+    x = _c(x, np.int16)
+    out = np.zeros_like(x)
+    P = np.zeros((model.H, model.S, model.S), np.int16)
+    sat = C.c_uint64()
+    r = L.orc_train_block_forward(C.byref(ms), C.c_size_t(layer), _p(x), _p(out), _p(P), C.byref(sat))
+    return None if r else (out, P, sat.value)
+
+
+def linear_backward_input(g, lin: Linear, gin_scales=None):
+    g = _c(g, np.int16)
+    M = g.size // lin.output_dim
+    dx = np.zeros((M, lin.input_dim), np.int16)
+    s = lin.struct()
+    gs = None if gin_scales is None else np.ascontiguousarray(gin_scales, dtype=SCALE_DTYPE)
+    r = lib().orc_linear_backward_input(_p(g), C.c_size_t(M), C.byref(s), _p(gs), _p(dx))
+    return None if r else dx
+
+
+def gated_activation_backward(up, gate, g):
+    gu, gg = C.c_int16(), C.c_int16()
+    lib().orc_gated_activation_backward(C.c_int16(up), C.c_int16(gate), C.c_int16(g), C.byref(gu), C.byref(gg))
+    return gu.value, gg.value
+
+
+def gated_mlp_backward_input(grad_out, up_lin, gate_lin, down_lin, fwd_up, fwd_gate):
+    """mlp.rs:256-357 with identity grad-input scales: (grad_up, grad_gate, grad_in, saturations) or None."""
+    go = _c(grad_out, np.int16)
+    d, F = up_lin.input_dim, up_lin.output_dim
+    T = go.size // d
+    arr = (LinearParams * 3)(up_lin.struct(), gate_lin.struct(), down_lin.struct())
+    gu = np.zeros((T, F), np.int16)
+    gg = np.zeros((T, F), np.int16)
+    gi = np.zeros((T, d), np.int16)
+    sat = C.c_uint64()
+    fu, fg = _c(fwd_up, np.int16), _c(fwd_gate, np.int16)  # held until the call returns
+    r = lib().orc_gated_mlp_backward_input(_p(go), C.c_size_t(T), C.c_size_t(d), C.c_size_t(F), arr,
+                                           _p(fu), _p(fg), _p(gu), _p(gg), _p(gi), C.byref(sat))
+    return None if r else (gu, gg, gi, sat.value)
+
+
+def rms_norm_backward_rows(x, w, grad_out, eps, gw=None):
+    x = _c(x, np.int16)
+    d = len(w)
+    T = x.size // d
+    gi = np.zeros((T, d), np.int16)
+    gw = np.zeros(d, np.int64) if gw is None else gw
+    sat = C.c_uint64()
+    w16, go = _c(w, np.int16), _c(grad_out, np.int16)  # held until the call returns
+    r = lib().orc_rms_norm_backward_rows(_p(x), C.c_size_t(T), C.c_size_t(d), _p(w16), _p(go), C.c_uint64(eps),
+                                         _p(gi), _p(gw), C.byref(sat))
+    return None if r else (gi, gw, sat.value)
+
+
+def attention_probabilities(q, k, B, S, d, H):
+    P = np.zeros((B, H, S, S), np.int16)
+    q16, k16 = _c(q, np.int16), _c(k, np.int16)  # held until the call returns
+    r = lib().orc_attention_probabilities(_p(q16), _p(k16), C.c_size_t(B), C.c_size_t(S), C.c_size_t(d),
+                                          C.c_size_t(H), _p(P))
+    return None if r else P
+
+
+def attention_backward(q, k, v, P, dC, B, S, d, H):
+    dq = np.zeros((B * S, d), np.int16)
+    dk = np.zeros_like(dq)
+    dv = np.zeros_like(dq)
+    held = [_c(a, np.int16) for a in (q, k, v, P, dC)]  # held until the call returns
+    r = lib().orc_attention_backward(*[_p(a) for a in held], C.c_size_t(B), C.c_size_t(S), C.c_size_t(d),
+                                     C.c_size_t(H), _p(dq), _p(dk), _p(dv))
+    return None if r else (dq, dk, dv)
