@@ -36,9 +36,10 @@ HEAD_DIM = D_MODEL // HEADS
 TOKENS = BATCH * SEQ
 METRIC = "int attention-block tokens/s @1/2/4/8 B200, %INT8/HBM roofline, bit-exact"
 WORKLOAD = "prenorm causal attention + gated-MLP block forward, d256 h4x64 ff1024 s1024 b64/gpu"
-# dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant kernel,
-# from the ncu capture summarised in profiles/ (None until captured).
-NCU_TRAFFIC = {}
+# dram__bytes_read.sum + dram__bytes_write.sum per launch, from the ncu captures
+# summarised in profiles/ (attention: 100.8 MB read + 284.4 MB written; the gated
+# linear: 35.3 MB + 81.0 MB; decode at batch 32: 544.6 MB + 3.8 MB).
+NCU_TRAFFIC = {"attention_tc_hd64": 385181440, "linear_tc_gated": 116353024, "attention_decode": 548445696}
 
 
 def peaks():
@@ -182,7 +183,8 @@ def kernel_table(core_lib):
     return n, rows
 
 
-TENSOR_KERNELS = ("linear_tc", "attention_prefill", "attention_tc")
+TENSOR_KERNELS = ("linear_tc", "attention_prefill", "attention_tc", "accumulate_weight_grad",
+                  "attention_grad_products", "attention_dlogit", "linear_simt")
 
 # Config 5 (decode) and config 2 (linear sweep), measured after the headline.
 DEC_LAYERS, DEC_D, DEC_H, DEC_F, DEC_B, DEC_PREFIX = 4, 512, 8, 2048, 256, 8192
@@ -273,6 +275,143 @@ def run_decode(core, torch, steps, warmup, hbm, flush, batch=DEC_B):
             "kernel_share": {k: round(v["ms"] / sum(r["ms"] for r in rows.values()), 4) for k, v in rows.items()}}
 
 
+# Config 4 (training step): 4 layers, d256 h4x64 ff1024, seq 512, global batch
+# 256 windows split over the ranks (strong scaling), byte vocabulary 256.
+TR_LAYERS, TR_D, TR_H, TR_F, TR_S, TR_BATCH = 4, 256, 4, 1024, 512, 256
+LINEARS = ("q", "k", "v", "o", "up", "gate", "down")
+
+
+def make_train_model(core, torch):
+    from nsrl_b200 import synth as Y
+    from nsrl_b200 import train as TT
+    tw = Y.TrainWeights(seed=4040, layers=TR_LAYERS, d=TR_D, hidden=TR_F, seq_len=TR_S)
+    layers = []
+    for bw in tw.blocks:
+        e = {nm: core.Linear(torch.from_numpy(getattr(bw, nm)), core.make_scales(1, bw.shift[nm], bw.out_dim(nm)))
+             for nm in LINEARS}
+        e["attn_gamma"] = torch.from_numpy(bw.attn_gamma)
+        e["mlp_gamma"] = torch.from_numpy(bw.mlp_gamma)
+        layers.append(e)
+    head = core.Linear(torch.from_numpy(tw.head), core.make_scales(1, tw.head_shift, 256))
+    gm = TT.TrainModel(torch.from_numpy(tw.embeddings), torch.from_numpy(tw.positions), layers, head, TR_D, TR_H,
+                       TR_F, TR_S)
+    return tw, gm
+
+
+def train_cpu_sample(tw, ctx, tgt, threads):
+    """The oracle's map-reduce batch (forward + backward of every window, merged
+    in worker order) on `len(tgt)` windows with one worker per thread."""
+    from oracle import oracle as O
+    layers = []
+    for bw in tw.blocks:
+        e = {nm: O.Linear(getattr(bw, nm), O.scales(1, bw.shift[nm], bw.out_dim(nm))) for nm in LINEARS}
+        e["attn_gamma"], e["mlp_gamma"] = bw.attn_gamma, bw.mlp_gamma
+        layers.append(e)
+    m = O.TrainModel(tw.embeddings, tw.positions, layers, O.Linear(tw.head, O.scales(1, tw.head_shift, 256)), TR_D,
+                     TR_H, TR_F, TR_S)
+    t0 = time.perf_counter()
+    r = O.train_windows(m, ctx, tgt, workers=threads)
+    dt = time.perf_counter() - t0
+    if r is None:
+        raise RuntimeError("oracle rejected the CPU sample")
+    return len(tgt) * TR_S / dt, dt
+
+
+def run_train(core, torch, dist, world, rank, steps, warmup, flush, hbm, tfl, src, cpu_baseline):
+    """Config 4: the data-parallel training step (windows forward + backward,
+    exact int64 all-reduce, requantising apply) over TR_BATCH windows per step."""
+    from nsrl_b200 import synth as Y
+    from nsrl_b200 import train as TT
+    L = core.lib()
+    if TR_BATCH % world:
+        raise ValueError("the global batch must split evenly over the ranks")
+    W = TR_BATCH // world
+    tw, gm = make_train_model(core, torch)
+    state = TT.TrainState(gm)
+    buf = TT.TrainStepBuffers(gm, W)
+    cfg = TT.MiniTransformerTrainConfig()
+    nsteps = warmup + steps
+    ctx_all, tgt_all = Y.train_windows(0x7EA1, nsteps * TR_BATCH, TR_S)
+    lo, hi = rank * W, (rank + 1) * W
+    # device-resident windows of every step (the `value` leg)
+    dctx = [torch.from_numpy(ctx_all[i * TR_BATCH + lo:i * TR_BATCH + hi]).cuda() for i in range(nsteps)]
+    dtgt = [torch.from_numpy(tgt_all[i * TR_BATCH + lo:i * TR_BATCH + hi]).cuda() for i in range(nsteps)]
+    stream = torch.cuda.current_stream()
+    last = None
+    for i in range(warmup):
+        last = TT.mini_transformer_train_step(gm, state, dctx[i], dtgt[i], cfg, buf)
+        if last is None:
+            raise RuntimeError("training batch rejected in warm-up")
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    L.nsrl_profile_reset()
+    L.nsrl_profile_enable(1)
+    ev = []
+    for i in range(warmup, nsteps):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        last = TT.mini_transformer_train_step(gm, state, dctx[i], dtgt[i], cfg, buf)
+        b.record(stream)
+        ev.append((a, b))
+        if last is None:
+            raise RuntimeError("training batch rejected in the timed region")
+    torch.cuda.synchronize()
+    L.nsrl_profile_enable(0)
+    ms = sum(a.elapsed_time(b) for a, b in ev)
+    t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    n_launches, rows = kernel_table(L)
+    # end to end: this step's windows copied from pinned host memory, the stats read back
+    hctx = torch.from_numpy(ctx_all[lo:hi]).pin_memory()
+    htgt = torch.from_numpy(tgt_all[lo:hi]).pin_memory()
+    e2e_ms = 0.0
+    for i in range(max(1, min(steps, 3))):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        dc = hctx.cuda(non_blocking=True)
+        dt_ = htgt.cuda(non_blocking=True)
+        r = TT.mini_transformer_train_step(gm, state, dc, dt_, cfg, buf)
+        b.record(stream)
+        torch.cuda.synchronize()
+        if r is None:
+            raise RuntimeError("training batch rejected in the end-to-end loop")
+        e2e_ms += a.elapsed_time(b)
+    e2e_steps = max(1, min(steps, 3))
+    t = torch.tensor([e2e_ms], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t.item())
+    if rank != 0:
+        return None
+    tokens = TR_BATCH * TR_S
+    total = sum(r["ms"] for r in rows.values())
+    out = {"workload": f"data-parallel training step, {TR_LAYERS} layers d{TR_D} h{TR_H}x{TR_D // TR_H} ff{TR_F} "
+                       f"seq {TR_S}, global batch {TR_BATCH} windows over {world} GPU(s), byte vocabulary 256",
+           "metric": "training tokens/s (windows x seq_len per step, whole job)",
+           "value": tokens * steps / (ms / 1000.0), "unit": "tokens/s", "steps": steps, "warmup": warmup,
+           "ms_per_step": ms / steps, "scaling": "strong", "n_gpus": world,
+           "e2e": {"value": tokens * e2e_steps / (e2e_ms / 1000.0), "unit": "tokens/s",
+                   "h2d_bytes_per_step": int(W * (TR_S + 1)), "d2h_bytes_per_step": 3 * 8 + 8 * 4 + 8 * 8},
+           "gpu_launches_per_step": n_launches / steps,
+           "last_step": last,
+           "roofline": roofline(rows, hbm, tfl, src),
+           "kernels": {k: {"launches": v["launches"], "ms": round(v["ms"], 3), "share": round(v["ms"] / total, 4)}
+                       for k, v in sorted(rows.items(), key=lambda kv: -kv[1]["ms"])[:12]}}
+    if cpu_baseline and world == 1:
+        threads = os.cpu_count() or 1
+        n = max(1, min(threads, 16))
+        rate, dt = train_cpu_sample(tw, ctx_all[:n], tgt_all[:n], threads)
+        out["cpu_baseline"] = {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port",
+                               "sample": f"{n} windows x {TR_S} tokens, forward + backward + merge "
+                                         f"({dt:.1f} s, one worker per thread; the apply is not timed)"}
+    return out
+
+
 def run_sweep(core, torch, hbm, tflops, flush, reps=5):
     """Config 2: the i16 x i8 linear over M x K (K = N) through nsrl_linear_i16_i8_i16."""
     from nsrl_b200 import synth as Y
@@ -358,6 +497,9 @@ def run_secondary(args):
     if args.case == "decode":
         out = run_decode(core, torch, steps=args.steps, warmup=args.warmup, hbm=hbm, flush=flush,
                          batch=args.decode_batch)
+    elif args.case == "train":
+        out = run_train(core, torch, None, 1, 0, steps=args.steps, warmup=args.warmup, flush=flush, hbm=hbm, tfl=tfl,
+                        src=peaks()[2], cpu_baseline=not args.no_cpu_baseline)
     else:
         out = run_sweep(core, torch, hbm, tfl, flush)
     print(json.dumps(out), flush=True)
@@ -372,9 +514,10 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip the decode and linear-sweep measurements")
-    ap.add_argument("--case", default="block", choices=["block", "decode", "sweep"],
-                    help="decode / sweep: run only that secondary measurement (a small case for profiling)")
+    ap.add_argument("--case", default="block", choices=["block", "decode", "sweep", "train"],
+                    help="decode / sweep / train: run only that secondary measurement on one GPU")
     ap.add_argument("--decode-batch", type=int, default=DEC_B)
+    ap.add_argument("--train-steps", type=int, default=3, help="timed steps of the training-step measurement")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -481,6 +624,12 @@ def main():
         dist.barrier()
     e2e_ms = float(t.item())
 
+    # config 4 on every rank (its exchange is a collective)
+    train_out = None
+    if not args.no_extras:
+        hbm, tfl, src = peaks()
+        train_out = run_train(core, torch, dist, world, rank, steps=args.train_steps, warmup=2, flush=flush, hbm=hbm,
+                              tfl=tfl, src=src, cpu_baseline=not args.no_cpu_baseline)
     if rank == 0:
         hbm, tfl, src = peaks()
         value = world * TOKENS * args.steps / (elapsed_ms / 1000.0)
@@ -505,6 +654,8 @@ def main():
         if not args.no_extras and world == 1:
             out["decode"] = run_decode(core, torch, steps=8, warmup=2, hbm=hbm, flush=flush)
             out["linear_sweep"] = run_sweep(core, torch, hbm, tfl, flush)
+        if train_out is not None:
+            out["train"] = train_out
         if world == 1 and not args.no_cpu_baseline:
             from oracle import oracle as O
             O.use_native()

@@ -220,6 +220,111 @@ nsrl_status nsrl_apply_linear_weight_gradient_i64_to_i8(long long* accumulators,
                                                         int carry_residual, unsigned long long* stats,
                                                         nsrl_device_status* status, void* stream);
 
+/* i16 embedding apply (nsrl-train/src/lib.rs:14407-14510): per entry with a
+ * nonzero sum or residual, product = round_div(acc, count) * lr + residual,
+ * u = rhu(product, shift), residual' = product - (u << shift), e = sat_i16(e - u).
+ * stats (3 device uint64, added to): {saturations, zero deltas, sum |delta|}.
+ * The accumulators and the count are not cleared (the caller clears the
+ * token and position parts together, :14454). */
+nsrl_status nsrl_apply_embedding_gradient_i64_to_i16(const long long* accumulators, long long* residuals,
+                                                     int16_t* embeddings, size_t len,
+                                                     const unsigned long long* sample_count, int32_t learning_rate,
+                                                     uint8_t learning_rate_shift, unsigned long long* stats,
+                                                     nsrl_device_status* status, void* stream);
+
+/* ---------------------------------------------------- training backward --
+ * Backward-input linear over rows: dx[m][k] = requantize_i64_to_i16(
+ * sum_n g'[m][n] * W[n][k], grad_input_scales[k]) with g' = rhu(g * mult_n,
+ * shift_n) from the forward scales of `params` (a g' outside i32 rejects).
+ * grad_input_scales: [input_dim] or NULL (identity, as the mini transformer
+ * passes them).  Replaces linear_backward_input_i16_i8_i16_per_channel_checked
+ * (crates/nsrl-core/src/linear.rs:548-640).  g [rows][output_dim], dx
+ * [rows][input_dim] int16. */
+size_t nsrl_linear_backward_input_workspace_size(size_t rows, size_t input_dim, size_t output_dim);
+nsrl_status nsrl_linear_backward_input(const int16_t* grad_output, size_t rows, const nsrl_linear_params* params,
+                                       const nsrl_fixed_scale* grad_input_scales, int16_t* grad_input,
+                                       void* workspace, size_t workspace_bytes, nsrl_device_status* status,
+                                       void* stream);
+
+/* Gated-MLP backward input with identity grad-input scales (mlp.rs:256-357
+ * as the mini transformer calls it, nsrl-train/src/lib.rs:15670-15696):
+ * grad_up / grad_gate [rows][hidden] (mlp.rs:172-194), grad_input
+ * [rows][d_model] = sat(up^T + gate^T); *saturations (device uint64) +=
+ * the saturations of that sum. */
+size_t nsrl_gated_mlp_backward_input_workspace_size(size_t rows, size_t d_model, size_t hidden_dim);
+nsrl_status nsrl_gated_mlp_backward_input(const int16_t* grad_output, size_t rows, size_t d_model, size_t hidden_dim,
+                                          const nsrl_linear_params* up, const nsrl_linear_params* gate,
+                                          const nsrl_linear_params* down, const int16_t* forward_up,
+                                          const int16_t* forward_gate, int16_t* grad_up, int16_t* grad_gate,
+                                          int16_t* grad_input, unsigned long long* saturations, void* workspace,
+                                          size_t workspace_bytes, nsrl_device_status* status, void* stream);
+
+/* RMS-norm backward rows (crates/nsrl-core/src/rms_norm.rs:96-170, rows as in
+ * nsrl-train/src/lib.rs:15030-15077): grad_input [rows][d] int16; gamma
+ * gradients added into gamma_grad [d] int64; *saturations (device uint64)
+ * += saturated grad_input values. */
+nsrl_status nsrl_rms_norm_backward_rows(const int16_t* x, size_t rows, size_t d, const int16_t* gamma,
+                                        const int16_t* grad_output, uint64_t eps, int16_t* grad_input,
+                                        long long* gamma_grad, unsigned long long* saturations,
+                                        nsrl_device_status* status, void* stream);
+
+/* Causal attention with its probabilities: q, k, v rows of stride ld
+ * (sequence b at row b * seq_len, head h at column h * head_dim) -> context
+ * [batch*seq_len][d] and P [batch][heads][seq_len][seq_len] int16 (zero above
+ * the diagonal).  The forward half of nsrl-train/src/lib.rs:15161-15180 and
+ * :15353-15418. */
+nsrl_status nsrl_attention_with_probabilities(const int16_t* q, const int16_t* k, const int16_t* v, size_t ld,
+                                              size_t batch, size_t seq_len, size_t d_model, size_t heads,
+                                              int16_t* context, int16_t* probabilities, nsrl_device_status* status,
+                                              void* stream);
+
+/* Softmax-attention backward (nsrl-train/src/lib.rs:16623-16900): from q, k, v
+ * (stride ld), P and the context gradient dC [batch*seq_len][d] -> dq, dk, dv
+ * [batch*seq_len][d].  Workspace: nsrl_attention_backward_workspace_size. */
+size_t nsrl_attention_backward_workspace_size(size_t batch, size_t seq_len, size_t heads);
+nsrl_status nsrl_attention_backward(const int16_t* q, const int16_t* k, const int16_t* v, size_t ld,
+                                    const int16_t* probabilities, const int16_t* grad_context, size_t batch,
+                                    size_t seq_len, size_t d_model, size_t heads, int16_t* dq, int16_t* dk, int16_t* dv,
+                                    void* workspace, size_t workspace_bytes, nsrl_device_status* status, void* stream);
+
+/* ------------------------------------------------- training window step --
+ * The map-reduce worker of the reference's mini transformer
+ * (nsrl-train/src/lib.rs:7051-7399) for `windows` windows of seq_len bytes on
+ * one GPU: embeddings (+ learned positions), the stacked blocks forward with
+ * their caches, the byte head on the last position, the softmax gradient,
+ * and the backward of every block into i64 gradient accumulators.  The
+ * model structs live in host memory; every array they point to is device
+ * memory.  Forward multipliers must be 1 (the reference's scale tables). */
+typedef struct nsrl_train_layer {
+  const int16_t* attn_gamma; /* [d] or NULL: RMS norm disabled (both or neither) */
+  const int16_t* mlp_gamma;  /* [d] or NULL */
+  nsrl_linear_params lin[7]; /* q, k, v, o [d][d]; up, gate [hidden][d]; down [d][hidden] */
+} nsrl_train_layer;
+
+typedef struct nsrl_train_model {
+  size_t d_model, heads, hidden_dim, layers, seq_len;
+  const int16_t* embeddings; /* [256][d] */
+  const int16_t* positions;  /* [seq_len][d], or NULL for the position-free policy */
+  const nsrl_train_layer* layer; /* host array of `layers` blocks */
+  nsrl_linear_params head;   /* [256][d] byte head */
+} nsrl_train_model;
+
+/* Length (int64 elements) of the gradient arena: head [256][d]; per layer
+ * q, k, v, o, up, gate, down, rms_attention [d], rms_mlp [d]; token
+ * embeddings [256][d]; positions [seq_len][d].  counts: 2 + 9 * layers
+ * uint64 (head, 9 per layer in the same order, embeddings). */
+size_t nsrl_train_arena_len(const nsrl_train_model* model);
+size_t nsrl_train_workspace_size(const nsrl_train_model* model, size_t windows);
+/* contexts [windows][seq_len] uint8, targets [windows] uint8, freq_weights
+ * [256] int16 or NULL (all 32767).  Adds into arena / counts; stats (4
+ * device uint64) += {accepted windows, mlp saturations, attention
+ * saturations, residual saturations}.  A rejection anywhere rejects the
+ * whole batch (nsrl-train/src/lib.rs:5371-5375). */
+nsrl_status nsrl_train_windows(const nsrl_train_model* model, const uint8_t* contexts, const uint8_t* targets,
+                               const int16_t* freq_weights, size_t windows, long long* arena,
+                               unsigned long long* counts, unsigned long long* stats, void* workspace,
+                               size_t workspace_bytes, nsrl_device_status* status, void* stream);
+
 /* ------------------------------------------------------------ profiling --
  * Per-launch CUDA-event timing of the library's own kernels (no counterpart
  * in the reference, whose only timer is a wall clock around the block loop,

@@ -52,7 +52,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
     if failed:
         raise RuntimeError("nvcc failed")
     tmp = OUT + ".tmp"
-    subprocess.check_call([NVCC, "-shared", "-o", tmp] + objs + ["-Xcompiler", "-fPIC"])
+    subprocess.check_call([NVCC] + FLAGS[:2] + ["-shared", "-o", tmp] + objs + ["-Xcompiler", "-fPIC"])
     os.replace(tmp, OUT)
     return OUT
 

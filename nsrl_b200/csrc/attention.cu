@@ -329,6 +329,7 @@ struct RowArgs {
   int hd, shift;
   int16_t* out;
   long long ldo;
+  int16_t* probs;  // optional: causal prefill rows of P [B][H][S][S] (zero above the diagonal)
   nsrl_device_status* st;
 };
 
@@ -454,6 +455,10 @@ __global__ void __launch_bounds__(256) attention_rows_kernel(const RowArgs a) {
   const long long inv = (long long)recip_sum_q31(sum);
   for (int j = tid; j < L; j += 256) logits[j] = (int32_t)sat_i16(rhu64((long long)logits[j] * inv, 16));
   __syncthreads();
+  if (a.probs) {  // nsrl-train/src/lib.rs:15353-15418: the row of P, zeros past the causal limit
+    int16_t* pr = a.probs + ((b * gridDim.y + h) * (long long)a.rows_per_seq + tq) * a.rows_per_seq;
+    for (int j = tid; j < a.rows_per_seq; j += 256) pr[j] = j < L ? (int16_t)logits[j] : (int16_t)0;
+  }
 
   // ---- phase 3: context = sat(rhu(sum_j p_j v[j], 15)) ----
   if (LPK > 0) {
@@ -562,6 +567,31 @@ cudaError_t launch_attention(const Planes& qkv, size_t B, size_t S, size_t d, si
     return cudaGetLastError();
   }
   return cudaErrorNotSupported;  // caller falls back to the row kernel on int16 operands
+}
+
+// Causal attention over int16 q, k, v rows of stride ld (sequence b at row
+// b * S) -> ctx int16 [B*S][d] and the probabilities P [B][H][S][S].
+cudaError_t launch_attention_rows_probs(const int16_t* q, const int16_t* k, const int16_t* v, size_t ld, size_t B,
+                                        size_t S, size_t d, size_t H, int16_t* ctx, int16_t* probs,
+                                        nsrl_device_status* st, cudaStream_t stream) {
+  RowArgs a{};
+  a.q = q;
+  a.ldq = (long long)ld;
+  a.k = k;
+  a.v = v;
+  a.ldkv = (long long)ld;
+  a.kv_seq = (long long)(S * ld);
+  a.rows_per_seq = (int)S;
+  a.mode = 1;
+  a.lens = nullptr;
+  a.Lmax = (int)S;
+  a.hd = (int)(d / H);
+  a.shift = __builtin_ctz((unsigned)a.hd) / 2;
+  a.out = ctx;
+  a.ldo = (long long)d;
+  a.probs = probs;
+  a.st = st;
+  return launch_rows(a, (long long)(B * S), (int)H, stream);
 }
 
 // Fallback core over int16 q|k|v [B*S][3d] -> ctx int16 [B*S][d].

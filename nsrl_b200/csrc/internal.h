@@ -61,6 +61,9 @@ struct GemmArgs {
   unsigned long long* sat_counter;
   VtPlanes vt;
   nsrl_device_status* st;
+  // Backward-input form (linear.rs:594-640): the sum is an i64 (no prefix
+  // rule) requantised by requantize_i64_to_i16; A holds the prescaled grads.
+  bool wide = false;
 };
 
 // Launches the linear on `stream` (tcgen05 path when the shape allows TMA,
@@ -108,6 +111,12 @@ cudaError_t launch_decode_attention(const int16_t* q, const int16_t* kc, const i
 cudaError_t launch_kv_append(const Planes& qkv, size_t B, size_t d, size_t hd, const int32_t* pos, size_t Lmax,
                              int16_t* q16, int16_t* k_cache, int16_t* v_cache, nsrl_device_status* st,
                              cudaStream_t stream);
+
+// Causal attention on int16 q, k, v rows (row stride ld; sequence b starts at
+// row b * S) -> ctx int16 [B*S][d] and probabilities P [B][H][S][S] int16.
+cudaError_t launch_attention_rows_probs(const int16_t* q, const int16_t* k, const int16_t* v, size_t ld, size_t B,
+                                        size_t S, size_t d, size_t H, int16_t* ctx, int16_t* probs,
+                                        nsrl_device_status* st, cudaStream_t stream);
 
 // Planes -> int16.
 cudaError_t launch_join_planes(Planes in, size_t rows, size_t cols, int16_t* y, size_t ldy, cudaStream_t stream);

@@ -68,6 +68,7 @@ struct TcParams {
   uint8_t* vtl;
   int vt_S, vt_H, vt_hd, vt_col0;  // QKV_VT: output columns >= vt_col0 go to the transposed planes
   bool small_acc;                   // K * 127 * 32767 < 2^30: every accumulator is below 2^30
+  bool wide;                        // i64 accumulator, requantize_i64_to_i16 (backward-input linears)
   nsrl_device_status* st;
 };
 
@@ -148,6 +149,29 @@ __device__ __forceinline__ void requant_cols(const uint32_t (&h)[W], const uint3
     }
   }
 }
+// linear.rs:744-751 (requantize_i64_to_i16) of an i64 accumulator held as
+// two exact s32 plane sums: acc = 256 * hi + lo.  A multiplier that takes the
+// product out of i64 is the reference's `None` (flagged).
+__device__ __forceinline__ int requant_wide1(uint32_t h, uint32_t l, int mult, int shift, bool& bad) {
+  const long long acc = (long long)(int)h * 256ll + (long long)(int)l;
+  long long wide = acc;
+  if (mult != 1) {
+    const long long lo = (long long)((unsigned long long)acc * (unsigned long long)(long long)mult);
+    if (__mul64hi(acc, (long long)mult) != (lo >> 63)) bad = true;
+    wide = lo;
+  }
+  return (int)sat_i16(rhu64(wide, (uint32_t)shift));
+}
+__device__ __forceinline__ void requant_wide32(const uint32_t (&h)[32], const uint32_t (&l)[32], const ColScale& c,
+                                               int (&v)[32], bool& bad) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const int mult = c.uniform ? 1 : __shfl_sync(0xffffffffu, c.mult, i);
+    const int shift = c.uniform ? c.ushift : __shfl_sync(0xffffffffu, c.shift, i);
+    v[i] = requant_wide1(h[i], l[i], mult, shift, bad);
+  }
+}
+
 __device__ __forceinline__ void requant32(const uint32_t (&h)[32], const uint32_t (&l)[32], const ColScale& c,
                                           int (&v)[32], bool small) {
   requant_cols<32>(h, l, c, v, small);
@@ -428,7 +452,13 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
         tc_fence_before();
         if (lane == 0) mbar_arrive(&acc_empty[buf]);
         int v[32];
-        requant32(h, l, sc, v, p.small_acc);
+        if (p.wide) {
+          bool bad = false;
+          requant_wide32(h, l, sc, v, bad);
+          if (bad && row_ok && nvalid > 0) nsrl_flag(p.st, NSRL_FLAG_LINEAR_OVERFLOW);
+        } else {
+          requant32(h, l, sc, v, p.small_acc);
+        }
         uint32_t o[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) o[i] = pack2(v[2 * i], v[2 * i + 1]);
@@ -533,7 +563,14 @@ __global__ void gemm_simt_kernel(const SimtParams s) {
     const int nl = s.nseg == 3 ? n % s.seg_rows : n;
     int h, l;
     simt_dot(s, m, sg, nl, h, l);
-    v = finish1(h, l, p.bias[sg], p.scales[sg], nl);
+    if (p.wide) {
+      bool bad = false;
+      const nsrl_fixed_scale sc = p.scales[sg][nl];
+      v = (int16_t)requant_wide1((uint32_t)h, (uint32_t)l, sc.multiplier, sc.right_shift, bad);
+      if (bad) nsrl_flag(p.st, NSRL_FLAG_LINEAR_OVERFLOW);
+    } else {
+      v = finish1(h, l, p.bias[sg], p.scales[sg], nl);
+    }
   }
   if (s.epi == (int)Epi::I16) {
     p.y[(long long)m * p.ldy + n] = v;
@@ -782,7 +819,10 @@ cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t stream) {
   p.vt_hd = a.vt.hd;
   p.vt_col0 = a.epi == Epi::QKV_VT ? 2 * (int)a.seg[0].rows : INT_MAX;
   p.small_acc = (unsigned long long)a.K * 127ull * 32767ull < (1ull << 30);
+  p.wide = a.wide;
   p.st = a.st;
+  // The wide form keeps each plane's s32 sum exact: K * 255 * 127 < 2^31.
+  if (a.wide && (a.K > 66000 || gated || a.epi == Epi::QKV_VT || a.nseg != 1)) return cudaErrorInvalidValue;
 
   bool tc = tma_supported() && (a.K % 16) == 0 && (a.lda % 16) == 0 && aligned16(a.a_hi) && aligned16(a.a_lo);
   for (int i = 0; i < a.nseg; ++i) tc = tc && aligned16(a.seg[i].w);
@@ -838,7 +878,7 @@ cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t stream) {
   // (linear.rs:144-173); then rows outside the L1 bound are rescanned.
   bool any_bias = false;
   for (int i = 0; i < a.nseg; ++i) any_bias = any_bias || a.seg[i].bias != nullptr;
-  if (any_bias || (unsigned long long)a.K * 127ull * 32767ull > 2147483647ull) {
+  if (!a.wide && (any_bias || (unsigned long long)a.K * 127ull * 32767ull > 2147483647ull)) {
     if (!a.a_l1) return cudaErrorInvalidValue;
     CheckParams c{};
     c.a_hi = a.a_hi;

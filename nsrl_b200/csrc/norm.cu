@@ -13,25 +13,6 @@
 namespace nsrl {
 namespace {
 
-// rms_norm.rs:47-66 for value > 0.  The normalised exponent + 7 equals the
-// index of the most significant bit, so the shift is always to the right.
-__device__ __forceinline__ long long rsqrt_q30(unsigned long long v) {
-  const int msb = 63 - __clzll((long long)v);
-  const uint32_t mant = msb >= 7 ? (uint32_t)(v >> (msb - 7)) : (uint32_t)(v << (7 - msb));
-  long long inv = (long long)d_rsqrt_lut[(mant & 255u) - 128] << 15;
-  if (msb & 1) inv = rhu64(inv * 23170ll, 15);
-  const int half = msb / 2;
-  return half >= 63 ? 0 : (inv >> half);
-}
-
-// floor(ss / d) from a double reciprocal, corrected to the exact quotient
-// (ss < 2^53, so the double product is within one of it).
-__device__ __forceinline__ unsigned long long div_exact(unsigned long long ss, unsigned d, double rd) {
-  unsigned long long q = (unsigned long long)((double)ss * rd);
-  if (q * d > ss) --q;
-  if ((q + 1) * d <= ss) ++q;
-  return q;
-}
 
 // sat_i16(rhu(x * g * inv, 30)): |x * g| <= 2^30 and 0 <= inv < 2^30, so the
 // product fits i64 with no saturation and rhu is (v + 2^29) >> 30.

@@ -239,6 +239,60 @@ __global__ void apply_kernel(long long* __restrict__ acc, long long* __restrict_
   }
 }
 
+// nsrl-train/src/lib.rs:14457-14510 (apply_embedding_accumulators_i64_to_i16):
+// unlike the i8 apply, an entry is skipped only when both its sum and its
+// residual are zero, the residual is always carried (also on saturation),
+// and the accumulators are left for the caller to clear.
+__global__ void apply_embedding_kernel(const long long* __restrict__ acc, long long* __restrict__ res,
+                                       int16_t* __restrict__ w, long long len, const unsigned long long* count_p,
+                                       int lr, int shift, unsigned long long* stats, nsrl_device_status* st) {
+  const unsigned long long count = *count_p;
+  if (count == 0) return;
+  if (count > (unsigned long long)LLONG_MAX) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) nsrl_flag(st, NSRL_FLAG_LINEAR_OVERFLOW);
+    return;
+  }
+  const long long den = (long long)count;
+  unsigned long long sat = 0, zero = 0, l1 = 0;
+  bool bad = false;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < len; i += (long long)gridDim.x * blockDim.x) {
+    const long long raw = acc[i], r0 = res[i];
+    if (raw == 0 && r0 == 0) continue;
+    long long avg, product;
+    if (!round_div(raw, den, avg) || mul_ovf(avg, (long long)lr, product) || add_ovf(product, r0, product)) {
+      bad = true;
+      continue;
+    }
+    const long long scaled = rhu64(product, (uint32_t)shift);
+    // product - (scaled << shift), exact as in the i8 apply
+    res[i] = shift ? (long long)((unsigned long long)product - ((unsigned long long)scaled << shift)) : 0;
+    const long long delta = -scaled;
+    if (delta == 0) ++zero;
+    const int prev = w[i];
+    long long unclamped;
+    if (add_ovf((long long)prev, delta, unclamped)) {
+      bad = true;
+      continue;
+    }
+    const int clamped = (int)sat_i16(unclamped);
+    if ((long long)clamped != unclamped) ++sat;
+    l1 += (unsigned long long)abs(clamped - prev);
+    w[i] = (int16_t)clamped;
+  }
+  if (bad) nsrl_flag(st, NSRL_FLAG_LINEAR_OVERFLOW);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    sat += __shfl_xor_sync(0xffffffffu, sat, o);
+    zero += __shfl_xor_sync(0xffffffffu, zero, o);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    if (sat) atomicAdd(&stats[0], sat);
+    if (zero) atomicAdd(&stats[1], zero);
+    if (l1) atomicAdd(&stats[2], l1);
+  }
+}
+
 }  // namespace
 }  // namespace nsrl
 
@@ -326,6 +380,30 @@ nsrl_status nsrl_apply_linear_weight_gradient_i64_to_i8(long long* accumulators,
   if (e == cudaSuccess) e = cudaMemsetAsync(sample_count, 0, sizeof(unsigned long long), s);
   if (e != cudaSuccess) {
     set_error("apply: %s", cudaGetErrorString(e));
+    return NSRL_CUDA_ERROR;
+  }
+  return NSRL_OK;
+}
+
+nsrl_status nsrl_apply_embedding_gradient_i64_to_i16(const long long* accumulators, long long* residuals,
+                                                     int16_t* embeddings, size_t len,
+                                                     const unsigned long long* sample_count, int32_t learning_rate,
+                                                     uint8_t learning_rate_shift, unsigned long long* stats,
+                                                     nsrl_device_status* status, void* stream) {
+  // nsrl-train/src/lib.rs:14416-14421: InvalidConfig
+  if (len == 0 || learning_rate <= 0 || learning_rate_shift > 62 || !accumulators || !residuals || !embeddings ||
+      !sample_count || !stats || !status) {
+    set_error("invalid shape: embedding apply");
+    return NSRL_INVALID_SHAPE;
+  }
+  cudaStream_t s = (cudaStream_t)stream;
+  const unsigned blocks = (unsigned)std::min<size_t>((len + 255) / 256, 148 * 8);
+  ProfScope prof("apply_i64_to_i16", s, 0.0, 26.0 * (double)len);
+  apply_embedding_kernel<<<blocks, 256, 0, s>>>(accumulators, residuals, embeddings, (long long)len, sample_count,
+                                                learning_rate, learning_rate_shift, stats, status);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("embedding apply: %s", cudaGetErrorString(e));
     return NSRL_CUDA_ERROR;
   }
   return NSRL_OK;

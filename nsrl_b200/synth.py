@@ -122,3 +122,25 @@ def fnv1a_i16(values: np.ndarray) -> int:
     for b in data:
         h = ((h ^ b) * 0x100000001B3) & 0xFFFFFFFFFFFFFFFF
     return h
+
+
+# ------------------------------------------------------ training workload ---
+class TrainWeights:
+    """Synthetic mini-transformer weights for the training step: seeded
+    BlockWeights per layer, Q15 Gaussian token embeddings (sigma 4096),
+    Gaussian learned positions (sigma 1024) and a uniform i8 byte head
+    (output scale shift 8, the reference's fixed output scale)."""
+
+    def __init__(self, seed: int, layers: int, d: int, hidden: int, seq_len: int):
+        self.blocks = [BlockWeights(seed + 17 * (li + 1), d, hidden) for li in range(layers)]
+        self.embeddings = q15_gaussian(tensor_seed(seed, 101), (256, d))
+        self.positions = q15_gaussian(tensor_seed(seed, 102), (seq_len, d), sigma_shift=14)
+        self.head = i8_uniform(tensor_seed(seed, 103), (256, d))
+        self.head_shift = 8
+
+
+def train_windows(seed: int, windows: int, seq_len: int):
+    """Byte windows [windows][seq_len] and their targets, uniform over 0..255 (SplitMix64)."""
+    draws = splitmix(seed, windows * (seq_len + 1)) >> np.uint64(56)
+    a = draws.astype(np.uint8).reshape(windows, seq_len + 1)
+    return np.ascontiguousarray(a[:, :seq_len]), np.ascontiguousarray(a[:, seq_len])

@@ -148,3 +148,444 @@ def allreduce_weight_gradients_i64(gradients: Sequence[LinearWeightGradientI64],
         g.sample_count.copy_(counts[i:i + 1])
         off += n
     return ok
+
+
+# ------------------------------------------------------- training backward --
+class _TrainLayerC(C.Structure):
+    _fields_ = [("attn_gamma", C.c_void_p), ("mlp_gamma", C.c_void_p), ("lin", core.LinearParamsC * 7)]
+
+
+class _TrainModelC(C.Structure):
+    _fields_ = [("d_model", C.c_size_t), ("heads", C.c_size_t), ("hidden_dim", C.c_size_t), ("layers", C.c_size_t),
+                ("seq_len", C.c_size_t), ("embeddings", C.c_void_p), ("positions", C.c_void_p),
+                ("layer", C.c_void_p), ("head", core.LinearParamsC)]
+
+
+LAYER_LINEARS = ("q", "k", "v", "o", "up", "gate", "down")
+
+
+def _lib_bwd():
+    L = _lib()
+    if not getattr(L, "_bwd_bound", False):
+        vp, sz = C.c_void_p, C.c_size_t
+        lp = C.POINTER(core.LinearParamsC)
+        L.nsrl_linear_backward_input_workspace_size.restype = sz
+        L.nsrl_linear_backward_input_workspace_size.argtypes = [sz, sz, sz]
+        L.nsrl_linear_backward_input.argtypes = [vp, sz, lp, vp, vp, vp, sz, vp, vp]
+        L.nsrl_gated_mlp_backward_input_workspace_size.restype = sz
+        L.nsrl_gated_mlp_backward_input_workspace_size.argtypes = [sz, sz, sz]
+        L.nsrl_gated_mlp_backward_input.argtypes = [vp, sz, sz, sz, lp, lp, lp, vp, vp, vp, vp, vp, vp, vp, sz, vp, vp]
+        L.nsrl_rms_norm_backward_rows.argtypes = [vp, sz, sz, vp, vp, C.c_uint64, vp, vp, vp, vp, vp]
+        L.nsrl_attention_with_probabilities.argtypes = [vp, vp, vp, sz, sz, sz, sz, sz, vp, vp, vp, vp]
+        L.nsrl_attention_backward_workspace_size.restype = sz
+        L.nsrl_attention_backward_workspace_size.argtypes = [sz, sz, sz]
+        L.nsrl_attention_backward.argtypes = [vp, vp, vp, sz, vp, vp, sz, sz, sz, sz, vp, vp, vp, vp, sz, vp, vp]
+        L.nsrl_train_arena_len.restype = sz
+        L.nsrl_train_arena_len.argtypes = [vp]
+        L.nsrl_train_workspace_size.restype = sz
+        L.nsrl_train_workspace_size.argtypes = [vp, sz]
+        L.nsrl_train_windows.argtypes = [vp, vp, vp, vp, sz, vp, vp, vp, vp, sz, vp, vp]
+        L._bwd_bound = True
+    return L
+
+
+def _run_status(r, st):
+    if r == core.NSRL_INVALID_SHAPE:
+        raise ValueError(_lib().nsrl_last_error().decode())
+    core._check(r)
+    code, _ = st.fetch()
+    return code == core.NSRL_OK
+
+
+def linear_backward_input_i16_i8_i16_per_channel_checked(grad_output: torch.Tensor, lin: "core.Linear",
+                                                        grad_input_scales: Optional[torch.Tensor] = None):
+    """linear.rs:548-640 over the rows of grad_output [rows, output_dim]; None on a rejection."""
+    L = _lib_bwd()
+    g = core._i16(grad_output)
+    rows = g.numel() // lin.output_dim
+    dx = torch.empty((rows, lin.input_dim), dtype=torch.int16, device=g.device)
+    ws = core.workspace(L.nsrl_linear_backward_input_workspace_size(rows, lin.input_dim, lin.output_dim))
+    st = core.Status()
+    p = lin.c()
+    r = L.nsrl_linear_backward_input(core._ptr(g), rows, C.byref(p), core._ptr(grad_input_scales), core._ptr(dx),
+                                     core._ptr(ws), ws.numel(), core._ptr(st.buf), core._stream())
+    return dx if _run_status(r, st) else None
+
+
+def gated_mlp_backward_input_i16_q15_checked(grad_output, up, gate, down, forward_up, forward_gate):
+    """mlp.rs:256-357 with identity grad-input scales: (grad_up, grad_gate, grad_input, saturations) or None."""
+    L = _lib_bwd()
+    g = core._i16(grad_output)
+    d, F = up.input_dim, up.output_dim
+    rows = g.numel() // d
+    dev = g.device
+    gu = torch.empty((rows, F), dtype=torch.int16, device=dev)
+    gg = torch.empty_like(gu)
+    gi = torch.empty((rows, d), dtype=torch.int16, device=dev)
+    sat = torch.zeros(1, dtype=torch.int64, device=dev)
+    ws = core.workspace(L.nsrl_gated_mlp_backward_input_workspace_size(rows, d, F))
+    st = core.Status()
+    pu, pg, pd = up.c(), gate.c(), down.c()
+    fu, fg = core._i16(forward_up), core._i16(forward_gate)  # held until the call is enqueued
+    r = L.nsrl_gated_mlp_backward_input(core._ptr(g), rows, d, F, C.byref(pu), C.byref(pg), C.byref(pd),
+                                        core._ptr(fu), core._ptr(fg), core._ptr(gu), core._ptr(gg), core._ptr(gi),
+                                        core._ptr(sat), core._ptr(ws), ws.numel(), core._ptr(st.buf), core._stream())
+    return (gu, gg, gi, int(sat.item())) if _run_status(r, st) else None
+
+
+def rms_norm_backward_rows(x, gamma, grad_output, eps, gamma_grad: Optional[torch.Tensor] = None):
+    """rms_norm.rs:96-170 per row: (grad_input, gamma_grad i64, saturations) or None."""
+    L = _lib_bwd()
+    x = core._i16(x)
+    d = gamma.numel()
+    rows = x.numel() // d
+    gi = torch.empty((rows, d), dtype=torch.int16, device=x.device)
+    gw = torch.zeros(d, dtype=torch.int64, device=x.device) if gamma_grad is None else gamma_grad
+    sat = torch.zeros(1, dtype=torch.int64, device=x.device)
+    st = core.Status()
+    g16, go = core._i16(gamma), core._i16(grad_output)  # held until the call is enqueued
+    r = L.nsrl_rms_norm_backward_rows(core._ptr(x), rows, d, core._ptr(g16), core._ptr(go), int(eps), core._ptr(gi),
+                                      core._ptr(gw), core._ptr(sat), core._ptr(st.buf), core._stream())
+    return (gi, gw, int(sat.item())) if _run_status(r, st) else None
+
+
+def attention_with_probabilities(q, k, v, batch, seq_len, d_model, heads):
+    """Causal attention on int16 q, k, v [batch*seq_len, d]: (context, P [batch, heads, S, S]) or None."""
+    L = _lib_bwd()
+    q, k, v = core._i16(q), core._i16(k), core._i16(v)
+    ctx = torch.empty((batch * seq_len, d_model), dtype=torch.int16, device=q.device)
+    P = torch.empty((batch, heads, seq_len, seq_len), dtype=torch.int16, device=q.device)
+    st = core.Status()
+    r = L.nsrl_attention_with_probabilities(core._ptr(q), core._ptr(k), core._ptr(v), d_model, batch, seq_len, d_model,
+                                            heads, core._ptr(ctx), core._ptr(P), core._ptr(st.buf), core._stream())
+    return (ctx, P) if _run_status(r, st) else None
+
+
+def attention_backward(q, k, v, P, grad_context, batch, seq_len, d_model, heads):
+    """nsrl-train/src/lib.rs:16623-16900: (dq, dk, dv) or None."""
+    L = _lib_bwd()
+    q, k, v, P, dC = (core._i16(t) for t in (q, k, v, P, grad_context))
+    dq = torch.empty((batch * seq_len, d_model), dtype=torch.int16, device=q.device)
+    dk = torch.empty_like(dq)
+    dv = torch.empty_like(dq)
+    ws = core.workspace(L.nsrl_attention_backward_workspace_size(batch, seq_len, heads))
+    st = core.Status()
+    r = L.nsrl_attention_backward(core._ptr(q), core._ptr(k), core._ptr(v), d_model, core._ptr(P), core._ptr(dC),
+                                  batch, seq_len, d_model, heads, core._ptr(dq), core._ptr(dk), core._ptr(dv),
+                                  core._ptr(ws), ws.numel(), core._ptr(st.buf), core._stream())
+    return (dq, dk, dv) if _run_status(r, st) else None
+
+
+class TrainModel:
+    """The mini transformer (crates/nsrl-train MiniTransformerMlpModel) on one device.
+
+    layers: list of dicts with core.Linear entries q k v o up gate down and
+    optional int16 attn_gamma / mlp_gamma (RMS norm on when present)."""
+
+    def __init__(self, embeddings, positions, layers, head, d_model, heads, hidden_dim, seq_len):
+        dev = core._dev()
+        self.embeddings = embeddings.to(dev, torch.int16).contiguous()
+        self.positions = None if positions is None else positions.to(dev, torch.int16).contiguous()
+        self.layers = []
+        for ly in layers:
+            e = dict(ly)
+            for g in ("attn_gamma", "mlp_gamma"):
+                if e.get(g) is not None:
+                    e[g] = e[g].to(dev, torch.int16).contiguous()
+            self.layers.append(e)
+        self.head = head
+        self.d_model, self.heads, self.hidden_dim, self.seq_len = d_model, heads, hidden_dim, seq_len
+
+    def c(self):
+        arr = (_TrainLayerC * len(self.layers))()
+        for i, ly in enumerate(self.layers):
+            arr[i].attn_gamma = None if ly.get("attn_gamma") is None else ly["attn_gamma"].data_ptr()
+            arr[i].mlp_gamma = None if ly.get("mlp_gamma") is None else ly["mlp_gamma"].data_ptr()
+            for j, nm in enumerate(LAYER_LINEARS):
+                arr[i].lin[j] = ly[nm].c()
+        m = _TrainModelC(self.d_model, self.heads, self.hidden_dim, len(self.layers), self.seq_len,
+                         self.embeddings.data_ptr(), None if self.positions is None else self.positions.data_ptr(),
+                         C.cast(arr, C.c_void_p), self.head.c())
+        m._keep = arr
+        return m
+
+    def arena_layout(self):
+        """(offset, length) of every gradient in the arena, the same order as the oracle's."""
+        d, F, S = self.d_model, self.hidden_dim, self.seq_len
+        lay = {"head": (0, 256 * d)}
+        off = 256 * d
+        for li in range(len(self.layers)):
+            for nm, n in zip(LAYER_LINEARS + ("rms_attn", "rms_mlp"), [d * d] * 4 + [F * d] * 3 + [d, d]):
+                lay[(li, nm)] = (off, n)
+                off += n
+        lay["emb"] = (off, 256 * d)
+        off += 256 * d
+        lay["pos"] = (off, S * d)
+        off += S * d
+        lay["total"] = off
+        return lay
+
+
+class TrainStepBuffers:
+    """Gradient arena, sample counts, stats and workspace of nsrl_train_windows for W windows."""
+
+    def __init__(self, model: TrainModel, windows: int):
+        L = _lib_bwd()
+        m = model.c()
+        dev = core._dev()
+        self.n = L.nsrl_train_arena_len(C.byref(m))
+        self.arena = torch.zeros(self.n, dtype=torch.int64, device=dev)
+        self.counts = torch.zeros(2 + 9 * len(model.layers), dtype=torch.int64, device=dev)
+        self.stats = torch.zeros(4, dtype=torch.int64, device=dev)
+        nbytes = L.nsrl_train_workspace_size(C.byref(m), windows)
+        if nbytes == 0:
+            raise ValueError(L.nsrl_last_error().decode() or "invalid training-step shape")
+        self.ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        self.status = core.Status()
+        self.windows = windows
+
+    def clear(self):
+        self.arena.zero_()
+        self.counts.zero_()
+        self.stats.zero_()
+
+
+def launch_train_windows(model: TrainModel, contexts: torch.Tensor, targets: torch.Tensor,
+                         buf: TrainStepBuffers, freq_weights: Optional[torch.Tensor] = None) -> int:
+    """Enqueues nsrl_train_windows on the current stream; returns the C status code."""
+    L = _lib_bwd()
+    m = model.c()
+    return L.nsrl_train_windows(C.byref(m), core._ptr(contexts), core._ptr(targets), core._ptr(freq_weights),
+                                buf.windows, core._ptr(buf.arena), core._ptr(buf.counts), core._ptr(buf.stats),
+                                core._ptr(buf.ws), buf.ws.numel(), core._ptr(buf.status.buf), core._stream())
+
+
+def mini_transformer_map_reduce_worker_batch(model: TrainModel, contexts: torch.Tensor, targets: torch.Tensor,
+                                             freq_weights: Optional[torch.Tensor] = None):
+    """nsrl-train/src/lib.rs:7051-7399 for W windows [W, seq_len] uint8 with targets [W] uint8:
+    (arena i64, counts, stats dict), or None when the batch is rejected."""
+    contexts = contexts.to(core._dev(), torch.uint8).contiguous()
+    targets = targets.to(core._dev(), torch.uint8).contiguous()
+    buf = TrainStepBuffers(model, contexts.shape[0])
+    buf.status.reset()
+    r = launch_train_windows(model, contexts, targets, buf, freq_weights)
+    if not _run_status(r, buf.status):
+        return None
+    s = buf.stats.cpu().tolist()
+    return buf.arena, buf.counts, {"accepted": s[0], "mlp_saturation_count": s[1], "attention_saturation_count": s[2],
+                                   "residual_saturation_count": s[3]}
+
+
+# --------------------------------------------------- data-parallel step --
+import dataclasses
+
+
+@dataclasses.dataclass(frozen=True)
+class MiniTransformerTrainConfig:
+    """The learning-rate fields of MiniTransformerMlpTrainConfig (nsrl-train/src/lib.rs:300-390)
+    with the reference defaults (:86-91, :373-381)."""
+    learning_rate: int = 1
+    output_learning_rate_shift: int = 18
+    mlp_learning_rate_shift: int = 16
+    embedding_learning_rate_shift: int = 14
+    attention_learning_rate_shift: int = 24
+    attention_q_learning_rate_shift: int = 18
+    attention_qk_learning_rate_shift: int = 18
+
+
+MAX_RIGHT_SHIFT = 62
+STACKED_BLOCK_EXTRA_SHIFT = 2          # nsrl-train/src/lib.rs:1541
+STACKED_LOWER_LAYER_EXTRA_SHIFT = 14   # :1542
+STACKED_EMBEDDING_EXTRA_SHIFT = 0      # :1543
+
+
+def mini_transformer_batch_learning_rate_shift(batch_windows: int) -> Optional[int]:
+    """lib.rs:13591-13605: ceil(log2(batch_windows)), None for 0."""
+    if batch_windows == 0:
+        return None
+    shift, covered = 0, 1
+    while covered < batch_windows:
+        covered *= 2
+        shift += 1
+    return shift
+
+
+def mini_transformer_batch_component_shift_config(cfg: MiniTransformerTrainConfig, batch_windows: int):
+    """lib.rs:13607-13650: every component shift minus the batch shift (ValueError = InvalidConfig)."""
+    b = mini_transformer_batch_learning_rate_shift(batch_windows)
+    if b is None:
+        raise ValueError("invalid config: zero batch windows")
+    out = {}
+    for f in ("output_learning_rate_shift", "mlp_learning_rate_shift", "embedding_learning_rate_shift",
+              "attention_learning_rate_shift", "attention_q_learning_rate_shift", "attention_qk_learning_rate_shift"):
+        v = getattr(cfg, f) - b
+        if v < 0:
+            raise ValueError(f"invalid config: {f} below the batch shift {b}")
+        out[f] = v
+    return dataclasses.replace(cfg, **out)
+
+
+def mini_transformer_stacked_layer_runtime_config(cfg: MiniTransformerTrainConfig, layer_index: int,
+                                                  layer_count: int):
+    """lib.rs:15454-15495."""
+    f4 = ("mlp_learning_rate_shift", "attention_learning_rate_shift", "attention_q_learning_rate_shift",
+          "attention_qk_learning_rate_shift")
+    out = {f: min(getattr(cfg, f) + STACKED_BLOCK_EXTRA_SHIFT, MAX_RIGHT_SHIFT) for f in f4}
+    if layer_index + 1 < layer_count:
+        out = {f: min(v + STACKED_LOWER_LAYER_EXTRA_SHIFT, MAX_RIGHT_SHIFT) for f, v in out.items()}
+    return dataclasses.replace(cfg, **out)
+
+
+def layer_apply_shifts(cfg: MiniTransformerTrainConfig, accepted_windows: int, layers: int) -> dict:
+    """Every apply shift of one batch (lib.rs:6249-6400): output head, per layer the MLP and q/k/v/o, embeddings."""
+    b = mini_transformer_batch_component_shift_config(cfg, accepted_windows)
+    sh = {"head": b.output_learning_rate_shift}
+    for li in range(layers):
+        lc = mini_transformer_stacked_layer_runtime_config(b, li, layers) if layers > 1 else b
+        for nm in ("up", "gate", "down"):
+            sh[(li, nm)] = lc.mlp_learning_rate_shift
+        sh[(li, "q")] = lc.attention_q_learning_rate_shift
+        sh[(li, "k")] = lc.attention_qk_learning_rate_shift
+        sh[(li, "v")] = lc.attention_learning_rate_shift
+        sh[(li, "o")] = lc.attention_learning_rate_shift
+    emb = b.embedding_learning_rate_shift
+    if layers > 1:
+        emb = min(emb + STACKED_EMBEDDING_EXTRA_SHIFT, MAX_RIGHT_SHIFT)
+    sh["emb"] = emb
+    return sh
+
+
+class TrainState:
+    """Carried residuals of every applied parameter (the residual arrays of
+    LinearWeightGradientI64 and MiniTransformerEmbeddingGradientI64), laid
+    out like the gradient arena."""
+
+    def __init__(self, model: TrainModel):
+        self.residuals = torch.zeros(model.arena_layout()["total"], dtype=torch.int64, device=core._dev())
+
+
+def _lib_apply():
+    L = _lib_bwd()
+    if not getattr(L, "_apply_bound", False):
+        vp, sz = C.c_void_p, C.c_size_t
+        L.nsrl_apply_embedding_gradient_i64_to_i16.argtypes = [vp, vp, vp, sz, vp, C.c_int32, C.c_uint8, vp, vp, vp]
+        L._apply_bound = True
+    return L
+
+
+def allreduce_flat_i64(flat: torch.Tensor, group=None) -> tuple[torch.Tensor, bool]:
+    """Exact sum of an int64 vector over the ranks of `group` in rank order:
+    one all-reduce when the sum over ranks of max |x| proves that no prefix of
+    any ordering leaves i64, else all-gather and an ordered merge with
+    overflow detection.  Returns (sum, ok)."""
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    bound = torch.tensor([_abs_max(flat)], dtype=torch.float64, device=flat.device)
+    dist.all_reduce(bound, op=dist.ReduceOp.SUM, group=group)
+    if float(bound.item()) < 2.0**62:
+        flat = flat.clone()
+        dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=group)
+        return flat, True
+    parts = [torch.empty_like(flat) for _ in range(world)]
+    dist.all_gather(parts, flat, group=group)
+    merged, ovf = _ordered_merge(torch.stack(parts))
+    return merged, not ovf
+
+
+def allreduce_arena_i64(buf: TrainStepBuffers, group=None) -> bool:
+    """Sums the arena, the sample counts and the stats of every rank into every
+    rank, exactly (the ordered merge of lib.rs:7401-7471 with rank r = worker
+    chunk r).  False when that merge overflows i64."""
+    import torch.distributed as dist
+    if not dist.is_initialized() or dist.get_world_size(group) == 1:
+        return True
+    flat, ok = allreduce_flat_i64(torch.cat([buf.arena, buf.counts, buf.stats]), group)
+    n, c = buf.arena.numel(), buf.counts.numel()
+    buf.arena.copy_(flat[:n])
+    buf.counts.copy_(flat[n:n + c])
+    buf.stats.copy_(flat[n + c:])
+    return ok
+
+
+def apply_batch(model: TrainModel, state: TrainState, buf: TrainStepBuffers, cfg: MiniTransformerTrainConfig,
+                accepted_windows: int) -> Optional[dict]:
+    """Applies the merged batch gradients to every parameter (lib.rs:6249-6400):
+    i8 weights with carried residuals, then the i16 embeddings.  Returns the
+    summed update stats, or None on an arithmetic rejection."""
+    L = _lib_apply()
+    lay = model.arena_layout()
+    sh = layer_apply_shifts(cfg, accepted_windows, len(model.layers))
+    st = core.Status()
+    st.reset()
+    stats = torch.zeros(3, dtype=torch.int64, device=buf.arena.device)
+    total = torch.zeros(3, dtype=torch.int64, device=buf.arena.device)
+    lr = int(cfg.learning_rate)
+
+    def apply_i8(key, weights, count_idx):
+        o, n = lay[key]
+        r = L.nsrl_apply_linear_weight_gradient_i64_to_i8(
+            core._ptr(buf.arena[o:o + n]), core._ptr(state.residuals[o:o + n]), core._ptr(weights), n,
+            core._ptr(buf.counts[count_idx:count_idx + 1]), lr, int(sh[key]), 1, core._ptr(stats), core._ptr(st.buf),
+            core._stream())
+        core._check(r)
+        total.add_(stats)
+
+    apply_i8("head", model.head.weights, 0)
+    for li, ly in enumerate(model.layers):
+        for j, nm in enumerate(LAYER_LINEARS):
+            apply_i8((li, nm), ly[nm].weights, 1 + 9 * li + j)
+    ce = 1 + 9 * len(model.layers)
+    stats.zero_()
+    for key, emb in (("emb", model.embeddings), ("pos", model.positions)):
+        if emb is None:
+            continue
+        o, n = lay[key]
+        r = L.nsrl_apply_embedding_gradient_i64_to_i16(
+            core._ptr(buf.arena[o:o + n]), core._ptr(state.residuals[o:o + n]), core._ptr(emb), n,
+            core._ptr(buf.counts[ce:ce + 1]), lr, int(sh["emb"]), core._ptr(stats), core._ptr(st.buf), core._stream())
+        core._check(r)
+    total.add_(stats)
+    o, n = lay["emb"]
+    buf.arena[o:o + n + lay["pos"][1]].zero_()
+    buf.counts[ce].zero_()
+    code, _ = st.fetch()
+    if code != core.NSRL_OK:
+        return None
+    t = total.cpu().tolist()
+    return {"gradient_saturation_count": t[0], "zero_delta_count": t[1], "weight_delta_l1": t[2]}
+
+
+def mini_transformer_train_step(model: TrainModel, state: TrainState, contexts: torch.Tensor, targets: torch.Tensor,
+                                cfg: MiniTransformerTrainConfig, buf: TrainStepBuffers, group=None,
+                                freq_weights: Optional[torch.Tensor] = None) -> Optional[dict]:
+    """One data-parallel batch: this rank's windows forward + backward into i64
+    accumulators (lib.rs:7051-7399), the exact int64 all-reduce (:7401-7471),
+    and the requantising apply of every parameter (:6249-6400).  Returns the
+    batch stats, or None when the batch is rejected on any rank (:5371-5375).
+    A batch rejected before the apply leaves the model unchanged; the apply's
+    own checks (i64 overflow of avg * lr + residual) cannot fail for sums of
+    int16 products and are reported, not rolled back.  Every rank takes the
+    same collective steps."""
+    import torch.distributed as dist
+    buf.clear()
+    buf.status.reset()
+    r = launch_train_windows(model, contexts, targets, buf, freq_weights)
+    if r == core.NSRL_INVALID_SHAPE:
+        raise ValueError(_lib().nsrl_last_error().decode())
+    core._check(r)
+    code, _ = buf.status.fetch()
+    rejected = torch.tensor([0 if code == core.NSRL_OK else 1], dtype=torch.int64, device=buf.arena.device)
+    if dist.is_initialized() and dist.get_world_size(group) > 1:
+        dist.all_reduce(rejected, op=dist.ReduceOp.MAX, group=group)
+    if int(rejected.item()):
+        return None
+    if not allreduce_arena_i64(buf, group):
+        return None
+    s = buf.stats.cpu().tolist()
+    upd = apply_batch(model, state, buf, cfg, int(s[0]))
+    if upd is None:
+        return None
+    out = {"accepted": s[0], "mlp_saturation_count": s[1], "attention_saturation_count": s[2],
+           "residual_saturation_count": s[3]}
+    out.update(upd)
+    return out

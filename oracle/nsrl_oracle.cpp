@@ -1371,3 +1371,42 @@ int orc_train_block_forward(const TrainModel* m, size_t layer, const int16_t* x,
 }
 
 }  // extern "C"
+
+extern "C" {
+
+// nsrl-train/src/lib.rs:14457-14510: i16 embedding apply (see the CUDA entry
+// point of the same name for the rules); stats added to, accumulators kept.
+int orc_apply_embedding_gradient_i64_to_i16(const int64_t* acc, int64_t* residuals, int16_t* emb, size_t len,
+                                            uint64_t count, int32_t lr, uint8_t shift, uint64_t* stats) {
+  if (lr <= 0 || shift > MAX_RIGHT_SHIFT) return 1;
+  if (count == 0) return 0;
+  if (count > (uint64_t)INT64_MAX) return 1;
+  for (size_t i = 0; i < len; ++i) {
+    if (acc[i] == 0 && residuals[i] == 0) continue;
+    int64_t avg, product;
+    if (!round_ratio_i64(acc[i], (int64_t)count, &avg)) return 2;
+    if (__builtin_mul_overflow(avg, (int64_t)lr, &product)) return 2;
+    if (__builtin_add_overflow(product, residuals[i], &product)) return 2;
+    const int64_t scaled = rhu(product, shift);
+    if (shift == 0) {
+      residuals[i] = 0;
+    } else {
+      __int128 r = (__int128)product - ((__int128)scaled << shift);
+      if (r < INT64_MIN || r > INT64_MAX) return 2;
+      residuals[i] = (int64_t)r;
+    }
+    const int64_t delta = -scaled;
+    if (delta == 0) stats[1] += 1;
+    const int16_t prev = emb[i];
+    int64_t unclamped;
+    if (__builtin_add_overflow((int64_t)prev, delta, &unclamped)) return 2;
+    const int16_t cl = saturate_i16(unclamped);
+    if ((int64_t)cl != unclamped) stats[0] += 1;
+    const int64_t ad = (int64_t)cl - (int64_t)prev;
+    stats[2] += (uint64_t)(ad < 0 ? -ad : ad);
+    emb[i] = cl;
+  }
+  return 0;
+}
+
+}  // extern "C"

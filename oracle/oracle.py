@@ -436,3 +436,92 @@ def attention_backward(q, k, v, P, dC, B, S, d, H):
     r = lib().orc_attention_backward(*[_p(a) for a in held], C.c_size_t(B), C.c_size_t(S), C.c_size_t(d),
                                      C.c_size_t(H), _p(dq), _p(dk), _p(dv))
     return None if r else (dq, dk, dv)
+
+
+def apply_embedding_gradient_i64_to_i16(acc, residuals, emb, count, lr, shift, stats):
+    """nsrl-train/src/lib.rs:14457-14510 in place on numpy arrays; False on a rejection."""
+    return lib().orc_apply_embedding_gradient_i64_to_i16(_p(acc), _p(residuals), _p(emb), C.c_size_t(emb.size),
+                                                         C.c_uint64(int(count)), C.c_int32(lr), C.c_uint8(shift),
+                                                         _p(stats)) == 0
+
+
+def batch_apply_shifts(cfg: dict, accepted_windows: int, layers: int):
+    """Apply shifts of one batch: lib.rs:13591-13650 (batch shift), :15454-15495
+    (stacked layers: +2, lower layers +14, capped at 62), :6372-6380 (embeddings)."""
+    b, covered = 0, 1
+    while covered < accepted_windows:
+        covered *= 2
+        b += 1
+    c = {k: v - b for k, v in cfg.items() if k != "learning_rate"}
+    if min(c.values()) < 0:
+        return None
+    sh = {"head": c["output_learning_rate_shift"], "emb": c["embedding_learning_rate_shift"]}
+    for li in range(layers):
+        m, a, aq, ak = (c["mlp_learning_rate_shift"], c["attention_learning_rate_shift"],
+                        c["attention_q_learning_rate_shift"], c["attention_qk_learning_rate_shift"])
+        if layers > 1:
+            m, a, aq, ak = (min(v + 2, 62) for v in (m, a, aq, ak))
+            if li + 1 < layers:
+                m, a, aq, ak = (min(v + 14, 62) for v in (m, a, aq, ak))
+        for nm in ("up", "gate", "down"):
+            sh[(li, nm)] = m
+        sh[(li, "q")], sh[(li, "k")], sh[(li, "v")], sh[(li, "o")] = aq, ak, a, a
+    return sh
+
+
+DEFAULT_TRAIN_CONFIG = {"learning_rate": 1, "output_learning_rate_shift": 18, "mlp_learning_rate_shift": 16,
+                        "embedding_learning_rate_shift": 14, "attention_learning_rate_shift": 24,
+                        "attention_q_learning_rate_shift": 18, "attention_qk_learning_rate_shift": 18}
+
+
+def train_step(model: TrainModel, residuals, contexts, targets, cfg=None, workers=1):
+    """One map-reduce batch (lib.rs:6970-7050 with `workers` chunks merged in
+    order) and the apply of every parameter (lib.rs:6249-6400), in place on
+    the model's numpy weights and on `residuals` (arena layout).  Returns the
+    stats dict, or None when the batch is rejected."""
+    cfg = cfg or DEFAULT_TRAIN_CONFIG
+    r = train_windows(model, contexts, targets, workers=workers)
+    if r is None:
+        return None
+    acc, counts, stats = r
+    lay = model.arena_layout()
+    sh = batch_apply_shifts(cfg, stats["accepted"], len(model.layers))
+    if sh is None:
+        return None
+    lr = cfg["learning_rate"]
+    tot = [0, 0, 0]
+
+    def apply_i8(key, lin, count):
+        o, n = lay[key]
+        out = apply_linear_gradient_i64_to_i8(acc[o:o + n], residuals[o:o + n], lin.weights, count, lr, sh[key], True)
+        if out is None:
+            return False
+        residuals[o:o + n] = out[1]
+        lin.weights[...] = out[2].reshape(lin.weights.shape)
+        for i in range(3):
+            tot[i] += out[4][i]
+        return True
+
+    if not apply_i8("head", model.head, int(counts[0])):
+        return None
+    for li, ly in enumerate(model.layers):
+        for j, nm in enumerate(LAYER_LINEARS):
+            if not apply_i8((li, nm), ly[nm], int(counts[1 + 9 * li + j])):
+                return None
+    est = np.zeros(3, np.uint64)
+    ce = int(counts[1 + 9 * len(model.layers)])
+    for key, emb in (("emb", model.embeddings), ("pos", model.positions)):
+        if emb is None:
+            continue
+        o, n = lay[key]
+        a = np.ascontiguousarray(acc[o:o + n])
+        rs = np.ascontiguousarray(residuals[o:o + n])
+        flat = emb.reshape(-1)
+        if not apply_embedding_gradient_i64_to_i16(a, rs, flat, ce, lr, sh["emb"], est):
+            return None
+        residuals[o:o + n] = rs
+    for i in range(3):
+        tot[i] += int(est[i])
+    stats = dict(stats)
+    stats.update({"gradient_saturation_count": tot[0], "zero_delta_count": tot[1], "weight_delta_l1": tot[2]})
+    return stats

@@ -1,0 +1,205 @@
+"""GPU parity of the training step: every backward primitive and the
+map-reduce window step against the oracle, bit for bit."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+
+from train_models import (TEXT, random_model, random_windows, reference_initial_model, window_starts,
+                          windows_from_text)
+
+pytestmark = pytest.mark.gpu
+
+
+def _core():
+    from nsrl_b200 import core, train
+    return core, train
+
+
+def _lin(lin):
+    core, _ = _core()
+    sc = core.make_scales(lin.scales["multiplier"].astype(np.int64), lin.scales["right_shift"].astype(np.int64))
+    return core.Linear(torch.from_numpy(lin.weights.copy()), sc,
+                       None if lin.bias is None else torch.from_numpy(lin.bias.copy()))
+
+
+def _dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def to_gpu(m):
+    _, train = _core()
+    layers = []
+    for ly in m.layers:
+        e = {nm: _lin(ly[nm]) for nm in O.LAYER_LINEARS}
+        for g in ("attn_gamma", "mlp_gamma"):
+            if ly.get(g) is not None:
+                e[g] = torch.from_numpy(ly[g].copy())
+        layers.append(e)
+    return train.TrainModel(torch.from_numpy(m.embeddings.copy()),
+                            None if m.positions is None else torch.from_numpy(m.positions.copy()), layers,
+                            _lin(m.head), m.d, m.H, m.F, m.S)
+
+
+@pytest.mark.parametrize("M,K,N,shift", [(7, 64, 48, 0), (300, 256, 256, 3), (129, 96, 1024, 0)])
+def test_linear_backward_input(M, K, N, shift):
+    _, train = _core()
+    rng = np.random.default_rng(M + K)
+    lin = O.Linear(rng.integers(-127, 128, (N, K)).astype(np.int8), O.scales(1, shift, N))
+    g = rng.integers(-32768, 32768, (M, N)).astype(np.int16)
+    ref = O.linear_backward_input(g, lin)
+    out = train.linear_backward_input_i16_i8_i16_per_channel_checked(_dev(g), _lin(lin))
+    assert np.array_equal(out.cpu().numpy(), ref)
+
+
+def test_linear_backward_input_general_scales():
+    """Multipliers other than 1 and per-channel grad-input scales (the SIMT form)."""
+    core, train = _core()
+    rng = np.random.default_rng(11)
+    M, K, N = 33, 48, 32
+    lin = O.Linear(rng.integers(-127, 128, (N, K)).astype(np.int8),
+                   O.scales(rng.integers(1, 5, N), rng.integers(0, 4, N)))
+    gin = O.scales(rng.integers(1, 3, K), rng.integers(0, 3, K))
+    g = rng.integers(-32768, 32768, (M, N)).astype(np.int16)
+    ref = O.linear_backward_input(g, lin, gin)
+    gin_t = core.make_scales(gin["multiplier"].astype(np.int64), gin["right_shift"].astype(np.int64))
+    out = train.linear_backward_input_i16_i8_i16_per_channel_checked(_dev(g), _lin(lin), gin_t)
+    assert np.array_equal(out.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("T,d,F", [(5, 32, 64), (257, 128, 256)])
+def test_gated_mlp_backward_input(T, d, F):
+    _, train = _core()
+    rng = np.random.default_rng(T)
+    up = O.Linear(rng.integers(-127, 128, (F, d)).astype(np.int8), O.scales(1, 10, F))
+    gate = O.Linear(rng.integers(-127, 128, (F, d)).astype(np.int8), O.scales(1, 10, F))
+    down = O.Linear(rng.integers(-127, 128, (d, F)).astype(np.int8), O.scales(1, 11, d))
+    fu = rng.integers(-32768, 32768, (T, F)).astype(np.int16)
+    fg = rng.integers(-32768, 32768, (T, F)).astype(np.int16)
+    g = rng.integers(-8000, 8000, (T, d)).astype(np.int16)
+    ref = O.gated_mlp_backward_input(g, up, gate, down, fu, fg)
+    out = train.gated_mlp_backward_input_i16_q15_checked(_dev(g), _lin(up), _lin(gate), _lin(down), _dev(fu), _dev(fg))
+    for a, b in zip(out[:3], ref[:3]):
+        assert np.array_equal(a.cpu().numpy(), b)
+    assert out[3] == ref[3]
+
+
+@pytest.mark.parametrize("T,d,eps", [(3, 4, 1), (513, 256, 1), (64, 128, 0)])
+def test_rms_norm_backward(T, d, eps):
+    _, train = _core()
+    rng = np.random.default_rng(T + d)
+    x = rng.integers(-32768, 32768, (T, d)).astype(np.int16)
+    x[0, :] = rng.integers(-3, 4, d)  # a small row: large inverse RMS
+    w = rng.integers(-32768, 32768, d).astype(np.int16)
+    go = rng.integers(-32768, 32768, (T, d)).astype(np.int16)
+    ref = O.rms_norm_backward_rows(x, w, go, eps)
+    gi, gw, sat = train.rms_norm_backward_rows(_dev(x), _dev(w), _dev(go), eps)
+    assert np.array_equal(gi.cpu().numpy(), ref[0])
+    assert np.array_equal(gw.cpu().numpy(), ref[1])
+    assert sat == ref[2]
+
+
+@pytest.mark.parametrize("B,S,d,H", [(2, 33, 64, 4), (3, 64, 128, 2), (1, 200, 64, 1)])
+def test_attention_probabilities_and_backward(B, S, d, H):
+    _, train = _core()
+    rng = np.random.default_rng(B * S)
+    q = rng.integers(-6000, 6000, (B * S, d)).astype(np.int16)
+    k = rng.integers(-6000, 6000, (B * S, d)).astype(np.int16)
+    v = rng.integers(-32768, 32768, (B * S, d)).astype(np.int16)
+    dC = rng.integers(-32768, 32768, (B * S, d)).astype(np.int16)
+    P = O.attention_probabilities(q, k, B, S, d, H)
+    ctx_g, P_g = train.attention_with_probabilities(_dev(q), _dev(k), _dev(v), B, S, d, H)
+    assert np.array_equal(P_g.cpu().numpy(), P)
+    ref = O.attention_backward(q, k, v, P, dC, B, S, d, H)
+    out = train.attention_backward(_dev(q), _dev(k), _dev(v), P_g, _dev(dC), B, S, d, H)
+    for a, b in zip(out, ref):
+        assert np.array_equal(a.cpu().numpy(), b)
+
+
+def _check_step(m, ctx, tgt):
+    _, train = _core()
+    ref = O.train_windows(m, ctx, tgt)
+    assert ref is not None
+    out = train.mini_transformer_map_reduce_worker_batch(to_gpu(m), torch.from_numpy(ctx), torch.from_numpy(tgt))
+    assert out is not None
+    arena, counts, stats = out
+    a = arena.cpu().numpy()
+    lay = m.arena_layout()
+    for key, span in lay.items():
+        if key == "total":
+            continue
+        o, n = span
+        assert np.array_equal(a[o:o + n], ref[0][o:o + n]), key
+    assert np.array_equal(counts.cpu().numpy().astype(np.uint64), ref[1])
+    assert stats == ref[2]
+
+
+def test_train_step_reference_initial_model():
+    """The reference's stacked map-reduce test case (lib.rs:22832-22925) on the GPU."""
+    m = reference_initial_model(seq_len=4, layers=2)
+    ctx, tgt = windows_from_text(TEXT, 4, window_starts(len(TEXT), 4, 1, 4))
+    _check_step(m, ctx, tgt)
+
+
+@pytest.mark.parametrize("d,H,F,L,S,W,rms,pos", [
+    (64, 4, 128, 2, 16, 3, True, True),
+    (64, 1, 128, 1, 24, 2, False, False),
+    (128, 2, 256, 2, 40, 2, True, False),
+])
+def test_train_step_random_models(d, H, F, L, S, W, rms, pos):
+    m = random_model(d, H, F, L, S, rms=rms, positions=pos, seed=d + S)
+    ctx, tgt = random_windows(W, S, seed=d + S)
+    _check_step(m, ctx, tgt)
+
+
+def _weights_equal(m, gm):
+    assert np.array_equal(gm.head.weights.cpu().numpy(), m.head.weights)
+    for ly, gly in zip(m.layers, gm.layers):
+        for nm in O.LAYER_LINEARS:
+            assert np.array_equal(gly[nm].weights.cpu().numpy(), ly[nm].weights), nm
+    assert np.array_equal(gm.embeddings.cpu().numpy(), m.embeddings)
+    if m.positions is not None:
+        assert np.array_equal(gm.positions.cpu().numpy(), m.positions)
+
+
+@pytest.mark.parametrize("L,rms", [(2, True), (1, False)])
+def test_data_parallel_step_updates_weights_bit_exact(L, rms):
+    """Two batches of the full step (windows, exchange, apply) against the oracle:
+    every updated i8 weight, i16 embedding and carried residual."""
+    _, train = _core()
+    d, H, F, S, W = 64, 4, 128, 16, 4
+    m = random_model(d, H, F, L, S, rms=rms, positions=True, seed=21 + L)
+    gm = to_gpu(m)
+    res = np.zeros(m.arena_layout()["total"], np.int64)
+    state = train.TrainState(gm)
+    buf = train.TrainStepBuffers(gm, W)
+    cfg = train.MiniTransformerTrainConfig(output_learning_rate_shift=10, mlp_learning_rate_shift=12,
+                                           embedding_learning_rate_shift=8, attention_learning_rate_shift=14,
+                                           attention_q_learning_rate_shift=12, attention_qk_learning_rate_shift=12)
+    ocfg = {f: getattr(cfg, f) for f in O.DEFAULT_TRAIN_CONFIG}
+    for step in range(2):
+        ctx, tgt = random_windows(W, S, seed=30 + step)
+        ref = O.train_step(m, res, ctx, tgt, cfg=ocfg)
+        out = train.mini_transformer_train_step(gm, state, torch.from_numpy(ctx).cuda(), torch.from_numpy(tgt).cuda(),
+                                                cfg, buf)
+        assert ref is not None and out is not None
+        assert out == ref
+        _weights_equal(m, gm)
+        assert np.array_equal(state.residuals.cpu().numpy(), res)
+
+
+def test_sharded_windows_sum_to_the_whole_batch():
+    """Rank chunks run separately and merged in order equal the one-GPU batch
+    (the reference's multi-worker == single-worker pin, lib.rs:22927-23000)."""
+    _, train = _core()
+    m = random_model(64, 4, 128, 2, 16, seed=40)
+    gm = to_gpu(m)
+    ctx, tgt = random_windows(6, 16, seed=41)
+    whole = train.mini_transformer_map_reduce_worker_batch(gm, torch.from_numpy(ctx), torch.from_numpy(tgt))
+    parts = [train.mini_transformer_map_reduce_worker_batch(gm, torch.from_numpy(ctx[i:i + 3]),
+                                                            torch.from_numpy(tgt[i:i + 3])) for i in (0, 3)]
+    merged, ovf = train._ordered_merge(torch.stack([p[0] for p in parts]))
+    assert not ovf
+    assert torch.equal(merged, whole[0])
+    assert torch.equal(parts[0][1] + parts[1][1], whole[1])

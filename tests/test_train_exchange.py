@@ -77,3 +77,49 @@ def test_allreduce_matches_ordered_merge(tmp_path, case):
             else:
                 assert res["ok"]
                 assert np.array_equal(res["acc"][i].ravel(), ref[0]) and res["count"][i] == ref[1]
+
+
+def _flat_worker(rank, world, port, case, out_dir):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+    import torch.distributed as dist
+    from nsrl_b200 import train as T
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    parts, _ = _parts(case, rank)
+    flat = torch.from_numpy(np.concatenate([p.ravel() for p in parts]))
+    out, ok = T.allreduce_flat_i64(flat)
+    np.save(os.path.join(out_dir, f"f{rank}.npy"), np.array({"ok": ok, "out": out.numpy().copy()}, dtype=object),
+            allow_pickle=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("case", ["random", "overflow", "large_ok"])
+def test_flat_arena_allreduce_matches_ordered_merge(tmp_path, case):
+    """The training step's single-vector exchange (arena + counts + stats)."""
+    world = 2
+    mp.start_processes(_flat_worker, args=(world, _free_port(), case, str(tmp_path)), nprocs=world, join=True,
+                       start_method="spawn")
+    parts = np.stack([np.concatenate([p.ravel() for p in _parts(case, r)[0]]) for r in range(world)])
+    ref = O.merge_i64(parts, [0] * world)
+    for r in range(world):
+        res = np.load(tmp_path / f"f{r}.npy", allow_pickle=True).item()
+        if ref is None:
+            assert not res["ok"]
+        else:
+            assert res["ok"] and np.array_equal(res["out"], ref[0])
+
+
+def test_apply_shift_rules_match_oracle():
+    """Batch and stacked-layer learning-rate shifts (lib.rs:13591-13650, :15454-15495)."""
+    from nsrl_b200 import train as T
+    cfg = T.MiniTransformerTrainConfig()
+    for layers in (1, 2, 4):
+        for windows in (1, 2, 3, 64, 256, 1000):
+            a = T.layer_apply_shifts(cfg, windows, layers)
+            b = O.batch_apply_shifts(O.DEFAULT_TRAIN_CONFIG, windows, layers)
+            assert a == b, (layers, windows)
+    assert T.mini_transformer_batch_learning_rate_shift(0) is None
+    with pytest.raises(ValueError):
+        T.mini_transformer_batch_component_shift_config(T.MiniTransformerTrainConfig(output_learning_rate_shift=1), 8)
