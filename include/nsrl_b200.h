@@ -287,6 +287,20 @@ nsrl_status nsrl_attention_backward(const int16_t* q, const int16_t* k, const in
                                     size_t seq_len, size_t d_model, size_t heads, int16_t* dq, int16_t* dk, int16_t* dv,
                                     void* workspace, size_t workspace_bytes, nsrl_device_status* status, void* stream);
 
+/* i64 weight-gradient accumulation on the tensor cores for int16 gradients:
+ * acc[n][k] += g'[r][n] * x[r][k] over r < rows with g' = rhu(g, shift_n)
+ * (forward scales with multiplier 1, the reference's tables; another
+ * multiplier rejects the call), *sample_count += rows.  The prescale of
+ * linear.rs:573-592 followed by accumulate_linear_weight_gradient_i64_prescaled
+ * (nsrl-train-core/src/lib.rs:344-384) once per row.  x [rows][input_dim],
+ * grad_output [rows][output_dim] int16, accumulators [output_dim][input_dim]. */
+size_t nsrl_accumulate_weight_gradient_i16_workspace_size(size_t rows, size_t input_dim, size_t output_dim);
+nsrl_status nsrl_accumulate_weight_gradient_i16(const int16_t* x, const int16_t* grad_output, size_t rows,
+                                                size_t input_dim, size_t output_dim, const nsrl_fixed_scale* scales,
+                                                long long* accumulators, unsigned long long* sample_count,
+                                                void* workspace, size_t workspace_bytes, nsrl_device_status* status,
+                                                void* stream);
+
 /* ------------------------------------------------- training window step --
  * The map-reduce worker of the reference's mini transformer
  * (nsrl-train/src/lib.rs:7051-7399) for `windows` windows of seq_len bytes on

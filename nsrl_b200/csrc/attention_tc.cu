@@ -67,6 +67,7 @@ struct Args {
   uint8_t* ctx_lo;
   unsigned long long* ctx_l1;
   long long ldc;
+  int16_t* probs;    // optional: P [B][H][S][S] of the visited key tiles (the caller zeroes the rest)
   nsrl_device_status* st;
 };
 
@@ -412,6 +413,11 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
               (uint32_t)min(32767ull, ((unsigned long long)(uint32_t)w[i + 1] * inv + 32768ull) >> 16);
           pw[i / 2] = p0 | (p1 << 16);
         }
+        if (a.probs && row_live && key0 < S) {  // nsrl-train/src/lib.rs:15353-15418: the cached P
+          uint4* dst = reinterpret_cast<uint4*>(a.probs + (((long long)b * a.H + h) * S + qi) * (long long)S + key0);
+          dst[0] = make_uint4(pw[0], pw[1], pw[2], pw[3]);
+          dst[1] = make_uint4(pw[4], pw[5], pw[6], pw[7]);
+        }
         const int pb = j & 1;
         if (j >= 2) wait_bar(&ctl->p_empty[pb], ((j >> 1) - 1) & 1, ctl, a.st);
         uint8_t* ph = sm + OFF_P + pb * 2 * PLANE_P;
@@ -551,7 +557,7 @@ size_t attention_tc_scratch_bytes(size_t B, size_t S, size_t d, size_t H) {
 
 cudaError_t launch_attention_tc(const Planes& qkv, const VtPlanes& vt, size_t B, size_t S, size_t d, size_t H,
                                 bool causal, Planes ctx, int16_t* wscr, nsrl_device_status* st,
-                                cudaStream_t stream) {
+                                cudaStream_t stream, int16_t* probs) {
   if (!attention_tc_supported(S, d, H) || encode_fn() == nullptr) return cudaErrorNotSupported;
   const size_t T = B * S;
   Maps m;
@@ -569,6 +575,7 @@ cudaError_t launch_attention_tc(const Planes& qkv, const VtPlanes& vt, size_t B,
   a.ctx_lo = ctx.lo;
   a.ctx_l1 = ctx.l1;
   a.ldc = (long long)ctx.ld;
+  a.probs = probs;
   a.st = st;
   static bool configured = false;
   if (!configured) {

@@ -89,9 +89,11 @@ cudaError_t launch_attention(const Planes& qkv, size_t B, size_t S, size_t d, si
 // cudaErrorNotSupported when the shape is outside what it takes.
 // wscr (optional, attention_tc_scratch_bytes): weights of the sum pass, so
 // that the last pass does not recompute Q K^T.
+// probs (optional): P [B][H][S][S] int16 of every visited key tile; the
+// causal tiles past a query tile's last row are not visited (zero them first).
 cudaError_t launch_attention_tc(const Planes& qkv, const VtPlanes& vt, size_t B, size_t S, size_t d, size_t H,
                                 bool causal, Planes ctx, int16_t* wscr, nsrl_device_status* st,
-                                cudaStream_t stream);
+                                cudaStream_t stream, int16_t* probs = nullptr);
 size_t attention_tc_wstride(size_t S);
 size_t attention_tc_scratch_bytes(size_t B, size_t S, size_t d, size_t H);
 // Shape rule of the tensor-core attention (head_dim 64, seq_len % 16 == 0,
@@ -117,6 +119,16 @@ cudaError_t launch_kv_append(const Planes& qkv, size_t B, size_t d, size_t hd, c
 cudaError_t launch_attention_rows_probs(const int16_t* q, const int16_t* k, const int16_t* v, size_t ld, size_t B,
                                         size_t S, size_t d, size_t H, int16_t* ctx, int16_t* probs,
                                         nsrl_device_status* st, cudaStream_t stream);
+
+// Weight-gradient accumulation on the tensor cores: acc [N][K] (int64) +=
+// G^T X over T rows, from byte planes of the transposes G^T [N][T] and
+// X^T [K][T] (row stride ldt bytes, a multiple of 16).  cudaErrorNotSupported
+// when TMA is unavailable.
+size_t wgrad_planes_ld(size_t T);
+cudaError_t launch_transpose_split(const int16_t* x, size_t T, size_t C, size_t ld, const nsrl_fixed_scale* sc,
+                                   int8_t* th, uint8_t* tl, size_t ldt, cudaStream_t s);
+cudaError_t launch_wgrad_tc(const int8_t* gh, const uint8_t* gl, const int8_t* xh, const uint8_t* xl, size_t ldt,
+                            size_t T, size_t N, size_t K, long long* acc, nsrl_device_status* st, cudaStream_t s);
 
 // Planes -> int16.
 cudaError_t launch_join_planes(Planes in, size_t rows, size_t cols, int16_t* y, size_t ldy, cudaStream_t stream);

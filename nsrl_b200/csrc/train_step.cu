@@ -189,6 +189,27 @@ cudaError_t accumulate(const int16_t* x, size_t ldx, const int16_t* g, size_t ld
   return cudaGetLastError();
 }
 
+// Transposed byte planes of one weight-gradient product (tensor-core path).
+struct WgBufs {
+  int8_t *gh, *xh;
+  uint8_t *gl, *xl;
+  size_t ldt;
+};
+
+// acc [N][K] += sum over rows of g'[r][n] x[r][k]: the tensor-core kernel on
+// transposed planes (g prescaled by rhu(g, shift_n); multipliers are 1 here),
+// or the SIMT kernel where TMA is unavailable.
+cudaError_t accumulate_tc(const WgBufs& b, const int16_t* x, size_t ldx, const int16_t* g, size_t ldg,
+                          const nsrl_fixed_scale* sc, size_t rows, size_t K, size_t N, long long* acc,
+                          nsrl_device_status* st, cudaStream_t s) {
+  if (rows == 0) return cudaSuccess;
+  TS_TRY_RET(launch_transpose_split(g, rows, N, ldg, sc, b.gh, b.gl, b.ldt, s));
+  TS_TRY_RET(launch_transpose_split(x, rows, K, ldx, nullptr, b.xh, b.xl, b.ldt, s));
+  const cudaError_t e = launch_wgrad_tc(b.gh, b.gl, b.xh, b.xl, b.ldt, rows, N, K, acc, st, s);
+  if (e == cudaErrorNotSupported) return accumulate(x, ldx, g, ldg, sc, rows, K, N, acc, st, s);
+  return e;
+}
+
 cudaError_t rms_backward(const int16_t* x, size_t rows, size_t d, const int16_t* w, const int16_t* go, uint64_t eps,
                          int16_t* gi, long long* gw, unsigned long long* sat, nsrl_device_status* st, cudaStream_t s) {
   if (rows == 0) return cudaSuccess;
@@ -266,6 +287,9 @@ struct StepLayout {
   int8_t* headT;
   nsrl_fixed_scale* ident;
   unsigned long long* fwd_res;
+  WgBufs wg;
+  Planes pqkv;  // q|k planes of the tensor-core attention (v goes to vt)
+  VtPlanes vt;
   size_t bytes;
 };
 
@@ -317,6 +341,20 @@ void carve_step(const nsrl_train_model* m, size_t W, bool rms, void* base, StepL
   o.headT = c.take<int8_t>(d * 256);
   o.ident = c.take<nsrl_fixed_scale>(std::max<size_t>(wide, 256));
   o.fwd_res = c.take<unsigned long long>(4);
+  o.wg.ldt = wgrad_planes_ld(T);
+  o.wg.gh = c.take<int8_t>(wide * o.wg.ldt);
+  o.wg.gl = c.take<uint8_t>(wide * o.wg.ldt);
+  o.wg.xh = c.take<int8_t>(wide * o.wg.ldt);
+  o.wg.xl = c.take<uint8_t>(wide * o.wg.ldt);
+  o.pqkv = Planes{nullptr, nullptr, nullptr, 3 * d};
+  o.vt = VtPlanes{nullptr, nullptr, (int)S, (int)H, (int)(d / H), nullptr};
+  if (attention_tc_supported(S, d, H)) {
+    o.pqkv = c.planes(T, 3 * d, false);
+    o.vt.hi = c.take<int8_t>(T * d);
+    o.vt.lo = c.take<uint8_t>(T * d);
+    const size_t ws = attention_tc_scratch_bytes(W, S, d, H);
+    if (ws) o.vt.wscr = c.take<int16_t>(ws / sizeof(int16_t));
+  }
   o.bytes = c.off;
 }
 
@@ -490,6 +528,44 @@ nsrl_status nsrl_attention_backward(const int16_t* q, const int16_t* k, const in
   return NSRL_OK;
 }
 
+size_t nsrl_accumulate_weight_gradient_i16_workspace_size(size_t rows, size_t input_dim, size_t output_dim) {
+  const size_t ldt = wgrad_planes_ld(rows);
+  return 2 * up256(output_dim * ldt) + 2 * up256(input_dim * ldt);
+}
+
+nsrl_status nsrl_accumulate_weight_gradient_i16(const int16_t* x, const int16_t* grad_output, size_t rows,
+                                                size_t input_dim, size_t output_dim, const nsrl_fixed_scale* scales,
+                                                long long* accumulators, unsigned long long* sample_count,
+                                                void* workspace, size_t workspace_bytes, nsrl_device_status* st,
+                                                void* stream) {
+  if (input_dim == 0 || output_dim == 0 || !x || !grad_output || !scales || !accumulators || !sample_count || !st)
+    return fail_shape("weight-gradient accumulation");
+  if (rows > (size_t)INT32_MAX || input_dim > (size_t)INT32_MAX || output_dim > (size_t)INT32_MAX)
+    return fail_shape("dimension too large");
+  if (rows == 0) return NSRL_OK;
+  if (!workspace || workspace_bytes < nsrl_accumulate_weight_gradient_i16_workspace_size(rows, input_dim, output_dim))
+    return fail_shape("workspace too small");
+  cudaStream_t s = (cudaStream_t)stream;
+  Carve c(workspace);
+  WgBufs b;
+  b.ldt = wgrad_planes_ld(rows);
+  b.gh = c.take<int8_t>(output_dim * b.ldt);
+  b.gl = c.take<uint8_t>(output_dim * b.ldt);
+  b.xh = c.take<int8_t>(input_dim * b.ldt);
+  b.xl = c.take<uint8_t>(input_dim * b.ldt);
+  check_mult_one_kernel<<<blocks_for((long long)output_dim), 256, 0, s>>>(scales, (int)output_dim, nullptr, st);
+  TS_TRY(accumulate_tc(b, x, input_dim, grad_output, output_dim, scales, rows, input_dim, output_dim, accumulators,
+                       st, s),
+         "weight-gradient accumulation");
+  CountInc inc{};
+  inc.n = 1;
+  inc.idx[0] = 0;
+  inc.v[0] = rows;
+  count_add_kernel<<<1, 32, 0, s>>>(sample_count, inc);
+  TS_TRY(cudaGetLastError(), "count");
+  return NSRL_OK;
+}
+
 // ------------------------------------------------------------ window step --
 size_t nsrl_train_arena_len(const nsrl_train_model* m) { return m ? arena_len(m) : 0; }
 
@@ -578,9 +654,39 @@ nsrl_status nsrl_train_windows(const nsrl_train_model* m, const uint8_t* context
       g.st = st;
       TS_TRY(launch_gemm(g, s), "qkv");
     }
-    TS_TRY(launch_attention_rows_probs(c.qkv, c.qkv + d, c.qkv + 2 * d, 3 * d, W, S, d, H, c.ctx, c.P, st, s),
-           "attention");
-    TS_TRY(launch_split_planes(c.ctx, T, d, d, pad, s), "split");
+    bool done = false;
+    if (o.vt.hi && tma_supported()) {
+      // tcgen05 attention with the probabilities written out: the Q|K planes and
+      // transposed V come from a second Q|K|V GEMM in the attention operand form.
+      GemmArgs g{};
+      g.a_hi = pad.hi;
+      g.a_lo = pad.lo;
+      g.a_l1 = pad.l1;
+      g.lda = d;
+      g.M = T;
+      g.K = d;
+      g.nseg = 3;
+      for (int i = 0; i < 3; ++i)
+        g.seg[i] = WeightSeg{ly.lin[i].weights, ly.lin[i].bias, ly.lin[i].scales, d};
+      g.epi = Epi::QKV_VT;
+      g.yp = o.pqkv;
+      g.vt = o.vt;
+      g.st = st;
+      TS_TRY(launch_gemm(g, s), "qkv planes");
+      TS_TRY(cudaMemsetAsync(c.P, 0, W * H * S * S * sizeof(int16_t), s), "memset");
+      TS_TRY(cudaMemsetAsync(pad.l1, 0, T * sizeof(unsigned long long), s), "memset");
+      const cudaError_t e = launch_attention_tc(o.pqkv, o.vt, W, S, d, H, true, pad, o.vt.wscr, st, s, c.P);
+      if (e != cudaErrorNotSupported) {
+        TS_TRY(e, "attention");
+        TS_TRY(launch_join_planes(pad, T, d, c.ctx, d, s), "join");
+        done = true;
+      }
+    }
+    if (!done) {
+      TS_TRY(launch_attention_rows_probs(c.qkv, c.qkv + d, c.qkv + 2 * d, 3 * d, W, S, d, H, c.ctx, c.P, st, s),
+             "attention");
+      TS_TRY(launch_split_planes(c.ctx, T, d, d, pad, s), "split");
+    }
     TS_TRY(fwd_gemm(pad, T, d, &ly.lin[3], Epi::RESID, c.ares, d, c.in, o.fwd_res, st, s), "o");
     if (rms)
       TS_TRY(launch_rms_norm(c.ares, T, d, ly.mlp_gamma, 1, c.mn, pad, st, s), "rms");
@@ -662,9 +768,10 @@ nsrl_status nsrl_train_windows(const nsrl_train_model* m, const uint8_t* context
                                                                                  &cnt[5], &cnt[6]);
       TS_TRY(cudaGetLastError(), "nonzero rows");
     }
-    TS_TRY(accumulate(c.gated, F, o.G, d, ly.lin[6].scales, T, F, d, acc + lin_off[6], st, s), "down grad");
-    TS_TRY(accumulate(c.mn, d, o.gup, F, ly.lin[4].scales, T, d, F, acc + lin_off[4], st, s), "up grad");
-    TS_TRY(accumulate(c.mn, d, o.ggate, F, ly.lin[5].scales, T, d, F, acc + lin_off[5], st, s), "gate grad");
+    TS_TRY(accumulate_tc(o.wg, c.gated, F, o.G, d, ly.lin[6].scales, T, F, d, acc + lin_off[6], st, s), "down grad");
+    TS_TRY(accumulate_tc(o.wg, c.mn, d, o.gup, F, ly.lin[4].scales, T, d, F, acc + lin_off[4], st, s), "up grad");
+    TS_TRY(accumulate_tc(o.wg, c.mn, d, o.ggate, F, ly.lin[5].scales, T, d, F, acc + lin_off[5], st, s),
+           "gate grad");
     // attention update, accumulate form (lib.rs:15777-16075)
     TS_TRY(prescale_split(o.gao, T, d, d, ly.lin[3].scales, padn, s), "prescale");
     TS_TRY(bwd_gemm(padn, T, d, c.wt[3], d, o.ident, o.gctx, d, nullptr, nullptr, st, s), "o^T");
@@ -684,8 +791,9 @@ nsrl_status nsrl_train_windows(const nsrl_train_model* m, const uint8_t* context
       TS_TRY(cudaGetLastError(), "fanin");
     }
     for (int i = 0; i < 3; ++i)
-      TS_TRY(accumulate(c.an, d, dqkv[i], d, ly.lin[i].scales, T, d, d, acc + lin_off[i], st, s), "qkv grad");
-    TS_TRY(accumulate(c.ctx, d, o.gao, d, ly.lin[3].scales, T, d, d, acc + lin_off[3], st, s), "o grad");
+      TS_TRY(accumulate_tc(o.wg, c.an, d, dqkv[i], d, ly.lin[i].scales, T, d, d, acc + lin_off[i], st, s),
+             "qkv grad");
+    TS_TRY(accumulate_tc(o.wg, c.ctx, d, o.gao, d, ly.lin[3].scales, T, d, d, acc + lin_off[3], st, s), "o grad");
     for (int i = 0; i < 4; ++i) add_count(1 + 9 * l + i, T);
     const int16_t* gai = o.gni;
     if (rms) {

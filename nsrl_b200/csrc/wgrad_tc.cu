@@ -1,0 +1,332 @@
+// i64 weight-gradient accumulation on the tensor cores (tcgen05, kind::i8):
+//   acc[n][k] += sum_t g'[t][n] * x[t][k]
+// for the rows t of a batch: crates/nsrl-train-core/src/lib.rs:344-384 summed
+// over rows (integer addition is exact in any order; i64 overflow is ruled
+// out by the caller's bound).
+//
+// Operands are byte planes of the transposed tensors, the reduction index t
+// contiguous: G^T [N][T] and X^T [K][T], hi = v >> 8 (s8), lo = v & 255 (u8).
+// With g = 256 gh + gl and x = 256 xh + xl,
+//   g x = 65536 gh xh + 256 (gh xl + gl xh) + gl xl,
+// so per 128-row block four MMAs fill three s32 TMEM accumulators:
+//   hh  += gh . xh        (s8 x s8, |term| <= 16384)
+//   mid += gh . xl + gl . xh  (s8 x u8 and u8 x s8, |two terms| <= 65280)
+//   ll  += gl . xl        (u8 x u8, term <= 65025)
+// A work item covers at most 32768 rows, so every accumulator stays below
+// 2^31 and is exact.  The epilogue forms 65536 hh + 256 mid + ll in i64 and
+// adds it to acc with red.global.add.u64 (two's-complement, exact).
+//
+// Persistent kernel, 18 warps: warp 0 issues TMA (a 3-stage ring of four
+// 16 KB plane tiles), warp 1 owns TMEM and issues the MMAs, warps 2..17 run
+// the epilogue (one TMEM lane quarter and 32 columns each).  Work items are
+// (n tile, k tile, row chunk) triples; several CTAs add into one tile.
+#include <algorithm>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace nsrl {
+namespace {
+
+constexpr int WB = 128;                  // n tile = k tile = row block
+constexpr int WTILE = WB * WB;           // one plane tile, 16 KB
+constexpr int WSTAGE = 4 * WTILE;        // gh, gl, xh, xl
+constexpr int WSTAGES = 3;
+constexpr int WEPI = 16;
+constexpr int WTHREADS = 64 + 32 * WEPI;
+constexpr uint32_t WTMEM = 512;          // hh [0,128), mid [128,256), ll [256,384)
+constexpr size_t WSMEM = (size_t)WSTAGES * WSTAGE + 1024 + 256;
+
+struct WgMaps {
+  CUtensorMap gh, gl, xh, xl;
+};
+
+struct WgParams {
+  int N, K;            // acc is [N][K]
+  int tiles_k;         // K tiles
+  int chunks;          // row chunks per tile
+  int chunk_blocks;    // 128-row blocks per chunk
+  int nblocks;         // 128-row blocks of T
+  int items;
+  long long* acc;
+  nsrl_device_status* st;
+};
+
+__device__ __forceinline__ void red_add_u64(long long* p, long long v) {
+  asm volatile("red.global.add.u64 [%0], %1;" ::"l"(p), "l"((unsigned long long)v) : "memory");
+}
+
+__global__ void __launch_bounds__(WTHREADS, 1) wgrad_tc_kernel(const __grid_constant__ WgMaps maps,
+                                                                const WgParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + WSTAGES * WSTAGE);
+  uint64_t* empty = full + WSTAGES;
+  uint64_t* acc_full = empty + WSTAGES;
+  uint64_t* acc_empty = acc_full + 1;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(acc_empty + 1);
+  uint32_t* skip_flag = tslot + 1;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) *skip_flag = timed_out(p.st) ? 1u : 0u;
+  __syncthreads();
+  if (*skip_flag) return;
+
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < WSTAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, WEPI);
+    fence_barrier_init();
+    prefetch_tmap(&maps.gh);
+    prefetch_tmap(&maps.gl);
+    prefetch_tmap(&maps.xh);
+    prefetch_tmap(&maps.xl);
+  }
+  if (warp == 1) {
+    tmem_alloc(tslot, WTMEM);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < p.items && ok; item += gridDim.x) {
+        const int c = item % p.chunks, tile = item / p.chunks;
+        const int n0 = (tile / p.tiles_k) * WB, k0 = (tile % p.tiles_k) * WB;
+        const int b0 = c * p.chunk_blocks, b1 = min(p.nblocks, b0 + p.chunk_blocks);
+        for (int b = b0; b < b1; ++b, ++it) {
+          const int s = it % WSTAGES;
+          const uint32_t ph = (it / WSTAGES) & 1;
+          if (it >= WSTAGES && !mbar_wait(&empty[s], ph ^ 1, p.st)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], WSTAGE);
+          uint8_t* sa = smem + s * WSTAGE;
+          tma_load_2d(sa, &maps.gh, &full[s], b * WB, n0);
+          tma_load_2d(sa + WTILE, &maps.gl, &full[s], b * WB, n0);
+          tma_load_2d(sa + 2 * WTILE, &maps.xh, &full[s], b * WB, k0);
+          tma_load_2d(sa + 3 * WTILE, &maps.xl, &full[s], b * WB, k0);
+        }
+      }
+      // the last loads in flight land before the CTA exits
+      for (uint32_t j = (it > WSTAGES ? it - WSTAGES : 0); j < it; ++j)
+        mbar_wait(&full[j % WSTAGES], (j / WSTAGES) & 1, p.st);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t id_ss = idesc_i8(WB, WB, 1, 1);
+      const uint32_t id_su = idesc_i8(WB, WB, 1, 0);
+      const uint32_t id_us = idesc_i8(WB, WB, 0, 1);
+      const uint32_t id_uu = idesc_i8(WB, WB, 0, 0);
+      uint32_t it = 0, local = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < p.items && ok; item += gridDim.x, ++local) {
+        const int c = item % p.chunks;
+        const int b0 = c * p.chunk_blocks, b1 = min(p.nblocks, b0 + p.chunk_blocks);
+        if (local > 0 && !mbar_wait(acc_empty, (local - 1) & 1, p.st)) break;
+        tc_fence_after();
+        for (int b = b0; b < b1; ++b, ++it) {
+          const int s = it % WSTAGES;
+          const uint32_t ph = (it / WSTAGES) & 1;
+          if (!mbar_wait(&full[s], ph, p.st)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t base = smem_u32(smem + s * WSTAGE);
+#pragma unroll
+          for (int j = 0; j < WB / 32; ++j) {
+            const uint64_t gh = sdesc_k128(base + 32 * j);
+            const uint64_t gl = sdesc_k128(base + WTILE + 32 * j);
+            const uint64_t xh = sdesc_k128(base + 2 * WTILE + 32 * j);
+            const uint64_t xl = sdesc_k128(base + 3 * WTILE + 32 * j);
+            const uint32_t acc = (b > b0 || j > 0) ? 1u : 0u;
+            umma_i8(tmem, gh, xh, id_ss, acc);
+            umma_i8(tmem + WB, gh, xl, id_su, acc);
+            umma_i8(tmem + WB, gl, xh, id_us, 1u);
+            umma_i8(tmem + 2 * WB, gl, xl, id_uu, acc);
+          }
+          umma_commit(&empty[s]);
+        }
+        umma_commit(acc_full);
+      }
+    }
+  } else {
+    // Epilogue: warp w reads TMEM lanes [32*(w%4), +32) (rows n) and columns
+    // [32*cg, +32) (k) of the three accumulators.
+    const int q = warp & 3;
+    const int cg = (warp - 2) >> 2;
+    uint32_t local = 0;
+    for (int item = blockIdx.x; item < p.items; item += gridDim.x, ++local) {
+      const int tile = item / p.chunks;
+      const int n0 = (tile / p.tiles_k) * WB, k0 = (tile % p.tiles_k) * WB;
+      const int n = n0 + q * 32 + lane;
+      const int kb = k0 + 32 * cg;
+      if (!mbar_wait(acc_full, local & 1, p.st)) break;
+      tc_fence_after();
+      const uint32_t row = tmem + ((uint32_t)(q * 32) << 16) + 32 * cg;
+      // two halves of 16 columns keep the three accumulators in 48 registers
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t hh[16], md[16], ll[16];
+        tmem_ld16(row + 16 * half, hh);
+        tmem_ld16(row + WB + 16 * half, md);
+        tmem_ld16(row + 2 * WB + 16 * half, ll);
+        tmem_wait_ld();
+        if (half == 1) {
+          tc_fence_before();
+          if (lane == 0) mbar_arrive(acc_empty);
+        }
+        if (n < p.N) {
+          long long* dst = p.acc + (long long)n * p.K + kb + 16 * half;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const long long v = (long long)(int)hh[i] * 65536ll + (long long)(int)md[i] * 256ll + (long long)ll[i];
+            if (kb + 16 * half + i < p.K && v != 0) red_add_u64(dst + i, v);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, WTMEM);
+  }
+}
+
+// [T][C] int16 (row stride ld) -> byte planes of the transpose [C][T]
+// (row stride ldt bytes), each value first prescaled by rhu(v, shift_c)
+// when `sc` is given (multiplier 1).  64 x 64 tiles through shared memory.
+__global__ void __launch_bounds__(256) transpose_split_kernel(const int16_t* __restrict__ x, long long T, int C,
+                                                              long long ld, const nsrl_fixed_scale* __restrict__ sc,
+                                                              int8_t* __restrict__ th, uint8_t* __restrict__ tl,
+                                                              long long ldt) {
+  __shared__ int16_t tile[64][65];
+  const long long t0 = (long long)blockIdx.x * 64;
+  const int c0 = blockIdx.y * 64;
+  const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;  // 64 x 4
+  for (int r = ty; r < 64; r += 4) {
+    const long long t = t0 + r;
+    const int c = c0 + tx;
+    int v = 0;
+    if (t < T && c < C) {
+      v = x[t * ld + c];
+      if (sc) {
+        const int s = sc[c].right_shift;
+        if (s) v = (int)rhu64(v, (uint32_t)s);
+      }
+    }
+    tile[r][tx] = (int16_t)v;
+  }
+  __syncthreads();
+  for (int r = ty; r < 64; r += 4) {
+    const int c = c0 + r;
+    const long long t = t0 + tx;
+    if (c < C && t < T) {
+      const int v = tile[tx][r];
+      th[(long long)c * ldt + t] = (int8_t)(v >> 8);
+      tl[(long long)c * ldt + t] = (uint8_t)(v & 255);
+    }
+  }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn wg_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+// uint8 [rows][inner] (row stride ld bytes), box 128 x 128 bytes, 128-byte swizzle.
+bool wg_map(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t rows, uint64_t ld) {
+  EncodeTiledFn fn = wg_encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {ld};
+  cuuint32_t box[2] = {(cuuint32_t)WB, (cuuint32_t)WB};
+  cuuint32_t es[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+size_t wgrad_planes_ld(size_t T) { return (T + 127) & ~size_t(127); }
+
+cudaError_t launch_transpose_split(const int16_t* x, size_t T, size_t C, size_t ld, const nsrl_fixed_scale* sc,
+                                   int8_t* th, uint8_t* tl, size_t ldt, cudaStream_t s) {
+  if (T == 0 || C == 0) return cudaSuccess;
+  dim3 grid((unsigned)((T + 63) / 64), (unsigned)((C + 63) / 64));
+  ProfScope prof("transpose_split", s, 0.0, 4.0 * (double)T * (double)C);
+  transpose_split_kernel<<<grid, 256, 0, s>>>(x, (long long)T, (int)C, (long long)ld, sc, th, tl, (long long)ldt);
+  return cudaGetLastError();
+}
+
+// acc [N][K] += G^T X from the transposed planes (row stride ldt, T rows).
+// Returns cudaErrorNotSupported when TMA is unavailable.
+cudaError_t launch_wgrad_tc(const int8_t* gh, const uint8_t* gl, const int8_t* xh, const uint8_t* xl, size_t ldt,
+                            size_t T, size_t N, size_t K, long long* acc, nsrl_device_status* st,
+                            cudaStream_t s) {
+  if (T == 0 || N == 0 || K == 0) return cudaSuccess;
+  if (ldt % 16 != 0 || T > (size_t)INT32_MAX || N > (size_t)INT32_MAX || K > (size_t)INT32_MAX)
+    return cudaErrorInvalidValue;
+  WgMaps maps;
+  if (!wg_map(&maps.gh, gh, T, N, ldt) || !wg_map(&maps.gl, gl, T, N, ldt) || !wg_map(&maps.xh, xh, T, K, ldt) ||
+      !wg_map(&maps.xl, xl, T, K, ldt))
+    return cudaErrorNotSupported;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(wgrad_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)WSMEM);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  WgParams p{};
+  p.N = (int)N;
+  p.K = (int)K;
+  p.tiles_k = (int)((K + WB - 1) / WB);
+  const int tiles = (int)((N + WB - 1) / WB) * p.tiles_k;
+  p.nblocks = (int)((T + WB - 1) / WB);
+  // rows per item: at most 32768 (exact s32 accumulators), and enough items
+  // for two waves of the 148 SMs where the row count allows
+  const int max_blocks = 32768 / WB;
+  int chunks = std::max((p.nblocks + max_blocks - 1) / max_blocks, (2 * 148 + tiles - 1) / tiles);
+  chunks = std::min(chunks, p.nblocks);
+  p.chunk_blocks = (p.nblocks + chunks - 1) / chunks;
+  p.chunks = (p.nblocks + p.chunk_blocks - 1) / p.chunk_blocks;
+  p.items = tiles * p.chunks;
+  p.acc = acc;
+  p.st = st;
+  int sms = 0, dev = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int grid = std::min(p.items, sms > 0 ? sms : 148);
+  ProfScope prof("accumulate_weight_grad_tc", s, 2.0 * (double)T * (double)N * (double)K,
+                 2.0 * (double)T * (double)(N + K) + 16.0 * (double)N * (double)K * p.chunks);
+  wgrad_tc_kernel<<<grid, WTHREADS, WSMEM, s>>>(maps, p);
+  return cudaGetLastError();
+}
+
+}  // namespace nsrl

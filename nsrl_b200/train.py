@@ -589,3 +589,26 @@ def mini_transformer_train_step(model: TrainModel, state: TrainState, contexts: 
            "residual_saturation_count": s[3]}
     out.update(upd)
     return out
+
+
+def accumulate_weight_gradient_i16(x: torch.Tensor, grad_output: torch.Tensor, scales: torch.Tensor,
+                                   accumulators: torch.Tensor, sample_count: torch.Tensor) -> bool:
+    """acc[n][k] += rhu(g[r][n], shift_n) * x[r][k] over the rows, on the tensor cores
+    (nsrl-train-core/src/lib.rs:344-384 with the prescale of linear.rs:573-592);
+    False when the call is rejected (a multiplier other than 1)."""
+    L = _lib_bwd()
+    if not getattr(L, "_acc16_bound", False):
+        vp, sz = C.c_void_p, C.c_size_t
+        L.nsrl_accumulate_weight_gradient_i16_workspace_size.restype = sz
+        L.nsrl_accumulate_weight_gradient_i16_workspace_size.argtypes = [sz, sz, sz]
+        L.nsrl_accumulate_weight_gradient_i16.argtypes = [vp, vp, sz, sz, sz, vp, vp, vp, vp, sz, vp, vp]
+        L._acc16_bound = True
+    x, g = core._i16(x), core._i16(grad_output)
+    N, K = accumulators.shape
+    rows = x.numel() // K
+    ws = core.workspace(L.nsrl_accumulate_weight_gradient_i16_workspace_size(rows, K, N))
+    st = core.Status()
+    r = L.nsrl_accumulate_weight_gradient_i16(core._ptr(x), core._ptr(g), rows, K, N, core._ptr(scales),
+                                              core._ptr(accumulators), core._ptr(sample_count), core._ptr(ws),
+                                              ws.numel(), core._ptr(st.buf), core._stream())
+    return _run_status(r, st)

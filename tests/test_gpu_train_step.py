@@ -203,3 +203,39 @@ def test_sharded_windows_sum_to_the_whole_batch():
     assert not ovf
     assert torch.equal(merged, whole[0])
     assert torch.equal(parts[0][1] + parts[1][1], whole[1])
+
+
+@pytest.mark.parametrize("rows,K,N,shift", [(300, 64, 48, 0), (1000, 256, 1024, 2), (4133, 200, 72, 0)])
+def test_weight_gradient_tensor_cores(rows, K, N, shift):
+    """The tcgen05 weight-gradient product against an exact int64 matmul of the prescaled grads."""
+    core, train = _core()
+    rng = np.random.default_rng(rows + K)
+    x = rng.integers(-32768, 32768, (rows, K)).astype(np.int16)
+    g = rng.integers(-32768, 32768, (rows, N)).astype(np.int16)
+    acc0 = rng.integers(-2**40, 2**40, (N, K)).astype(np.int64)
+    gp = g.astype(np.int64)
+    if shift:
+        gp = (gp + (1 << (shift - 1))) >> shift  # rhu with multiplier 1
+    ref = acc0 + gp.T @ x.astype(np.int64)
+    acc = torch.from_numpy(acc0.copy()).cuda()
+    cnt = torch.zeros(1, dtype=torch.int64, device="cuda")
+    assert train.accumulate_weight_gradient_i16(_dev(x), _dev(g), core.make_scales(1, shift, N), acc, cnt)
+    assert np.array_equal(acc.cpu().numpy(), ref)
+    assert int(cnt.item()) == rows
+
+
+def test_weight_gradient_tensor_cores_extreme_values():
+    """Byte-plane extremes over a 32768-row work item (the s32 limit of the
+    accumulators): 304 output tiles make one item per tile, so each item sums
+    all 32768 rows.  -32513 gives |gh xl + gl xh| = 65280 and -1 x 255 gives
+    gl xl = 65025 per row, the largest mid and low sums."""
+    core, train = _core()
+    rows, K, N = 32768, 2048, 2432
+    for gv, xv in ((-32768, -32768), (-32513, -32513), (-1, 255), (32767, 32767), (32767, -32768)):
+        x = torch.full((rows, K), xv, dtype=torch.int16, device="cuda")
+        g = torch.full((rows, N), gv, dtype=torch.int16, device="cuda")
+        acc = torch.zeros((N, K), dtype=torch.int64, device="cuda")
+        cnt = torch.zeros(1, dtype=torch.int64, device="cuda")
+        assert train.accumulate_weight_gradient_i16(x, g, core.make_scales(1, 0, N), acc, cnt)
+        assert bool((acc == rows * gv * xv).all()), (gv, xv)
+        del x, g, acc
