@@ -184,7 +184,7 @@ def kernel_table(core_lib):
 
 
 TENSOR_KERNELS = ("linear_tc", "attention_prefill", "attention_tc", "accumulate_weight_grad",
-                  "attention_grad_products", "attention_dlogit", "linear_simt")
+                  "attention_grad_products", "attention_dlogit", "attention_bwd", "linear_simt")
 
 # Config 5 (decode) and config 2 (linear sweep), measured after the headline.
 DEC_LAYERS, DEC_D, DEC_H, DEC_F, DEC_B, DEC_PREFIX = 4, 512, 8, 2048, 256, 8192

@@ -1,0 +1,449 @@
+// Softmax-attention backward on the int8 tensor cores (mma.sync m16n8k32),
+// crates/nsrl-train/src/lib.rs:16623-16900, per (sequence, head):
+//   dP[t][j] = sat(rhu(dC[t] . V[j], 15))                          j <= t
+//   dL[t][j] = sat(rhu(P[t][j] (dP[t][j] - rhu(sum_j dP P, 15)) 22713, 30))
+//   dQ[t]    = sat(rhu(sum_{j<=t} dL[t][j] K[j], log4 hd))
+//   dK[j]    = sat(rhu(sum_{t>=j} dL[t][j] Q[t], log4 hd))
+//   dV[j]    = sat(rhu(sum_t P[t][j] dC[t], 15))
+// Every product is i16 x i16 = (256 ah + al)(256 bh + bl): four int8 MMAs
+// into three s32 sums (hh, mid = ah bl + al bh, ll), recombined in i64.  Per
+// product |mid| <= 65280 and ll <= 65025, so the sums are exact for up to
+// 32768 terms (seq_len <= 16384, head_dim <= 64).
+//
+// attn_bwd_q_kernel: one CTA of 4 warps per 64 query rows.  Pass 1 forms dP
+//   tile by tile and the row sums sum_j dP P; pass 2 forms dP again, then dL
+//   (written to global for the key side) and dQ += dL K, dL entering the MMA
+//   as A fragments straight from the dP accumulator layout (K^T is staged in
+//   the matching key order).
+// attn_bwd_kv_kernel: one CTA per 64 keys; dK (A = dL^T) or dV (A = P^T)
+//   over the query tiles at or after the keys, operands staged transposed as
+//   byte planes in shared memory.
+#include "common.cuh"
+#include "internal.h"
+
+namespace nsrl {
+namespace {
+
+#define NSRL_BWD_MMA(NAME, TA, TB)                                                                          \
+  __device__ __forceinline__ void NAME(int (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {     \
+    asm volatile("mma.sync.aligned.m16n8k32.row.col.s32." TA "." TB                                        \
+                 ".s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"                               \
+                 : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])                                           \
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));                           \
+  }
+NSRL_BWD_MMA(bmma_ss, "s8", "s8")
+NSRL_BWD_MMA(bmma_su, "s8", "u8")
+NSRL_BWD_MMA(bmma_us, "u8", "s8")
+NSRL_BWD_MMA(bmma_uu, "u8", "u8")
+
+__device__ __forceinline__ uint32_t lds32b(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
+
+// Position of key j (0..31) in the MMA k order that matches the C-fragment
+// layout of an S tile (see the forward prefill kernel).
+__device__ __forceinline__ int bkey_slot(int j) {
+  return 16 * (j >> 4) + 4 * ((j & 7) >> 1) + 2 * ((j & 15) >> 3) + (j & 1);
+}
+
+// Four int16 values -> their hi bytes and lo bytes, packed.
+__device__ __forceinline__ void split4(const int16_t* v, uint32_t& hi, uint32_t& lo) {
+  uint32_t h = 0, l = 0;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    h |= (uint32_t)(((int)v[e] >> 8) & 255) << (8 * e);
+    l |= (uint32_t)((int)v[e] & 255) << (8 * e);
+  }
+  hi = h;
+  lo = l;
+}
+
+constexpr int BQ = 64;  // query rows per CTA (4 warps x 16)
+constexpr int BK = 32;  // keys per tile
+
+struct QArgs {
+  const int16_t* dC;
+  long long ldc;
+  const int16_t* V;
+  const int16_t* K;
+  long long ldkv;
+  const int16_t* P;
+  int S, H, shift;
+  int16_t* dL;
+  int16_t* dQ;
+  long long ldo;
+  nsrl_device_status* st;
+};
+
+template <int HD>
+struct QSmem {
+  static constexpr int KSTR = HD == 16 ? 48 : HD + 16;
+  static constexpr int VSTR = 48;
+  uint8_t v_hi[BK * KSTR];
+  uint8_t v_lo[BK * KSTR];
+  uint8_t kt_hi[HD * VSTR];
+  uint8_t kt_lo[HD * VSTR];
+};
+
+template <int HD>
+__global__ void __launch_bounds__(128) attn_bwd_q_kernel(const QArgs a) {
+  constexpr int KC = HD >= 32 ? HD / 32 : 1;
+  constexpr int NT = HD / 8;
+  __shared__ __align__(16) QSmem<HD> sm;
+  constexpr int KSTR = QSmem<HD>::KSTR, VSTR = QSmem<HD>::VSTR;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int q0 = blockIdx.x * BQ, h = blockIdx.y, b = blockIdx.z;
+  const int S = a.S;
+  const long long row0 = (long long)b * S;
+  const int qw = q0 + warp * 16;
+  const int r0 = qw + g, r1 = r0 + 8;
+  const int16_t* Pbh = a.P + ((long long)b * a.H + h) * S * (long long)S;
+  int16_t* dLbh = a.dL + ((long long)b * a.H + h) * S * (long long)S;
+
+  // A fragments of dC rows r0 / r1 (k = dims)
+  uint32_t ca_hi[KC][4], ca_lo[KC][4];
+#pragma unroll
+  for (int c = 0; c < KC; ++c)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = (i & 1) ? r1 : r0;
+      const int k = 32 * c + 4 * t + ((i & 2) ? 16 : 0);
+      uint32_t hv = 0, lv = 0;
+      if (r < S && k < HD) {
+        const uint2 u = *reinterpret_cast<const uint2*>(a.dC + (row0 + r) * a.ldc + (long long)h * HD + k);
+        split4(reinterpret_cast<const int16_t*>(&u), hv, lv);
+      }
+      ca_hi[c][i] = hv;
+      ca_lo[c][i] = lv;
+    }
+
+  const int kend = min(S, q0 + BQ);  // keys visited by this CTA (causal)
+  const int ntiles = (kend + BK - 1) / BK;
+  const int wlast = min(qw + 15, S - 1);
+  long long wsum[2] = {0, 0}, wq[2] = {0, 0};
+  int dq_hh[NT][4], dq_mid[NT][4], dq_ll[NT][4];
+#pragma unroll
+  for (int n = 0; n < NT; ++n)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) dq_hh[n][i] = dq_mid[n][i] = dq_ll[n][i] = 0;
+  bool neg = false;
+
+  for (int pass = 0; pass < 2; ++pass) {
+    for (int kt = 0; kt < ntiles; ++kt) {
+      const int kb = kt * BK;
+      __syncthreads();
+      // stage V rows [key][dim] as planes; in pass 2 also K^T [dim][key slot]
+      for (int i = tid; i < BK * (HD / 4); i += 128) {
+        const int j = i / (HD / 4), c4 = i % (HD / 4);
+        const int key = kb + j;
+        uint32_t vh = 0, vl = 0;
+        if (key < kend) {
+          const uint2 u = *reinterpret_cast<const uint2*>(a.V + (row0 + key) * a.ldkv + (long long)h * HD + 4 * c4);
+          split4(reinterpret_cast<const int16_t*>(&u), vh, vl);
+        }
+        *reinterpret_cast<uint32_t*>(&sm.v_hi[j * KSTR + 4 * c4]) = vh;
+        *reinterpret_cast<uint32_t*>(&sm.v_lo[j * KSTR + 4 * c4]) = vl;
+        if (pass == 1) {
+          uint32_t kh = 0, kl = 0;
+          if (key < kend) {
+            const uint2 u =
+                *reinterpret_cast<const uint2*>(a.K + (row0 + key) * a.ldkv + (long long)h * HD + 4 * c4);
+            split4(reinterpret_cast<const int16_t*>(&u), kh, kl);
+          }
+          const int slot = bkey_slot(j);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            sm.kt_hi[(4 * c4 + e) * VSTR + slot] = (uint8_t)(kh >> (8 * e));
+            sm.kt_lo[(4 * c4 + e) * VSTR + slot] = (uint8_t)(kl >> (8 * e));
+          }
+        }
+      }
+      if (HD == 16) {  // zero the unused k half of the V rows (dims 16..31)
+        for (int i = tid; i < BK * 4; i += 128) {
+          const int j = i / 4, c4 = i % 4;
+          *reinterpret_cast<uint32_t*>(&sm.v_hi[j * KSTR + 16 + 4 * c4]) = 0u;
+          *reinterpret_cast<uint32_t*>(&sm.v_lo[j * KSTR + 16 + 4 * c4]) = 0u;
+        }
+      }
+      __syncthreads();
+      if (kb > wlast || qw >= S) continue;  // fully masked for this warp
+
+      // dP raw sums for 16 rows x 32 keys
+      int s_hh[4][4], s_mid[4][4], s_ll[4][4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) s_hh[j][i] = s_mid[j][i] = s_ll[j][i] = 0;
+        const uint8_t* vh = &sm.v_hi[(8 * j + g) * KSTR + 4 * t];
+        const uint8_t* vl = &sm.v_lo[(8 * j + g) * KSTR + 4 * t];
+#pragma unroll
+        for (int c = 0; c < KC; ++c) {
+          const uint32_t bh0 = lds32b(vh + 32 * c), bl0 = lds32b(vl + 32 * c);
+          const uint32_t bh1 = lds32b(vh + 32 * c + 16), bl1 = lds32b(vl + 32 * c + 16);
+          bmma_ss(s_hh[j], ca_hi[c], bh0, bh1);
+          bmma_su(s_mid[j], ca_hi[c], bl0, bl1);
+          bmma_us(s_mid[j], ca_lo[c], bh0, bh1);
+          bmma_uu(s_ll[j], ca_lo[c], bl0, bl1);
+        }
+      }
+      int dl[2][8];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {  // row r0 (hf 0) or r1 (hf 1): C elements 2 hf, 2 hf + 1
+          const int r = hf ? r1 : r0;
+          const int key = kb + 8 * j + 2 * t;
+          int pv[2] = {0, 0};
+          const bool rl = r < S;
+          if (rl && key < S) {  // the two probabilities of this pair of keys
+            const uint32_t u = *reinterpret_cast<const uint32_t*>(Pbh + (long long)r * S + key);
+            pv[0] = (int)(int16_t)(u & 0xFFFF);
+            pv[1] = (int)(int16_t)(u >> 16);
+          }
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int i = 2 * hf + e;
+            const int kk = key + e;
+            const bool live = rl && kk <= r && kk < S;
+            int out = 0;
+            if (live) {
+              const long long raw =
+                  (long long)s_hh[j][i] * 65536 + (long long)s_mid[j][i] * 256 + (long long)s_ll[j][i];
+              const long long dp = sat_i16(rhu64(raw, 15));
+              neg |= pv[e] < 0;
+              if (pass == 0) {
+                wsum[hf] += dp * (long long)pv[e];
+              } else {
+                out = sat_i16(rhu64((long long)pv[e] * (dp - wq[hf]) * 22713ll, 30));
+              }
+            }
+            dl[hf][2 * j + e] = out;
+          }
+        }
+      }
+      if (pass == 0) continue;
+      // dL to global (the key side reads it), then the dQ product
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          const int r = hf ? r1 : r0;
+          const int key = kb + 8 * j + 2 * t;
+          if (r < S && key < S)
+            *reinterpret_cast<uint32_t*>(dLbh + (long long)r * S + key) =
+                (uint32_t)(dl[hf][2 * j] & 0xFFFF) | ((uint32_t)dl[hf][2 * j + 1] << 16);
+        }
+      uint32_t ah[4], al[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int hf = i & 1;
+        const int base = (i & 2) ? 4 : 0;
+        uint32_t hv = 0, lv = 0;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int v = dl[hf][base + e];
+          hv |= (uint32_t)((v >> 8) & 255) << (8 * e);
+          lv |= (uint32_t)(v & 255) << (8 * e);
+        }
+        ah[i] = hv;
+        al[i] = lv;
+      }
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        const uint8_t* kh = &sm.kt_hi[(8 * n + g) * VSTR + 4 * t];
+        const uint8_t* kl = &sm.kt_lo[(8 * n + g) * VSTR + 4 * t];
+        const uint32_t bh0 = lds32b(kh), bh1 = lds32b(kh + 16), bl0 = lds32b(kl), bl1 = lds32b(kl + 16);
+        bmma_ss(dq_hh[n], ah, bh0, bh1);
+        bmma_su(dq_mid[n], ah, bl0, bl1);
+        bmma_us(dq_mid[n], al, bh0, bh1);
+        bmma_uu(dq_ll[n], al, bl0, bl1);
+      }
+    }
+    if (pass == 0) {
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+#pragma unroll
+        for (int o = 1; o <= 2; o <<= 1) wsum[hf] += __shfl_xor_sync(0xffffffffu, wsum[hf], o);
+        wq[hf] = rhu64(wsum[hf], 15);
+      }
+    }
+  }
+  if (neg) nsrl_flag(a.st, NSRL_FLAG_LINEAR_OVERFLOW);  // a negative probability: the reference rejects
+#pragma unroll
+  for (int n = 0; n < NT; ++n)
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      const int r = hf ? r1 : r0;
+      if (r >= S) continue;
+      int v[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int i = 2 * hf + e;
+        const long long tot = (long long)dq_hh[n][i] * 65536 + (long long)dq_mid[n][i] * 256 + (long long)dq_ll[n][i];
+        v[e] = sat_i16(rhu64(tot, (uint32_t)a.shift));
+      }
+      *reinterpret_cast<uint32_t*>(a.dQ + (row0 + r) * a.ldo + (long long)h * HD + 8 * n + 2 * t) =
+          (uint32_t)(v[0] & 0xFFFF) | ((uint32_t)v[1] << 16);
+    }
+}
+
+struct KVArgs {
+  const int16_t* M;  // dL or P, [B][H][S][S]
+  const int16_t* X;  // Q or dC rows
+  long long ldx;
+  int S, H, shift;
+  int16_t* out;
+  long long ldo;
+};
+
+template <int HD>
+struct KVSmem {
+  static constexpr int ASTR = 48;  // 32 queries + padding, bytes
+  uint8_t at_hi[BQ * ASTR];        // [key][query]
+  uint8_t at_lo[BQ * ASTR];
+  uint8_t xt_hi[HD * ASTR];        // [dim][query]
+  uint8_t xt_lo[HD * ASTR];
+};
+
+// out[j] = sat(rhu(sum_{t >= j} M[t][j] X[t], shift)) for the 64 keys j of this CTA.
+template <int HD>
+__global__ void __launch_bounds__(128) attn_bwd_kv_kernel(const KVArgs a) {
+  constexpr int NT = HD / 8;
+  __shared__ __align__(16) KVSmem<HD> sm;
+  constexpr int ASTR = KVSmem<HD>::ASTR;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int k0 = blockIdx.x * BQ, h = blockIdx.y, b = blockIdx.z;
+  const int S = a.S;
+  const long long row0 = (long long)b * S;
+  const int16_t* Mbh = a.M + ((long long)b * a.H + h) * S * (long long)S;
+  const int kw = k0 + warp * 16;  // this warp's keys kw + g, kw + g + 8
+  int acc_hh[NT][4], acc_mid[NT][4], acc_ll[NT][4];
+#pragma unroll
+  for (int n = 0; n < NT; ++n)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc_hh[n][i] = acc_mid[n][i] = acc_ll[n][i] = 0;
+
+  for (int tq = k0; tq < S; tq += BK) {
+    __syncthreads();
+    // M^T tile: M[tq + q][k0 + kc] -> at[kc][q]
+    for (int i = tid; i < BK * (BQ / 4); i += 128) {
+      const int q = i / (BQ / 4), c4 = i % (BQ / 4);
+      const int tr = tq + q, kc = 4 * c4;
+      int16_t v[4] = {0, 0, 0, 0};
+      if (tr < S) {
+        if (k0 + kc + 3 < S) {
+          const uint2 u = *reinterpret_cast<const uint2*>(Mbh + (long long)tr * S + k0 + kc);
+          const int16_t* e = reinterpret_cast<const int16_t*>(&u);
+#pragma unroll
+          for (int z = 0; z < 4; ++z) v[z] = e[z];
+        } else {
+#pragma unroll
+          for (int z = 0; z < 4; ++z)
+            if (k0 + kc + z < S) v[z] = Mbh[(long long)tr * S + k0 + kc + z];
+        }
+      }
+#pragma unroll
+      for (int z = 0; z < 4; ++z) {
+        sm.at_hi[(kc + z) * ASTR + q] = (uint8_t)(((int)v[z] >> 8) & 255);
+        sm.at_lo[(kc + z) * ASTR + q] = (uint8_t)((int)v[z] & 255);
+      }
+    }
+    // X^T tile: X[tq + q][h HD + dim] -> xt[dim][q]
+    for (int i = tid; i < BK * (HD / 4); i += 128) {
+      const int q = i / (HD / 4), c4 = i % (HD / 4);
+      const int tr = tq + q;
+      uint32_t xh = 0, xl = 0;
+      if (tr < S) {
+        const uint2 u = *reinterpret_cast<const uint2*>(a.X + (row0 + tr) * a.ldx + (long long)h * HD + 4 * c4);
+        split4(reinterpret_cast<const int16_t*>(&u), xh, xl);
+      }
+#pragma unroll
+      for (int z = 0; z < 4; ++z) {
+        sm.xt_hi[(4 * c4 + z) * ASTR + q] = (uint8_t)(xh >> (8 * z));
+        sm.xt_lo[(4 * c4 + z) * ASTR + q] = (uint8_t)(xl >> (8 * z));
+      }
+    }
+    __syncthreads();
+    if (kw >= S || tq + BK - 1 < kw) continue;  // keys past the sequence, or queries all before them
+    uint32_t ah[4], al[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int kr = warp * 16 + g + ((i & 1) ? 8 : 0);
+      const int qc = 4 * t + ((i & 2) ? 16 : 0);
+      ah[i] = lds32b(&sm.at_hi[kr * ASTR + qc]);
+      al[i] = lds32b(&sm.at_lo[kr * ASTR + qc]);
+    }
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      const uint8_t* xh = &sm.xt_hi[(8 * n + g) * ASTR + 4 * t];
+      const uint8_t* xl = &sm.xt_lo[(8 * n + g) * ASTR + 4 * t];
+      const uint32_t bh0 = lds32b(xh), bh1 = lds32b(xh + 16), bl0 = lds32b(xl), bl1 = lds32b(xl + 16);
+      bmma_ss(acc_hh[n], ah, bh0, bh1);
+      bmma_su(acc_mid[n], ah, bl0, bl1);
+      bmma_us(acc_mid[n], al, bh0, bh1);
+      bmma_uu(acc_ll[n], al, bl0, bl1);
+    }
+  }
+#pragma unroll
+  for (int n = 0; n < NT; ++n)
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      const int kr = kw + g + (hf ? 8 : 0);
+      if (kr >= S) continue;
+      int v[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int i = 2 * hf + e;
+        const long long tot =
+            (long long)acc_hh[n][i] * 65536 + (long long)acc_mid[n][i] * 256 + (long long)acc_ll[n][i];
+        v[e] = sat_i16(rhu64(tot, (uint32_t)a.shift));
+      }
+      *reinterpret_cast<uint32_t*>(a.out + (row0 + kr) * a.ldo + (long long)h * HD + 8 * n + 2 * t) =
+          (uint32_t)(v[0] & 0xFFFF) | ((uint32_t)v[1] << 16);
+    }
+}
+
+}  // namespace
+
+// dQ, dK, dV (and dL into `dl`, zeroed here) of causal attention on int16
+// operands: q, k, v rows of stride ld, P [B][H][S][S], dC rows of stride ldc;
+// outputs [B*S][d].  head_dim 16 or 64, S a multiple of 4 (else cudaErrorNotSupported).
+cudaError_t launch_attention_backward_tc(const int16_t* q, const int16_t* k, const int16_t* v, size_t ld,
+                                         const int16_t* P, const int16_t* dC, size_t ldc, size_t B, size_t S, size_t d,
+                                         size_t H, int16_t* dl, int16_t* dq, int16_t* dk, int16_t* dv,
+                                         nsrl_device_status* st, cudaStream_t s) {
+  const size_t hd = d / H;
+  // 8-byte loads of P / dL rows, dC, q, k, v need S, ld, ldc multiples of 4
+  if ((hd != 16 && hd != 64) || S % 4 != 0 || ld % 4 != 0 || ldc % 4 != 0 || d % 4 != 0 || S > 16384)
+    return cudaErrorNotSupported;
+  const int shift = __builtin_ctzll(hd) / 2;
+  cudaError_t e = cudaMemsetAsync(dl, 0, B * H * S * S * sizeof(int16_t), s);
+  if (e != cudaSuccess) return e;
+  const double pairs = (double)B * (double)H * (double)S * (double)(S + 1) / 2.0;
+  dim3 grid((unsigned)((S + BQ - 1) / BQ), (unsigned)H, (unsigned)B);
+  QArgs qa{dC, (long long)ldc, v, k, (long long)ld, P, (int)S, (int)H, shift, dl, dq, (long long)d, st};
+  {
+    ProfScope prof("attention_bwd_q", s, 3.0 * 2.0 * (double)hd * pairs,
+                   2.0 * 2.0 * (double)B * H * S * S + 8.0 * (double)B * S * d);
+    if (hd == 64)
+      attn_bwd_q_kernel<64><<<grid, 128, 0, s>>>(qa);
+    else
+      attn_bwd_q_kernel<16><<<grid, 128, 0, s>>>(qa);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  KVArgs ka{dl, q, (long long)ld, (int)S, (int)H, shift, dk, (long long)d};
+  KVArgs va{P, dC, (long long)ldc, (int)S, (int)H, 15, dv, (long long)d};
+  ProfScope prof("attention_bwd_kv", s, 2.0 * 2.0 * (double)hd * pairs,
+                 2.0 * 2.0 * (double)B * H * S * S + 8.0 * (double)B * S * d);
+  if (hd == 64) {
+    attn_bwd_kv_kernel<64><<<grid, 128, 0, s>>>(ka);
+    attn_bwd_kv_kernel<64><<<grid, 128, 0, s>>>(va);
+  } else {
+    attn_bwd_kv_kernel<16><<<grid, 128, 0, s>>>(ka);
+    attn_bwd_kv_kernel<16><<<grid, 128, 0, s>>>(va);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace nsrl

@@ -199,12 +199,14 @@ struct WgBufs {
 // acc [N][K] += sum over rows of g'[r][n] x[r][k]: the tensor-core kernel on
 // transposed planes (g prescaled by rhu(g, shift_n); multipliers are 1 here),
 // or the SIMT kernel where TMA is unavailable.
+// x_ready: the X planes already hold this x (the q, k and v gradients share one
+// input, and so do up and gate).
 cudaError_t accumulate_tc(const WgBufs& b, const int16_t* x, size_t ldx, const int16_t* g, size_t ldg,
                           const nsrl_fixed_scale* sc, size_t rows, size_t K, size_t N, long long* acc,
-                          nsrl_device_status* st, cudaStream_t s) {
+                          nsrl_device_status* st, cudaStream_t s, bool x_ready = false) {
   if (rows == 0) return cudaSuccess;
   TS_TRY_RET(launch_transpose_split(g, rows, N, ldg, sc, b.gh, b.gl, b.ldt, s));
-  TS_TRY_RET(launch_transpose_split(x, rows, K, ldx, nullptr, b.xh, b.xl, b.ldt, s));
+  if (!x_ready) TS_TRY_RET(launch_transpose_split(x, rows, K, ldx, nullptr, b.xh, b.xl, b.ldt, s));
   const cudaError_t e = launch_wgrad_tc(b.gh, b.gl, b.xh, b.xl, b.ldt, rows, N, K, acc, st, s);
   if (e == cudaErrorNotSupported) return accumulate(x, ldx, g, ldg, sc, rows, K, N, acc, st, s);
   return e;
@@ -235,6 +237,8 @@ cudaError_t add_sat(const int16_t* a, const int16_t* b, size_t n, int16_t* out, 
 cudaError_t attn_backward(const int16_t* q, const int16_t* k, const int16_t* v, size_t ld, const int16_t* P,
                           const int16_t* dC, size_t ldc, size_t B, size_t S, size_t d, size_t H, int16_t* dL,
                           int16_t* dq, int16_t* dk, int16_t* dv, nsrl_device_status* st, cudaStream_t s) {
+  const cudaError_t tce = launch_attention_backward_tc(q, k, v, ld, P, dC, ldc, B, S, d, H, dL, dq, dk, dv, st, s);
+  if (tce != cudaErrorNotSupported) return tce;
   const size_t hd = d / H;
   const int shift = __builtin_ctzll(hd) / 2;
   const size_t smem = S * sizeof(int32_t);
@@ -770,7 +774,7 @@ nsrl_status nsrl_train_windows(const nsrl_train_model* m, const uint8_t* context
     }
     TS_TRY(accumulate_tc(o.wg, c.gated, F, o.G, d, ly.lin[6].scales, T, F, d, acc + lin_off[6], st, s), "down grad");
     TS_TRY(accumulate_tc(o.wg, c.mn, d, o.gup, F, ly.lin[4].scales, T, d, F, acc + lin_off[4], st, s), "up grad");
-    TS_TRY(accumulate_tc(o.wg, c.mn, d, o.ggate, F, ly.lin[5].scales, T, d, F, acc + lin_off[5], st, s),
+    TS_TRY(accumulate_tc(o.wg, c.mn, d, o.ggate, F, ly.lin[5].scales, T, d, F, acc + lin_off[5], st, s, true),
            "gate grad");
     // attention update, accumulate form (lib.rs:15777-16075)
     TS_TRY(prescale_split(o.gao, T, d, d, ly.lin[3].scales, padn, s), "prescale");
@@ -791,7 +795,7 @@ nsrl_status nsrl_train_windows(const nsrl_train_model* m, const uint8_t* context
       TS_TRY(cudaGetLastError(), "fanin");
     }
     for (int i = 0; i < 3; ++i)
-      TS_TRY(accumulate_tc(o.wg, c.an, d, dqkv[i], d, ly.lin[i].scales, T, d, d, acc + lin_off[i], st, s),
+      TS_TRY(accumulate_tc(o.wg, c.an, d, dqkv[i], d, ly.lin[i].scales, T, d, d, acc + lin_off[i], st, s, i > 0),
              "qkv grad");
     TS_TRY(accumulate_tc(o.wg, c.ctx, d, o.gao, d, ly.lin[3].scales, T, d, d, acc + lin_off[3], st, s), "o grad");
     for (int i = 0; i < 4; ++i) add_count(1 + 9 * l + i, T);

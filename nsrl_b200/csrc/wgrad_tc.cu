@@ -207,36 +207,65 @@ __global__ void __launch_bounds__(WTHREADS, 1) wgrad_tc_kernel(const __grid_cons
 
 // [T][C] int16 (row stride ld) -> byte planes of the transpose [C][T]
 // (row stride ldt bytes), each value first prescaled by rhu(v, shift_c)
-// when `sc` is given (multiplier 1).  64 x 64 tiles through shared memory.
+// when `sc` is given (multiplier 1).  64 x 64 tiles through shared memory:
+// 8-byte loads of four columns, 4-byte stores of four rows per plane.
 __global__ void __launch_bounds__(256) transpose_split_kernel(const int16_t* __restrict__ x, long long T, int C,
                                                               long long ld, const nsrl_fixed_scale* __restrict__ sc,
                                                               int8_t* __restrict__ th, uint8_t* __restrict__ tl,
-                                                              long long ldt) {
-  __shared__ int16_t tile[64][65];
+                                                              long long ldt, bool vec) {
+  __shared__ int16_t tile[64][66];  // [t][c]
   const long long t0 = (long long)blockIdx.x * 64;
   const int c0 = blockIdx.y * 64;
-  const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;  // 64 x 4
-  for (int r = ty; r < 64; r += 4) {
+  for (int i = threadIdx.x; i < 64 * 16; i += 256) {
+    const int r = i >> 4, c4 = (i & 15) * 4;
     const long long t = t0 + r;
-    const int c = c0 + tx;
-    int v = 0;
-    if (t < T && c < C) {
-      v = x[t * ld + c];
+    const int c = c0 + c4;
+    int v[4] = {0, 0, 0, 0};
+    if (t < T) {
+      if (vec && c + 3 < C) {
+        const uint2 u = *reinterpret_cast<const uint2*>(x + t * ld + c);
+        v[0] = (int16_t)(u.x & 0xFFFF);
+        v[1] = (int16_t)(u.x >> 16);
+        v[2] = (int16_t)(u.y & 0xFFFF);
+        v[3] = (int16_t)(u.y >> 16);
+      } else {
+#pragma unroll
+        for (int z = 0; z < 4; ++z)
+          if (c + z < C) v[z] = x[t * ld + c + z];
+      }
       if (sc) {
-        const int s = sc[c].right_shift;
-        if (s) v = (int)rhu64(v, (uint32_t)s);
+#pragma unroll
+        for (int z = 0; z < 4; ++z)
+          if (c + z < C) {
+            const int s = sc[c + z].right_shift;
+            if (s) v[z] = (int)rhu64(v[z], (uint32_t)s);
+          }
       }
     }
-    tile[r][tx] = (int16_t)v;
+#pragma unroll
+    for (int z = 0; z < 4; ++z) tile[r][c4 + z] = (int16_t)v[z];
   }
   __syncthreads();
-  for (int r = ty; r < 64; r += 4) {
-    const int c = c0 + r;
-    const long long t = t0 + tx;
-    if (c < C && t < T) {
-      const int v = tile[tx][r];
-      th[(long long)c * ldt + t] = (int8_t)(v >> 8);
-      tl[(long long)c * ldt + t] = (uint8_t)(v & 255);
+  for (int i = threadIdx.x; i < 64 * 16; i += 256) {
+    const int cr = i >> 4, t4 = (i & 15) * 4;
+    const int c = c0 + cr;
+    const long long t = t0 + t4;
+    if (c >= C || t >= T) continue;
+    uint32_t hv = 0, lv = 0;
+#pragma unroll
+    for (int z = 0; z < 4; ++z) {
+      const int v = tile[t4 + z][cr];
+      hv |= (uint32_t)((v >> 8) & 255) << (8 * z);
+      lv |= (uint32_t)(v & 255) << (8 * z);
+    }
+    if (t + 3 < T) {  // ldt and t are multiples of 4: aligned word stores
+      *reinterpret_cast<uint32_t*>(th + (long long)c * ldt + t) = hv;
+      *reinterpret_cast<uint32_t*>(tl + (long long)c * ldt + t) = lv;
+    } else {
+      for (int z = 0; t + z < T; ++z) {
+        th[(long long)c * ldt + t + z] = (int8_t)(hv >> (8 * z));
+        tl[(long long)c * ldt + t + z] = (uint8_t)(lv >> (8 * z));
+      }
     }
   }
 }
@@ -281,7 +310,9 @@ cudaError_t launch_transpose_split(const int16_t* x, size_t T, size_t C, size_t 
   if (T == 0 || C == 0) return cudaSuccess;
   dim3 grid((unsigned)((T + 63) / 64), (unsigned)((C + 63) / 64));
   ProfScope prof("transpose_split", s, 0.0, 4.0 * (double)T * (double)C);
-  transpose_split_kernel<<<grid, 256, 0, s>>>(x, (long long)T, (int)C, (long long)ld, sc, th, tl, (long long)ldt);
+  const bool vec = ld % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 7) == 0;
+  transpose_split_kernel<<<grid, 256, 0, s>>>(x, (long long)T, (int)C, (long long)ld, sc, th, tl, (long long)ldt,
+                                              vec);
   return cudaGetLastError();
 }
 

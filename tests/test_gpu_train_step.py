@@ -100,7 +100,8 @@ def test_rms_norm_backward(T, d, eps):
     assert sat == ref[2]
 
 
-@pytest.mark.parametrize("B,S,d,H", [(2, 33, 64, 4), (3, 64, 128, 2), (1, 200, 64, 1)])
+@pytest.mark.parametrize("B,S,d,H", [(2, 33, 64, 4), (3, 64, 128, 2), (1, 200, 64, 1), (2, 48, 64, 4),
+                                     (1, 520, 128, 2), (2, 4, 64, 1)])
 def test_attention_probabilities_and_backward(B, S, d, H):
     _, train = _core()
     rng = np.random.default_rng(B * S)
