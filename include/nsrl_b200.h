@@ -281,7 +281,7 @@ nsrl_status nsrl_attention_with_probabilities(const int16_t* q, const int16_t* k
 /* Softmax-attention backward (nsrl-train/src/lib.rs:16623-16900): from q, k, v
  * (stride ld), P and the context gradient dC [batch*seq_len][d] -> dq, dk, dv
  * [batch*seq_len][d].  Workspace: nsrl_attention_backward_workspace_size. */
-size_t nsrl_attention_backward_workspace_size(size_t batch, size_t seq_len, size_t heads);
+size_t nsrl_attention_backward_workspace_size(size_t batch, size_t seq_len, size_t d_model, size_t heads);
 nsrl_status nsrl_attention_backward(const int16_t* q, const int16_t* k, const int16_t* v, size_t ld,
                                     const int16_t* probabilities, const int16_t* grad_context, size_t batch,
                                     size_t seq_len, size_t d_model, size_t heads, int16_t* dq, int16_t* dk, int16_t* dv,

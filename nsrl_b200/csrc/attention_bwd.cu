@@ -59,12 +59,100 @@ __device__ __forceinline__ void split4(const int16_t* v, uint32_t& hi, uint32_t&
 constexpr int BQ = 64;  // query rows per CTA (4 warps x 16)
 constexpr int BK = 32;  // keys per tile
 
+// ---------------------------------------------------------------- planes --
+// Row p of a 32-key block holds key bkey_inv(p): the inverse of bkey_slot.
+__device__ __forceinline__ int bkey_inv(int p) { return 16 * (p >> 4) + 8 * ((p >> 1) & 1) + 2 * ((p >> 2) & 3) + (p & 1); }
+
+// X rows (row b*S + s, columns h*HD .. +HD, stride ld) -> per-head transposed
+// byte planes XT[((b*H + h)*HD + dim)*Sp + p]: p = s, or with perm the
+// MMA key order inside each 32-key block (zeros past S up to Sp).
+template <int HD>
+__global__ void __launch_bounds__(256) head_transpose_kernel(const int16_t* __restrict__ x, long long ld, int S, int Sp,
+                                                             int H, bool perm, int8_t* __restrict__ th,
+                                                             uint8_t* __restrict__ tl) {
+  __shared__ int16_t tile[64][HD + 2];
+  const int s0 = blockIdx.x * 64, h = blockIdx.y, b = blockIdx.z;
+  for (int i = threadIdx.x; i < 64 * (HD / 4); i += 256) {
+    const int r = i / (HD / 4), c4 = 4 * (i % (HD / 4));
+    int16_t v[4] = {0, 0, 0, 0};
+    if (s0 + r < S) {
+      const uint2 u = *reinterpret_cast<const uint2*>(x + ((long long)b * S + s0 + r) * ld + (long long)h * HD + c4);
+      v[0] = (int16_t)(u.x & 0xFFFF);
+      v[1] = (int16_t)(u.x >> 16);
+      v[2] = (int16_t)(u.y & 0xFFFF);
+      v[3] = (int16_t)(u.y >> 16);
+    }
+#pragma unroll
+    for (int z = 0; z < 4; ++z) tile[r][c4 + z] = v[z];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < HD * 16; i += 256) {
+    const int dim = i / 16, w = i % 16;  // word w: positions s0 + 4w .. +3
+    const int p0 = s0 + 4 * w;
+    if (p0 >= Sp) continue;
+    uint32_t hv = 0, lv = 0;
+#pragma unroll
+    for (int z = 0; z < 4; ++z) {
+      const int pl = 4 * w + z;  // position inside this 64-wide tile
+      const int src = perm ? (pl & ~31) + bkey_inv(pl & 31) : pl;
+      const int v = (s0 + src < S) ? tile[src][dim] : 0;
+      hv |= (uint32_t)((v >> 8) & 255) << (8 * z);
+      lv |= (uint32_t)(v & 255) << (8 * z);
+    }
+    const long long off = (((long long)b * H + h) * HD + dim) * Sp + p0;
+    *reinterpret_cast<uint32_t*>(th + off) = hv;
+    *reinterpret_cast<uint32_t*>(tl + off) = lv;
+  }
+}
+
+// M [BH][S][S] int16 -> MT byte planes, MT[bh][j][i] = M[bh][i][j], for the
+// tiles with i-tile >= j-tile (the causal part the key side reads).
+__global__ void __launch_bounds__(256) sq_transpose_kernel(const int16_t* __restrict__ M, int S,
+                                                           int8_t* __restrict__ th, uint8_t* __restrict__ tl) {
+  const int j0 = blockIdx.x * 64, i0 = blockIdx.y * 64;
+  if (i0 + 63 < j0) return;
+  __shared__ int16_t tile[64][66];  // [i][j]
+  const long long base = (long long)blockIdx.z * S * S;
+  for (int e = threadIdx.x; e < 64 * 16; e += 256) {
+    const int r = e >> 4, c4 = 4 * (e & 15);
+    int16_t v[4] = {0, 0, 0, 0};
+    if (i0 + r < S && j0 + c4 < S) {  // S % 4 == 0: the four columns are all inside
+      const uint2 u = *reinterpret_cast<const uint2*>(M + base + (long long)(i0 + r) * S + j0 + c4);
+      v[0] = (int16_t)(u.x & 0xFFFF);
+      v[1] = (int16_t)(u.x >> 16);
+      v[2] = (int16_t)(u.y & 0xFFFF);
+      v[3] = (int16_t)(u.y >> 16);
+    }
+#pragma unroll
+    for (int z = 0; z < 4; ++z) tile[r][c4 + z] = v[z];
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < 64 * 16; e += 256) {
+    const int jr = e >> 4, i4 = 4 * (e & 15);
+    if (j0 + jr >= S || i0 + i4 >= S) continue;
+    uint32_t hv = 0, lv = 0;
+#pragma unroll
+    for (int z = 0; z < 4; ++z) {
+      const int v = tile[i4 + z][jr];
+      hv |= (uint32_t)((v >> 8) & 255) << (8 * z);
+      lv |= (uint32_t)(v & 255) << (8 * z);
+    }
+    const long long off = base + (long long)(j0 + jr) * S + i0 + i4;
+    *reinterpret_cast<uint32_t*>(th + off) = hv;
+    *reinterpret_cast<uint32_t*>(tl + off) = lv;
+  }
+}
+
+// ---------------------------------------------------------------- query side --
 struct QArgs {
   const int16_t* dC;
   long long ldc;
-  const int16_t* V;
-  const int16_t* K;
-  long long ldkv;
+  const int8_t* v_hi;   // V planes [T][d]
+  const uint8_t* v_lo;
+  int d;
+  const int8_t* kt_hi;  // K^T planes [B][H][HD][Sp], MMA key order per 32-key block
+  const uint8_t* kt_lo;
+  int Sp;
   const int16_t* P;
   int S, H, shift;
   int16_t* dL;
@@ -98,6 +186,7 @@ __global__ void __launch_bounds__(128) attn_bwd_q_kernel(const QArgs a) {
   const int r0 = qw + g, r1 = r0 + 8;
   const int16_t* Pbh = a.P + ((long long)b * a.H + h) * S * (long long)S;
   int16_t* dLbh = a.dL + ((long long)b * a.H + h) * S * (long long)S;
+  const long long ktb = ((long long)b * a.H + h) * HD * (long long)a.Sp;
 
   // A fragments of dC rows r0 / r1 (k = dims)
   uint32_t ca_hi[KC][4], ca_lo[KC][4];
@@ -115,6 +204,12 @@ __global__ void __launch_bounds__(128) attn_bwd_q_kernel(const QArgs a) {
       ca_hi[c][i] = hv;
       ca_lo[c][i] = lv;
     }
+  if (HD == 16) {  // the k half past the head's 16 dims is zero in every V row
+    for (int i = tid; i < BK; i += 128) {
+      *reinterpret_cast<uint4*>(&sm.v_hi[i * KSTR + 16]) = make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4*>(&sm.v_lo[i * KSTR + 16]) = make_uint4(0, 0, 0, 0);
+    }
+  }
 
   const int kend = min(S, q0 + BQ);  // keys visited by this CTA (causal)
   const int ntiles = (kend + BK - 1) / BK;
@@ -131,37 +226,25 @@ __global__ void __launch_bounds__(128) attn_bwd_q_kernel(const QArgs a) {
     for (int kt = 0; kt < ntiles; ++kt) {
       const int kb = kt * BK;
       __syncthreads();
-      // stage V rows [key][dim] as planes; in pass 2 also K^T [dim][key slot]
-      for (int i = tid; i < BK * (HD / 4); i += 128) {
-        const int j = i / (HD / 4), c4 = i % (HD / 4);
+      // V rows [key][dim]: 16-byte copies of the planes
+      for (int i = tid; i < BK * (HD / 16); i += 128) {
+        const int j = i / (HD / 16), c16 = 16 * (i % (HD / 16));
         const int key = kb + j;
-        uint32_t vh = 0, vl = 0;
+        uint4 vh = make_uint4(0, 0, 0, 0), vl = vh;
         if (key < kend) {
-          const uint2 u = *reinterpret_cast<const uint2*>(a.V + (row0 + key) * a.ldkv + (long long)h * HD + 4 * c4);
-          split4(reinterpret_cast<const int16_t*>(&u), vh, vl);
+          const long long off = (row0 + key) * a.d + (long long)h * HD + c16;
+          vh = *reinterpret_cast<const uint4*>(a.v_hi + off);
+          vl = *reinterpret_cast<const uint4*>(a.v_lo + off);
         }
-        *reinterpret_cast<uint32_t*>(&sm.v_hi[j * KSTR + 4 * c4]) = vh;
-        *reinterpret_cast<uint32_t*>(&sm.v_lo[j * KSTR + 4 * c4]) = vl;
-        if (pass == 1) {
-          uint32_t kh = 0, kl = 0;
-          if (key < kend) {
-            const uint2 u =
-                *reinterpret_cast<const uint2*>(a.K + (row0 + key) * a.ldkv + (long long)h * HD + 4 * c4);
-            split4(reinterpret_cast<const int16_t*>(&u), kh, kl);
-          }
-          const int slot = bkey_slot(j);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            sm.kt_hi[(4 * c4 + e) * VSTR + slot] = (uint8_t)(kh >> (8 * e));
-            sm.kt_lo[(4 * c4 + e) * VSTR + slot] = (uint8_t)(kl >> (8 * e));
-          }
-        }
+        *reinterpret_cast<uint4*>(&sm.v_hi[j * KSTR + c16]) = vh;
+        *reinterpret_cast<uint4*>(&sm.v_lo[j * KSTR + c16]) = vl;
       }
-      if (HD == 16) {  // zero the unused k half of the V rows (dims 16..31)
-        for (int i = tid; i < BK * 4; i += 128) {
-          const int j = i / 4, c4 = i % 4;
-          *reinterpret_cast<uint32_t*>(&sm.v_hi[j * KSTR + 16 + 4 * c4]) = 0u;
-          *reinterpret_cast<uint32_t*>(&sm.v_lo[j * KSTR + 16 + 4 * c4]) = 0u;
+      if (pass == 1) {  // K^T [dim][32 key slots]: two 16-byte copies per dim and plane
+        for (int i = tid; i < HD * 2; i += 128) {
+          const int dim = i >> 1, half = 16 * (i & 1);
+          const long long off = ktb + (long long)dim * a.Sp + kb + half;
+          *reinterpret_cast<uint4*>(&sm.kt_hi[dim * VSTR + half]) = *reinterpret_cast<const uint4*>(a.kt_hi + off);
+          *reinterpret_cast<uint4*>(&sm.kt_lo[dim * VSTR + half]) = *reinterpret_cast<const uint4*>(a.kt_lo + off);
         }
       }
       __syncthreads();
@@ -286,10 +369,12 @@ __global__ void __launch_bounds__(128) attn_bwd_q_kernel(const QArgs a) {
     }
 }
 
+// ------------------------------------------------------------------ key side --
 struct KVArgs {
-  const int16_t* M;  // dL or P, [B][H][S][S]
-  const int16_t* X;  // Q or dC rows
-  long long ldx;
+  const int8_t* mt_hi;  // M^T planes [BH][S][S]: row = key, column = query
+  const uint8_t* mt_lo;
+  const int8_t* xt_hi;  // X^T planes [BH][HD][S]
+  const uint8_t* xt_lo;
   int S, H, shift;
   int16_t* out;
   long long ldo;
@@ -315,7 +400,7 @@ __global__ void __launch_bounds__(128) attn_bwd_kv_kernel(const KVArgs a) {
   const int k0 = blockIdx.x * BQ, h = blockIdx.y, b = blockIdx.z;
   const int S = a.S;
   const long long row0 = (long long)b * S;
-  const int16_t* Mbh = a.M + ((long long)b * a.H + h) * S * (long long)S;
+  const long long bh = (long long)b * a.H + h;
   const int kw = k0 + warp * 16;  // this warp's keys kw + g, kw + g + 8
   int acc_hh[NT][4], acc_mid[NT][4], acc_ll[NT][4];
 #pragma unroll
@@ -325,43 +410,29 @@ __global__ void __launch_bounds__(128) attn_bwd_kv_kernel(const KVArgs a) {
 
   for (int tq = k0; tq < S; tq += BK) {
     __syncthreads();
-    // M^T tile: M[tq + q][k0 + kc] -> at[kc][q]
-    for (int i = tid; i < BK * (BQ / 4); i += 128) {
-      const int q = i / (BQ / 4), c4 = i % (BQ / 4);
-      const int tr = tq + q, kc = 4 * c4;
-      int16_t v[4] = {0, 0, 0, 0};
-      if (tr < S) {
-        if (k0 + kc + 3 < S) {
-          const uint2 u = *reinterpret_cast<const uint2*>(Mbh + (long long)tr * S + k0 + kc);
-          const int16_t* e = reinterpret_cast<const int16_t*>(&u);
-#pragma unroll
-          for (int z = 0; z < 4; ++z) v[z] = e[z];
-        } else {
-#pragma unroll
-          for (int z = 0; z < 4; ++z)
-            if (k0 + kc + z < S) v[z] = Mbh[(long long)tr * S + k0 + kc + z];
-        }
+    // M^T rows (keys) x 32 queries, 4-byte copies (S % 4 == 0)
+    for (int i = tid; i < BQ * 8; i += 128) {
+      const int kr = i >> 3, w4 = 4 * (i & 7);
+      uint32_t vh = 0, vl = 0;
+      if (k0 + kr < S && tq + w4 < S) {
+        const long long off = (bh * S + k0 + kr) * (long long)S + tq + w4;
+        vh = *reinterpret_cast<const uint32_t*>(a.mt_hi + off);
+        vl = *reinterpret_cast<const uint32_t*>(a.mt_lo + off);
       }
-#pragma unroll
-      for (int z = 0; z < 4; ++z) {
-        sm.at_hi[(kc + z) * ASTR + q] = (uint8_t)(((int)v[z] >> 8) & 255);
-        sm.at_lo[(kc + z) * ASTR + q] = (uint8_t)((int)v[z] & 255);
-      }
+      *reinterpret_cast<uint32_t*>(&sm.at_hi[kr * ASTR + w4]) = vh;
+      *reinterpret_cast<uint32_t*>(&sm.at_lo[kr * ASTR + w4]) = vl;
     }
-    // X^T tile: X[tq + q][h HD + dim] -> xt[dim][q]
-    for (int i = tid; i < BK * (HD / 4); i += 128) {
-      const int q = i / (HD / 4), c4 = i % (HD / 4);
-      const int tr = tq + q;
-      uint32_t xh = 0, xl = 0;
-      if (tr < S) {
-        const uint2 u = *reinterpret_cast<const uint2*>(a.X + (row0 + tr) * a.ldx + (long long)h * HD + 4 * c4);
-        split4(reinterpret_cast<const int16_t*>(&u), xh, xl);
+    // X^T dims x 32 queries
+    for (int i = tid; i < HD * 8; i += 128) {
+      const int dim = i >> 3, w4 = 4 * (i & 7);
+      uint32_t vh = 0, vl = 0;
+      if (tq + w4 < S) {
+        const long long off = (bh * HD + dim) * (long long)S + tq + w4;
+        vh = *reinterpret_cast<const uint32_t*>(a.xt_hi + off);
+        vl = *reinterpret_cast<const uint32_t*>(a.xt_lo + off);
       }
-#pragma unroll
-      for (int z = 0; z < 4; ++z) {
-        sm.xt_hi[(4 * c4 + z) * ASTR + q] = (uint8_t)(xh >> (8 * z));
-        sm.xt_lo[(4 * c4 + z) * ASTR + q] = (uint8_t)(xl >> (8 * z));
-      }
+      *reinterpret_cast<uint32_t*>(&sm.xt_hi[dim * ASTR + w4]) = vh;
+      *reinterpret_cast<uint32_t*>(&sm.xt_lo[dim * ASTR + w4]) = vl;
     }
     __syncthreads();
     if (kw >= S || tq + BK - 1 < kw) continue;  // keys past the sequence, or queries all before them
@@ -405,23 +476,72 @@ __global__ void __launch_bounds__(128) attn_bwd_kv_kernel(const KVArgs a) {
 
 }  // namespace
 
+size_t attention_backward_tc_scratch_bytes(size_t B, size_t S, size_t d, size_t H) {
+  const size_t Sp = (S + 31) & ~size_t(31);
+  auto up = [](size_t b) { return (b + 255) & ~size_t(255); };
+  // V planes [T][d], K^T (padded rows), Q^T, dC^T, P^T, dL^T: two planes each
+  return 2 * (up(B * S * d) + up(B * d * Sp) + 2 * up(B * d * S) + 2 * up(B * H * S * S));
+}
+
 // dQ, dK, dV (and dL into `dl`, zeroed here) of causal attention on int16
 // operands: q, k, v rows of stride ld, P [B][H][S][S], dC rows of stride ldc;
-// outputs [B*S][d].  head_dim 16 or 64, S a multiple of 4 (else cudaErrorNotSupported).
+// outputs [B*S][d].  head_dim 16 or 64, S a multiple of 4, d a multiple of 16
+// (else cudaErrorNotSupported).  scratch: attention_backward_tc_scratch_bytes.
 cudaError_t launch_attention_backward_tc(const int16_t* q, const int16_t* k, const int16_t* v, size_t ld,
                                          const int16_t* P, const int16_t* dC, size_t ldc, size_t B, size_t S, size_t d,
                                          size_t H, int16_t* dl, int16_t* dq, int16_t* dk, int16_t* dv,
-                                         nsrl_device_status* st, cudaStream_t s) {
+                                         void* scratch, size_t scratch_bytes, nsrl_device_status* st,
+                                         cudaStream_t s) {
   const size_t hd = d / H;
   // 8-byte loads of P / dL rows, dC, q, k, v need S, ld, ldc multiples of 4
-  if ((hd != 16 && hd != 64) || S % 4 != 0 || ld % 4 != 0 || ldc % 4 != 0 || d % 4 != 0 || S > 16384)
+  if ((hd != 16 && hd != 64) || S % 4 != 0 || ld % 4 != 0 || ldc % 4 != 0 || d % 16 != 0 || S > 16384 ||
+      !scratch || scratch_bytes < attention_backward_tc_scratch_bytes(B, S, d, H))
     return cudaErrorNotSupported;
   const int shift = __builtin_ctzll(hd) / 2;
+  const size_t Sp = (S + 31) & ~size_t(31);
+  uint8_t* w = static_cast<uint8_t*>(scratch);
+  size_t off = 0;
+  auto take = [&](size_t n) {
+    uint8_t* p = w + off;
+    off += (n + 255) & ~size_t(255);
+    return p;
+  };
+  int8_t* vph = reinterpret_cast<int8_t*>(take(B * S * d));
+  uint8_t* vpl = take(B * S * d);
+  int8_t* kth = reinterpret_cast<int8_t*>(take(B * d * Sp));
+  uint8_t* ktl = take(B * d * Sp);
+  int8_t* qth = reinterpret_cast<int8_t*>(take(B * d * S));
+  uint8_t* qtl = take(B * d * S);
+  int8_t* cth = reinterpret_cast<int8_t*>(take(B * d * S));
+  uint8_t* ctl = take(B * d * S);
+  int8_t* pth = reinterpret_cast<int8_t*>(take(B * H * S * S));
+  uint8_t* ptl = take(B * H * S * S);
+  int8_t* lth = reinterpret_cast<int8_t*>(take(B * H * S * S));
+  uint8_t* ltl = take(B * H * S * S);
   cudaError_t e = cudaMemsetAsync(dl, 0, B * H * S * S * sizeof(int16_t), s);
   if (e != cudaSuccess) return e;
   const double pairs = (double)B * (double)H * (double)S * (double)(S + 1) / 2.0;
+  {
+    ProfScope prof("attention_bwd_planes", s, 0.0, 8.0 * (double)B * S * d + 2.0 * 2.0 * (double)B * H * S * S);
+    e = launch_split_planes(v, B * S, d, ld, Planes{vph, vpl, nullptr, d}, s);
+    if (e != cudaSuccess) return e;
+    dim3 tg((unsigned)((S + 63) / 64), (unsigned)H, (unsigned)B);
+    if (hd == 64) {
+      head_transpose_kernel<64><<<tg, 256, 0, s>>>(k, (long long)ld, (int)S, (int)Sp, (int)H, true, kth, ktl);
+      head_transpose_kernel<64><<<tg, 256, 0, s>>>(q, (long long)ld, (int)S, (int)S, (int)H, false, qth, qtl);
+      head_transpose_kernel<64><<<tg, 256, 0, s>>>(dC, (long long)ldc, (int)S, (int)S, (int)H, false, cth, ctl);
+    } else {
+      head_transpose_kernel<16><<<tg, 256, 0, s>>>(k, (long long)ld, (int)S, (int)Sp, (int)H, true, kth, ktl);
+      head_transpose_kernel<16><<<tg, 256, 0, s>>>(q, (long long)ld, (int)S, (int)S, (int)H, false, qth, qtl);
+      head_transpose_kernel<16><<<tg, 256, 0, s>>>(dC, (long long)ldc, (int)S, (int)S, (int)H, false, cth, ctl);
+    }
+    dim3 sg((unsigned)((S + 63) / 64), (unsigned)((S + 63) / 64), (unsigned)(B * H));
+    sq_transpose_kernel<<<sg, 256, 0, s>>>(P, (int)S, pth, ptl);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
   dim3 grid((unsigned)((S + BQ - 1) / BQ), (unsigned)H, (unsigned)B);
-  QArgs qa{dC, (long long)ldc, v, k, (long long)ld, P, (int)S, (int)H, shift, dl, dq, (long long)d, st};
+  QArgs qa{dC, (long long)ldc, vph, vpl, (int)d, kth, ktl, (int)Sp, P, (int)S, (int)H, shift, dl, dq, (long long)d, st};
   {
     ProfScope prof("attention_bwd_q", s, 3.0 * 2.0 * (double)hd * pairs,
                    2.0 * 2.0 * (double)B * H * S * S + 8.0 * (double)B * S * d);
@@ -432,8 +552,15 @@ cudaError_t launch_attention_backward_tc(const int16_t* q, const int16_t* k, con
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
-  KVArgs ka{dl, q, (long long)ld, (int)S, (int)H, shift, dk, (long long)d};
-  KVArgs va{P, dC, (long long)ldc, (int)S, (int)H, 15, dv, (long long)d};
+  {
+    dim3 sg((unsigned)((S + 63) / 64), (unsigned)((S + 63) / 64), (unsigned)(B * H));
+    ProfScope prof("attention_bwd_planes", s, 0.0, 4.0 * (double)B * H * S * S);
+    sq_transpose_kernel<<<sg, 256, 0, s>>>(dl, (int)S, lth, ltl);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  KVArgs ka{lth, ltl, qth, qtl, (int)S, (int)H, shift, dk, (long long)d};
+  KVArgs va{pth, ptl, cth, ctl, (int)S, (int)H, 15, dv, (long long)d};
   ProfScope prof("attention_bwd_kv", s, 2.0 * 2.0 * (double)hd * pairs,
                  2.0 * 2.0 * (double)B * H * S * S + 8.0 * (double)B * S * d);
   if (hd == 64) {

@@ -132,11 +132,14 @@ cudaError_t launch_wgrad_tc(const int8_t* gh, const uint8_t* gl, const int8_t* x
 
 // Softmax-attention backward on the int8 tensor cores (mma.sync): dQ, dK, dV
 // and dL (zeroed, then written) from int16 q, k, v (row stride ld), P and dC.
-// cudaErrorNotSupported outside head_dim 16/64, S % 4 == 0, S <= 16384.
+// cudaErrorNotSupported outside head_dim 16/64, S % 4 == 0, d % 16 == 0,
+// S <= 16384, or with a scratch below attention_backward_tc_scratch_bytes.
+size_t attention_backward_tc_scratch_bytes(size_t B, size_t S, size_t d, size_t H);
 cudaError_t launch_attention_backward_tc(const int16_t* q, const int16_t* k, const int16_t* v, size_t ld,
                                          const int16_t* P, const int16_t* dC, size_t ldc, size_t B, size_t S, size_t d,
                                          size_t H, int16_t* dl, int16_t* dq, int16_t* dk, int16_t* dv,
-                                         nsrl_device_status* st, cudaStream_t s);
+                                         void* scratch, size_t scratch_bytes, nsrl_device_status* st,
+                                         cudaStream_t s);
 
 // Planes -> int16.
 cudaError_t launch_join_planes(Planes in, size_t rows, size_t cols, int16_t* y, size_t ldy, cudaStream_t stream);

@@ -236,8 +236,10 @@ cudaError_t add_sat(const int16_t* a, const int16_t* b, size_t n, int16_t* out, 
 // dL, then dQ, dK, dV of one attention layer (nsrl-train/src/lib.rs:16623-16900).
 cudaError_t attn_backward(const int16_t* q, const int16_t* k, const int16_t* v, size_t ld, const int16_t* P,
                           const int16_t* dC, size_t ldc, size_t B, size_t S, size_t d, size_t H, int16_t* dL,
-                          int16_t* dq, int16_t* dk, int16_t* dv, nsrl_device_status* st, cudaStream_t s) {
-  const cudaError_t tce = launch_attention_backward_tc(q, k, v, ld, P, dC, ldc, B, S, d, H, dL, dq, dk, dv, st, s);
+                          int16_t* dq, int16_t* dk, int16_t* dv, void* scratch, size_t scratch_bytes,
+                          nsrl_device_status* st, cudaStream_t s) {
+  const cudaError_t tce = launch_attention_backward_tc(q, k, v, ld, P, dC, ldc, B, S, d, H, dL, dq, dk, dv, scratch,
+                                                       scratch_bytes, st, s);
   if (tce != cudaErrorNotSupported) return tce;
   const size_t hd = d / H;
   const int shift = __builtin_ctzll(hd) / 2;
@@ -294,6 +296,8 @@ struct StepLayout {
   WgBufs wg;
   Planes pqkv;  // q|k planes of the tensor-core attention (v goes to vt)
   VtPlanes vt;
+  void* abw;    // scratch of the tensor-core attention backward
+  size_t abw_bytes;
   size_t bytes;
 };
 
@@ -359,6 +363,8 @@ void carve_step(const nsrl_train_model* m, size_t W, bool rms, void* base, StepL
     const size_t ws = attention_tc_scratch_bytes(W, S, d, H);
     if (ws) o.vt.wscr = c.take<int16_t>(ws / sizeof(int16_t));
   }
+  o.abw_bytes = attention_backward_tc_scratch_bytes(W, S, d, H);
+  o.abw = c.take<uint8_t>(o.abw_bytes);
   o.bytes = c.off;
 }
 
@@ -513,7 +519,9 @@ nsrl_status nsrl_attention_with_probabilities(const int16_t* q, const int16_t* k
   return NSRL_OK;
 }
 
-size_t nsrl_attention_backward_workspace_size(size_t B, size_t S, size_t H) { return up256(B * H * S * S * 2); }
+size_t nsrl_attention_backward_workspace_size(size_t B, size_t S, size_t d, size_t H) {
+  return up256(B * H * S * S * 2) + attention_backward_tc_scratch_bytes(B, S, d, H);
+}
 
 nsrl_status nsrl_attention_backward(const int16_t* q, const int16_t* k, const int16_t* v, size_t ld, const int16_t* P,
                                     const int16_t* dC, size_t B, size_t S, size_t d, size_t H, int16_t* dq,
@@ -524,9 +532,11 @@ nsrl_status nsrl_attention_backward(const int16_t* q, const int16_t* k, const in
   if (!is_pow4(hd)) return fail_shape("head_dim must be a power of four");
   if (hd != 16 && hd != 64) return fail_shape("attention backward: head_dim 16 or 64");
   if (ld % 8 != 0 || d % 8 != 0 || S > 16384) return fail_shape("row strides multiples of 8, seq_len <= 16384");
-  if (!workspace || workspace_bytes < nsrl_attention_backward_workspace_size(B, S, H))
+  if (!workspace || workspace_bytes < nsrl_attention_backward_workspace_size(B, S, d, H))
     return fail_shape("workspace too small");
-  TS_TRY(attn_backward(q, k, v, ld, P, dC, d, B, S, d, H, static_cast<int16_t*>(workspace), dq, dk, dv, st,
+  const size_t dl_bytes = up256(B * H * S * S * 2);
+  TS_TRY(attn_backward(q, k, v, ld, P, dC, d, B, S, d, H, static_cast<int16_t*>(workspace), dq, dk, dv,
+                       static_cast<uint8_t*>(workspace) + dl_bytes, workspace_bytes - dl_bytes, st,
                        (cudaStream_t)stream),
          "attention backward");
   return NSRL_OK;
@@ -780,7 +790,7 @@ nsrl_status nsrl_train_windows(const nsrl_train_model* m, const uint8_t* context
     TS_TRY(prescale_split(o.gao, T, d, d, ly.lin[3].scales, padn, s), "prescale");
     TS_TRY(bwd_gemm(padn, T, d, c.wt[3], d, o.ident, o.gctx, d, nullptr, nullptr, st, s), "o^T");
     TS_TRY(attn_backward(c.qkv, c.qkv + d, c.qkv + 2 * d, 3 * d, c.P, o.gctx, d, W, S, d, H, o.dL, o.dq, o.dk, o.dv,
-                         st, s),
+                         o.abw, o.abw_bytes, st, s),
            "attention backward");
     int16_t* gin[3] = {o.gq, o.gk, o.gv};
     const int16_t* dqkv[3] = {o.dq, o.dk, o.dv};

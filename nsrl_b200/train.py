@@ -178,7 +178,7 @@ def _lib_bwd():
         L.nsrl_rms_norm_backward_rows.argtypes = [vp, sz, sz, vp, vp, C.c_uint64, vp, vp, vp, vp, vp]
         L.nsrl_attention_with_probabilities.argtypes = [vp, vp, vp, sz, sz, sz, sz, sz, vp, vp, vp, vp]
         L.nsrl_attention_backward_workspace_size.restype = sz
-        L.nsrl_attention_backward_workspace_size.argtypes = [sz, sz, sz]
+        L.nsrl_attention_backward_workspace_size.argtypes = [sz, sz, sz, sz]
         L.nsrl_attention_backward.argtypes = [vp, vp, vp, sz, vp, vp, sz, sz, sz, sz, vp, vp, vp, vp, sz, vp, vp]
         L.nsrl_train_arena_len.restype = sz
         L.nsrl_train_arena_len.argtypes = [vp]
@@ -268,7 +268,7 @@ def attention_backward(q, k, v, P, grad_context, batch, seq_len, d_model, heads)
     dq = torch.empty((batch * seq_len, d_model), dtype=torch.int16, device=q.device)
     dk = torch.empty_like(dq)
     dv = torch.empty_like(dq)
-    ws = core.workspace(L.nsrl_attention_backward_workspace_size(batch, seq_len, heads))
+    ws = core.workspace(L.nsrl_attention_backward_workspace_size(batch, seq_len, d_model, heads))
     st = core.Status()
     r = L.nsrl_attention_backward(core._ptr(q), core._ptr(k), core._ptr(v), d_model, core._ptr(P), core._ptr(dC),
                                   batch, seq_len, d_model, heads, core._ptr(dq), core._ptr(dk), core._ptr(dv),
