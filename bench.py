@@ -317,12 +317,14 @@ def train_cpu_sample(tw, ctx, tgt, threads):
     return len(tgt) * TR_S / dt, dt
 
 
-def run_train(core, torch, dist, world, rank, steps, warmup, flush, hbm, tfl, src, cpu_baseline):
+def run_train(core, torch, dist, world, rank, steps, warmup, flush, hbm, tfl, src, cpu_baseline, batch=TR_BATCH):
     """Config 4: the data-parallel training step (windows forward + backward,
-    exact int64 all-reduce, requantising apply) over TR_BATCH windows per step."""
+    exact int64 all-reduce, requantising apply) over `batch` windows per step
+    (TR_BATCH for the measurement; smaller for profiling captures)."""
     from nsrl_b200 import synth as Y
     from nsrl_b200 import train as TT
     L = core.lib()
+    TR_BATCH = batch
     if TR_BATCH % world:
         raise ValueError("the global batch must split evenly over the ranks")
     W = TR_BATCH // world
@@ -499,7 +501,7 @@ def run_secondary(args):
                          batch=args.decode_batch)
     elif args.case == "train":
         out = run_train(core, torch, None, 1, 0, steps=args.steps, warmup=args.warmup, flush=flush, hbm=hbm, tfl=tfl,
-                        src=peaks()[2], cpu_baseline=not args.no_cpu_baseline)
+                        src=peaks()[2], cpu_baseline=not args.no_cpu_baseline, batch=args.train_windows)
     else:
         out = run_sweep(core, torch, hbm, tfl, flush)
     print(json.dumps(out), flush=True)
@@ -518,6 +520,8 @@ def main():
                     help="decode / sweep / train: run only that secondary measurement on one GPU")
     ap.add_argument("--decode-batch", type=int, default=DEC_B)
     ap.add_argument("--train-steps", type=int, default=3, help="timed steps of the training-step measurement")
+    ap.add_argument("--train-windows", type=int, default=TR_BATCH,
+                    help="--case train: windows per step (the measurement uses the global batch of 256)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)

@@ -74,6 +74,8 @@ nsrl_status fail_shape(const char* what) {
     if (_e != cudaSuccess) return _e;    \
   } while (0)
 
+bool aligned_to(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
 bool is_pow4(size_t v) { return v != 0 && (v & (v - 1)) == 0 && (__builtin_ctzll(v) % 2) == 0; }
 
 __global__ void fill_identity_kernel(nsrl_fixed_scale* s, int n) {
@@ -128,8 +130,11 @@ cudaError_t prescale_split(const int16_t* g, size_t M, size_t N, size_t ldg, con
                            cudaStream_t s) {
   const long long n = (long long)M * (long long)N;
   ProfScope prof("prescale_split", s, 0.0, 4.0 * (double)n);
-  prescale_split_kernel<<<blocks_for(n, 148 * 32), 256, 0, s>>>(g, (long long)M, (int)N, (long long)ldg, sc, out.hi,
-                                                                 out.lo, (long long)out.ld);
+  if (N % 8 == 0 && ldg == N && out.ld == N && aligned_to(g, 16) && aligned_to(out.hi, 8) && aligned_to(out.lo, 8))
+    prescale_split_vec_kernel<<<blocks_for(n / 8, 148 * 32), 256, 0, s>>>(g, n / 8, (int)N, sc, out.hi, out.lo);
+  else
+    prescale_split_kernel<<<blocks_for(n, 148 * 32), 256, 0, s>>>(g, (long long)M, (int)N, (long long)ldg, sc,
+                                                                   out.hi, out.lo, (long long)out.ld);
   return cudaGetLastError();
 }
 
@@ -217,6 +222,23 @@ cudaError_t rms_backward(const int16_t* x, size_t rows, size_t d, const int16_t*
   if (rows == 0) return cudaSuccess;
   const size_t smem = d * sizeof(long long);
   ProfScope prof("rms_backward", s, 0.0, 6.0 * (double)rows * (double)d);
+  if (d % 32 == 0 && d <= 512) {
+    const unsigned blocks = blocks_for((long long)rows * 32, 148 * 8);
+#define TS_RMS_CASE(N)                                                                                   \
+  case N:                                                                                                \
+    rms_backward_reg_kernel<N><<<blocks, 256, 0, s>>>(x, (long long)rows, w, go, eps, gi, gw, sat, st); \
+    return cudaGetLastError();
+    switch (d / 32) {
+      TS_RMS_CASE(1)
+      TS_RMS_CASE(2)
+      TS_RMS_CASE(4)
+      TS_RMS_CASE(8)
+      TS_RMS_CASE(16)
+      default:
+        break;
+    }
+#undef TS_RMS_CASE
+  }
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(rms_backward_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
@@ -229,7 +251,10 @@ cudaError_t rms_backward(const int16_t* x, size_t rows, size_t d, const int16_t*
 cudaError_t add_sat(const int16_t* a, const int16_t* b, size_t n, int16_t* out, unsigned long long* sat,
                     cudaStream_t s) {
   ProfScope prof("add_saturating", s, 0.0, 6.0 * (double)n);
-  add_sat_kernel<<<blocks_for((long long)n), 256, 0, s>>>(a, b, (long long)n, out, sat);
+  if (n % 8 == 0 && aligned_to(a, 16) && aligned_to(b, 16) && aligned_to(out, 16))
+    add_sat_vec_kernel<<<blocks_for((long long)n / 8, 148 * 32), 256, 0, s>>>(a, b, (long long)n / 8, out, sat);
+  else
+    add_sat_kernel<<<blocks_for((long long)n), 256, 0, s>>>(a, b, (long long)n, out, sat);
   return cudaGetLastError();
 }
 
@@ -761,9 +786,9 @@ nsrl_status nsrl_train_windows(const nsrl_train_model* m, const uint8_t* context
     {
       const long long n = (long long)T * F;
       ProfScope prof("gated_backward", s, 0.0, 14.0 * (double)n);
-      gated_backward_kernel<<<blocks_for(n, 148 * 32), 256, 0, s>>>(o.gg, c.up, c.gate, n, (int)F, ly.lin[4].scales,
-                                                                    ly.lin[5].scales, o.gup, o.ggate, paFn.hi, paFn.lo,
-                                                                    pbF.hi, pbF.lo);
+      gated_backward_vec_kernel<<<blocks_for(n / 8, 148 * 32), 256, 0, s>>>(
+          o.gg, c.up, c.gate, n / 8, (int)F, ly.lin[4].scales, ly.lin[5].scales, o.gup, o.ggate, paFn.hi, paFn.lo,
+          pbF.hi, pbF.lo);
       TS_TRY(cudaGetLastError(), "gated backward");
     }
     TS_TRY(bwd_gemm(paFn, T, F, c.wt[4], d, o.ident, o.gui, d, nullptr, nullptr, st, s), "up^T");
@@ -801,7 +826,10 @@ nsrl_status nsrl_train_windows(const nsrl_train_model* m, const uint8_t* context
     {
       const long long n = (long long)T * d;
       ProfScope prof("fanin", s, 0.0, 8.0 * (double)n);
-      fanin3_kernel<<<blocks_for(n), 256, 0, s>>>(o.gq, o.gk, o.gv, n, o.gni, attn_sat);
+      if (n % 8 == 0)  // carved buffers are 256-byte aligned
+        fanin3_vec_kernel<<<blocks_for(n / 8, 148 * 32), 256, 0, s>>>(o.gq, o.gk, o.gv, n / 8, o.gni, attn_sat);
+      else
+        fanin3_kernel<<<blocks_for(n), 256, 0, s>>>(o.gq, o.gk, o.gv, n, o.gni, attn_sat);
       TS_TRY(cudaGetLastError(), "fanin");
     }
     for (int i = 0; i < 3; ++i)

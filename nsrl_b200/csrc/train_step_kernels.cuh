@@ -100,6 +100,130 @@ __global__ void gated_backward_kernel(const int16_t* __restrict__ gg, const int1
   }
 }
 
+// Eight int16 values of a 16-byte load.
+__device__ __forceinline__ void unpack8(const uint4& u, int (&v)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = (int)(int16_t)(w[i] & 0xFFFF);
+    v[2 * i + 1] = (int)(int16_t)(w[i] >> 16);
+  }
+}
+__device__ __forceinline__ uint4 pack8(const int (&v)[8]) {
+  return make_uint4((uint32_t)(v[0] & 0xFFFF) | ((uint32_t)v[1] << 16), (uint32_t)(v[2] & 0xFFFF) | ((uint32_t)v[3] << 16),
+                    (uint32_t)(v[4] & 0xFFFF) | ((uint32_t)v[5] << 16), (uint32_t)(v[6] & 0xFFFF) | ((uint32_t)v[7] << 16));
+}
+// hi bytes (s8) and lo bytes (u8) of eight values, as two 8-byte words.
+__device__ __forceinline__ void planes8(const int (&v)[8], uint2& hi, uint2& lo) {
+  uint32_t h[2] = {0, 0}, l[2] = {0, 0};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    h[i >> 2] |= (uint32_t)((v[i] >> 8) & 255) << (8 * (i & 3));
+    l[i >> 2] |= (uint32_t)(v[i] & 255) << (8 * (i & 3));
+  }
+  hi = make_uint2(h[0], h[1]);
+  lo = make_uint2(l[0], l[1]);
+}
+
+// gated_backward_kernel on eight consecutive hidden units per thread
+// (F % 8 == 0, 16-byte aligned rows).
+__global__ void gated_backward_vec_kernel(const int16_t* __restrict__ gg, const int16_t* __restrict__ up,
+                                          const int16_t* __restrict__ gate, long long n8, int F,
+                                          const nsrl_fixed_scale* __restrict__ su,
+                                          const nsrl_fixed_scale* __restrict__ sg, int16_t* __restrict__ gup,
+                                          int16_t* __restrict__ ggate, int8_t* __restrict__ uh,
+                                          uint8_t* __restrict__ ul, int8_t* __restrict__ gh,
+                                          uint8_t* __restrict__ gl) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
+    int g[8], u[8], ga[8], ou[8], og[8], pu[8], pg[8];
+    unpack8(reinterpret_cast<const uint4*>(gg)[i], g);
+    unpack8(reinterpret_cast<const uint4*>(up)[i], u);
+    unpack8(reinterpret_cast<const uint4*>(gate)[i], ga);
+    const int f0 = (int)((i * 8) % F);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int silu = (ga[e] * ((ga[e] >> 2) + 16384) + 16384) >> 15;
+      ou[e] = (g[e] * silu + 16384) >> 15;
+      const int grad_silu = (g[e] * u[e] + 16384) >> 15;
+      og[e] = sat16((grad_silu * ((ga[e] >> 1) + 16384) + 16384) >> 15);
+      const int s1 = su[f0 + e].right_shift, s2 = sg[f0 + e].right_shift;
+      pu[e] = s1 ? (int)rhu64(ou[e], (uint32_t)s1) : ou[e];
+      pg[e] = s2 ? (int)rhu64(og[e], (uint32_t)s2) : og[e];
+    }
+    reinterpret_cast<uint4*>(gup)[i] = pack8(ou);
+    reinterpret_cast<uint4*>(ggate)[i] = pack8(og);
+    uint2 h, l;
+    planes8(pu, h, l);
+    reinterpret_cast<uint2*>(uh)[i] = h;
+    reinterpret_cast<uint2*>(ul)[i] = l;
+    planes8(pg, h, l);
+    reinterpret_cast<uint2*>(gh)[i] = h;
+    reinterpret_cast<uint2*>(gl)[i] = l;
+  }
+}
+
+// prescale_split_kernel on eight consecutive columns (N % 8 == 0, ldg == ldp == N).
+__global__ void prescale_split_vec_kernel(const int16_t* __restrict__ g, long long n8, int N,
+                                          const nsrl_fixed_scale* __restrict__ sc, int8_t* __restrict__ hi,
+                                          uint8_t* __restrict__ lo) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
+    int v[8];
+    unpack8(reinterpret_cast<const uint4*>(g)[i], v);
+    const int c0 = (int)((i * 8) % N);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int s = sc[c0 + e].right_shift;
+      if (s) v[e] = (int)rhu64(v[e], (uint32_t)s);
+    }
+    uint2 h, l;
+    planes8(v, h, l);
+    reinterpret_cast<uint2*>(hi)[i] = h;
+    reinterpret_cast<uint2*>(lo)[i] = l;
+  }
+}
+
+// add_sat_kernel / fanin3_kernel on eight elements per thread (n % 8 == 0).
+__global__ void add_sat_vec_kernel(const int16_t* __restrict__ a, const int16_t* __restrict__ b, long long n8,
+                                   int16_t* __restrict__ out, unsigned long long* sat) {
+  unsigned long long c = 0;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
+    int x[8], y[8], o[8];
+    unpack8(reinterpret_cast<const uint4*>(a)[i], x);
+    unpack8(reinterpret_cast<const uint4*>(b)[i], y);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int w = x[e] + y[e];
+      o[e] = sat16(w);
+      c += o[e] != w;
+    }
+    reinterpret_cast<uint4*>(out)[i] = pack8(o);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+  if ((threadIdx.x & 31) == 0 && c) atomicAdd(sat, c);
+}
+__global__ void fanin3_vec_kernel(const int16_t* __restrict__ a, const int16_t* __restrict__ b,
+                                  const int16_t* __restrict__ c3, long long n8, int16_t* __restrict__ out,
+                                  unsigned long long* sat) {
+  unsigned long long cnt = 0;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
+    int x[8], y[8], z[8], o[8];
+    unpack8(reinterpret_cast<const uint4*>(a)[i], x);
+    unpack8(reinterpret_cast<const uint4*>(b)[i], y);
+    unpack8(reinterpret_cast<const uint4*>(c3)[i], z);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int w = (x[e] + y[e] + z[e] + 1) >> 1;
+      o[e] = sat16(w);
+      cnt += o[e] != w;
+    }
+    reinterpret_cast<uint4*>(out)[i] = pack8(o);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+  if ((threadIdx.x & 31) == 0 && cnt) atomicAdd(sat, cnt);
+}
+
 // mlp.rs:150-170 forward gating on cached up / gate rows -> gated int16 and
 // byte planes with the row L1 (one warp per row).
 __global__ void gated_forward_kernel(const int16_t* __restrict__ up, const int16_t* __restrict__ gate, long long rows,
@@ -374,6 +498,79 @@ __global__ void __launch_bounds__(256) rms_backward_kernel(const int16_t* __rest
   __syncthreads();
   for (int i = threadIdx.x; i < d; i += blockDim.x)
     if (sgw[i]) atomicAdd(reinterpret_cast<unsigned long long*>(&gw[i]), (unsigned long long)sgw[i]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) nsat += __shfl_xor_sync(0xffffffffu, nsat, o);
+  if (lane == 0 && nsat) atomicAdd(sat, nsat);
+}
+
+// rms_backward_kernel with the row held in registers: D32 = d / 32 columns per
+// lane (lane + 32 i), gamma gradients summed per lane over the warp's rows and
+// added once per warp.  Same arithmetic; the rounding adds cannot saturate
+// here (see the range note above), so rhu is (v + 2^(s-1)) >> s.
+template <int D32>
+__global__ void __launch_bounds__(256) rms_backward_reg_kernel(const int16_t* __restrict__ x, long long rows,
+                                                               const int16_t* __restrict__ w,
+                                                               const int16_t* __restrict__ go, unsigned long long eps,
+                                                               int16_t* __restrict__ gi, long long* __restrict__ gw,
+                                                               unsigned long long* sat, nsrl_device_status* st) {
+  constexpr int d = 32 * D32;
+  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+  int wv[D32];
+  long long gacc[D32];
+#pragma unroll
+  for (int i = 0; i < D32; ++i) {
+    wv[i] = w[lane + 32 * i];
+    gacc[i] = 0;
+  }
+  unsigned long long nsat = 0;
+  for (long long r = (long long)blockIdx.x * warps + (threadIdx.x >> 5); r < rows; r += (long long)gridDim.x * warps) {
+    int xv[D32], gv[D32];
+#pragma unroll
+    for (int i = 0; i < D32; ++i) {
+      xv[i] = x[r * d + lane + 32 * i];
+      gv[i] = go[r * d + lane + 32 * i];
+    }
+    unsigned long long ss = 0;
+#pragma unroll
+    for (int i = 0; i < D32; ++i) ss += (unsigned long long)(unsigned)(xv[i] * xv[i]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const unsigned long long mean = ss / (unsigned long long)d;
+    const unsigned long long v = mean + eps;
+    if (v < mean || v == 0) {
+      if (lane == 0) nsrl_flag(st, NSRL_FLAG_RMS_ZERO);
+      continue;
+    }
+    const long long inv = rsqrt_q30(v);
+    int nm[D32], sg[D32];
+    long long dot = 0;
+#pragma unroll
+    for (int i = 0; i < D32; ++i) {
+      nm[i] = (int)(((long long)xv[i] * inv + (1ll << 14)) >> 15);
+      const long long proj = ((long long)(xv[i] * wv[i]) * inv + (1ll << 29)) >> 30;
+      const bool active = proj >= -32768 && proj <= 32767;
+      sg[i] = active ? ((gv[i] * wv[i] + (1 << 14)) >> 15) : 0;
+      dot += (long long)sg[i] * (long long)nm[i];
+      if (active) gacc[i] += ((long long)gv[i] * (long long)nm[i] + (1ll << 14)) >> 15;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+    const long long den = (long long)d << 15;
+    const long long tq = dot + den / 2;
+    long long mdot = tq / den;
+    if ((tq % den) != 0 && tq < 0) --mdot;
+#pragma unroll
+    for (int i = 0; i < D32; ++i) {
+      const long long cross = ((long long)nm[i] * mdot + (1ll << 14)) >> 15;
+      const long long gg = (((long long)sg[i] - cross) * inv + (1ll << 29)) >> 30;
+      const int16_t cl = sat_i16(gg);
+      nsat += (long long)cl != gg;
+      gi[r * d + lane + 32 * i] = cl;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < D32; ++i)
+    if (gacc[i]) atomicAdd(reinterpret_cast<unsigned long long*>(&gw[lane + 32 * i]), (unsigned long long)gacc[i]);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) nsat += __shfl_xor_sync(0xffffffffu, nsat, o);
   if (lane == 0 && nsat) atomicAdd(sat, nsat);
