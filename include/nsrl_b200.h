@@ -339,6 +339,25 @@ nsrl_status nsrl_train_windows(const nsrl_train_model* model, const uint8_t* con
                                unsigned long long* counts, unsigned long long* stats, void* workspace,
                                size_t workspace_bytes, nsrl_device_status* status, void* stream);
 
+/* The transformer block over HOST buffers (pinned host memory for the
+ * overlap): the batch runs in chunks of `chunk` sequences, and the copy in of
+ * chunk i+1, the block of chunk i and the copy out of chunk i-1 overlap (two
+ * library-owned copy streams per device and thread).  The call is complete on
+ * `stream` when y_host holds the output.  No counterpart in the reference
+ * (its blocks read host memory); it is nsrl_prenorm_transformer_block for a
+ * caller whose activations live on the host.  Workspace:
+ * nsrl_transformer_block_host_workspace_size(chunk, ...). */
+size_t nsrl_transformer_block_host_workspace_size(size_t chunk, size_t seq_len, size_t d_model, size_t heads,
+                                                  size_t hidden_dim);
+nsrl_status nsrl_prenorm_transformer_block_host(const int16_t* x_host, size_t batch, size_t chunk, size_t seq_len,
+                                                size_t d_model, size_t heads, size_t hidden_dim,
+                                                const int16_t* attn_gamma, const int16_t* mlp_gamma, uint64_t rms_eps,
+                                                const nsrl_linear_params* q, const nsrl_linear_params* k,
+                                                const nsrl_linear_params* v, const nsrl_linear_params* o,
+                                                const nsrl_linear_params* up, const nsrl_linear_params* gate,
+                                                const nsrl_linear_params* down, int16_t* y_host, void* workspace,
+                                                size_t workspace_bytes, nsrl_device_status* status, void* stream);
+
 /* ------------------------------------------------------------ profiling --
  * Per-launch CUDA-event timing of the library's own kernels (no counterpart
  * in the reference, whose only timer is a wall clock around the block loop,

@@ -289,14 +289,18 @@ __global__ void __launch_bounds__(128) attn_bwd_q_kernel(const QArgs a) {
             const bool live = rl && kk <= r && kk < S;
             int out = 0;
             if (live) {
-              const long long raw =
-                  (long long)s_hh[j][i] * 65536 + (long long)s_mid[j][i] * 256 + (long long)s_ll[j][i];
-              const long long dp = sat_i16(rhu64(raw, 15));
+              // dP = sat(rhu(65536 hh + rm, 15)) with rm = 256 mid + ll (|rm| < 2^31 for
+              // head_dim <= 64): 65536 hh is a multiple of 2^15, so the rounded shift is
+              // 2 hh + ((rm + 2^14) >> 15), all in i32 (|hh| <= 2^20).
+              const int rm = s_mid[j][i] * 256 + s_ll[j][i];
+              const int dp = sat16(2 * s_hh[j][i] + ((rm + 16384) >> 15));
               neg |= pv[e] < 0;
               if (pass == 0) {
-                wsum[hf] += dp * (long long)pv[e];
+                wsum[hf] += (long long)(dp * pv[e]);  // |dp * p| <= 2^30
               } else {
-                out = sat_i16(rhu64((long long)pv[e] * (dp - wq[hf]) * 22713ll, 30));
+                // P (dP - wq) 22713 = (22713 P) (dP - wq): 22713 P < 2^30, |dP - wq| < 2^18
+                const long long prod = (long long)(pv[e] * 22713) * (long long)(dp - (int)wq[hf]);
+                out = sat16((int)((prod + (1ll << 29)) >> 30));
               }
             }
             dl[hf][2 * j + e] = out;
@@ -474,6 +478,133 @@ __global__ void __launch_bounds__(128) attn_bwd_kv_kernel(const KVArgs a) {
     }
 }
 
+// attn_bwd_kv_kernel for S % 16 == 0 with 16-byte staging prefetched one
+// tile ahead into registers (double-buffered shared memory), and 8 warps for
+// head_dim 64: warp w owns keys 16 (w & 3) .. +15 and dims 32 (w >> 2) .. +31,
+// so each warp keeps 48 accumulator registers instead of 96.
+template <int HD>
+__global__ void __launch_bounds__(HD == 64 ? 256 : 128) attn_bwd_kv2_kernel(const KVArgs a) {
+  constexpr int WN = HD < 32 ? HD : 32;  // dims per warp
+  constexpr int NT = WN / 8;
+  constexpr int NTHREADS = 128 * (HD / WN);
+  constexpr int ASTR = 48;
+  constexpr int MWORDS = BQ * 2;        // 16-byte words of one M^T tile plane (64 keys x 32 q)
+  constexpr int XWORDS = HD * 2;        // of one X^T tile plane
+  constexpr int WORDS = 2 * (MWORDS + XWORDS);
+  constexpr int PER = (WORDS + NTHREADS - 1) / NTHREADS;
+  __shared__ __align__(16) uint8_t buf[2][2 * (BQ + HD) * ASTR];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int k0 = blockIdx.x * BQ, h = blockIdx.y, b = blockIdx.z;
+  const int S = a.S;
+  const long long row0 = (long long)b * S;
+  const long long bh = (long long)b * a.H + h;
+  const int kw = k0 + (warp & 3) * 16;
+  const int d0 = (warp >> 2) * WN;
+  int acc_hh[NT][4], acc_mid[NT][4], acc_ll[NT][4];
+#pragma unroll
+  for (int n = 0; n < NT; ++n)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc_hh[n][i] = acc_mid[n][i] = acc_ll[n][i] = 0;
+
+  // word e of a tile: [M^T hi | M^T lo | X^T hi | X^T lo], two 16-byte words per row
+  auto load_tile = [&](int tq, uint4 (&r)[PER]) {
+#pragma unroll
+    for (int z = 0; z < PER; ++z) {
+      const int e = tid + z * NTHREADS;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (e < WORDS) {
+        const int part = e < 2 * MWORDS ? 0 : 1;
+        const int ee = part == 0 ? e : e - 2 * MWORDS;
+        const int pw = part == 0 ? MWORDS : XWORDS;
+        const int plane = ee / pw, w = ee % pw;
+        const int row = w >> 1, half = 16 * (w & 1);
+        const int q = tq + half;
+        if (q < S) {
+          if (part == 0) {
+            if (k0 + row < S) {
+              const long long off = (bh * S + k0 + row) * (long long)S + q;
+              v = plane ? *reinterpret_cast<const uint4*>(a.mt_lo + off) : *reinterpret_cast<const uint4*>(a.mt_hi + off);
+            }
+          } else {
+            const long long off = (bh * HD + row) * (long long)S + q;
+            v = plane ? *reinterpret_cast<const uint4*>(a.xt_lo + off) : *reinterpret_cast<const uint4*>(a.xt_hi + off);
+          }
+        }
+      }
+      r[z] = v;
+    }
+  };
+  auto store_tile = [&](int sb, const uint4 (&r)[PER]) {
+#pragma unroll
+    for (int z = 0; z < PER; ++z) {
+      const int e = tid + z * NTHREADS;
+      if (e >= WORDS) continue;
+      const int part = e < 2 * MWORDS ? 0 : 1;
+      const int ee = part == 0 ? e : e - 2 * MWORDS;
+      const int pw = part == 0 ? MWORDS : XWORDS;
+      const int plane = ee / pw, w = ee % pw;
+      const int row = w >> 1, half = 16 * (w & 1);
+      // layout: at_hi [BQ][ASTR], at_lo, xt_hi [HD][ASTR], xt_lo
+      const int base = part == 0 ? plane * BQ * ASTR : 2 * BQ * ASTR + plane * HD * ASTR;
+      *reinterpret_cast<uint4*>(&buf[sb][base + row * ASTR + half]) = r[z];
+    }
+  };
+
+  uint4 pre[PER];
+  load_tile(k0, pre);
+  store_tile(0, pre);
+  __syncthreads();
+  int sb = 0;
+  for (int tq = k0; tq < S; tq += BK, sb ^= 1) {
+    const bool more = tq + BK < S;
+    if (more) load_tile(tq + BK, pre);  // in flight during the MMAs below
+    if (kw < S && tq + BK - 1 >= kw) {
+      const uint8_t* at_hi = &buf[sb][0];
+      const uint8_t* at_lo = &buf[sb][BQ * ASTR];
+      const uint8_t* xt_hi = &buf[sb][2 * BQ * ASTR];
+      const uint8_t* xt_lo = &buf[sb][2 * BQ * ASTR + HD * ASTR];
+      uint32_t ah[4], al[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int kr = (warp & 3) * 16 + g + ((i & 1) ? 8 : 0);
+        const int qc = 4 * t + ((i & 2) ? 16 : 0);
+        ah[i] = lds32b(at_hi + kr * ASTR + qc);
+        al[i] = lds32b(at_lo + kr * ASTR + qc);
+      }
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        const uint8_t* xh = xt_hi + (d0 + 8 * n + g) * ASTR + 4 * t;
+        const uint8_t* xl = xt_lo + (d0 + 8 * n + g) * ASTR + 4 * t;
+        const uint32_t bh0 = lds32b(xh), bh1 = lds32b(xh + 16), bl0 = lds32b(xl), bl1 = lds32b(xl + 16);
+        bmma_ss(acc_hh[n], ah, bh0, bh1);
+        bmma_su(acc_mid[n], ah, bl0, bl1);
+        bmma_us(acc_mid[n], al, bh0, bh1);
+        bmma_uu(acc_ll[n], al, bl0, bl1);
+      }
+    }
+    if (more) store_tile(sb ^ 1, pre);
+    __syncthreads();
+  }
+#pragma unroll
+  for (int n = 0; n < NT; ++n)
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      const int kr = kw + g + (hf ? 8 : 0);
+      if (kr >= S) continue;
+      int v[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int i = 2 * hf + e;
+        const long long tot =
+            (long long)acc_hh[n][i] * 65536 + (long long)acc_mid[n][i] * 256 + (long long)acc_ll[n][i];
+        v[e] = sat_i16(rhu64(tot, (uint32_t)a.shift));
+      }
+      *reinterpret_cast<uint32_t*>(a.out + (row0 + kr) * a.ldo + (long long)h * HD + d0 + 8 * n + 2 * t) =
+          (uint32_t)(v[0] & 0xFFFF) | ((uint32_t)v[1] << 16);
+    }
+}
+
 }  // namespace
 
 size_t attention_backward_tc_scratch_bytes(size_t B, size_t S, size_t d, size_t H) {
@@ -563,7 +694,15 @@ cudaError_t launch_attention_backward_tc(const int16_t* q, const int16_t* k, con
   KVArgs va{pth, ptl, cth, ctl, (int)S, (int)H, 15, dv, (long long)d};
   ProfScope prof("attention_bwd_kv", s, 2.0 * 2.0 * (double)hd * pairs,
                  2.0 * 2.0 * (double)B * H * S * S + 8.0 * (double)B * S * d);
-  if (hd == 64) {
+  if (S % 16 == 0) {  // 16-byte staging of the M^T and X^T rows
+    if (hd == 64) {
+      attn_bwd_kv2_kernel<64><<<grid, 256, 0, s>>>(ka);
+      attn_bwd_kv2_kernel<64><<<grid, 256, 0, s>>>(va);
+    } else {
+      attn_bwd_kv2_kernel<16><<<grid, 128, 0, s>>>(ka);
+      attn_bwd_kv2_kernel<16><<<grid, 128, 0, s>>>(va);
+    }
+  } else if (hd == 64) {
     attn_bwd_kv_kernel<64><<<grid, 128, 0, s>>>(ka);
     attn_bwd_kv_kernel<64><<<grid, 128, 0, s>>>(va);
   } else {

@@ -5,6 +5,8 @@
 #include <cstdio>
 #include <cstring>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "internal.h"
 
@@ -458,6 +460,106 @@ nsrl_status nsrl_prenorm_transformer_block(const int16_t* x, size_t batch, size_
   if (r != NSRL_OK) return r;
   c.off = mark;  // the MLP block reuses the attention scratch
   return mlp_block(h, T, d_model, hidden_dim, mlp_gamma, rms_eps, up_p, gate, down, y, c, status, s);
+}
+
+// ---- transformer block over host buffers: chunked copy / compute overlap ----
+namespace {
+struct HostPipe {
+  int device = -1;
+  cudaStream_t h2d = nullptr, d2h = nullptr;
+  cudaEvent_t in[2], comp[2], out[2], done;
+  bool ok = false;
+};
+
+HostPipe* host_pipe() {
+  static thread_local HostPipe p;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  if (p.ok && p.device == dev) return &p;
+  p = HostPipe{};
+  p.device = dev;
+  if (cudaStreamCreateWithFlags(&p.h2d, cudaStreamNonBlocking) != cudaSuccess) return nullptr;
+  if (cudaStreamCreateWithFlags(&p.d2h, cudaStreamNonBlocking) != cudaSuccess) return nullptr;
+  for (int b = 0; b < 2; ++b)
+    if (cudaEventCreateWithFlags(&p.in[b], cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&p.comp[b], cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&p.out[b], cudaEventDisableTiming) != cudaSuccess)
+      return nullptr;
+  if (cudaEventCreateWithFlags(&p.done, cudaEventDisableTiming) != cudaSuccess) return nullptr;
+  p.ok = true;
+  return &p;
+}
+}  // namespace
+
+size_t nsrl_transformer_block_host_workspace_size(size_t chunk, size_t seq_len, size_t d_model, size_t heads,
+                                                  size_t hidden_dim) {
+  if (heads == 0 || chunk == 0) return 0;
+  return 4 * up(chunk * seq_len * d_model * sizeof(int16_t)) +
+         nsrl_transformer_block_workspace_size(chunk, seq_len, d_model, heads, hidden_dim);
+}
+
+nsrl_status nsrl_prenorm_transformer_block_host(const int16_t* x_host, size_t batch, size_t chunk, size_t seq_len,
+                                                size_t d_model, size_t heads, size_t hidden_dim,
+                                                const int16_t* attn_gamma, const int16_t* mlp_gamma, uint64_t rms_eps,
+                                                const nsrl_linear_params* q, const nsrl_linear_params* k,
+                                                const nsrl_linear_params* v, const nsrl_linear_params* o,
+                                                const nsrl_linear_params* up_p, const nsrl_linear_params* gate,
+                                                const nsrl_linear_params* down, int16_t* y_host, void* workspace,
+                                                size_t workspace_bytes, nsrl_device_status* status, void* stream) {
+  if (chunk == 0 || !x_host || !y_host) return shape_fail("chunk must be nonzero, host buffers non-NULL");
+  if (batch == 0) return NSRL_OK;
+  if (chunk > batch) chunk = batch;
+  if (!workspace ||
+      workspace_bytes < nsrl_transformer_block_host_workspace_size(chunk, seq_len, d_model, heads, hidden_dim))
+    return shape_fail("workspace too small");
+  HostPipe* pp = host_pipe();
+  if (!pp) return cuda_fail(cudaGetLastError(), "copy streams");
+  HostPipe& P = *pp;
+  cudaStream_t s = (cudaStream_t)stream;
+  const size_t elems = chunk * seq_len * d_model;
+  Carver c(workspace);
+  int16_t* xd[2] = {c.take<int16_t>(elems), c.take<int16_t>(elems)};
+  int16_t* yd[2] = {c.take<int16_t>(elems), c.take<int16_t>(elems)};
+  void* bws = static_cast<uint8_t*>(workspace) + c.off;
+  const size_t bws_bytes = workspace_bytes - c.off;
+  const size_t n = (batch + chunk - 1) / chunk;
+  const size_t row = seq_len * d_model;
+  // the copies may start once the caller's earlier work on `stream` is done
+  NSRL_TRY(cudaEventRecord(P.done, s), "event");
+  NSRL_TRY(cudaStreamWaitEvent(P.h2d, P.done, 0), "event");
+  NSRL_TRY(cudaStreamWaitEvent(P.d2h, P.done, 0), "event");
+  auto h2d = [&](size_t i) -> nsrl_status {
+    const int b = (int)(i & 1);
+    const size_t nb = std::min(chunk, batch - i * chunk);
+    if (i >= 2) NSRL_TRY(cudaStreamWaitEvent(P.h2d, P.comp[b], 0), "event");  // x[b] free
+    NSRL_TRY(cudaMemcpyAsync(xd[b], x_host + i * chunk * row, nb * row * sizeof(int16_t), cudaMemcpyHostToDevice,
+                             P.h2d),
+             "copy in");
+    NSRL_TRY(cudaEventRecord(P.in[b], P.h2d), "event");
+    return NSRL_OK;
+  };
+  nsrl_status r = h2d(0);
+  if (r != NSRL_OK) return r;
+  for (size_t i = 0; i < n; ++i) {
+    const int b = (int)(i & 1);
+    const size_t nb = std::min(chunk, batch - i * chunk);
+    if (i + 1 < n && (r = h2d(i + 1)) != NSRL_OK) return r;
+    NSRL_TRY(cudaStreamWaitEvent(s, P.in[b], 0), "event");
+    if (i >= 2) NSRL_TRY(cudaStreamWaitEvent(s, P.out[b], 0), "event");  // y[b] copied out
+    r = nsrl_prenorm_transformer_block(xd[b], nb, seq_len, d_model, heads, hidden_dim, attn_gamma, mlp_gamma, rms_eps,
+                                       q, k, v, o, up_p, gate, down, yd[b], bws, bws_bytes, status, stream);
+    if (r != NSRL_OK) return r;
+    NSRL_TRY(cudaEventRecord(P.comp[b], s), "event");
+    NSRL_TRY(cudaStreamWaitEvent(P.d2h, P.comp[b], 0), "event");
+    NSRL_TRY(cudaMemcpyAsync(y_host + i * chunk * row, yd[b], nb * row * sizeof(int16_t), cudaMemcpyDeviceToHost,
+                             P.d2h),
+             "copy out");
+    NSRL_TRY(cudaEventRecord(P.out[b], P.d2h), "event");
+  }
+  // the call is complete on `stream` once the last copy out has landed
+  NSRL_TRY(cudaEventRecord(P.done, P.d2h), "event");
+  NSRL_TRY(cudaStreamWaitEvent(s, P.done, 0), "event");
+  return NSRL_OK;
 }
 
 size_t nsrl_decode_block_workspace_size(size_t batch, size_t d_model, size_t heads) {
