@@ -66,6 +66,10 @@ def lib():
         L.nsrl_prenorm_transformer_block.argtypes = [vp, sz, sz, sz, sz, sz, vp, vp, C.c_uint64, lp, lp, lp, lp, lp,
                                                      lp, lp, vp, vp, sz, vp, vp]
         L.nsrl_attention_decode.argtypes = [vp, vp, vp, vp, sz, sz, sz, sz, vp, vp, vp]
+        L.nsrl_transformer_block_host_workspace_size.restype = sz
+        L.nsrl_transformer_block_host_workspace_size.argtypes = [sz, sz, sz, sz, sz]
+        L.nsrl_prenorm_transformer_block_host.argtypes = [vp, sz, sz, sz, sz, sz, sz, vp, vp, C.c_uint64, lp, lp, lp,
+                                                          lp, lp, lp, lp, vp, vp, sz, vp, vp]
         L.nsrl_profile_enable.argtypes = [C.c_int]
         L.nsrl_profile_count.restype = sz
         _lib = L
@@ -259,6 +263,19 @@ class TransformerBlock:
             _ptr(x), batch, seq_len, self.d_model, self.heads, self.hidden_dim, _ptr(self.attn_gamma),
             _ptr(self.mlp_gamma), self.rms_eps, *[C.byref(p) for p in self._ps], _ptr(y), _ptr(ws), ws.numel(),
             _ptr(status.buf), stream if stream is not None else _stream())
+
+    def host_workspace_bytes(self, chunk, seq_len):
+        return lib().nsrl_transformer_block_host_workspace_size(chunk, seq_len, self.d_model, self.heads,
+                                                                self.hidden_dim)
+
+    def launch_host(self, x_host, y_host, batch, seq_len, chunk, ws, status: Status, stream=None) -> int:
+        """Enqueues the block over pinned host tensors x_host -> y_host in chunks of
+        `chunk` sequences, copies overlapping compute; returns the C status code."""
+        return lib().nsrl_prenorm_transformer_block_host(
+            C.c_void_p(x_host.data_ptr()), batch, chunk, seq_len, self.d_model, self.heads, self.hidden_dim,
+            _ptr(self.attn_gamma), _ptr(self.mlp_gamma), self.rms_eps, *[C.byref(p) for p in self._ps],
+            C.c_void_p(y_host.data_ptr()), _ptr(ws), ws.numel(), _ptr(status.buf),
+            stream if stream is not None else _stream())
 
     def __call__(self, x, batch, seq_len):
         """Returns (y, attention saturations, mlp saturations) or None."""

@@ -27,7 +27,11 @@ def test_header_declares_entry_points():
     names = declared()
     for n in ("nsrl_linear_i16_i8_i16", "nsrl_rms_norm_rows", "nsrl_self_attention",
               "nsrl_prenorm_attention_residual_block", "nsrl_prenorm_gated_mlp_residual_block",
-              "nsrl_prenorm_transformer_block", "nsrl_attention_decode", "nsrl_status_fetch"):
+              "nsrl_prenorm_transformer_block", "nsrl_attention_decode", "nsrl_status_fetch",
+              "nsrl_linear_backward_input", "nsrl_gated_mlp_backward_input", "nsrl_rms_norm_backward_rows",
+              "nsrl_attention_with_probabilities", "nsrl_attention_backward", "nsrl_train_windows",
+              "nsrl_accumulate_weight_gradient_i16", "nsrl_apply_embedding_gradient_i64_to_i16",
+              "nsrl_prenorm_transformer_block_host"):
         assert n in names
 
 
@@ -82,3 +86,35 @@ def test_shape_validation_matches_reference_none(lib):
     assert r == 1
     lib.nsrl_last_error.restype = C.c_char_p
     assert b"invalid shape" in lib.nsrl_last_error()
+
+
+def test_training_step_shape_rules(lib):
+    """nsrl_train_windows validates the model on the host (no launch): head_dim a
+    power of four and 16 or 64, RMS gammas in every layer or none, [256][d] head."""
+    from nsrl_b200.core import LinearParamsC as LP
+    from nsrl_b200.train import _TrainLayerC, _TrainModelC
+    lib.nsrl_train_workspace_size.restype = C.c_size_t
+    lib.nsrl_train_workspace_size.argtypes = [C.c_void_p, C.c_size_t]
+    lib.nsrl_train_arena_len.restype = C.c_size_t
+    lib.nsrl_train_arena_len.argtypes = [C.c_void_p]
+
+    def model(d, H, F, L, S, gammas=(True, True)):
+        arr = (_TrainLayerC * L)()
+        for i in range(L):
+            arr[i].attn_gamma = 16 if gammas[0] else None
+            arr[i].mlp_gamma = 16 if gammas[1] else None
+            dims = [(d, d)] * 4 + [(d, F), (d, F), (F, d)]
+            for j, (inp, out) in enumerate(dims):
+                arr[i].lin[j] = LP(16, None, 16, inp, out)
+        m = _TrainModelC(d, H, F, L, S, 16, 16, C.cast(arr, C.c_void_p), LP(16, None, 16, d, 256))
+        m._keep = arr
+        return m
+
+    good = model(256, 4, 1024, 4, 512)
+    assert lib.nsrl_train_workspace_size(C.byref(good), 256) > 0
+    # arena: head, per layer 4 d^2 + 3 d F + 2 d, embeddings, positions
+    assert lib.nsrl_train_arena_len(C.byref(good)) == 256 * 256 + 4 * (4 * 65536 + 3 * 262144 + 512) + 65536 + 512 * 256
+    for bad in (model(128, 4, 256, 2, 8),            # head_dim 32: not a power of four
+                model(256, 1, 1024, 2, 8),           # head_dim 256: not taken by the training step
+                model(64, 4, 128, 2, 8, (True, False))):  # RMS gammas: both or neither
+        assert lib.nsrl_train_workspace_size(C.byref(bad), 4) == 0

@@ -225,6 +225,30 @@ def test_transformer_block_parity(core):
     assert np.array_equal(host(out[0]), y2) and out[1] == s1 and out[2] == s2
 
 
+@pytest.mark.parametrize("B,chunk", [(5, 2), (3, 3), (4, 8)])
+def test_transformer_block_host_buffers(core, B, chunk):
+    """The host-buffer block (chunked copy / compute overlap, a ragged last chunk)
+    equals the oracle, saturation counts included."""
+    import torch
+    S, d, H, F = 128, 128, 2, 512
+    bw = Y.BlockWeights(8, d, F)
+    P = {nm: lin_pair(core, getattr(bw, nm), bw.shift[nm]) for nm in ("q", "k", "v", "o", "up", "gate", "down")}
+    x = Y.q15_gaussian(4, (B * S, d))
+    y1, s1 = O.prenorm_attention_block(x, B, S, d, H, bw.attn_gamma, 1, *[P[n][0] for n in "qkvo"], threads=4)
+    y2, s2 = O.prenorm_mlp_block(y1, B * S, d, F, bw.mlp_gamma, 1, P["up"][0], P["gate"][0], P["down"][0], threads=4)
+    tb = core.TransformerBlock(d, H, F, *[P[n][1] for n in ("q", "k", "v", "o", "up", "gate", "down")],
+                               dev(bw.attn_gamma), dev(bw.mlp_gamma), 1)
+    xh = torch.from_numpy(x).pin_memory()
+    yh = torch.zeros_like(xh).pin_memory()
+    ws = core.workspace(tb.host_workspace_bytes(min(chunk, B), S))
+    st = core.Status()
+    st.reset()
+    assert tb.launch_host(xh, yh, B, S, chunk, ws, st) == 0
+    code, h = st.fetch()
+    assert code == 0
+    assert np.array_equal(yh.numpy(), y2) and h.attention_saturations == s1 and h.mlp_saturations == s2
+
+
 # ----------------------------------------------------------------- decode ---
 @pytest.mark.parametrize("B,H,hd,Lmax", [(3, 2, 64, 300), (4, 4, 16, 129), (2, 1, 256, 70), (2, 3, 4, 50)])
 def test_decode_attention_parity(core, B, H, hd, Lmax):
