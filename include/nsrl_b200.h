@@ -232,6 +232,34 @@ nsrl_status nsrl_apply_embedding_gradient_i64_to_i16(const long long* accumulato
                                                      uint8_t learning_rate_shift, unsigned long long* stats,
                                                      nsrl_device_status* status, void* stream);
 
+/* Integer Adam (crates/nsrl-train-core/src/lib.rs:276-661): IntegerAdamConfig
+ * with beta1 = 1 - 2^-beta1_decay_shift, beta2 = 1 - 2^-beta2_decay_shift. */
+typedef struct nsrl_integer_adam_config {
+  int32_t learning_rate;
+  uint8_t step_shift;
+  uint8_t beta1_decay_shift;
+  uint8_t beta2_decay_shift;
+  uint8_t pad;
+  uint64_t epsilon;
+} nsrl_integer_adam_config;
+
+/* apply_integer_adam_accumulators_i64_to_i8 / _to_i16 (lib.rs:469-593): per
+ * entry g = round_div(acc, count), the moments and the carried residual
+ * advance (integer_adam_delta, :602-661), the weight moves by the rounded
+ * update with saturation.  Device arrays: moments, residuals [len], *step
+ * (uint64, +1 per call with a nonzero count), stats (3 uint64, added to):
+ * {saturations, zero deltas, sum |delta|}.  The accumulators are read only. */
+nsrl_status nsrl_apply_integer_adam_i64_to_i8(const long long* accumulators, const unsigned long long* sample_count,
+                                              int8_t* weights, size_t len, const nsrl_integer_adam_config* config,
+                                              long long* first_moments, unsigned long long* second_moments,
+                                              long long* update_residuals, unsigned long long* step,
+                                              unsigned long long* stats, nsrl_device_status* status, void* stream);
+nsrl_status nsrl_apply_integer_adam_i64_to_i16(const long long* accumulators, const unsigned long long* sample_count,
+                                               int16_t* weights, size_t len, const nsrl_integer_adam_config* config,
+                                               long long* first_moments, unsigned long long* second_moments,
+                                               long long* update_residuals, unsigned long long* step,
+                                               unsigned long long* stats, nsrl_device_status* status, void* stream);
+
 /* ---------------------------------------------------- training backward --
  * Backward-input linear over rows: dx[m][k] = requantize_i64_to_i16(
  * sum_n g'[m][n] * W[n][k], grad_input_scales[k]) with g' = rhu(g * mult_n,

@@ -293,6 +293,136 @@ __global__ void apply_embedding_kernel(const long long* __restrict__ acc, long l
   }
 }
 
+// ---------------------------------------------------------- integer Adam --
+// crates/nsrl-train-core/src/lib.rs:602-661 (integer_adam_delta) with the
+// reference's i128 intermediates as __int128.  Returns false on a rejection.
+struct AdamCfg {
+  int lr;
+  int step_shift, b1, b2;
+  unsigned long long eps;
+};
+
+__device__ __forceinline__ bool rhu128_i64(__int128 v, int s, long long& out) {
+  if (s) v += (__int128)1 << (s - 1);  // |v| < 2^127 - 2^61 here: no overflow
+  v >>= s;
+  if (v < (__int128)LLONG_MIN || v > (__int128)LLONG_MAX) return false;
+  out = (long long)v;
+  return true;
+}
+
+__device__ __forceinline__ bool adam_delta(long long g, const AdamCfg& c, long long& m1, unsigned long long& m2,
+                                           long long& res, long long& delta, bool& sat) {
+  const long long lim = 2147483647ll;
+  const long long bg = g < -lim ? -lim : (g > lim ? lim : g);
+  sat = bg != g;
+  // |m1| < 2^63 and 2^b1 - 1 < 2^62: the product stays below 2^125
+  if (!rhu128_i64((__int128)m1 * (((__int128)1 << c.b1) - 1) + bg, c.b1, m1)) return false;
+  __int128 n2 = (__int128)m2 * (((__int128)1 << c.b2) - 1) + (__int128)bg * bg;  // < 2^126 + 2^62
+  if (c.b2) n2 += (__int128)1 << (c.b2 - 1);
+  n2 >>= c.b2;
+  if (n2 < 0 || n2 > (__int128)0xFFFFFFFFFFFFFFFFull) return false;
+  m2 = (unsigned long long)n2;
+  const unsigned long long var = m2 + c.eps;
+  if (var < m2) return false;  // u64 overflow: the reference's checked_add
+  const long long inv = rsqrt_q30(var);
+  long long n15;
+  if (!rhu128_i64((__int128)m1 * inv, 15, n15)) return false;
+  n15 = n15 < -32767 ? -32767 : (n15 > 32767 ? 32767 : n15);
+  long long num;
+  if (mul_ovf(n15, (long long)c.lr, num) || add_ovf(num, res, num)) return false;
+  const int eff = 15 + c.step_shift;
+  const long long scaled = rhu64(num, (uint32_t)eff);
+  const __int128 r = (__int128)num - ((__int128)scaled << eff);
+  if (r < (__int128)LLONG_MIN || r > (__int128)LLONG_MAX) return false;
+  res = (long long)r;
+  delta = -scaled;
+  return true;
+}
+
+// apply_integer_adam_accumulators_i64_to_i8 / _to_i16 (lib.rs:469-593):
+// weights W (int8 or int16) clamped to [lo, hi]; stats added to; the step
+// advances once per call with a nonzero sample count.
+template <class W>
+__global__ void adam_kernel(const long long* __restrict__ acc, const unsigned long long* count_p, W* __restrict__ w,
+                            long long len, AdamCfg c, long long* __restrict__ m1, unsigned long long* __restrict__ m2,
+                            long long* __restrict__ res, unsigned long long* step, unsigned long long* stats, int lo,
+                            int hi, nsrl_device_status* st) {
+  const unsigned long long count = *count_p;
+  if (count == 0) return;
+  if (count > (unsigned long long)LLONG_MAX) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) nsrl_flag(st, NSRL_FLAG_LINEAR_OVERFLOW);
+    return;
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) atomicAdd(step, 1ull);
+  const long long den = (long long)count;
+  unsigned long long sat = 0, zero = 0, l1 = 0;
+  bool bad = false;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < len; i += (long long)gridDim.x * blockDim.x) {
+    long long g, a = m1[i], r = res[i], delta;
+    unsigned long long b = m2[i];
+    bool gs;
+    if (!round_div(acc[i], den, g) || !adam_delta(g, c, a, b, r, delta, gs)) {
+      bad = true;
+      continue;
+    }
+    sat += gs;
+    zero += delta == 0;
+    const long long prev = w[i];
+    long long un;
+    if (add_ovf(prev, delta, un)) {
+      bad = true;
+      continue;
+    }
+    const long long cl = un < lo ? lo : (un > hi ? hi : un);
+    if (cl != un) {
+      ++sat;
+      r = 0;
+    }
+    l1 += (unsigned long long)(cl > prev ? cl - prev : prev - cl);
+    w[i] = (W)cl;
+    m1[i] = a;
+    m2[i] = b;
+    res[i] = r;
+  }
+  if (bad) nsrl_flag(st, NSRL_FLAG_LINEAR_OVERFLOW);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    sat += __shfl_xor_sync(0xffffffffu, sat, o);
+    zero += __shfl_xor_sync(0xffffffffu, zero, o);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    if (sat) atomicAdd(&stats[0], sat);
+    if (zero) atomicAdd(&stats[1], zero);
+    if (l1) atomicAdd(&stats[2], l1);
+  }
+}
+
+template <class W>
+nsrl_status launch_adam(const long long* acc, const unsigned long long* count, W* w, size_t len,
+                        const nsrl_integer_adam_config* cfg, long long* m1, unsigned long long* m2, long long* res,
+                        unsigned long long* step, unsigned long long* stats, int lo, int hi, nsrl_device_status* st,
+                        void* stream, const char* name) {
+  // lib.rs:299-309 (is_valid) and the shape rule of :476-478
+  if (!cfg || cfg->learning_rate <= 0 || cfg->beta1_decay_shift == 0 || cfg->beta2_decay_shift == 0 ||
+      cfg->beta1_decay_shift > 62 || cfg->beta2_decay_shift > 62 || cfg->step_shift > 62 - 15 || cfg->epsilon == 0 ||
+      len == 0 || !acc || !count || !w || !m1 || !m2 || !res || !step || !stats || !st) {
+    set_error("invalid config or shape: integer Adam");
+    return NSRL_INVALID_SHAPE;
+  }
+  AdamCfg c{cfg->learning_rate, cfg->step_shift, cfg->beta1_decay_shift, cfg->beta2_decay_shift, cfg->epsilon};
+  cudaStream_t s = (cudaStream_t)stream;
+  const unsigned blocks = (unsigned)std::min<size_t>((len + 255) / 256, 148 * 8);
+  ProfScope prof(name, s, 0.0, (8.0 + 8.0 + 8.0 + 8.0 + 8.0 + 8.0 + 2.0 * sizeof(W)) * (double)len);
+  adam_kernel<W><<<blocks, 256, 0, s>>>(acc, count, w, (long long)len, c, m1, m2, res, step, stats, lo, hi, st);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("integer Adam: %s", cudaGetErrorString(e));
+    return NSRL_CUDA_ERROR;
+  }
+  return NSRL_OK;
+}
+
 }  // namespace
 }  // namespace nsrl
 
@@ -383,6 +513,24 @@ nsrl_status nsrl_apply_linear_weight_gradient_i64_to_i8(long long* accumulators,
     return NSRL_CUDA_ERROR;
   }
   return NSRL_OK;
+}
+
+nsrl_status nsrl_apply_integer_adam_i64_to_i8(const long long* accumulators, const unsigned long long* sample_count,
+                                              int8_t* weights, size_t len, const nsrl_integer_adam_config* config,
+                                              long long* first_moments, unsigned long long* second_moments,
+                                              long long* update_residuals, unsigned long long* step,
+                                              unsigned long long* stats, nsrl_device_status* status, void* stream) {
+  return launch_adam(accumulators, sample_count, weights, len, config, first_moments, second_moments,
+                     update_residuals, step, stats, -128, 127, status, stream, "integer_adam_i8");
+}
+
+nsrl_status nsrl_apply_integer_adam_i64_to_i16(const long long* accumulators, const unsigned long long* sample_count,
+                                               int16_t* weights, size_t len, const nsrl_integer_adam_config* config,
+                                               long long* first_moments, unsigned long long* second_moments,
+                                               long long* update_residuals, unsigned long long* step,
+                                               unsigned long long* stats, nsrl_device_status* status, void* stream) {
+  return launch_adam(accumulators, sample_count, weights, len, config, first_moments, second_moments,
+                     update_residuals, step, stats, -32768, 32767, status, stream, "integer_adam_i16");
 }
 
 nsrl_status nsrl_apply_embedding_gradient_i64_to_i16(const long long* accumulators, long long* residuals,

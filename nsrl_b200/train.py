@@ -612,3 +612,50 @@ def accumulate_weight_gradient_i16(x: torch.Tensor, grad_output: torch.Tensor, s
                                               core._ptr(accumulators), core._ptr(sample_count), core._ptr(ws),
                                               ws.numel(), core._ptr(st.buf), core._stream())
     return _run_status(r, st)
+
+
+# ------------------------------------------------------------ integer Adam --
+class IntegerAdamConfigC(C.Structure):
+    """IntegerAdamConfig (nsrl-train-core/src/lib.rs:279-297) with the reference defaults."""
+    _fields_ = [("learning_rate", C.c_int32), ("step_shift", C.c_uint8), ("beta1_decay_shift", C.c_uint8),
+                ("beta2_decay_shift", C.c_uint8), ("pad", C.c_uint8), ("epsilon", C.c_uint64)]
+
+    def __init__(self, learning_rate=1, step_shift=4, beta1_decay_shift=3, beta2_decay_shift=7, epsilon=1):
+        super().__init__(learning_rate, step_shift, beta1_decay_shift, beta2_decay_shift, 0, epsilon)
+
+
+class IntegerAdamState:
+    """IntegerAdamStateWorkspace on the device: step, moments, update residuals."""
+
+    def __init__(self, n, device=None):
+        dev = device if device is not None else core._dev()
+        self.step = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.first_moments = torch.zeros(n, dtype=torch.int64, device=dev)
+        self.second_moments = torch.zeros(n, dtype=torch.int64, device=dev)  # holds u64
+        self.update_residuals = torch.zeros(n, dtype=torch.int64, device=dev)
+
+
+def apply_integer_adam_accumulators(accumulators: torch.Tensor, sample_count: torch.Tensor, weights: torch.Tensor,
+                                    config: IntegerAdamConfigC, state: IntegerAdamState) -> Optional[dict]:
+    """apply_integer_adam_accumulators_i64_to_i8 / _to_i16 (lib.rs:469-593) on device
+    tensors (weights int8 or int16): the stats dict, or None on a rejection."""
+    L = _lib()
+    if not getattr(L, "_adam_bound", False):
+        vp, sz = C.c_void_p, C.c_size_t
+        for fn in (L.nsrl_apply_integer_adam_i64_to_i8, L.nsrl_apply_integer_adam_i64_to_i16):
+            fn.argtypes = [vp, vp, vp, sz, C.POINTER(IntegerAdamConfigC), vp, vp, vp, vp, vp, vp, vp]
+        L._adam_bound = True
+    fn = L.nsrl_apply_integer_adam_i64_to_i8 if weights.dtype == torch.int8 else L.nsrl_apply_integer_adam_i64_to_i16
+    stats = torch.zeros(3, dtype=torch.int64, device=weights.device)
+    st = core.Status()
+    r = fn(core._ptr(accumulators), core._ptr(sample_count), core._ptr(weights), weights.numel(), C.byref(config),
+           core._ptr(state.first_moments), core._ptr(state.second_moments), core._ptr(state.update_residuals),
+           core._ptr(state.step), core._ptr(stats), core._ptr(st.buf), core._stream())
+    if r == core.NSRL_INVALID_SHAPE:
+        raise ValueError(L.nsrl_last_error().decode())
+    core._check(r)
+    code, _ = st.fetch()
+    if code != core.NSRL_OK:
+        return None
+    s = stats.cpu().tolist()
+    return {"gradient_saturation_count": s[0], "zero_delta_count": s[1], "weight_delta_l1": s[2]}

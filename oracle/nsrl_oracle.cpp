@@ -1410,3 +1410,118 @@ int orc_apply_embedding_gradient_i64_to_i16(const int64_t* acc, int64_t* residua
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------ integer Adam --
+// crates/nsrl-train-core/src/lib.rs:276-310 (config), :469-661 (apply and delta).
+namespace orc {
+
+struct AdamConfig {
+  int32_t learning_rate;
+  uint8_t step_shift, beta1_decay_shift, beta2_decay_shift, pad;
+  uint64_t epsilon;
+};
+
+static bool adam_valid(const AdamConfig& c) {  // lib.rs:299-309
+  return c.learning_rate > 0 && c.beta1_decay_shift > 0 && c.beta2_decay_shift > 0 &&
+         c.beta1_decay_shift <= MAX_RIGHT_SHIFT && c.beta2_decay_shift <= MAX_RIGHT_SHIFT &&
+         c.step_shift <= MAX_RIGHT_SHIFT - Q15_SHIFT && c.epsilon > 0;
+}
+
+// lib.rs:663-679
+static bool rhu128(__int128 v, uint8_t s, __int128* out) {
+  if (s == 0) {
+    *out = v;
+    return true;
+  }
+  const __int128 off = (__int128)1 << (s - 1);
+  const __int128 lim = ~((__int128)1 << 127);
+  if (v > lim - off) return false;
+  *out = (v + off) >> s;
+  return true;
+}
+static bool rhu128_i64(__int128 v, uint8_t s, int64_t* out) {
+  __int128 r;
+  if (!rhu128(v, s, &r) || r < INT64_MIN || r > INT64_MAX) return false;
+  *out = (int64_t)r;
+  return true;
+}
+
+// lib.rs:602-661
+static bool adam_delta(int64_t g, const AdamConfig& c, int64_t* m1, uint64_t* m2, int64_t* res, int64_t* delta,
+                       bool* sat) {
+  const int64_t lim = INT32_MAX;
+  const int64_t bg = std::clamp<int64_t>(g, -lim, lim);
+  *sat = bg != g;
+  const __int128 b1 = (__int128)1 << c.beta1_decay_shift;
+  if (!rhu128_i64((__int128)*m1 * (b1 - 1) + bg, c.beta1_decay_shift, m1)) return false;
+  const __int128 sq = (__int128)bg * bg;
+  const __int128 b2 = (__int128)1 << c.beta2_decay_shift;
+  __int128 n2;
+  if (!rhu128((__int128)*m2 * (b2 - 1) + sq, c.beta2_decay_shift, &n2)) return false;
+  if (n2 < 0 || n2 > (__int128)UINT64_MAX) return false;
+  *m2 = (uint64_t)n2;
+  uint64_t var;
+  if (__builtin_add_overflow(*m2, c.epsilon, &var)) return false;
+  int64_t inv;
+  if (!integer_rsqrt_q30(var, &inv)) return false;
+  int64_t n15;
+  if (!rhu128_i64((__int128)*m1 * inv, Q15_SHIFT, &n15)) return false;
+  n15 = std::clamp<int64_t>(n15, -32767, 32767);
+  int64_t num;
+  if (__builtin_mul_overflow(n15, (int64_t)c.learning_rate, &num)) return false;
+  if (__builtin_add_overflow(num, *res, &num)) return false;
+  const uint8_t eff = Q15_SHIFT + c.step_shift;
+  const int64_t scaled = rhu(num, eff);
+  const __int128 r = (__int128)num - ((__int128)scaled << eff);
+  if (r < INT64_MIN || r > INT64_MAX) return false;
+  *res = (int64_t)r;
+  *delta = -scaled;
+  return true;
+}
+
+template <class W>
+static int adam_apply(const int64_t* acc, uint64_t count, W* w, size_t len, const AdamConfig& c, int64_t* m1,
+                      uint64_t* m2, int64_t* res, uint64_t* step, uint64_t* stats, int64_t lo, int64_t hi) {
+  stats[0] = stats[1] = stats[2] = 0;
+  if (!adam_valid(c)) return 1;
+  if (count == 0) return 0;
+  if (count > (uint64_t)INT64_MAX) return 1;
+  for (size_t i = 0; i < len; ++i) {
+    int64_t g;
+    if (!round_ratio_i64(acc[i], (int64_t)count, &g)) return 2;
+    int64_t delta;
+    bool sat;
+    if (!adam_delta(g, c, &m1[i], &m2[i], &res[i], &delta, &sat)) return 2;
+    if (sat) stats[0] += 1;
+    if (delta == 0) stats[1] += 1;
+    int64_t un;
+    if (__builtin_add_overflow((int64_t)w[i], delta, &un)) return 2;
+    const int64_t cl = std::clamp<int64_t>(un, lo, hi);
+    if (cl != un) {
+      stats[0] += 1;
+      res[i] = 0;
+    }
+    const int64_t ad = cl - (int64_t)w[i];
+    stats[2] += (uint64_t)(ad < 0 ? -ad : ad);
+    w[i] = (W)cl;
+  }
+  *step += 1;
+  return 0;
+}
+
+}  // namespace orc
+
+extern "C" {
+
+// apply_integer_adam_accumulators_i64_to_i8 / _to_i16 (lib.rs:469-593):
+// 0 = ok, 1 = invalid config, 2 = rejected.  stats = {saturations, zero deltas, sum |delta|}.
+int orc_integer_adam_i8(const int64_t* acc, uint64_t count, int8_t* w, size_t len, const AdamConfig* c, int64_t* m1,
+                        uint64_t* m2, int64_t* res, uint64_t* step, uint64_t* stats) {
+  return adam_apply(acc, count, w, len, *c, m1, m2, res, step, stats, -128, 127);
+}
+int orc_integer_adam_i16(const int64_t* acc, uint64_t count, int16_t* w, size_t len, const AdamConfig* c, int64_t* m1,
+                         uint64_t* m2, int64_t* res, uint64_t* step, uint64_t* stats) {
+  return adam_apply(acc, count, w, len, *c, m1, m2, res, step, stats, -32768, 32767);
+}
+
+}  // extern "C"

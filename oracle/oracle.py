@@ -525,3 +525,38 @@ def train_step(model: TrainModel, residuals, contexts, targets, cfg=None, worker
     stats = dict(stats)
     stats.update({"gradient_saturation_count": tot[0], "zero_delta_count": tot[1], "weight_delta_l1": tot[2]})
     return stats
+
+
+# --------------------------------------------------------- integer Adam --
+class AdamConfig(C.Structure):
+    """IntegerAdamConfig (nsrl-train-core/src/lib.rs:279-297); defaults lr 1, step 4, beta shifts 3 / 7, eps 1."""
+    _fields_ = [("learning_rate", C.c_int32), ("step_shift", C.c_uint8), ("beta1_decay_shift", C.c_uint8),
+                ("beta2_decay_shift", C.c_uint8), ("pad", C.c_uint8), ("epsilon", C.c_uint64)]
+
+    def __init__(self, learning_rate=1, step_shift=4, beta1_decay_shift=3, beta2_decay_shift=7, epsilon=1):
+        super().__init__(learning_rate, step_shift, beta1_decay_shift, beta2_decay_shift, 0, epsilon)
+
+
+class AdamState:
+    """IntegerAdamStateWorkspace: step, first / second moments, update residuals (numpy)."""
+
+    def __init__(self, n):
+        self.step = 0
+        self.first = np.zeros(n, np.int64)
+        self.second = np.zeros(n, np.uint64)
+        self.residuals = np.zeros(n, np.int64)
+
+
+def integer_adam(acc, count, weights, cfg: AdamConfig, state: AdamState):
+    """apply_integer_adam_accumulators_i64_to_i8 / _to_i16 in place on `weights`
+    (int8 or int16 numpy); returns the stats list, or None on a rejection."""
+    a = _c(acc, np.int64)
+    stats = np.zeros(3, np.uint64)
+    st = C.c_uint64(state.step)
+    fn = lib().orc_integer_adam_i8 if weights.dtype == np.int8 else lib().orc_integer_adam_i16
+    r = fn(_p(a), C.c_uint64(int(count)), _p(weights), C.c_size_t(weights.size), C.byref(cfg), _p(state.first),
+           _p(state.second), _p(state.residuals), C.byref(st), _p(stats))
+    if r:
+        return None
+    state.step = st.value
+    return [int(s) for s in stats]

@@ -118,3 +118,16 @@ def test_training_step_shape_rules(lib):
                 model(256, 1, 1024, 2, 8),           # head_dim 256: not taken by the training step
                 model(64, 4, 128, 2, 8, (True, False))):  # RMS gammas: both or neither
         assert lib.nsrl_train_workspace_size(C.byref(bad), 4) == 0
+
+
+def test_integer_adam_config_rules(lib):
+    """IntegerAdamConfig::is_valid (nsrl-train-core/src/lib.rs:299-309) is checked on the host."""
+    from nsrl_b200.train import IntegerAdamConfigC
+    f = lib.nsrl_apply_integer_adam_i64_to_i8
+    f.argtypes = [C.c_void_p] * 4 + [C.POINTER(IntegerAdamConfigC)] + [C.c_void_p] * 7
+    f.argtypes[3] = C.c_size_t
+    p = C.c_void_p(16)
+    for bad in (IntegerAdamConfigC(learning_rate=0), IntegerAdamConfigC(beta1_decay_shift=0),
+                IntegerAdamConfigC(beta2_decay_shift=63), IntegerAdamConfigC(step_shift=48),
+                IntegerAdamConfigC(epsilon=0)):
+        assert f(p, p, p, 4, C.byref(bad), p, p, p, p, p, p, None) == 1

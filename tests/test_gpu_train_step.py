@@ -240,3 +240,33 @@ def test_weight_gradient_tensor_cores_extreme_values():
         assert train.accumulate_weight_gradient_i16(x, g, core.make_scales(1, 0, N), acc, cnt)
         assert bool((acc == rows * gv * xv).all()), (gv, xv)
         del x, g, acc
+
+
+@pytest.mark.parametrize("wdtype,count", [(np.int8, 3), (np.int16, 7), (np.int8, 1)])
+def test_integer_adam_matches_oracle(wdtype, count):
+    """Five steps of integer Adam over random and extreme accumulators, moments,
+    residuals, weights and stats, against the oracle."""
+    _, train = _core()
+    rng = np.random.default_rng(count)
+    n = 3000
+    info = np.iinfo(wdtype)
+    w = rng.integers(info.min, info.max + 1, n).astype(wdtype)
+    cfg_o = O.AdamConfig(learning_rate=3, step_shift=2, beta1_decay_shift=3, beta2_decay_shift=7, epsilon=1)
+    cfg_g = train.IntegerAdamConfigC(learning_rate=3, step_shift=2, beta1_decay_shift=3, beta2_decay_shift=7,
+                                     epsilon=1)
+    so = O.AdamState(n)
+    sg = train.IntegerAdamState(n)
+    wg = torch.from_numpy(w.copy()).cuda()
+    cnt = torch.tensor([count], dtype=torch.int64, device="cuda")
+    for step in range(5):
+        acc = rng.integers(-2**40, 2**40, n).astype(np.int64)
+        acc[:4] = [2**62, -2**62, 0, 2**33]  # the first two saturate the moment gradient
+        ref = O.integer_adam(acc, count, w, cfg_o, so)
+        got = train.apply_integer_adam_accumulators(torch.from_numpy(acc).cuda(), cnt, wg, cfg_g, sg)
+        assert ref is not None and got is not None
+        assert [got["gradient_saturation_count"], got["zero_delta_count"], got["weight_delta_l1"]] == ref
+        assert np.array_equal(wg.cpu().numpy(), w)
+        assert np.array_equal(sg.first_moments.cpu().numpy(), so.first)
+        assert np.array_equal(sg.second_moments.cpu().numpy().view(np.uint64), so.second)
+        assert np.array_equal(sg.update_residuals.cpu().numpy(), so.residuals)
+        assert int(sg.step.item()) == so.step == step + 1

@@ -138,3 +138,54 @@ def test_block_forward_cache_matches_prenorm_blocks(rms, pos):
         y1, _ = O.prenorm_attention_block(x, 1, S, d, H, ly["attn_gamma"], 1, ly["q"], ly["k"], ly["v"], ly["o"])
         y2, _ = O.prenorm_mlp_block(y1, S, d, F, ly["mlp_gamma"], 1, ly["up"], ly["gate"], ly["down"])
         assert np.array_equal(out, y2)
+
+
+def test_integer_adam_zero_gradient_keeps_weights_and_advances_state():  # nsrl-train-core lib.rs:1950-1977
+    w = np.array([7, -9], np.int8)
+    s = O.AdamState(2)
+    st = O.integer_adam(np.zeros(2, np.int64), 1, w, O.AdamConfig(), s)
+    assert list(w) == [7, -9] and s.step == 1 and not s.first.any() and not s.second.any()
+    assert st[1] == 2 and st[2] == 0
+
+
+def test_integer_adam_constant_gradient_moves_in_descent_direction():  # lib.rs:1980-2016
+    w = np.array([10, -10], np.int8)
+    s = O.AdamState(2)
+    for _ in range(4):
+        assert O.integer_adam(np.array([1024, -1024]), 1, w, O.AdamConfig(step_shift=0), s) is not None
+    assert w[0] < 10 and w[1] > -10 and s.step == 4
+    assert s.first[0] > 0 and s.first[1] < 0 and (s.second > 0).all()
+
+
+def test_integer_adam_carries_sub_i8_updates():  # lib.rs:2018-2057
+    w = np.array([10], np.int8)
+    s = O.AdamState(1)
+    st = O.integer_adam(np.array([4096]), 1, w, O.AdamConfig(step_shift=4), s)
+    assert list(w) == [10] and st[1] == 1 and s.residuals[0] != 0
+    for _ in range(20):
+        O.integer_adam(np.array([4096]), 1, w, O.AdamConfig(step_shift=4), s)
+    assert w[0] < 10
+
+
+def test_integer_adam_reports_gradient_and_weight_saturation():  # lib.rs:2059-2089
+    w = np.array([-128], np.int8)
+    s = O.AdamState(1)
+    st = O.integer_adam(np.array([2**63 - 1]), 1, w, O.AdamConfig(step_shift=0), s)
+    assert list(w) == [-128] and st[0] >= 2 and s.residuals[0] == 0
+
+
+def test_integer_adam_i16_path_is_deterministic():  # lib.rs:2091-2120
+    def run():
+        w = np.array([100, -100, 0], np.int16)
+        s = O.AdamState(3)
+        for _ in range(12):
+            O.integer_adam(np.array([500, -750, 125]), 2, w, O.AdamConfig(), s)
+        return w.copy(), s.first.copy(), s.second.copy()
+    a, b = run(), run()
+    assert all(np.array_equal(x, y) for x, y in zip(a, b))
+
+
+def test_integer_adam_rejects_invalid_config():  # lib.rs:299-309
+    w = np.zeros(1, np.int8)
+    assert O.integer_adam(np.zeros(1), 1, w, O.AdamConfig(beta1_decay_shift=0), O.AdamState(1)) is None
+    assert O.integer_adam(np.zeros(1), 1, w, O.AdamConfig(step_shift=48), O.AdamState(1)) is None
