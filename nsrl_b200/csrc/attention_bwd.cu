@@ -10,11 +10,11 @@
 // product |mid| <= 65280 and ll <= 65025, so the sums are exact for up to
 // 32768 terms (seq_len <= 16384, head_dim <= 64).
 //
-// attn_bwd_q_kernel: one CTA of 4 warps per 64 query rows.  Pass 1 forms dP
-//   tile by tile and the row sums sum_j dP P; pass 2 forms dP again, then dL
-//   (written to global for the key side) and dQ += dL K, dL entering the MMA
-//   as A fragments straight from the dP accumulator layout (K^T is staged in
-//   the matching key order).
+// attn_bwd_dl_kernel: one CTA of 4 warps per 64 query rows.  Pass 1 forms
+//   dP tile by tile and the row sums sum_j dP P; pass 2 turns the stored dP
+//   into dL in place (written to global for the dQ and key-side products).
+// attn_bwd_dq_kernel: dQ += dL K with the A fragments taken straight from the
+//   dL rows (K^T is staged in the matching key order).
 // attn_bwd_kv_kernel: one CTA per 64 keys; dK (A = dL^T) or dV (A = P^T)
 //   over the query tiles at or after the keys, operands staged transposed as
 //   byte planes in shared memory.
@@ -105,8 +105,106 @@ __global__ void __launch_bounds__(256) head_transpose_kernel(const int16_t* __re
   }
 }
 
+// head_transpose_kernel<64> with 16-byte loads and stores (ld % 8 == 0,
+// Sp % 16 == 0): the 64 x 64 tile is kept as 32-bit words (two dims) with the
+// word index XORed by 8 ((s / 16) mod 4); each thread gathers 16 positions of
+// one dim pair.  With perm, position p of a 32-key block reads key
+// bkey_inv(p), which stays inside the same 16-row group.
+__global__ void __launch_bounds__(128) head_transpose16_kernel(const int16_t* __restrict__ x, long long ld, int S,
+                                                               int Sp, int H, bool perm, int8_t* __restrict__ th,
+                                                               uint8_t* __restrict__ tl) {
+  constexpr int HD = 64;
+  __shared__ __align__(16) uint32_t tile[64 * 32];  // [s][dim pair ^ swizzle]
+  const int s0 = blockIdx.x * 64, h = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x;
+#pragma unroll
+  for (int z = 0; z < 4; ++z) {
+    const int e = tid + 128 * z;
+    const int r = e >> 3, c8 = (e & 7) * 8;
+    uint4 u = make_uint4(0, 0, 0, 0);
+    if (s0 + r < S) u = *reinterpret_cast<const uint4*>(x + ((long long)b * S + s0 + r) * ld + (long long)h * HD + c8);
+    *reinterpret_cast<uint4*>(&tile[r * 32 + ((c8 >> 1) ^ (((r >> 4) & 3) << 3))]) = u;
+  }
+  __syncthreads();
+  const int dw = tid >> 2;        // dim pair 0..31
+  const int pb = (tid & 3) * 16;  // positions s0 + pb .. +15
+  const int wc = dw ^ (((pb >> 4) & 3) << 3);
+  if (s0 + pb >= Sp) return;
+  uint32_t hi[2][4], lo[2][4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint32_t w[4];
+#pragma unroll
+    for (int z = 0; z < 4; ++z) {
+      const int pl = pb + 4 * q + z;
+      const int src = perm ? (pl & ~31) + bkey_inv(pl & 31) : pl;
+      w[z] = tile[src * 32 + wc];
+    }
+    const uint32_t ah = __byte_perm(w[0], w[1], 0x7531), bh = __byte_perm(w[2], w[3], 0x7531);
+    const uint32_t al = __byte_perm(w[0], w[1], 0x6420), bl = __byte_perm(w[2], w[3], 0x6420);
+    hi[0][q] = __byte_perm(ah, bh, 0x6420);
+    hi[1][q] = __byte_perm(ah, bh, 0x7531);
+    lo[0][q] = __byte_perm(al, bl, 0x6420);
+    lo[1][q] = __byte_perm(al, bl, 0x7531);
+  }
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    const long long off = (((long long)b * H + h) * HD + 2 * dw + e) * Sp + s0 + pb;
+    *reinterpret_cast<uint4*>(th + off) = make_uint4(hi[e][0], hi[e][1], hi[e][2], hi[e][3]);
+    *reinterpret_cast<uint4*>(tl + off) = make_uint4(lo[e][0], lo[e][1], lo[e][2], lo[e][3]);
+  }
+}
+
 // M [BH][S][S] int16 -> MT byte planes, MT[bh][j][i] = M[bh][i][j], for the
-// tiles with i-tile >= j-tile (the causal part the key side reads).
+// 64 x 64 tiles with i-tile >= j-tile (the causal part the key side reads),
+// S % 16 == 0.  16-byte loads of eight j into shared memory, kept as 32-bit
+// words (two j) with the word index XORed by 8 ((i / 16) mod 4) so that the
+// column reads are conflict-free; each thread then gathers 16 i of one j pair
+// and writes 16-byte words of both planes for both j.
+__global__ void __launch_bounds__(128) sq_transpose16_kernel(const int16_t* __restrict__ M, int S,
+                                                             int8_t* __restrict__ th, uint8_t* __restrict__ tl) {
+  const int j0 = blockIdx.x * 64, i0 = blockIdx.y * 64;
+  if (i0 + 63 < j0) return;
+  __shared__ __align__(16) uint32_t tile[64 * 32];  // [i][j pair ^ swizzle]
+  const long long base = (long long)blockIdx.z * S * S;
+  const int tid = threadIdx.x;
+#pragma unroll
+  for (int z = 0; z < 4; ++z) {
+    const int e = tid + 128 * z;
+    const int r = e >> 3, j8 = (e & 7) * 8;
+    uint4 u = make_uint4(0, 0, 0, 0);
+    if (i0 + r < S && j0 + j8 < S)  // S % 16 == 0: all eight j are inside
+      u = *reinterpret_cast<const uint4*>(M + base + (long long)(i0 + r) * S + j0 + j8);
+    *reinterpret_cast<uint4*>(&tile[r * 32 + ((j8 >> 1) ^ (((r >> 4) & 3) << 3))]) = u;
+  }
+  __syncthreads();
+  const int jw = tid >> 2;        // j pair 0..31
+  const int ib = (tid & 3) * 16;  // i rows ib .. ib + 15
+  const int wc = jw ^ (((ib >> 4) & 3) << 3);
+  uint32_t hi[2][4], lo[2][4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint32_t w0 = tile[(ib + 4 * q) * 32 + wc], w1 = tile[(ib + 4 * q + 1) * 32 + wc];
+    const uint32_t w2 = tile[(ib + 4 * q + 2) * 32 + wc], w3 = tile[(ib + 4 * q + 3) * 32 + wc];
+    const uint32_t ah = __byte_perm(w0, w1, 0x7531), bh = __byte_perm(w2, w3, 0x7531);
+    const uint32_t al = __byte_perm(w0, w1, 0x6420), bl = __byte_perm(w2, w3, 0x6420);
+    hi[0][q] = __byte_perm(ah, bh, 0x6420);
+    hi[1][q] = __byte_perm(ah, bh, 0x7531);
+    lo[0][q] = __byte_perm(al, bl, 0x6420);
+    lo[1][q] = __byte_perm(al, bl, 0x7531);
+  }
+  if (i0 + ib >= S) return;
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    const int j = j0 + 2 * jw + e;
+    if (j >= S) continue;
+    const long long off = base + (long long)j * S + i0 + ib;
+    *reinterpret_cast<uint4*>(th + off) = make_uint4(hi[e][0], hi[e][1], hi[e][2], hi[e][3]);
+    *reinterpret_cast<uint4*>(tl + off) = make_uint4(lo[e][0], lo[e][1], lo[e][2], lo[e][3]);
+  }
+}
+
+// The same for S % 4 == 0: 64 x 64 tiles, 8-byte loads, 4-byte stores.
 __global__ void __launch_bounds__(256) sq_transpose_kernel(const int16_t* __restrict__ M, int S,
                                                            int8_t* __restrict__ th, uint8_t* __restrict__ tl) {
   const int j0 = blockIdx.x * 64, i0 = blockIdx.y * 64;
@@ -144,39 +242,32 @@ __global__ void __launch_bounds__(256) sq_transpose_kernel(const int16_t* __rest
 }
 
 // ---------------------------------------------------------------- query side --
-struct QArgs {
+struct DlArgs {
   const int16_t* dC;
   long long ldc;
-  const int8_t* v_hi;   // V planes [T][d]
+  const int8_t* v_hi;  // V planes [T][d]
   const uint8_t* v_lo;
   int d;
-  const int8_t* kt_hi;  // K^T planes [B][H][HD][Sp], MMA key order per 32-key block
-  const uint8_t* kt_lo;
-  int Sp;
   const int16_t* P;
-  int S, H, shift;
-  int16_t* dL;
-  int16_t* dQ;
-  long long ldo;
+  int S, H;
+  int16_t* dL;  // [BH][S][S]: dP after the first pass, dL after the second
   nsrl_device_status* st;
 };
 
+// attn_bwd_dl_kernel: one CTA of 4 warps per 64 query rows.  Pass 1 forms dP
+// tile by tile on the tensor cores (V staged 16 bytes at a time, prefetched a
+// tile ahead into double-buffered shared memory), stores it into the dL
+// buffer and sums dP P per row; pass 2 reads back the values each lane stored
+// (its own writes, so no barrier) and turns them into dL in place.  Every key
+// below min(S, end of the block) is written, zeros above the diagonal, so the
+// causal 64 x 64 tiles the key side reads need no clearing.
 template <int HD>
-struct QSmem {
-  static constexpr int KSTR = HD == 16 ? 48 : HD + 16;
-  static constexpr int VSTR = 48;
-  uint8_t v_hi[BK * KSTR];
-  uint8_t v_lo[BK * KSTR];
-  uint8_t kt_hi[HD * VSTR];
-  uint8_t kt_lo[HD * VSTR];
-};
-
-template <int HD>
-__global__ void __launch_bounds__(128) attn_bwd_q_kernel(const QArgs a) {
+__global__ void __launch_bounds__(128, 5) attn_bwd_dl_kernel(const DlArgs a) {
   constexpr int KC = HD >= 32 ? HD / 32 : 1;
-  constexpr int NT = HD / 8;
-  __shared__ __align__(16) QSmem<HD> sm;
-  constexpr int KSTR = QSmem<HD>::KSTR, VSTR = QSmem<HD>::VSTR;
+  constexpr int KSTR = HD == 16 ? 48 : HD + 16;  // bytes per staged V row
+  constexpr int VW = BK * (HD / 16);            // 16-byte words of one V plane tile
+  constexpr int PER = (2 * VW + 127) / 128;
+  __shared__ __align__(16) uint8_t vbuf[2][2][BK * KSTR];  // [stage][plane]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t = lane & 3;
   const int q0 = blockIdx.x * BQ, h = blockIdx.y, b = blockIdx.z;
@@ -186,7 +277,6 @@ __global__ void __launch_bounds__(128) attn_bwd_q_kernel(const QArgs a) {
   const int r0 = qw + g, r1 = r0 + 8;
   const int16_t* Pbh = a.P + ((long long)b * a.H + h) * S * (long long)S;
   int16_t* dLbh = a.dL + ((long long)b * a.H + h) * S * (long long)S;
-  const long long ktb = ((long long)b * a.H + h) * HD * (long long)a.Sp;
 
   // A fragments of dC rows r0 / r1 (k = dims)
   uint32_t ca_hi[KC][4], ca_lo[KC][4];
@@ -204,157 +294,274 @@ __global__ void __launch_bounds__(128) attn_bwd_q_kernel(const QArgs a) {
       ca_hi[c][i] = hv;
       ca_lo[c][i] = lv;
     }
-  if (HD == 16) {  // the k half past the head's 16 dims is zero in every V row
-    for (int i = tid; i < BK; i += 128) {
-      *reinterpret_cast<uint4*>(&sm.v_hi[i * KSTR + 16]) = make_uint4(0, 0, 0, 0);
-      *reinterpret_cast<uint4*>(&sm.v_lo[i * KSTR + 16]) = make_uint4(0, 0, 0, 0);
+  if (HD == 16) {  // the k half past the head's 16 dims (A is zero there too)
+    for (int i = tid; i < 2 * 2 * BK; i += 128) {
+      const int st = i / (2 * BK), pl = (i / BK) & 1, j = i % BK;
+      *reinterpret_cast<uint4*>(&vbuf[st][pl][j * KSTR + 16]) = make_uint4(0, 0, 0, 0);
     }
   }
 
   const int kend = min(S, q0 + BQ);  // keys visited by this CTA (causal)
   const int ntiles = (kend + BK - 1) / BK;
   const int wlast = min(qw + 15, S - 1);
-  long long wsum[2] = {0, 0}, wq[2] = {0, 0};
-  int dq_hh[NT][4], dq_mid[NT][4], dq_ll[NT][4];
-#pragma unroll
-  for (int n = 0; n < NT; ++n)
-#pragma unroll
-    for (int i = 0; i < 4; ++i) dq_hh[n][i] = dq_mid[n][i] = dq_ll[n][i] = 0;
-  bool neg = false;
 
-  for (int pass = 0; pass < 2; ++pass) {
-    for (int kt = 0; kt < ntiles; ++kt) {
-      const int kb = kt * BK;
-      __syncthreads();
-      // V rows [key][dim]: 16-byte copies of the planes
-      for (int i = tid; i < BK * (HD / 16); i += 128) {
-        const int j = i / (HD / 16), c16 = 16 * (i % (HD / 16));
-        const int key = kb + j;
-        uint4 vh = make_uint4(0, 0, 0, 0), vl = vh;
+  // word e: plane e / VW, key row (e % VW) / (HD / 16), 16-byte column
+  auto load_tile = [&](int kb, uint4 (&r)[PER]) {
+#pragma unroll
+    for (int z = 0; z < PER; ++z) {
+      const int e = tid + z * 128;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (e < 2 * VW) {
+        const int pl = e / VW, w = e % VW;
+        const int key = kb + w / (HD / 16), c16 = 16 * (w % (HD / 16));
         if (key < kend) {
           const long long off = (row0 + key) * a.d + (long long)h * HD + c16;
-          vh = *reinterpret_cast<const uint4*>(a.v_hi + off);
-          vl = *reinterpret_cast<const uint4*>(a.v_lo + off);
-        }
-        *reinterpret_cast<uint4*>(&sm.v_hi[j * KSTR + c16]) = vh;
-        *reinterpret_cast<uint4*>(&sm.v_lo[j * KSTR + c16]) = vl;
-      }
-      if (pass == 1) {  // K^T [dim][32 key slots]: two 16-byte copies per dim and plane
-        for (int i = tid; i < HD * 2; i += 128) {
-          const int dim = i >> 1, half = 16 * (i & 1);
-          const long long off = ktb + (long long)dim * a.Sp + kb + half;
-          *reinterpret_cast<uint4*>(&sm.kt_hi[dim * VSTR + half]) = *reinterpret_cast<const uint4*>(a.kt_hi + off);
-          *reinterpret_cast<uint4*>(&sm.kt_lo[dim * VSTR + half]) = *reinterpret_cast<const uint4*>(a.kt_lo + off);
+          v = pl ? *reinterpret_cast<const uint4*>(a.v_lo + off) : *reinterpret_cast<const uint4*>(a.v_hi + off);
         }
       }
-      __syncthreads();
-      if (kb > wlast || qw >= S) continue;  // fully masked for this warp
+      r[z] = v;
+    }
+  };
+  auto store_tile = [&](int sb, const uint4 (&r)[PER]) {
+#pragma unroll
+    for (int z = 0; z < PER; ++z) {
+      const int e = tid + z * 128;
+      if (e >= 2 * VW) continue;
+      const int pl = e / VW, w = e % VW;
+      *reinterpret_cast<uint4*>(&vbuf[sb][pl][(w / (HD / 16)) * KSTR + 16 * (w % (HD / 16))]) = r[z];
+    }
+  };
 
-      // dP raw sums for 16 rows x 32 keys
-      int s_hh[4][4], s_mid[4][4], s_ll[4][4];
+  long long wsum[2] = {0, 0};
+  bool neg = false;
+  {
+    uint4 pre[PER];
+    load_tile(0, pre);
+    store_tile(0, pre);
+    __syncthreads();
+  }
+  for (int kt = 0; kt < ntiles; ++kt) {
+    const int kb = kt * BK, sb = kt & 1;
+    const bool more = kt + 1 < ntiles;
+    uint4 pre[PER];
+    if (more) load_tile(kb + BK, pre);  // in flight during the MMAs below
+    // the probabilities of this tile: rows r0 / r1, key pairs kb + 8 j + 2 t
+    uint32_t pw[2][4];
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf)
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
+        const int r = hf ? r1 : r0, key = kb + 8 * j + 2 * t;
+        pw[hf][j] = (r < S && key < S) ? *reinterpret_cast<const uint32_t*>(Pbh + (long long)r * S + key) : 0u;
+      }
+    const bool active = qw < S && kb <= wlast;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) s_hh[j][i] = s_mid[j][i] = s_ll[j][i] = 0;
-        const uint8_t* vh = &sm.v_hi[(8 * j + g) * KSTR + 4 * t];
-        const uint8_t* vl = &sm.v_lo[(8 * j + g) * KSTR + 4 * t];
+    for (int j = 0; j < 4; ++j) {  // 8 keys at a time: dP raw sums for 16 rows x 8 keys, then their values
+      int s_hh[4] = {0, 0, 0, 0}, s_mid[4] = {0, 0, 0, 0}, s_ll[4] = {0, 0, 0, 0};
+      if (active) {
+        const uint8_t* vh = &vbuf[sb][0][(8 * j + g) * KSTR + 4 * t];
+        const uint8_t* vl = &vbuf[sb][1][(8 * j + g) * KSTR + 4 * t];
 #pragma unroll
         for (int c = 0; c < KC; ++c) {
           const uint32_t bh0 = lds32b(vh + 32 * c), bl0 = lds32b(vl + 32 * c);
           const uint32_t bh1 = lds32b(vh + 32 * c + 16), bl1 = lds32b(vl + 32 * c + 16);
-          bmma_ss(s_hh[j], ca_hi[c], bh0, bh1);
-          bmma_su(s_mid[j], ca_hi[c], bl0, bl1);
-          bmma_us(s_mid[j], ca_lo[c], bh0, bh1);
-          bmma_uu(s_ll[j], ca_lo[c], bl0, bl1);
+          bmma_ss(s_hh, ca_hi[c], bh0, bh1);
+          bmma_su(s_mid, ca_hi[c], bl0, bl1);
+          bmma_us(s_mid, ca_lo[c], bh0, bh1);
+          bmma_uu(s_ll, ca_lo[c], bl0, bl1);
         }
       }
-      int dl[2][8];
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {  // row r0 (hf 0) or r1 (hf 1): C elements 2 hf, 2 hf + 1
+        const int r = hf ? r1 : r0;
+        const int key = kb + 8 * j + 2 * t;
+        if (r >= S || key >= S) continue;  // S % 4 == 0: key + 1 < S as well
+        int dp[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int i = 2 * hf + e;
+          const int p = (int)(int16_t)(pw[hf][j] >> (16 * e));
+          dp[e] = 0;
+          if (key + e <= r) {
+            // dP = sat(rhu(65536 hh + rm, 15)) with rm = 256 mid + ll (|rm| < 2^31 for
+            // head_dim <= 64): 65536 hh is a multiple of 2^15, so the rounded shift is
+            // 2 hh + ((rm + 2^14) >> 15), all in i32 (|hh| <= 2^20).
+            const int rm = s_mid[i] * 256 + s_ll[i];
+            dp[e] = sat16(2 * s_hh[i] + ((rm + 16384) >> 15));
+            neg |= p < 0;
+            wsum[hf] += (long long)(dp[e] * p);  // |dP P| <= 2^30
+          }
+        }
+        *reinterpret_cast<uint32_t*>(dLbh + (long long)r * S + key) = (uint32_t)(dp[0] & 0xFFFF) | ((uint32_t)dp[1] << 16);
+      }
+    }
+    if (more) store_tile(sb ^ 1, pre);
+    __syncthreads();
+  }
+  int wq[2];
+#pragma unroll
+  for (int hf = 0; hf < 2; ++hf) {
+#pragma unroll
+    for (int o = 1; o <= 2; o <<= 1) wsum[hf] += __shfl_xor_sync(0xffffffffu, wsum[hf], o);
+    wq[hf] = (int)rhu64(wsum[hf], 15);
+  }
+  if (neg) nsrl_flag(a.st, NSRL_FLAG_LINEAR_OVERFLOW);  // a negative probability: the reference rejects
+  // pass 2: dL = sat(rhu(P (dP - wq) 22713, 30)) over the values this lane stored
+  if (qw >= S) return;
+  for (int kt = 0; kt < ntiles; ++kt) {
+    const int kb = kt * BK;
+    uint32_t pw[2][4], dw[2][4];
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf)
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-#pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {  // row r0 (hf 0) or r1 (hf 1): C elements 2 hf, 2 hf + 1
-          const int r = hf ? r1 : r0;
-          const int key = kb + 8 * j + 2 * t;
-          int pv[2] = {0, 0};
-          const bool rl = r < S;
-          if (rl && key < S) {  // the two probabilities of this pair of keys
-            const uint32_t u = *reinterpret_cast<const uint32_t*>(Pbh + (long long)r * S + key);
-            pv[0] = (int)(int16_t)(u & 0xFFFF);
-            pv[1] = (int)(int16_t)(u >> 16);
-          }
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int i = 2 * hf + e;
-            const int kk = key + e;
-            const bool live = rl && kk <= r && kk < S;
-            int out = 0;
-            if (live) {
-              // dP = sat(rhu(65536 hh + rm, 15)) with rm = 256 mid + ll (|rm| < 2^31 for
-              // head_dim <= 64): 65536 hh is a multiple of 2^15, so the rounded shift is
-              // 2 hh + ((rm + 2^14) >> 15), all in i32 (|hh| <= 2^20).
-              const int rm = s_mid[j][i] * 256 + s_ll[j][i];
-              const int dp = sat16(2 * s_hh[j][i] + ((rm + 16384) >> 15));
-              neg |= pv[e] < 0;
-              if (pass == 0) {
-                wsum[hf] += (long long)(dp * pv[e]);  // |dp * p| <= 2^30
-              } else {
-                // P (dP - wq) 22713 = (22713 P) (dP - wq): 22713 P < 2^30, |dP - wq| < 2^18
-                const long long prod = (long long)(pv[e] * 22713) * (long long)(dp - (int)wq[hf]);
-                out = sat16((int)((prod + (1ll << 29)) >> 30));
-              }
-            }
-            dl[hf][2 * j + e] = out;
-          }
-        }
+        const int r = hf ? r1 : r0, key = kb + 8 * j + 2 * t;
+        const bool in = r < S && key < S && key <= r;
+        pw[hf][j] = in ? *reinterpret_cast<const uint32_t*>(Pbh + (long long)r * S + key) : 0u;
+        dw[hf][j] = in ? *reinterpret_cast<const uint32_t*>(dLbh + (long long)r * S + key) : 0u;
       }
-      if (pass == 0) continue;
-      // dL to global (the key side reads it), then the dQ product
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
+    for (int hf = 0; hf < 2; ++hf)
 #pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          const int r = hf ? r1 : r0;
-          const int key = kb + 8 * j + 2 * t;
-          if (r < S && key < S)
-            *reinterpret_cast<uint32_t*>(dLbh + (long long)r * S + key) =
-                (uint32_t)(dl[hf][2 * j] & 0xFFFF) | ((uint32_t)dl[hf][2 * j + 1] << 16);
+      for (int j = 0; j < 4; ++j) {
+        const int r = hf ? r1 : r0, key = kb + 8 * j + 2 * t;
+        if (r >= S || key >= S || key > r) continue;  // zeros already there
+        int dl[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int p = (int)(int16_t)(pw[hf][j] >> (16 * e));
+          const int dp = (int)(int16_t)(dw[hf][j] >> (16 * e));
+          // P (dP - wq) 22713 = (22713 P) (dP - wq): |22713 P| < 2^30, |dP - wq| < 2^30
+          const long long prod = (long long)(p * 22713) * (long long)(dp - wq[hf]);
+          dl[e] = key + e <= r ? sat16((int)((prod + (1ll << 29)) >> 30)) : 0;
         }
+        *reinterpret_cast<uint32_t*>(dLbh + (long long)r * S + key) = (uint32_t)(dl[0] & 0xFFFF) | ((uint32_t)dl[1] << 16);
+      }
+  }
+}
+
+struct DqArgs {
+  const int8_t* kt_hi;  // K^T planes [B][H][HD][Sp], MMA key order per 32-key block
+  const uint8_t* kt_lo;
+  int Sp;
+  const int16_t* dL;  // [BH][S][S]
+  int S, H, shift;
+  int16_t* dQ;
+  long long ldo;
+};
+
+// dQ[t] = sat(rhu(sum_{j <= t} dL[t][j] K[j], shift)): one CTA per 64 query
+// rows; for head_dim 64, 8 warps, warp w owning rows 16 (w & 3) .. +15 and
+// dims 32 (w >> 2) .. +31.  The A fragments come straight from the dL rows
+// (two 4-byte key pairs per fragment register, matching the key order of the
+// K^T planes), prefetched a tile ahead; K^T is staged 16 bytes at a time into
+// double-buffered shared memory.
+template <int HD>
+__global__ void __launch_bounds__(HD == 64 ? 256 : 128) attn_bwd_dq_kernel(const DqArgs a) {
+  constexpr int WN = HD < 32 ? HD : 32;  // dims per warp
+  constexpr int NT = WN / 8;
+  constexpr int NTHREADS = 128 * (HD / WN);
+  constexpr int VSTR = 48;
+  constexpr int KW = HD * 2;  // 16-byte words of one K^T plane tile (HD dims x 32 slots)
+  constexpr int PER = (2 * KW + NTHREADS - 1) / NTHREADS;
+  __shared__ __align__(16) uint8_t kbuf[2][2][HD * VSTR];  // [stage][plane]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int q0 = blockIdx.x * BQ, h = blockIdx.y, b = blockIdx.z;
+  const int S = a.S;
+  const long long row0 = (long long)b * S;
+  const int qw = q0 + (warp & 3) * 16;
+  const int d0 = (warp >> 2) * WN;
+  const int r0 = qw + g, r1 = r0 + 8;
+  const long long ktb = ((long long)b * a.H + h) * HD * (long long)a.Sp;
+  const int16_t* dLbh = a.dL + ((long long)b * a.H + h) * S * (long long)S;
+  const int kend = min(S, q0 + BQ);
+  const int ntiles = (kend + BK - 1) / BK;
+  const int wlast = min(qw + 15, S - 1);
+
+  auto load_tile = [&](int kb, uint4 (&r)[PER]) {
+#pragma unroll
+    for (int z = 0; z < PER; ++z) {
+      const int e = tid + z * NTHREADS;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (e < 2 * KW) {
+        const int pl = e / KW, w = e % KW;
+        const long long off = ktb + (long long)(w >> 1) * a.Sp + kb + 16 * (w & 1);
+        v = pl ? *reinterpret_cast<const uint4*>(a.kt_lo + off) : *reinterpret_cast<const uint4*>(a.kt_hi + off);
+      }
+      r[z] = v;
+    }
+  };
+  auto store_tile = [&](int sb, const uint4 (&r)[PER]) {
+#pragma unroll
+    for (int z = 0; z < PER; ++z) {
+      const int e = tid + z * NTHREADS;
+      if (e >= 2 * KW) continue;
+      const int pl = e / KW, w = e % KW;
+      *reinterpret_cast<uint4*>(&kbuf[sb][pl][(w >> 1) * VSTR + 16 * (w & 1)]) = r[z];
+    }
+  };
+  // fragment register i: row (i & 1 ? r1 : r0), key pairs kb + 2t + (i & 2 ? 16 : 0) and + 8
+  auto load_dl = [&](int kb, uint32_t (&u)[4][2]) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = (i & 1) ? r1 : r0;
+      const int key = kb + 2 * t + ((i & 2) ? 16 : 0);
+#pragma unroll
+      for (int z = 0; z < 2; ++z) {
+        const int kk = key + 8 * z;
+        u[i][z] = (r < S && kk < S) ? *reinterpret_cast<const uint32_t*>(dLbh + (long long)r * S + kk) : 0u;
+      }
+    }
+  };
+
+  int acc_hh[NT][4], acc_mid[NT][4], acc_ll[NT][4];
+#pragma unroll
+  for (int n = 0; n < NT; ++n)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc_hh[n][i] = acc_mid[n][i] = acc_ll[n][i] = 0;
+  uint32_t du[4][2];
+  {
+    uint4 pre[PER];
+    load_tile(0, pre);
+    store_tile(0, pre);
+    load_dl(0, du);
+    __syncthreads();
+  }
+  for (int kt = 0; kt < ntiles; ++kt) {
+    const int kb = kt * BK, sb = kt & 1;
+    const bool more = kt + 1 < ntiles;
+    uint4 pre[PER];
+    uint32_t dn[4][2];
+    if (more) {
+      load_tile(kb + BK, pre);
+      load_dl(kb + BK, dn);
+    }
+    if (qw < S && kb <= wlast) {
       uint32_t ah[4], al[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int hf = i & 1;
-        const int base = (i & 2) ? 4 : 0;
-        uint32_t hv = 0, lv = 0;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int v = dl[hf][base + e];
-          hv |= (uint32_t)((v >> 8) & 255) << (8 * e);
-          lv |= (uint32_t)(v & 255) << (8 * e);
-        }
-        ah[i] = hv;
-        al[i] = lv;
+      for (int i = 0; i < 4; ++i) {  // the hi / lo bytes of the four int16 values
+        ah[i] = __byte_perm(du[i][0], du[i][1], 0x7531);
+        al[i] = __byte_perm(du[i][0], du[i][1], 0x6420);
       }
 #pragma unroll
       for (int n = 0; n < NT; ++n) {
-        const uint8_t* kh = &sm.kt_hi[(8 * n + g) * VSTR + 4 * t];
-        const uint8_t* kl = &sm.kt_lo[(8 * n + g) * VSTR + 4 * t];
+        const uint8_t* kh = &kbuf[sb][0][(d0 + 8 * n + g) * VSTR + 4 * t];
+        const uint8_t* kl = &kbuf[sb][1][(d0 + 8 * n + g) * VSTR + 4 * t];
         const uint32_t bh0 = lds32b(kh), bh1 = lds32b(kh + 16), bl0 = lds32b(kl), bl1 = lds32b(kl + 16);
-        bmma_ss(dq_hh[n], ah, bh0, bh1);
-        bmma_su(dq_mid[n], ah, bl0, bl1);
-        bmma_us(dq_mid[n], al, bh0, bh1);
-        bmma_uu(dq_ll[n], al, bl0, bl1);
+        bmma_ss(acc_hh[n], ah, bh0, bh1);
+        bmma_su(acc_mid[n], ah, bl0, bl1);
+        bmma_us(acc_mid[n], al, bh0, bh1);
+        bmma_uu(acc_ll[n], al, bl0, bl1);
       }
     }
-    if (pass == 0) {
+    if (more) {
+      store_tile(sb ^ 1, pre);
 #pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-#pragma unroll
-        for (int o = 1; o <= 2; o <<= 1) wsum[hf] += __shfl_xor_sync(0xffffffffu, wsum[hf], o);
-        wq[hf] = rhu64(wsum[hf], 15);
-      }
+      for (int i = 0; i < 4; ++i) du[i][0] = dn[i][0], du[i][1] = dn[i][1];
     }
+    __syncthreads();
   }
-  if (neg) nsrl_flag(a.st, NSRL_FLAG_LINEAR_OVERFLOW);  // a negative probability: the reference rejects
 #pragma unroll
   for (int n = 0; n < NT; ++n)
 #pragma unroll
@@ -365,10 +572,10 @@ __global__ void __launch_bounds__(128) attn_bwd_q_kernel(const QArgs a) {
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int i = 2 * hf + e;
-        const long long tot = (long long)dq_hh[n][i] * 65536 + (long long)dq_mid[n][i] * 256 + (long long)dq_ll[n][i];
+        const long long tot = (long long)acc_hh[n][i] * 65536 + (long long)acc_mid[n][i] * 256 + (long long)acc_ll[n][i];
         v[e] = sat_i16(rhu64(tot, (uint32_t)a.shift));
       }
-      *reinterpret_cast<uint32_t*>(a.dQ + (row0 + r) * a.ldo + (long long)h * HD + 8 * n + 2 * t) =
+      *reinterpret_cast<uint32_t*>(a.dQ + (row0 + r) * a.ldo + (long long)h * HD + d0 + 8 * n + 2 * t) =
           (uint32_t)(v[0] & 0xFFFF) | ((uint32_t)v[1] << 16);
     }
 }
@@ -605,6 +812,15 @@ __global__ void __launch_bounds__(HD == 64 ? 256 : 128) attn_bwd_kv2_kernel(cons
     }
 }
 
+cudaError_t launch_sq_transpose(const int16_t* M, size_t BH, size_t S, int8_t* th, uint8_t* tl, cudaStream_t s) {
+  dim3 sg((unsigned)((S + 63) / 64), (unsigned)((S + 63) / 64), (unsigned)BH);
+  if (S % 16 == 0)
+    sq_transpose16_kernel<<<sg, 128, 0, s>>>(M, (int)S, th, tl);
+  else
+    sq_transpose_kernel<<<sg, 256, 0, s>>>(M, (int)S, th, tl);
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 size_t attention_backward_tc_scratch_bytes(size_t B, size_t S, size_t d, size_t H) {
@@ -614,7 +830,8 @@ size_t attention_backward_tc_scratch_bytes(size_t B, size_t S, size_t d, size_t 
   return 2 * (up(B * S * d) + up(B * d * Sp) + 2 * up(B * d * S) + 2 * up(B * H * S * S));
 }
 
-// dQ, dK, dV (and dL into `dl`, zeroed here) of causal attention on int16
+// dQ, dK, dV (and dL into `dl`: every causal 64 x 64 tile written, the rest
+// untouched) of causal attention on int16
 // operands: q, k, v rows of stride ld, P [B][H][S][S], dC rows of stride ldc;
 // outputs [B*S][d].  head_dim 16 or 64, S a multiple of 4, d a multiple of 16
 // (else cudaErrorNotSupported).  scratch: attention_backward_tc_scratch_bytes.
@@ -649,15 +866,18 @@ cudaError_t launch_attention_backward_tc(const int16_t* q, const int16_t* k, con
   uint8_t* ptl = take(B * H * S * S);
   int8_t* lth = reinterpret_cast<int8_t*>(take(B * H * S * S));
   uint8_t* ltl = take(B * H * S * S);
-  cudaError_t e = cudaMemsetAsync(dl, 0, B * H * S * S * sizeof(int16_t), s);
-  if (e != cudaSuccess) return e;
+  cudaError_t e = cudaSuccess;
   const double pairs = (double)B * (double)H * (double)S * (double)(S + 1) / 2.0;
   {
     ProfScope prof("attention_bwd_planes", s, 0.0, 8.0 * (double)B * S * d + 2.0 * 2.0 * (double)B * H * S * S);
     e = launch_split_planes(v, B * S, d, ld, Planes{vph, vpl, nullptr, d}, s);
     if (e != cudaSuccess) return e;
     dim3 tg((unsigned)((S + 63) / 64), (unsigned)H, (unsigned)B);
-    if (hd == 64) {
+    if (hd == 64 && S % 16 == 0 && ld % 8 == 0 && ldc % 8 == 0) {
+      head_transpose16_kernel<<<tg, 128, 0, s>>>(k, (long long)ld, (int)S, (int)Sp, (int)H, true, kth, ktl);
+      head_transpose16_kernel<<<tg, 128, 0, s>>>(q, (long long)ld, (int)S, (int)S, (int)H, false, qth, qtl);
+      head_transpose16_kernel<<<tg, 128, 0, s>>>(dC, (long long)ldc, (int)S, (int)S, (int)H, false, cth, ctl);
+    } else if (hd == 64) {
       head_transpose_kernel<64><<<tg, 256, 0, s>>>(k, (long long)ld, (int)S, (int)Sp, (int)H, true, kth, ktl);
       head_transpose_kernel<64><<<tg, 256, 0, s>>>(q, (long long)ld, (int)S, (int)S, (int)H, false, qth, qtl);
       head_transpose_kernel<64><<<tg, 256, 0, s>>>(dC, (long long)ldc, (int)S, (int)S, (int)H, false, cth, ctl);
@@ -666,28 +886,37 @@ cudaError_t launch_attention_backward_tc(const int16_t* q, const int16_t* k, con
       head_transpose_kernel<16><<<tg, 256, 0, s>>>(q, (long long)ld, (int)S, (int)S, (int)H, false, qth, qtl);
       head_transpose_kernel<16><<<tg, 256, 0, s>>>(dC, (long long)ldc, (int)S, (int)S, (int)H, false, cth, ctl);
     }
-    dim3 sg((unsigned)((S + 63) / 64), (unsigned)((S + 63) / 64), (unsigned)(B * H));
-    sq_transpose_kernel<<<sg, 256, 0, s>>>(P, (int)S, pth, ptl);
+    e = launch_sq_transpose(P, B * H, S, pth, ptl, s);
+    if (e != cudaSuccess) return e;
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
   dim3 grid((unsigned)((S + BQ - 1) / BQ), (unsigned)H, (unsigned)B);
-  QArgs qa{dC, (long long)ldc, vph, vpl, (int)d, kth, ktl, (int)Sp, P, (int)S, (int)H, shift, dl, dq, (long long)d, st};
   {
-    ProfScope prof("attention_bwd_q", s, 3.0 * 2.0 * (double)hd * pairs,
-                   2.0 * 2.0 * (double)B * H * S * S + 8.0 * (double)B * S * d);
+    DlArgs la{dC, (long long)ldc, vph, vpl, (int)d, P, (int)S, (int)H, dl, st};
+    ProfScope prof("attention_bwd_dl", s, 2.0 * (double)hd * pairs,
+                   2.0 * 2.0 * (double)B * H * S * S + 4.0 * (double)B * S * d);
     if (hd == 64)
-      attn_bwd_q_kernel<64><<<grid, 128, 0, s>>>(qa);
+      attn_bwd_dl_kernel<64><<<grid, 128, 0, s>>>(la);
     else
-      attn_bwd_q_kernel<16><<<grid, 128, 0, s>>>(qa);
+      attn_bwd_dl_kernel<16><<<grid, 128, 0, s>>>(la);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
   {
-    dim3 sg((unsigned)((S + 63) / 64), (unsigned)((S + 63) / 64), (unsigned)(B * H));
-    ProfScope prof("attention_bwd_planes", s, 0.0, 4.0 * (double)B * H * S * S);
-    sq_transpose_kernel<<<sg, 256, 0, s>>>(dl, (int)S, lth, ltl);
+    DqArgs qa{kth, ktl, (int)Sp, dl, (int)S, (int)H, shift, dq, (long long)d};
+    ProfScope prof("attention_bwd_dq", s, 2.0 * (double)hd * pairs,
+                   2.0 * (double)B * H * S * S + 4.0 * (double)B * S * d);
+    if (hd == 64)
+      attn_bwd_dq_kernel<64><<<grid, 256, 0, s>>>(qa);
+    else
+      attn_bwd_dq_kernel<16><<<grid, 128, 0, s>>>(qa);
     e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  {
+    ProfScope prof("attention_bwd_planes", s, 0.0, 4.0 * (double)B * H * S * S);
+    e = launch_sq_transpose(dl, B * H, S, lth, ltl, s);
     if (e != cudaSuccess) return e;
   }
   KVArgs ka{lth, ltl, qth, qtl, (int)S, (int)H, shift, dk, (long long)d};

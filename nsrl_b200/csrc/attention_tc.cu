@@ -52,7 +52,9 @@ constexpr int OFF_P = OFF_STAGE + ST * STAGE_BYTES;
 constexpr int OFF_X = OFF_P + 2 * 2 * PLANE_P;  // row-statistics exchange
 constexpr int X_BYTES = 4 * QT * 8 * 3;
 constexpr int OFF_LUT = OFF_X + X_BYTES;
-constexpr int OFF_BAR = OFF_LUT + 512;
+constexpr int OFF_WPF = OFF_LUT + 512;               // WS weights of the next tile: [2 buffers][2 halves][512 threads] x 16 B
+constexpr int WPF_BUF = 2 * 32 * SOFTMAX_WARPS * 16;
+constexpr int OFF_BAR = OFF_WPF + 2 * WPF_BUF;
 constexpr size_t SMEM_BYTES = OFF_BAR + 256 + 1024;
 
 struct Maps {
@@ -67,7 +69,7 @@ struct Args {
   uint8_t* ctx_lo;
   unsigned long long* ctx_l1;
   long long ldc;
-  int16_t* probs;    // optional: P [B][H][S][S] of the visited key tiles (the caller zeroes the rest)
+  int16_t* probs;    // optional P [B][H][S][S]: the visited key tiles only, zeros above the diagonal
   nsrl_device_status* st;
 };
 
@@ -141,6 +143,8 @@ __device__ __forceinline__ void scores_weight(const uint32_t (&hh)[16], const ui
 
 // WS: the sum pass stores its weights w (int16) in global scratch and the
 // last pass reads them back instead of recomputing S (no K tiles, no QK MMAs).
+// The last pass stages the next tile's weights in shared memory with
+// cp.async (no registers held across the tile loop).
 template <bool WS>
 __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_constant__ Maps maps, const Args a) {
   extern __shared__ uint8_t smem_raw[];
@@ -325,15 +329,33 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
     // WS: this thread's row of the weight scratch
     int16_t* wrow = WS ? a.wscr + ((((long long)b * a.H + h) * gridDim.x + blockIdx.x) * QT + row) * a.wstride
                        : nullptr;
+    // WS, last pass: this thread's 32 bytes of weights per tile, copied a tile
+    // ahead into slot [buffer][half][thread] (its own copies: no barrier)
+    const int sidx = threadIdx.x - 64;
+    auto wpf_issue = [&](int j) {
+      const int16_t* src = wrow + j * KT + 16 * g;  // keys below ntiles * 64 <= wstride, written in pass 1
+      const uint32_t dst = smem_u32(sm + OFF_WPF + (j & 1) * WPF_BUF + sidx * 16);
+      cp_async16(dst, src);
+      cp_async16(dst + WPF_BUF / 2, src + 8);
+      cp_async_commit();
+    };
     for (int pass = 0; pass < 3; ++pass) {
+      if (WS && pass == 2 && ntiles > 0) wpf_issue(0);
       for (int j = 0; j < ntiles; ++j) {
         const int key0 = j * KT + 16 * g;
         const int nlive = max(0, min(16, last_key - key0 + 1));
         int w[16];
         if (WS && pass == 2) {
           // weights of the sum pass (0 beyond the live keys)
-          const uint4* src = reinterpret_cast<const uint4*>(wrow + key0);
-          const uint4 u0 = src[0], u1 = src[1];
+          if (j + 1 < ntiles) {
+            wpf_issue(j + 1);
+            cp_async_wait<1>();
+          } else {
+            cp_async_wait<0>();
+          }
+          const uint8_t* slot = sm + OFF_WPF + (j & 1) * WPF_BUF + sidx * 16;
+          const uint4 u0 = *reinterpret_cast<const uint4*>(slot);
+          const uint4 u1 = *reinterpret_cast<const uint4*>(slot + WPF_BUF / 2);
           const uint32_t wv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
 #pragma unroll
           for (int i = 0; i < 8; ++i) {

@@ -77,6 +77,17 @@ __device__ __forceinline__ unsigned long long div_exact(unsigned long long ss, u
   return q;
 }
 
+// 16-byte global -> shared copies that complete asynchronously (cp.async,
+// L2 only); a thread sees its own copies after cp_async_wait.
+__device__ __forceinline__ void cp_async16(uint32_t saddr, const void* g) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr), "l"(g) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // Saturating i32 -> i16 (one cvt.sat), returned sign-extended.
 __device__ __forceinline__ int sat16(int v) {
   short r;

@@ -476,24 +476,28 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
               o[i] = pack2(sa, sb);
             }
             store32_i16(p.y + (long long)r * p.ldy + n, o, nvalid, vec_skip);
-          } else if (EPI == (int)Epi::QKV_VT && n >= p.vt_col0) {
-            // v columns: byte stores into [b][h][dim][s]; the 32 lanes of the
-            // warp hold 32 consecutive positions, so each store instruction
-            // writes one contiguous 32-byte run per plane.
-            const int b = r / p.vt_S, spos = r % p.vt_S;
-            const int c0 = n - p.vt_col0;
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              if (i < nvalid) {
-                const int c = c0 + i, hh = c / p.vt_hd, dd = c % p.vt_hd;
-                const long long off = ((long long)(b * p.vt_H + hh) * p.vt_hd + dd) * p.vt_S + spos;
-                p.vth[off] = (int8_t)(v[i] >> 8);
-                p.vtl[off] = (uint8_t)(v[i] & 255);
-              }
-            }
           } else {
-            const long long off = (long long)r * p.ldp + n;
-            store32_planes(p.yh + off, p.yl + off, o, nvalid, ((p.ldp | n) & 15) == 0, l1);
+            if (EPI == (int)Epi::QKV_VT && p.y)  // the int16 rows as well (the training step's cache)
+              store32_i16(p.y + (long long)r * p.ldy + n, o, nvalid, ((p.ldy | n) & 7) == 0);
+            if (EPI == (int)Epi::QKV_VT && n >= p.vt_col0) {
+              // v columns: byte stores into [b][h][dim][s]; the 32 lanes of the
+              // warp hold 32 consecutive positions, so each store instruction
+              // writes one contiguous 32-byte run per plane.
+              const int b = r / p.vt_S, spos = r % p.vt_S;
+              const int c0 = n - p.vt_col0;
+#pragma unroll
+              for (int i = 0; i < 32; ++i) {
+                if (i < nvalid) {
+                  const int c = c0 + i, hh = c / p.vt_hd, dd = c % p.vt_hd;
+                  const long long off = ((long long)(b * p.vt_H + hh) * p.vt_hd + dd) * p.vt_S + spos;
+                  p.vth[off] = (int8_t)(v[i] >> 8);
+                  p.vtl[off] = (uint8_t)(v[i] & 255);
+                }
+              }
+            } else {
+              const long long off = (long long)r * p.ldp + n;
+              store32_planes(p.yh + off, p.yl + off, o, nvalid, ((p.ldp | n) & 15) == 0, l1);
+            }
           }
         }
       }
@@ -579,11 +583,13 @@ __global__ void gemm_simt_kernel(const SimtParams s) {
     if (w < -32768 || w > 32767) atomicAdd(p.sat, 1ull);
     p.y[(long long)m * p.ldy + n] = sat_i16_i32(w);
   } else if (s.epi == (int)Epi::QKV_VT && n >= p.vt_col0) {
+    if (p.y) p.y[(long long)m * p.ldy + n] = v;
     const int b = m / p.vt_S, spos = m % p.vt_S, c = n - p.vt_col0;
     const long long off = ((long long)(b * p.vt_H + c / p.vt_hd) * p.vt_hd + c % p.vt_hd) * p.vt_S + spos;
     p.vth[off] = (int8_t)(v >> 8);
     p.vtl[off] = (uint8_t)(v & 255);
   } else {
+    if (s.epi == (int)Epi::QKV_VT && p.y) p.y[(long long)m * p.ldy + n] = v;
     p.yh[(long long)m * p.ldp + n] = (int8_t)(v >> 8);
     p.yl[(long long)m * p.ldp + n] = (uint8_t)(v & 255);
     if (p.yl1) atomicAdd(&p.yl1[m], (unsigned long long)abs((int)v));

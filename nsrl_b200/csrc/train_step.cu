@@ -676,6 +676,9 @@ nsrl_status nsrl_train_windows(const nsrl_train_model* m, const uint8_t* context
       TS_TRY(launch_rms_norm(c.in, T, d, ly.attn_gamma, 1, c.an, pad, st, s), "rms");
     else
       TS_TRY(launch_split_planes(c.in, T, d, d, pad, s), "split");
+    // Q|K|V: with the tcgen05 attention, one GEMM writes the int16 rows (the
+    // cache the backward reads), the Q|K planes and the transposed V planes.
+    const bool tc_attn = o.vt.hi && tma_supported() && attention_tc_supported(S, d, H);
     {
       GemmArgs g{};
       g.a_hi = pad.hi;
@@ -687,32 +690,20 @@ nsrl_status nsrl_train_windows(const nsrl_train_model* m, const uint8_t* context
       g.nseg = 3;
       for (int i = 0; i < 3; ++i)
         g.seg[i] = WeightSeg{ly.lin[i].weights, ly.lin[i].bias, ly.lin[i].scales, d};
-      g.epi = Epi::I16;
+      g.epi = tc_attn ? Epi::QKV_VT : Epi::I16;
       g.y = c.qkv;
       g.ldy = 3 * d;
+      if (tc_attn) {
+        g.yp = o.pqkv;
+        g.vt = o.vt;
+      }
       g.st = st;
       TS_TRY(launch_gemm(g, s), "qkv");
     }
     bool done = false;
-    if (o.vt.hi && tma_supported()) {
-      // tcgen05 attention with the probabilities written out: the Q|K planes and
-      // transposed V come from a second Q|K|V GEMM in the attention operand form.
-      GemmArgs g{};
-      g.a_hi = pad.hi;
-      g.a_lo = pad.lo;
-      g.a_l1 = pad.l1;
-      g.lda = d;
-      g.M = T;
-      g.K = d;
-      g.nseg = 3;
-      for (int i = 0; i < 3; ++i)
-        g.seg[i] = WeightSeg{ly.lin[i].weights, ly.lin[i].bias, ly.lin[i].scales, d};
-      g.epi = Epi::QKV_VT;
-      g.yp = o.pqkv;
-      g.vt = o.vt;
-      g.st = st;
-      TS_TRY(launch_gemm(g, s), "qkv planes");
-      TS_TRY(cudaMemsetAsync(c.P, 0, W * H * S * S * sizeof(int16_t), s), "memset");
+    if (tc_attn) {
+      // every P entry the backward reads is written: the visited key tiles of
+      // each 128-query tile, zeros above the diagonal
       TS_TRY(cudaMemsetAsync(pad.l1, 0, T * sizeof(unsigned long long), s), "memset");
       const cudaError_t e = launch_attention_tc(o.pqkv, o.vt, W, S, d, H, true, pad, o.vt.wscr, st, s, c.P);
       if (e != cudaErrorNotSupported) {
@@ -735,8 +726,12 @@ nsrl_status nsrl_train_windows(const nsrl_train_model* m, const uint8_t* context
     TS_TRY(fwd_gemm(pad, T, d, &ly.lin[5], Epi::I16, c.gate, F, nullptr, nullptr, st, s), "gate");
     {
       ProfScope prof("gated_forward", s, 0.0, 8.0 * (double)T * (double)F);
-      gated_forward_kernel<<<blocks_for((long long)T * 32, 148 * 16), 256, 0, s>>>(c.up, c.gate, (long long)T, (int)F,
-                                                                                  c.gated, paF.hi, paF.lo, paF.l1);
+      if (F % 8 == 0)
+        gated_forward_vec_kernel<<<blocks_for((long long)T * 32, 148 * 16), 256, 0, s>>>(
+            c.up, c.gate, (long long)T, (int)F, c.gated, paF.hi, paF.lo, paF.l1);
+      else
+        gated_forward_kernel<<<blocks_for((long long)T * 32, 148 * 16), 256, 0, s>>>(
+            c.up, c.gate, (long long)T, (int)F, c.gated, paF.hi, paF.lo, paF.l1);
       TS_TRY(cudaGetLastError(), "gated");
     }
     TS_TRY(fwd_gemm(paF, T, F, &ly.lin[6], Epi::RESID, c.out, d, c.ares, o.fwd_res, st, s), "down");

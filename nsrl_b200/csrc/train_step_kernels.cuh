@@ -134,21 +134,29 @@ __global__ void gated_backward_vec_kernel(const int16_t* __restrict__ gg, const 
                                           int16_t* __restrict__ ggate, int8_t* __restrict__ uh,
                                           uint8_t* __restrict__ ul, int8_t* __restrict__ gh,
                                           uint8_t* __restrict__ gl) {
+  int fcur = -1, s1[8], s2[8];  // the shifts of columns fcur .. +7
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
     int g[8], u[8], ga[8], ou[8], og[8], pu[8], pg[8];
     unpack8(reinterpret_cast<const uint4*>(gg)[i], g);
     unpack8(reinterpret_cast<const uint4*>(up)[i], u);
     unpack8(reinterpret_cast<const uint4*>(gate)[i], ga);
     const int f0 = (int)((i * 8) % F);
+    if (f0 != fcur) {
+      fcur = f0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        s1[e] = su[f0 + e].right_shift;
+        s2[e] = sg[f0 + e].right_shift;
+      }
+    }
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       const int silu = (ga[e] * ((ga[e] >> 2) + 16384) + 16384) >> 15;
       ou[e] = (g[e] * silu + 16384) >> 15;
       const int grad_silu = (g[e] * u[e] + 16384) >> 15;
       og[e] = sat16((grad_silu * ((ga[e] >> 1) + 16384) + 16384) >> 15);
-      const int s1 = su[f0 + e].right_shift, s2 = sg[f0 + e].right_shift;
-      pu[e] = s1 ? (int)rhu64(ou[e], (uint32_t)s1) : ou[e];
-      pg[e] = s2 ? (int)rhu64(og[e], (uint32_t)s2) : og[e];
+      pu[e] = s1[e] ? (int)rhu64(ou[e], (uint32_t)s1[e]) : ou[e];
+      pg[e] = s2[e] ? (int)rhu64(og[e], (uint32_t)s2[e]) : og[e];
     }
     reinterpret_cast<uint4*>(gup)[i] = pack8(ou);
     reinterpret_cast<uint4*>(ggate)[i] = pack8(og);
@@ -166,19 +174,33 @@ __global__ void gated_backward_vec_kernel(const int16_t* __restrict__ gg, const 
 __global__ void prescale_split_vec_kernel(const int16_t* __restrict__ g, long long n8, int N,
                                           const nsrl_fixed_scale* __restrict__ sc, int8_t* __restrict__ hi,
                                           uint8_t* __restrict__ lo) {
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
-    int v[8];
-    unpack8(reinterpret_cast<const uint4*>(g)[i], v);
-    const int c0 = (int)((i * 8) % N);
+  // two words in flight per thread; each slot keeps the shifts of its
+  // columns cur[k] .. +7 (the same every pass when the stride is a multiple of N)
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  int cur[2] = {-1, -1}, sh[2][8];
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += 2 * stride) {
+    const uint4 u[2] = {reinterpret_cast<const uint4*>(g)[i],
+                        i + stride < n8 ? reinterpret_cast<const uint4*>(g)[i + stride] : make_uint4(0, 0, 0, 0)};
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const int s = sc[c0 + e].right_shift;
-      if (s) v[e] = (int)rhu64(v[e], (uint32_t)s);
+    for (int k = 0; k < 2; ++k) {
+      const long long ik = i + k * stride;
+      if (ik >= n8) break;
+      int v[8];
+      unpack8(u[k], v);
+      const int c0 = (int)((ik * 8) % N);
+      if (c0 != cur[k]) {
+        cur[k] = c0;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) sh[k][e] = sc[c0 + e].right_shift;
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (sh[k][e]) v[e] = (int)rhu64(v[e], (uint32_t)sh[k][e]);
+      uint2 h, l;
+      planes8(v, h, l);
+      reinterpret_cast<uint2*>(hi)[ik] = h;
+      reinterpret_cast<uint2*>(lo)[ik] = l;
     }
-    uint2 h, l;
-    planes8(v, h, l);
-    reinterpret_cast<uint2*>(hi)[i] = h;
-    reinterpret_cast<uint2*>(lo)[i] = l;
   }
 }
 
@@ -239,6 +261,35 @@ __global__ void gated_forward_kernel(const int16_t* __restrict__ up, const int16
       hi[i] = (int8_t)(v >> 8);
       lo[i] = (uint8_t)(v & 255);
       s += (unsigned long long)abs(v);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) l1[r] = s;
+  }
+}
+
+// gated_forward_kernel on eight consecutive hidden units per lane (F % 8 == 0).
+__global__ void gated_forward_vec_kernel(const int16_t* __restrict__ up, const int16_t* __restrict__ gate,
+                                         long long rows, int F, int16_t* __restrict__ gated, int8_t* __restrict__ hi,
+                                         uint8_t* __restrict__ lo, unsigned long long* __restrict__ l1) {
+  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+  for (long long r = (long long)blockIdx.x * warps + (threadIdx.x >> 5); r < rows; r += (long long)gridDim.x * warps) {
+    unsigned long long s = 0;
+    for (int f = 8 * lane; f < F; f += 256) {
+      const long long i8 = (r * F + f) >> 3;
+      int u[8], g[8], v[8];
+      unpack8(reinterpret_cast<const uint4*>(up)[i8], u);
+      unpack8(reinterpret_cast<const uint4*>(gate)[i8], g);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        v[e] = gated_act(u[e], g[e]);
+        s += (unsigned long long)abs(v[e]);
+      }
+      reinterpret_cast<uint4*>(gated)[i8] = pack8(v);
+      uint2 h, l;
+      planes8(v, h, l);
+      reinterpret_cast<uint2*>(hi)[i8] = h;
+      reinterpret_cast<uint2*>(lo)[i8] = l;
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
@@ -568,9 +619,17 @@ __global__ void __launch_bounds__(256) rms_backward_reg_kernel(const int16_t* __
       gi[r * d + lane + 32 * i] = cl;
     }
   }
+  // gamma gradients: the block's warps add into shared memory, then one
+  // global add per column and block
+  __shared__ unsigned long long gsum[d];
+  for (int i = threadIdx.x; i < d; i += blockDim.x) gsum[i] = 0;
+  __syncthreads();
 #pragma unroll
   for (int i = 0; i < D32; ++i)
-    if (gacc[i]) atomicAdd(reinterpret_cast<unsigned long long*>(&gw[lane + 32 * i]), (unsigned long long)gacc[i]);
+    if (gacc[i]) atomicAdd(&gsum[lane + 32 * i], (unsigned long long)gacc[i]);
+  __syncthreads();
+  for (int i = threadIdx.x; i < d; i += blockDim.x)
+    if (gsum[i]) atomicAdd(reinterpret_cast<unsigned long long*>(&gw[i]), gsum[i]);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) nsat += __shfl_xor_sync(0xffffffffu, nsat, o);
   if (lane == 0 && nsat) atomicAdd(sat, nsat);

@@ -207,66 +207,82 @@ __global__ void __launch_bounds__(WTHREADS, 1) wgrad_tc_kernel(const __grid_cons
 
 // [T][C] int16 (row stride ld) -> byte planes of the transpose [C][T]
 // (row stride ldt bytes), each value first prescaled by rhu(v, shift_c)
-// when `sc` is given (multiplier 1).  64 x 64 tiles through shared memory:
-// 8-byte loads of four columns, 4-byte stores of four rows per plane.
+// when `sc` is given (multiplier 1).  A CTA moves 128 rows x 64 columns:
+// 16-byte loads of eight columns into shared memory, kept as 32-bit words
+// (two columns) with the word index XORed by 4 ((t / 16) mod 8) so that the
+// column reads below are conflict-free; then each thread gathers 16 rows of
+// one column pair and writes 16-byte words of both planes for both columns.
+// Rows t >= T are written as zeros up to the next multiple of 128 (inside
+// ldt); columns c >= C are not written.
 __global__ void __launch_bounds__(256) transpose_split_kernel(const int16_t* __restrict__ x, long long T, int C,
                                                               long long ld, const nsrl_fixed_scale* __restrict__ sc,
                                                               int8_t* __restrict__ th, uint8_t* __restrict__ tl,
                                                               long long ldt, bool vec) {
-  __shared__ int16_t tile[64][66];  // [t][c]
-  const long long t0 = (long long)blockIdx.x * 64;
+  __shared__ __align__(16) uint32_t tile[128 * 32];  // [t][column pair ^ swizzle]
+  const long long t0 = (long long)blockIdx.x * 128;
   const int c0 = blockIdx.y * 64;
-  for (int i = threadIdx.x; i < 64 * 16; i += 256) {
-    const int r = i >> 4, c4 = (i & 15) * 4;
+  const int tid = threadIdx.x;
+#pragma unroll
+  for (int z = 0; z < 4; ++z) {
+    const int i = tid + 256 * z;
+    const int r = i >> 3, c8 = (i & 7) * 8;
     const long long t = t0 + r;
-    const int c = c0 + c4;
-    int v[4] = {0, 0, 0, 0};
+    const int c = c0 + c8;
+    int v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     if (t < T) {
-      if (vec && c + 3 < C) {
-        const uint2 u = *reinterpret_cast<const uint2*>(x + t * ld + c);
-        v[0] = (int16_t)(u.x & 0xFFFF);
-        v[1] = (int16_t)(u.x >> 16);
-        v[2] = (int16_t)(u.y & 0xFFFF);
-        v[3] = (int16_t)(u.y >> 16);
+      if (vec && c + 7 < C) {
+        const uint4 u = *reinterpret_cast<const uint4*>(x + t * ld + c);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          v[2 * q] = (int16_t)(w[q] & 0xFFFF);
+          v[2 * q + 1] = (int16_t)(w[q] >> 16);
+        }
       } else {
 #pragma unroll
-        for (int z = 0; z < 4; ++z)
-          if (c + z < C) v[z] = x[t * ld + c + z];
+        for (int q = 0; q < 8; ++q)
+          if (c + q < C) v[q] = x[t * ld + c + q];
       }
       if (sc) {
 #pragma unroll
-        for (int z = 0; z < 4; ++z)
-          if (c + z < C) {
-            const int s = sc[c + z].right_shift;
-            if (s) v[z] = (int)rhu64(v[z], (uint32_t)s);
+        for (int q = 0; q < 8; ++q)
+          if (c + q < C) {
+            const int s = sc[c + q].right_shift;
+            if (s) v[q] = (int)rhu64(v[q], (uint32_t)s);
           }
       }
     }
-#pragma unroll
-    for (int z = 0; z < 4; ++z) tile[r][c4 + z] = (int16_t)v[z];
+    uint4 o;
+    o.x = (uint32_t)(v[0] & 0xFFFF) | ((uint32_t)v[1] << 16);
+    o.y = (uint32_t)(v[2] & 0xFFFF) | ((uint32_t)v[3] << 16);
+    o.z = (uint32_t)(v[4] & 0xFFFF) | ((uint32_t)v[5] << 16);
+    o.w = (uint32_t)(v[6] & 0xFFFF) | ((uint32_t)v[7] << 16);
+    const int wc = (c8 >> 1) ^ (((r >> 4) & 7) << 2);  // a multiple of 4: the 4 words stay together
+    *reinterpret_cast<uint4*>(&tile[r * 32 + wc]) = o;
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < 64 * 16; i += 256) {
-    const int cr = i >> 4, t4 = (i & 15) * 4;
-    const int c = c0 + cr;
-    const long long t = t0 + t4;
-    if (c >= C || t >= T) continue;
-    uint32_t hv = 0, lv = 0;
+  const int cw = tid >> 3;         // column pair 0..31
+  const int tb = (tid & 7) * 16;   // rows tb .. tb + 15
+  const int wc = cw ^ (((tb >> 4) & 7) << 2);
+  uint32_t hi[2][4], lo[2][4];     // [column of the pair][word of 4 rows]
 #pragma unroll
-    for (int z = 0; z < 4; ++z) {
-      const int v = tile[t4 + z][cr];
-      hv |= (uint32_t)((v >> 8) & 255) << (8 * z);
-      lv |= (uint32_t)(v & 255) << (8 * z);
-    }
-    if (t + 3 < T) {  // ldt and t are multiples of 4: aligned word stores
-      *reinterpret_cast<uint32_t*>(th + (long long)c * ldt + t) = hv;
-      *reinterpret_cast<uint32_t*>(tl + (long long)c * ldt + t) = lv;
-    } else {
-      for (int z = 0; t + z < T; ++z) {
-        th[(long long)c * ldt + t + z] = (int8_t)(hv >> (8 * z));
-        tl[(long long)c * ldt + t + z] = (uint8_t)(lv >> (8 * z));
-      }
-    }
+  for (int q = 0; q < 4; ++q) {
+    const uint32_t w0 = tile[(tb + 4 * q) * 32 + wc], w1 = tile[(tb + 4 * q + 1) * 32 + wc];
+    const uint32_t w2 = tile[(tb + 4 * q + 2) * 32 + wc], w3 = tile[(tb + 4 * q + 3) * 32 + wc];
+    const uint32_t ah = __byte_perm(w0, w1, 0x7531), bh = __byte_perm(w2, w3, 0x7531);  // hi bytes, c0 c1 c0 c1
+    const uint32_t al = __byte_perm(w0, w1, 0x6420), bl = __byte_perm(w2, w3, 0x6420);  // lo bytes
+    hi[0][q] = __byte_perm(ah, bh, 0x6420);
+    hi[1][q] = __byte_perm(ah, bh, 0x7531);
+    lo[0][q] = __byte_perm(al, bl, 0x6420);
+    lo[1][q] = __byte_perm(al, bl, 0x7531);
+  }
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    const int c = c0 + 2 * cw + e;
+    if (c >= C) continue;
+    const long long off = (long long)c * ldt + t0 + tb;
+    *reinterpret_cast<uint4*>(th + off) = make_uint4(hi[e][0], hi[e][1], hi[e][2], hi[e][3]);
+    *reinterpret_cast<uint4*>(tl + off) = make_uint4(lo[e][0], lo[e][1], lo[e][2], lo[e][3]);
   }
 }
 
@@ -308,9 +324,14 @@ size_t wgrad_planes_ld(size_t T) { return (T + 127) & ~size_t(127); }
 cudaError_t launch_transpose_split(const int16_t* x, size_t T, size_t C, size_t ld, const nsrl_fixed_scale* sc,
                                    int8_t* th, uint8_t* tl, size_t ldt, cudaStream_t s) {
   if (T == 0 || C == 0) return cudaSuccess;
-  dim3 grid((unsigned)((T + 63) / 64), (unsigned)((C + 63) / 64));
+  // 16-byte stores of 16 rows need ldt, the plane bases and the zero-padded
+  // tail (T rounded up to 128) inside the rows
+  if (ldt % 16 != 0 || ldt < ((T + 127) & ~size_t(127)) || (reinterpret_cast<uintptr_t>(th) & 15) != 0 ||
+      (reinterpret_cast<uintptr_t>(tl) & 15) != 0)
+    return cudaErrorInvalidValue;
+  dim3 grid((unsigned)((T + 127) / 128), (unsigned)((C + 63) / 64));
   ProfScope prof("transpose_split", s, 0.0, 4.0 * (double)T * (double)C);
-  const bool vec = ld % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 7) == 0;
+  const bool vec = ld % 8 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
   transpose_split_kernel<<<grid, 256, 0, s>>>(x, (long long)T, (int)C, (long long)ld, sc, th, tl, (long long)ldt,
                                               vec);
   return cudaGetLastError();

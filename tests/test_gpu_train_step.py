@@ -101,7 +101,7 @@ def test_rms_norm_backward(T, d, eps):
 
 
 @pytest.mark.parametrize("B,S,d,H", [(2, 33, 64, 4), (3, 64, 128, 2), (1, 200, 64, 1), (2, 48, 64, 4),
-                                     (1, 520, 128, 2), (2, 4, 64, 1)])
+                                     (1, 520, 128, 2), (2, 4, 64, 1), (2, 256, 256, 4), (1, 528, 128, 2)])
 def test_attention_probabilities_and_backward(B, S, d, H):
     _, train = _core()
     rng = np.random.default_rng(B * S)
@@ -206,7 +206,8 @@ def test_sharded_windows_sum_to_the_whole_batch():
     assert torch.equal(parts[0][1] + parts[1][1], whole[1])
 
 
-@pytest.mark.parametrize("rows,K,N,shift", [(300, 64, 48, 0), (1000, 256, 1024, 2), (4133, 200, 72, 0)])
+@pytest.mark.parametrize("rows,K,N,shift", [(300, 64, 48, 0), (1000, 256, 1024, 2), (4133, 200, 72, 0),
+                                          (777, 100, 37, 1)])
 def test_weight_gradient_tensor_cores(rows, K, N, shift):
     """The tcgen05 weight-gradient product against an exact int64 matmul of the prescaled grads."""
     core, train = _core()
