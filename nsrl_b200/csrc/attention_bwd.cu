@@ -56,6 +56,15 @@ __device__ __forceinline__ void split4(const int16_t* v, uint32_t& hi, uint32_t&
   lo = l;
 }
 
+// The prescaled planes of two adjacent columns col, col + 1 of one row.
+__device__ __forceinline__ void store_grad_planes2(const GradPlanes& gp, long long off, int col, const int (&v)[2]) {
+  int p[2];
+#pragma unroll
+  for (int e = 0; e < 2; ++e) p[e] = rhu_i16(v[e], gp.sc[col + e].right_shift);
+  *reinterpret_cast<uint16_t*>(gp.hi + off) = (uint16_t)(((p[0] >> 8) & 255) | (((p[1] >> 8) & 255) << 8));
+  *reinterpret_cast<uint16_t*>(gp.lo + off) = (uint16_t)((p[0] & 255) | ((p[1] & 255) << 8));
+}
+
 constexpr int BQ = 64;  // query rows per CTA (4 warps x 16)
 constexpr int BK = 32;  // keys per tile
 
@@ -448,6 +457,7 @@ struct DqArgs {
   int S, H, shift;
   int16_t* dQ;
   long long ldo;
+  GradPlanes gp;  // optional prescaled planes of dQ
 };
 
 // dQ[t] = sat(rhu(sum_{j <= t} dL[t][j] K[j], shift)): one CTA per 64 query
@@ -457,7 +467,7 @@ struct DqArgs {
 // K^T planes), prefetched a tile ahead; K^T is staged 16 bytes at a time into
 // double-buffered shared memory.
 template <int HD>
-__global__ void __launch_bounds__(HD == 64 ? 256 : 128) attn_bwd_dq_kernel(const DqArgs a) {
+__global__ void __launch_bounds__(HD == 64 ? 256 : 128, 2) attn_bwd_dq_kernel(const DqArgs a) {
   constexpr int WN = HD < 32 ? HD : 32;  // dims per warp
   constexpr int NT = WN / 8;
   constexpr int NTHREADS = 128 * (HD / WN);
@@ -479,27 +489,19 @@ __global__ void __launch_bounds__(HD == 64 ? 256 : 128) attn_bwd_dq_kernel(const
   const int ntiles = (kend + BK - 1) / BK;
   const int wlast = min(qw + 15, S - 1);
 
-  auto load_tile = [&](int kb, uint4 (&r)[PER]) {
+  // K^T tile kb -> stage sb with cp.async (no registers held across the MMAs)
+  auto issue_tile = [&](int kb, int sb) {
 #pragma unroll
     for (int z = 0; z < PER; ++z) {
       const int e = tid + z * NTHREADS;
-      uint4 v = make_uint4(0, 0, 0, 0);
       if (e < 2 * KW) {
         const int pl = e / KW, w = e % KW;
         const long long off = ktb + (long long)(w >> 1) * a.Sp + kb + 16 * (w & 1);
-        v = pl ? *reinterpret_cast<const uint4*>(a.kt_lo + off) : *reinterpret_cast<const uint4*>(a.kt_hi + off);
+        cp_async16(smem_u32(&kbuf[sb][pl][(w >> 1) * VSTR + 16 * (w & 1)]), pl ? (const void*)(a.kt_lo + off)
+                                                                               : (const void*)(a.kt_hi + off));
       }
-      r[z] = v;
     }
-  };
-  auto store_tile = [&](int sb, const uint4 (&r)[PER]) {
-#pragma unroll
-    for (int z = 0; z < PER; ++z) {
-      const int e = tid + z * NTHREADS;
-      if (e >= 2 * KW) continue;
-      const int pl = e / KW, w = e % KW;
-      *reinterpret_cast<uint4*>(&kbuf[sb][pl][(w >> 1) * VSTR + 16 * (w & 1)]) = r[z];
-    }
+    cp_async_commit();
   };
   // fragment register i: row (i & 1 ? r1 : r0), key pairs kb + 2t + (i & 2 ? 16 : 0) and + 8
   auto load_dl = [&](int kb, uint32_t (&u)[4][2]) {
@@ -521,22 +523,20 @@ __global__ void __launch_bounds__(HD == 64 ? 256 : 128) attn_bwd_dq_kernel(const
 #pragma unroll
     for (int i = 0; i < 4; ++i) acc_hh[n][i] = acc_mid[n][i] = acc_ll[n][i] = 0;
   uint32_t du[4][2];
-  {
-    uint4 pre[PER];
-    load_tile(0, pre);
-    store_tile(0, pre);
-    load_dl(0, du);
-    __syncthreads();
-  }
+  issue_tile(0, 0);
+  load_dl(0, du);
   for (int kt = 0; kt < ntiles; ++kt) {
     const int kb = kt * BK, sb = kt & 1;
     const bool more = kt + 1 < ntiles;
-    uint4 pre[PER];
     uint32_t dn[4][2];
     if (more) {
-      load_tile(kb + BK, pre);
+      issue_tile(kb + BK, sb ^ 1);  // stage sb ^ 1 was last read before the previous barrier
       load_dl(kb + BK, dn);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
     }
+    __syncthreads();  // every thread's copies of stage sb have landed
     if (qw < S && kb <= wlast) {
       uint32_t ah[4], al[4];
 #pragma unroll
@@ -556,18 +556,21 @@ __global__ void __launch_bounds__(HD == 64 ? 256 : 128) attn_bwd_dq_kernel(const
       }
     }
     if (more) {
-      store_tile(sb ^ 1, pre);
 #pragma unroll
       for (int i = 0; i < 4; ++i) du[i][0] = dn[i][0], du[i][1] = dn[i][1];
     }
-    __syncthreads();
+    __syncthreads();  // stage sb is read before the next iteration's copies reuse it
   }
+  // the 64 x HD block goes through shared memory (the K^T buffers are free
+  // after the last barrier), then out as 16-byte rows of dQ and 8-byte rows
+  // of its prescaled planes
+  constexpr int OSTR = HD + 8;
+  static_assert(64 * OSTR * 2 <= (int)sizeof(kbuf), "dQ staging fits the K^T buffers");
+  int16_t* so = reinterpret_cast<int16_t*>(&kbuf[0][0][0]);
 #pragma unroll
   for (int n = 0; n < NT; ++n)
 #pragma unroll
     for (int hf = 0; hf < 2; ++hf) {
-      const int r = hf ? r1 : r0;
-      if (r >= S) continue;
       int v[2];
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
@@ -575,9 +578,27 @@ __global__ void __launch_bounds__(HD == 64 ? 256 : 128) attn_bwd_dq_kernel(const
         const long long tot = (long long)acc_hh[n][i] * 65536 + (long long)acc_mid[n][i] * 256 + (long long)acc_ll[n][i];
         v[e] = sat_i16(rhu64(tot, (uint32_t)a.shift));
       }
-      *reinterpret_cast<uint32_t*>(a.dQ + (row0 + r) * a.ldo + (long long)h * HD + d0 + 8 * n + 2 * t) =
-          (uint32_t)(v[0] & 0xFFFF) | ((uint32_t)v[1] << 16);
+      const int lr = (warp & 3) * 16 + g + 8 * hf;
+      *reinterpret_cast<uint32_t*>(&so[lr * OSTR + d0 + 8 * n + 2 * t]) = (uint32_t)(v[0] & 0xFFFF) | ((uint32_t)v[1] << 16);
     }
+  __syncthreads();
+  for (int e = tid; e < 64 * (HD / 8); e += NTHREADS) {
+    const int lr = e / (HD / 8), c8 = 8 * (e % (HD / 8));
+    if (q0 + lr >= S) continue;
+    const uint4 u = *reinterpret_cast<const uint4*>(&so[lr * OSTR + c8]);
+    const long long off = (row0 + q0 + lr) * a.ldo + (long long)h * HD + c8;
+    *reinterpret_cast<uint4*>(a.dQ + off) = u;
+    if (a.gp.hi) {
+      int v[8];
+      unpack8(u, v);
+#pragma unroll
+      for (int z = 0; z < 8; ++z) v[z] = rhu_i16(v[z], a.gp.sc[h * HD + c8 + z].right_shift);
+      uint2 ph, pl;
+      planes8(v, ph, pl);
+      *reinterpret_cast<uint2*>(a.gp.hi + off) = ph;
+      *reinterpret_cast<uint2*>(a.gp.lo + off) = pl;
+    }
+  }
 }
 
 // ------------------------------------------------------------------ key side --
@@ -589,6 +610,7 @@ struct KVArgs {
   int S, H, shift;
   int16_t* out;
   long long ldo;
+  GradPlanes gp;  // optional prescaled planes of the output
 };
 
 template <int HD>
@@ -680,8 +702,9 @@ __global__ void __launch_bounds__(128) attn_bwd_kv_kernel(const KVArgs a) {
             (long long)acc_hh[n][i] * 65536 + (long long)acc_mid[n][i] * 256 + (long long)acc_ll[n][i];
         v[e] = sat_i16(rhu64(tot, (uint32_t)a.shift));
       }
-      *reinterpret_cast<uint32_t*>(a.out + (row0 + kr) * a.ldo + (long long)h * HD + 8 * n + 2 * t) =
-          (uint32_t)(v[0] & 0xFFFF) | ((uint32_t)v[1] << 16);
+      const int col = h * HD + 8 * n + 2 * t;
+      *reinterpret_cast<uint32_t*>(a.out + (row0 + kr) * a.ldo + col) = (uint32_t)(v[0] & 0xFFFF) | ((uint32_t)v[1] << 16);
+      if (a.gp.hi) store_grad_planes2(a.gp, (row0 + kr) * a.ldo + col, col, v);
     }
 }
 
@@ -807,8 +830,9 @@ __global__ void __launch_bounds__(HD == 64 ? 256 : 128) attn_bwd_kv2_kernel(cons
             (long long)acc_hh[n][i] * 65536 + (long long)acc_mid[n][i] * 256 + (long long)acc_ll[n][i];
         v[e] = sat_i16(rhu64(tot, (uint32_t)a.shift));
       }
-      *reinterpret_cast<uint32_t*>(a.out + (row0 + kr) * a.ldo + (long long)h * HD + d0 + 8 * n + 2 * t) =
-          (uint32_t)(v[0] & 0xFFFF) | ((uint32_t)v[1] << 16);
+      const int col = h * HD + d0 + 8 * n + 2 * t;
+      *reinterpret_cast<uint32_t*>(a.out + (row0 + kr) * a.ldo + col) = (uint32_t)(v[0] & 0xFFFF) | ((uint32_t)v[1] << 16);
+      if (a.gp.hi) store_grad_planes2(a.gp, (row0 + kr) * a.ldo + col, col, v);
     }
 }
 
@@ -830,16 +854,16 @@ size_t attention_backward_tc_scratch_bytes(size_t B, size_t S, size_t d, size_t 
   return 2 * (up(B * S * d) + up(B * d * Sp) + 2 * up(B * d * S) + 2 * up(B * H * S * S));
 }
 
-// dQ, dK, dV (and dL into `dl`: every causal 64 x 64 tile written, the rest
-// untouched) of causal attention on int16
-// operands: q, k, v rows of stride ld, P [B][H][S][S], dC rows of stride ldc;
-// outputs [B*S][d].  head_dim 16 or 64, S a multiple of 4, d a multiple of 16
+// dQ, dK, dV of causal attention on int16 operands (and dL into `dl`: every
+// causal 64 x 64 tile written, the rest untouched; with `planes`, also the
+// prescaled byte planes of dQ, dK, dV): q, k, v rows of stride ld,
+// P [B][H][S][S], dC rows of stride ldc; outputs [B*S][d].  head_dim 16 or 64, S a multiple of 4, d a multiple of 16
 // (else cudaErrorNotSupported).  scratch: attention_backward_tc_scratch_bytes.
 cudaError_t launch_attention_backward_tc(const int16_t* q, const int16_t* k, const int16_t* v, size_t ld,
                                          const int16_t* P, const int16_t* dC, size_t ldc, size_t B, size_t S, size_t d,
                                          size_t H, int16_t* dl, int16_t* dq, int16_t* dk, int16_t* dv,
                                          void* scratch, size_t scratch_bytes, nsrl_device_status* st,
-                                         cudaStream_t s) {
+                                         cudaStream_t s, const GradPlanes* planes) {
   const size_t hd = d / H;
   // 8-byte loads of P / dL rows, dC, q, k, v need S, ld, ldc multiples of 4
   if ((hd != 16 && hd != 64) || S % 4 != 0 || ld % 4 != 0 || ldc % 4 != 0 || d % 16 != 0 || S > 16384 ||
@@ -904,7 +928,7 @@ cudaError_t launch_attention_backward_tc(const int16_t* q, const int16_t* k, con
     if (e != cudaSuccess) return e;
   }
   {
-    DqArgs qa{kth, ktl, (int)Sp, dl, (int)S, (int)H, shift, dq, (long long)d};
+    DqArgs qa{kth, ktl, (int)Sp, dl, (int)S, (int)H, shift, dq, (long long)d, planes ? planes[0] : GradPlanes{}};
     ProfScope prof("attention_bwd_dq", s, 2.0 * (double)hd * pairs,
                    2.0 * (double)B * H * S * S + 4.0 * (double)B * S * d);
     if (hd == 64)
@@ -919,8 +943,8 @@ cudaError_t launch_attention_backward_tc(const int16_t* q, const int16_t* k, con
     e = launch_sq_transpose(dl, B * H, S, lth, ltl, s);
     if (e != cudaSuccess) return e;
   }
-  KVArgs ka{lth, ltl, qth, qtl, (int)S, (int)H, shift, dk, (long long)d};
-  KVArgs va{pth, ptl, cth, ctl, (int)S, (int)H, 15, dv, (long long)d};
+  KVArgs ka{lth, ltl, qth, qtl, (int)S, (int)H, shift, dk, (long long)d, planes ? planes[1] : GradPlanes{}};
+  KVArgs va{pth, ptl, cth, ctl, (int)S, (int)H, 15, dv, (long long)d, planes ? planes[2] : GradPlanes{}};
   ProfScope prof("attention_bwd_kv", s, 2.0 * 2.0 * (double)hd * pairs,
                  2.0 * 2.0 * (double)B * H * S * S + 8.0 * (double)B * S * d);
   if (S % 16 == 0) {  // 16-byte staging of the M^T and X^T rows

@@ -51,6 +51,14 @@ __device__ __forceinline__ long long rhu64(long long v, uint32_t s) {
   return r >> s;
 }
 
+// rhu64(v, s) for |v| <= 2^15 in 32-bit arithmetic: for s >= 16 the rounded
+// shift of such a v is 0 (v + 2^(s-1) lies in [0, 2^s)).
+__device__ __forceinline__ int rhu_i16(int v, int s) {
+  if (s == 0) return v;
+  if (s >= 16) return 0;
+  return (v + (1 << (s - 1))) >> s;
+}
+
 // numeric.rs:59-70: identity scale saturates; otherwise i64 multiply, rhu, saturate.
 __device__ __forceinline__ int16_t requant_i32(int acc, int mult, uint32_t shift) {
   if (mult == 1 && shift == 0) return sat_i16_i32(acc);
@@ -75,6 +83,31 @@ __device__ __forceinline__ unsigned long long div_exact(unsigned long long ss, u
   if (q * d > ss) --q;
   if ((q + 1) * d <= ss) ++q;
   return q;
+}
+
+// Eight int16 values of a 16-byte load.
+__device__ __forceinline__ void unpack8(const uint4& u, int (&v)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = (int)(int16_t)(w[i] & 0xFFFF);
+    v[2 * i + 1] = (int)(int16_t)(w[i] >> 16);
+  }
+}
+__device__ __forceinline__ uint4 pack8(const int (&v)[8]) {
+  return make_uint4((uint32_t)(v[0] & 0xFFFF) | ((uint32_t)v[1] << 16), (uint32_t)(v[2] & 0xFFFF) | ((uint32_t)v[3] << 16),
+                    (uint32_t)(v[4] & 0xFFFF) | ((uint32_t)v[5] << 16), (uint32_t)(v[6] & 0xFFFF) | ((uint32_t)v[7] << 16));
+}
+// hi bytes (s8) and lo bytes (u8) of eight values, as two 8-byte words.
+__device__ __forceinline__ void planes8(const int (&v)[8], uint2& hi, uint2& lo) {
+  uint32_t h[2] = {0, 0}, l[2] = {0, 0};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    h[i >> 2] |= (uint32_t)((v[i] >> 8) & 255) << (8 * (i & 3));
+    l[i >> 2] |= (uint32_t)(v[i] & 255) << (8 * (i & 3));
+  }
+  hi = make_uint2(h[0], h[1]);
+  lo = make_uint2(l[0], l[1]);
 }
 
 // 16-byte global -> shared copies that complete asynchronously (cp.async,

@@ -134,12 +134,19 @@ cudaError_t launch_wgrad_tc(const int8_t* gh, const uint8_t* gl, const int8_t* x
 // and dL (zeroed, then written) from int16 q, k, v (row stride ld), P and dC.
 // cudaErrorNotSupported outside head_dim 16/64, S % 4 == 0, d % 16 == 0,
 // S <= 16384, or with a scratch below attention_backward_tc_scratch_bytes.
+// Optional second form of an attention gradient: byte planes [B*S][d] of
+// rhu(g, sc[col].right_shift) (the backward-input prescale with multiplier 1).
+struct GradPlanes {
+  const nsrl_fixed_scale* sc = nullptr;
+  int8_t* hi = nullptr;
+  uint8_t* lo = nullptr;
+};
 size_t attention_backward_tc_scratch_bytes(size_t B, size_t S, size_t d, size_t H);
 cudaError_t launch_attention_backward_tc(const int16_t* q, const int16_t* k, const int16_t* v, size_t ld,
                                          const int16_t* P, const int16_t* dC, size_t ldc, size_t B, size_t S, size_t d,
                                          size_t H, int16_t* dl, int16_t* dq, int16_t* dk, int16_t* dv,
                                          void* scratch, size_t scratch_bytes, nsrl_device_status* st,
-                                         cudaStream_t s);
+                                         cudaStream_t s, const GradPlanes* planes = nullptr);
 
 // Planes -> int16.
 cudaError_t launch_join_planes(Planes in, size_t rows, size_t cols, int16_t* y, size_t ldy, cudaStream_t stream);

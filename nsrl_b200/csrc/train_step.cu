@@ -258,14 +258,25 @@ cudaError_t add_sat(const int16_t* a, const int16_t* b, size_t n, int16_t* out, 
   return cudaGetLastError();
 }
 
-// dL, then dQ, dK, dV of one attention layer (nsrl-train/src/lib.rs:16623-16900).
+// dL, then dQ, dK, dV of one attention layer (nsrl-train/src/lib.rs:16623-16900),
+// with `planes` also the prescaled planes of dQ, dK, dV (ld d) for their
+// backward-input linears.
 cudaError_t attn_backward(const int16_t* q, const int16_t* k, const int16_t* v, size_t ld, const int16_t* P,
                           const int16_t* dC, size_t ldc, size_t B, size_t S, size_t d, size_t H, int16_t* dL,
                           int16_t* dq, int16_t* dk, int16_t* dv, void* scratch, size_t scratch_bytes,
-                          nsrl_device_status* st, cudaStream_t s) {
+                          nsrl_device_status* st, cudaStream_t s, const GradPlanes* planes = nullptr) {
   const cudaError_t tce = launch_attention_backward_tc(q, k, v, ld, P, dC, ldc, B, S, d, H, dL, dq, dk, dv, scratch,
-                                                       scratch_bytes, st, s);
+                                                       scratch_bytes, st, s, planes);
   if (tce != cudaErrorNotSupported) return tce;
+  if (planes) {
+    const cudaError_t e = attn_backward(q, k, v, ld, P, dC, ldc, B, S, d, H, dL, dq, dk, dv, scratch, scratch_bytes,
+                                        st, s, nullptr);
+    if (e != cudaSuccess) return e;
+    const int16_t* g[3] = {dq, dk, dv};
+    for (int i = 0; i < 3; ++i)
+      TS_TRY_RET(prescale_split(g[i], B * S, d, d, planes[i].sc, Planes{planes[i].hi, planes[i].lo, nullptr, d}, s));
+    return cudaSuccess;
+  }
   const size_t hd = d / H;
   const int shift = __builtin_ctzll(hd) / 2;
   const size_t smem = S * sizeof(int32_t);
@@ -320,6 +331,7 @@ struct StepLayout {
   unsigned long long* fwd_res;
   WgBufs wg;
   Planes pqkv;  // q|k planes of the tensor-core attention (v goes to vt)
+  Planes pg[3];  // prescaled planes of dQ, dK, dV
   VtPlanes vt;
   void* abw;    // scratch of the tensor-core attention backward
   size_t abw_bytes;
@@ -365,6 +377,7 @@ void carve_step(const nsrl_train_model* m, size_t W, bool rms, void* base, StepL
   o.gup = c.take<int16_t>(T * F);
   o.ggate = c.take<int16_t>(T * F);
   o.dL = c.take<int16_t>(W * H * S * S);
+  for (int i = 0; i < 3; ++i) o.pg[i] = c.planes(T, d, false);
   o.feat = c.take<int16_t>(W * d);
   o.logits = c.take<int16_t>(W * 256);
   o.hgrad = c.take<int16_t>(W * 256);
@@ -809,15 +822,17 @@ nsrl_status nsrl_train_windows(const nsrl_train_model* m, const uint8_t* context
     // attention update, accumulate form (lib.rs:15777-16075)
     TS_TRY(prescale_split(o.gao, T, d, d, ly.lin[3].scales, padn, s), "prescale");
     TS_TRY(bwd_gemm(padn, T, d, c.wt[3], d, o.ident, o.gctx, d, nullptr, nullptr, st, s), "o^T");
+    GradPlanes gp[3];
+    for (int i = 0; i < 3; ++i) gp[i] = GradPlanes{ly.lin[i].scales, o.pg[i].hi, o.pg[i].lo};
     TS_TRY(attn_backward(c.qkv, c.qkv + d, c.qkv + 2 * d, 3 * d, c.P, o.gctx, d, W, S, d, H, o.dL, o.dq, o.dk, o.dv,
-                         o.abw, o.abw_bytes, st, s),
+                         o.abw, o.abw_bytes, st, s, gp),
            "attention backward");
     int16_t* gin[3] = {o.gq, o.gk, o.gv};
     const int16_t* dqkv[3] = {o.dq, o.dk, o.dv};
-    for (int i = 0; i < 3; ++i) {
-      TS_TRY(prescale_split(dqkv[i], T, d, d, ly.lin[i].scales, padn, s), "prescale");
-      TS_TRY(bwd_gemm(padn, T, d, c.wt[i], d, o.ident, gin[i], d, nullptr, nullptr, st, s), "qkv^T");
-    }
+    for (int i = 0; i < 3; ++i)
+      TS_TRY(bwd_gemm(Planes{o.pg[i].hi, o.pg[i].lo, nullptr, d}, T, d, c.wt[i], d, o.ident, gin[i], d, nullptr,
+                      nullptr, st, s),
+             "qkv^T");
     {
       const long long n = (long long)T * d;
       ProfScope prof("fanin", s, 0.0, 8.0 * (double)n);

@@ -100,31 +100,6 @@ __global__ void gated_backward_kernel(const int16_t* __restrict__ gg, const int1
   }
 }
 
-// Eight int16 values of a 16-byte load.
-__device__ __forceinline__ void unpack8(const uint4& u, int (&v)[8]) {
-  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    v[2 * i] = (int)(int16_t)(w[i] & 0xFFFF);
-    v[2 * i + 1] = (int)(int16_t)(w[i] >> 16);
-  }
-}
-__device__ __forceinline__ uint4 pack8(const int (&v)[8]) {
-  return make_uint4((uint32_t)(v[0] & 0xFFFF) | ((uint32_t)v[1] << 16), (uint32_t)(v[2] & 0xFFFF) | ((uint32_t)v[3] << 16),
-                    (uint32_t)(v[4] & 0xFFFF) | ((uint32_t)v[5] << 16), (uint32_t)(v[6] & 0xFFFF) | ((uint32_t)v[7] << 16));
-}
-// hi bytes (s8) and lo bytes (u8) of eight values, as two 8-byte words.
-__device__ __forceinline__ void planes8(const int (&v)[8], uint2& hi, uint2& lo) {
-  uint32_t h[2] = {0, 0}, l[2] = {0, 0};
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    h[i >> 2] |= (uint32_t)((v[i] >> 8) & 255) << (8 * (i & 3));
-    l[i >> 2] |= (uint32_t)(v[i] & 255) << (8 * (i & 3));
-  }
-  hi = make_uint2(h[0], h[1]);
-  lo = make_uint2(l[0], l[1]);
-}
-
 // gated_backward_kernel on eight consecutive hidden units per thread
 // (F % 8 == 0, 16-byte aligned rows).
 __global__ void gated_backward_vec_kernel(const int16_t* __restrict__ gg, const int16_t* __restrict__ up,
@@ -155,8 +130,8 @@ __global__ void gated_backward_vec_kernel(const int16_t* __restrict__ gg, const 
       ou[e] = (g[e] * silu + 16384) >> 15;
       const int grad_silu = (g[e] * u[e] + 16384) >> 15;
       og[e] = sat16((grad_silu * ((ga[e] >> 1) + 16384) + 16384) >> 15);
-      pu[e] = s1[e] ? (int)rhu64(ou[e], (uint32_t)s1[e]) : ou[e];
-      pg[e] = s2[e] ? (int)rhu64(og[e], (uint32_t)s2[e]) : og[e];
+      pu[e] = rhu_i16(ou[e], s1[e]);  // |ou|, |og| <= 2^15
+      pg[e] = rhu_i16(og[e], s2[e]);
     }
     reinterpret_cast<uint4*>(gup)[i] = pack8(ou);
     reinterpret_cast<uint4*>(ggate)[i] = pack8(og);
@@ -194,8 +169,7 @@ __global__ void prescale_split_vec_kernel(const int16_t* __restrict__ g, long lo
         for (int e = 0; e < 8; ++e) sh[k][e] = sc[c0 + e].right_shift;
       }
 #pragma unroll
-      for (int e = 0; e < 8; ++e)
-        if (sh[k][e]) v[e] = (int)rhu64(v[e], (uint32_t)sh[k][e]);
+      for (int e = 0; e < 8; ++e) v[e] = rhu_i16(v[e], sh[k][e]);
       uint2 h, l;
       planes8(v, h, l);
       reinterpret_cast<uint2*>(hi)[ik] = h;

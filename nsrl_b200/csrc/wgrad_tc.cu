@@ -247,8 +247,7 @@ __global__ void __launch_bounds__(256) transpose_split_kernel(const int16_t* __r
 #pragma unroll
         for (int q = 0; q < 8; ++q)
           if (c + q < C) {
-            const int s = sc[c + q].right_shift;
-            if (s) v[q] = (int)rhu64(v[q], (uint32_t)s);
+            v[q] = rhu_i16(v[q], sc[c + q].right_shift);
           }
       }
     }
