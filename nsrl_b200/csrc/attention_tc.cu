@@ -141,6 +141,87 @@ __device__ __forceinline__ void scores_weight(const uint32_t (&hh)[16], const ui
   }
 }
 
+constexpr uint32_t FULLMASK = 0xffffffffu;
+
+// The exp2 table replicated once per lane, s_lutr[32 * f + lane] =
+// EXP2_NEG_FRAC_LUT_8BIT[f] (attention.rs:142-158): lane i reads bank i only,
+// so the random table lookups of a warp never conflict.  A static shared
+// array, so its address is a constant of the load instruction.
+__shared__ uint32_t s_lutr[256 * 32];
+
+// x >> s for every s; amounts of 32 or more give 0 (PTX shr clamps them).
+__device__ __forceinline__ uint32_t shr_clamp(uint32_t x, uint32_t s) {
+  uint32_t r;
+  asm("shr.u32 %0, %1, %2;" : "=r"(r) : "r"(x), "r"(s));
+  return r;
+}
+
+__device__ __forceinline__ int max3i(int a, int b, int c) { return max(max(a, b), c); }
+__device__ __forceinline__ int min3i(int a, int b, int c) { return min(min(a, b), c); }
+__device__ __forceinline__ int max16(const int (&v)[16]) {
+  const int a = max3i(v[0], v[1], v[2]), b = max3i(v[3], v[4], v[5]), c = max3i(v[6], v[7], v[8]);
+  const int d = max3i(v[9], v[10], v[11]), e = max3i(v[12], v[13], v[14]);
+  return max(max3i(a, b, c), max3i(d, e, v[15]));
+}
+__device__ __forceinline__ int min16(const int (&v)[16]) {
+  const int a = min3i(v[0], v[1], v[2]), b = min3i(v[3], v[4], v[5]), c = min3i(v[6], v[7], v[8]);
+  const int d = min3i(v[9], v[10], v[11]), e = min3i(v[12], v[13], v[14]);
+  return min(min3i(a, b, c), min3i(d, e, v[15]));
+}
+__device__ __forceinline__ uint32_t sum16(const uint32_t (&v)[16]) {
+  const uint32_t a = v[0] + v[1] + v[2], b = v[3] + v[4] + v[5], c = v[6] + v[7] + v[8];
+  const uint32_t d = v[9] + v[10] + v[11], e = v[12] + v[13] + v[14];
+  return (a + b + c) + (d + e + v[15]);
+}
+
+// Pass 0 on one S tile of a warp (32 rows x 16 keys).  When every hh of the
+// warp's tile lies in [-16384, 16384], raw = 65536*hh + 256*mid + ll is an
+// exact i32 (|raw| <= 2^30 + B_MID < 2^31) and wrapping 32-bit arithmetic
+// gives it; the guard looks at all 16 elements, live or not, so a masked
+// element can only send the tile to the per-element path, never change a
+// result.
+template <bool FULL>
+__device__ __forceinline__ void tile_max(const uint32_t (&hh)[16], const uint32_t (&mid)[16],
+                                         const uint32_t (&ll)[16], int nlive, int& mx32, long long& mx64,
+                                         long long& mn64) {
+  int hv[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) hv[i] = (int)hh[i];
+  const int hmax = max16(hv), hmin = min16(hv);
+  if (__all_sync(FULLMASK, hmax <= 16384 && hmin >= -16384)) {
+    int r[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int raw = (int)(hh[i] * 65536u + mid[i] * 256u + ll[i]);
+      r[i] = (FULL || i < nlive) ? raw : INT_MIN;
+    }
+    mx32 = max(mx32, max16(r));
+  } else {
+    scores_max<FULL>(hh, mid, ll, nlive, mx32, mx64, mn64);
+  }
+}
+
+// Pass-1 weights of a warp whose 32 rows all have exact i32 raw values
+// (|raw| <= 2^30 + B_MID).  With C = rawmax + cround (mod 2^32),
+// t = C - raw = (rawmax - raw) + cround < 2^32 exactly, mag = lgmax - lg =
+// t >> 3, and w = LUT[mag & 255] >> (mag >> 8) = lutr[(t >> 3) & 255] >> (t >> 11):
+// t >= 30720 (mag >= 3840) shifts by 15 or more and gives 0 as the
+// reference's `shift >= 15` test does, since every table value is below 2^15.
+// Masked keys get t = 2^32 - 1, hence w = 0.
+template <bool FULL>
+__device__ __forceinline__ void weights_fast(const uint32_t (&hh)[16], const uint32_t (&mid)[16],
+                                             const uint32_t (&ll)[16], int nlive, uint32_t C, uint32_t lane4,
+                                             uint32_t (&w)[16]) {
+  const uint8_t* tab = reinterpret_cast<const uint8_t*>(s_lutr);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    uint32_t t = C - (hh[i] * 65536u + mid[i] * 256u + ll[i]);
+    if (!FULL && i >= nlive) t = 0xFFFFFFFFu;
+    const uint32_t v = *reinterpret_cast<const uint32_t*>(tab + (((t << 4) & 0x7F80u) | lane4));
+    w[i] = shr_clamp(v, t >> 11);
+  }
+}
+
 // WS: the sum pass stores its weights w (int16) in global scratch and the
 // last pass reads them back instead of recomputing S (no K tiles, no QK MMAs).
 // The last pass stages the next tile's weights in shared memory with
@@ -156,13 +237,20 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
   unsigned long long* xsum = reinterpret_cast<unsigned long long*>(xmin + 4 * QT);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int q0 = blockIdx.x * QT, h = blockIdx.y, b = blockIdx.z;
+  // query tiles in reverse order: the causal CTAs with the most key tiles
+  // start first and the short ones fill the tail of the grid
+  const int qt = (int)gridDim.x - 1 - (int)blockIdx.x;
+  const int q0 = qt * QT, h = blockIdx.y, b = blockIdx.z;
   const int S = a.S;
   const int kend = a.causal ? min(S, q0 + QT) : S;
   const int ntiles = (kend + KT - 1) / KT;
 
   if (threadIdx.x == 0) ctl->abort = timed_out(a.st) ? 1u : 0u;
   for (int i = threadIdx.x; i < 256; i += THREADS) lut[i] = d_exp2_lut[i];
+  for (int i = threadIdx.x; i < 256 * 8; i += THREADS) {
+    const uint32_t v = (uint32_t)(uint16_t)d_exp2_lut[i >> 3];
+    reinterpret_cast<uint4*>(s_lutr)[i] = make_uint4(v, v, v, v);
+  }
   __syncthreads();
   if (ctl->abort) return;
 
@@ -311,26 +399,148 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
     const bool row_live = qi < S;
     const int last_key = row_live ? (a.causal ? min(qi, S - 1) : S - 1) : -1;
     const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16);
-    // Pass 0 keeps the row max / min of the raw dot product.  With head_dim 64
-    // |256*mid + ll| <= B_MID (< 2^30), so raw = 65536*hh + 256*mid + ll is
-    // an exact i32 whenever |hh| <= 16384; other elements take an i64 path.
+    const uint32_t lane4 = (uint32_t)lane * 4u;
+    uint32_t use0 = 0, use1 = 0;  // uses of each S buffer, in the MMA issuer's order
+    // This warp's 32 rows x 16 keys of an S tile, from TMEM into registers;
+    // the buffer is released as soon as the values are loaded.
+    auto fetch_s = [&](int sb, uint32_t(&hh)[16], uint32_t(&mid)[16], uint32_t(&ll)[16]) {
+      wait_bar(&ctl->s_full[sb], (sb ? use1 : use0) & 1, ctl, a.st);
+      if (sb)
+        ++use1;
+      else
+        ++use0;
+      tc_fence_after();
+      const uint32_t tb = trow + (uint32_t)sb * S_BUF1 + 16 * g;
+      tmem_ld16(tb + S_HH, hh);
+      tmem_ld16(tb + S_MID, mid);
+      tmem_ld16(tb + S_LL, ll);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ctl->s_empty[sb]);
+    };
+    auto live_keys = [&](int j) { return max(0, min(16, last_key - (j * KT + 16 * g) + 1)); };
+
+    // ---- pass 0: row max of raw = q.k ----
+    // With head_dim 64 |256*mid + ll| <= B_MID (< 2^30), so raw is an exact
+    // i32 whenever |hh| <= 16384 (mx32); other elements take an i64 path that
+    // also keeps the row min for the i32 range check of the logits.
     int mx32 = INT_MIN;
     long long mx64 = LLONG_MIN, mn64 = LLONG_MAX;
-    // Per-row constants of passes 1 and 2 (see the element loop).
+    uint32_t it = 0;  // S tiles of passes 0 and 1, which alternate the two S buffers
+    for (int j = 0; j < ntiles; ++j, ++it) {
+      uint32_t hh[16], mid[16], ll[16];
+      fetch_s((int)(it & 1), hh, mid, ll);
+      const int nlive = live_keys(j);
+      if (__all_sync(FULLMASK, nlive == 16))
+        tile_max<true>(hh, mid, ll, nlive, mx32, mx64, mn64);
+      else
+        tile_max<false>(hh, mid, ll, nlive, mx32, mx64, mn64);
+    }
+    // Per-row constants of passes 1 and 2.
     uint32_t rawmax_lo = 0, cround = 0;
     int hh_floor = INT_MAX;
-    bool slow_row = false;
+    bool slow_row = false, row_fast = false, range_bad = false, masked_bad = false;
     long long rawmax = 0, lgmax = 0;
-    unsigned long long rsum = 0;
-    uint32_t inv = 0;
-    uint32_t use0 = 0, use1 = 0;  // uses of each S buffer, in the MMA issuer's order
-    uint32_t it = 0;            // items of the max and sum passes
-    bool range_bad = false, masked_bad = false;
+    {
+      // INT_MIN is never an exact-i32 raw value (> -2^30 - B_MID), so it marks "none".
+      long long rmx = max(mx32 == INT_MIN ? LLONG_MIN : (long long)mx32, mx64);
+      long long rmn = mn64;
+      xmax[g * QT + row] = rmx;
+      xmin[g * QT + row] = rmn;
+      named_sync_softmax();
+#pragma unroll
+      for (int o = 1; o < 4; ++o) {
+        rmx = max(rmx, xmax[((g + o) & 3) * QT + row]);
+        rmn = min(rmn, xmin[((g + o) & 3) * QT + row]);
+      }
+      if (row_live) {
+        rawmax = rmx;
+        lgmax = rawmax >> 3;
+        if (lgmax > INT_MAX || (rmn != LLONG_MAX && (rmn >> 3) < INT_MIN)) range_bad = true;
+        if (lgmax <= (long long)INT_MIN) masked_bad = true;  // every live logit masked or out of range
+        slow_row = lgmax < (long long)INT_MIN + 15 * 256;
+        rawmax_lo = (uint32_t)rawmax;
+        cround = 7u - (uint32_t)(rawmax & 7);
+        // candidates for w != 0: 65536*hh + B_MID > rawmax - 30720
+        const long long fl = (rawmax - 30720 - B_MID) >> 16;
+        hh_floor = (int)max((long long)INT_MIN, min((long long)INT_MAX, fl));
+        // no element of the row took the i64 path: every raw value of the
+        // row, rawmax included, is an exact i32 of magnitude <= 2^30 + B_MID
+        row_fast = rmn == LLONG_MAX;
+      }
+    }
+    const uint32_t cfast = rawmax_lo + cround;
+    const bool warp_fast = __all_sync(FULLMASK, row_fast || !row_live);
+    // Weights w of one S tile of this warp (0 for masked keys).
+    auto weights = [&](const uint32_t(&hh)[16], const uint32_t(&mid)[16], const uint32_t(&ll)[16], int nlive,
+                       uint32_t(&w)[16]) {
+      const bool full = __all_sync(FULLMASK, nlive == 16);
+      if (warp_fast) {
+        if (full)
+          weights_fast<true>(hh, mid, ll, nlive, cfast, lane4, w);
+        else
+          weights_fast<false>(hh, mid, ll, nlive, cfast, lane4, w);
+        return;
+      }
+      int wi[16];
+      if (!slow_row) {
+        if (full)
+          scores_weight<true>(hh, mid, ll, nlive, hh_floor, rawmax_lo, cround, lut, wi);
+        else
+          scores_weight<false>(hh, mid, ll, nlive, hh_floor, rawmax_lo, cround, lut, wi);
+      } else {
+        // Rows whose max logit lies within 15 * 256 of i32::MIN: exact i64
+        // path, with logits equal to MASKED_LOGIT excluded (attention.rs:266-276).
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          int v = 0;
+          if (i < nlive) {
+            const long long raw = (long long)(int)hh[i] * 65536 + (long long)(int)mid[i] * 256 + (long long)(int)ll[i];
+            const long long lg = raw >> 3;
+            const long long delta = lg - lgmax;
+            if (delta > -15 * 256 && lg != (long long)INT_MIN) {
+              const int mag = (int)(-delta);
+              v = (int)lut[mag & 255] >> (mag >> 8);
+            }
+          }
+          wi[i] = v;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) w[i] = (uint32_t)wi[i];
+    };
+
+    // ---- pass 1: weights and the row sum ----
     // WS: this thread's row of the weight scratch
-    int16_t* wrow = WS ? a.wscr + ((((long long)b * a.H + h) * gridDim.x + blockIdx.x) * QT + row) * a.wstride
-                       : nullptr;
-    // WS, last pass: this thread's 32 bytes of weights per tile, copied a tile
-    // ahead into slot [buffer][half][thread] (its own copies: no barrier)
+    int16_t* wrow = WS ? a.wscr + ((((long long)b * a.H + h) * gridDim.x + qt) * QT + row) * a.wstride : nullptr;
+    uint32_t rsum = 0;  // this thread's keys: at most 16384 / 4 weights below 2^15
+    for (int j = 0; j < ntiles; ++j, ++it) {
+      uint32_t hh[16], mid[16], ll[16], w[16];
+      fetch_s((int)(it & 1), hh, mid, ll);
+      weights(hh, mid, ll, live_keys(j), w);
+      rsum += sum16(w);
+      if (WS) {
+        uint4* dst = reinterpret_cast<uint4*>(wrow + j * KT + 16 * g);
+        dst[0] = make_uint4(__byte_perm(w[0], w[1], 0x5410), __byte_perm(w[2], w[3], 0x5410),
+                            __byte_perm(w[4], w[5], 0x5410), __byte_perm(w[6], w[7], 0x5410));
+        dst[1] = make_uint4(__byte_perm(w[8], w[9], 0x5410), __byte_perm(w[10], w[11], 0x5410),
+                            __byte_perm(w[12], w[13], 0x5410), __byte_perm(w[14], w[15], 0x5410));
+      }
+    }
+    uint32_t inv = 0;
+    {
+      unsigned long long tot = rsum;
+      xsum[g * QT + row] = tot;
+      named_sync_softmax();
+#pragma unroll
+      for (int o = 1; o < 4; ++o) tot += xsum[((g + o) & 3) * QT + row];
+      inv = (row_live && tot) ? recip_sum_q31(tot) : 0u;
+    }
+
+    // ---- pass 2: P = sat_i16(rhu(w * inv, 16)) as byte planes, O += P V ----
+    // WS: this thread's 32 bytes of weights per tile, copied a tile ahead into
+    // slot [buffer][half][thread] (its own copies: no barrier)
     const int sidx = threadIdx.x - 64;
     auto wpf_issue = [&](int j) {
       const int16_t* src = wrow + j * KT + 16 * g;  // keys below ntiles * 64 <= wstride, written in pass 1
@@ -339,155 +549,60 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
       cp_async16(dst + WPF_BUF / 2, src + 8);
       cp_async_commit();
     };
-    for (int pass = 0; pass < 3; ++pass) {
-      if (WS && pass == 2 && ntiles > 0) wpf_issue(0);
-      for (int j = 0; j < ntiles; ++j) {
-        const int key0 = j * KT + 16 * g;
-        const int nlive = max(0, min(16, last_key - key0 + 1));
-        int w[16];
-        if (WS && pass == 2) {
-          // weights of the sum pass (0 beyond the live keys)
-          if (j + 1 < ntiles) {
-            wpf_issue(j + 1);
-            cp_async_wait<1>();
-          } else {
-            cp_async_wait<0>();
-          }
-          const uint8_t* slot = sm + OFF_WPF + (j & 1) * WPF_BUF + sidx * 16;
-          const uint4 u0 = *reinterpret_cast<const uint4*>(slot);
-          const uint4 u1 = *reinterpret_cast<const uint4*>(slot + WPF_BUF / 2);
-          const uint32_t wv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            w[2 * i] = (int)(wv[i] & 0xFFFF);
-            w[2 * i + 1] = (int)(wv[i] >> 16);
-          }
+    if (WS && ntiles > 0) wpf_issue(0);
+    for (int j = 0; j < ntiles; ++j) {
+      const int key0 = j * KT + 16 * g;
+      uint32_t w[16];
+      if (WS) {
+        if (j + 1 < ntiles) {
+          wpf_issue(j + 1);
+          cp_async_wait<1>();
         } else {
-        const int sb = pass < 2 ? (int)(it++ & 1) : 0;
+          cp_async_wait<0>();
+        }
+        const uint8_t* slot = sm + OFF_WPF + (j & 1) * WPF_BUF + sidx * 16;
+        const uint4 u0 = *reinterpret_cast<const uint4*>(slot);
+        const uint4 u1 = *reinterpret_cast<const uint4*>(slot + WPF_BUF / 2);
+        const uint32_t wv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          w[2 * i] = wv[i] & 0xFFFFu;
+          w[2 * i + 1] = wv[i] >> 16;
+        }
+      } else {
         uint32_t hh[16], mid[16], ll[16];
-        wait_bar(&ctl->s_full[sb], (sb ? use1 : use0) & 1, ctl, a.st);
-        if (sb)
-          ++use1;
-        else
-          ++use0;
-        tc_fence_after();
-        const uint32_t tb = trow + (uint32_t)sb * S_BUF1 + 16 * g;
-        tmem_ld16(tb + S_HH, hh);
-        tmem_ld16(tb + S_MID, mid);
-        tmem_ld16(tb + S_LL, ll);
-        tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&ctl->s_empty[sb]);
-        const bool full = __all_sync(0xffffffffu, nlive == 16) != 0;
-        if (pass == 0) {
-          if (full)
-            scores_max<true>(hh, mid, ll, nlive, mx32, mx64, mn64);
-          else
-            scores_max<false>(hh, mid, ll, nlive, mx32, mx64, mn64);
-          continue;
-        }
-        if (!slow_row) {
-          if (full)
-            scores_weight<true>(hh, mid, ll, nlive, hh_floor, rawmax_lo, cround, lut, w);
-          else
-            scores_weight<false>(hh, mid, ll, nlive, hh_floor, rawmax_lo, cround, lut, w);
-        } else {
-          // Rows whose max logit lies within 15 * 256 of i32::MIN: exact i64
-          // path, with logits equal to MASKED_LOGIT excluded (attention.rs:266-276).
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            int wi = 0;
-            if (i < nlive) {
-              const long long raw =
-                  (long long)(int)hh[i] * 65536 + (long long)(int)mid[i] * 256 + (long long)(int)ll[i];
-              const long long lg = raw >> 3;
-              const long long delta = lg - lgmax;
-              if (delta > -15 * 256 && lg != (long long)INT_MIN) {
-                const int mag = (int)(-delta);
-                wi = (int)lut[mag & 255] >> (mag >> 8);
-              }
-            }
-            w[i] = wi;
-          }
-        }
-        if (WS && pass == 1) {
-          uint4* dst = reinterpret_cast<uint4*>(wrow + key0);
-          dst[0] = make_uint4((uint32_t)w[0] | ((uint32_t)w[1] << 16), (uint32_t)w[2] | ((uint32_t)w[3] << 16),
-                              (uint32_t)w[4] | ((uint32_t)w[5] << 16), (uint32_t)w[6] | ((uint32_t)w[7] << 16));
-          dst[1] = make_uint4((uint32_t)w[8] | ((uint32_t)w[9] << 16), (uint32_t)w[10] | ((uint32_t)w[11] << 16),
-                              (uint32_t)w[12] | ((uint32_t)w[13] << 16), (uint32_t)w[14] | ((uint32_t)w[15] << 16));
-        }
-        }
-        if (pass == 1) {
-          unsigned s = 0;
-#pragma unroll
-          for (int i = 0; i < 16; ++i) s += (unsigned)w[i];
-          rsum += s;
-          continue;
-        }
-        // pass 2: p = sat_i16(rhu(w * inv, 16)), w * inv < 2^47
-        uint32_t pw[8];
-#pragma unroll
-        for (int i = 0; i < 16; i += 2) {
-          const uint32_t p0 = (uint32_t)min(32767ull, ((unsigned long long)(uint32_t)w[i] * inv + 32768ull) >> 16);
-          const uint32_t p1 =
-              (uint32_t)min(32767ull, ((unsigned long long)(uint32_t)w[i + 1] * inv + 32768ull) >> 16);
-          pw[i / 2] = p0 | (p1 << 16);
-        }
-        if (a.probs && row_live && key0 < S) {  // nsrl-train/src/lib.rs:15353-15418: the cached P
-          uint4* dst = reinterpret_cast<uint4*>(a.probs + (((long long)b * a.H + h) * S + qi) * (long long)S + key0);
-          dst[0] = make_uint4(pw[0], pw[1], pw[2], pw[3]);
-          dst[1] = make_uint4(pw[4], pw[5], pw[6], pw[7]);
-        }
-        const int pb = j & 1;
-        if (j >= 2) wait_bar(&ctl->p_empty[pb], ((j >> 1) - 1) & 1, ctl, a.st);
-        uint8_t* ph = sm + OFF_P + pb * 2 * PLANE_P;
-        uint8_t* pl = ph + PLANE_P;
-        uint32_t hw[4], lw[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          hw[k] = __byte_perm(pw[2 * k], pw[2 * k + 1], 0x7531);
-          lw[k] = __byte_perm(pw[2 * k], pw[2 * k + 1], 0x6420);
-        }
-        const uint32_t off = swz64_chunk((uint32_t)row, (uint32_t)g);
-        *reinterpret_cast<uint4*>(ph + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-        *reinterpret_cast<uint4*>(pl + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&ctl->p_full[pb]);
+        fetch_s(0, hh, mid, ll);
+        weights(hh, mid, ll, live_keys(j), w);
       }
-      if (pass == 0) {
-        // INT_MIN is never an exact-i32 raw value (> -2^30 - B_MID), so it marks "none".
-        long long rmx = max(mx32 == INT_MIN ? LLONG_MIN : (long long)mx32, mx64);
-        long long rmn = mn64;
-        xmax[g * QT + row] = rmx;
-        xmin[g * QT + row] = rmn;
-        named_sync_softmax();
+      // w * inv + 2^15 < 2^47 + 2^15, so the value shifted by 16 fits in 32 bits
+      uint32_t pw[8];
 #pragma unroll
-        for (int o = 1; o < 4; ++o) {
-          rmx = max(rmx, xmax[((g + o) & 3) * QT + row]);
-          rmn = min(rmn, xmin[((g + o) & 3) * QT + row]);
-        }
-        if (row_live) {
-          rawmax = rmx;
-          lgmax = rawmax >> 3;
-          if (lgmax > INT_MAX || (rmn != LLONG_MAX && (rmn >> 3) < INT_MIN)) range_bad = true;
-          if (lgmax <= (long long)INT_MIN) masked_bad = true;  // every live logit masked or out of range
-          slow_row = lgmax < (long long)INT_MIN + 15 * 256;
-          rawmax_lo = (uint32_t)rawmax;
-          cround = 7u - (uint32_t)(rawmax & 7);
-          // candidates for w != 0: 65536*hh + B_MID > rawmax - 30720
-          const long long fl = (rawmax - 30720 - B_MID) >> 16;
-          hh_floor = (int)max((long long)INT_MIN, min((long long)INT_MAX, fl));
-        }
-      } else if (pass == 1) {
-        xsum[g * QT + row] = rsum;
-        named_sync_softmax();
-#pragma unroll
-        for (int o = 1; o < 4; ++o) rsum += xsum[((g + o) & 3) * QT + row];
-        inv = (row_live && rsum) ? recip_sum_q31(rsum) : 0u;
+      for (int i = 0; i < 8; ++i) {
+        const uint32_t p0 = min((uint32_t)(((unsigned long long)w[2 * i] * inv + 32768ull) >> 16), 32767u);
+        const uint32_t p1 = min((uint32_t)(((unsigned long long)w[2 * i + 1] * inv + 32768ull) >> 16), 32767u);
+        pw[i] = __byte_perm(p0, p1, 0x5410);
       }
+      if (a.probs && row_live && key0 < S) {  // nsrl-train/src/lib.rs:15353-15418: the cached P
+        uint4* dst = reinterpret_cast<uint4*>(a.probs + (((long long)b * a.H + h) * S + qi) * (long long)S + key0);
+        dst[0] = make_uint4(pw[0], pw[1], pw[2], pw[3]);
+        dst[1] = make_uint4(pw[4], pw[5], pw[6], pw[7]);
+      }
+      const int pb = j & 1;
+      if (j >= 2) wait_bar(&ctl->p_empty[pb], ((j >> 1) - 1) & 1, ctl, a.st);
+      uint8_t* ph = sm + OFF_P + pb * 2 * PLANE_P;
+      uint8_t* pl = ph + PLANE_P;
+      uint32_t hw[4], lw[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        hw[k] = __byte_perm(pw[2 * k], pw[2 * k + 1], 0x7531);
+        lw[k] = __byte_perm(pw[2 * k], pw[2 * k + 1], 0x6420);
+      }
+      const uint32_t off = swz64_chunk((uint32_t)row, (uint32_t)g);
+      *reinterpret_cast<uint4*>(ph + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+      *reinterpret_cast<uint4*>(pl + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ctl->p_full[pb]);
     }
     if (range_bad) nsrl_flag(a.st, NSRL_FLAG_LOGIT_RANGE);
     if (masked_bad) nsrl_flag(a.st, NSRL_FLAG_ALL_MASKED);
