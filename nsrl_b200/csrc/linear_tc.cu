@@ -615,8 +615,36 @@ struct CheckParams {
   nsrl_device_status* st;
 };
 
-__global__ void prefix_check_kernel(const CheckParams c) {
+constexpr int PREFIX_CHECK_THREADS = 256;
+
+// Rescans row m of the linear in the reference's order (bias, then k = 0, 1,
+// ...): any i32 prefix outside the range flags the call (linear.rs:282-296).
+__device__ void prefix_rescan_row(const CheckParams& c, int m, int lane) {
+  const int8_t* ah = c.a_hi + (long long)m * c.lda;
+  const uint8_t* al = c.a_lo + (long long)m * c.lda;
+  for (int sg = 0; sg < c.nseg; ++sg) {
+    for (int n = lane; n < c.rows[sg]; n += 32) {
+      const int8_t* w = c.w[sg] + (long long)n * c.K;
+      int acc = c.bias[sg] ? c.bias[sg][n] : 0;
+      bool bad = false;
+      for (int k = 0; k < c.K && !bad; ++k) {
+        int x = (int)ah[k] * 256 + (int)al[k];
+        long long t = (long long)acc + (long long)(x * (int)w[k]);
+        if (t < INT_MIN || t > INT_MAX) bad = true;
+        acc = (int)t;
+      }
+      if (bad) nsrl_flag(c.st, NSRL_FLAG_LINEAR_OVERFLOW);
+    }
+  }
+}
+
+// A row can overflow an i32 prefix only if |bias| + 127 * sum |x| > i32::MAX.
+// One thread per row tests that bound; the rows outside it (rare) are queued
+// in shared memory and rescanned exactly, one warp per row.
+__global__ void __launch_bounds__(PREFIX_CHECK_THREADS) prefix_check_kernel(const CheckParams c) {
   __shared__ long long s_maxb;
+  __shared__ int s_rows[PREFIX_CHECK_THREADS];
+  __shared__ int s_n;
   if (threadIdx.x == 0) s_maxb = 0;
   __syncthreads();
   long long mb = 0;
@@ -627,25 +655,15 @@ __global__ void prefix_check_kernel(const CheckParams c) {
   __syncthreads();
   const long long maxb = s_maxb;
   const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
-  for (int m = blockIdx.x * warps + (threadIdx.x >> 5); m < c.M; m += gridDim.x * warps) {
-    const long long bound = 127ll * (long long)c.l1[m] + maxb;
-    if (bound <= (long long)INT_MAX) continue;
-    const int8_t* ah = c.a_hi + (long long)m * c.lda;
-    const uint8_t* al = c.a_lo + (long long)m * c.lda;
-    for (int sg = 0; sg < c.nseg; ++sg) {
-      for (int n = lane; n < c.rows[sg]; n += 32) {
-        const int8_t* w = c.w[sg] + (long long)n * c.K;
-        int acc = c.bias[sg] ? c.bias[sg][n] : 0;
-        bool bad = false;
-        for (int k = 0; k < c.K && !bad; ++k) {
-          int x = (int)ah[k] * 256 + (int)al[k];
-          long long t = (long long)acc + (long long)(x * (int)w[k]);
-          if (t < INT_MIN || t > INT_MAX) bad = true;
-          acc = (int)t;
-        }
-        if (bad) nsrl_flag(c.st, NSRL_FLAG_LINEAR_OVERFLOW);
-      }
-    }
+  for (int base = blockIdx.x * PREFIX_CHECK_THREADS; base < c.M; base += gridDim.x * PREFIX_CHECK_THREADS) {
+    if (threadIdx.x == 0) s_n = 0;
+    __syncthreads();
+    const int m = base + (int)threadIdx.x;
+    if (m < c.M && 127ll * (long long)c.l1[m] + maxb > (long long)INT_MAX) s_rows[atomicAdd(&s_n, 1)] = m;
+    __syncthreads();
+    const int nq = s_n;
+    for (int qi = threadIdx.x >> 5; qi < nq; qi += warps) prefix_rescan_row(c, s_rows[qi], lane);
+    __syncthreads();
   }
 }
 
@@ -900,9 +918,10 @@ cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t stream) {
       c.rows[i] = (int)a.seg[i].rows;
     }
     c.st = a.st;
-    unsigned blocks = (unsigned)std::min<size_t>((a.M + 7) / 8, 4096);
+    const unsigned blocks =
+        (unsigned)std::min<size_t>((a.M + PREFIX_CHECK_THREADS - 1) / PREFIX_CHECK_THREADS, 148 * 8);
     ProfScope prof("linear_prefix_check", stream, 0.0, 8.0 * Mx);
-    prefix_check_kernel<<<blocks, 256, 0, stream>>>(c);
+    prefix_check_kernel<<<blocks, PREFIX_CHECK_THREADS, 0, stream>>>(c);
     err = cudaGetLastError();
   }
   return err;

@@ -93,6 +93,107 @@ __global__ void rms_norm_kernel(const int16_t* __restrict__ x, long long rows, i
   }
 }
 
+// Rows of d = 256 * VPL (VPL a power of two, so floor(ss / d) is a shift):
+// each warp normalises RPW rows at once with every row held in registers
+// (lane l owns 16-byte vectors l, l + 32, ...), so the loads of RPW rows are in
+// flight together and each row is read from memory once.
+template <int VPL, int RPW>
+__global__ void __launch_bounds__(256, VPL >= 4 ? 2 : 3) rms_norm_reg_kernel(
+    const int16_t* __restrict__ x, long long rows, const int16_t* __restrict__ g, unsigned long long eps,
+    int16_t* __restrict__ y, int8_t* __restrict__ yh, uint8_t* __restrict__ yl, unsigned long long* __restrict__ yl1,
+    long long ldp, nsrl_device_status* st) {
+  constexpr int D = 256 * VPL;
+  constexpr int LOG2D = VPL == 1 ? 8 : (VPL == 2 ? 9 : 10);
+  const int lane = threadIdx.x & 31;
+  const long long warp0 = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const long long nwarps = (long long)gridDim.x * (blockDim.x >> 5);
+  uint4 gv[VPL];
+#pragma unroll
+  for (int v = 0; v < VPL; ++v) gv[v] = reinterpret_cast<const uint4*>(g)[v * 32 + lane];
+  // rows of the group starting at r0 (a ragged last group re-reads the last row)
+  auto load_group = [&](long long r0, uint4(&xv)[RPW][VPL]) {
+#pragma unroll
+    for (int rr = 0; rr < RPW; ++rr) {
+      const long long r = min(r0 + rr, rows - 1);
+#pragma unroll
+      for (int v = 0; v < VPL; ++v) xv[rr][v] = __ldcs(reinterpret_cast<const uint4*>(x + r * D) + v * 32 + lane);
+    }
+  };
+  uint4 nxt[RPW][VPL];
+  if (warp0 * RPW < rows) load_group(warp0 * RPW, nxt);
+  for (long long r0 = warp0 * RPW; r0 < rows; r0 += nwarps * RPW) {
+    uint4 xv[RPW][VPL];
+#pragma unroll
+    for (int rr = 0; rr < RPW; ++rr)
+#pragma unroll
+      for (int v = 0; v < VPL; ++v) xv[rr][v] = nxt[rr][v];
+    // the next group's loads are in flight while this group is normalised
+    if (r0 + nwarps * RPW < rows) load_group(r0 + nwarps * RPW, nxt);
+    unsigned long long ss[RPW];
+#pragma unroll
+    for (int rr = 0; rr < RPW; ++rr) {
+      unsigned long long s = 0;
+#pragma unroll
+      for (int v = 0; v < VPL; ++v) {
+        const uint32_t w[4] = {xv[rr][v].x, xv[rr][v].y, xv[rr][v].z, xv[rr][v].w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {  // a pair of squares is at most 2^31
+          const int lo = (int)(int16_t)(w[k] & 0xFFFFu), hi = (int)w[k] >> 16;
+          s += (unsigned long long)((unsigned)(lo * lo) + (unsigned)(hi * hi));
+        }
+      }
+      ss[rr] = s;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int rr = 0; rr < RPW; ++rr) ss[rr] += __shfl_xor_sync(0xffffffffu, ss[rr], o);
+#pragma unroll
+    for (int rr = 0; rr < RPW; ++rr) {
+      const long long r = r0 + rr;
+      const unsigned long long mean = ss[rr] >> LOG2D;
+      const unsigned long long vsum = mean + eps;
+      int inv = 0;  // < 2^30
+      if (vsum < mean || vsum == 0) {  // u64 overflow of mean + eps, or rsqrt(0): the reference returns None
+        if (lane == 0 && r < rows) nsrl_flag(st, NSRL_FLAG_RMS_ZERO);
+      } else {
+        inv = (int)rsqrt_q30(vsum);
+      }
+      unsigned l1 = 0;
+#pragma unroll
+      for (int v = 0; v < VPL; ++v) {
+        const uint32_t xw[4] = {xv[rr][v].x, xv[rr][v].y, xv[rr][v].z, xv[rr][v].w};
+        const uint32_t gw[4] = {gv[v].x, gv[v].y, gv[v].z, gv[v].w};
+        uint32_t pk[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          // sat_i16(rhu(x * g * inv, 30)) with |x * g| <= 2^30, 0 <= inv < 2^30
+          const int p0 = (int)(int16_t)(xw[k] & 0xFFFFu) * (int)(int16_t)(gw[k] & 0xFFFFu);
+          const int p1 = ((int)xw[k] >> 16) * ((int)gw[k] >> 16);
+          const int o0 = sat16((int)(((long long)p0 * inv + (1ll << 29)) >> 30));
+          const int o1 = sat16((int)(((long long)p1 * inv + (1ll << 29)) >> 30));
+          l1 += (unsigned)(abs(o0) + abs(o1));
+          pk[k] = __byte_perm((uint32_t)o0, (uint32_t)o1, 0x5410);
+        }
+        if (r < rows) {
+          if (y) __stcs(reinterpret_cast<uint4*>(y + r * D) + v * 32 + lane, make_uint4(pk[0], pk[1], pk[2], pk[3]));
+          if (yh) {
+            reinterpret_cast<uint2*>(yh + r * ldp)[v * 32 + lane] =
+                make_uint2(__byte_perm(pk[0], pk[1], 0x7531), __byte_perm(pk[2], pk[3], 0x7531));
+            reinterpret_cast<uint2*>(yl + r * ldp)[v * 32 + lane] =
+                make_uint2(__byte_perm(pk[0], pk[1], 0x6420), __byte_perm(pk[2], pk[3], 0x6420));
+          }
+        }
+      }
+      if (yl1) {  // per row at most D * 32768 < 2^26
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+        if (lane == 0 && r < rows) yl1[r] = l1;
+      }
+    }
+  }
+}
+
 }  // namespace
 
 cudaError_t launch_rms_norm(const int16_t* x, size_t rows, size_t d, const int16_t* gamma, uint64_t eps,
@@ -104,7 +205,21 @@ cudaError_t launch_rms_norm(const int16_t* x, size_t rows, size_t d, const int16
                    (!yp.hi || ((reinterpret_cast<uintptr_t>(yp.hi) | reinterpret_cast<uintptr_t>(yp.lo)) % 8 == 0 &&
                                yp.ld % 8 == 0));
   ProfScope prof("rms_norm", stream, 0.0, 4.0 * rows * d + (yp.l1 ? 8.0 * rows : 0.0));
-  if (vec)
+  if (vec && (d == 256 || d == 512 || d == 1024)) {
+    const size_t rpw = d == 256 ? 2 : 1;
+    const size_t groups = (rows + rpw - 1) / rpw;
+    const unsigned nb = (unsigned)std::min<size_t>((groups + 7) / 8, d == 1024 ? 148 * 2 : 148 * 3);
+#define NSRL_RMS_REG(VPL)                                                                                  \
+  rms_norm_reg_kernel<VPL, (VPL == 1 ? 2 : 1)><<<nb, 256, 0, stream>>>(x, (long long)rows, gamma, eps, y_i16,   \
+                                                                        yp.hi, yp.lo, yp.l1, (long long)yp.ld, st)
+    if (d == 256)
+      NSRL_RMS_REG(1);
+    else if (d == 512)
+      NSRL_RMS_REG(2);
+    else
+      NSRL_RMS_REG(4);
+#undef NSRL_RMS_REG
+  } else if (vec)
     rms_norm_kernel<true><<<blocks, 256, 0, stream>>>(x, (long long)rows, (int)d, 1.0 / (double)d, gamma, eps, y_i16,
                                                       yp.hi, yp.lo, yp.l1, (long long)yp.ld, st);
   else

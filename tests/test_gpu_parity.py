@@ -101,7 +101,8 @@ def test_linear_rejects_prefix_overflow_with_fitting_total(core):
 
 
 # --------------------------------------------------------------- rms norm ---
-@pytest.mark.parametrize("rows,d,eps", [(1000, 256, 1), (37, 100, 1), (8, 4, 0), (3, 4096, 7)])
+@pytest.mark.parametrize("rows,d,eps", [(1000, 256, 1), (1001, 256, 1), (77, 512, 3), (33, 1024, 1), (37, 100, 1),
+                                        (8, 4, 0), (3, 4096, 7)])
 def test_rms_norm_parity(core, rows, d, eps):
     x = Y.q15_gaussian(d + rows, (rows, d))
     x[0, :] = 0
