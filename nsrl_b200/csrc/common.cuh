@@ -212,6 +212,7 @@ __device__ __forceinline__ unsigned long long global_ns() {
 // unwind (the host then reports the call as failed).
 #define NSRL_WAIT_NS 2000000000ull
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, nsrl_device_status* st) {
+  if (mbar_try_wait(bar, parity)) return true;  // the common case reads no timer
   const unsigned long long t0 = global_ns();
   for (uint32_t i = 0;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;

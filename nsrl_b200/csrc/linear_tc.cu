@@ -85,6 +85,8 @@ __device__ __forceinline__ int requant_fast(int acc, int mult, uint32_t shift) {
   return (int)sat_i16(rhu64((long long)acc * (long long)mult, shift));
 }
 
+__device__ __forceinline__ int clamp16(int v) { return max(-32768, min(32767, v)); }
+
 __device__ __forceinline__ uint32_t pack2(int a, int b) { return (uint32_t)(a & 0xFFFF) | ((uint32_t)b << 16); }
 
 // Per-lane copy of the scale (and bias) of column `lane` of a chunk, plus a
@@ -124,16 +126,16 @@ __device__ __forceinline__ void requant_cols(const uint32_t (&h)[W], const uint3
     const uint32_t s = (uint32_t)c.ushift;
     if (s == 0) {
 #pragma unroll
-      for (int i = 0; i < W; ++i) v[i] = sat16((int)(h[i] * 256u + l[i]));
+      for (int i = 0; i < W; ++i) v[i] = clamp16((int)(h[i] * 256u + l[i]));
     } else if (s < 32 && small) {
       const int half = 1 << (s - 1);
 #pragma unroll
-      for (int i = 0; i < W; ++i) v[i] = sat16(((int)(h[i] * 256u + l[i]) + half) >> s);
+      for (int i = 0; i < W; ++i) v[i] = clamp16(((int)(h[i] * 256u + l[i]) + half) >> s);
     } else if (s < 32) {
 #pragma unroll
       for (int i = 0; i < W; ++i) {
         const int acc = (int)(h[i] * 256u + l[i]);
-        v[i] = sat16((acc >> s) + ((acc >> (s - 1)) & 1));
+        v[i] = clamp16((acc >> s) + ((acc >> (s - 1)) & 1));
       }
     } else {
 #pragma unroll
@@ -211,6 +213,38 @@ __device__ __forceinline__ void store16_planes(int8_t* dh, uint8_t* dl, const ui
       }
     }
   }
+}
+
+// Splits 16 packed int16 values into hi / lo byte planes.
+__device__ __forceinline__ void store16_planes_nol1(int8_t* dh, uint8_t* dl, const uint32_t (&o)[8], int nvalid,
+                                                    bool vec_ok) {
+  if (vec_ok && nvalid == 16) {
+    uint32_t hw[4], lw[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      hw[i] = __byte_perm(o[2 * i], o[2 * i + 1], 0x7531);
+      lw[i] = __byte_perm(o[2 * i], o[2 * i + 1], 0x6420);
+    }
+    *reinterpret_cast<uint4*>(dh) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    *reinterpret_cast<uint4*>(dl) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      if (i < nvalid) {
+        const int v = (int16_t)(o[i / 2] >> (16 * (i & 1)));
+        dh[i] = (int8_t)(v >> 8);
+        dl[i] = (uint8_t)(v & 255);
+      }
+    }
+  }
+}
+
+// mlp.rs:150-170 on values already in [-32768, 32767] (int arguments, no
+// conversions); the result lies within +-24575 (see gated_act).
+__device__ __forceinline__ int gated_act_i32(int up, int gate) {
+  const int gv = (gate >> 2) + 16384;
+  const int silu = (gate * gv + 16384) >> 15;
+  return (up * silu + 16384) >> 15;
 }
 
 __device__ __forceinline__ void store32_i16(int16_t* dst, const uint32_t (&o)[16], int nvalid, bool vec_ok) {
@@ -404,14 +438,20 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
         int up[16], gt[16];
         requant16(hu, lu, su, up, p.small_acc);
         requant16(hg, lg, sg, gt, p.small_acc);
+        int act[16];
+        unsigned a1 = 0;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          act[i] = gated_act_i32(up[i], gt[i]);
+          a1 += (i < nvalid) ? (unsigned)abs(act[i]) : 0u;
+        }
         uint32_t o[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-          o[i] = pack2(gated_act((int16_t)up[2 * i], (int16_t)gt[2 * i]),
-                       gated_act((int16_t)up[2 * i + 1], (int16_t)gt[2 * i + 1]));
+        for (int i = 0; i < 8; ++i) o[i] = __byte_perm((uint32_t)act[2 * i], (uint32_t)act[2 * i + 1], 0x5410);
         if (row_ok && nvalid > 0) {
           const long long off = (long long)r * p.ldp + fb;
-          store16_planes(p.yh + off, p.yl + off, o, nvalid, ((p.ldp | fb) & 15) == 0, l1);
+          l1 += a1;
+          store16_planes_nol1(p.yh + off, p.yl + off, o, nvalid, ((p.ldp | fb) & 15) == 0);
         }
       } else {
         const int nb = nt * BN;
@@ -483,13 +523,14 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
               // v columns: byte stores into [b][h][dim][s]; the 32 lanes of the
               // warp hold 32 consecutive positions, so each store instruction
               // writes one contiguous 32-byte run per plane.
+              // [b][h][dim][s] is contiguous over (h, dim): row (b, c) of the
+              // planes is b * H * hd + c for value column c.
               const int b = r / p.vt_S, spos = r % p.vt_S;
-              const int c0 = n - p.vt_col0;
+              const long long off0 = ((long long)b * (p.vt_H * p.vt_hd) + (n - p.vt_col0)) * p.vt_S + spos;
 #pragma unroll
               for (int i = 0; i < 32; ++i) {
                 if (i < nvalid) {
-                  const int c = c0 + i, hh = c / p.vt_hd, dd = c % p.vt_hd;
-                  const long long off = ((long long)(b * p.vt_H + hh) * p.vt_hd + dd) * p.vt_S + spos;
+                  const long long off = off0 + (long long)i * p.vt_S;
                   p.vth[off] = (int8_t)(v[i] >> 8);
                   p.vtl[off] = (uint8_t)(v[i] & 255);
                 }
