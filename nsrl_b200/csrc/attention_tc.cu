@@ -4,44 +4,54 @@
 // Reference: crates/nsrl-core/src/attention.rs:742-877 (full attention),
 // :261-293 (base-2 softmax), :117-140 (QK dot), :596-668 (AV).
 //
-// One CTA per (128-query tile, head, sequence); 18 warps:
-//   warp 0      TMA producer: Q planes once, then per 64-key tile the K planes
-//               (and in the last pass the transposed V planes)
-//   warp 1      TMEM allocator + single-thread MMA issuer
-//   warps 2..17 softmax: warp w owns query rows 32*(w%4) .. +31 (its TMEM lane
-//               quarter) and key columns [16*g, 16*g+16) of each key tile,
-//               g = (w-2)/4
-// q.k = 65536*(qh.kh) + 256*(qh.kl + ql.kh) + ql.kl: each S tile (128 x 64)
-// is three s32 TMEM accumulators (hh, mid, ll), recombined in i64 by the
-// softmax warps.  The probabilities are rounded to Q15 with the reciprocal of
+// One CTA per (128-query tile, head, pair of sequences): two independent
+// groups of 10 warps, one per sequence, so that the row exchanges, the
+// first-tile latency and the tail of one group overlap the steady state of the
+// other.  The warps of a group:
+//   warp 0     TMA producer: Q planes once, then per 32-key tile the K planes
+//              (max and sum passes) or the transposed V planes (last pass)
+//   warp 1     TMEM allocator + single-thread MMA issuer
+//   warps 2..9 softmax: warp w owns query rows 32*(w%4) .. +31 (its TMEM lane
+//              quarter) and keys [16*g, 16*g+16) of each 32-key tile,
+//              g = (w-2)/4
+// q.k = 65536*(qh.kh) + 256*(qh.kl + ql.kh) + ql.kl: each S tile (128 x 32)
+// is three s32 TMEM accumulators (hh, mid, ll) that the softmax warps
+// recombine, in exact 32-bit arithmetic where a guard proves it exact and in
+// i64 otherwise.  The probabilities are rounded to Q15 with the reciprocal of
 // the complete row sum before the AV product (attention.rs:285-290), so the
-// keys are swept three times: row max, row sum, then P and O = P V.  P is
-// written to shared memory as byte planes (ph <= 127, pl) in the MMA's
-// K-major layout; O = P V uses three more s32 accumulators (65536*hh +
-// 256*mid + ll), exact for up to 16384 keys.
+// keys are swept three times: row max, row sum (whose weights go to a global
+// scratch), then P = sat(rhu(w * inv, 16)) and O = P V.  P is written to
+// shared memory as byte planes (ph <= 127, pl) in the MMA's K-major layout;
+// O = P V uses three more s32 accumulators (65536*hh + 256*mid + ll), exact
+// for up to 16384 keys.
 //
-// TMEM (512 columns): S hh/mid/ll at [0,192) and, in the max and sum passes,
-// a second S buffer at [256,448); O hh/mid/ll at [256,448) in the last pass
-// (the second S buffer is no longer used by then).
-// Operand tiles use the 64-byte swizzle (rows of 64 bytes), as TMA writes it.
+// TMEM (256 columns per group): two S buffers of 3 x 32 columns at [0, 96) and
+// [96, 192) in the max and sum passes; O hh/mid/ll (3 x 64 columns) at
+// [0, 192) in the last pass, which reads no S.
+// Q and K tiles use the 64-byte swizzle (rows of 64 bytes), P and V^T tiles
+// the 32-byte swizzle (rows of 32 bytes), as TMA writes them.
 #include "common.cuh"
 #include "internal.h"
 
 namespace nsrl {
 namespace {
 
-constexpr int QT = 128, KT = 64, HD = 64;
+constexpr int QT = 128, KT = 32, HD = 64;
 constexpr int ST = 4;                 // K / V^T stage ring
 constexpr int PLANE_Q = QT * HD;      // 8 KB per plane
-constexpr int PLANE_K = KT * HD;      // 4 KB
-constexpr int PLANE_V = HD * KT;      // 4 KB
-constexpr int STAGE_BYTES = 2 * PLANE_K + 2 * PLANE_V;
-constexpr int PLANE_P = QT * KT;      // 8 KB
-constexpr int SOFTMAX_WARPS = 16;
-constexpr int THREADS = 64 + 32 * SOFTMAX_WARPS;
-constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t S_HH = 0, S_MID = 64, S_LL = 128, O_HH = 256, O_MID = 320, O_LL = 384;
-constexpr uint32_t S_BUF1 = 256;  // column offset of the second S buffer
+constexpr int PLANE_K = KT * HD;      // 2 KB: 32 keys x 64 dims
+constexpr int PLANE_V = HD * KT;      // 2 KB: 64 dims x 32 keys
+static_assert(PLANE_K == PLANE_V, "a stage holds either K or V^T planes");
+constexpr int STAGE_BYTES = 2 * PLANE_K;
+constexpr int PLANE_P = QT * KT;      // 4 KB
+constexpr int SOFTMAX_WARPS = 8;
+constexpr int GROUP_WARPS = 2 + SOFTMAX_WARPS;          // producer, MMA issuer, softmax warps
+constexpr int GROUPS = 2;
+constexpr int GROUP_THREADS = 32 * GROUP_WARPS;
+constexpr int THREADS = GROUPS * GROUP_THREADS;
+constexpr uint32_t TMEM_COLS = 512;                     // 256 per group
+constexpr uint32_t S_HH = 0, S_MID = 32, S_LL = 64, S_BUF1 = 96;
+constexpr uint32_t O_HH = 0, O_MID = 64, O_LL = 128;
 // Bound on |256 * mid + ll| of one 64-dim dot product: |mid| <= 64 * 2 * 128 * 255,
 // 0 <= ll <= 64 * 255 * 255.
 constexpr long long B_MID = 64LL * 2 * 128 * 255 * 256 + 64LL * 255 * 255;
@@ -49,21 +59,23 @@ constexpr long long B_MID = 64LL * 2 * 128 * 255 * 256 + 64LL * 255 * 255;
 constexpr int OFF_Q = 0;
 constexpr int OFF_STAGE = OFF_Q + 2 * PLANE_Q;
 constexpr int OFF_P = OFF_STAGE + ST * STAGE_BYTES;
-constexpr int OFF_X = OFF_P + 2 * 2 * PLANE_P;  // row-statistics exchange
-constexpr int X_BYTES = 4 * QT * 8 * 3;
+constexpr int OFF_X = OFF_P + 2 * 2 * PLANE_P;  // row-statistics exchange: max, min, sum of [2][QT]
+constexpr int X_BYTES = 2 * QT * 8 * 3;
 constexpr int OFF_LUT = OFF_X + X_BYTES;
-constexpr int OFF_WPF = OFF_LUT + 512;               // WS weights of the next tile: [2 buffers][2 halves][512 threads] x 16 B
-constexpr int WPF_BUF = 2 * 32 * SOFTMAX_WARPS * 16;
-constexpr int OFF_BAR = OFF_WPF + 2 * WPF_BUF;
-constexpr size_t SMEM_BYTES = OFF_BAR + 256 + 1024;
+constexpr int WPF_BUF = 2 * 32 * SOFTMAX_WARPS * 16;  // last-pass weights of one tile: [2 halves][256 threads] x 16 B
+constexpr int WPF_N = 4;                              // tile buffers; the copies run WPF_N - 1 tiles ahead
+constexpr int OFF_WPF = OFF_LUT + 512;
+constexpr int OFF_BAR = OFF_WPF + WPF_N * WPF_BUF;
+constexpr int GROUP_BYTES = (OFF_BAR + 256 + 1023) / 1024 * 1024;  // one group's region (offsets above are within it)
+constexpr size_t SMEM_BYTES = (size_t)GROUPS * GROUP_BYTES + 1024;
 
 struct Maps {
-  CUtensorMap q_hi, q_lo, k_hi, k_lo, vt_hi, vt_lo;  // q: 128-row boxes, k: 64-row boxes
+  CUtensorMap q_hi, q_lo, k_hi, k_lo, vt_hi, vt_lo;  // q: 128-row boxes, k: 32-row boxes, vt: 64 x 32-byte boxes
 };
 
 struct Args {
-  int S, d, H, causal, shift;
-  int16_t* wscr;     // WS: per-CTA scratch of the sum pass's weights w, [128 rows][wstride]
+  int S, d, H, causal, b0, nb;  // sequences [b0, b0 + nb) in this launch (batch chunks)
+  int16_t* wscr;     // per-CTA scratch of the sum pass's weights w, [128 rows][wstride]
   long long wstride; // S rounded up to a multiple of 64
   int8_t* ctx_hi;
   uint8_t* ctx_lo;
@@ -78,9 +90,15 @@ __device__ __forceinline__ uint64_t sdesc_k64(uint32_t saddr) {
   return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(512 >> 4) << 32) |
          ((uint64_t)1 << 46) | ((uint64_t)4 << 61);
 }
+// Shared-memory descriptor, K-major, 32-byte swizzle: 8-row atoms of 256 B.
+__device__ __forceinline__ uint64_t sdesc_k32(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(256 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)6 << 61);
+}
 
-// Byte offset of 16-byte chunk c (0..3) of row r in a 64-byte-swizzled tile.
-__device__ __forceinline__ uint32_t swz64_chunk(uint32_t r, uint32_t c) { return r * 64u + ((c ^ ((r >> 1) & 3u)) << 4); }
+// Byte offset of 16-byte chunk c (0..1) of row r in a 32-byte-swizzled tile
+// (address bit 4 ^= bit 7).
+__device__ __forceinline__ uint32_t swz32_chunk(uint32_t r, uint32_t c) { return r * 32u + ((c ^ ((r >> 2) & 1u)) << 4); }
 
 struct Ctl {
   uint64_t q_full, full[ST], empty[ST], s_full[2], s_empty[2], p_full[2], p_empty[2], o_full;
@@ -95,7 +113,10 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, Ctl* c,
   return false;
 }
 
-__device__ __forceinline__ void named_sync_softmax() { asm volatile("bar.sync 1, %0;" ::"n"(32 * SOFTMAX_WARPS)); }
+// Barrier of one group's softmax warps (ids 1 and 2; 0 is __syncthreads).
+__device__ __forceinline__ void named_sync_softmax(int grp) {
+  asm volatile("bar.sync %0, %1;" ::"r"(1 + grp), "n"(32 * SOFTMAX_WARPS));
+}
 
 // Pass-0 update of one warp's 16 scores.  raw = 65536*hh + 256*mid + ll is an
 // exact i32 when |hh| <= 16384 (|256*mid + ll| <= B_MID < 2^30); then the
@@ -147,8 +168,9 @@ constexpr uint32_t FULLMASK = 0xffffffffu;
 // The exp2 table replicated once per lane, s_lutr[32 * f + lane] =
 // EXP2_NEG_FRAC_LUT_8BIT[f] (attention.rs:142-158): lane i reads bank i only,
 // so the random table lookups of a warp never conflict.  A static shared
-// array, so its address is a constant of the load instruction.
-__shared__ uint32_t s_lutr[256 * 32];
+// array, so its address is a constant of the load instruction; 16-byte
+// aligned for the vector stores that fill it.
+__shared__ __align__(16) uint32_t s_lutr[256 * 32];
 
 // x >> s for every s; amounts of 32 or more give 0 (PTX shr clamps them).
 __device__ __forceinline__ uint32_t shr_clamp(uint32_t x, uint32_t s) {
@@ -223,37 +245,44 @@ __device__ __forceinline__ void weights_fast(const uint32_t (&hh)[16], const uin
   }
 }
 
-// WS: the sum pass stores its weights w (int16) in global scratch and the
-// last pass reads them back instead of recomputing S (no K tiles, no QK MMAs).
-// The last pass stages the next tile's weights in shared memory with
-// cp.async (no registers held across the tile loop).
-template <bool WS>
+// A kernel that allocates TMEM runs one CTA per SM, so the CTA holds two
+// independent groups of 10 warps (producer, MMA issuer, 8 softmax warps), each
+// on its own sequence with its own shared-memory region, barriers and 256 TMEM
+// columns: the row exchanges, first-tile latency and tail of one group overlap
+// the steady state of the other.
 __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_constant__ Maps maps, const Args a) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint32_t s_abort, s_tslot;
+  const int gw = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int grp = gw / GROUP_WARPS, warp = gw % GROUP_WARPS;  // group, warp within the group
+  const int gtid = (int)threadIdx.x - grp * GROUP_THREADS;    // thread within the group
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023)) +
+                grp * GROUP_BYTES;
   Ctl* ctl = reinterpret_cast<Ctl*>(sm + OFF_BAR);
   int16_t* lut = reinterpret_cast<int16_t*>(sm + OFF_LUT);
-  long long* xmax = reinterpret_cast<long long*>(sm + OFF_X);  // [4][QT]
-  long long* xmin = xmax + 4 * QT;                             // [4][QT]
-  unsigned long long* xsum = reinterpret_cast<unsigned long long*>(xmin + 4 * QT);
+  long long* xmax = reinterpret_cast<long long*>(sm + OFF_X);  // [2][QT]
+  long long* xmin = xmax + 2 * QT;                             // [2][QT]
+  unsigned long long* xsum = reinterpret_cast<unsigned long long*>(xmin + 2 * QT);
 
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // query tiles in reverse order: the causal CTAs with the most key tiles
-  // start first and the short ones fill the tail of the grid
-  const int qt = (int)gridDim.x - 1 - (int)blockIdx.x;
-  const int q0 = qt * QT, h = blockIdx.y, b = blockIdx.z;
+  // The query tile is the slowest grid dimension and runs in reverse: every
+  // causal CTA with the most key tiles starts before any with fewer, and the
+  // shortest fill the tail of the grid.
+  const int nq = (int)gridDim.z, qt = nq - 1 - (int)blockIdx.z;
+  const int q0 = qt * QT, h = blockIdx.x, bl = GROUPS * blockIdx.y + grp, b = a.b0 + bl;
+  const bool active = bl < a.nb;  // an odd batch leaves the last CTA's second group idle
   const int S = a.S;
   const int kend = a.causal ? min(S, q0 + QT) : S;
   const int ntiles = (kend + KT - 1) / KT;
 
-  if (threadIdx.x == 0) ctl->abort = timed_out(a.st) ? 1u : 0u;
-  for (int i = threadIdx.x; i < 256; i += THREADS) lut[i] = d_exp2_lut[i];
+  if (threadIdx.x == 0) s_abort = timed_out(a.st) ? 1u : 0u;
+  if (gtid == 0) ctl->abort = 0u;
+  for (int i = gtid; i < 256; i += GROUP_THREADS) lut[i] = d_exp2_lut[i];
   for (int i = threadIdx.x; i < 256 * 8; i += THREADS) {
     const uint32_t v = (uint32_t)(uint16_t)d_exp2_lut[i >> 3];
     reinterpret_cast<uint4*>(s_lutr)[i] = make_uint4(v, v, v, v);
   }
   __syncthreads();
-  if (ctl->abort) return;
+  if (s_abort) return;  // a wait of this call already timed out: the whole CTA skips its work
 
   if (warp == 0 && lane == 0) {
     mbar_init(&ctl->q_full, 1);
@@ -264,25 +293,25 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
     for (int i = 0; i < 2; ++i) {
       mbar_init(&ctl->s_full[i], 1);
       mbar_init(&ctl->s_empty[i], SOFTMAX_WARPS);
-    }
-    for (int i = 0; i < 2; ++i) {
       mbar_init(&ctl->p_full[i], SOFTMAX_WARPS);
       mbar_init(&ctl->p_empty[i], 1);
     }
     mbar_init(&ctl->o_full, 1);
     fence_barrier_init();
   }
-  if (warp == 1) {
-    tmem_alloc(&ctl->tslot, TMEM_COLS);
+  if (gw == 1) {
+    tmem_alloc(&s_tslot, TMEM_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = ctl->tslot;
+  const uint32_t tmem = s_tslot + 256u * (uint32_t)grp;  // this group's 256 columns
   const int row0 = b * S;  // first token row of this sequence
 
-  if (warp == 0) {
+  if (!active) {
+    // idle group: nothing to do before the final barrier
+  } else if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       mbar_arrive_expect_tx(&ctl->q_full, 2 * PLANE_Q);
@@ -298,16 +327,14 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
             break;
           }
           uint8_t* stg = sm + OFF_STAGE + s * STAGE_BYTES;
-          const bool kload = !(WS && pass == 2);
-          mbar_arrive_expect_tx(&ctl->full[s], (kload ? 2 * PLANE_K : 0) + (pass == 2 ? 2 * PLANE_V : 0));
-          if (kload) {
+          mbar_arrive_expect_tx(&ctl->full[s], STAGE_BYTES);
+          if (pass < 2) {  // K rows j*32 .. +31 of this head
             tma_load_2d(stg, &maps.k_hi, &ctl->full[s], a.d + h * HD, row0 + j * KT);
             tma_load_2d(stg + PLANE_K, &maps.k_lo, &ctl->full[s], a.d + h * HD, row0 + j * KT);
-          }
-          if (pass == 2) {
+          } else {         // V^T: 64 dims x keys j*32 .. +31
             const int vrow = (b * a.H + h) * HD;
-            tma_load_2d(stg + 2 * PLANE_K, &maps.vt_hi, &ctl->full[s], j * KT, vrow);
-            tma_load_2d(stg + 2 * PLANE_K + PLANE_V, &maps.vt_lo, &ctl->full[s], j * KT, vrow);
+            tma_load_2d(stg, &maps.vt_hi, &ctl->full[s], j * KT, vrow);
+            tma_load_2d(stg + PLANE_V, &maps.vt_lo, &ctl->full[s], j * KT, vrow);
           }
         }
       }
@@ -319,70 +346,55 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
     if (lane == 0) {
       const uint32_t id_ss = idesc_i8(QT, KT, 1, 1), id_su = idesc_i8(QT, KT, 1, 0);
       const uint32_t id_us = idesc_i8(QT, KT, 0, 1), id_uu = idesc_i8(QT, KT, 0, 0);
+      const uint32_t pv_us = idesc_i8(QT, HD, 0, 1), pv_uu = idesc_i8(QT, HD, 0, 0);
       const uint32_t qh = smem_u32(sm + OFF_Q), ql = qh + PLANE_Q;
       uint32_t use0 = 0, use1 = 0;  // uses of each S buffer
       wait_bar(&ctl->q_full, 0, ctl, a.st);
-      auto issue_s = [&](int s, int sb) {
-        const uint32_t n = sb ? use1 : use0;
-        if (n > 0) wait_bar(&ctl->s_empty[sb], (n - 1) & 1, ctl, a.st);
-        tc_fence_after();
-        const uint32_t kh = smem_u32(sm + OFF_STAGE + s * STAGE_BYTES), kl = kh + PLANE_K;
-        const uint32_t d = tmem + (uint32_t)sb * S_BUF1;
-#pragma unroll
-        for (int ks = 0; ks < HD / 32; ++ks) {
-          const uint64_t aqh = sdesc_k64(qh + 32 * ks), aql = sdesc_k64(ql + 32 * ks);
-          const uint64_t bkh = sdesc_k64(kh + 32 * ks), bkl = sdesc_k64(kl + 32 * ks);
-          const uint32_t acc = ks > 0 ? 1u : 0u;
-          umma_i8(d + S_HH, aqh, bkh, id_ss, acc);
-          umma_i8(d + S_MID, aqh, bkl, id_su, acc);
-          umma_i8(d + S_MID, aql, bkh, id_us, 1u);
-          umma_i8(d + S_LL, aql, bkl, id_uu, acc);
-        }
-        umma_commit(&ctl->s_full[sb]);
-        if (sb)
-          ++use1;
-        else
-          ++use0;
-      };
       uint32_t it = 0;
       for (int pass = 0; pass < 2; ++pass) {
         for (int j = 0; j < ntiles; ++j, ++it) {
           const int s = it % ST;
+          const int sb = (int)(it & 1);
           wait_bar(&ctl->full[s], (it / ST) & 1, ctl, a.st);
-          issue_s(s, (int)(it & 1));
+          const uint32_t n = sb ? use1 : use0;
+          if (n > 0) wait_bar(&ctl->s_empty[sb], (n - 1) & 1, ctl, a.st);
+          tc_fence_after();
+          const uint32_t kh = smem_u32(sm + OFF_STAGE + s * STAGE_BYTES), kl = kh + PLANE_K;
+          const uint32_t d = tmem + (uint32_t)sb * S_BUF1;
+#pragma unroll
+          for (int ks = 0; ks < HD / 32; ++ks) {
+            const uint64_t aqh = sdesc_k64(qh + 32 * ks), aql = sdesc_k64(ql + 32 * ks);
+            const uint64_t bkh = sdesc_k64(kh + 32 * ks), bkl = sdesc_k64(kl + 32 * ks);
+            const uint32_t acc = ks > 0 ? 1u : 0u;
+            umma_i8(d + S_HH, aqh, bkh, id_ss, acc);
+            umma_i8(d + S_MID, aqh, bkl, id_su, acc);
+            umma_i8(d + S_MID, aql, bkh, id_us, 1u);
+            umma_i8(d + S_LL, aql, bkl, id_uu, acc);
+          }
+          umma_commit(&ctl->s_full[sb]);
           umma_commit(&ctl->empty[s]);
+          if (sb)
+            ++use1;
+          else
+            ++use0;
         }
       }
-      // pass 2: S(j+1) is issued before O += P(j) V(j) so that the softmax
-      // warps can work on tile j+1 while the tensor core does the AV product.
-      const uint32_t base = it;
-      if (!WS) {
-        wait_bar(&ctl->full[base % ST], (base / ST) & 1, ctl, a.st);
-        issue_s(base % ST, 0);
-      }
-      for (int j = 0; j < ntiles; ++j) {
-        if (!WS && j + 1 < ntiles) {
-          const uint32_t n1 = base + j + 1;
-          wait_bar(&ctl->full[n1 % ST], (n1 / ST) & 1, ctl, a.st);
-          issue_s(n1 % ST, 0);
-        }
-        if (WS) wait_bar(&ctl->full[(base + j) % ST], ((base + j) / ST) & 1, ctl, a.st);
+      // last pass: O += P(j) V(j), one 32-key K step per tile
+      for (int j = 0; j < ntiles; ++j, ++it) {
+        const int s = it % ST;
+        wait_bar(&ctl->full[s], (it / ST) & 1, ctl, a.st);
         const int pb = j & 1;
         wait_bar(&ctl->p_full[pb], (j >> 1) & 1, ctl, a.st);
         tc_fence_after();
-        const uint32_t s = (base + j) % ST;
-        const uint32_t vh = smem_u32(sm + OFF_STAGE + s * STAGE_BYTES + 2 * PLANE_K), vl = vh + PLANE_V;
+        const uint32_t vh = smem_u32(sm + OFF_STAGE + s * STAGE_BYTES), vl = vh + PLANE_V;
         const uint32_t ph = smem_u32(sm + OFF_P + pb * 2 * PLANE_P), pl = ph + PLANE_P;
-#pragma unroll
-        for (int ks = 0; ks < KT / 32; ++ks) {
-          const uint64_t aph = sdesc_k64(ph + 32 * ks), apl = sdesc_k64(pl + 32 * ks);
-          const uint64_t bvh = sdesc_k64(vh + 32 * ks), bvl = sdesc_k64(vl + 32 * ks);
-          const uint32_t acc = (j > 0 || ks > 0) ? 1u : 0u;
-          umma_i8(tmem + O_HH, aph, bvh, id_us, acc);
-          umma_i8(tmem + O_MID, aph, bvl, id_uu, acc);
-          umma_i8(tmem + O_MID, apl, bvh, id_us, 1u);
-          umma_i8(tmem + O_LL, apl, bvl, id_uu, acc);
-        }
+        const uint64_t aph = sdesc_k32(ph), apl = sdesc_k32(pl);
+        const uint64_t bvh = sdesc_k32(vh), bvl = sdesc_k32(vl);
+        const uint32_t acc = j > 0 ? 1u : 0u;
+        umma_i8(tmem + O_HH, aph, bvh, pv_us, acc);
+        umma_i8(tmem + O_MID, aph, bvl, pv_uu, acc);
+        umma_i8(tmem + O_MID, apl, bvh, pv_us, 1u);
+        umma_i8(tmem + O_LL, apl, bvl, pv_uu, acc);
         umma_commit(&ctl->p_empty[pb]);
         umma_commit(&ctl->empty[s]);
       }
@@ -392,9 +404,9 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
     }
   } else {
     // -------------------------------------------------------------- softmax
-    // Warp w owns query rows 32*(w%4)..+31 and key columns [16*g, 16*g+16)
-    // of each 64-key tile, g = (w-2)/4.
-    const int q = warp & 3, g = (warp - 2) >> 2;
+    // Warp w owns query rows 32*(w%4)..+31 and keys [16*g, 16*g+16) of each
+    // 32-key tile, g = (w-2)/4.
+    const int q = gw & 3, g = (warp - 2) >> 2;  // TMEM lane quarter follows the warp's index in the CTA
     const int row = q * 32 + lane;
     const int qi = q0 + row;
     const bool row_live = qi < S;
@@ -449,12 +461,9 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
       long long rmn = mn64;
       xmax[g * QT + row] = rmx;
       xmin[g * QT + row] = rmn;
-      named_sync_softmax();
-#pragma unroll
-      for (int o = 1; o < 4; ++o) {
-        rmx = max(rmx, xmax[((g + o) & 3) * QT + row]);
-        rmn = min(rmn, xmin[((g + o) & 3) * QT + row]);
-      }
+      named_sync_softmax(grp);
+      rmx = max(rmx, xmax[(g ^ 1) * QT + row]);
+      rmn = min(rmn, xmin[(g ^ 1) * QT + row]);
       if (row_live) {
         rawmax = rmx;
         lgmax = rawmax >> 3;
@@ -513,67 +522,59 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
     };
 
     // ---- pass 1: weights and the row sum ----
-    // WS: this thread's row of the weight scratch
-    int16_t* wrow = WS ? a.wscr + ((((long long)b * a.H + h) * gridDim.x + qt) * QT + row) * a.wstride : nullptr;
-    uint32_t rsum = 0;  // this thread's keys: at most 16384 / 4 weights below 2^15
+    // this thread's row of the weight scratch
+    int16_t* wrow = a.wscr + ((((long long)bl * a.H + h) * nq + qt) * QT + row) * a.wstride;
+    uint32_t rsum = 0;  // this thread's keys: at most 16384 / 2 weights below 2^15
     for (int j = 0; j < ntiles; ++j, ++it) {
       uint32_t hh[16], mid[16], ll[16], w[16];
       fetch_s((int)(it & 1), hh, mid, ll);
       weights(hh, mid, ll, live_keys(j), w);
       rsum += sum16(w);
-      if (WS) {
-        uint4* dst = reinterpret_cast<uint4*>(wrow + j * KT + 16 * g);
-        dst[0] = make_uint4(__byte_perm(w[0], w[1], 0x5410), __byte_perm(w[2], w[3], 0x5410),
-                            __byte_perm(w[4], w[5], 0x5410), __byte_perm(w[6], w[7], 0x5410));
-        dst[1] = make_uint4(__byte_perm(w[8], w[9], 0x5410), __byte_perm(w[10], w[11], 0x5410),
-                            __byte_perm(w[12], w[13], 0x5410), __byte_perm(w[14], w[15], 0x5410));
-      }
+      uint4* dst = reinterpret_cast<uint4*>(wrow + j * KT + 16 * g);
+      dst[0] = make_uint4(__byte_perm(w[0], w[1], 0x5410), __byte_perm(w[2], w[3], 0x5410),
+                          __byte_perm(w[4], w[5], 0x5410), __byte_perm(w[6], w[7], 0x5410));
+      dst[1] = make_uint4(__byte_perm(w[8], w[9], 0x5410), __byte_perm(w[10], w[11], 0x5410),
+                          __byte_perm(w[12], w[13], 0x5410), __byte_perm(w[14], w[15], 0x5410));
     }
     uint32_t inv = 0;
     {
       unsigned long long tot = rsum;
       xsum[g * QT + row] = tot;
-      named_sync_softmax();
-#pragma unroll
-      for (int o = 1; o < 4; ++o) tot += xsum[((g + o) & 3) * QT + row];
+      named_sync_softmax(grp);
+      tot += xsum[(g ^ 1) * QT + row];
       inv = (row_live && tot) ? recip_sum_q31(tot) : 0u;
     }
 
     // ---- pass 2: P = sat_i16(rhu(w * inv, 16)) as byte planes, O += P V ----
-    // WS: this thread's 32 bytes of weights per tile, copied a tile ahead into
-    // slot [buffer][half][thread] (its own copies: no barrier)
-    const int sidx = threadIdx.x - 64;
+    // This thread's 32 bytes of weights per tile, copied WPF_N - 1 tiles ahead
+    // into slot [tile % WPF_N][half][thread] (its own copies: no barrier).
+    // Every step commits one copy group, empty past the last tile, so that
+    // waiting for all but the newest WPF_N - 1 groups means tile j has landed.
+    const int sidx = gtid - 64;
     auto wpf_issue = [&](int j) {
-      const int16_t* src = wrow + j * KT + 16 * g;  // keys below ntiles * 64 <= wstride, written in pass 1
-      const uint32_t dst = smem_u32(sm + OFF_WPF + (j & 1) * WPF_BUF + sidx * 16);
-      cp_async16(dst, src);
-      cp_async16(dst + WPF_BUF / 2, src + 8);
+      if (j < ntiles) {
+        const int16_t* src = wrow + j * KT + 16 * g;  // keys below ntiles * 32 <= wstride, written in pass 1
+        const uint32_t dst = smem_u32(sm + OFF_WPF + (j % WPF_N) * WPF_BUF + sidx * 16);
+        cp_async16(dst, src);
+        cp_async16(dst + WPF_BUF / 2, src + 8);
+      }
       cp_async_commit();
     };
-    if (WS && ntiles > 0) wpf_issue(0);
+#pragma unroll
+    for (int k = 0; k < WPF_N - 1; ++k) wpf_issue(k);
     for (int j = 0; j < ntiles; ++j) {
       const int key0 = j * KT + 16 * g;
       uint32_t w[16];
-      if (WS) {
-        if (j + 1 < ntiles) {
-          wpf_issue(j + 1);
-          cp_async_wait<1>();
-        } else {
-          cp_async_wait<0>();
-        }
-        const uint8_t* slot = sm + OFF_WPF + (j & 1) * WPF_BUF + sidx * 16;
-        const uint4 u0 = *reinterpret_cast<const uint4*>(slot);
-        const uint4 u1 = *reinterpret_cast<const uint4*>(slot + WPF_BUF / 2);
-        const uint32_t wv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+      wpf_issue(j + WPF_N - 1);
+      cp_async_wait<WPF_N - 1>();
+      const uint8_t* slot = sm + OFF_WPF + (j % WPF_N) * WPF_BUF + sidx * 16;
+      const uint4 u0 = *reinterpret_cast<const uint4*>(slot);
+      const uint4 u1 = *reinterpret_cast<const uint4*>(slot + WPF_BUF / 2);
+      const uint32_t wv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          w[2 * i] = wv[i] & 0xFFFFu;
-          w[2 * i + 1] = wv[i] >> 16;
-        }
-      } else {
-        uint32_t hh[16], mid[16], ll[16];
-        fetch_s(0, hh, mid, ll);
-        weights(hh, mid, ll, live_keys(j), w);
+      for (int i = 0; i < 8; ++i) {
+        w[2 * i] = wv[i] & 0xFFFFu;
+        w[2 * i + 1] = wv[i] >> 16;
       }
       // w * inv + 2^15 < 2^47 + 2^15, so the value shifted by 16 fits in 32 bits
       uint32_t pw[8];
@@ -598,7 +599,7 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
         hw[k] = __byte_perm(pw[2 * k], pw[2 * k + 1], 0x7531);
         lw[k] = __byte_perm(pw[2 * k], pw[2 * k + 1], 0x6420);
       }
-      const uint32_t off = swz64_chunk((uint32_t)row, (uint32_t)g);
+      const uint32_t off = swz32_chunk((uint32_t)row, (uint32_t)g);
       *reinterpret_cast<uint4*>(ph + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
       *reinterpret_cast<uint4*>(pl + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
       fence_proxy_async_smem();
@@ -608,47 +609,51 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
     if (range_bad) nsrl_flag(a.st, NSRL_FLAG_LOGIT_RANGE);
     if (masked_bad) nsrl_flag(a.st, NSRL_FLAG_ALL_MASKED);
     // ---- context: sat(rhu(65536*hh + 256*mid + ll, 15)) as byte planes ----
+    // The exact sum fits i32: p <= w * inv / 2^16 + 1/2 with inv <= 2^31 *
+    // (129/128) / sum(w) (8-bit reciprocal mantissa), so sum(p) <= 33024 +
+    // keys / 2 <= 41216 for at most 16384 keys, and |sum(p * v)| <=
+    // 41216 * 32768 < 2^31 - 2^14.  Wrapping 32-bit recombination is exact
+    // and rhu(tot, 15) = (tot + 2^14) >> 15 cannot overflow.
     wait_bar(&ctl->o_full, 0, ctl, a.st);
     tc_fence_after();
-    uint32_t oh[16], om[16], ol[16];
-    tmem_ld16(trow + O_HH + 16 * g, oh);
-    tmem_ld16(trow + O_MID + 16 * g, om);
-    tmem_ld16(trow + O_LL + 16 * g, ol);
-    tmem_wait_ld();
-    if (row_live) {
-      // The exact sum fits i32: p <= w * inv / 2^16 + 1/2 with inv <= 2^31 *
-      // (129/128) / sum(w) (8-bit reciprocal mantissa), so sum(p) <= 33024 +
-      // keys / 2 <= 41216 for at most 16384 keys, and |sum(p * v)| <=
-      // 41216 * 32768 < 2^31 - 2^14.  Wrapping 32-bit recombination is exact
-      // and rhu(tot, 15) = (tot + 2^14) >> 15 cannot overflow.
-      uint32_t pk[8];
-      unsigned l1 = 0;
+    unsigned l1 = 0;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int t0 = (int)(oh[2 * i] * 65536u + om[2 * i] * 256u + ol[2 * i]);
-        const int t1 = (int)(oh[2 * i + 1] * 65536u + om[2 * i + 1] * 256u + ol[2 * i + 1]);
-        const int v0 = max(-32768, min(32767, (t0 + 16384) >> 15));
-        const int v1 = max(-32768, min(32767, (t1 + 16384) >> 15));
-        l1 += (unsigned)(abs(v0) + abs(v1));
-        pk[i] = __byte_perm((uint32_t)v0, (uint32_t)v1, 0x5410);
-      }
-      uint32_t hw[4], lw[4];
+    for (int c = 0; c < 2; ++c) {  // dims [32g + 16c, +16)
+      uint32_t oh[16], om[16], ol[16];
+      const uint32_t col = (uint32_t)(32 * g + 16 * c);
+      tmem_ld16(trow + O_HH + col, oh);
+      tmem_ld16(trow + O_MID + col, om);
+      tmem_ld16(trow + O_LL + col, ol);
+      tmem_wait_ld();
+      if (row_live) {
+        uint32_t pk[8];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        hw[k] = __byte_perm(pk[2 * k], pk[2 * k + 1], 0x7531);
-        lw[k] = __byte_perm(pk[2 * k], pk[2 * k + 1], 0x6420);
+        for (int i = 0; i < 8; ++i) {
+          const int t0 = (int)(oh[2 * i] * 65536u + om[2 * i] * 256u + ol[2 * i]);
+          const int t1 = (int)(oh[2 * i + 1] * 65536u + om[2 * i + 1] * 256u + ol[2 * i + 1]);
+          const int v0 = max(-32768, min(32767, (t0 + 16384) >> 15));
+          const int v1 = max(-32768, min(32767, (t1 + 16384) >> 15));
+          l1 += (unsigned)(abs(v0) + abs(v1));
+          pk[i] = __byte_perm((uint32_t)v0, (uint32_t)v1, 0x5410);
+        }
+        uint32_t hw[4], lw[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          hw[k] = __byte_perm(pk[2 * k], pk[2 * k + 1], 0x7531);
+          lw[k] = __byte_perm(pk[2 * k], pk[2 * k + 1], 0x6420);
+        }
+        const long long off = (long long)(row0 + qi) * a.ldc + h * HD + col;
+        *reinterpret_cast<uint4*>(a.ctx_hi + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        *reinterpret_cast<uint4*>(a.ctx_lo + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
       }
-      const long long off = (long long)(row0 + qi) * a.ldc + h * HD + 16 * g;
-      *reinterpret_cast<uint4*>(a.ctx_hi + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-      *reinterpret_cast<uint4*>(a.ctx_lo + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-      if (a.ctx_l1) atomicAdd(&a.ctx_l1[row0 + qi], (unsigned long long)l1);
     }
+    if (row_live && a.ctx_l1) atomicAdd(&a.ctx_l1[row0 + qi], (unsigned long long)l1);
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (gw == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, TMEM_COLS);
+    tmem_dealloc(s_tslot, TMEM_COLS);
   }
 }
 
@@ -670,17 +675,32 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// 2-D uint8 map [rows][inner] (row stride ld bytes), box [box_rows][64 bytes], 64-byte swizzle.
-bool make_map64(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t rows, uint64_t ld, uint32_t box_rows) {
+// 2-D uint8 map [rows][inner] (row stride ld bytes), box [box_rows][box_inner
+// bytes] with the swizzle of that row width (64 or 32 bytes).
+bool make_map(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t rows, uint64_t ld, uint32_t box_inner,
+              uint32_t box_rows) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   cuuint64_t dims[2] = {inner, rows};
   cuuint64_t strides[1] = {ld};
-  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t box[2] = {box_inner, box_rows};
   cuuint32_t es[2] = {1, 1};
+  const CUtensorMapSwizzle sw = box_inner == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B;
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, es,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Bytes of weight scratch per sequence, and the sequences one launch covers:
+// at most 4 GiB of scratch (at least one sequence), reused by the launches of
+// a larger batch in stream order.
+size_t scratch_per_seq(size_t S, size_t H) {
+  const size_t nq = (S + QT - 1) / QT;
+  return H * nq * QT * attention_tc_wstride(S) * sizeof(int16_t);
+}
+size_t chunk_seqs(size_t B, size_t S, size_t H) {
+  const size_t per = scratch_per_seq(S, H);
+  return std::max<size_t>(1, std::min<size_t>(B, ((size_t)4 << 30) / per));
 }
 
 }  // namespace
@@ -689,57 +709,57 @@ bool attention_tc_supported(size_t S, size_t d, size_t H) {
   return H != 0 && d / H == (size_t)HD && d % H == 0 && S % 16 == 0 && S <= 16384 && (3 * d) % 16 == 0;
 }
 
-size_t attention_tc_wstride(size_t S) { return (S + KT - 1) / KT * KT; }
+size_t attention_tc_wstride(size_t S) { return (S + 63) / 64 * 64; }
 
 size_t attention_tc_scratch_bytes(size_t B, size_t S, size_t d, size_t H) {
-  if (!attention_tc_supported(S, d, H)) return 0;
-  const size_t nq = (S + QT - 1) / QT;
-  const size_t bytes = B * H * nq * QT * attention_tc_wstride(S) * sizeof(int16_t);
-  return bytes <= ((size_t)4 << 30) ? bytes : 0;  // beyond 4 GiB the last pass recomputes S instead
+  if (!attention_tc_supported(S, d, H) || B == 0) return 0;
+  return chunk_seqs(B, S, H) * scratch_per_seq(S, H);
 }
 
 cudaError_t launch_attention_tc(const Planes& qkv, const VtPlanes& vt, size_t B, size_t S, size_t d, size_t H,
                                 bool causal, Planes ctx, int16_t* wscr, nsrl_device_status* st,
                                 cudaStream_t stream, int16_t* probs) {
-  if (!attention_tc_supported(S, d, H) || encode_fn() == nullptr) return cudaErrorNotSupported;
+  if (!attention_tc_supported(S, d, H) || encode_fn() == nullptr || wscr == nullptr) return cudaErrorNotSupported;
+  if (B == 0) return cudaSuccess;
   const size_t T = B * S;
   Maps m;
-  const bool ok = make_map64(&m.q_hi, qkv.hi, 3 * d, T, qkv.ld, QT) && make_map64(&m.q_lo, qkv.lo, 3 * d, T, qkv.ld, QT) &&
-                  make_map64(&m.k_hi, qkv.hi, 3 * d, T, qkv.ld, KT) && make_map64(&m.k_lo, qkv.lo, 3 * d, T, qkv.ld, KT) &&
-                  make_map64(&m.vt_hi, vt.hi, S, B * H * HD, S, HD) && make_map64(&m.vt_lo, vt.lo, S, B * H * HD, S, HD);
+  const bool ok =
+      make_map(&m.q_hi, qkv.hi, 3 * d, T, qkv.ld, 64, QT) && make_map(&m.q_lo, qkv.lo, 3 * d, T, qkv.ld, 64, QT) &&
+      make_map(&m.k_hi, qkv.hi, 3 * d, T, qkv.ld, 64, KT) && make_map(&m.k_lo, qkv.lo, 3 * d, T, qkv.ld, 64, KT) &&
+      make_map(&m.vt_hi, vt.hi, S, B * H * HD, S, KT, HD) && make_map(&m.vt_lo, vt.lo, S, B * H * HD, S, KT, HD);
   if (!ok) return cudaErrorNotSupported;
   Args a{};
   a.S = (int)S;
   a.d = (int)d;
   a.H = (int)H;
   a.causal = causal ? 1 : 0;
-  a.shift = 3;  // log4(64)
   a.ctx_hi = ctx.hi;
   a.ctx_lo = ctx.lo;
   a.ctx_l1 = ctx.l1;
   a.ldc = (long long)ctx.ld;
   a.probs = probs;
   a.st = st;
+  a.wscr = wscr;
+  a.wstride = (long long)attention_tc_wstride(S);
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(attention_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)SMEM_BYTES);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(attention_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)SMEM_BYTES);
+    const cudaError_t e =
+        cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  a.wscr = wscr;
-  a.wstride = (long long)attention_tc_wstride(S);
-  dim3 grid((unsigned)((S + QT - 1) / QT), (unsigned)H, (unsigned)B);
   const double pairs = causal ? (double)S * (S + 1) / 2.0 : (double)S * S;
   ProfScope prof("attention_tc_hd64", stream, 4.0 * HD * (double)H * (double)B * pairs, 8.0 * (double)T * (double)d);
-  if (wscr)
-    attention_tc_kernel<true><<<grid, THREADS, SMEM_BYTES, stream>>>(m, a);
-  else
-    attention_tc_kernel<false><<<grid, THREADS, SMEM_BYTES, stream>>>(m, a);
-  return cudaGetLastError();
+  const size_t chunk = chunk_seqs(B, S, H);
+  for (size_t b0 = 0; b0 < B; b0 += chunk) {
+    a.b0 = (int)b0;
+    a.nb = (int)std::min(chunk, B - b0);
+    const dim3 grid((unsigned)H, (unsigned)((a.nb + GROUPS - 1) / GROUPS), (unsigned)((S + QT - 1) / QT));
+    attention_tc_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(m, a);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 }  // namespace nsrl
