@@ -118,10 +118,11 @@ __device__ __forceinline__ ColScale load_scales(const nsrl_fixed_scale* sc, cons
 // requantize_i32_to_i16 of W columns: acc = 256*hi + lo (+ bias), wrapping
 // u32 arithmetic (exact whenever the true i32 sum fits).
 // `small`: |acc| < 2^30 (K * 127 * 32767 < 2^30, no bias), so acc + 2^(s-1)
-// cannot overflow and rhu is one add and one shift.
+// cannot overflow and rhu is one add and one shift.  Column i of the chunk
+// takes the scale held by lane base + i.
 template <int W>
 __device__ __forceinline__ void requant_cols(const uint32_t (&h)[W], const uint32_t (&l)[W], const ColScale& c,
-                                             int (&v)[W], bool small) {
+                                             int (&v)[W], bool small, int base = 0) {
   if (c.uniform) {
     const uint32_t s = (uint32_t)c.ushift;
     if (s == 0) {
@@ -144,9 +145,9 @@ __device__ __forceinline__ void requant_cols(const uint32_t (&h)[W], const uint3
   } else {
 #pragma unroll
     for (int i = 0; i < W; ++i) {
-      const int mult = __shfl_sync(0xffffffffu, c.mult, i);
-      const int shift = __shfl_sync(0xffffffffu, c.shift, i);
-      const int b = __shfl_sync(0xffffffffu, c.bias, i);
+      const int mult = __shfl_sync(0xffffffffu, c.mult, base + i);
+      const int shift = __shfl_sync(0xffffffffu, c.shift, base + i);
+      const int b = __shfl_sync(0xffffffffu, c.bias, base + i);
       v[i] = requant_fast((int)(h[i] * 256u + l[i] + (uint32_t)b), mult, (uint32_t)shift);
     }
   }
@@ -164,55 +165,18 @@ __device__ __forceinline__ int requant_wide1(uint32_t h, uint32_t l, int mult, i
   }
   return (int)sat_i16(rhu64(wide, (uint32_t)shift));
 }
-__device__ __forceinline__ void requant_wide32(const uint32_t (&h)[32], const uint32_t (&l)[32], const ColScale& c,
-                                               int (&v)[32], bool& bad) {
+__device__ __forceinline__ void requant_wide16(const uint32_t (&h)[16], const uint32_t (&l)[16], const ColScale& c,
+                                               int (&v)[16], bool& bad, int base) {
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    const int mult = c.uniform ? 1 : __shfl_sync(0xffffffffu, c.mult, i);
-    const int shift = c.uniform ? c.ushift : __shfl_sync(0xffffffffu, c.shift, i);
+  for (int i = 0; i < 16; ++i) {
+    const int mult = c.uniform ? 1 : __shfl_sync(0xffffffffu, c.mult, base + i);
+    const int shift = c.uniform ? c.ushift : __shfl_sync(0xffffffffu, c.shift, base + i);
     v[i] = requant_wide1(h[i], l[i], mult, shift, bad);
   }
-}
-
-__device__ __forceinline__ void requant32(const uint32_t (&h)[32], const uint32_t (&l)[32], const ColScale& c,
-                                          int (&v)[32], bool small) {
-  requant_cols<32>(h, l, c, v, small);
 }
 __device__ __forceinline__ void requant16(const uint32_t (&h)[16], const uint32_t (&l)[16], const ColScale& c,
                                           int (&v)[16], bool small) {
   requant_cols<16>(h, l, c, v, small);
-}
-
-// Splits 16 packed int16 values into hi / lo byte planes (+ L1 of the values).
-__device__ __forceinline__ void store16_planes(int8_t* dh, uint8_t* dl, const uint32_t (&o)[8], int nvalid,
-                                               bool vec_ok, unsigned long long& l1) {
-  uint32_t hw[4], lw[4];
-  unsigned acc = 0;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint32_t a = o[2 * i], b = o[2 * i + 1];
-    hw[i] = __byte_perm(a, b, 0x7531);
-    lw[i] = __byte_perm(a, b, 0x6420);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int v = (int16_t)(((j < 2) ? a : b) >> (16 * (j & 1)));
-      if (4 * i + j < nvalid) acc += (unsigned)abs(v);
-    }
-  }
-  l1 += acc;
-  if (vec_ok && nvalid == 16) {
-    *reinterpret_cast<uint4*>(dh) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-    *reinterpret_cast<uint4*>(dl) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-  } else {
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      if (i < nvalid) {
-        const int v = (int16_t)(o[i / 2] >> (16 * (i & 1)));
-        dh[i] = (int8_t)(v >> 8);
-        dl[i] = (uint8_t)(v & 255);
-      }
-    }
-  }
 }
 
 // Splits 16 packed int16 values into hi / lo byte planes.
@@ -247,52 +211,15 @@ __device__ __forceinline__ int gated_act_i32(int up, int gate) {
   return (up * silu + 16384) >> 15;
 }
 
-__device__ __forceinline__ void store32_i16(int16_t* dst, const uint32_t (&o)[16], int nvalid, bool vec_ok) {
-  if (vec_ok && nvalid == 32) {
+__device__ __forceinline__ void store16_i16(int16_t* dst, const uint32_t (&o)[8], int nvalid, bool vec_ok) {
+  if (vec_ok && nvalid == 16) {
     uint4* d = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) d[i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+    d[0] = make_uint4(o[0], o[1], o[2], o[3]);
+    d[1] = make_uint4(o[4], o[5], o[6], o[7]);
   } else {
 #pragma unroll
-    for (int i = 0; i < 32; ++i)
+    for (int i = 0; i < 16; ++i)
       if (i < nvalid) dst[i] = (int16_t)(o[i / 2] >> (16 * (i & 1)));
-  }
-}
-
-// Splits 32 packed int16 values into hi / lo byte planes (+ L1 of the values).
-__device__ __forceinline__ void store32_planes(int8_t* dh, uint8_t* dl, const uint32_t (&o)[16], int nvalid,
-                                               bool vec_ok, unsigned long long& l1) {
-  uint32_t hw[8], lw[8];
-  unsigned acc = 0;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const uint32_t a = o[2 * i], b = o[2 * i + 1];  // values 4i..4i+3 as int16 pairs
-    // hi bytes: byte 1 of each int16, lo bytes: byte 0
-    hw[i] = __byte_perm(a, b, 0x7531);
-    lw[i] = __byte_perm(a, b, 0x6420);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int v = (int16_t)(((j < 2) ? a : b) >> (16 * (j & 1)));
-      if (4 * i + j < nvalid) acc += (unsigned)abs(v);
-    }
-  }
-  l1 += acc;
-  if (vec_ok && nvalid == 32) {
-    uint4* ah = reinterpret_cast<uint4*>(dh);
-    uint4* al = reinterpret_cast<uint4*>(dl);
-    ah[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-    ah[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
-    al[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-    al[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
-  } else {
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      if (i < nvalid) {
-        const int v = (int16_t)(o[i / 2] >> (16 * (i & 1)));
-        dh[i] = (int8_t)(v >> 8);
-        dl[i] = (uint8_t)(v & 255);
-      }
-    }
   }
 }
 
@@ -439,11 +366,15 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
         requant16(hu, lu, su, up, p.small_acc);
         requant16(hg, lg, sg, gt, p.small_acc);
         int act[16];
-        unsigned a1 = 0;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          act[i] = gated_act_i32(up[i], gt[i]);
-          a1 += (i < nvalid) ? (unsigned)abs(act[i]) : 0u;
+        for (int i = 0; i < 16; ++i) act[i] = gated_act_i32(up[i], gt[i]);
+        unsigned a1 = 0;
+        if (nvalid == 16) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) a1 += (unsigned)abs(act[i]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) a1 += (i < nvalid) ? (unsigned)abs(act[i]) : 0u;
         }
         uint32_t o[8];
 #pragma unroll
@@ -462,7 +393,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
         const ColScale sc = load_scales(p.scales[sseg], p.bias[sseg], nloc + lane, lane < nvalid);
         // The residual rows do not depend on the accumulator: fetch them first.
         uint32_t s16[16];
-        const bool vec_skip = EPI == (int)Epi::RESID && ((p.ldskip | p.ldy | n) & 7) == 0 && nvalid == 32;
+        const bool vec_skip = EPI == (int)Epi::RESID && ((p.ldskip | p.ldy | n) & 7) == 0 && nvalid == 32;  // both halves full
         if (EPI == (int)Epi::RESID && row_ok && nvalid > 0) {
           const int16_t* sk = p.skip + (long long)r * p.ldskip + n;
           if (vec_skip) {
@@ -483,61 +414,73 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
             }
           }
         }
-        uint32_t h[32], l[32];
         if (!mbar_wait(&acc_full[buf], use & 1, p.st)) break;
         tc_fence_after();
-        tmem_ld32(lrow + 32 * cg, h);
-        tmem_ld32(lrow + BN + 32 * cg, l);
-        tmem_wait_ld();
-        tc_fence_before();
-        if (lane == 0) mbar_arrive(&acc_empty[buf]);
-        int v[32];
-        if (p.wide) {
-          bool bad = false;
-          requant_wide32(h, l, sc, v, bad);
-          if (bad && row_ok && nvalid > 0) nsrl_flag(p.st, NSRL_FLAG_LINEAR_OVERFLOW);
-        } else {
-          requant32(h, l, sc, v, p.small_acc);
-        }
-        uint32_t o[16];
+        // Two halves of 16 columns keep the live registers low; the buffer is
+        // released once the second half is loaded.
 #pragma unroll
-        for (int i = 0; i < 16; ++i) o[i] = pack2(v[2 * i], v[2 * i + 1]);
-        if (row_ok && nvalid > 0) {
-          if (EPI == (int)Epi::I16) {
-            store32_i16(p.y + (long long)r * p.ldy + n, o, nvalid, ((p.ldy | n) & 7) == 0);
-          } else if (EPI == (int)Epi::RESID) {
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const int a = (int)(int16_t)(s16[i] & 0xFFFF) + v[2 * i];
-              const int b = (int)(int16_t)(s16[i] >> 16) + v[2 * i + 1];
-              const int sa = sat16(a), sb = sat16(b);
-              if (2 * i < nvalid && sa != a) ++sat;
-              if (2 * i + 1 < nvalid && sb != b) ++sat;
-              o[i] = pack2(sa, sb);
-            }
-            store32_i16(p.y + (long long)r * p.ldy + n, o, nvalid, vec_skip);
+        for (int hf = 0; hf < 2; ++hf) {
+          uint32_t h[16], l[16];
+          tmem_ld16(lrow + 32 * cg + 16 * hf, h);
+          tmem_ld16(lrow + BN + 32 * cg + 16 * hf, l);
+          tmem_wait_ld();
+          if (hf == 1) {
+            tc_fence_before();
+            if (lane == 0) mbar_arrive(&acc_empty[buf]);
+          }
+          const int nv = max(0, min(16, nvalid - 16 * hf));
+          const int nh = n + 16 * hf;
+          int v[16];
+          if (p.wide) {
+            bool bad = false;
+            requant_wide16(h, l, sc, v, bad, 16 * hf);
+            if (bad && row_ok && nv > 0) nsrl_flag(p.st, NSRL_FLAG_LINEAR_OVERFLOW);
           } else {
-            if (EPI == (int)Epi::QKV_VT && p.y)  // the int16 rows as well (the training step's cache)
-              store32_i16(p.y + (long long)r * p.ldy + n, o, nvalid, ((p.ldy | n) & 7) == 0);
-            if (EPI == (int)Epi::QKV_VT && n >= p.vt_col0) {
+            requant_cols<16>(h, l, sc, v, p.small_acc, 16 * hf);
+          }
+          if (!row_ok || nv == 0) continue;
+          uint32_t o[8];
+          if (EPI == (int)Epi::RESID) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const uint32_t sk = s16[8 * hf + i];
+              const int a = (int)(int16_t)(sk & 0xFFFF) + v[2 * i];
+              const int b = (int)(int16_t)(sk >> 16) + v[2 * i + 1];
+              const int sa = clamp16(a), sb = clamp16(b);
+              if (2 * i < nv && sa != a) ++sat;
+              if (2 * i + 1 < nv && sb != b) ++sat;
+              o[i] = __byte_perm((uint32_t)sa, (uint32_t)sb, 0x5410);
+            }
+            store16_i16(p.y + (long long)r * p.ldy + nh, o, nv, vec_skip);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o[i] = __byte_perm((uint32_t)v[2 * i], (uint32_t)v[2 * i + 1], 0x5410);
+            if (EPI == (int)Epi::I16 || (EPI == (int)Epi::QKV_VT && p.y))  // QKV_VT: the training step's int16 cache
+              store16_i16(p.y + (long long)r * p.ldy + nh, o, nv, ((p.ldy | nh) & 7) == 0);
+            if (EPI == (int)Epi::I16) continue;
+            if (EPI == (int)Epi::QKV_VT && nh >= p.vt_col0) {
               // v columns: byte stores into [b][h][dim][s]; the 32 lanes of the
               // warp hold 32 consecutive positions, so each store instruction
-              // writes one contiguous 32-byte run per plane.
-              // [b][h][dim][s] is contiguous over (h, dim): row (b, c) of the
-              // planes is b * H * hd + c for value column c.
+              // writes one contiguous 32-byte run per plane.  [b][h][dim][s] is
+              // contiguous over (h, dim): row (b, c) of the planes is
+              // b * H * hd + c for value column c.
               const int b = r / p.vt_S, spos = r % p.vt_S;
-              const long long off0 = ((long long)b * (p.vt_H * p.vt_hd) + (n - p.vt_col0)) * p.vt_S + spos;
+              const long long off0 = ((long long)b * (p.vt_H * p.vt_hd) + (nh - p.vt_col0)) * p.vt_S + spos;
 #pragma unroll
-              for (int i = 0; i < 32; ++i) {
-                if (i < nvalid) {
+              for (int i = 0; i < 16; ++i) {
+                if (i < nv) {
                   const long long off = off0 + (long long)i * p.vt_S;
                   p.vth[off] = (int8_t)(v[i] >> 8);
                   p.vtl[off] = (uint8_t)(v[i] & 255);
                 }
               }
             } else {
-              const long long off = (long long)r * p.ldp + n;
-              store32_planes(p.yh + off, p.yl + off, o, nvalid, ((p.ldp | n) & 15) == 0, l1);
+              if (p.yl1) {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) l1 += (i < nv) ? (unsigned)abs(v[i]) : 0u;
+              }
+              const long long off = (long long)r * p.ldp + nh;
+              store16_planes_nol1(p.yh + off, p.yl + off, o, nv, ((p.ldp | nh) & 15) == 0);
             }
           }
         }
