@@ -368,9 +368,12 @@ nsrl_status nsrl_train_windows(const nsrl_train_model* model, const uint8_t* con
                                size_t workspace_bytes, nsrl_device_status* status, void* stream);
 
 /* The transformer block over HOST buffers (pinned host memory for the
- * overlap): the batch runs in chunks of `chunk` sequences, and the copy in of
- * chunk i+1, the block of chunk i and the copy out of chunk i-1 overlap (two
- * library-owned copy streams per device and thread).  The call is complete on
+ * overlap): the batch runs in steps of at most `chunk` sequences; the copy
+ * in of step i+1, the block of step i and the copy out of step i-1 overlap
+ * (two device buffers per direction, two library-owned copy streams per
+ * device and thread).  The steps ramp up
+ * from chunk / 4 and back down at the end, so that the copy in of the first
+ * step and the copy out of the last, the two that nothing hides, are short.  The call is complete on
  * `stream` when y_host holds the output.  No counterpart in the reference
  * (its blocks read host memory); it is nsrl_prenorm_transformer_block for a
  * caller whose activations live on the host.  Workspace:

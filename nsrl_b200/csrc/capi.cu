@@ -7,6 +7,8 @@
 
 #include <algorithm>
 
+#include <vector>
+
 #include "common.cuh"
 #include "internal.h"
 
@@ -464,10 +466,12 @@ nsrl_status nsrl_prenorm_transformer_block(const int16_t* x, size_t batch, size_
 
 // ---- transformer block over host buffers: chunked copy / compute overlap ----
 namespace {
+constexpr int HOST_BUFS = 2;  // device buffers per direction of the host-buffer pipeline
+
 struct HostPipe {
   int device = -1;
   cudaStream_t h2d = nullptr, d2h = nullptr;
-  cudaEvent_t in[2], comp[2], out[2], done;
+  cudaEvent_t in[HOST_BUFS], comp[HOST_BUFS], out[HOST_BUFS], done;
   bool ok = false;
 };
 
@@ -480,7 +484,7 @@ HostPipe* host_pipe() {
   p.device = dev;
   if (cudaStreamCreateWithFlags(&p.h2d, cudaStreamNonBlocking) != cudaSuccess) return nullptr;
   if (cudaStreamCreateWithFlags(&p.d2h, cudaStreamNonBlocking) != cudaSuccess) return nullptr;
-  for (int b = 0; b < 2; ++b)
+  for (int b = 0; b < HOST_BUFS; ++b)
     if (cudaEventCreateWithFlags(&p.in[b], cudaEventDisableTiming) != cudaSuccess ||
         cudaEventCreateWithFlags(&p.comp[b], cudaEventDisableTiming) != cudaSuccess ||
         cudaEventCreateWithFlags(&p.out[b], cudaEventDisableTiming) != cudaSuccess)
@@ -494,9 +498,32 @@ HostPipe* host_pipe() {
 size_t nsrl_transformer_block_host_workspace_size(size_t chunk, size_t seq_len, size_t d_model, size_t heads,
                                                   size_t hidden_dim) {
   if (heads == 0 || chunk == 0) return 0;
-  return 4 * up(chunk * seq_len * d_model * sizeof(int16_t)) +
+  return 2 * HOST_BUFS * up(chunk * seq_len * d_model * sizeof(int16_t)) +
          nsrl_transformer_block_workspace_size(chunk, seq_len, d_model, heads, hidden_dim);
 }
+
+namespace {
+// Sequences per step of the host-buffer pipeline: chunk / 4, chunk / 2, then
+// full chunks, and the same ramp backwards at the end.  Only the first step's
+// copy in and the last step's copy out are not hidden behind a block, so they
+// are made small; the steps in between keep the block's grid full.
+std::vector<size_t> host_steps(size_t batch, size_t chunk) {
+  std::vector<size_t> ramp, out;
+  size_t rest = batch;
+  for (size_t c = std::max<size_t>(1, chunk / 4); c < chunk && rest > 2 * c; c *= 2) {
+    ramp.push_back(c);
+    rest -= 2 * c;
+  }
+  out = ramp;
+  while (rest > 0) {
+    const size_t c = std::min(chunk, rest);
+    out.push_back(c);
+    rest -= c;
+  }
+  out.insert(out.end(), ramp.rbegin(), ramp.rend());
+  return out;
+}
+}  // namespace
 
 nsrl_status nsrl_prenorm_transformer_block_host(const int16_t* x_host, size_t batch, size_t chunk, size_t seq_len,
                                                 size_t d_model, size_t heads, size_t hidden_dim,
@@ -518,40 +545,47 @@ nsrl_status nsrl_prenorm_transformer_block_host(const int16_t* x_host, size_t ba
   cudaStream_t s = (cudaStream_t)stream;
   const size_t elems = chunk * seq_len * d_model;
   Carver c(workspace);
-  int16_t* xd[2] = {c.take<int16_t>(elems), c.take<int16_t>(elems)};
-  int16_t* yd[2] = {c.take<int16_t>(elems), c.take<int16_t>(elems)};
+  int16_t* xd[HOST_BUFS];
+  int16_t* yd[HOST_BUFS];
+  for (int b = 0; b < HOST_BUFS; ++b) xd[b] = c.take<int16_t>(elems);
+  for (int b = 0; b < HOST_BUFS; ++b) yd[b] = c.take<int16_t>(elems);
   void* bws = static_cast<uint8_t*>(workspace) + c.off;
   const size_t bws_bytes = workspace_bytes - c.off;
-  const size_t n = (batch + chunk - 1) / chunk;
+  const std::vector<size_t> steps = host_steps(batch, chunk);
+  const size_t n = steps.size();
+  std::vector<size_t> first(n + 1, 0);  // first sequence of each step
+  for (size_t i = 0; i < n; ++i) first[i + 1] = first[i] + steps[i];
   const size_t row = seq_len * d_model;
   // the copies may start once the caller's earlier work on `stream` is done
   NSRL_TRY(cudaEventRecord(P.done, s), "event");
   NSRL_TRY(cudaStreamWaitEvent(P.h2d, P.done, 0), "event");
   NSRL_TRY(cudaStreamWaitEvent(P.d2h, P.done, 0), "event");
   auto h2d = [&](size_t i) -> nsrl_status {
-    const int b = (int)(i & 1);
-    const size_t nb = std::min(chunk, batch - i * chunk);
-    if (i >= 2) NSRL_TRY(cudaStreamWaitEvent(P.h2d, P.comp[b], 0), "event");  // x[b] free
-    NSRL_TRY(cudaMemcpyAsync(xd[b], x_host + i * chunk * row, nb * row * sizeof(int16_t), cudaMemcpyHostToDevice,
+    const int b = (int)(i % HOST_BUFS);
+    const size_t nb = steps[i];
+    if (i >= HOST_BUFS) NSRL_TRY(cudaStreamWaitEvent(P.h2d, P.comp[b], 0), "event");  // x[b] free
+    NSRL_TRY(cudaMemcpyAsync(xd[b], x_host + first[i] * row, nb * row * sizeof(int16_t), cudaMemcpyHostToDevice,
                              P.h2d),
              "copy in");
     NSRL_TRY(cudaEventRecord(P.in[b], P.h2d), "event");
     return NSRL_OK;
   };
-  nsrl_status r = h2d(0);
-  if (r != NSRL_OK) return r;
+  // The copies in run up to HOST_BUFS - 1 steps ahead of the blocks.
+  nsrl_status r = NSRL_OK;
+  for (size_t i = 0; i + 1 < (size_t)HOST_BUFS && i < n; ++i)
+    if ((r = h2d(i)) != NSRL_OK) return r;
   for (size_t i = 0; i < n; ++i) {
-    const int b = (int)(i & 1);
-    const size_t nb = std::min(chunk, batch - i * chunk);
-    if (i + 1 < n && (r = h2d(i + 1)) != NSRL_OK) return r;
+    const int b = (int)(i % HOST_BUFS);
+    const size_t nb = steps[i];
+    if (i + HOST_BUFS - 1 < n && (r = h2d(i + HOST_BUFS - 1)) != NSRL_OK) return r;
     NSRL_TRY(cudaStreamWaitEvent(s, P.in[b], 0), "event");
-    if (i >= 2) NSRL_TRY(cudaStreamWaitEvent(s, P.out[b], 0), "event");  // y[b] copied out
+    if (i >= (size_t)HOST_BUFS) NSRL_TRY(cudaStreamWaitEvent(s, P.out[b], 0), "event");  // y[b] copied out
     r = nsrl_prenorm_transformer_block(xd[b], nb, seq_len, d_model, heads, hidden_dim, attn_gamma, mlp_gamma, rms_eps,
                                        q, k, v, o, up_p, gate, down, yd[b], bws, bws_bytes, status, stream);
     if (r != NSRL_OK) return r;
     NSRL_TRY(cudaEventRecord(P.comp[b], s), "event");
     NSRL_TRY(cudaStreamWaitEvent(P.d2h, P.comp[b], 0), "event");
-    NSRL_TRY(cudaMemcpyAsync(y_host + i * chunk * row, yd[b], nb * row * sizeof(int16_t), cudaMemcpyDeviceToHost,
+    NSRL_TRY(cudaMemcpyAsync(y_host + first[i] * row, yd[b], nb * row * sizeof(int16_t), cudaMemcpyDeviceToHost,
                              P.d2h),
              "copy out");
     NSRL_TRY(cudaEventRecord(P.out[b], P.d2h), "event");

@@ -226,10 +226,11 @@ def test_transformer_block_parity(core):
     assert np.array_equal(host(out[0]), y2) and out[1] == s1 and out[2] == s2
 
 
-@pytest.mark.parametrize("B,chunk", [(5, 2), (3, 3), (4, 8)])
+@pytest.mark.parametrize("B,chunk", [(5, 2), (3, 3), (4, 8), (21, 8)])
 def test_transformer_block_host_buffers(core, B, chunk):
-    """The host-buffer block (chunked copy / compute overlap, a ragged last chunk)
-    equals the oracle, saturation counts included."""
+    """The host-buffer block (chunked copy / compute overlap with steps that ramp
+    up and down, e.g. 2, 4, 8, 1, 4, 2 sequences for 21 in chunks of 8) equals the
+    oracle, saturation counts included."""
     import torch
     S, d, H, F = 128, 128, 2, 512
     bw = Y.BlockWeights(8, d, F)
