@@ -201,6 +201,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete may
+// sleep for up to `hint_ns` nanoseconds instead of returning at once, so a
+// waiting warp does not spin through issue slots that others could use.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ unsigned long long global_ns() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -215,8 +230,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, nsrl_d
   if (mbar_try_wait(bar, parity)) return true;  // the common case reads no timer
   const unsigned long long t0 = global_ns();
   for (uint32_t i = 0;; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 255u && global_ns() - t0 > NSRL_WAIT_NS) {
+    if (mbar_try_wait_hint(bar, parity, 20000u)) return true;
+    if ((i & 15u) == 15u && global_ns() - t0 > NSRL_WAIT_NS) {
       nsrl_flag(st, NSRL_FLAG_WAIT_TIMEOUT);
       return false;
     }
