@@ -121,14 +121,12 @@ cudaError_t launch_attention_rows_probs(const int16_t* q, const int16_t* k, cons
                                         nsrl_device_status* st, cudaStream_t stream);
 
 // Weight-gradient accumulation on the tensor cores: acc [N][K] (int64) +=
-// G^T X over T rows, from byte planes of the transposes G^T [N][T] and
-// X^T [K][T] (row stride ldt bytes, a multiple of 16).  cudaErrorNotSupported
-// when TMA is unavailable.
-size_t wgrad_planes_ld(size_t T);
-cudaError_t launch_transpose_split(const int16_t* x, size_t T, size_t C, size_t ld, const nsrl_fixed_scale* sc,
-                                   int8_t* th, uint8_t* tl, size_t ldt, cudaStream_t s);
-cudaError_t launch_wgrad_tc(const int8_t* gh, const uint8_t* gl, const int8_t* xh, const uint8_t* xl, size_t ldt,
-                            size_t T, size_t N, size_t K, long long* acc, nsrl_device_status* st, cudaStream_t s);
+// G^T X over T rows, from the byte planes of G [T][N] and X [T][K] as their
+// producers write them (row strides ldg, ldx bytes, multiples of 16; 16-byte
+// aligned bases).  cudaErrorNotSupported when TMA cannot take them.
+cudaError_t launch_wgrad_tc(const int8_t* gh, const uint8_t* gl, size_t ldg, const int8_t* xh, const uint8_t* xl,
+                            size_t ldx, size_t T, size_t N, size_t K, long long* acc, nsrl_device_status* st,
+                            cudaStream_t s);
 
 // Softmax-attention backward on the int8 tensor cores (mma.sync): dQ, dK, dV
 // and dL (zeroed, then written) from int16 q, k, v (row stride ld), P and dC.

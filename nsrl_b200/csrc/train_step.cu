@@ -194,27 +194,21 @@ cudaError_t accumulate(const int16_t* x, size_t ldx, const int16_t* g, size_t ld
   return cudaGetLastError();
 }
 
-// Transposed byte planes of one weight-gradient product (tensor-core path).
-struct WgBufs {
-  int8_t *gh, *xh;
-  uint8_t *gl, *xl;
-  size_t ldt;
-};
-
-// acc [N][K] += sum over rows of g'[r][n] x[r][k]: the tensor-core kernel on
-// transposed planes (g prescaled by rhu(g, shift_n); multipliers are 1 here),
-// or the SIMT kernel where TMA is unavailable.
-// x_ready: the X planes already hold this x (the q, k and v gradients share one
-// input, and so do up and gate).
-cudaError_t accumulate_tc(const WgBufs& b, const int16_t* x, size_t ldx, const int16_t* g, size_t ldg,
-                          const nsrl_fixed_scale* sc, size_t rows, size_t K, size_t N, long long* acc,
-                          nsrl_device_status* st, cudaStream_t s, bool x_ready = false) {
+// acc [N][K] += sum over rows of g'[r][n] x[r][k] from byte planes: g' [rows][N]
+// already prescaled by rhu(g, shift_n) (multipliers are 1 here) and x
+// [rows][K], as their producers write them.  The tensor-core kernel reads them
+// in place; the SIMT kernel takes operands TMA cannot.
+cudaError_t accumulate_planes(const Planes& g, const Planes& x, size_t rows, size_t K, size_t N, long long* acc,
+                              nsrl_device_status* st, cudaStream_t s) {
   if (rows == 0) return cudaSuccess;
-  TS_TRY_RET(launch_transpose_split(g, rows, N, ldg, sc, b.gh, b.gl, b.ldt, s));
-  if (!x_ready) TS_TRY_RET(launch_transpose_split(x, rows, K, ldx, nullptr, b.xh, b.xl, b.ldt, s));
-  const cudaError_t e = launch_wgrad_tc(b.gh, b.gl, b.xh, b.xl, b.ldt, rows, N, K, acc, st, s);
-  if (e == cudaErrorNotSupported) return accumulate(x, ldx, g, ldg, sc, rows, K, N, acc, st, s);
-  return e;
+  const cudaError_t e = launch_wgrad_tc(g.hi, g.lo, g.ld, x.hi, x.lo, x.ld, rows, N, K, acc, st, s);
+  if (e != cudaErrorNotSupported) return e;
+  dim3 grid((unsigned)((K + ATK - 1) / ATK), (unsigned)((N + ATN - 1) / ATN));
+  ProfScope prof("accumulate_weight_grad", s, 2.0 * (double)rows * (double)K * (double)N,
+                 2.0 * (double)rows * (double)(K + N) + 16.0 * (double)K * (double)N);
+  accumulate_planes_kernel<<<grid, 256, 0, s>>>(g.hi, g.lo, (long long)g.ld, x.hi, x.lo, (long long)x.ld, (int)rows,
+                                                (int)K, (int)N, acc);
+  return cudaGetLastError();
 }
 
 cudaError_t rms_backward(const int16_t* x, size_t rows, size_t d, const int16_t* w, const int16_t* go, uint64_t eps,
@@ -313,7 +307,10 @@ cudaError_t attn_backward(const int16_t* q, const int16_t* k, const int16_t* v, 
 
 // ------------------------------------------------------------------ layout --
 struct LayerCache {
-  int16_t *in, *an, *qkv, *ctx, *P, *ares, *mn, *up, *gate, *gated, *out;
+  int16_t *in, *qkv, *P, *ares, *up, *gate, *out;
+  // inputs of the linears as byte planes (+ row L1): the forward GEMMs read
+  // them and the weight gradients read them again in the backward
+  Planes an, ctx, mn, gated;  // q|k|v input, o input, up|gate input, down input
   int8_t *wt[7];  // transposed q k v o (d x d), up, gate ([d][F]), down ([F][d])
 };
 
@@ -329,7 +326,6 @@ struct StepLayout {
   int8_t* headT;
   nsrl_fixed_scale* ident;
   unsigned long long* fwd_res;
-  WgBufs wg;
   Planes pqkv;  // q|k planes of the tensor-core attention (v goes to vt)
   Planes pg[3];  // prescaled planes of dQ, dK, dV
   VtPlanes vt;
@@ -355,15 +351,15 @@ void carve_step(const nsrl_train_model* m, size_t W, bool rms, void* base, StepL
   for (size_t l = 0; l < o.L; ++l) {
     LayerCache& lc = o.lc[l];
     lc.in = l == 0 ? o.xemb : o.lc[l - 1].out;
-    lc.an = rms ? c.take<int16_t>(T * d) : lc.in;
+    lc.an = c.planes(T, d, true);
     lc.qkv = c.take<int16_t>(T * 3 * d);
-    lc.ctx = c.take<int16_t>(T * d);
+    lc.ctx = c.planes(T, d, true);
     lc.P = c.take<int16_t>(W * H * S * S);
     lc.ares = c.take<int16_t>(T * d);
-    lc.mn = rms ? c.take<int16_t>(T * d) : lc.ares;
+    lc.mn = c.planes(T, d, true);
     lc.up = c.take<int16_t>(T * F);
     lc.gate = c.take<int16_t>(T * F);
-    lc.gated = c.take<int16_t>(T * F);
+    lc.gated = c.planes(T, F, true);
     lc.out = c.take<int16_t>(T * d);
     for (int i = 0; i < 4; ++i) lc.wt[i] = c.take<int8_t>(d * d);
     for (int i = 4; i < 7; ++i) lc.wt[i] = c.take<int8_t>(d * F);
@@ -387,11 +383,6 @@ void carve_step(const nsrl_train_model* m, size_t W, bool rms, void* base, StepL
   o.headT = c.take<int8_t>(d * 256);
   o.ident = c.take<nsrl_fixed_scale>(std::max<size_t>(wide, 256));
   o.fwd_res = c.take<unsigned long long>(4);
-  o.wg.ldt = wgrad_planes_ld(T);
-  o.wg.gh = c.take<int8_t>(wide * o.wg.ldt);
-  o.wg.gl = c.take<uint8_t>(wide * o.wg.ldt);
-  o.wg.xh = c.take<int8_t>(wide * o.wg.ldt);
-  o.wg.xl = c.take<uint8_t>(wide * o.wg.ldt);
   o.pqkv = Planes{nullptr, nullptr, nullptr, 3 * d};
   o.vt = VtPlanes{nullptr, nullptr, (int)S, (int)H, (int)(d / H), nullptr};
   if (attention_tc_supported(S, d, H)) {
@@ -580,9 +571,11 @@ nsrl_status nsrl_attention_backward(const int16_t* q, const int16_t* k, const in
   return NSRL_OK;
 }
 
+// Rows of the byte planes of the standalone weight gradient: 16-byte multiples (TMA strides).
+size_t plane_ld(size_t dim) { return (dim + 15) & ~size_t(15); }
+
 size_t nsrl_accumulate_weight_gradient_i16_workspace_size(size_t rows, size_t input_dim, size_t output_dim) {
-  const size_t ldt = wgrad_planes_ld(rows);
-  return 2 * up256(output_dim * ldt) + 2 * up256(input_dim * ldt);
+  return 2 * up256(rows * plane_ld(output_dim)) + 2 * up256(rows * plane_ld(input_dim));
 }
 
 nsrl_status nsrl_accumulate_weight_gradient_i16(const int16_t* x, const int16_t* grad_output, size_t rows,
@@ -599,16 +592,13 @@ nsrl_status nsrl_accumulate_weight_gradient_i16(const int16_t* x, const int16_t*
     return fail_shape("workspace too small");
   cudaStream_t s = (cudaStream_t)stream;
   Carve c(workspace);
-  WgBufs b;
-  b.ldt = wgrad_planes_ld(rows);
-  b.gh = c.take<int8_t>(output_dim * b.ldt);
-  b.gl = c.take<uint8_t>(output_dim * b.ldt);
-  b.xh = c.take<int8_t>(input_dim * b.ldt);
-  b.xl = c.take<uint8_t>(input_dim * b.ldt);
+  // byte planes of g' = rhu(g, shift_n) and of x, row-major as the kernel reads them
+  const Planes gp = c.planes(rows, plane_ld(output_dim), false);
+  const Planes xp = c.planes(rows, plane_ld(input_dim), false);
   check_mult_one_kernel<<<blocks_for((long long)output_dim), 256, 0, s>>>(scales, (int)output_dim, nullptr, st);
-  TS_TRY(accumulate_tc(b, x, input_dim, grad_output, output_dim, scales, rows, input_dim, output_dim, accumulators,
-                       st, s),
-         "weight-gradient accumulation");
+  TS_TRY(prescale_split(grad_output, rows, output_dim, output_dim, scales, gp, s), "prescale");
+  TS_TRY(launch_split_planes(x, rows, input_dim, input_dim, xp, s), "split");
+  TS_TRY(accumulate_planes(gp, xp, rows, input_dim, output_dim, accumulators, st, s), "weight-gradient accumulation");
   CountInc inc{};
   inc.n = 1;
   inc.idx[0] = 0;
@@ -680,23 +670,21 @@ nsrl_status nsrl_train_windows(const nsrl_train_model* m, const uint8_t* context
                                                                   m->embeddings, m->positions, o.xemb);
     TS_TRY(cudaGetLastError(), "embed");
   }
-  Planes pad{o.pa.hi, o.pa.lo, o.pa.l1, d};
-  Planes paF{o.pa.hi, o.pa.lo, o.pa.l1, F};
   for (size_t l = 0; l < L; ++l) {
     const nsrl_train_layer& ly = m->layer[l];
     LayerCache& c = o.lc[l];
     if (rms)
-      TS_TRY(launch_rms_norm(c.in, T, d, ly.attn_gamma, 1, c.an, pad, st, s), "rms");
+      TS_TRY(launch_rms_norm(c.in, T, d, ly.attn_gamma, 1, nullptr, c.an, st, s), "rms");
     else
-      TS_TRY(launch_split_planes(c.in, T, d, d, pad, s), "split");
+      TS_TRY(launch_split_planes(c.in, T, d, d, c.an, s), "split");
     // Q|K|V: with the tcgen05 attention, one GEMM writes the int16 rows (the
     // cache the backward reads), the Q|K planes and the transposed V planes.
     const bool tc_attn = o.vt.hi && tma_supported() && attention_tc_supported(S, d, H);
     {
       GemmArgs g{};
-      g.a_hi = pad.hi;
-      g.a_lo = pad.lo;
-      g.a_l1 = pad.l1;
+      g.a_hi = c.an.hi;
+      g.a_lo = c.an.lo;
+      g.a_l1 = c.an.l1;
       g.lda = d;
       g.M = T;
       g.K = d;
@@ -717,37 +705,36 @@ nsrl_status nsrl_train_windows(const nsrl_train_model* m, const uint8_t* context
     if (tc_attn) {
       // every P entry the backward reads is written: the visited key tiles of
       // each 128-query tile, zeros above the diagonal
-      TS_TRY(cudaMemsetAsync(pad.l1, 0, T * sizeof(unsigned long long), s), "memset");
-      const cudaError_t e = launch_attention_tc(o.pqkv, o.vt, W, S, d, H, true, pad, o.vt.wscr, st, s, c.P);
+      TS_TRY(cudaMemsetAsync(c.ctx.l1, 0, T * sizeof(unsigned long long), s), "memset");
+      const cudaError_t e = launch_attention_tc(o.pqkv, o.vt, W, S, d, H, true, c.ctx, o.vt.wscr, st, s, c.P);
       if (e != cudaErrorNotSupported) {
         TS_TRY(e, "attention");
-        TS_TRY(launch_join_planes(pad, T, d, c.ctx, d, s), "join");
         done = true;
       }
     }
-    if (!done) {
-      TS_TRY(launch_attention_rows_probs(c.qkv, c.qkv + d, c.qkv + 2 * d, 3 * d, W, S, d, H, c.ctx, c.P, st, s),
+    if (!done) {  // int16 context in a backward buffer that is free during the forward
+      TS_TRY(launch_attention_rows_probs(c.qkv, c.qkv + d, c.qkv + 2 * d, 3 * d, W, S, d, H, o.gctx, c.P, st, s),
              "attention");
-      TS_TRY(launch_split_planes(c.ctx, T, d, d, pad, s), "split");
+      TS_TRY(launch_split_planes(o.gctx, T, d, d, c.ctx, s), "split");
     }
-    TS_TRY(fwd_gemm(pad, T, d, &ly.lin[3], Epi::RESID, c.ares, d, c.in, o.fwd_res, st, s), "o");
+    TS_TRY(fwd_gemm(c.ctx, T, d, &ly.lin[3], Epi::RESID, c.ares, d, c.in, o.fwd_res, st, s), "o");
     if (rms)
-      TS_TRY(launch_rms_norm(c.ares, T, d, ly.mlp_gamma, 1, c.mn, pad, st, s), "rms");
+      TS_TRY(launch_rms_norm(c.ares, T, d, ly.mlp_gamma, 1, nullptr, c.mn, st, s), "rms");
     else
-      TS_TRY(launch_split_planes(c.ares, T, d, d, pad, s), "split");
-    TS_TRY(fwd_gemm(pad, T, d, &ly.lin[4], Epi::I16, c.up, F, nullptr, nullptr, st, s), "up");
-    TS_TRY(fwd_gemm(pad, T, d, &ly.lin[5], Epi::I16, c.gate, F, nullptr, nullptr, st, s), "gate");
+      TS_TRY(launch_split_planes(c.ares, T, d, d, c.mn, s), "split");
+    TS_TRY(fwd_gemm(c.mn, T, d, &ly.lin[4], Epi::I16, c.up, F, nullptr, nullptr, st, s), "up");
+    TS_TRY(fwd_gemm(c.mn, T, d, &ly.lin[5], Epi::I16, c.gate, F, nullptr, nullptr, st, s), "gate");
     {
       ProfScope prof("gated_forward", s, 0.0, 8.0 * (double)T * (double)F);
       if (F % 8 == 0)
         gated_forward_vec_kernel<<<blocks_for((long long)T * 32, 148 * 16), 256, 0, s>>>(
-            c.up, c.gate, (long long)T, (int)F, c.gated, paF.hi, paF.lo, paF.l1);
+            c.up, c.gate, (long long)T, (int)F, nullptr, c.gated.hi, c.gated.lo, c.gated.l1);
       else
         gated_forward_kernel<<<blocks_for((long long)T * 32, 148 * 16), 256, 0, s>>>(
-            c.up, c.gate, (long long)T, (int)F, c.gated, paF.hi, paF.lo, paF.l1);
+            c.up, c.gate, (long long)T, (int)F, nullptr, c.gated.hi, c.gated.lo, c.gated.l1);
       TS_TRY(cudaGetLastError(), "gated");
     }
-    TS_TRY(fwd_gemm(paF, T, F, &ly.lin[6], Epi::RESID, c.out, d, c.ares, o.fwd_res, st, s), "down");
+    TS_TRY(fwd_gemm(c.gated, T, F, &ly.lin[6], Epi::RESID, c.out, d, c.ares, o.fwd_res, st, s), "down");
   }
 
   // ---- byte head on the last position, softmax gradient (lib.rs:17455-17488, :18845-18949)
@@ -791,6 +778,9 @@ nsrl_status nsrl_train_windows(const nsrl_train_model* m, const uint8_t* context
     // gated MLP backward input (mlp.rs:256-357)
     TS_TRY(prescale_split(o.G, T, d, d, ly.lin[6].scales, padn, s), "prescale");
     TS_TRY(bwd_gemm(padn, T, d, c.wt[6], F, o.ident, o.gg, F, nullptr, nullptr, st, s), "down^T");
+    // down weight gradient (lib.rs:13783-13871) from the prescaled G planes,
+    // before the gated backward reuses their buffer
+    TS_TRY(accumulate_planes(padn, c.gated, T, F, d, acc + lin_off[6], st, s), "down grad");
     {
       const long long n = (long long)T * F;
       ProfScope prof("gated_backward", s, 0.0, 14.0 * (double)n);
@@ -815,20 +805,19 @@ nsrl_status nsrl_train_windows(const nsrl_train_model* m, const uint8_t* context
                                                                                  &cnt[5], &cnt[6]);
       TS_TRY(cudaGetLastError(), "nonzero rows");
     }
-    TS_TRY(accumulate_tc(o.wg, c.gated, F, o.G, d, ly.lin[6].scales, T, F, d, acc + lin_off[6], st, s), "down grad");
-    TS_TRY(accumulate_tc(o.wg, c.mn, d, o.gup, F, ly.lin[4].scales, T, d, F, acc + lin_off[4], st, s), "up grad");
-    TS_TRY(accumulate_tc(o.wg, c.mn, d, o.ggate, F, ly.lin[5].scales, T, d, F, acc + lin_off[5], st, s, true),
-           "gate grad");
+    // up and gate weight gradients from the gated backward's prescaled planes
+    TS_TRY(accumulate_planes(paFn, c.mn, T, d, F, acc + lin_off[4], st, s), "up grad");
+    TS_TRY(accumulate_planes(pbF, c.mn, T, d, F, acc + lin_off[5], st, s), "gate grad");
     // attention update, accumulate form (lib.rs:15777-16075)
     TS_TRY(prescale_split(o.gao, T, d, d, ly.lin[3].scales, padn, s), "prescale");
     TS_TRY(bwd_gemm(padn, T, d, c.wt[3], d, o.ident, o.gctx, d, nullptr, nullptr, st, s), "o^T");
+    TS_TRY(accumulate_planes(padn, c.ctx, T, d, d, acc + lin_off[3], st, s), "o grad");
     GradPlanes gp[3];
     for (int i = 0; i < 3; ++i) gp[i] = GradPlanes{ly.lin[i].scales, o.pg[i].hi, o.pg[i].lo};
     TS_TRY(attn_backward(c.qkv, c.qkv + d, c.qkv + 2 * d, 3 * d, c.P, o.gctx, d, W, S, d, H, o.dL, o.dq, o.dk, o.dv,
                          o.abw, o.abw_bytes, st, s, gp),
            "attention backward");
     int16_t* gin[3] = {o.gq, o.gk, o.gv};
-    const int16_t* dqkv[3] = {o.dq, o.dk, o.dv};
     for (int i = 0; i < 3; ++i)
       TS_TRY(bwd_gemm(Planes{o.pg[i].hi, o.pg[i].lo, nullptr, d}, T, d, c.wt[i], d, o.ident, gin[i], d, nullptr,
                       nullptr, st, s),
@@ -842,10 +831,9 @@ nsrl_status nsrl_train_windows(const nsrl_train_model* m, const uint8_t* context
         fanin3_kernel<<<blocks_for(n), 256, 0, s>>>(o.gq, o.gk, o.gv, n, o.gni, attn_sat);
       TS_TRY(cudaGetLastError(), "fanin");
     }
-    for (int i = 0; i < 3; ++i)
-      TS_TRY(accumulate_tc(o.wg, c.an, d, dqkv[i], d, ly.lin[i].scales, T, d, d, acc + lin_off[i], st, s, i > 0),
+    for (int i = 0; i < 3; ++i)  // from the prescaled dQ, dK, dV planes of the attention backward
+      TS_TRY(accumulate_planes(Planes{o.pg[i].hi, o.pg[i].lo, nullptr, d}, c.an, T, d, d, acc + lin_off[i], st, s),
              "qkv grad");
-    TS_TRY(accumulate_tc(o.wg, c.ctx, d, o.gao, d, ly.lin[3].scales, T, d, d, acc + lin_off[3], st, s), "o grad");
     for (int i = 0; i < 4; ++i) add_count(1 + 9 * l + i, T);
     const int16_t* gai = o.gni;
     if (rms) {

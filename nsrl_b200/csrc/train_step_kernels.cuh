@@ -231,7 +231,7 @@ __global__ void gated_forward_kernel(const int16_t* __restrict__ up, const int16
     for (int f = lane; f < F; f += 32) {
       const long long i = r * F + f;
       const int v = gated_act(up[i], gate[i]);
-      gated[i] = (int16_t)v;
+      if (gated) gated[i] = (int16_t)v;
       hi[i] = (int8_t)(v >> 8);
       lo[i] = (uint8_t)(v & 255);
       s += (unsigned long long)abs(v);
@@ -259,7 +259,7 @@ __global__ void gated_forward_vec_kernel(const int16_t* __restrict__ up, const i
         v[e] = gated_act(u[e], g[e]);
         s += (unsigned long long)abs(v[e]);
       }
-      reinterpret_cast<uint4*>(gated)[i8] = pack8(v);
+      if (gated) reinterpret_cast<uint4*>(gated)[i8] = pack8(v);
       uint2 h, l;
       planes8(v, h, l);
       reinterpret_cast<uint2*>(hi)[i8] = h;
@@ -447,6 +447,62 @@ __global__ void __launch_bounds__(256) accumulate_pre_kernel(const int16_t* __re
     __syncthreads();
   }
   if (bad) nsrl_flag(st, NSRL_FLAG_LINEAR_OVERFLOW);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int n = n0 + tn + 16 * i;
+    if (n >= N) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int k = k0 + tk + 16 * j;
+      if (k < K) acc[(long long)n * K + k] += c[i][j];
+    }
+  }
+}
+
+// acc[n][k] += sum_r g'[r][n] * x[r][k] from byte planes (g' already
+// prescaled: 256 * gh + gl; x = 256 * xh + xl), the SIMT form of the
+// tensor-core weight gradient for operands TMA cannot take.
+__global__ void __launch_bounds__(256) accumulate_planes_kernel(const int8_t* __restrict__ gh,
+                                                                const uint8_t* __restrict__ gl, long long ldg,
+                                                                const int8_t* __restrict__ xh,
+                                                                const uint8_t* __restrict__ xl, long long ldx,
+                                                                int rows, int K, int N, long long* __restrict__ acc) {
+  __shared__ int32_t sg[ATR][ATN];
+  __shared__ int32_t sx[ATR][ATK + 1];
+  const int n0 = blockIdx.y * ATN, k0 = blockIdx.x * ATK;
+  const int tn = threadIdx.x / 16, tk = threadIdx.x % 16;
+  long long c[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) c[i][j] = 0;
+  for (int r0 = 0; r0 < rows; r0 += ATR) {
+    for (int i = threadIdx.x; i < ATR * ATN; i += 256) {
+      const int rr = i / ATN, nn = i % ATN;
+      const long long o = (long long)(r0 + rr) * ldg + n0 + nn;
+      sg[rr][nn] = (r0 + rr < rows && n0 + nn < N) ? (int)gh[o] * 256 + (int)gl[o] : 0;
+    }
+    for (int i = threadIdx.x; i < ATR * ATK; i += 256) {
+      const int rr = i / ATK, kk = i % ATK;
+      const long long o = (long long)(r0 + rr) * ldx + k0 + kk;
+      sx[rr][kk] = (r0 + rr < rows && k0 + kk < K) ? (int)xh[o] * 256 + (int)xl[o] : 0;
+    }
+    __syncthreads();
+#pragma unroll 4
+    for (int rr = 0; rr < ATR; ++rr) {
+      long long gv[4];
+      int xv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) gv[i] = sg[rr][tn + 16 * i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) xv[j] = sx[rr][tk + 16 * j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) c[i][j] += gv[i] * xv[j];
+    }
+    __syncthreads();
+  }
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int n = n0 + tn + 16 * i;

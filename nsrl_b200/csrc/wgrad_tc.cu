@@ -4,8 +4,10 @@
 // over rows (integer addition is exact in any order; i64 overflow is ruled
 // out by the caller's bound).
 //
-// Operands are byte planes of the transposed tensors, the reduction index t
-// contiguous: G^T [N][T] and X^T [K][T], hi = v >> 8 (s8), lo = v & 255 (u8).
+// Operands are the byte planes of the row-major tensors, G [T][N] and X [T][K]
+// (hi = v >> 8, s8; lo = v & 255, u8), as their producers write them; the MMAs
+// read them MN-major (n and k contiguous, the reduction index t across rows),
+// so nothing is transposed.
 // With g = 256 gh + gl and x = 256 xh + xl,
 //   g x = 65536 gh xh + 256 (gh xl + gl xh) + gl xl,
 // so per 128-row block four MMAs fill three s32 TMEM accumulators:
@@ -17,9 +19,10 @@
 // adds it to acc with red.global.add.u64 (two's-complement, exact).
 //
 // Persistent kernel, 18 warps: warp 0 issues TMA (a 3-stage ring of four
-// 16 KB plane tiles), warp 1 owns TMEM and issues the MMAs, warps 2..17 run
-// the epilogue (one TMEM lane quarter and 32 columns each).  Work items are
-// (n tile, k tile, row chunk) triples; several CTAs add into one tile.
+// 16 KB plane tiles of 128 rows x 128 columns), warp 1 owns TMEM and issues
+// the MMAs, warps 2..17 run the epilogue (one TMEM lane quarter and 32 columns
+// each).  Work items are (n tile, k tile, row chunk) triples; several CTAs add
+// into one tile.
 #include <algorithm>
 
 #include "common.cuh"
@@ -51,6 +54,18 @@ struct WgParams {
   long long* acc;
   nsrl_device_status* st;
 };
+
+// Shared-memory descriptor of an MN-major operand tile in the 128-byte
+// swizzle: each 128-byte row holds 128 consecutive n (or k) of one t, 8-row
+// groups 1024 B apart (stride byte offset); the tile is one 128-byte MN chunk.
+__device__ __forceinline__ uint64_t sdesc_mn128(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// kind::i8 instruction descriptor with both operands MN-major.
+constexpr uint32_t idesc_i8_mn(uint32_t M, uint32_t N, uint32_t a_signed, uint32_t b_signed) {
+  return idesc_i8(M, N, a_signed, b_signed) | (1u << 15) | (1u << 16);
+}
 
 __device__ __forceinline__ void red_add_u64(long long* p, long long v) {
   asm volatile("red.global.add.u64 [%0], %1;" ::"l"(p), "l"((unsigned long long)v) : "memory");
@@ -111,10 +126,10 @@ __global__ void __launch_bounds__(WTHREADS, 1) wgrad_tc_kernel(const __grid_cons
           }
           mbar_arrive_expect_tx(&full[s], WSTAGE);
           uint8_t* sa = smem + s * WSTAGE;
-          tma_load_2d(sa, &maps.gh, &full[s], b * WB, n0);
-          tma_load_2d(sa + WTILE, &maps.gl, &full[s], b * WB, n0);
-          tma_load_2d(sa + 2 * WTILE, &maps.xh, &full[s], b * WB, k0);
-          tma_load_2d(sa + 3 * WTILE, &maps.xl, &full[s], b * WB, k0);
+          tma_load_2d(sa, &maps.gh, &full[s], n0, b * WB);
+          tma_load_2d(sa + WTILE, &maps.gl, &full[s], n0, b * WB);
+          tma_load_2d(sa + 2 * WTILE, &maps.xh, &full[s], k0, b * WB);
+          tma_load_2d(sa + 3 * WTILE, &maps.xl, &full[s], k0, b * WB);
         }
       }
       // the last loads in flight land before the CTA exits
@@ -123,10 +138,10 @@ __global__ void __launch_bounds__(WTHREADS, 1) wgrad_tc_kernel(const __grid_cons
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t id_ss = idesc_i8(WB, WB, 1, 1);
-      const uint32_t id_su = idesc_i8(WB, WB, 1, 0);
-      const uint32_t id_us = idesc_i8(WB, WB, 0, 1);
-      const uint32_t id_uu = idesc_i8(WB, WB, 0, 0);
+      const uint32_t id_ss = idesc_i8_mn(WB, WB, 1, 1);
+      const uint32_t id_su = idesc_i8_mn(WB, WB, 1, 0);
+      const uint32_t id_us = idesc_i8_mn(WB, WB, 0, 1);
+      const uint32_t id_uu = idesc_i8_mn(WB, WB, 0, 0);
       uint32_t it = 0, local = 0;
       bool ok = true;
       for (int item = blockIdx.x; item < p.items && ok; item += gridDim.x, ++local) {
@@ -144,11 +159,11 @@ __global__ void __launch_bounds__(WTHREADS, 1) wgrad_tc_kernel(const __grid_cons
           tc_fence_after();
           const uint32_t base = smem_u32(smem + s * WSTAGE);
 #pragma unroll
-          for (int j = 0; j < WB / 32; ++j) {
-            const uint64_t gh = sdesc_k128(base + 32 * j);
-            const uint64_t gl = sdesc_k128(base + WTILE + 32 * j);
-            const uint64_t xh = sdesc_k128(base + 2 * WTILE + 32 * j);
-            const uint64_t xl = sdesc_k128(base + 3 * WTILE + 32 * j);
+          for (int j = 0; j < WB / 32; ++j) {  // 32 rows t (4 KB of each tile) per MMA
+            const uint64_t gh = sdesc_mn128(base + 4096 * j);
+            const uint64_t gl = sdesc_mn128(base + WTILE + 4096 * j);
+            const uint64_t xh = sdesc_mn128(base + 2 * WTILE + 4096 * j);
+            const uint64_t xl = sdesc_mn128(base + 3 * WTILE + 4096 * j);
             const uint32_t acc = (b > b0 || j > 0) ? 1u : 0u;
             umma_i8(tmem, gh, xh, id_ss, acc);
             umma_i8(tmem + WB, gh, xl, id_su, acc);
@@ -205,86 +220,6 @@ __global__ void __launch_bounds__(WTHREADS, 1) wgrad_tc_kernel(const __grid_cons
   }
 }
 
-// [T][C] int16 (row stride ld) -> byte planes of the transpose [C][T]
-// (row stride ldt bytes), each value first prescaled by rhu(v, shift_c)
-// when `sc` is given (multiplier 1).  A CTA moves 128 rows x 64 columns:
-// 16-byte loads of eight columns into shared memory, kept as 32-bit words
-// (two columns) with the word index XORed by 4 ((t / 16) mod 8) so that the
-// column reads below are conflict-free; then each thread gathers 16 rows of
-// one column pair and writes 16-byte words of both planes for both columns.
-// Rows t >= T are written as zeros up to the next multiple of 128 (inside
-// ldt); columns c >= C are not written.
-__global__ void __launch_bounds__(256) transpose_split_kernel(const int16_t* __restrict__ x, long long T, int C,
-                                                              long long ld, const nsrl_fixed_scale* __restrict__ sc,
-                                                              int8_t* __restrict__ th, uint8_t* __restrict__ tl,
-                                                              long long ldt, bool vec) {
-  __shared__ __align__(16) uint32_t tile[128 * 32];  // [t][column pair ^ swizzle]
-  const long long t0 = (long long)blockIdx.x * 128;
-  const int c0 = blockIdx.y * 64;
-  const int tid = threadIdx.x;
-#pragma unroll
-  for (int z = 0; z < 4; ++z) {
-    const int i = tid + 256 * z;
-    const int r = i >> 3, c8 = (i & 7) * 8;
-    const long long t = t0 + r;
-    const int c = c0 + c8;
-    int v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    if (t < T) {
-      if (vec && c + 7 < C) {
-        const uint4 u = *reinterpret_cast<const uint4*>(x + t * ld + c);
-        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          v[2 * q] = (int16_t)(w[q] & 0xFFFF);
-          v[2 * q + 1] = (int16_t)(w[q] >> 16);
-        }
-      } else {
-#pragma unroll
-        for (int q = 0; q < 8; ++q)
-          if (c + q < C) v[q] = x[t * ld + c + q];
-      }
-      if (sc) {
-#pragma unroll
-        for (int q = 0; q < 8; ++q)
-          if (c + q < C) {
-            v[q] = rhu_i16(v[q], sc[c + q].right_shift);
-          }
-      }
-    }
-    uint4 o;
-    o.x = (uint32_t)(v[0] & 0xFFFF) | ((uint32_t)v[1] << 16);
-    o.y = (uint32_t)(v[2] & 0xFFFF) | ((uint32_t)v[3] << 16);
-    o.z = (uint32_t)(v[4] & 0xFFFF) | ((uint32_t)v[5] << 16);
-    o.w = (uint32_t)(v[6] & 0xFFFF) | ((uint32_t)v[7] << 16);
-    const int wc = (c8 >> 1) ^ (((r >> 4) & 7) << 2);  // a multiple of 4: the 4 words stay together
-    *reinterpret_cast<uint4*>(&tile[r * 32 + wc]) = o;
-  }
-  __syncthreads();
-  const int cw = tid >> 3;         // column pair 0..31
-  const int tb = (tid & 7) * 16;   // rows tb .. tb + 15
-  const int wc = cw ^ (((tb >> 4) & 7) << 2);
-  uint32_t hi[2][4], lo[2][4];     // [column of the pair][word of 4 rows]
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const uint32_t w0 = tile[(tb + 4 * q) * 32 + wc], w1 = tile[(tb + 4 * q + 1) * 32 + wc];
-    const uint32_t w2 = tile[(tb + 4 * q + 2) * 32 + wc], w3 = tile[(tb + 4 * q + 3) * 32 + wc];
-    const uint32_t ah = __byte_perm(w0, w1, 0x7531), bh = __byte_perm(w2, w3, 0x7531);  // hi bytes, c0 c1 c0 c1
-    const uint32_t al = __byte_perm(w0, w1, 0x6420), bl = __byte_perm(w2, w3, 0x6420);  // lo bytes
-    hi[0][q] = __byte_perm(ah, bh, 0x6420);
-    hi[1][q] = __byte_perm(ah, bh, 0x7531);
-    lo[0][q] = __byte_perm(al, bl, 0x6420);
-    lo[1][q] = __byte_perm(al, bl, 0x7531);
-  }
-#pragma unroll
-  for (int e = 0; e < 2; ++e) {
-    const int c = c0 + 2 * cw + e;
-    if (c >= C) continue;
-    const long long off = (long long)c * ldt + t0 + tb;
-    *reinterpret_cast<uint4*>(th + off) = make_uint4(hi[e][0], hi[e][1], hi[e][2], hi[e][3]);
-    *reinterpret_cast<uint4*>(tl + off) = make_uint4(lo[e][0], lo[e][1], lo[e][2], lo[e][3]);
-  }
-}
-
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -303,7 +238,7 @@ EncodeTiledFn wg_encode_fn() {
   return fn;
 }
 
-// uint8 [rows][inner] (row stride ld bytes), box 128 x 128 bytes, 128-byte swizzle.
+// uint8 [rows][inner] (row stride ld bytes), box 128 rows x 128 bytes, 128-byte swizzle.
 bool wg_map(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t rows, uint64_t ld) {
   EncodeTiledFn fn = wg_encode_fn();
   if (!fn) return false;
@@ -318,35 +253,20 @@ bool wg_map(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t rows, uint
 
 }  // namespace
 
-size_t wgrad_planes_ld(size_t T) { return (T + 127) & ~size_t(127); }
-
-cudaError_t launch_transpose_split(const int16_t* x, size_t T, size_t C, size_t ld, const nsrl_fixed_scale* sc,
-                                   int8_t* th, uint8_t* tl, size_t ldt, cudaStream_t s) {
-  if (T == 0 || C == 0) return cudaSuccess;
-  // 16-byte stores of 16 rows need ldt, the plane bases and the zero-padded
-  // tail (T rounded up to 128) inside the rows
-  if (ldt % 16 != 0 || ldt < ((T + 127) & ~size_t(127)) || (reinterpret_cast<uintptr_t>(th) & 15) != 0 ||
-      (reinterpret_cast<uintptr_t>(tl) & 15) != 0)
-    return cudaErrorInvalidValue;
-  dim3 grid((unsigned)((T + 127) / 128), (unsigned)((C + 63) / 64));
-  ProfScope prof("transpose_split", s, 0.0, 4.0 * (double)T * (double)C);
-  const bool vec = ld % 8 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
-  transpose_split_kernel<<<grid, 256, 0, s>>>(x, (long long)T, (int)C, (long long)ld, sc, th, tl, (long long)ldt,
-                                              vec);
-  return cudaGetLastError();
-}
-
-// acc [N][K] += G^T X from the transposed planes (row stride ldt, T rows).
-// Returns cudaErrorNotSupported when TMA is unavailable.
-cudaError_t launch_wgrad_tc(const int8_t* gh, const uint8_t* gl, const int8_t* xh, const uint8_t* xl, size_t ldt,
-                            size_t T, size_t N, size_t K, long long* acc, nsrl_device_status* st,
+// acc [N][K] += G^T X from the row-major planes G [T][N] (row stride ldg
+// bytes) and X [T][K] (ldx).  Returns cudaErrorNotSupported when TMA cannot
+// take them (no TMA, or a stride / base not 16-byte aligned).
+cudaError_t launch_wgrad_tc(const int8_t* gh, const uint8_t* gl, size_t ldg, const int8_t* xh, const uint8_t* xl,
+                            size_t ldx, size_t T, size_t N, size_t K, long long* acc, nsrl_device_status* st,
                             cudaStream_t s) {
   if (T == 0 || N == 0 || K == 0) return cudaSuccess;
-  if (ldt % 16 != 0 || T > (size_t)INT32_MAX || N > (size_t)INT32_MAX || K > (size_t)INT32_MAX)
-    return cudaErrorInvalidValue;
+  if (T > (size_t)INT32_MAX || N > (size_t)INT32_MAX || K > (size_t)INT32_MAX) return cudaErrorInvalidValue;
+  auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+  if (ldg % 16 != 0 || ldx % 16 != 0 || !al16(gh) || !al16(gl) || !al16(xh) || !al16(xl))
+    return cudaErrorNotSupported;
   WgMaps maps;
-  if (!wg_map(&maps.gh, gh, T, N, ldt) || !wg_map(&maps.gl, gl, T, N, ldt) || !wg_map(&maps.xh, xh, T, K, ldt) ||
-      !wg_map(&maps.xl, xl, T, K, ldt))
+  if (!wg_map(&maps.gh, gh, N, T, ldg) || !wg_map(&maps.gl, gl, N, T, ldg) || !wg_map(&maps.xh, xh, K, T, ldx) ||
+      !wg_map(&maps.xl, xl, K, T, ldx))
     return cudaErrorNotSupported;
   static bool configured = false;
   if (!configured) {
