@@ -587,7 +587,7 @@ __global__ void __launch_bounds__(HD == 64 ? 256 : 128, 2) attn_bwd_dq_kernel(co
     if (q0 + lr >= S) continue;
     const uint4 u = *reinterpret_cast<const uint4*>(&so[lr * OSTR + c8]);
     const long long off = (row0 + q0 + lr) * a.ldo + (long long)h * HD + c8;
-    *reinterpret_cast<uint4*>(a.dQ + off) = u;
+    if (a.dQ) *reinterpret_cast<uint4*>(a.dQ + off) = u;
     if (a.gp.hi) {
       int v[8];
       unpack8(u, v);
@@ -703,7 +703,8 @@ __global__ void __launch_bounds__(128) attn_bwd_kv_kernel(const KVArgs a) {
         v[e] = sat_i16(rhu64(tot, (uint32_t)a.shift));
       }
       const int col = h * HD + 8 * n + 2 * t;
-      *reinterpret_cast<uint32_t*>(a.out + (row0 + kr) * a.ldo + col) = (uint32_t)(v[0] & 0xFFFF) | ((uint32_t)v[1] << 16);
+      if (a.out)
+        *reinterpret_cast<uint32_t*>(a.out + (row0 + kr) * a.ldo + col) = (uint32_t)(v[0] & 0xFFFF) | ((uint32_t)v[1] << 16);
       if (a.gp.hi) store_grad_planes2(a.gp, (row0 + kr) * a.ldo + col, col, v);
     }
 }
@@ -831,7 +832,8 @@ __global__ void __launch_bounds__(HD == 64 ? 256 : 128) attn_bwd_kv2_kernel(cons
         v[e] = sat_i16(rhu64(tot, (uint32_t)a.shift));
       }
       const int col = h * HD + d0 + 8 * n + 2 * t;
-      *reinterpret_cast<uint32_t*>(a.out + (row0 + kr) * a.ldo + col) = (uint32_t)(v[0] & 0xFFFF) | ((uint32_t)v[1] << 16);
+      if (a.out)
+        *reinterpret_cast<uint32_t*>(a.out + (row0 + kr) * a.ldo + col) = (uint32_t)(v[0] & 0xFFFF) | ((uint32_t)v[1] << 16);
       if (a.gp.hi) store_grad_planes2(a.gp, (row0 + kr) * a.ldo + col, col, v);
     }
 }
@@ -928,7 +930,9 @@ cudaError_t launch_attention_backward_tc(const int16_t* q, const int16_t* k, con
     if (e != cudaSuccess) return e;
   }
   {
-    DqArgs qa{kth, ktl, (int)Sp, dl, (int)S, (int)H, shift, dq, (long long)d, planes ? planes[0] : GradPlanes{}};
+    // with plane outputs the int16 gradients are not written (nothing reads them)
+    DqArgs qa{kth, ktl, (int)Sp, dl, (int)S, (int)H, shift, planes ? nullptr : dq, (long long)d,
+              planes ? planes[0] : GradPlanes{}};
     ProfScope prof("attention_bwd_dq", s, 2.0 * (double)hd * pairs,
                    2.0 * (double)B * H * S * S + 4.0 * (double)B * S * d);
     if (hd == 64)
@@ -943,8 +947,10 @@ cudaError_t launch_attention_backward_tc(const int16_t* q, const int16_t* k, con
     e = launch_sq_transpose(dl, B * H, S, lth, ltl, s);
     if (e != cudaSuccess) return e;
   }
-  KVArgs ka{lth, ltl, qth, qtl, (int)S, (int)H, shift, dk, (long long)d, planes ? planes[1] : GradPlanes{}};
-  KVArgs va{pth, ptl, cth, ctl, (int)S, (int)H, 15, dv, (long long)d, planes ? planes[2] : GradPlanes{}};
+  KVArgs ka{lth, ltl, qth, qtl, (int)S, (int)H, shift, planes ? nullptr : dk, (long long)d,
+            planes ? planes[1] : GradPlanes{}};
+  KVArgs va{pth, ptl, cth, ctl, (int)S, (int)H, 15, planes ? nullptr : dv, (long long)d,
+            planes ? planes[2] : GradPlanes{}};
   ProfScope prof("attention_bwd_kv", s, 2.0 * 2.0 * (double)hd * pairs,
                  2.0 * 2.0 * (double)B * H * S * S + 8.0 * (double)B * S * d);
   if (S % 16 == 0) {  // 16-byte staging of the M^T and X^T rows

@@ -133,7 +133,8 @@ cudaError_t launch_wgrad_tc(const int8_t* gh, const uint8_t* gl, size_t ldg, con
 // cudaErrorNotSupported outside head_dim 16/64, S % 4 == 0, d % 16 == 0,
 // S <= 16384, or with a scratch below attention_backward_tc_scratch_bytes.
 // Optional second form of an attention gradient: byte planes [B*S][d] of
-// rhu(g, sc[col].right_shift) (the backward-input prescale with multiplier 1).
+// rhu(g, sc[col].right_shift) (the backward-input prescale with multiplier 1);
+// with them, dq, dk and dv themselves are not written.
 struct GradPlanes {
   const nsrl_fixed_scale* sc = nullptr;
   int8_t* hi = nullptr;

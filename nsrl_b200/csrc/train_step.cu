@@ -252,9 +252,10 @@ cudaError_t add_sat(const int16_t* a, const int16_t* b, size_t n, int16_t* out, 
   return cudaGetLastError();
 }
 
-// dL, then dQ, dK, dV of one attention layer (nsrl-train/src/lib.rs:16623-16900),
-// with `planes` also the prescaled planes of dQ, dK, dV (ld d) for their
-// backward-input linears.
+// dL, then dQ, dK, dV of one attention layer (nsrl-train/src/lib.rs:16623-16900);
+// with `planes`, the prescaled planes of dQ, dK, dV (ld d) for their
+// backward-input linears and weight gradients (the tensor-core kernels then
+// leave the int16 dq, dk, dv unwritten).
 cudaError_t attn_backward(const int16_t* q, const int16_t* k, const int16_t* v, size_t ld, const int16_t* P,
                           const int16_t* dC, size_t ldc, size_t B, size_t S, size_t d, size_t H, int16_t* dL,
                           int16_t* dq, int16_t* dk, int16_t* dv, void* scratch, size_t scratch_bytes,
@@ -320,7 +321,7 @@ struct StepLayout {
   std::vector<LayerCache> lc;
   int16_t* xemb;
   Planes pa, pb;
-  int16_t *G, *Gn, *gg, *gup, *ggate, *gui, *gmi, *gmr, *gao, *gctx, *dq, *dk, *dv, *gq, *gk, *gv, *gni, *gai, *dL;
+  int16_t *G, *Gn, *gg, *gui, *gmi, *gmr, *gao, *gctx, *dq, *dk, *dv, *gq, *gk, *gv, *gni, *gai, *dL;
   int16_t *feat, *logits, *hgrad, *glast;
   Planes fp, hp;
   int8_t* headT;
@@ -370,8 +371,6 @@ void carve_step(const nsrl_train_model* m, size_t W, bool rms, void* base, StepL
                     &o.gq, &o.gk, &o.gv, &o.gni, &o.gai};
   for (int16_t** p : td) *p = c.take<int16_t>(T * d);
   o.gg = c.take<int16_t>(T * F);
-  o.gup = c.take<int16_t>(T * F);
-  o.ggate = c.take<int16_t>(T * F);
   o.dL = c.take<int16_t>(W * H * S * S);
   for (int i = 0; i < 3; ++i) o.pg[i] = c.planes(T, d, false);
   o.feat = c.take<int16_t>(W * d);
@@ -785,7 +784,7 @@ nsrl_status nsrl_train_windows(const nsrl_train_model* m, const uint8_t* context
       const long long n = (long long)T * F;
       ProfScope prof("gated_backward", s, 0.0, 14.0 * (double)n);
       gated_backward_vec_kernel<<<blocks_for(n / 8, 148 * 32), 256, 0, s>>>(
-          o.gg, c.up, c.gate, n / 8, (int)F, ly.lin[4].scales, ly.lin[5].scales, o.gup, o.ggate, paFn.hi, paFn.lo,
+          o.gg, c.up, c.gate, n / 8, (int)F, ly.lin[4].scales, ly.lin[5].scales, nullptr, nullptr, paFn.hi, paFn.lo,
           pbF.hi, pbF.lo);
       TS_TRY(cudaGetLastError(), "gated backward");
     }

@@ -133,8 +133,8 @@ __global__ void gated_backward_vec_kernel(const int16_t* __restrict__ gg, const 
       pu[e] = rhu_i16(ou[e], s1[e]);  // |ou|, |og| <= 2^15
       pg[e] = rhu_i16(og[e], s2[e]);
     }
-    reinterpret_cast<uint4*>(gup)[i] = pack8(ou);
-    reinterpret_cast<uint4*>(ggate)[i] = pack8(og);
+    if (gup) reinterpret_cast<uint4*>(gup)[i] = pack8(ou);
+    if (ggate) reinterpret_cast<uint4*>(ggate)[i] = pack8(og);
     uint2 h, l;
     planes8(pu, h, l);
     reinterpret_cast<uint2*>(uh)[i] = h;
