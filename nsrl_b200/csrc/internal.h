@@ -55,6 +55,7 @@ struct GemmArgs {
   Epi epi;
   int16_t* y;
   size_t ldy;
+  int16_t* y2 = nullptr;  // GATED with y set: y takes the up values and y2 the gate values (int16, ldy)
   Planes yp;
   const int16_t* skip;
   size_t ldskip;

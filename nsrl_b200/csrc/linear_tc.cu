@@ -57,6 +57,7 @@ struct TcParams {
   const nsrl_fixed_scale* scales[3];
   int16_t* y;
   long long ldy;
+  int16_t* y2;  // GATED: with y, the up (y) and gate (y2) values as int16
   int8_t* yh;
   uint8_t* yl;
   unsigned long long* yl1;
@@ -365,6 +366,17 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
         int up[16], gt[16];
         requant16(hu, lu, su, up, p.small_acc);
         requant16(hg, lg, sg, gt, p.small_acc);
+        if (p.y && row_ok && nvalid > 0) {  // the up and gate values themselves (the training step's caches)
+          uint32_t ou[8], og[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            ou[i] = __byte_perm((uint32_t)up[2 * i], (uint32_t)up[2 * i + 1], 0x5410);
+            og[i] = __byte_perm((uint32_t)gt[2 * i], (uint32_t)gt[2 * i + 1], 0x5410);
+          }
+          const bool vok = ((p.ldy | fb) & 7) == 0;
+          store16_i16(p.y + (long long)r * p.ldy + fb, ou, nvalid, vok);
+          store16_i16(p.y2 + (long long)r * p.ldy + fb, og, nvalid, vok);
+        }
         int act[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) act[i] = gated_act_i32(up[i], gt[i]);
@@ -545,6 +557,10 @@ __global__ void gemm_simt_kernel(const SimtParams s) {
     int16_t up = finish1(h, l, p.bias[0], p.scales[0], n);
     simt_dot(s, m, 1, n, h, l);
     int16_t g = finish1(h, l, p.bias[1], p.scales[1], n);
+    if (p.y) {
+      p.y[(long long)m * p.ldy + n] = up;
+      p.y2[(long long)m * p.ldy + n] = g;
+    }
     v = gated_act(up, g);
   } else {
     const int sg = s.nseg == 3 ? n / s.seg_rows : 0;
@@ -813,6 +829,7 @@ cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t stream) {
   }
   p.y = a.y;
   p.ldy = (long long)a.ldy;
+  p.y2 = a.y2;
   p.yh = a.yp.hi;
   p.yl = a.yp.lo;
   p.yl1 = a.yp.l1;

@@ -721,17 +721,27 @@ nsrl_status nsrl_train_windows(const nsrl_train_model* m, const uint8_t* context
       TS_TRY(launch_rms_norm(c.ares, T, d, ly.mlp_gamma, 1, nullptr, c.mn, st, s), "rms");
     else
       TS_TRY(launch_split_planes(c.ares, T, d, d, c.mn, s), "split");
-    TS_TRY(fwd_gemm(c.mn, T, d, &ly.lin[4], Epi::I16, c.up, F, nullptr, nullptr, st, s), "up");
-    TS_TRY(fwd_gemm(c.mn, T, d, &ly.lin[5], Epi::I16, c.gate, F, nullptr, nullptr, st, s), "gate");
     {
-      ProfScope prof("gated_forward", s, 0.0, 8.0 * (double)T * (double)F);
-      if (F % 8 == 0)
-        gated_forward_vec_kernel<<<blocks_for((long long)T * 32, 148 * 16), 256, 0, s>>>(
-            c.up, c.gate, (long long)T, (int)F, nullptr, c.gated.hi, c.gated.lo, c.gated.l1);
-      else
-        gated_forward_kernel<<<blocks_for((long long)T * 32, 148 * 16), 256, 0, s>>>(
-            c.up, c.gate, (long long)T, (int)F, nullptr, c.gated.hi, c.gated.lo, c.gated.l1);
-      TS_TRY(cudaGetLastError(), "gated");
+      // up and gate in one GEMM: the cached up and gate values, the gated
+      // product as planes with its row L1 (mlp.rs:211-254)
+      TS_TRY(cudaMemsetAsync(c.gated.l1, 0, T * sizeof(unsigned long long), s), "memset");
+      GemmArgs g{};
+      g.a_hi = c.mn.hi;
+      g.a_lo = c.mn.lo;
+      g.a_l1 = c.mn.l1;
+      g.lda = d;
+      g.M = T;
+      g.K = d;
+      g.nseg = 2;
+      g.seg[0] = WeightSeg{ly.lin[4].weights, ly.lin[4].bias, ly.lin[4].scales, F};
+      g.seg[1] = WeightSeg{ly.lin[5].weights, ly.lin[5].bias, ly.lin[5].scales, F};
+      g.epi = Epi::GATED;
+      g.y = c.up;
+      g.y2 = c.gate;
+      g.ldy = F;
+      g.yp = c.gated;
+      g.st = st;
+      TS_TRY(launch_gemm(g, s), "up/gate");
     }
     TS_TRY(fwd_gemm(c.gated, T, F, &ly.lin[6], Epi::RESID, c.out, d, c.ares, o.fwd_res, st, s), "down");
   }

@@ -220,57 +220,6 @@ __global__ void fanin3_vec_kernel(const int16_t* __restrict__ a, const int16_t* 
   if ((threadIdx.x & 31) == 0 && cnt) atomicAdd(sat, cnt);
 }
 
-// mlp.rs:150-170 forward gating on cached up / gate rows -> gated int16 and
-// byte planes with the row L1 (one warp per row).
-__global__ void gated_forward_kernel(const int16_t* __restrict__ up, const int16_t* __restrict__ gate, long long rows,
-                                     int F, int16_t* __restrict__ gated, int8_t* __restrict__ hi,
-                                     uint8_t* __restrict__ lo, unsigned long long* __restrict__ l1) {
-  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
-  for (long long r = (long long)blockIdx.x * warps + (threadIdx.x >> 5); r < rows; r += (long long)gridDim.x * warps) {
-    unsigned long long s = 0;
-    for (int f = lane; f < F; f += 32) {
-      const long long i = r * F + f;
-      const int v = gated_act(up[i], gate[i]);
-      if (gated) gated[i] = (int16_t)v;
-      hi[i] = (int8_t)(v >> 8);
-      lo[i] = (uint8_t)(v & 255);
-      s += (unsigned long long)abs(v);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    if (lane == 0) l1[r] = s;
-  }
-}
-
-// gated_forward_kernel on eight consecutive hidden units per lane (F % 8 == 0).
-__global__ void gated_forward_vec_kernel(const int16_t* __restrict__ up, const int16_t* __restrict__ gate,
-                                         long long rows, int F, int16_t* __restrict__ gated, int8_t* __restrict__ hi,
-                                         uint8_t* __restrict__ lo, unsigned long long* __restrict__ l1) {
-  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
-  for (long long r = (long long)blockIdx.x * warps + (threadIdx.x >> 5); r < rows; r += (long long)gridDim.x * warps) {
-    unsigned long long s = 0;
-    for (int f = 8 * lane; f < F; f += 256) {
-      const long long i8 = (r * F + f) >> 3;
-      int u[8], g[8], v[8];
-      unpack8(reinterpret_cast<const uint4*>(up)[i8], u);
-      unpack8(reinterpret_cast<const uint4*>(gate)[i8], g);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        v[e] = gated_act(u[e], g[e]);
-        s += (unsigned long long)abs(v[e]);
-      }
-      if (gated) reinterpret_cast<uint4*>(gated)[i8] = pack8(v);
-      uint2 h, l;
-      planes8(v, h, l);
-      reinterpret_cast<uint2*>(hi)[i8] = h;
-      reinterpret_cast<uint2*>(lo)[i8] = l;
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    if (lane == 0) l1[r] = s;
-  }
-}
-
 // out = sat(a + b) with the saturation count (numeric.rs:25-45,
 // nsrl-train/src/lib.rs:17490-17506).
 __global__ void add_sat_kernel(const int16_t* __restrict__ a, const int16_t* __restrict__ b, long long n,
