@@ -894,12 +894,22 @@ cudaError_t launch_attention_backward_tc(const int16_t* q, const int16_t* k, con
   uint8_t* ltl = take(B * H * S * S);
   cudaError_t e = cudaSuccess;
   const double pairs = (double)B * (double)H * (double)S * (double)(S + 1) / 2.0;
+  // Key side on the tcgen05 kernel: P, dL as causal row-major planes and Q, dC
+  // as row-major planes (no transposes; the Q^T / dC^T / P^T / dL^T buffers
+  // hold these instead).
+  const bool kv_tc = attention_kv_tc_supported(S, d, H) && S % 8 == 0;
   {
     ProfScope prof("attention_bwd_planes", s, 0.0, 8.0 * (double)B * S * d + 2.0 * 2.0 * (double)B * H * S * S);
     e = launch_split_planes(v, B * S, d, ld, Planes{vph, vpl, nullptr, d}, s);
     if (e != cudaSuccess) return e;
     dim3 tg((unsigned)((S + 63) / 64), (unsigned)H, (unsigned)B);
-    if (hd == 64 && S % 16 == 0 && ld % 8 == 0 && ldc % 8 == 0) {
+    if (kv_tc) {
+      head_transpose16_kernel<<<tg, 128, 0, s>>>(k, (long long)ld, (int)S, (int)Sp, (int)H, true, kth, ktl);
+      e = launch_split_planes(q, B * S, d, ld, Planes{qth, qtl, nullptr, d}, s);
+      if (e == cudaSuccess) e = launch_split_planes(dC, B * S, d, ldc, Planes{cth, ctl, nullptr, d}, s);
+      if (e == cudaSuccess) e = launch_split_causal(P, B * H, S, pth, ptl, s);
+      if (e != cudaSuccess) return e;
+    } else if (hd == 64 && S % 16 == 0 && ld % 8 == 0 && ldc % 8 == 0) {
       head_transpose16_kernel<<<tg, 128, 0, s>>>(k, (long long)ld, (int)S, (int)Sp, (int)H, true, kth, ktl);
       head_transpose16_kernel<<<tg, 128, 0, s>>>(q, (long long)ld, (int)S, (int)S, (int)H, false, qth, qtl);
       head_transpose16_kernel<<<tg, 128, 0, s>>>(dC, (long long)ldc, (int)S, (int)S, (int)H, false, cth, ctl);
@@ -912,8 +922,10 @@ cudaError_t launch_attention_backward_tc(const int16_t* q, const int16_t* k, con
       head_transpose_kernel<16><<<tg, 256, 0, s>>>(q, (long long)ld, (int)S, (int)S, (int)H, false, qth, qtl);
       head_transpose_kernel<16><<<tg, 256, 0, s>>>(dC, (long long)ldc, (int)S, (int)S, (int)H, false, cth, ctl);
     }
-    e = launch_sq_transpose(P, B * H, S, pth, ptl, s);
-    if (e != cudaSuccess) return e;
+    if (!kv_tc) {
+      e = launch_sq_transpose(P, B * H, S, pth, ptl, s);
+      if (e != cudaSuccess) return e;
+    }
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
@@ -941,6 +953,14 @@ cudaError_t launch_attention_backward_tc(const int16_t* q, const int16_t* k, con
       attn_bwd_dq_kernel<16><<<grid, 128, 0, s>>>(qa);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
+  }
+  if (kv_tc) {
+    e = launch_split_causal(dl, B * H, S, lth, ltl, s);
+    if (e != cudaSuccess) return e;
+    return launch_attention_kv_tc(Planes{lth, ltl, nullptr, S}, Planes{pth, ptl, nullptr, S},
+                                  Planes{qth, qtl, nullptr, d}, Planes{cth, ctl, nullptr, d}, B, S, d, H,
+                                  planes ? nullptr : dk, planes ? nullptr : dv, planes ? planes[1] : GradPlanes{},
+                                  planes ? planes[2] : GradPlanes{}, st, s);
   }
   {
     ProfScope prof("attention_bwd_planes", s, 0.0, 4.0 * (double)B * H * S * S);

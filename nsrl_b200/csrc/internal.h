@@ -148,6 +148,17 @@ cudaError_t launch_attention_backward_tc(const int16_t* q, const int16_t* k, con
                                          void* scratch, size_t scratch_bytes, nsrl_device_status* st,
                                          cudaStream_t s, const GradPlanes* planes = nullptr);
 
+// Key side of the attention backward on the tensor cores (head_dim 64):
+// dK = dL^T Q and dV = P^T dC per (sequence, head) from row-major byte planes
+// read in place: l, p = [B*H][S][S] with entries above the diagonal zero (as
+// launch_split_causal writes them), qp, cp = [B][S][d] (row stride ld).
+// Outputs int16 [B*S][d] (NULL to skip) and/or prescaled planes.
+bool attention_kv_tc_supported(size_t S, size_t d, size_t H);
+cudaError_t launch_split_causal(const int16_t* M, size_t BH, size_t S, int8_t* hi, uint8_t* lo, cudaStream_t s);
+cudaError_t launch_attention_kv_tc(const Planes& l, const Planes& p, const Planes& qp, const Planes& cp, size_t B,
+                                   size_t S, size_t d, size_t H, int16_t* dk, int16_t* dv, const GradPlanes& gk,
+                                   const GradPlanes& gv, nsrl_device_status* st, cudaStream_t s);
+
 // Planes -> int16.
 cudaError_t launch_join_planes(Planes in, size_t rows, size_t cols, int16_t* y, size_t ldy, cudaStream_t stream);
 

@@ -147,6 +147,7 @@ def test_train_step_reference_initial_model():
     (64, 4, 128, 2, 16, 3, True, True),
     (64, 1, 128, 1, 24, 2, False, False),
     (128, 2, 256, 2, 40, 2, True, False),
+    (128, 2, 256, 2, 144, 2, True, True),   # head_dim 64, S % 16 == 0: the tensor-core key side, a ragged key tile
 ])
 def test_train_step_random_models(d, H, F, L, S, W, rms, pos):
     m = random_model(d, H, F, L, S, rms=rms, positions=pos, seed=d + S)
