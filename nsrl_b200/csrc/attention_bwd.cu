@@ -261,6 +261,11 @@ struct DlArgs {
   int S, H;
   int16_t* dL;  // [BH][S][S]: dP after the first pass, dL after the second
   nsrl_device_status* st;
+  // planes form (PL): P read from, and dP / dL written to, [BH][S][S] byte planes
+  const int8_t* p_hi;
+  const uint8_t* p_lo;
+  int8_t* l_hi;
+  uint8_t* l_lo;
 };
 
 // attn_bwd_dl_kernel: one CTA of 4 warps per 64 query rows.  Pass 1 forms dP
@@ -270,13 +275,24 @@ struct DlArgs {
 // (its own writes, so no barrier) and turns them into dL in place.  Every key
 // below min(S, end of the block) is written, zeros above the diagonal, so the
 // causal 64 x 64 tiles the key side reads need no clearing.
-template <int HD>
+//
+// PL (S % 16 == 0): P comes from byte planes and dP / dL go to byte planes.
+// Lane l of a warp owns the 16-key piece (row qw + l / 2, keys 16 (l % 2) ..
+// +15) of each 32-key tile: pass 1 moves P in and dP out as 16-byte plane
+// pieces through a per-warp shared tile (the MMA fragments hold 2-key pairs),
+// pass 2 works on its own pieces.  The first 64-row block of each 128-row
+// block also writes zero planes for keys [q0 + 64, q0 + 128), so every
+// 128 x 128 causal tile the tensor-core kernels read is written.
+constexpr int PSTR = 20;  // words per row of a warp's staged 16 x 32 pair tile (conflict-free fragment access)
+
+template <int HD, bool PL>
 __global__ void __launch_bounds__(128, 5) attn_bwd_dl_kernel(const DlArgs a) {
   constexpr int KC = HD >= 32 ? HD / 32 : 1;
   constexpr int KSTR = HD == 16 ? 48 : HD + 16;  // bytes per staged V row
   constexpr int VW = BK * (HD / 16);            // 16-byte words of one V plane tile
   constexpr int PER = (2 * VW + 127) / 128;
   __shared__ __align__(16) uint8_t vbuf[2][2][BK * KSTR];  // [stage][plane]
+  __shared__ __align__(16) uint32_t pstage[PL ? 4 : 1][PL ? 16 * PSTR : 4];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t = lane & 3;
   const int q0 = blockIdx.x * BQ, h = blockIdx.y, b = blockIdx.z;
@@ -284,8 +300,52 @@ __global__ void __launch_bounds__(128, 5) attn_bwd_dl_kernel(const DlArgs a) {
   const long long row0 = (long long)b * S;
   const int qw = q0 + warp * 16;
   const int r0 = qw + g, r1 = r0 + 8;
-  const int16_t* Pbh = a.P + ((long long)b * a.H + h) * S * (long long)S;
-  int16_t* dLbh = a.dL + ((long long)b * a.H + h) * S * (long long)S;
+  const long long mat = ((long long)b * a.H + h) * S * (long long)S;
+  const int16_t* Pbh = PL ? nullptr : a.P + mat;
+  int16_t* dLbh = PL ? nullptr : a.dL + mat;
+  // PL: this lane's piece and the warp's staged tile of key pairs
+  const int pr = qw + (lane >> 1), ph = 16 * (lane & 1);
+  uint32_t* ps = pstage[PL ? warp : 0];
+  uint32_t* pmine = ps + (lane >> 1) * PSTR + 8 * (lane & 1);
+  // the piece of tile kb of a plane pair as 8 packed pairs (zeros outside the matrix)
+  auto piece_ld = [&](const int8_t* hi, const uint8_t* lo, int kb, uint32_t(&wv)[8]) {
+    uint4 H = make_uint4(0, 0, 0, 0), L = H;
+    if (pr < S && kb + ph < S) {
+      const long long o = mat + (long long)pr * S + kb + ph;
+      H = *reinterpret_cast<const uint4*>(hi + o);
+      L = *reinterpret_cast<const uint4*>(lo + o);
+    }
+    const uint32_t hw[4] = {H.x, H.y, H.z, H.w}, lw[4] = {L.x, L.y, L.z, L.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      wv[2 * k] = __byte_perm(lw[k], hw[k], 0x5140);
+      wv[2 * k + 1] = __byte_perm(lw[k], hw[k], 0x7362);
+    }
+  };
+  auto piece_st = [&](int kb, const uint32_t(&wv)[8]) {
+    if (pr >= S || kb + ph >= S) return;
+    uint32_t hw[4], lw[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      hw[k] = __byte_perm(wv[2 * k], wv[2 * k + 1], 0x7531);
+      lw[k] = __byte_perm(wv[2 * k], wv[2 * k + 1], 0x6420);
+    }
+    const long long o = mat + (long long)pr * S + kb + ph;
+    *reinterpret_cast<uint4*>(a.l_hi + o) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    *reinterpret_cast<uint4*>(a.l_lo + o) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+  };
+  if (PL && q0 % 128 == 0 && q0 + BQ < S) {
+    // zero planes of rows [q0, q0 + 64) x keys [q0 + 64, min(S, q0 + 128))
+    const int kz = q0 + BQ, nz = (min(S, q0 + 128) - kz) / 16;
+    for (int i = tid; i < 2 * BQ * nz; i += 128) {
+      const int pl = i / (BQ * nz), w = i % (BQ * nz);
+      const int r = q0 + w / nz, key = kz + 16 * (w % nz);
+      if (r >= S) continue;
+      const long long o = mat + (long long)r * S + key;
+      uint4* dst = pl ? reinterpret_cast<uint4*>(a.l_lo + o) : reinterpret_cast<uint4*>(a.l_hi + o);
+      *dst = make_uint4(0, 0, 0, 0);
+    }
+  }
 
   // A fragments of dC rows r0 / r1 (k = dims)
   uint32_t ca_hi[KC][4], ca_lo[KC][4];
@@ -315,7 +375,7 @@ __global__ void __launch_bounds__(128, 5) attn_bwd_dl_kernel(const DlArgs a) {
   const int wlast = min(qw + 15, S - 1);
 
   // word e: plane e / VW, key row (e % VW) / (HD / 16), 16-byte column
-  auto load_tile = [&](int kb, uint4 (&r)[PER]) {
+  auto load_tile = [&](int kb, uint4(&r)[PER]) {
 #pragma unroll
     for (int z = 0; z < PER; ++z) {
       const int e = tid + z * 128;
@@ -331,7 +391,7 @@ __global__ void __launch_bounds__(128, 5) attn_bwd_dl_kernel(const DlArgs a) {
       r[z] = v;
     }
   };
-  auto store_tile = [&](int sb, const uint4 (&r)[PER]) {
+  auto store_tile = [&](int sb, const uint4(&r)[PER]) {
 #pragma unroll
     for (int z = 0; z < PER; ++z) {
       const int e = tid + z * 128;
@@ -356,13 +416,26 @@ __global__ void __launch_bounds__(128, 5) attn_bwd_dl_kernel(const DlArgs a) {
     if (more) load_tile(kb + BK, pre);  // in flight during the MMAs below
     // the probabilities of this tile: rows r0 / r1, key pairs kb + 8 j + 2 t
     uint32_t pw[2][4];
+    if constexpr (PL) {
+      uint32_t wv[8];
+      piece_ld(a.p_hi, a.p_lo, kb, wv);
+      reinterpret_cast<uint4*>(pmine)[0] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+      reinterpret_cast<uint4*>(pmine)[1] = make_uint4(wv[4], wv[5], wv[6], wv[7]);
+      __syncwarp();
 #pragma unroll
-    for (int hf = 0; hf < 2; ++hf)
+      for (int hf = 0; hf < 2; ++hf)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int r = hf ? r1 : r0, key = kb + 8 * j + 2 * t;
-        pw[hf][j] = (r < S && key < S) ? *reinterpret_cast<const uint32_t*>(Pbh + (long long)r * S + key) : 0u;
-      }
+        for (int j = 0; j < 4; ++j) pw[hf][j] = ps[(g + 8 * hf) * PSTR + 4 * j + t];
+      __syncwarp();  // read before the dP pairs overwrite the tile
+    } else {
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int r = hf ? r1 : r0, key = kb + 8 * j + 2 * t;
+          pw[hf][j] = (r < S && key < S) ? *reinterpret_cast<const uint32_t*>(Pbh + (long long)r * S + key) : 0u;
+        }
+    }
     const bool active = qw < S && kb <= wlast;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {  // 8 keys at a time: dP raw sums for 16 rows x 8 keys, then their values
@@ -401,8 +474,19 @@ __global__ void __launch_bounds__(128, 5) attn_bwd_dl_kernel(const DlArgs a) {
             wsum[hf] += (long long)(dp[e] * p);  // |dP P| <= 2^30
           }
         }
-        *reinterpret_cast<uint32_t*>(dLbh + (long long)r * S + key) = (uint32_t)(dp[0] & 0xFFFF) | ((uint32_t)dp[1] << 16);
+        const uint32_t pk = (uint32_t)(dp[0] & 0xFFFF) | ((uint32_t)dp[1] << 16);
+        if constexpr (PL)
+          ps[(g + 8 * hf) * PSTR + 4 * j + t] = pk;
+        else
+          *reinterpret_cast<uint32_t*>(dLbh + (long long)r * S + key) = pk;
       }
+    }
+    if constexpr (PL) {  // the dP pieces out as planes (pieces outside the matrix are skipped)
+      __syncwarp();
+      const uint4 u0 = reinterpret_cast<const uint4*>(pmine)[0], u1 = reinterpret_cast<const uint4*>(pmine)[1];
+      const uint32_t wv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+      piece_st(kb, wv);
+      __syncwarp();  // the next tile's P overwrites the staged tile
     }
     if (more) store_tile(sb ^ 1, pre);
     __syncthreads();
@@ -417,6 +501,33 @@ __global__ void __launch_bounds__(128, 5) attn_bwd_dl_kernel(const DlArgs a) {
   if (neg) nsrl_flag(a.st, NSRL_FLAG_LINEAR_OVERFLOW);  // a negative probability: the reference rejects
   // pass 2: dL = sat(rhu(P (dP - wq) 22713, 30)) over the values this lane stored
   if (qw >= S) return;
+  if constexpr (PL) {
+    // wq of this lane's piece row (qw + l / 2) from the quad that reduced it
+    const int rr = lane >> 1;
+    const int w0 = __shfl_sync(0xffffffffu, wq[0], 4 * (rr & 7)), w1 = __shfl_sync(0xffffffffu, wq[1], 4 * (rr & 7));
+    const int myw = rr >= 8 ? w1 : w0;
+    for (int kt = 0; kt < ntiles; ++kt) {
+      const int kb = kt * BK;
+      if (pr >= S || kb + ph >= S || kb + ph > pr) continue;  // outside, or above the diagonal (zeros already)
+      uint32_t pv[8], dv[8], ov[8];
+      piece_ld(a.p_hi, a.p_lo, kb, pv);
+      piece_ld(a.l_hi, a.l_lo, kb, dv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        int dl[2];
+#pragma unroll
+        for (int z = 0; z < 2; ++z) {
+          const int p = (int)(int16_t)(pv[e] >> (16 * z));
+          const int dp = (int)(int16_t)(dv[e] >> (16 * z));
+          const long long prod = (long long)(p * 22713) * (long long)(dp - myw);
+          dl[z] = kb + ph + 2 * e + z <= pr ? sat16((int)((prod + (1ll << 29)) >> 30)) : 0;
+        }
+        ov[e] = (uint32_t)(dl[0] & 0xFFFF) | ((uint32_t)dl[1] << 16);
+      }
+      piece_st(kb, ov);
+    }
+    return;
+  }
   for (int kt = 0; kt < ntiles; ++kt) {
     const int kb = kt * BK;
     uint32_t pw[2][4], dw[2][4];
@@ -865,7 +976,7 @@ cudaError_t launch_attention_backward_tc(const int16_t* q, const int16_t* k, con
                                          const int16_t* P, const int16_t* dC, size_t ldc, size_t B, size_t S, size_t d,
                                          size_t H, int16_t* dl, int16_t* dq, int16_t* dk, int16_t* dv,
                                          void* scratch, size_t scratch_bytes, nsrl_device_status* st,
-                                         cudaStream_t s, const GradPlanes* planes) {
+                                         cudaStream_t s, const GradPlanes* planes, const Planes* p_planes) {
   const size_t hd = d / H;
   // 8-byte loads of P / dL rows, dC, q, k, v need S, ld, ldc multiples of 4
   if ((hd != 16 && hd != 64) || S % 4 != 0 || ld % 4 != 0 || ldc % 4 != 0 || d % 16 != 0 || S > 16384 ||
@@ -894,22 +1005,46 @@ cudaError_t launch_attention_backward_tc(const int16_t* q, const int16_t* k, con
   uint8_t* ltl = take(B * H * S * S);
   cudaError_t e = cudaSuccess;
   const double pairs = (double)B * (double)H * (double)S * (double)(S + 1) / 2.0;
-  // Key side on the tcgen05 kernel: P, dL as causal row-major planes and Q, dC
-  // as row-major planes (no transposes; the Q^T / dC^T / P^T / dL^T buffers
-  // hold these instead).
-  const bool kv_tc = attention_kv_tc_supported(S, d, H) && S % 8 == 0;
+  if (attention_kv_tc_supported(S, d, H)) {
+    // Tensor-core path (head_dim 64, S % 16 == 0): V, K, Q, dC as row-major
+    // planes [B*S][d], P (unless given as planes) and dL as causal planes
+    // [B*H][S][S]; the dL kernel reads and writes planes, one persistent
+    // tcgen05 kernel forms dK, dV and dQ.  The K^T / Q^T / dC^T / P^T / dL^T
+    // scratch buffers hold these instead; the int16 dl is not written.
+    {
+      ProfScope prof("attention_bwd_planes", s, 0.0, 16.0 * (double)B * S * d);
+      e = launch_split_planes(v, B * S, d, ld, Planes{vph, vpl, nullptr, d}, s);
+      if (e == cudaSuccess) e = launch_split_planes(k, B * S, d, ld, Planes{kth, ktl, nullptr, d}, s);
+      if (e == cudaSuccess) e = launch_split_planes(q, B * S, d, ld, Planes{qth, qtl, nullptr, d}, s);
+      if (e == cudaSuccess) e = launch_split_planes(dC, B * S, d, ldc, Planes{cth, ctl, nullptr, d}, s);
+      if (e != cudaSuccess) return e;
+    }
+    const Planes pp = p_planes ? *p_planes : Planes{pth, ptl, nullptr, S};
+    if (!p_planes) {
+      e = launch_split_causal(P, B * H, S, pth, ptl, s);
+      if (e != cudaSuccess) return e;
+    }
+    {
+      DlArgs la{dC, (long long)ldc, vph, vpl, (int)d, nullptr, (int)S, (int)H, nullptr, st, pp.hi, pp.lo, lth, ltl};
+      ProfScope prof("attention_bwd_dl", s, 2.0 * (double)hd * pairs,
+                     2.0 * 2.0 * (double)B * H * S * S + 4.0 * (double)B * S * d);
+      attn_bwd_dl_kernel<64, true><<<dim3((unsigned)((S + BQ - 1) / BQ), (unsigned)H, (unsigned)B), 128, 0, s>>>(la);
+      e = cudaGetLastError();
+      if (e != cudaSuccess) return e;
+    }
+    const Planes kp{kth, ktl, nullptr, d};
+    return launch_attention_kv_tc(Planes{lth, ltl, nullptr, S}, pp, Planes{qth, qtl, nullptr, d},
+                                  Planes{cth, ctl, nullptr, d}, B, S, d, H, planes ? nullptr : dk,
+                                  planes ? nullptr : dv, planes ? planes[1] : GradPlanes{},
+                                  planes ? planes[2] : GradPlanes{}, st, s, &kp, planes ? nullptr : dq,
+                                  planes ? planes[0] : GradPlanes{});
+  }
   {
     ProfScope prof("attention_bwd_planes", s, 0.0, 8.0 * (double)B * S * d + 2.0 * 2.0 * (double)B * H * S * S);
     e = launch_split_planes(v, B * S, d, ld, Planes{vph, vpl, nullptr, d}, s);
     if (e != cudaSuccess) return e;
     dim3 tg((unsigned)((S + 63) / 64), (unsigned)H, (unsigned)B);
-    if (kv_tc) {
-      head_transpose16_kernel<<<tg, 128, 0, s>>>(k, (long long)ld, (int)S, (int)Sp, (int)H, true, kth, ktl);
-      e = launch_split_planes(q, B * S, d, ld, Planes{qth, qtl, nullptr, d}, s);
-      if (e == cudaSuccess) e = launch_split_planes(dC, B * S, d, ldc, Planes{cth, ctl, nullptr, d}, s);
-      if (e == cudaSuccess) e = launch_split_causal(P, B * H, S, pth, ptl, s);
-      if (e != cudaSuccess) return e;
-    } else if (hd == 64 && S % 16 == 0 && ld % 8 == 0 && ldc % 8 == 0) {
+    if (hd == 64 && S % 16 == 0 && ld % 8 == 0 && ldc % 8 == 0) {
       head_transpose16_kernel<<<tg, 128, 0, s>>>(k, (long long)ld, (int)S, (int)Sp, (int)H, true, kth, ktl);
       head_transpose16_kernel<<<tg, 128, 0, s>>>(q, (long long)ld, (int)S, (int)S, (int)H, false, qth, qtl);
       head_transpose16_kernel<<<tg, 128, 0, s>>>(dC, (long long)ldc, (int)S, (int)S, (int)H, false, cth, ctl);
@@ -922,22 +1057,20 @@ cudaError_t launch_attention_backward_tc(const int16_t* q, const int16_t* k, con
       head_transpose_kernel<16><<<tg, 256, 0, s>>>(q, (long long)ld, (int)S, (int)S, (int)H, false, qth, qtl);
       head_transpose_kernel<16><<<tg, 256, 0, s>>>(dC, (long long)ldc, (int)S, (int)S, (int)H, false, cth, ctl);
     }
-    if (!kv_tc) {
-      e = launch_sq_transpose(P, B * H, S, pth, ptl, s);
-      if (e != cudaSuccess) return e;
-    }
+    e = launch_sq_transpose(P, B * H, S, pth, ptl, s);
+    if (e != cudaSuccess) return e;
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
   dim3 grid((unsigned)((S + BQ - 1) / BQ), (unsigned)H, (unsigned)B);
   {
-    DlArgs la{dC, (long long)ldc, vph, vpl, (int)d, P, (int)S, (int)H, dl, st};
+    DlArgs la{dC, (long long)ldc, vph, vpl, (int)d, P, (int)S, (int)H, dl, st, nullptr, nullptr, nullptr, nullptr};
     ProfScope prof("attention_bwd_dl", s, 2.0 * (double)hd * pairs,
                    2.0 * 2.0 * (double)B * H * S * S + 4.0 * (double)B * S * d);
     if (hd == 64)
-      attn_bwd_dl_kernel<64><<<grid, 128, 0, s>>>(la);
+      attn_bwd_dl_kernel<64, false><<<grid, 128, 0, s>>>(la);
     else
-      attn_bwd_dl_kernel<16><<<grid, 128, 0, s>>>(la);
+      attn_bwd_dl_kernel<16, false><<<grid, 128, 0, s>>>(la);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
@@ -953,14 +1086,6 @@ cudaError_t launch_attention_backward_tc(const int16_t* q, const int16_t* k, con
       attn_bwd_dq_kernel<16><<<grid, 128, 0, s>>>(qa);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-  }
-  if (kv_tc) {
-    e = launch_split_causal(dl, B * H, S, lth, ltl, s);
-    if (e != cudaSuccess) return e;
-    return launch_attention_kv_tc(Planes{lth, ltl, nullptr, S}, Planes{pth, ptl, nullptr, S},
-                                  Planes{qth, qtl, nullptr, d}, Planes{cth, ctl, nullptr, d}, B, S, d, H,
-                                  planes ? nullptr : dk, planes ? nullptr : dv, planes ? planes[1] : GradPlanes{},
-                                  planes ? planes[2] : GradPlanes{}, st, s);
   }
   {
     ProfScope prof("attention_bwd_planes", s, 0.0, 4.0 * (double)B * H * S * S);

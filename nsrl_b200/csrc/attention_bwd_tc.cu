@@ -1,24 +1,28 @@
-// Key side of the softmax-attention backward on the B200 tensor cores
-// (tcgen05, kind::i8), head_dim 64, crates/nsrl-train/src/lib.rs:16623-16900:
+// Key and query sides of the softmax-attention backward on the B200 tensor
+// cores (tcgen05, kind::i8), head_dim 64, crates/nsrl-train/src/lib.rs:16623-16900:
 //   dK[j] = sat(rhu(sum_{t >= j} dL[t][j] Q[t], log4 hd))
 //   dV[j] = sat(rhu(sum_{t >= j} P[t][j] dC[t], 15))
-// per (sequence, head).  Both are (S x S)^T (S x 64) products whose operands
-// are read in place, MN-major, from row-major byte planes: dL and P as
-// [B*H][S][S] (keys contiguous; entries above the diagonal zero), Q and dC as
-// [B][S][d] (dims contiguous).  Nothing is transposed.
+//   dQ[t] = sat(rhu(sum_{j <= t} dL[t][j] K[j], log4 hd))
+// per (sequence, head).  dK and dV are (S x S)^T (S x 64) products, dQ an
+// (S x S) (S x 64) product; every operand is read in place from row-major
+// byte planes: dL and P as [B*H][S][S] (keys contiguous; entries above the
+// diagonal zero up to the end of each row's 128-key block), Q, K and dC as
+// [B][S][d] (dims contiguous).  dL^T and P^T are MN-major A operands, dL a
+// K-major one; Q, K and dC are MN-major B operands.  Nothing is transposed.
 //
 // Every product is i16 x i16 = (256 ah + al)(256 bh + bl): four int8 MMAs into
 // three s32 TMEM accumulators (hh, mid = ah bl + al bh, ll); per term
-// |mid| <= 65280 and ll <= 65025, so the sums are exact for up to 32768 queries
+// |mid| <= 65280 and ll <= 65025, so the sums are exact for up to 32768 terms
 // (seq_len <= 16384).  The epilogue recombines them in i64 and applies the
 // reference's rounded shift and saturation.
 //
 // Persistent kernel, one CTA per SM; a work item is dK or dV of one 128-key
-// tile of one (sequence, head), items with the most queries first.  10 warps:
-// warp 0 issues TMA (a 6-stage ring of 32-query steps: the dL or P tile,
-// 32 x 128 bytes per plane, and the Q or dC tile, 32 x 64 bytes per plane),
-// warp 1 owns TMEM (two accumulator sets of 3 x 64 columns) and issues the
-// MMAs, warps 2..9 run the epilogue of one item while the next accumulates.
+// tile, or dQ of one 128-query tile, of one (sequence, head); items with the
+// most 32-wide steps first.  10 warps: warp 0 issues TMA (a 6-stage ring of
+// steps: a dL or P tile of 32 x 128 or 128 x 32 bytes per plane and a Q, K or
+// dC tile of 32 x 64 bytes per plane), warp 1 owns TMEM (two accumulator sets
+// of 3 x 64 columns) and issues the MMAs, warps 2..9 run the epilogue of one
+// item while the next accumulates.
 #include <algorithm>
 
 #include "common.cuh"
@@ -31,8 +35,8 @@ constexpr int KQ = 32;    // queries per MMA K step
 constexpr int KK = 128;   // keys per work item (MMA M)
 constexpr int KD = 64;    // head dim (MMA N)
 constexpr int KST = 6;    // stages
-constexpr int TM = KQ * KK;  // 4 KB: one plane of a dL or P step, [32 queries][128 keys]
-constexpr int TX = KQ * KD;  // 2 KB: one plane of a Q or dC step, [32 queries][64 dims]
+constexpr int TM = KQ * KK;  // 4 KB: one plane of a dL or P step, [32 queries][128 keys] or [128 queries][32 keys]
+constexpr int TX = KQ * KD;  // 2 KB: one plane of a Q, K or dC step, [32 rows][64 dims]
 constexpr int OFF_AH = 0, OFF_AL = TM, OFF_BH = 2 * TM, OFF_BL = 2 * TM + TX;
 constexpr int KSTAGE = 2 * TM + 2 * TX;  // 12 KB
 constexpr int KEPI = 8;                  // epilogue warps: two per TMEM lane quarter
@@ -43,31 +47,51 @@ constexpr size_t KSMEM = (size_t)KST * KSTAGE + 1024 + 256;
 
 struct KvMaps {
   CUtensorMap l_hi, l_lo, p_hi, p_lo, q_hi, q_lo, c_hi, c_lo;
+  CUtensorMap lr_hi, lr_lo, k_hi, k_lo;  // dL row tiles (K-major, 128 x 32) and K, for dQ
 };
 
 struct KvArgs {
   int S, H, d, k_shift;
-  int B, nk, items;
+  int B, nk, kinds, items;
   int16_t* dk;  // int16 outputs [B*S][d] (row stride d), or NULL
   int16_t* dv;
-  GradPlanes gk, gv;  // optional prescaled planes of dK, dV ([B*S][d])
+  int16_t* dq;
+  GradPlanes gk, gv, gq;  // optional prescaled planes of dK, dV, dQ ([B*S][d])
   nsrl_device_status* st;
 };
 
-// A work item is dK (kind 0) or dV (kind 1) of one 128-key tile of one
-// (sequence, head); the key tile varies slowest, first tile (most queries) first.
+// A work item is dK (kind 0) or dV (kind 1) of the 128-key tile at k0, or dQ
+// (kind 2) of the 128-query tile at k0, of one (sequence, head).  Level L
+// holds the key tile 128 L and the query tile 128 (nk - 1 - L): both take
+// about (S - 128 L) / 32 steps, and the levels run longest first.
 struct KvItem {
   int kind, h, b, k0;
+  int x0, x1;  // the steps' queries (dK, dV) or keys (dQ): [x0, x1) by 32
 };
 __device__ __forceinline__ KvItem kv_item(const KvArgs& a, int i) {
-  const int per = 2 * a.B * a.H;
+  const int per = a.kinds * a.B * a.H;
+  const int level = i / per, r = i % per;
   KvItem it;
-  it.k0 = (i / per) * KK;
-  const int r = i % per;
-  it.kind = r & 1;
-  it.h = (r >> 1) % a.H;
-  it.b = (r >> 1) / a.H;
+  it.kind = r % a.kinds;
+  it.h = (r / a.kinds) % a.H;
+  it.b = (r / a.kinds) / a.H;
+  if (it.kind < 2) {
+    it.k0 = level * KK;
+    it.x0 = it.k0;  // queries t >= k0 (entries with t < j are zero)
+    it.x1 = a.S;
+  } else {
+    it.k0 = (a.nk - 1 - level) * KK;
+    it.x0 = 0;  // keys j < the end of the query tile (entries with j > t are zero)
+    it.x1 = min(a.S, it.k0 + KK);
+  }
   return it;
+}
+
+// K-major tile of 32-byte rows (32 keys of one query), 32-byte swizzle:
+// 8-row groups 256 bytes apart.
+__device__ __forceinline__ uint64_t sdesc_k32(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(256 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)6 << 61);
 }
 
 // MN-major operand tiles: rows of 128 (keys) or 64 (dims) bytes, one per
@@ -79,6 +103,9 @@ __device__ __forceinline__ uint64_t sdesc_mn(uint32_t saddr, uint32_t sbo, uint3
 constexpr uint32_t LAYOUT_SW128 = 2, LAYOUT_SW64 = 4;
 constexpr uint32_t idesc_mn(uint32_t a_signed, uint32_t b_signed) {
   return idesc_i8(KK, KD, a_signed, b_signed) | (1u << 15) | (1u << 16);
+}
+constexpr uint32_t idesc_kmn(uint32_t a_signed, uint32_t b_signed) {  // K-major A, MN-major B
+  return idesc_i8(KK, KD, a_signed, b_signed) | (1u << 16);
 }
 
 // Byte planes of 16 values of one output row, prescaled by rhu(v, shift_col).
@@ -145,22 +172,24 @@ __global__ void __launch_bounds__(KTHREADS, 1) attn_kv_tc_kernel(const __grid_co
       for (int item = blockIdx.x; item < a.items && ok; item += gridDim.x) {
         const KvItem w = kv_item(a, item);
         const int bh = w.b * a.H + w.h;
-        const CUtensorMap* ma_hi = w.kind ? &maps.p_hi : &maps.l_hi;
-        const CUtensorMap* ma_lo = w.kind ? &maps.p_lo : &maps.l_lo;
-        const CUtensorMap* mb_hi = w.kind ? &maps.c_hi : &maps.q_hi;
-        const CUtensorMap* mb_lo = w.kind ? &maps.c_lo : &maps.q_lo;
-        for (int tq = w.k0; tq < S; tq += KQ, ++it) {  // queries t >= k0 (entries with t < j are zero)
+        const CUtensorMap* ma_hi = w.kind == 2 ? &maps.lr_hi : w.kind ? &maps.p_hi : &maps.l_hi;
+        const CUtensorMap* ma_lo = w.kind == 2 ? &maps.lr_lo : w.kind ? &maps.p_lo : &maps.l_lo;
+        const CUtensorMap* mb_hi = w.kind == 2 ? &maps.k_hi : w.kind ? &maps.c_hi : &maps.q_hi;
+        const CUtensorMap* mb_lo = w.kind == 2 ? &maps.k_lo : w.kind ? &maps.c_lo : &maps.q_lo;
+        for (int x = w.x0; x < w.x1; x += KQ, ++it) {
           const int s = it % KST;
           if (it >= KST && !mbar_wait(&empty[s], ((it / KST) - 1) & 1, a.st)) {
             ok = false;
             break;
           }
           uint8_t* stg = sm + s * KSTAGE;
+          // A: dL / P rows x..x+31, keys k0..k0+127 (dK, dV) or rows k0..k0+127, keys x..x+31 (dQ)
+          const int ac0 = w.kind == 2 ? x : w.k0, ac1 = w.kind == 2 ? w.k0 : x;
           mbar_arrive_expect_tx(&full[s], KSTAGE);
-          tma_load_3d(stg + OFF_AH, ma_hi, &full[s], w.k0, tq, bh);
-          tma_load_3d(stg + OFF_AL, ma_lo, &full[s], w.k0, tq, bh);
-          tma_load_3d(stg + OFF_BH, mb_hi, &full[s], w.h * KD, tq, w.b);
-          tma_load_3d(stg + OFF_BL, mb_lo, &full[s], w.h * KD, tq, w.b);
+          tma_load_3d(stg + OFF_AH, ma_hi, &full[s], ac0, ac1, bh);
+          tma_load_3d(stg + OFF_AL, ma_lo, &full[s], ac0, ac1, bh);
+          tma_load_3d(stg + OFF_BH, mb_hi, &full[s], w.h * KD, x, w.b);
+          tma_load_3d(stg + OFF_BL, mb_lo, &full[s], w.h * KD, x, w.b);
         }
       }
       // the last loads in flight land before the CTA exits
@@ -168,8 +197,10 @@ __global__ void __launch_bounds__(KTHREADS, 1) attn_kv_tc_kernel(const __grid_co
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      // dK: dL (s8 hi / u8 lo) x Q (s8 / u8); dV: P (hi <= 127, as u8) x dC (s8 / u8)
+      // dK: dL (s8 hi / u8 lo) x Q (s8 / u8); dV: P (hi <= 127, as u8) x dC (s8 / u8);
+      // dQ: dL x K (s8 / u8), A K-major
       const uint32_t id_ss = idesc_mn(1, 1), id_su = idesc_mn(1, 0), id_us = idesc_mn(0, 1), id_uu = idesc_mn(0, 0);
+      const uint32_t iq_ss = idesc_kmn(1, 1), iq_su = idesc_kmn(1, 0), iq_us = idesc_kmn(0, 1), iq_uu = idesc_kmn(0, 0);
       uint32_t it = 0, local = 0;
       bool ok = true;
       for (int item = blockIdx.x; item < a.items && ok; item += gridDim.x, ++local) {
@@ -178,8 +209,10 @@ __global__ void __launch_bounds__(KTHREADS, 1) attn_kv_tc_kernel(const __grid_co
         if (use > 0 && !mbar_wait(&acc_empty[buf], (use - 1) & 1, a.st)) break;
         tc_fence_after();
         const uint32_t d = tmem + buf * ACC_COLS;
-        const uint32_t i_hh = w.kind ? id_us : id_ss, i_hl = w.kind ? id_uu : id_su;
-        for (int tq = w.k0; tq < S; tq += KQ, ++it) {
+        const bool kq = w.kind == 2;
+        const uint32_t i_hh = kq ? iq_ss : w.kind ? id_us : id_ss, i_hl = kq ? iq_su : w.kind ? id_uu : id_su;
+        const uint32_t i_lh = kq ? iq_us : id_us, i_ll = kq ? iq_uu : id_uu;
+        for (int x = w.x0; x < w.x1; x += KQ, ++it) {
           const int s = it % KST;
           if (!mbar_wait(&full[s], (it / KST) & 1, a.st)) {
             ok = false;
@@ -187,21 +220,22 @@ __global__ void __launch_bounds__(KTHREADS, 1) attn_kv_tc_kernel(const __grid_co
           }
           tc_fence_after();
           const uint32_t base = smem_u32(sm + s * KSTAGE);
-          const uint64_t ah = sdesc_mn(base + OFF_AH, 1024, LAYOUT_SW128), al = sdesc_mn(base + OFF_AL, 1024, LAYOUT_SW128);
+          const uint64_t ah = kq ? sdesc_k32(base + OFF_AH) : sdesc_mn(base + OFF_AH, 1024, LAYOUT_SW128);
+          const uint64_t al = kq ? sdesc_k32(base + OFF_AL) : sdesc_mn(base + OFF_AL, 1024, LAYOUT_SW128);
           const uint64_t bhd = sdesc_mn(base + OFF_BH, 512, LAYOUT_SW64), bld = sdesc_mn(base + OFF_BL, 512, LAYOUT_SW64);
-          const uint32_t acc = tq > w.k0 ? 1u : 0u;
+          const uint32_t acc = x > w.x0 ? 1u : 0u;
           umma_i8(d, ah, bhd, i_hh, acc);            // hh
           umma_i8(d + 64, ah, bld, i_hl, acc);       // mid: hi x lo
-          umma_i8(d + 64, al, bhd, id_us, 1u);       //      lo x hi
-          umma_i8(d + 128, al, bld, id_uu, acc);     // ll
+          umma_i8(d + 64, al, bhd, i_lh, 1u);        //      lo x hi
+          umma_i8(d + 128, al, bld, i_ll, acc);      // ll
           umma_commit(&empty[s]);
         }
         umma_commit(&acc_full[buf]);
       }
     }
   } else {
-    // Epilogue: warp w reads TMEM lanes [32 (w % 4), +32) (key j of the item)
-    // and dims [32 g, 32 g + 32), g = (w - 2) / 4.
+    // Epilogue: warp w reads TMEM lanes [32 (w % 4), +32) (key j, or query t
+    // for dQ, of the item) and dims [32 g, 32 g + 32), g = (w - 2) / 4.
     const int q = warp & 3, g = (warp - 2) >> 2;
     uint32_t local = 0;
     for (int item = blockIdx.x; item < a.items; item += gridDim.x, ++local) {
@@ -211,9 +245,9 @@ __global__ void __launch_bounds__(KTHREADS, 1) attn_kv_tc_kernel(const __grid_co
       tc_fence_after();
       const int j = w.k0 + q * 32 + lane;
       const uint32_t row = tmem + buf * ACC_COLS + ((uint32_t)(q * 32) << 16);
-      const uint32_t shift = w.kind ? 15u : (uint32_t)a.k_shift;
-      int16_t* out = w.kind ? a.dv : a.dk;
-      const GradPlanes& gp = w.kind ? a.gv : a.gk;
+      const uint32_t shift = w.kind == 1 ? 15u : (uint32_t)a.k_shift;
+      int16_t* out = w.kind == 2 ? a.dq : w.kind ? a.dv : a.dk;
+      const GradPlanes& gp = w.kind == 2 ? a.gq : w.kind ? a.gv : a.gk;
       const long long orow = ((long long)w.b * S + j) * a.d + (long long)w.h * KD;
 #pragma unroll
       for (int c = 32 * g; c < 32 * g + 32; c += 16) {
@@ -304,17 +338,20 @@ EncodeTiledFn kv_encode_fn() {
   return fn;
 }
 
-// uint8 [n2][n1][n0] (strides s1, s2 bytes), box [1][KQ rows][box0 bytes] with the
-// swizzle of the row width; rows past n1 (the sequence) read zeros.
+// uint8 [n2][n1][n0] (strides s1, s2 bytes), box [1][box1 rows][box0 bytes]
+// (box0 = 128, 64 or 32) with the swizzle of the row width; rows past n1 and
+// columns past n0 (the sequence) read zeros.
 bool kv_map(CUtensorMap* m, const void* ptr, uint64_t n0, uint64_t n1, uint64_t n2, uint64_t s1, uint64_t s2,
-            uint32_t box0) {
+            uint32_t box0, uint32_t box1 = KQ) {
   EncodeTiledFn fn = kv_encode_fn();
   if (!fn) return false;
   cuuint64_t dims[3] = {n0, n1, n2};
   cuuint64_t strides[2] = {s1, s2};
-  cuuint32_t box[3] = {box0, (cuuint32_t)KQ, 1};
+  cuuint32_t box[3] = {box0, box1, 1};
   cuuint32_t es[3] = {1, 1, 1};
-  const CUtensorMapSwizzle sw = box0 == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  const CUtensorMapSwizzle sw = box0 == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : box0 == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                             : CU_TENSOR_MAP_SWIZZLE_32B;
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(ptr), dims, strides, box, es,
             CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
@@ -337,10 +374,11 @@ cudaError_t launch_split_causal(const int16_t* M, size_t BH, size_t S, int8_t* h
 
 cudaError_t launch_attention_kv_tc(const Planes& l, const Planes& p, const Planes& qp, const Planes& cp, size_t B,
                                    size_t S, size_t d, size_t H, int16_t* dk, int16_t* dv, const GradPlanes& gk,
-                                   const GradPlanes& gv, nsrl_device_status* st, cudaStream_t s) {
+                                   const GradPlanes& gv, nsrl_device_status* st, cudaStream_t s, const Planes* kp,
+                                   int16_t* dq, const GradPlanes& gq) {
   if (!attention_kv_tc_supported(S, d, H)) return cudaErrorNotSupported;
   if (B == 0) return cudaSuccess;
-  KvMaps m;
+  KvMaps m{};
   const uint64_t BH = (uint64_t)B * H;
   const bool ok = kv_map(&m.l_hi, l.hi, S, S, BH, S, (uint64_t)S * S, KK) &&
                   kv_map(&m.l_lo, l.lo, S, S, BH, S, (uint64_t)S * S, KK) &&
@@ -349,7 +387,11 @@ cudaError_t launch_attention_kv_tc(const Planes& l, const Planes& p, const Plane
                   kv_map(&m.q_hi, qp.hi, d, S, B, qp.ld, (uint64_t)S * qp.ld, KD) &&
                   kv_map(&m.q_lo, qp.lo, d, S, B, qp.ld, (uint64_t)S * qp.ld, KD) &&
                   kv_map(&m.c_hi, cp.hi, d, S, B, cp.ld, (uint64_t)S * cp.ld, KD) &&
-                  kv_map(&m.c_lo, cp.lo, d, S, B, cp.ld, (uint64_t)S * cp.ld, KD);
+                  kv_map(&m.c_lo, cp.lo, d, S, B, cp.ld, (uint64_t)S * cp.ld, KD) &&
+                  (!kp || (kv_map(&m.lr_hi, l.hi, S, S, BH, S, (uint64_t)S * S, KQ, KK) &&
+                           kv_map(&m.lr_lo, l.lo, S, S, BH, S, (uint64_t)S * S, KQ, KK) &&
+                           kv_map(&m.k_hi, kp->hi, d, S, B, kp->ld, (uint64_t)S * kp->ld, KD) &&
+                           kv_map(&m.k_lo, kp->lo, d, S, B, kp->ld, (uint64_t)S * kp->ld, KD)));
   if (!ok) return cudaErrorNotSupported;
   static bool configured = false;
   if (!configured) {
@@ -365,19 +407,23 @@ cudaError_t launch_attention_kv_tc(const Planes& l, const Planes& p, const Plane
   a.k_shift = 3;  // log4(64)
   a.B = (int)B;
   a.nk = (int)((S + KK - 1) / KK);
-  if ((size_t)2 * B * H * a.nk > 0x7fffffffull) return cudaErrorNotSupported;
-  a.items = 2 * a.B * a.H * a.nk;
+  a.kinds = kp ? 3 : 2;
+  if ((size_t)a.kinds * B * H * a.nk > 0x7fffffffull) return cudaErrorNotSupported;
+  a.items = a.kinds * a.B * a.H * a.nk;
   a.dk = dk;
   a.dv = dv;
+  a.dq = dq;
   a.gk = gk;
   a.gv = gv;
+  a.gq = gq;
   a.st = st;
   int sms = 0, dev = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const unsigned grid = (unsigned)std::min(a.items, sms > 0 ? sms : 148);
   const double pairs = (double)B * (double)H * (double)S * (double)(S + 1) / 2.0;
-  ProfScope prof("attention_bwd_kv", s, 2.0 * 2.0 * 64.0 * pairs, 2.0 * 2.0 * pairs + 8.0 * (double)B * S * d);
+  ProfScope prof(kp ? "attention_bwd_qkv" : "attention_bwd_kv", s, a.kinds * 2.0 * 64.0 * pairs,
+                 a.kinds * 2.0 * pairs + 4.0 * a.kinds * (double)B * S * d);
   attn_kv_tc_kernel<<<grid, KTHREADS, KSMEM, s>>>(m, a);
   return cudaGetLastError();
 }

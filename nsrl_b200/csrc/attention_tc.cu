@@ -82,6 +82,8 @@ struct Args {
   unsigned long long* ctx_l1;
   long long ldc;
   int16_t* probs;    // optional P [B][H][S][S]: the visited key tiles only, zeros above the diagonal
+  int8_t* probs_hi;  // optional P as byte planes [B][H][S][S], the same entries
+  uint8_t* probs_lo;
   nsrl_device_status* st;
 };
 
@@ -602,6 +604,11 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
       const uint32_t off = swz32_chunk((uint32_t)row, (uint32_t)g);
       *reinterpret_cast<uint4*>(ph + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
       *reinterpret_cast<uint4*>(pl + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+      if (a.probs_hi && row_live && key0 < S) {  // the cached P as planes (S % 16 == 0: 16-byte rows)
+        const long long o = (((long long)b * a.H + h) * S + qi) * (long long)S + key0;
+        *reinterpret_cast<uint4*>(a.probs_hi + o) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        *reinterpret_cast<uint4*>(a.probs_lo + o) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+      }
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&ctl->p_full[pb]);
@@ -718,8 +725,9 @@ size_t attention_tc_scratch_bytes(size_t B, size_t S, size_t d, size_t H) {
 
 cudaError_t launch_attention_tc(const Planes& qkv, const VtPlanes& vt, size_t B, size_t S, size_t d, size_t H,
                                 bool causal, Planes ctx, int16_t* wscr, nsrl_device_status* st,
-                                cudaStream_t stream, int16_t* probs) {
+                                cudaStream_t stream, int16_t* probs, const Planes* probs_planes) {
   if (!attention_tc_supported(S, d, H) || encode_fn() == nullptr || wscr == nullptr) return cudaErrorNotSupported;
+  if (probs_planes && (!causal || probs_planes->ld != S)) return cudaErrorInvalidValue;
   if (B == 0) return cudaSuccess;
   const size_t T = B * S;
   Maps m;
@@ -738,6 +746,8 @@ cudaError_t launch_attention_tc(const Planes& qkv, const VtPlanes& vt, size_t B,
   a.ctx_l1 = ctx.l1;
   a.ldc = (long long)ctx.ld;
   a.probs = probs;
+  a.probs_hi = probs_planes ? probs_planes->hi : nullptr;
+  a.probs_lo = probs_planes ? probs_planes->lo : nullptr;
   a.st = st;
   a.wscr = wscr;
   a.wstride = (long long)attention_tc_wstride(S);

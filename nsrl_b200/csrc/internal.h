@@ -92,9 +92,13 @@ cudaError_t launch_attention(const Planes& qkv, size_t B, size_t S, size_t d, si
 // that the last pass does not recompute Q K^T.
 // probs (optional): P [B][H][S][S] int16 of every visited key tile; the
 // causal tiles past a query tile's last row are not visited (zero them first).
+// probs_planes (optional, causal only, ld S): the same entries as byte planes;
+// row t is written for keys below the end of its 128-key block, zeros above
+// the diagonal, which is the causal plane form the backward reads.
 cudaError_t launch_attention_tc(const Planes& qkv, const VtPlanes& vt, size_t B, size_t S, size_t d, size_t H,
                                 bool causal, Planes ctx, int16_t* wscr, nsrl_device_status* st,
-                                cudaStream_t stream, int16_t* probs = nullptr);
+                                cudaStream_t stream, int16_t* probs = nullptr,
+                                const Planes* probs_planes = nullptr);
 size_t attention_tc_wstride(size_t S);
 size_t attention_tc_scratch_bytes(size_t B, size_t S, size_t d, size_t H);
 // Shape rule of the tensor-core attention (head_dim 64, seq_len % 16 == 0,
@@ -146,18 +150,23 @@ cudaError_t launch_attention_backward_tc(const int16_t* q, const int16_t* k, con
                                          const int16_t* P, const int16_t* dC, size_t ldc, size_t B, size_t S, size_t d,
                                          size_t H, int16_t* dl, int16_t* dq, int16_t* dk, int16_t* dv,
                                          void* scratch, size_t scratch_bytes, nsrl_device_status* st,
-                                         cudaStream_t s, const GradPlanes* planes = nullptr);
+                                         cudaStream_t s, const GradPlanes* planes = nullptr,
+                                         const Planes* p_planes = nullptr);
 
-// Key side of the attention backward on the tensor cores (head_dim 64):
-// dK = dL^T Q and dV = P^T dC per (sequence, head) from row-major byte planes
-// read in place: l, p = [B*H][S][S] with entries above the diagonal zero (as
-// launch_split_causal writes them), qp, cp = [B][S][d] (row stride ld).
-// Outputs int16 [B*S][d] (NULL to skip) and/or prescaled planes.
+// Key and query sides of the attention backward on the tensor cores
+// (head_dim 64): dK = dL^T Q, dV = P^T dC and, with kp, dQ = dL K per
+// (sequence, head) from row-major byte planes read in place: l, p =
+// [B*H][S][S] with entries above the diagonal zero up to the end of each
+// row's 128-column block (as launch_split_causal writes them), qp, cp, kp =
+// [B][S][d] (row stride ld).  Outputs int16 [B*S][d] (NULL to skip) and/or
+// prescaled planes.
 bool attention_kv_tc_supported(size_t S, size_t d, size_t H);
 cudaError_t launch_split_causal(const int16_t* M, size_t BH, size_t S, int8_t* hi, uint8_t* lo, cudaStream_t s);
 cudaError_t launch_attention_kv_tc(const Planes& l, const Planes& p, const Planes& qp, const Planes& cp, size_t B,
                                    size_t S, size_t d, size_t H, int16_t* dk, int16_t* dv, const GradPlanes& gk,
-                                   const GradPlanes& gv, nsrl_device_status* st, cudaStream_t s);
+                                   const GradPlanes& gv, nsrl_device_status* st, cudaStream_t s,
+                                   const Planes* kp = nullptr, int16_t* dq = nullptr,
+                                   const GradPlanes& gq = GradPlanes{});
 
 // Planes -> int16.
 cudaError_t launch_join_planes(Planes in, size_t rows, size_t cols, int16_t* y, size_t ldy, cudaStream_t stream);

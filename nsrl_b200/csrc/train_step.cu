@@ -259,10 +259,12 @@ cudaError_t add_sat(const int16_t* a, const int16_t* b, size_t n, int16_t* out, 
 cudaError_t attn_backward(const int16_t* q, const int16_t* k, const int16_t* v, size_t ld, const int16_t* P,
                           const int16_t* dC, size_t ldc, size_t B, size_t S, size_t d, size_t H, int16_t* dL,
                           int16_t* dq, int16_t* dk, int16_t* dv, void* scratch, size_t scratch_bytes,
-                          nsrl_device_status* st, cudaStream_t s, const GradPlanes* planes = nullptr) {
+                          nsrl_device_status* st, cudaStream_t s, const GradPlanes* planes = nullptr,
+                          const Planes* p_planes = nullptr) {
   const cudaError_t tce = launch_attention_backward_tc(q, k, v, ld, P, dC, ldc, B, S, d, H, dL, dq, dk, dv, scratch,
-                                                       scratch_bytes, st, s, planes);
+                                                       scratch_bytes, st, s, planes, p_planes);
   if (tce != cudaErrorNotSupported) return tce;
+  if (p_planes) return cudaErrorInvalidValue;  // only the tensor-core path reads P as planes
   if (planes) {
     const cudaError_t e = attn_backward(q, k, v, ld, P, dC, ldc, B, S, d, H, dL, dq, dk, dv, scratch, scratch_bytes,
                                         st, s, nullptr);
@@ -308,12 +310,21 @@ cudaError_t attn_backward(const int16_t* q, const int16_t* k, const int16_t* v, 
 
 // ------------------------------------------------------------------ layout --
 struct LayerCache {
+  // P: [W][H][S][S] int16, or (p_planes) the same bytes as its two byte planes,
+  // hi then lo, in the causal form the tensor-core forward writes
   int16_t *in, *qkv, *P, *ares, *up, *gate, *out;
+  bool p_planes;
   // inputs of the linears as byte planes (+ row L1): the forward GEMMs read
   // them and the weight gradients read them again in the backward
   Planes an, ctx, mn, gated;  // q|k|v input, o input, up|gate input, down input
   int8_t *wt[7];  // transposed q k v o (d x d), up, gate ([d][F]), down ([F][d])
 };
+
+// The cached P buffer (n int16 entries) viewed as two byte planes of row length ld.
+Planes p_cache_planes(const LayerCache& c, size_t n, size_t ld) {
+  int8_t* hi = reinterpret_cast<int8_t*>(c.P);
+  return Planes{hi, reinterpret_cast<uint8_t*>(hi + n), nullptr, ld};
+}
 
 struct StepLayout {
   size_t W, S, T, d, F, H, L;
@@ -356,6 +367,7 @@ void carve_step(const nsrl_train_model* m, size_t W, bool rms, void* base, StepL
     lc.qkv = c.take<int16_t>(T * 3 * d);
     lc.ctx = c.planes(T, d, true);
     lc.P = c.take<int16_t>(W * H * S * S);
+    lc.p_planes = false;
     lc.ares = c.take<int16_t>(T * d);
     lc.mn = c.planes(T, d, true);
     lc.up = c.take<int16_t>(T * F);
@@ -701,14 +713,20 @@ nsrl_status nsrl_train_windows(const nsrl_train_model* m, const uint8_t* context
       TS_TRY(launch_gemm(g, s), "qkv");
     }
     bool done = false;
+    c.p_planes = false;
     if (tc_attn) {
       // every P entry the backward reads is written: the visited key tiles of
-      // each 128-query tile, zeros above the diagonal
+      // each 128-query tile, zeros above the diagonal; as byte planes when the
+      // tensor-core backward takes the shape (it reads them in place)
       TS_TRY(cudaMemsetAsync(c.ctx.l1, 0, T * sizeof(unsigned long long), s), "memset");
-      const cudaError_t e = launch_attention_tc(o.pqkv, o.vt, W, S, d, H, true, c.ctx, o.vt.wscr, st, s, c.P);
+      const bool pl = attention_kv_tc_supported(S, d, H);
+      const Planes pv = p_cache_planes(c, W * H * S * S, S);
+      const cudaError_t e = launch_attention_tc(o.pqkv, o.vt, W, S, d, H, true, c.ctx, o.vt.wscr, st, s,
+                                                pl ? nullptr : c.P, pl ? &pv : nullptr);
       if (e != cudaErrorNotSupported) {
         TS_TRY(e, "attention");
         done = true;
+        c.p_planes = pl;
       }
     }
     if (!done) {  // int16 context in a backward buffer that is free during the forward
@@ -823,8 +841,9 @@ nsrl_status nsrl_train_windows(const nsrl_train_model* m, const uint8_t* context
     TS_TRY(accumulate_planes(padn, c.ctx, T, d, d, acc + lin_off[3], st, s), "o grad");
     GradPlanes gp[3];
     for (int i = 0; i < 3; ++i) gp[i] = GradPlanes{ly.lin[i].scales, o.pg[i].hi, o.pg[i].lo};
-    TS_TRY(attn_backward(c.qkv, c.qkv + d, c.qkv + 2 * d, 3 * d, c.P, o.gctx, d, W, S, d, H, o.dL, o.dq, o.dk, o.dv,
-                         o.abw, o.abw_bytes, st, s, gp),
+    const Planes pv = p_cache_planes(c, W * H * S * S, S);
+    TS_TRY(attn_backward(c.qkv, c.qkv + d, c.qkv + 2 * d, 3 * d, c.p_planes ? nullptr : c.P, o.gctx, d, W, S, d, H,
+                         o.dL, o.dq, o.dk, o.dv, o.abw, o.abw_bytes, st, s, gp, c.p_planes ? &pv : nullptr),
            "attention backward");
     int16_t* gin[3] = {o.gq, o.gk, o.gv};
     for (int i = 0; i < 3; ++i)

@@ -147,7 +147,8 @@ def test_train_step_reference_initial_model():
     (64, 4, 128, 2, 16, 3, True, True),
     (64, 1, 128, 1, 24, 2, False, False),
     (128, 2, 256, 2, 40, 2, True, False),
-    (128, 2, 256, 2, 144, 2, True, True),   # head_dim 64, S % 16 == 0: the tensor-core key side, a ragged key tile
+    (128, 2, 256, 2, 144, 2, True, True),   # head_dim 64, S % 16 == 0: the tensor-core backward, a ragged key tile
+    (128, 2, 256, 1, 272, 2, False, True),  # three 128-query tiles: P cached as planes, dQ on the tensor cores
 ])
 def test_train_step_random_models(d, H, F, L, S, W, rms, pos):
     m = random_model(d, H, F, L, S, rms=rms, positions=pos, seed=d + S)
