@@ -11,9 +11,11 @@
 // With g = 256 gh + gl and x = 256 xh + xl,
 //   g x = 65536 gh xh + 256 (gh xl + gl xh) + gl xl,
 // so per 128-row block four MMAs fill three s32 TMEM accumulators:
-//   hh  += gh . xh        (s8 x s8, |term| <= 16384)
-//   mid += gh . xl + gl . xh  (s8 x u8 and u8 x s8, |two terms| <= 65280)
-//   ll  += gl . xl        (u8 x u8, term <= 65025)
+//   hh  += xh . gh        (s8 x s8, |term| <= 16384)
+//   mid += xh . gl + xl . gh  (s8 x u8 and u8 x s8, |two terms| <= 65280)
+//   ll  += xl . gl        (u8 x u8, term <= 65025)
+// X is the A operand (TMEM lane = k) and G the B operand (column = n), so a
+// warp's 32 lanes add into 32 consecutive k of one accumulator row.
 // A work item covers at most 32768 rows, so every accumulator stays below
 // 2^31 and is exact.  The epilogue forms 65536 hh + 256 mid + ll in i64 and
 // adds it to acc with red.global.add.u64 (two's-complement, exact).
@@ -165,10 +167,10 @@ __global__ void __launch_bounds__(WTHREADS, 1) wgrad_tc_kernel(const __grid_cons
             const uint64_t xh = sdesc_mn128(base + 2 * WTILE + 4096 * j);
             const uint64_t xl = sdesc_mn128(base + 3 * WTILE + 4096 * j);
             const uint32_t acc = (b > b0 || j > 0) ? 1u : 0u;
-            umma_i8(tmem, gh, xh, id_ss, acc);
-            umma_i8(tmem + WB, gh, xl, id_su, acc);
-            umma_i8(tmem + WB, gl, xh, id_us, 1u);
-            umma_i8(tmem + 2 * WB, gl, xl, id_uu, acc);
+            umma_i8(tmem, xh, gh, id_ss, acc);
+            umma_i8(tmem + WB, xh, gl, id_su, acc);
+            umma_i8(tmem + WB, xl, gh, id_us, 1u);
+            umma_i8(tmem + 2 * WB, xl, gl, id_uu, acc);
           }
           umma_commit(&empty[s]);
         }
@@ -176,16 +178,16 @@ __global__ void __launch_bounds__(WTHREADS, 1) wgrad_tc_kernel(const __grid_cons
       }
     }
   } else {
-    // Epilogue: warp w reads TMEM lanes [32*(w%4), +32) (rows n) and columns
-    // [32*cg, +32) (k) of the three accumulators.
+    // Epilogue: warp w reads TMEM lanes [32*(w%4), +32) (k) and columns
+    // [32*cg, +32) (n) of the three accumulators.
     const int q = warp & 3;
     const int cg = (warp - 2) >> 2;
     uint32_t local = 0;
     for (int item = blockIdx.x; item < p.items; item += gridDim.x, ++local) {
       const int tile = item / p.chunks;
       const int n0 = (tile / p.tiles_k) * WB, k0 = (tile % p.tiles_k) * WB;
-      const int n = n0 + q * 32 + lane;
-      const int kb = k0 + 32 * cg;
+      const int k = k0 + q * 32 + lane;
+      const int nb = n0 + 32 * cg;
       if (!mbar_wait(acc_full, local & 1, p.st)) break;
       tc_fence_after();
       const uint32_t row = tmem + ((uint32_t)(q * 32) << 16) + 32 * cg;
@@ -201,12 +203,12 @@ __global__ void __launch_bounds__(WTHREADS, 1) wgrad_tc_kernel(const __grid_cons
           tc_fence_before();
           if (lane == 0) mbar_arrive(acc_empty);
         }
-        if (n < p.N) {
-          long long* dst = p.acc + (long long)n * p.K + kb + 16 * half;
+        if (k < p.K) {
+          long long* dst = p.acc + (long long)(nb + 16 * half) * p.K + k;
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const long long v = (long long)(int)hh[i] * 65536ll + (long long)(int)md[i] * 256ll + (long long)ll[i];
-            if (kb + 16 * half + i < p.K && v != 0) red_add_u64(dst + i, v);
+            if (nb + 16 * half + i < p.N && v != 0) red_add_u64(dst + (long long)i * p.K, v);
           }
         }
       }
@@ -280,20 +282,32 @@ cudaError_t launch_wgrad_tc(const int8_t* gh, const uint8_t* gl, size_t ldg, con
   p.tiles_k = (int)((K + WB - 1) / WB);
   const int tiles = (int)((N + WB - 1) / WB) * p.tiles_k;
   p.nblocks = (int)((T + WB - 1) / WB);
-  // rows per item: at most 32768 (exact s32 accumulators), and enough items
-  // for two waves of the 148 SMs where the row count allows
+  int sms = 0, dev = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (sms <= 0) sms = 148;
+  // Rows per item: at most 32768 (exact s32 accumulators).  Items are equal,
+  // so the time is about rounds x (blocks per item + one block's worth of
+  // epilogue), rounds = ceil(items / SMs): take the chunking that minimises it
+  // (fewer items on a tie: fewer atomic adds).
   const int max_blocks = 32768 / WB;
-  int chunks = std::max((p.nblocks + max_blocks - 1) / max_blocks, (2 * 148 + tiles - 1) / tiles);
-  chunks = std::min(chunks, p.nblocks);
-  p.chunk_blocks = (p.nblocks + chunks - 1) / chunks;
+  int best_cb = 0;
+  long long best_cost = 0;
+  for (int chunks = (p.nblocks + max_blocks - 1) / max_blocks; chunks <= std::min(p.nblocks, 8 * sms); ++chunks) {
+    const int cb = (p.nblocks + chunks - 1) / chunks;
+    const long long items = (long long)tiles * ((p.nblocks + cb - 1) / cb);
+    const long long cost = (items + sms - 1) / sms * (cb + 1);
+    if (best_cb == 0 || cost < best_cost) {
+      best_cb = cb;
+      best_cost = cost;
+    }
+  }
+  p.chunk_blocks = best_cb;
   p.chunks = (p.nblocks + p.chunk_blocks - 1) / p.chunk_blocks;
   p.items = tiles * p.chunks;
   p.acc = acc;
   p.st = st;
-  int sms = 0, dev = 0;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int grid = std::min(p.items, sms > 0 ? sms : 148);
+  const int grid = std::min(p.items, sms);
   ProfScope prof("accumulate_weight_grad_tc", s, 2.0 * (double)T * (double)N * (double)K,
                  2.0 * (double)T * (double)(N + K) + 16.0 * (double)N * (double)K * p.chunks);
   wgrad_tc_kernel<<<grid, WTHREADS, WSMEM, s>>>(maps, p);
