@@ -168,6 +168,20 @@ __device__ __forceinline__ int requant_wide1(uint32_t h, uint32_t l, int mult, i
 }
 __device__ __forceinline__ void requant_wide16(const uint32_t (&h)[16], const uint32_t (&l)[16], const ColScale& c,
                                                int (&v)[16], bool& bad, int base) {
+  if (c.uniform) {
+    // multiplier 1 and one shift s for every column: |256 hi + lo| < 2^40, so
+    // rhu64's saturating add cannot saturate; the sum is one wide
+    // multiply-add and the rounded shift one 64-bit shift
+    const uint32_t sh = min((uint32_t)c.ushift, 62u);
+    const long long bias = sh ? (1ll << (sh - 1)) : 0ll;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const long long a = ((long long)(int)h[i] * 256ll + ((long long)(int)l[i] + bias)) >> sh;
+      const int lo = (int)a, hi = (int)(a >> 32);
+      v[i] = hi == (lo >> 31) ? max(-32768, min(32767, lo)) : (hi < 0 ? -32768 : 32767);
+    }
+    return;
+  }
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     const int mult = c.uniform ? 1 : __shfl_sync(0xffffffffu, c.mult, base + i);

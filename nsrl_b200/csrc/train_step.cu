@@ -211,10 +211,32 @@ cudaError_t accumulate_planes(const Planes& g, const Planes& x, size_t rows, siz
   return cudaGetLastError();
 }
 
+cudaError_t add_sat(const int16_t* a, const int16_t* b, size_t n, int16_t* out, unsigned long long* sat,
+                    cudaStream_t s);
+
+// RMS-norm backward of the rows of x (rms_norm.rs:140-190).  With res, out =
+// sat(res + gi) (the residual add of the block backward, saturations into
+// res_sat); gi is then scratch that only the fallback path writes.
 cudaError_t rms_backward(const int16_t* x, size_t rows, size_t d, const int16_t* w, const int16_t* go, uint64_t eps,
-                         int16_t* gi, long long* gw, unsigned long long* sat, nsrl_device_status* st, cudaStream_t s) {
+                         int16_t* gi, long long* gw, unsigned long long* sat, nsrl_device_status* st, cudaStream_t s,
+                         const int16_t* res = nullptr, int16_t* out = nullptr,
+                         unsigned long long* res_sat = nullptr) {
   if (rows == 0) return cudaSuccess;
   const size_t smem = d * sizeof(long long);
+  // d = 256: the 16-byte row kernel, two rows per warp (wider rows stay on
+  // the kernels below, which hold fewer values per lane)
+  if (d == 256 && aligned_to(x, 16) && aligned_to(w, 16) && aligned_to(go, 16) &&
+      aligned_to(res ? (const void*)res : (const void*)gi, 16) && aligned_to(res ? (void*)out : (void*)gi, 16)) {
+    ProfScope prof("rms_backward", s, 0.0, (res ? 8.0 : 6.0) * (double)rows * (double)d);
+    rms_backward_vec_kernel<2><<<blocks_for((long long)(rows + 1) / 2 * 32, 148 * 8), 256, 0, s>>>(
+        x, (long long)rows, w, go, eps, gi, gw, sat, st, res, out, res_sat);
+    return cudaGetLastError();
+  }
+  if (res) {
+    const cudaError_t e = rms_backward(x, rows, d, w, go, eps, gi, gw, sat, st, s);
+    if (e != cudaSuccess) return e;
+    return add_sat(res, gi, rows * d, out, res_sat, s);
+  }
   ProfScope prof("rms_backward", s, 0.0, 6.0 * (double)rows * (double)d);
   if (d % 32 == 0 && d <= 512) {
     const unsigned blocks = blocks_for((long long)rows * 32, 148 * 8);
@@ -818,13 +840,14 @@ nsrl_status nsrl_train_windows(const nsrl_train_model* m, const uint8_t* context
     }
     TS_TRY(bwd_gemm(paFn, T, F, c.wt[4], d, o.ident, o.gui, d, nullptr, nullptr, st, s), "up^T");
     TS_TRY(bwd_gemm(pbF, T, F, c.wt[5], d, o.ident, o.gmi, d, o.gui, mlp_sat, st, s), "gate^T");
-    const int16_t* gmr = o.gmi;
-    if (rms) {
-      TS_TRY(rms_backward(c.ares, T, d, ly.mlp_gamma, o.gmi, 1, o.gmr, acc + rms_m_off, mlp_sat, st, s), "rms bwd");
-      gmr = o.gmr;
+    if (rms) {  // the norm's backward with the residual add fused: gao = sat(G + rms'(gmi))
+      TS_TRY(rms_backward(c.ares, T, d, ly.mlp_gamma, o.gmi, 1, o.gmr, acc + rms_m_off, mlp_sat, st, s, o.G, o.gao,
+                          res_sat),
+             "rms bwd");
       add_count(1 + 9 * l + 8, T);
+    } else {
+      TS_TRY(add_sat(o.G, o.gmi, T * d, o.gao, res_sat, s), "residual");
     }
-    TS_TRY(add_sat(o.G, gmr, T * d, o.gao, res_sat, s), "residual");
     // gated-MLP weight gradients (lib.rs:13783-13871)
     {
       ProfScope prof("nonzero_rows", s, 0.0, 2.0 * (double)T * (double)d);
@@ -863,13 +886,14 @@ nsrl_status nsrl_train_windows(const nsrl_train_model* m, const uint8_t* context
       TS_TRY(accumulate_planes(Planes{o.pg[i].hi, o.pg[i].lo, nullptr, d}, c.an, T, d, d, acc + lin_off[i], st, s),
              "qkv grad");
     for (int i = 0; i < 4; ++i) add_count(1 + 9 * l + i, T);
-    const int16_t* gai = o.gni;
-    if (rms) {
-      TS_TRY(rms_backward(c.in, T, d, ly.attn_gamma, o.gni, 1, o.gai, acc + rms_a_off, res_sat, st, s), "rms bwd");
-      gai = o.gai;
+    if (rms) {  // Gn = sat(gao + rms'(gni))
+      TS_TRY(rms_backward(c.in, T, d, ly.attn_gamma, o.gni, 1, o.gai, acc + rms_a_off, res_sat, st, s, o.gao, o.Gn,
+                          res_sat),
+             "rms bwd");
       add_count(1 + 9 * l + 7, T);
+    } else {
+      TS_TRY(add_sat(o.gao, o.gni, T * d, o.Gn, res_sat, s), "residual");
     }
-    TS_TRY(add_sat(o.gao, gai, T * d, o.Gn, res_sat, s), "residual");
     std::swap(o.G, o.Gn);
   }
   // embedding gradients (lib.rs:14336-14405)

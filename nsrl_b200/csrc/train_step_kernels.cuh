@@ -614,6 +614,136 @@ __global__ void __launch_bounds__(256) rms_backward_reg_kernel(const int16_t* __
   if (lane == 0 && nsat) atomicAdd(sat, nsat);
 }
 
+// Exact warp sums through the 32-bit reduction unit: an unsigned partial
+// below 2^37 as two 16-bit-split halves, a signed one below 2^52 in magnitude
+// as three pieces (each piece sums below 2^27 over 32 lanes).
+__device__ __forceinline__ unsigned long long warp_sum_u37(unsigned long long p) {
+  const unsigned a = __reduce_add_sync(0xffffffffu, (unsigned)(p >> 16));
+  const unsigned b = __reduce_add_sync(0xffffffffu, (unsigned)(p & 0xFFFF));
+  return ((unsigned long long)a << 16) + b;
+}
+__device__ __forceinline__ long long warp_sum_s52(long long q) {
+  const int h = __reduce_add_sync(0xffffffffu, (int)(q >> 32));
+  const unsigned m = __reduce_add_sync(0xffffffffu, (unsigned)((q >> 16) & 0xFFFF));
+  const unsigned l = __reduce_add_sync(0xffffffffu, (unsigned)(q & 0xFFFF));
+  return (long long)h * 4294967296ll + (long long)m * 65536ll + (long long)l;
+}
+
+// rms_backward_reg_kernel for d = 256 with 16-byte rows: lane l owns columns
+// 8 l .. 8 l + 7, each warp works on RPW rows at once (independent chains for
+// the scheduler), the row sums go through the reduction unit, and the
+// products run on 32-bit operands (inv <= 2^30, |nm| <= 2^30, |x w|, |g w| <=
+// 2^30) into 64-bit results.  Per lane |sum x^2| <= 2^33 and |sum sg nm| <=
+// 2^48, inside the exact ranges of the warp sums.  With `res`, the residual
+// add that follows the norm in the block backward is fused: out = sat(res +
+// gi), its saturations counted in res_sat (gi is not written); otherwise gi is
+// written as in rms_backward_reg_kernel.
+template <int RPW>
+__global__ void __launch_bounds__(256) rms_backward_vec_kernel(
+    const int16_t* __restrict__ x, long long rows, const int16_t* __restrict__ w, const int16_t* __restrict__ go,
+    unsigned long long eps, int16_t* __restrict__ gi, long long* __restrict__ gw, unsigned long long* sat,
+    nsrl_device_status* st, const int16_t* __restrict__ res, int16_t* __restrict__ out, unsigned long long* res_sat) {
+  constexpr int d = 256;
+  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+  int wv[8];
+  long long gacc[8];
+  unpack8(*reinterpret_cast<const uint4*>(w + 8 * lane), wv);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) gacc[i] = 0;
+  unsigned long long nsat = 0, rsat = 0;
+  const long long step = (long long)gridDim.x * warps * RPW;
+  for (long long r0 = ((long long)blockIdx.x * warps + (threadIdx.x >> 5)) * RPW; r0 < rows; r0 += step) {
+    int xv[RPW][8], gv[RPW][8];
+    bool live[RPW];
+#pragma unroll
+    for (int k = 0; k < RPW; ++k) {
+      live[k] = r0 + k < rows;
+      const long long o = (r0 + k) * d + 8 * lane;
+      unpack8(live[k] ? *reinterpret_cast<const uint4*>(x + o) : make_uint4(0, 0, 0, 0), xv[k]);
+      unpack8(live[k] ? *reinterpret_cast<const uint4*>(go + o) : make_uint4(0, 0, 0, 0), gv[k]);
+    }
+    int inv[RPW];
+    bool ok[RPW];
+#pragma unroll
+    for (int k = 0; k < RPW; ++k) {
+      unsigned long long ss = 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += (unsigned long long)(unsigned)(xv[k][i] * xv[k][i]);
+      ss = warp_sum_u37(ss);
+      const unsigned long long mean = ss / (unsigned long long)d;
+      const unsigned long long v = mean + eps;
+      ok[k] = live[k] && !(v < mean || v == 0);
+      if (live[k] && !ok[k] && lane == 0) nsrl_flag(st, NSRL_FLAG_RMS_ZERO);
+      inv[k] = ok[k] ? (int)rsqrt_q30(v) : 0;  // <= 2^30
+    }
+    int nm[RPW][8], sg[RPW][8];
+    long long mdot[RPW];
+#pragma unroll
+    for (int k = 0; k < RPW; ++k) {
+      long long dot = 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        nm[k][i] = (int)(((long long)xv[k][i] * inv[k] + (1ll << 14)) >> 15);
+        const long long proj = ((long long)(xv[k][i] * wv[i]) * inv[k] + (1ll << 29)) >> 30;
+        const bool active = ok[k] && proj >= -32768 && proj <= 32767;
+        sg[k][i] = active ? ((gv[k][i] * wv[i] + (1 << 14)) >> 15) : 0;
+        dot += (long long)sg[k][i] * nm[k][i];
+        if (active) gacc[i] += ((long long)gv[k][i] * nm[k][i] + (1ll << 14)) >> 15;
+      }
+      dot = warp_sum_s52(dot);
+      constexpr long long den = (long long)d << 15;
+      const long long tq = dot + den / 2;
+      mdot[k] = tq / den;
+      if ((tq % den) != 0 && tq < 0) --mdot[k];
+    }
+#pragma unroll
+    for (int k = 0; k < RPW; ++k) {
+      if (!ok[k]) continue;
+      const long long o = (r0 + k) * d + 8 * lane;
+      uint4 rn = make_uint4(0, 0, 0, 0);
+      if (res) rn = *reinterpret_cast<const uint4*>(res + o);
+      int o16[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const long long cross = ((long long)nm[k][i] * mdot[k] + (1ll << 14)) >> 15;
+        const long long gg = (((long long)sg[k][i] - cross) * inv[k] + (1ll << 29)) >> 30;
+        const int cl = sat_i16(gg);
+        nsat += (long long)cl != gg;
+        o16[i] = cl;
+      }
+      if (res) {
+        int rv[8];
+        unpack8(rn, rv);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int sum = rv[i] + o16[i];
+          o16[i] = sat16(sum);
+          rsat += o16[i] != sum;
+        }
+        *reinterpret_cast<uint4*>(out + o) = pack8(o16);
+      } else {
+        *reinterpret_cast<uint4*>(gi + o) = pack8(o16);
+      }
+    }
+  }
+  __shared__ unsigned long long gsum[d];
+  for (int i = threadIdx.x; i < d; i += blockDim.x) gsum[i] = 0;
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    if (gacc[i]) atomicAdd(&gsum[8 * lane + i], (unsigned long long)gacc[i]);
+  __syncthreads();
+  for (int i = threadIdx.x; i < d; i += blockDim.x)
+    if (gsum[i]) atomicAdd(reinterpret_cast<unsigned long long*>(&gw[i]), gsum[i]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    nsat += __shfl_xor_sync(0xffffffffu, nsat, o);
+    rsat += __shfl_xor_sync(0xffffffffu, rsat, o);
+  }
+  if (lane == 0 && nsat) atomicAdd(sat, nsat);
+  if (lane == 0 && rsat) atomicAdd(res_sat, rsat);
+}
+
 // nsrl-train/src/lib.rs:16623-16747 for one (query row, head, sequence):
 // dP[j] = sat(rhu(dC[t] . V[j], 15)) for j <= t, then
 // dL[j] = sat(rhu(P[j] * (dP[j] - rhu(sum_j dP[j] P[j], 15)) * 22713, 30)),
