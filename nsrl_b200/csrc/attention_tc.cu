@@ -71,6 +71,7 @@ constexpr size_t SMEM_BYTES = (size_t)GROUPS * GROUP_BYTES + 1024;
 
 struct Maps {
   CUtensorMap q_hi, q_lo, k_hi, k_lo, vt_hi, vt_lo;  // q: 128-row boxes, k: 32-row boxes, vt: 64 x 32-byte boxes
+  CUtensorMap p_hi, p_lo;  // P planes [B*H][S][S], 128 x 32-byte boxes (stores of the cached P)
 };
 
 struct Args {
@@ -82,8 +83,7 @@ struct Args {
   unsigned long long* ctx_l1;
   long long ldc;
   int16_t* probs;    // optional P [B][H][S][S]: the visited key tiles only, zeros above the diagonal
-  int8_t* probs_hi;  // optional P as byte planes [B][H][S][S], the same entries
-  uint8_t* probs_lo;
+  int pstore;        // write P as byte planes [B][H][S][S] (the same entries) through maps.p_hi / p_lo
   nsrl_device_status* st;
 };
 
@@ -296,7 +296,8 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
       mbar_init(&ctl->s_full[i], 1);
       mbar_init(&ctl->s_empty[i], SOFTMAX_WARPS);
       mbar_init(&ctl->p_full[i], SOFTMAX_WARPS);
-      mbar_init(&ctl->p_empty[i], 1);
+      // the MMAs that read the P buffer, and (storing P) the TMA store that reads it
+      mbar_init(&ctl->p_empty[i], a.pstore ? 2 : 1);
     }
     mbar_init(&ctl->o_full, 1);
     fence_barrier_init();
@@ -382,12 +383,19 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
         }
       }
       // last pass: O += P(j) V(j), one 32-key K step per tile
+      const int pz = b * a.H + h;  // this (sequence, head)'s P matrix
       for (int j = 0; j < ntiles; ++j, ++it) {
         const int s = it % ST;
         wait_bar(&ctl->full[s], (it / ST) & 1, ctl, a.st);
         const int pb = j & 1;
         wait_bar(&ctl->p_full[pb], (j >> 1) & 1, ctl, a.st);
         tc_fence_after();
+        if (a.pstore) {  // the cached P of rows q0.. (keys j*32 ..): straight from the MMA's P tile
+          const uint8_t* pt = sm + OFF_P + pb * 2 * PLANE_P;
+          tma_store_3d(&maps.p_hi, pt, j * KT, q0, pz);
+          tma_store_3d(&maps.p_lo, pt + PLANE_P, j * KT, q0, pz);
+          bulk_commit();
+        }
         const uint32_t vh = smem_u32(sm + OFF_STAGE + s * STAGE_BYTES), vl = vh + PLANE_V;
         const uint32_t ph = smem_u32(sm + OFF_P + pb * 2 * PLANE_P), pl = ph + PLANE_P;
         const uint64_t aph = sdesc_k32(ph), apl = sdesc_k32(pl);
@@ -399,8 +407,13 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
         umma_i8(tmem + O_LL, apl, bvl, pv_uu, acc);
         umma_commit(&ctl->p_empty[pb]);
         umma_commit(&ctl->empty[s]);
+        if (a.pstore && j > 0) {  // the previous tile's store has read its P buffer
+          bulk_wait_read<1>();
+          mbar_arrive(&ctl->p_empty[pb ^ 1]);
+        }
       }
       umma_commit(&ctl->o_full);
+      if (a.pstore) bulk_wait_all();  // the P stores are complete before the CTA (and its shared memory) ends
       // every MMA of this CTA completes before TMEM is released
       mbar_wait(&ctl->o_full, 0, a.st);
     }
@@ -604,11 +617,6 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
       const uint32_t off = swz32_chunk((uint32_t)row, (uint32_t)g);
       *reinterpret_cast<uint4*>(ph + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
       *reinterpret_cast<uint4*>(pl + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-      if (a.probs_hi && row_live && key0 < S) {  // the cached P as planes (S % 16 == 0: 16-byte rows)
-        const long long o = (((long long)b * a.H + h) * S + qi) * (long long)S + key0;
-        *reinterpret_cast<uint4*>(a.probs_hi + o) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-        *reinterpret_cast<uint4*>(a.probs_lo + o) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-      }
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&ctl->p_full[pb]);
@@ -710,6 +718,22 @@ size_t chunk_seqs(size_t B, size_t S, size_t H) {
   return std::max<size_t>(1, std::min<size_t>(B, ((size_t)4 << 30) / per));
 }
 
+// 3-D uint8 map of the P planes [BH][S][S] (keys contiguous), box [1][QT
+// rows][KT bytes], 32-byte swizzle (the layout of the MMA's P tile); rows and
+// keys past S lie outside the tensor, so a store of the last query tile stops
+// at the sequence's end.
+bool make_p_map(CUtensorMap* m, const void* ptr, uint64_t S, uint64_t BH) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {S, S, BH};
+  cuuint64_t strides[2] = {S, S * S};
+  cuuint32_t box[3] = {(cuuint32_t)KT, (cuuint32_t)QT, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(ptr), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace
 
 bool attention_tc_supported(size_t S, size_t d, size_t H) {
@@ -734,8 +758,13 @@ cudaError_t launch_attention_tc(const Planes& qkv, const VtPlanes& vt, size_t B,
   const bool ok =
       make_map(&m.q_hi, qkv.hi, 3 * d, T, qkv.ld, 64, QT) && make_map(&m.q_lo, qkv.lo, 3 * d, T, qkv.ld, 64, QT) &&
       make_map(&m.k_hi, qkv.hi, 3 * d, T, qkv.ld, 64, KT) && make_map(&m.k_lo, qkv.lo, 3 * d, T, qkv.ld, 64, KT) &&
-      make_map(&m.vt_hi, vt.hi, S, B * H * HD, S, KT, HD) && make_map(&m.vt_lo, vt.lo, S, B * H * HD, S, KT, HD);
+      make_map(&m.vt_hi, vt.hi, S, B * H * HD, S, KT, HD) && make_map(&m.vt_lo, vt.lo, S, B * H * HD, S, KT, HD) &&
+      (!probs_planes || (make_p_map(&m.p_hi, probs_planes->hi, S, B * H) && make_p_map(&m.p_lo, probs_planes->lo, S, B * H)));
   if (!ok) return cudaErrorNotSupported;
+  if (!probs_planes) {
+    m.p_hi = m.q_hi;  // unused
+    m.p_lo = m.q_lo;
+  }
   Args a{};
   a.S = (int)S;
   a.d = (int)d;
@@ -746,8 +775,7 @@ cudaError_t launch_attention_tc(const Planes& qkv, const VtPlanes& vt, size_t B,
   a.ctx_l1 = ctx.l1;
   a.ldc = (long long)ctx.ld;
   a.probs = probs;
-  a.probs_hi = probs_planes ? probs_planes->hi : nullptr;
-  a.probs_lo = probs_planes ? probs_planes->lo : nullptr;
+  a.pstore = probs_planes ? 1 : 0;
   a.st = st;
   a.wscr = wscr;
   a.wstride = (long long)attention_tc_wstride(S);
