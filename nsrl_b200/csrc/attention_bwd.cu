@@ -254,7 +254,7 @@ __global__ void __launch_bounds__(256) sq_transpose_kernel(const int16_t* __rest
 struct DlArgs {
   const int16_t* dC;
   long long ldc;
-  const int8_t* v_hi;  // V planes [T][d]
+  const int8_t* v_hi;  // V planes [T][d] (row stride d)
   const uint8_t* v_lo;
   int d;
   const int16_t* P;
@@ -976,7 +976,8 @@ cudaError_t launch_attention_backward_tc(const int16_t* q, const int16_t* k, con
                                          const int16_t* P, const int16_t* dC, size_t ldc, size_t B, size_t S, size_t d,
                                          size_t H, int16_t* dl, int16_t* dq, int16_t* dk, int16_t* dv,
                                          void* scratch, size_t scratch_bytes, nsrl_device_status* st,
-                                         cudaStream_t s, const GradPlanes* planes, const Planes* p_planes) {
+                                         cudaStream_t s, const GradPlanes* planes, const Planes* p_planes,
+                                         const Planes* qkv_planes) {
   const size_t hd = d / H;
   // 8-byte loads of P / dL rows, dC, q, k, v need S, ld, ldc multiples of 4
   if ((hd != 16 && hd != 64) || S % 4 != 0 || ld % 4 != 0 || ldc % 4 != 0 || d % 16 != 0 || S > 16384 ||
@@ -1005,36 +1006,43 @@ cudaError_t launch_attention_backward_tc(const int16_t* q, const int16_t* k, con
   uint8_t* ltl = take(B * H * S * S);
   cudaError_t e = cudaSuccess;
   const double pairs = (double)B * (double)H * (double)S * (double)(S + 1) / 2.0;
+  if ((p_planes || qkv_planes) && !attention_kv_tc_supported(S, d, H)) return cudaErrorInvalidValue;
   if (attention_kv_tc_supported(S, d, H)) {
     // Tensor-core path (head_dim 64, S % 16 == 0): V, K, Q, dC as row-major
-    // planes [B*S][d], P (unless given as planes) and dL as causal planes
-    // [B*H][S][S]; the dL kernel reads and writes planes, one persistent
-    // tcgen05 kernel forms dK, dV and dQ.  The K^T / Q^T / dC^T / P^T / dL^T
-    // scratch buffers hold these instead; the int16 dl is not written.
-    {
-      ProfScope prof("attention_bwd_planes", s, 0.0, 16.0 * (double)B * S * d);
-      e = launch_split_planes(v, B * S, d, ld, Planes{vph, vpl, nullptr, d}, s);
-      if (e == cudaSuccess) e = launch_split_planes(k, B * S, d, ld, Planes{kth, ktl, nullptr, d}, s);
-      if (e == cudaSuccess) e = launch_split_planes(q, B * S, d, ld, Planes{qth, qtl, nullptr, d}, s);
-      if (e == cudaSuccess) e = launch_split_planes(dC, B * S, d, ldc, Planes{cth, ctl, nullptr, d}, s);
+    // planes [B*S][d] (q|k|v as given, or split here), P (unless given as
+    // planes) and dL as causal planes [B*H][S][S]; the dL kernel reads and
+    // writes planes, one persistent tcgen05 kernel forms dK, dV and dQ.  The
+    // K^T / Q^T / dC^T / P^T / dL^T scratch buffers hold these instead; the
+    // int16 dl is not written.
+    Planes qp{qth, qtl, nullptr, d}, kp{kth, ktl, nullptr, d}, vp{vph, vpl, nullptr, d};
+    if (qkv_planes) {
+      const Planes& a = *qkv_planes;
+      qp = Planes{a.hi, a.lo, nullptr, a.ld};
+      kp = Planes{a.hi + d, a.lo + d, nullptr, a.ld};
+      vp = Planes{a.hi + 2 * d, a.lo + 2 * d, nullptr, a.ld};
+    } else {
+      e = launch_split_planes(v, B * S, d, ld, vp, s);
+      if (e == cudaSuccess) e = launch_split_planes(k, B * S, d, ld, kp, s);
+      if (e == cudaSuccess) e = launch_split_planes(q, B * S, d, ld, qp, s);
       if (e != cudaSuccess) return e;
     }
+    e = launch_split_planes(dC, B * S, d, ldc, Planes{cth, ctl, nullptr, d}, s);
+    if (e != cudaSuccess) return e;
     const Planes pp = p_planes ? *p_planes : Planes{pth, ptl, nullptr, S};
     if (!p_planes) {
       e = launch_split_causal(P, B * H, S, pth, ptl, s);
       if (e != cudaSuccess) return e;
     }
     {
-      DlArgs la{dC, (long long)ldc, vph, vpl, (int)d, nullptr, (int)S, (int)H, nullptr, st, pp.hi, pp.lo, lth, ltl};
+      DlArgs la{dC, (long long)ldc, vp.hi, vp.lo, (int)vp.ld, nullptr, (int)S, (int)H, nullptr, st, pp.hi, pp.lo, lth, ltl};
       ProfScope prof("attention_bwd_dl", s, 2.0 * (double)hd * pairs,
                      2.0 * 2.0 * (double)B * H * S * S + 4.0 * (double)B * S * d);
       attn_bwd_dl_kernel<64, true><<<dim3((unsigned)((S + BQ - 1) / BQ), (unsigned)H, (unsigned)B), 128, 0, s>>>(la);
       e = cudaGetLastError();
       if (e != cudaSuccess) return e;
     }
-    const Planes kp{kth, ktl, nullptr, d};
-    return launch_attention_kv_tc(Planes{lth, ltl, nullptr, S}, pp, Planes{qth, qtl, nullptr, d},
-                                  Planes{cth, ctl, nullptr, d}, B, S, d, H, planes ? nullptr : dk,
+    return launch_attention_kv_tc(Planes{lth, ltl, nullptr, S}, pp, qp, Planes{cth, ctl, nullptr, d}, B, S, d, H,
+                                  planes ? nullptr : dk,
                                   planes ? nullptr : dv, planes ? planes[1] : GradPlanes{},
                                   planes ? planes[2] : GradPlanes{}, st, s, &kp, planes ? nullptr : dq,
                                   planes ? planes[0] : GradPlanes{});

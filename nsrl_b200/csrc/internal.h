@@ -61,6 +61,7 @@ struct GemmArgs {
   size_t ldskip;
   unsigned long long* sat_counter;
   VtPlanes vt;
+  bool v_rows = false;  // QKV_VT: the v columns also go to yp (row-major q|k|v planes)
   nsrl_device_status* st;
   // Backward-input form (linear.rs:594-640): the sum is an i64 (no prefix
   // rule) requantised by requantize_i64_to_i16; A holds the prescaled grads.
@@ -151,7 +152,7 @@ cudaError_t launch_attention_backward_tc(const int16_t* q, const int16_t* k, con
                                          size_t H, int16_t* dl, int16_t* dq, int16_t* dk, int16_t* dv,
                                          void* scratch, size_t scratch_bytes, nsrl_device_status* st,
                                          cudaStream_t s, const GradPlanes* planes = nullptr,
-                                         const Planes* p_planes = nullptr);
+                                         const Planes* p_planes = nullptr, const Planes* qkv_planes = nullptr);
 
 // Key and query sides of the attention backward on the tensor cores
 // (head_dim 64): dK = dL^T Q, dV = P^T dC and, with kp, dQ = dL K per

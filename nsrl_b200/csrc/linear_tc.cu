@@ -68,6 +68,7 @@ struct TcParams {
   int8_t* vth;
   uint8_t* vtl;
   int vt_S, vt_H, vt_hd, vt_col0;  // QKV_VT: output columns >= vt_col0 go to the transposed planes
+  bool v_rows;                      // QKV_VT: and to the row-major planes as well
   bool small_acc;                   // K * 127 * 32767 < 2^30: every accumulator is below 2^30
   bool wide;                        // i64 accumulator, requantize_i64_to_i16 (backward-input linears)
   nsrl_device_status* st;
@@ -500,7 +501,8 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
                   p.vtl[off] = (uint8_t)(v[i] & 255);
                 }
               }
-            } else {
+            }
+            if (EPI != (int)Epi::QKV_VT || nh < p.vt_col0 || p.v_rows) {
               if (p.yl1) {
 #pragma unroll
                 for (int i = 0; i < 16; ++i) l1 += (i < nv) ? (unsigned)abs(v[i]) : 0u;
@@ -602,6 +604,10 @@ __global__ void gemm_simt_kernel(const SimtParams s) {
     const long long off = ((long long)(b * p.vt_H + c / p.vt_hd) * p.vt_hd + c % p.vt_hd) * p.vt_S + spos;
     p.vth[off] = (int8_t)(v >> 8);
     p.vtl[off] = (uint8_t)(v & 255);
+    if (p.v_rows) {
+      p.yh[(long long)m * p.ldp + n] = (int8_t)(v >> 8);
+      p.yl[(long long)m * p.ldp + n] = (uint8_t)(v & 255);
+    }
   } else {
     if (s.epi == (int)Epi::QKV_VT && p.y) p.y[(long long)m * p.ldy + n] = v;
     p.yh[(long long)m * p.ldp + n] = (int8_t)(v >> 8);
@@ -857,6 +863,7 @@ cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t stream) {
   p.vt_H = a.vt.H;
   p.vt_hd = a.vt.hd;
   p.vt_col0 = a.epi == Epi::QKV_VT ? 2 * (int)a.seg[0].rows : INT_MAX;
+  p.v_rows = a.v_rows;
   p.small_acc = (unsigned long long)a.K * 127ull * 32767ull < (1ull << 30);
   p.wide = a.wide;
   p.st = a.st;

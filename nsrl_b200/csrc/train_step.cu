@@ -282,11 +282,11 @@ cudaError_t attn_backward(const int16_t* q, const int16_t* k, const int16_t* v, 
                           const int16_t* dC, size_t ldc, size_t B, size_t S, size_t d, size_t H, int16_t* dL,
                           int16_t* dq, int16_t* dk, int16_t* dv, void* scratch, size_t scratch_bytes,
                           nsrl_device_status* st, cudaStream_t s, const GradPlanes* planes = nullptr,
-                          const Planes* p_planes = nullptr) {
+                          const Planes* p_planes = nullptr, const Planes* qkv_planes = nullptr) {
   const cudaError_t tce = launch_attention_backward_tc(q, k, v, ld, P, dC, ldc, B, S, d, H, dL, dq, dk, dv, scratch,
-                                                       scratch_bytes, st, s, planes, p_planes);
+                                                       scratch_bytes, st, s, planes, p_planes, qkv_planes);
   if (tce != cudaErrorNotSupported) return tce;
-  if (p_planes) return cudaErrorInvalidValue;  // only the tensor-core path reads P as planes
+  if (p_planes || qkv_planes) return cudaErrorInvalidValue;  // only the tensor-core path reads planes
   if (planes) {
     const cudaError_t e = attn_backward(q, k, v, ld, P, dC, ldc, B, S, d, H, dL, dq, dk, dv, scratch, scratch_bytes,
                                         st, s, nullptr);
@@ -336,6 +336,9 @@ struct LayerCache {
   // hi then lo, in the causal form the tensor-core forward writes
   int16_t *in, *qkv, *P, *ares, *up, *gate, *out;
   bool p_planes;
+  // q|k|v as row-major byte planes [T][3d] (the tensor-core attention's input;
+  // with p_planes the backward reads them too and qkv is not written)
+  Planes pqkv;
   // inputs of the linears as byte planes (+ row L1): the forward GEMMs read
   // them and the weight gradients read them again in the backward
   Planes an, ctx, mn, gated;  // q|k|v input, o input, up|gate input, down input
@@ -360,7 +363,6 @@ struct StepLayout {
   int8_t* headT;
   nsrl_fixed_scale* ident;
   unsigned long long* fwd_res;
-  Planes pqkv;  // q|k planes of the tensor-core attention (v goes to vt)
   Planes pg[3];  // prescaled planes of dQ, dK, dV
   VtPlanes vt;
   void* abw;    // scratch of the tensor-core attention backward
@@ -390,6 +392,7 @@ void carve_step(const nsrl_train_model* m, size_t W, bool rms, void* base, StepL
     lc.ctx = c.planes(T, d, true);
     lc.P = c.take<int16_t>(W * H * S * S);
     lc.p_planes = false;
+    lc.pqkv = attention_tc_supported(S, d, H) ? c.planes(T, 3 * d, false) : Planes{nullptr, nullptr, nullptr, 3 * d};
     lc.ares = c.take<int16_t>(T * d);
     lc.mn = c.planes(T, d, true);
     lc.up = c.take<int16_t>(T * F);
@@ -416,10 +419,8 @@ void carve_step(const nsrl_train_model* m, size_t W, bool rms, void* base, StepL
   o.headT = c.take<int8_t>(d * 256);
   o.ident = c.take<nsrl_fixed_scale>(std::max<size_t>(wide, 256));
   o.fwd_res = c.take<unsigned long long>(4);
-  o.pqkv = Planes{nullptr, nullptr, nullptr, 3 * d};
   o.vt = VtPlanes{nullptr, nullptr, (int)S, (int)H, (int)(d / H), nullptr};
   if (attention_tc_supported(S, d, H)) {
-    o.pqkv = c.planes(T, 3 * d, false);
     o.vt.hi = c.take<int8_t>(T * d);
     o.vt.lo = c.take<uint8_t>(T * d);
     const size_t ws = attention_tc_scratch_bytes(W, S, d, H);
@@ -710,9 +711,11 @@ nsrl_status nsrl_train_windows(const nsrl_train_model* m, const uint8_t* context
       TS_TRY(launch_rms_norm(c.in, T, d, ly.attn_gamma, 1, nullptr, c.an, st, s), "rms");
     else
       TS_TRY(launch_split_planes(c.in, T, d, d, c.an, s), "split");
-    // Q|K|V: with the tcgen05 attention, one GEMM writes the int16 rows (the
-    // cache the backward reads), the Q|K planes and the transposed V planes.
+    // Q|K|V: with the tcgen05 attention, one GEMM writes the row-major q|k|v
+    // planes (cached for the backward) and the transposed V planes; the int16
+    // rows only when the backward cannot take the planes.
     const bool tc_attn = o.vt.hi && tma_supported() && attention_tc_supported(S, d, H);
+    const bool planes_bwd = tc_attn && attention_kv_tc_supported(S, d, H);
     {
       GemmArgs g{};
       g.a_hi = c.an.hi;
@@ -725,11 +728,12 @@ nsrl_status nsrl_train_windows(const nsrl_train_model* m, const uint8_t* context
       for (int i = 0; i < 3; ++i)
         g.seg[i] = WeightSeg{ly.lin[i].weights, ly.lin[i].bias, ly.lin[i].scales, d};
       g.epi = tc_attn ? Epi::QKV_VT : Epi::I16;
-      g.y = c.qkv;
+      g.y = planes_bwd ? nullptr : c.qkv;
       g.ldy = 3 * d;
       if (tc_attn) {
-        g.yp = o.pqkv;
+        g.yp = c.pqkv;
         g.vt = o.vt;
+        g.v_rows = planes_bwd;
       }
       g.st = st;
       TS_TRY(launch_gemm(g, s), "qkv");
@@ -741,14 +745,14 @@ nsrl_status nsrl_train_windows(const nsrl_train_model* m, const uint8_t* context
       // each 128-query tile, zeros above the diagonal; as byte planes when the
       // tensor-core backward takes the shape (it reads them in place)
       TS_TRY(cudaMemsetAsync(c.ctx.l1, 0, T * sizeof(unsigned long long), s), "memset");
-      const bool pl = attention_kv_tc_supported(S, d, H);
       const Planes pv = p_cache_planes(c, W * H * S * S, S);
-      const cudaError_t e = launch_attention_tc(o.pqkv, o.vt, W, S, d, H, true, c.ctx, o.vt.wscr, st, s,
-                                                pl ? nullptr : c.P, pl ? &pv : nullptr);
-      if (e != cudaErrorNotSupported) {
+      const cudaError_t e = launch_attention_tc(c.pqkv, o.vt, W, S, d, H, true, c.ctx, o.vt.wscr, st, s,
+                                                planes_bwd ? nullptr : c.P, planes_bwd ? &pv : nullptr);
+      // without the int16 q|k|v rows there is no other path
+      if (e != cudaErrorNotSupported || planes_bwd) {
         TS_TRY(e, "attention");
         done = true;
-        c.p_planes = pl;
+        c.p_planes = planes_bwd;
       }
     }
     if (!done) {  // int16 context in a backward buffer that is free during the forward
@@ -865,8 +869,10 @@ nsrl_status nsrl_train_windows(const nsrl_train_model* m, const uint8_t* context
     GradPlanes gp[3];
     for (int i = 0; i < 3; ++i) gp[i] = GradPlanes{ly.lin[i].scales, o.pg[i].hi, o.pg[i].lo};
     const Planes pv = p_cache_planes(c, W * H * S * S, S);
-    TS_TRY(attn_backward(c.qkv, c.qkv + d, c.qkv + 2 * d, 3 * d, c.p_planes ? nullptr : c.P, o.gctx, d, W, S, d, H,
-                         o.dL, o.dq, o.dk, o.dv, o.abw, o.abw_bytes, st, s, gp, c.p_planes ? &pv : nullptr),
+    TS_TRY(attn_backward(c.p_planes ? nullptr : c.qkv, c.p_planes ? nullptr : c.qkv + d,
+                         c.p_planes ? nullptr : c.qkv + 2 * d, 3 * d, c.p_planes ? nullptr : c.P, o.gctx, d, W, S, d,
+                         H, o.dL, o.dq, o.dk, o.dv, o.abw, o.abw_bytes, st, s, gp, c.p_planes ? &pv : nullptr,
+                         c.p_planes ? &c.pqkv : nullptr),
            "attention backward");
     int16_t* gin[3] = {o.gq, o.gk, o.gv};
     for (int i = 0; i < 3; ++i)

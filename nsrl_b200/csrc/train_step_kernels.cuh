@@ -678,12 +678,15 @@ __global__ void __launch_bounds__(256) rms_backward_vec_kernel(
     }
     int nm[RPW][8], sg[RPW][8];
     long long mdot[RPW];
+    bool fast[RPW];
 #pragma unroll
     for (int k = 0; k < RPW; ++k) {
       long long dot = 0;
+      unsigned nmax = 0;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         nm[k][i] = (int)(((long long)xv[k][i] * inv[k] + (1ll << 14)) >> 15);
+        nmax = max(nmax, (unsigned)abs(nm[k][i]));
         const long long proj = ((long long)(xv[k][i] * wv[i]) * inv[k] + (1ll << 29)) >> 30;
         const bool active = ok[k] && proj >= -32768 && proj <= 32767;
         sg[k][i] = active ? ((gv[k][i] * wv[i] + (1 << 14)) >> 15) : 0;
@@ -695,6 +698,10 @@ __global__ void __launch_bounds__(256) rms_backward_vec_kernel(
       const long long tq = dot + den / 2;
       mdot[k] = tq / den;
       if ((tq % den) != 0 && tq < 0) --mdot[k];
+      // 32-bit cross terms when every |nm * mdot| + 2^14 of the row fits an int
+      nmax = __reduce_max_sync(0xffffffffu, nmax);
+      const unsigned long long amd = (unsigned long long)(mdot[k] < 0 ? -mdot[k] : mdot[k]);
+      fast[k] = amd < (1ull << 31) && (unsigned long long)nmax * amd < (1ull << 31) - (1ull << 14);
     }
 #pragma unroll
     for (int k = 0; k < RPW; ++k) {
@@ -703,13 +710,27 @@ __global__ void __launch_bounds__(256) rms_backward_vec_kernel(
       uint4 rn = make_uint4(0, 0, 0, 0);
       if (res) rn = *reinterpret_cast<const uint4*>(res + o);
       int o16[8];
+      if (fast[k]) {
+        // |cross| < 2^16 and |sg| <= 2^15, so |(sg - cross) inv| < 2^47 and
+        // the rounded shift fits an int
+        const int md = (int)mdot[k];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const long long cross = ((long long)nm[k][i] * mdot[k] + (1ll << 14)) >> 15;
-        const long long gg = (((long long)sg[k][i] - cross) * inv[k] + (1ll << 29)) >> 30;
-        const int cl = sat_i16(gg);
-        nsat += (long long)cl != gg;
-        o16[i] = cl;
+        for (int i = 0; i < 8; ++i) {
+          const int cross = (nm[k][i] * md + (1 << 14)) >> 15;
+          const int gg = (int)(((long long)(sg[k][i] - cross) * inv[k] + (1ll << 29)) >> 30);
+          const int cl = max(-32768, min(32767, gg));
+          nsat += cl != gg;
+          o16[i] = cl;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const long long cross = ((long long)nm[k][i] * mdot[k] + (1ll << 14)) >> 15;
+          const long long gg = (((long long)sg[k][i] - cross) * inv[k] + (1ll << 29)) >> 30;
+          const int cl = sat_i16(gg);
+          nsat += (long long)cl != gg;
+          o16[i] = cl;
+        }
       }
       if (res) {
         int rv[8];
