@@ -18,11 +18,12 @@
 //
 // Persistent kernel, one CTA per SM; a work item is dK or dV of one 128-key
 // tile, or dQ of one 128-query tile, of one (sequence, head); items with the
-// most 32-wide steps first.  10 warps: warp 0 issues TMA (a 6-stage ring of
-// steps: a dL or P tile of 32 x 128 or 128 x 32 bytes per plane and a Q, K or
-// dC tile of 32 x 64 bytes per plane), warp 1 owns TMEM (two accumulator sets
-// of 3 x 64 columns) and issues the MMAs, warps 2..9 run the epilogue of one
-// item while the next accumulates.
+// most steps first.  10 warps: warp 0 issues TMA (a 6-stage ring of 64-wide
+// steps: a dL or P tile of 64 x 128 or 128 x 64 bytes per plane and a Q, K or
+// dC tile of 64 x 64 bytes per plane; larger boxes, half the TMA issues of
+// 32-wide steps), warp 1 owns TMEM (two accumulator sets of 3 x 64 columns)
+// and issues two K = 32 sub-steps of MMAs per stage, warps 2..9 run the
+// epilogue of one item while the next accumulates.
 #include <algorithm>
 
 #include "common.cuh"
@@ -31,23 +32,27 @@
 namespace nsrl {
 namespace {
 
-constexpr int KQ = 32;    // queries per MMA K step
+constexpr int KQ = 64;    // queries (dK, dV) or keys (dQ) per stage: two K = 32 MMA sub-steps
 constexpr int KK = 128;   // keys per work item (MMA M)
 constexpr int KD = 64;    // head dim (MMA N)
 constexpr int KST = 6;    // stages
-constexpr int TM = KQ * KK;  // 4 KB: one plane of a dL or P step, [32 queries][128 keys] or [128 queries][32 keys]
-constexpr int TX = KQ * KD;  // 2 KB: one plane of a Q, K or dC step, [32 rows][64 dims]
+constexpr int TM = KQ * KK;  // 8 KB: one plane of a dL or P stage, [64 queries][128 keys] or [128 queries][64 keys]
+constexpr int TX = KQ * KD;  // 4 KB: one plane of a Q, K or dC stage, [64 rows][64 dims]
 constexpr int OFF_AH = 0, OFF_AL = TM, OFF_BH = 2 * TM, OFF_BL = 2 * TM + TX;
-constexpr int KSTAGE = 2 * TM + 2 * TX;  // 12 KB
+constexpr int KSTAGE = 2 * TM + 2 * TX;  // 24 KB
 constexpr int KEPI = 8;                  // epilogue warps: two per TMEM lane quarter
 constexpr int KTHREADS = 64 + 32 * KEPI;
 constexpr uint32_t KTMEM = 512;
 constexpr uint32_t ACC_COLS = 256;       // one item's hh, mid, ll (3 x 64) per buffer, two buffers
-constexpr size_t KSMEM = (size_t)KST * KSTAGE + 1024 + 256;
+// ring + 1024-byte alignment slack + barriers (full/empty per stage, two acc
+// pairs) and the TMEM slot / skip words
+constexpr size_t KBAR_BYTES = (2 * KST + 4) * 8 + 8;
+static_assert(KBAR_BYTES <= 512, "barrier area");
+constexpr size_t KSMEM = (size_t)KST * KSTAGE + 1024 + 512;
 
 struct KvMaps {
   CUtensorMap l_hi, l_lo, p_hi, p_lo, q_hi, q_lo, c_hi, c_lo;
-  CUtensorMap lr_hi, lr_lo, k_hi, k_lo;  // dL row tiles (K-major, 128 x 32) and K, for dQ
+  CUtensorMap lr_hi, lr_lo, k_hi, k_lo;  // dL row tiles (K-major, 128 x 64) and K, for dQ
 };
 
 struct KvArgs {
@@ -63,10 +68,10 @@ struct KvArgs {
 // A work item is dK (kind 0) or dV (kind 1) of the 128-key tile at k0, or dQ
 // (kind 2) of the 128-query tile at k0, of one (sequence, head).  Level L
 // holds the key tile 128 L and the query tile 128 (nk - 1 - L): both take
-// about (S - 128 L) / 32 steps, and the levels run longest first.
+// about (S - 128 L) / 64 steps, and the levels run longest first.
 struct KvItem {
   int kind, h, b, k0;
-  int x0, x1;  // the steps' queries (dK, dV) or keys (dQ): [x0, x1) by 32
+  int x0, x1;  // the steps' queries (dK, dV) or keys (dQ): [x0, x1) by KQ
 };
 __device__ __forceinline__ KvItem kv_item(const KvArgs& a, int i) {
   const int per = a.kinds * a.B * a.H;
@@ -87,11 +92,11 @@ __device__ __forceinline__ KvItem kv_item(const KvArgs& a, int i) {
   return it;
 }
 
-// K-major tile of 32-byte rows (32 keys of one query), 32-byte swizzle:
-// 8-row groups 256 bytes apart.
-__device__ __forceinline__ uint64_t sdesc_k32(uint32_t saddr) {
-  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(256 >> 4) << 32) |
-         ((uint64_t)1 << 46) | ((uint64_t)6 << 61);
+// K-major tile of 64-byte rows (64 keys of one query), 64-byte swizzle:
+// 8-row groups 512 bytes apart; a K = 32 sub-step starts 32 bytes into the row.
+__device__ __forceinline__ uint64_t sdesc_k64(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(512 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)4 << 61);
 }
 
 // MN-major operand tiles: rows of 128 (keys) or 64 (dims) bytes, one per
@@ -220,14 +225,22 @@ __global__ void __launch_bounds__(KTHREADS, 1) attn_kv_tc_kernel(const __grid_co
           }
           tc_fence_after();
           const uint32_t base = smem_u32(sm + s * KSTAGE);
-          const uint64_t ah = kq ? sdesc_k32(base + OFF_AH) : sdesc_mn(base + OFF_AH, 1024, LAYOUT_SW128);
-          const uint64_t al = kq ? sdesc_k32(base + OFF_AL) : sdesc_mn(base + OFF_AL, 1024, LAYOUT_SW128);
-          const uint64_t bhd = sdesc_mn(base + OFF_BH, 512, LAYOUT_SW64), bld = sdesc_mn(base + OFF_BL, 512, LAYOUT_SW64);
-          const uint32_t acc = x > w.x0 ? 1u : 0u;
-          umma_i8(d, ah, bhd, i_hh, acc);            // hh
-          umma_i8(d + 64, ah, bld, i_hl, acc);       // mid: hi x lo
-          umma_i8(d + 64, al, bhd, i_lh, 1u);        //      lo x hi
-          umma_i8(d + 128, al, bld, i_ll, acc);      // ll
+#pragma unroll
+          for (int j = 0; j < KQ / 32; ++j) {
+            // sub-step j: rows 32 j .. of the MN-major tiles (4096 / 2048 bytes
+            // per 32 rows), or bytes 32 j .. of the K-major dL rows
+            const uint64_t ah = kq ? sdesc_k64(base + OFF_AH + 32 * j)
+                                   : sdesc_mn(base + OFF_AH + 4096 * j, 1024, LAYOUT_SW128);
+            const uint64_t al = kq ? sdesc_k64(base + OFF_AL + 32 * j)
+                                   : sdesc_mn(base + OFF_AL + 4096 * j, 1024, LAYOUT_SW128);
+            const uint64_t bhd = sdesc_mn(base + OFF_BH + 2048 * j, 512, LAYOUT_SW64);
+            const uint64_t bld = sdesc_mn(base + OFF_BL + 2048 * j, 512, LAYOUT_SW64);
+            const uint32_t acc = (x > w.x0 || j > 0) ? 1u : 0u;
+            umma_i8(d, ah, bhd, i_hh, acc);            // hh
+            umma_i8(d + 64, ah, bld, i_hl, acc);       // mid: hi x lo
+            umma_i8(d + 64, al, bhd, i_lh, 1u);        //      lo x hi
+            umma_i8(d + 128, al, bld, i_ll, acc);      // ll
+          }
           umma_commit(&empty[s]);
         }
         umma_commit(&acc_full[buf]);
