@@ -239,7 +239,9 @@ __device__ __forceinline__ void store16_i16(int16_t* dst, const uint32_t (&o)[8]
   }
 }
 
-template <int EPI>
+// WIDE (= p.wide) is a template parameter so that each kernel holds only one
+// requantisation form: a smaller epilogue for the instruction cache.
+template <int EPI, bool WIDE>
 __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_constant__ TcMaps maps, const TcParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -458,7 +460,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
           const int nv = max(0, min(16, nvalid - 16 * hf));
           const int nh = n + 16 * hf;
           int v[16];
-          if (p.wide) {
+          if (WIDE) {
             bool bad = false;
             requant_wide16(h, l, sc, v, bad, 16 * hf);
             if (bad && row_ok && nv > 0) nsrl_flag(p.st, NSRL_FLAG_LINEAR_OVERFLOW);
@@ -782,31 +784,34 @@ bool make_map(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t rows, ui
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int EPI>
+template <int EPI, bool WIDE>
 cudaError_t launch_tc(const TcMaps& maps, const TcParams& p, int grid, cudaStream_t stream) {
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<EPI, WIDE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)SMEM_BYTES);
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  gemm_tc_kernel<EPI><<<grid, THREADS, SMEM_BYTES, stream>>>(maps, p);
+  gemm_tc_kernel<EPI, WIDE><<<grid, THREADS, SMEM_BYTES, stream>>>(maps, p);
   return cudaGetLastError();
 }
 
 cudaError_t launch_tc_epi(Epi epi, const TcMaps& maps, const TcParams& p, int grid, cudaStream_t stream) {
   switch (epi) {
     case Epi::I16:
-      return launch_tc<(int)Epi::I16>(maps, p, grid, stream);
+      return p.wide ? launch_tc<(int)Epi::I16, true>(maps, p, grid, stream)
+                    : launch_tc<(int)Epi::I16, false>(maps, p, grid, stream);
     case Epi::PLANES:
-      return launch_tc<(int)Epi::PLANES>(maps, p, grid, stream);
+      return p.wide ? launch_tc<(int)Epi::PLANES, true>(maps, p, grid, stream)
+                    : launch_tc<(int)Epi::PLANES, false>(maps, p, grid, stream);
     case Epi::RESID:
-      return launch_tc<(int)Epi::RESID>(maps, p, grid, stream);
-    case Epi::GATED:
-      return launch_tc<(int)Epi::GATED>(maps, p, grid, stream);
+      return p.wide ? launch_tc<(int)Epi::RESID, true>(maps, p, grid, stream)
+                    : launch_tc<(int)Epi::RESID, false>(maps, p, grid, stream);
+    case Epi::GATED:  // the wide form takes neither of these (launch_gemm rejects it)
+      return launch_tc<(int)Epi::GATED, false>(maps, p, grid, stream);
     case Epi::QKV_VT:
-      return launch_tc<(int)Epi::QKV_VT>(maps, p, grid, stream);
+      return launch_tc<(int)Epi::QKV_VT, false>(maps, p, grid, stream);
   }
   return cudaErrorInvalidValue;
 }

@@ -687,8 +687,10 @@ __global__ void __launch_bounds__(256) rms_backward_vec_kernel(
       for (int i = 0; i < 8; ++i) {
         nm[k][i] = (int)(((long long)xv[k][i] * inv[k] + (1ll << 14)) >> 15);
         nmax = max(nmax, (unsigned)abs(nm[k][i]));
-        const long long proj = ((long long)(xv[k][i] * wv[i]) * inv[k] + (1ll << 29)) >> 30;
-        const bool active = ok[k] && proj >= -32768 && proj <= 32767;
+        // proj = t >> 30 lies in [-2^15, 2^15) iff t in [-2^45, 2^45), i.e. iff
+        // the high word of t lies in [-2^13, 2^13)
+        const long long t = (long long)(xv[k][i] * wv[i]) * inv[k] + (1ll << 29);
+        const bool active = ok[k] && (unsigned)((int)(t >> 32) + 8192) < 16384u;
         sg[k][i] = active ? ((gv[k][i] * wv[i] + (1 << 14)) >> 15) : 0;
         dot += (long long)sg[k][i] * nm[k][i];
         if (active) gacc[i] += ((long long)gv[k][i] * nm[k][i] + (1ll << 14)) >> 15;
