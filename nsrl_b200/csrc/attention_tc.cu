@@ -72,6 +72,7 @@ constexpr size_t SMEM_BYTES = (size_t)GROUPS * GROUP_BYTES + 1024;
 struct Maps {
   CUtensorMap q_hi, q_lo, k_hi, k_lo, vt_hi, vt_lo;  // q: 128-row boxes, k: 32-row boxes, vt: 64 x 32-byte boxes
   CUtensorMap p_hi, p_lo;  // P planes [B*H][S][S], 128 x 32-byte boxes (stores of the cached P)
+  CUtensorMap w;           // weight scratch as bytes [rows][2 wstride], 128 x 64-byte boxes (sum-pass stores)
 };
 
 struct Args {
@@ -537,19 +538,42 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
     };
 
     // ---- pass 1: weights and the row sum ----
-    // this thread's row of the weight scratch
+    // this thread's row of the weight scratch (read back by the last pass)
     int16_t* wrow = a.wscr + ((((long long)bl * a.H + h) * nq + qt) * QT + row) * a.wstride;
+    // Each 128 x 32 tile of weights goes through shared memory (three 8 KB
+    // buffers in the last pass's prefetch region, [row][64 bytes] with the
+    // 64-byte swizzle) and out with one TMA store, instead of 32 row-strided
+    // 16-byte stores per warp.  A buffer is rewritten three tiles later: the
+    // storing thread waits for all but its newest store to have read shared
+    // memory before it reaches the next tile's barrier, which the writers of
+    // that buffer pass only afterwards.
+    uint8_t* wst = sm + OFF_WPF;
+    const int wy = (((int)bl * a.H + h) * nq + qt) * QT;  // this CTA's first scratch row
+    const uint32_t wsw = ((uint32_t)row >> 1) & 3u;
     uint32_t rsum = 0;  // this thread's keys: at most 16384 / 2 weights below 2^15
     for (int j = 0; j < ntiles; ++j, ++it) {
       uint32_t hh[16], mid[16], ll[16], w[16];
       fetch_s((int)(it & 1), hh, mid, ll);
       weights(hh, mid, ll, live_keys(j), w);
       rsum += sum16(w);
-      uint4* dst = reinterpret_cast<uint4*>(wrow + j * KT + 16 * g);
-      dst[0] = make_uint4(__byte_perm(w[0], w[1], 0x5410), __byte_perm(w[2], w[3], 0x5410),
-                          __byte_perm(w[4], w[5], 0x5410), __byte_perm(w[6], w[7], 0x5410));
-      dst[1] = make_uint4(__byte_perm(w[8], w[9], 0x5410), __byte_perm(w[10], w[11], 0x5410),
-                          __byte_perm(w[12], w[13], 0x5410), __byte_perm(w[14], w[15], 0x5410));
+      uint8_t* tb = wst + (j % 3) * (QT * 64);
+      *reinterpret_cast<uint4*>(tb + row * 64 + (((2u * g) ^ wsw) << 4)) =
+          make_uint4(__byte_perm(w[0], w[1], 0x5410), __byte_perm(w[2], w[3], 0x5410),
+                     __byte_perm(w[4], w[5], 0x5410), __byte_perm(w[6], w[7], 0x5410));
+      *reinterpret_cast<uint4*>(tb + row * 64 + (((2u * g + 1u) ^ wsw) << 4)) =
+          make_uint4(__byte_perm(w[8], w[9], 0x5410), __byte_perm(w[10], w[11], 0x5410),
+                     __byte_perm(w[12], w[13], 0x5410), __byte_perm(w[14], w[15], 0x5410));
+      fence_proxy_async_smem();
+      named_sync_softmax(grp);
+      if (gtid == 64) {
+        tma_store_2d(&maps.w, tb, j * KT * 2, wy);
+        bulk_commit();
+        bulk_wait_read<1>();
+      }
+    }
+    if (gtid == 64) {  // the stores are complete before the last pass reads the scratch back
+      bulk_wait_all();
+      fence_proxy_async_global();
     }
     uint32_t inv = 0;
     {
@@ -759,7 +783,9 @@ cudaError_t launch_attention_tc(const Planes& qkv, const VtPlanes& vt, size_t B,
       make_map(&m.q_hi, qkv.hi, 3 * d, T, qkv.ld, 64, QT) && make_map(&m.q_lo, qkv.lo, 3 * d, T, qkv.ld, 64, QT) &&
       make_map(&m.k_hi, qkv.hi, 3 * d, T, qkv.ld, 64, KT) && make_map(&m.k_lo, qkv.lo, 3 * d, T, qkv.ld, 64, KT) &&
       make_map(&m.vt_hi, vt.hi, S, B * H * HD, S, KT, HD) && make_map(&m.vt_lo, vt.lo, S, B * H * HD, S, KT, HD) &&
-      (!probs_planes || (make_p_map(&m.p_hi, probs_planes->hi, S, B * H) && make_p_map(&m.p_lo, probs_planes->lo, S, B * H)));
+      (!probs_planes || (make_p_map(&m.p_hi, probs_planes->hi, S, B * H) && make_p_map(&m.p_lo, probs_planes->lo, S, B * H))) &&
+      make_map(&m.w, wscr, 2 * attention_tc_wstride(S), chunk_seqs(B, S, H) * H * ((S + QT - 1) / QT) * QT,
+               2 * attention_tc_wstride(S), 64, QT);
   if (!ok) return cudaErrorNotSupported;
   if (!probs_planes) {
     m.p_hi = m.q_hi;  // unused
