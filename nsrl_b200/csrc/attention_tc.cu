@@ -62,8 +62,8 @@ constexpr int OFF_P = OFF_STAGE + ST * STAGE_BYTES;
 constexpr int OFF_X = OFF_P + 2 * 2 * PLANE_P;  // row-statistics exchange: max, min, sum of [2][QT]
 constexpr int X_BYTES = 2 * QT * 8 * 3;
 constexpr int OFF_LUT = OFF_X + X_BYTES;
-constexpr int WPF_BUF = 2 * 32 * SOFTMAX_WARPS * 16;  // last-pass weights of one tile: [2 halves][256 threads] x 16 B
-constexpr int WPF_N = 4;                              // tile buffers; the copies run WPF_N - 1 tiles ahead
+constexpr int WPF_BUF = QT * KT * 2;  // weights of one tile: [128 rows][32 keys] int16, 64-byte swizzle
+constexpr int WPF_N = 4;              // last-pass weight ring slots (the sum pass stages its stores in 3 of them)
 constexpr int OFF_WPF = OFF_LUT + 512;
 constexpr int OFF_BAR = OFF_WPF + WPF_N * WPF_BUF;
 constexpr int GROUP_BYTES = (OFF_BAR + 256 + 1023) / 1024 * 1024;  // one group's region (offsets above are within it)
@@ -105,8 +105,10 @@ __device__ __forceinline__ uint32_t swz32_chunk(uint32_t r, uint32_t c) { return
 
 struct Ctl {
   uint64_t q_full, full[ST], empty[ST], s_full[2], s_empty[2], p_full[2], p_empty[2], o_full;
+  uint64_t w_ready, w_full[WPF_N], w_empty[WPF_N];  // the weight scratch written / its last-pass tile ring
   uint32_t tslot, abort;
 };
+static_assert(sizeof(Ctl) <= 256, "barrier area");
 
 __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, Ctl* c, nsrl_device_status* st) {
   if (mbar_try_wait(bar, parity)) return true;
@@ -276,6 +278,7 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
   const int S = a.S;
   const int kend = a.causal ? min(S, q0 + QT) : S;
   const int ntiles = (kend + KT - 1) / KT;
+  const int wy = ((bl * a.H + h) * nq + qt) * QT;  // first row of this group's block of the weight scratch
 
   if (threadIdx.x == 0) s_abort = timed_out(a.st) ? 1u : 0u;
   if (gtid == 0) ctl->abort = 0u;
@@ -301,6 +304,11 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
       mbar_init(&ctl->p_empty[i], a.pstore ? 2 : 1);
     }
     mbar_init(&ctl->o_full, 1);
+    mbar_init(&ctl->w_ready, 1);
+    for (int i = 0; i < WPF_N; ++i) {
+      mbar_init(&ctl->w_full[i], 1);
+      mbar_init(&ctl->w_empty[i], SOFTMAX_WARPS);
+    }
     fence_barrier_init();
   }
   if (gw == 1) {
@@ -339,6 +347,16 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
             const int vrow = (b * a.H + h) * HD;
             tma_load_2d(stg, &maps.vt_hi, &ctl->full[s], j * KT, vrow);
             tma_load_2d(stg + PLANE_V, &maps.vt_lo, &ctl->full[s], j * KT, vrow);
+            // the sum pass's weights of tile j, into ring slot j % WPF_N, once
+            // the whole scratch block is written
+            const int wb = j % WPF_N;
+            if ((j == 0 && !wait_bar(&ctl->w_ready, 0, ctl, a.st)) ||
+                (j >= WPF_N && !wait_bar(&ctl->w_empty[wb], ((j / WPF_N) - 1) & 1, ctl, a.st))) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&ctl->w_full[wb], WPF_BUF);
+            tma_load_2d(sm + OFF_WPF + wb * WPF_BUF, &maps.w, &ctl->w_full[wb], j * KT * 2, wy);
           }
         }
       }
@@ -538,8 +556,6 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
     };
 
     // ---- pass 1: weights and the row sum ----
-    // this thread's row of the weight scratch (read back by the last pass)
-    int16_t* wrow = a.wscr + ((((long long)bl * a.H + h) * nq + qt) * QT + row) * a.wstride;
     // Each 128 x 32 tile of weights goes through shared memory (three 8 KB
     // buffers in the last pass's prefetch region, [row][64 bytes] with the
     // 64-byte swizzle) and out with one TMA store, instead of 32 row-strided
@@ -548,7 +564,6 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
     // memory before it reaches the next tile's barrier, which the writers of
     // that buffer pass only afterwards.
     uint8_t* wst = sm + OFF_WPF;
-    const int wy = (((int)bl * a.H + h) * nq + qt) * QT;  // this CTA's first scratch row
     const uint32_t wsw = ((uint32_t)row >> 1) & 3u;
     uint32_t rsum = 0;  // this thread's keys: at most 16384 / 2 weights below 2^15
     for (int j = 0; j < ntiles; ++j, ++it) {
@@ -571,9 +586,10 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
         bulk_wait_read<1>();
       }
     }
-    if (gtid == 64) {  // the stores are complete before the last pass reads the scratch back
+    if (gtid == 64) {  // the stores are complete before the producer loads the tiles back
       bulk_wait_all();
       fence_proxy_async_global();
+      mbar_arrive(&ctl->w_ready);
     }
     uint32_t inv = 0;
     {
@@ -585,30 +601,18 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
     }
 
     // ---- pass 2: P = sat_i16(rhu(w * inv, 16)) as byte planes, O += P V ----
-    // This thread's 32 bytes of weights per tile, copied WPF_N - 1 tiles ahead
-    // into slot [tile % WPF_N][half][thread] (its own copies: no barrier).
-    // Every step commits one copy group, empty past the last tile, so that
-    // waiting for all but the newest WPF_N - 1 groups means tile j has landed.
-    const int sidx = gtid - 64;
-    auto wpf_issue = [&](int j) {
-      if (j < ntiles) {
-        const int16_t* src = wrow + j * KT + 16 * g;  // keys below ntiles * 32 <= wstride, written in pass 1
-        const uint32_t dst = smem_u32(sm + OFF_WPF + (j % WPF_N) * WPF_BUF + sidx * 16);
-        cp_async16(dst, src);
-        cp_async16(dst + WPF_BUF / 2, src + 8);
-      }
-      cp_async_commit();
-    };
-#pragma unroll
-    for (int k = 0; k < WPF_N - 1; ++k) wpf_issue(k);
+    // The weights come back as 128 x 32 tiles that the producer loads by TMA
+    // into a WPF_N-slot ring (the layout the sum pass stored them from).
     for (int j = 0; j < ntiles; ++j) {
       const int key0 = j * KT + 16 * g;
       uint32_t w[16];
-      wpf_issue(j + WPF_N - 1);
-      cp_async_wait<WPF_N - 1>();
-      const uint8_t* slot = sm + OFF_WPF + (j % WPF_N) * WPF_BUF + sidx * 16;
-      const uint4 u0 = *reinterpret_cast<const uint4*>(slot);
-      const uint4 u1 = *reinterpret_cast<const uint4*>(slot + WPF_BUF / 2);
+      const int wb = j % WPF_N;
+      wait_bar(&ctl->w_full[wb], (j / WPF_N) & 1, ctl, a.st);
+      const uint8_t* wt = sm + OFF_WPF + wb * WPF_BUF + row * 64;
+      const uint4 u0 = *reinterpret_cast<const uint4*>(wt + (((2u * g) ^ wsw) << 4));
+      const uint4 u1 = *reinterpret_cast<const uint4*>(wt + (((2u * g + 1u) ^ wsw) << 4));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ctl->w_empty[wb]);
       const uint32_t wv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
