@@ -85,6 +85,21 @@ __device__ __forceinline__ unsigned long long div_exact(unsigned long long ss, u
   return q;
 }
 
+// Exact warp sums through the 32-bit reduction unit: an unsigned partial
+// below 2^37 as two 16-bit-split halves, a signed one below 2^52 in magnitude
+// as three pieces (each piece sums below 2^27 over 32 lanes).
+__device__ __forceinline__ unsigned long long warp_sum_u37(unsigned long long p) {
+  const unsigned a = __reduce_add_sync(0xffffffffu, (unsigned)(p >> 16));
+  const unsigned b = __reduce_add_sync(0xffffffffu, (unsigned)(p & 0xFFFF));
+  return ((unsigned long long)a << 16) + b;
+}
+__device__ __forceinline__ long long warp_sum_s52(long long q) {
+  const int h = __reduce_add_sync(0xffffffffu, (int)(q >> 32));
+  const unsigned m = __reduce_add_sync(0xffffffffu, (unsigned)((q >> 16) & 0xFFFF));
+  const unsigned l = __reduce_add_sync(0xffffffffu, (unsigned)(q & 0xFFFF));
+  return (long long)h * 4294967296ll + (long long)m * 65536ll + (long long)l;
+}
+
 // Eight int16 values of a 16-byte load.
 __device__ __forceinline__ void unpack8(const uint4& u, int (&v)[8]) {
   const uint32_t w[4] = {u.x, u.y, u.z, u.w};

@@ -145,9 +145,10 @@ __global__ void __launch_bounds__(256, VPL >= 4 ? 2 : 3) rms_norm_reg_kernel(
       ss[rr] = s;
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-      for (int rr = 0; rr < RPW; ++rr) ss[rr] += __shfl_xor_sync(0xffffffffu, ss[rr], o);
+    for (int rr = 0; rr < RPW; ++rr) {  // per lane at most 8 VPL squares of at most 2^30
+      static_assert(8 * VPL <= 128, "warp_sum_u37 takes partials below 2^37");
+      ss[rr] = warp_sum_u37(ss[rr]);
+    }
 #pragma unroll
     for (int rr = 0; rr < RPW; ++rr) {
       const long long r = r0 + rr;
@@ -186,8 +187,7 @@ __global__ void __launch_bounds__(256, VPL >= 4 ? 2 : 3) rms_norm_reg_kernel(
         }
       }
       if (yl1) {  // per row at most D * 32768 < 2^26
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+        l1 = __reduce_add_sync(0xffffffffu, l1);
         if (lane == 0 && r < rows) yl1[r] = l1;
       }
     }

@@ -614,21 +614,6 @@ __global__ void __launch_bounds__(256) rms_backward_reg_kernel(const int16_t* __
   if (lane == 0 && nsat) atomicAdd(sat, nsat);
 }
 
-// Exact warp sums through the 32-bit reduction unit: an unsigned partial
-// below 2^37 as two 16-bit-split halves, a signed one below 2^52 in magnitude
-// as three pieces (each piece sums below 2^27 over 32 lanes).
-__device__ __forceinline__ unsigned long long warp_sum_u37(unsigned long long p) {
-  const unsigned a = __reduce_add_sync(0xffffffffu, (unsigned)(p >> 16));
-  const unsigned b = __reduce_add_sync(0xffffffffu, (unsigned)(p & 0xFFFF));
-  return ((unsigned long long)a << 16) + b;
-}
-__device__ __forceinline__ long long warp_sum_s52(long long q) {
-  const int h = __reduce_add_sync(0xffffffffu, (int)(q >> 32));
-  const unsigned m = __reduce_add_sync(0xffffffffu, (unsigned)((q >> 16) & 0xFFFF));
-  const unsigned l = __reduce_add_sync(0xffffffffu, (unsigned)(q & 0xFFFF));
-  return (long long)h * 4294967296ll + (long long)m * 65536ll + (long long)l;
-}
-
 // rms_backward_reg_kernel for d = 256 with 16-byte rows: lane l owns columns
 // 8 l .. 8 l + 7, each warp works on RPW rows at once (independent chains for
 // the scheduler), the row sums go through the reduction unit, and the
