@@ -11,6 +11,12 @@
 namespace nsrl {
 namespace ts {
 
+// Column of flat element e in rows of N: a mask when N is a power of two
+// (every width of the training step), a 64-bit remainder otherwise.
+__device__ __forceinline__ int col_of(long long e, int N) {
+  return (N & (N - 1)) == 0 ? (int)(e & (long long)(N - 1)) : (int)(e % N);
+}
+
 // W [R][C] int8 -> WT [C][R] (the B operand of a backward-input linear).
 __global__ void transpose_i8_kernel(const int8_t* __restrict__ w, int R, int C, int8_t* __restrict__ wt) {
   __shared__ int8_t tile[32][33];
@@ -35,7 +41,7 @@ __global__ void prescale_split_kernel(const int16_t* __restrict__ g, long long M
   const long long total = M * N;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
     const long long r = i / N;
-    const int n = (int)(i % N);
+    const int n = col_of(i, N);
     int v = g[r * ldg + n];
     const int s = sc[n].right_shift;
     if (s) v = (int)rhu64(v, (uint32_t)s);
@@ -90,7 +96,7 @@ __global__ void gated_backward_kernel(const int16_t* __restrict__ gg, const int1
     const int grad_gate = sat16((grad_silu * deriv + 16384) >> 15);
     gup[i] = (int16_t)grad_up;
     ggate[i] = (int16_t)grad_gate;
-    const int f = (int)(i % F);
+    const int f = col_of(i, F);
     const int pu = su[f].right_shift ? (int)rhu64(grad_up, su[f].right_shift) : grad_up;
     const int pg = sg[f].right_shift ? (int)rhu64(grad_gate, sg[f].right_shift) : grad_gate;
     uh[i] = (int8_t)(pu >> 8);
@@ -115,7 +121,7 @@ __global__ void gated_backward_vec_kernel(const int16_t* __restrict__ gg, const 
     unpack8(reinterpret_cast<const uint4*>(gg)[i], g);
     unpack8(reinterpret_cast<const uint4*>(up)[i], u);
     unpack8(reinterpret_cast<const uint4*>(gate)[i], ga);
-    const int f0 = (int)((i * 8) % F);
+    const int f0 = col_of(i * 8, F);
     if (f0 != fcur) {
       fcur = f0;
 #pragma unroll
@@ -162,7 +168,7 @@ __global__ void prescale_split_vec_kernel(const int16_t* __restrict__ g, long lo
       if (ik >= n8) break;
       int v[8];
       unpack8(u[k], v);
-      const int c0 = (int)((ik * 8) % N);
+      const int c0 = col_of(ik * 8, N);
       if (c0 != cur[k]) {
         cur[k] = c0;
 #pragma unroll
