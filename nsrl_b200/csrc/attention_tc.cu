@@ -282,11 +282,6 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
 
   if (threadIdx.x == 0) s_abort = timed_out(a.st) ? 1u : 0u;
   if (gtid == 0) ctl->abort = 0u;
-  for (int i = gtid; i < 256; i += GROUP_THREADS) lut[i] = d_exp2_lut[i];
-  for (int i = threadIdx.x; i < 256 * 8; i += THREADS) {
-    const uint32_t v = (uint32_t)(uint16_t)d_exp2_lut[i >> 3];
-    reinterpret_cast<uint4*>(s_lutr)[i] = make_uint4(v, v, v, v);
-  }
   __syncthreads();
   if (s_abort) return;  // a wait of this call already timed out: the whole CTA skips its work
 
@@ -440,6 +435,15 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
     // -------------------------------------------------------------- softmax
     // Warp w owns query rows 32*(w%4)..+31 and keys [16*g, 16*g+16) of each
     // 32-key tile, g = (w-2)/4.
+    // The exp2 tables are first read in the sum pass, after the max pass's
+    // exchange barrier: each group's softmax warps fill them while the first
+    // S tiles load (both groups write the same values into the shared
+    // lane-replicated copy, and each reads it only after its own fill).
+    for (int i = gtid - 64; i < 256; i += 32 * SOFTMAX_WARPS) lut[i] = d_exp2_lut[i];
+    for (int i = gtid - 64; i < 256 * 8; i += 32 * SOFTMAX_WARPS) {
+      const uint32_t v = (uint32_t)(uint16_t)d_exp2_lut[i >> 3];
+      reinterpret_cast<uint4*>(s_lutr)[i] = make_uint4(v, v, v, v);
+    }
     const int q = gw & 3, g = (warp - 2) >> 2;  // TMEM lane quarter follows the warp's index in the CTA
     const int row = q * 32 + lane;
     const int qi = q0 + row;
