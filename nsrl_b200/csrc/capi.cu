@@ -468,10 +468,15 @@ nsrl_status nsrl_prenorm_transformer_block(const int16_t* x, size_t batch, size_
 namespace {
 constexpr int HOST_BUFS = 2;  // device buffers per direction of the host-buffer pipeline
 
+// Step i of the pipeline uses device buffers i % HOST_BUFS and compute
+// stream i % HOST_BUFS (with its own block workspace), so that the block of
+// one step can overlap the tail of the previous one: a block on a few
+// sequences leaves much of the GPU idle at its end (its longest attention
+// tiles run alone).
 struct HostPipe {
   int device = -1;
-  cudaStream_t h2d = nullptr, d2h = nullptr;
-  cudaEvent_t in[HOST_BUFS], comp[HOST_BUFS], out[HOST_BUFS], done;
+  cudaStream_t h2d = nullptr, d2h = nullptr, comp_s[HOST_BUFS] = {nullptr, nullptr};
+  cudaEvent_t in[HOST_BUFS], comp[HOST_BUFS], out[HOST_BUFS], done, fin[HOST_BUFS];
   bool ok = false;
 };
 
@@ -485,9 +490,11 @@ HostPipe* host_pipe() {
   if (cudaStreamCreateWithFlags(&p.h2d, cudaStreamNonBlocking) != cudaSuccess) return nullptr;
   if (cudaStreamCreateWithFlags(&p.d2h, cudaStreamNonBlocking) != cudaSuccess) return nullptr;
   for (int b = 0; b < HOST_BUFS; ++b)
-    if (cudaEventCreateWithFlags(&p.in[b], cudaEventDisableTiming) != cudaSuccess ||
+    if (cudaStreamCreateWithFlags(&p.comp_s[b], cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&p.in[b], cudaEventDisableTiming) != cudaSuccess ||
         cudaEventCreateWithFlags(&p.comp[b], cudaEventDisableTiming) != cudaSuccess ||
-        cudaEventCreateWithFlags(&p.out[b], cudaEventDisableTiming) != cudaSuccess)
+        cudaEventCreateWithFlags(&p.out[b], cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&p.fin[b], cudaEventDisableTiming) != cudaSuccess)
       return nullptr;
   if (cudaEventCreateWithFlags(&p.done, cudaEventDisableTiming) != cudaSuccess) return nullptr;
   p.ok = true;
@@ -499,7 +506,7 @@ size_t nsrl_transformer_block_host_workspace_size(size_t chunk, size_t seq_len, 
                                                   size_t hidden_dim) {
   if (heads == 0 || chunk == 0) return 0;
   return 2 * HOST_BUFS * up(chunk * seq_len * d_model * sizeof(int16_t)) +
-         nsrl_transformer_block_workspace_size(chunk, seq_len, d_model, heads, hidden_dim);
+         HOST_BUFS * up(nsrl_transformer_block_workspace_size(chunk, seq_len, d_model, heads, hidden_dim));
 }
 
 namespace {
@@ -549,8 +556,9 @@ nsrl_status nsrl_prenorm_transformer_block_host(const int16_t* x_host, size_t ba
   int16_t* yd[HOST_BUFS];
   for (int b = 0; b < HOST_BUFS; ++b) xd[b] = c.take<int16_t>(elems);
   for (int b = 0; b < HOST_BUFS; ++b) yd[b] = c.take<int16_t>(elems);
-  void* bws = static_cast<uint8_t*>(workspace) + c.off;
-  const size_t bws_bytes = workspace_bytes - c.off;
+  const size_t bws_bytes = up(nsrl_transformer_block_workspace_size(chunk, seq_len, d_model, heads, hidden_dim));
+  void* bws[HOST_BUFS];
+  for (int b = 0; b < HOST_BUFS; ++b) bws[b] = c.take<uint8_t>(bws_bytes);
   const std::vector<size_t> steps = host_steps(batch, chunk);
   const size_t n = steps.size();
   std::vector<size_t> first(n + 1, 0);  // first sequence of each step
@@ -560,6 +568,7 @@ nsrl_status nsrl_prenorm_transformer_block_host(const int16_t* x_host, size_t ba
   NSRL_TRY(cudaEventRecord(P.done, s), "event");
   NSRL_TRY(cudaStreamWaitEvent(P.h2d, P.done, 0), "event");
   NSRL_TRY(cudaStreamWaitEvent(P.d2h, P.done, 0), "event");
+  for (int b = 0; b < HOST_BUFS; ++b) NSRL_TRY(cudaStreamWaitEvent(P.comp_s[b], P.done, 0), "event");
   auto h2d = [&](size_t i) -> nsrl_status {
     const int b = (int)(i % HOST_BUFS);
     const size_t nb = steps[i];
@@ -578,21 +587,27 @@ nsrl_status nsrl_prenorm_transformer_block_host(const int16_t* x_host, size_t ba
     const int b = (int)(i % HOST_BUFS);
     const size_t nb = steps[i];
     if (i + HOST_BUFS - 1 < n && (r = h2d(i + HOST_BUFS - 1)) != NSRL_OK) return r;
-    NSRL_TRY(cudaStreamWaitEvent(s, P.in[b], 0), "event");
-    if (i >= (size_t)HOST_BUFS) NSRL_TRY(cudaStreamWaitEvent(s, P.out[b], 0), "event");  // y[b] copied out
+    cudaStream_t cs = P.comp_s[b];
+    NSRL_TRY(cudaStreamWaitEvent(cs, P.in[b], 0), "event");
+    if (i >= (size_t)HOST_BUFS) NSRL_TRY(cudaStreamWaitEvent(cs, P.out[b], 0), "event");  // y[b] copied out
     r = nsrl_prenorm_transformer_block(xd[b], nb, seq_len, d_model, heads, hidden_dim, attn_gamma, mlp_gamma, rms_eps,
-                                       q, k, v, o, up_p, gate, down, yd[b], bws, bws_bytes, status, stream);
+                                       q, k, v, o, up_p, gate, down, yd[b], bws[b], bws_bytes, status, cs);
     if (r != NSRL_OK) return r;
-    NSRL_TRY(cudaEventRecord(P.comp[b], s), "event");
+    NSRL_TRY(cudaEventRecord(P.comp[b], cs), "event");
     NSRL_TRY(cudaStreamWaitEvent(P.d2h, P.comp[b], 0), "event");
     NSRL_TRY(cudaMemcpyAsync(y_host + first[i] * row, yd[b], nb * row * sizeof(int16_t), cudaMemcpyDeviceToHost,
                              P.d2h),
              "copy out");
     NSRL_TRY(cudaEventRecord(P.out[b], P.d2h), "event");
   }
-  // the call is complete on `stream` once the last copy out has landed
+  // the call is complete on `stream` once the last copy out has landed and
+  // both compute streams are idle (the next call reuses their workspaces)
   NSRL_TRY(cudaEventRecord(P.done, P.d2h), "event");
   NSRL_TRY(cudaStreamWaitEvent(s, P.done, 0), "event");
+  for (int b = 0; b < HOST_BUFS; ++b) {
+    NSRL_TRY(cudaEventRecord(P.fin[b], P.comp_s[b]), "event");
+    NSRL_TRY(cudaStreamWaitEvent(s, P.fin[b], 0), "event");
+  }
   return NSRL_OK;
 }
 
