@@ -119,27 +119,34 @@ def make_block_inputs(rank: int):
     return bw, np.concatenate(chunks)
 
 
-def cpu_sample(bw, x, threads: int, sequences: int):
-    """Times the oracle block (attention + MLP) over `sequences` sequences; returns tokens/s."""
+def oracle_module():
+    """The oracle, loaded as its -march=native build (every CPU leg times the same build)."""
     from oracle import oracle as O
+    O.use_native()
+    return O
+
+
+def cpu_sample(bw, x, threads: int, sequences: int, heads: int = HEADS):
+    """Times the oracle block (attention + MLP) over the first `sequences`
+    sequences of x; returns (tokens/s, seconds, output)."""
+    O = oracle_module()
     L = {nm: O.Linear(getattr(bw, nm), O.scales(1, bw.shift[nm], bw.out_dim(nm)))
          for nm in ("q", "k", "v", "o", "up", "gate", "down")}
     xs = x[:sequences * SEQ]
     t0 = time.perf_counter()
-    y1, _ = O.prenorm_attention_block(xs, sequences, SEQ, D_MODEL, HEADS, bw.attn_gamma, 1,
+    y1, _ = O.prenorm_attention_block(xs, sequences, SEQ, D_MODEL, heads, bw.attn_gamma, 1,
                                       L["q"], L["k"], L["v"], L["o"], threads=threads)
-    O.prenorm_mlp_block(y1, sequences * SEQ, D_MODEL, HIDDEN, bw.mlp_gamma, 1, L["up"], L["gate"], L["down"],
-                        threads=threads)
+    y2, _ = O.prenorm_mlp_block(y1, sequences * SEQ, D_MODEL, HIDDEN, bw.mlp_gamma, 1, L["up"], L["gate"], L["down"],
+                                threads=threads)
     dt = time.perf_counter() - t0
-    return sequences * SEQ / dt, dt
+    return sequences * SEQ / dt, dt, y2
 
 
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    from oracle import oracle as O
-    O.use_native()
+    oracle_module()
     threads = os.cpu_count() or 1
     bw, x = make_block_inputs(0)
     seqs = max(1, min(BATCH, threads))
@@ -148,7 +155,7 @@ def run_reference(args):
     rates = []
     t_total = 0.0
     for _ in range(args.steps):
-        r, dt = cpu_sample(bw, x, threads, seqs)
+        r, dt, _ = cpu_sample(bw, x, threads, seqs)
         rates.append(r)
         t_total += dt
     value = seqs * SEQ * args.steps / t_total
@@ -199,7 +206,7 @@ def run_decode(core, torch, steps, warmup, hbm, flush, batch=DEC_B):
     from nsrl_b200 import synth as Y
     L = core.lib()
     gen = torch.Generator(device="cuda").manual_seed(5)
-    lmax = DEC_PREFIX + warmup + steps + 1
+    lmax = DEC_PREFIX + warmup + 2 * steps + 1
     layers = []
     for li in range(DEC_LAYERS):
         bw = Y.BlockWeights(seed=77 + li, d=DEC_D, hidden=DEC_F)
@@ -245,24 +252,28 @@ def run_decode(core, torch, steps, warmup, hbm, flush, batch=DEC_B):
     for _ in range(warmup):
         x = step(x)
     torch.cuda.synchronize()
-    ctx_rows = DEC_PREFIX + warmup  # keys attended at the first timed step = this + 1
-    L.nsrl_profile_reset()
-    L.nsrl_profile_enable(1)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(steps):
         x = step(x)
     e1.record()
     torch.cuda.synchronize()
-    L.nsrl_profile_enable(0)
     ms = e0.elapsed_time(e1)
+    # the same number of steps again with per-launch events, for the kernel table
+    ctx_rows = DEC_PREFIX + warmup + steps  # keys attended at the first profiled step = this + 1
+    L.nsrl_profile_reset()
+    L.nsrl_profile_enable(1)
+    for _ in range(steps):
+        x = step(x)
+    torch.cuda.synchronize()
+    L.nsrl_profile_enable(0)
     code, hs = st.fetch()
     if code != 0:
         raise RuntimeError(f"decode rejected (flags {hs.flags:#x})")
     _, rows = kernel_table(L)
     dec = rows["attention_decode"]
-    # algorithmic bytes of the timed decode-attention launches: every cached K and V
-    # row once (positions + 1 keys), plus q in and the context out
+    # algorithmic bytes of the profiled decode-attention launches: every cached K
+    # and V row once (positions + 1 keys), plus q in and the context out
     keys = sum(DEC_B * (ctx_rows + t + 1) for t in range(steps)) * DEC_LAYERS
     dbytes = 2.0 * 2 * DEC_D * keys + 2.0 * 2 * DEC_D * DEC_B * steps * DEC_LAYERS
     ach = dbytes / (dec["ms"] / 1000.0) / 1e9
@@ -299,23 +310,59 @@ def make_train_model(core, torch):
     return tw, gm
 
 
-def train_cpu_sample(tw, ctx, tgt, threads):
-    """The oracle's map-reduce batch (forward + backward of every window, merged
-    in worker order) on `len(tgt)` windows with one worker per thread."""
-    from oracle import oracle as O
+def oracle_train_model(tw):
+    """The oracle's copy of the synthetic training model (its own weight arrays)."""
+    O = oracle_module()
     layers = []
     for bw in tw.blocks:
-        e = {nm: O.Linear(getattr(bw, nm), O.scales(1, bw.shift[nm], bw.out_dim(nm))) for nm in LINEARS}
+        e = {nm: O.Linear(getattr(bw, nm).copy(), O.scales(1, bw.shift[nm], bw.out_dim(nm))) for nm in LINEARS}
         e["attn_gamma"], e["mlp_gamma"] = bw.attn_gamma, bw.mlp_gamma
         layers.append(e)
-    m = O.TrainModel(tw.embeddings, tw.positions, layers, O.Linear(tw.head, O.scales(1, tw.head_shift, 256)), TR_D,
-                     TR_H, TR_F, TR_S)
+    return O.TrainModel(tw.embeddings.copy(), tw.positions.copy(), layers,
+                        O.Linear(tw.head.copy(), O.scales(1, tw.head_shift, 256)), TR_D, TR_H, TR_F, TR_S)
+
+
+def train_cpu_sample(tw, ctx, tgt, threads):
+    """The oracle's whole batch on `len(tgt)` windows with one worker per
+    thread: forward + backward of every window, the merge in worker order and
+    the requantising apply of every parameter."""
+    O = oracle_module()
+    m = oracle_train_model(tw)
+    res = np.zeros(m.arena_layout()["total"], np.int64)
     t0 = time.perf_counter()
-    r = O.train_windows(m, ctx, tgt, workers=threads)
+    r = O.train_step(m, res, ctx, tgt, workers=threads)
     dt = time.perf_counter() - t0
     if r is None:
         raise RuntimeError("oracle rejected the CPU sample")
     return len(tgt) * TR_S / dt, dt
+
+
+def train_parity(core, torch, windows=4):
+    """One step of the full training model on `windows` fresh windows, on the
+    GPU and in the oracle from the same initial model: stats, every updated
+    weight and embedding, and the carried residuals must be equal."""
+    from nsrl_b200 import synth as Y
+    from nsrl_b200 import train as TT
+    O = oracle_module()
+    tw, gm = make_train_model(core, torch)
+    om = oracle_train_model(tw)
+    ctx, tgt = Y.train_windows(0x9A41, windows, TR_S)
+    cfg = TT.MiniTransformerTrainConfig()
+    res = np.zeros(om.arena_layout()["total"], np.int64)
+    ref = O.train_step(om, res, ctx, tgt, cfg={f: getattr(cfg, f) for f in O.DEFAULT_TRAIN_CONFIG}, workers=windows)
+    state = TT.TrainState(gm)
+    got = TT.mini_transformer_train_step(gm, state, torch.from_numpy(ctx).cuda(), torch.from_numpy(tgt).cuda(), cfg,
+                                         TT.TrainStepBuffers(gm, windows))
+    eq = ref is not None and got == ref
+    eq = eq and np.array_equal(gm.head.weights.cpu().numpy(), om.head.weights)
+    for gl, ol in zip(gm.layers, om.layers):
+        for nm in LINEARS:
+            eq = eq and np.array_equal(gl[nm].weights.cpu().numpy(), ol[nm].weights)
+    eq = eq and np.array_equal(gm.embeddings.cpu().numpy(), om.embeddings)
+    eq = eq and np.array_equal(gm.positions.cpu().numpy(), om.positions)
+    eq = eq and np.array_equal(state.residuals.cpu().numpy(), res)
+    return {"windows": windows, "compared": "stats, i8 weights, i16 embeddings and positions, residuals",
+            "equal": bool(eq)}
 
 
 def run_train(core, torch, dist, world, rank, steps, warmup, flush, hbm, tfl, src, cpu_baseline, batch=TR_BATCH):
@@ -333,47 +380,62 @@ def run_train(core, torch, dist, world, rank, steps, warmup, flush, hbm, tfl, sr
     state = TT.TrainState(gm)
     buf = TT.TrainStepBuffers(gm, W)
     cfg = TT.MiniTransformerTrainConfig()
-    nsteps = warmup + steps
+    e2e_steps = max(1, min(steps, 3))
+    prof_steps = 1
+    nsteps = warmup + steps + prof_steps + e2e_steps
     ctx_all, tgt_all = Y.train_windows(0x7EA1, nsteps * TR_BATCH, TR_S)
     lo, hi = rank * W, (rank + 1) * W
-    # device-resident windows of every step (the `value` leg)
-    dctx = [torch.from_numpy(ctx_all[i * TR_BATCH + lo:i * TR_BATCH + hi]).cuda() for i in range(nsteps)]
-    dtgt = [torch.from_numpy(tgt_all[i * TR_BATCH + lo:i * TR_BATCH + hi]).cuda() for i in range(nsteps)]
+    win = lambda i, a: a[i * TR_BATCH + lo:i * TR_BATCH + hi]
+    # device-resident windows of the warm-up, timed and profiled steps (the `value` leg)
+    ndev = warmup + steps + prof_steps
+    dctx = [torch.from_numpy(win(i, ctx_all)).cuda() for i in range(ndev)]
+    dtgt = [torch.from_numpy(win(i, tgt_all)).cuda() for i in range(ndev)]
     stream = torch.cuda.current_stream()
-    last = None
+
+    def one(i):
+        r = TT.mini_transformer_train_step(gm, state, dctx[i], dtgt[i], cfg, buf)
+        if r is None:
+            raise RuntimeError(f"training batch {i} rejected")
+        return r
+
     for i in range(warmup):
-        last = TT.mini_transformer_train_step(gm, state, dctx[i], dtgt[i], cfg, buf)
-        if last is None:
-            raise RuntimeError("training batch rejected in warm-up")
+        one(i)
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
-    L.nsrl_profile_reset()
-    L.nsrl_profile_enable(1)
     ev = []
-    for i in range(warmup, nsteps):
+    last = None
+    for i in range(warmup, warmup + steps):
         flush.zero_()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
-        last = TT.mini_transformer_train_step(gm, state, dctx[i], dtgt[i], cfg, buf)
+        last = one(i)
         b.record(stream)
         ev.append((a, b))
-        if last is None:
-            raise RuntimeError("training batch rejected in the timed region")
     torch.cuda.synchronize()
-    L.nsrl_profile_enable(0)
     ms = sum(a.elapsed_time(b) for a, b in ev)
     t = torch.tensor([ms], dtype=torch.float64, device="cuda")
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
-    n_launches, rows = kernel_table(L)
-    # end to end: this step's windows copied from pinned host memory, the stats read back
-    hctx = torch.from_numpy(ctx_all[lo:hi]).pin_memory()
-    htgt = torch.from_numpy(tgt_all[lo:hi]).pin_memory()
-    e2e_ms = 0.0
-    for i in range(max(1, min(steps, 3))):
+    # one more step with per-launch events, for the kernel table
+    L.nsrl_profile_reset()
+    L.nsrl_profile_enable(1)
+    for i in range(warmup + steps, ndev):
         flush.zero_()
+        one(i)
+    torch.cuda.synchronize()
+    L.nsrl_profile_enable(0)
+    n_launches, rows = kernel_table(L)
+    # end to end: each step's own windows copied from pinned host memory, the stats read back
+    e2e_ms = 0.0
+    for i in range(ndev, nsteps):
+        hctx = torch.from_numpy(win(i, ctx_all)).pin_memory()
+        htgt = torch.from_numpy(win(i, tgt_all)).pin_memory()
+        flush.zero_()
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
         dc = hctx.cuda(non_blocking=True)
@@ -384,7 +446,6 @@ def run_train(core, torch, dist, world, rank, steps, warmup, flush, hbm, tfl, sr
         if r is None:
             raise RuntimeError("training batch rejected in the end-to-end loop")
         e2e_ms += a.elapsed_time(b)
-    e2e_steps = max(1, min(steps, 3))
     t = torch.tensor([e2e_ms], dtype=torch.float64, device="cuda")
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -399,19 +460,25 @@ def run_train(core, torch, dist, world, rank, steps, warmup, flush, hbm, tfl, sr
            "value": tokens * steps / (ms / 1000.0), "unit": "tokens/s", "steps": steps, "warmup": warmup,
            "ms_per_step": ms / steps, "scaling": "strong", "n_gpus": world,
            "e2e": {"value": tokens * e2e_steps / (e2e_ms / 1000.0), "unit": "tokens/s",
-                   "h2d_bytes_per_step": int(W * (TR_S + 1)), "d2h_bytes_per_step": 3 * 8 + 8 * 4 + 8 * 8},
-           "gpu_launches_per_step": n_launches / steps,
+                   "h2d_bytes_per_step": int(W * (TR_S + 1)), "d2h_bytes_per_step": 3 * 8 + 8 * 4 + 8 * 8,
+                   "steps": e2e_steps},
+           "gpu_launches_per_step": n_launches / prof_steps,
            "last_step": last,
            "roofline": roofline(rows, hbm, tfl, src),
+           "kernel_table": f"{prof_steps} further step with per-launch events (the timed steps run without them)",
            "kernels": {k: {"launches": v["launches"], "ms": round(v["ms"], 3), "share": round(v["ms"] / total, 4)}
                        for k, v in sorted(rows.items(), key=lambda kv: -kv[1]["ms"])[:12]}}
+    if world == 1:
+        out["parity"] = train_parity(core, torch)
+        if not out["parity"]["equal"]:
+            raise RuntimeError("training step differs from the oracle")
     if cpu_baseline and world == 1:
         threads = os.cpu_count() or 1
         n = max(1, min(3 * threads, 64))  # about 10 s of CPU work
         rate, dt = train_cpu_sample(tw, ctx_all[:n], tgt_all[:n], threads)
         out["cpu_baseline"] = {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port",
-                               "sample": f"{n} windows x {TR_S} tokens, forward + backward + merge "
-                                         f"({dt:.1f} s, one worker per thread; the apply is not timed)"}
+                               "sample": f"{n} windows x {TR_S} tokens: forward + backward, the merge and the apply "
+                                         f"({dt:.1f} s, one worker per thread)"}
     return out
 
 
@@ -420,13 +487,12 @@ def run_sweep(core, torch, hbm, tflops, flush, reps=5):
     from nsrl_b200 import synth as Y
     L = core.lib()
     out = []
-    gen = torch.Generator(device="cuda").manual_seed(9)
     for K in SWEEP_KN:
         N = K
         w = torch.from_numpy(Y.i8_uniform(K, (N, K)))
         lin = core.Linear(w, core.make_scales(1, Y.shift_for(K), N))
         for M in SWEEP_M:
-            x = (torch.randn((M, K), generator=gen, device="cuda") * 4096).clamp_(-32768, 32767).to(torch.int16)
+            x = Y.q15_gaussian_torch(Y.tensor_seed(0x5EE9, M * 8192 + K), (M, K), "cuda")
             y = torch.empty((M, N), dtype=torch.int16, device="cuda")
             ws = core.workspace(L.nsrl_linear_workspace_size(M, K, N))
             st = core.Status()
@@ -438,10 +504,8 @@ def run_sweep(core, torch, hbm, tflops, flush, reps=5):
                 if r != 0:
                     raise RuntimeError(L.nsrl_last_error())
 
-            for _ in range(2):
+            for _ in range(3):
                 call()
-            L.nsrl_profile_reset()
-            L.nsrl_profile_enable(1)
             tot = 0.0
             for _ in range(reps):
                 flush.zero_()
@@ -451,6 +515,13 @@ def run_sweep(core, torch, hbm, tflops, flush, reps=5):
                 b.record()
                 torch.cuda.synchronize()
                 tot += a.elapsed_time(b)
+            # the same calls again with per-launch events, for the GEMM's own time
+            L.nsrl_profile_reset()
+            L.nsrl_profile_enable(1)
+            for _ in range(reps):
+                flush.zero_()
+                call()
+            torch.cuda.synchronize()
             L.nsrl_profile_enable(0)
             _, rows = kernel_table(L)
             code, _ = st.fetch()
@@ -488,6 +559,112 @@ def roofline(rows, hbm_gbs, tflops, src):
     out["algorithmic_ops_per_launch"] = r["ops"] / r["launches"]
     out["ms_per_launch"] = r["ms"] / r["launches"]
     return out
+
+
+def run_config1(core, torch, flush, reps=50):
+    """The reference's CPU-runnable case: one causal attention layer forward
+    (Q, K, V, O linears and the exact softmax), batch 4, seq 128, d_model 128,
+    2 heads x 64 (head_dim 32 is rejected by the reference).  A latency line:
+    each call timed alone (L2 flushed before it), parity on the whole output."""
+    from nsrl_b200 import synth as Y
+    O = oracle_module()
+    import ctypes as C
+    B, S, d, H = 4, 128, 128, 2
+    L = core.lib()
+    bw = Y.BlockWeights(seed=101, d=d, hidden=4 * d)
+    lin = {nm: core.Linear(torch.from_numpy(getattr(bw, nm)), core.make_scales(1, bw.shift[nm], d)) for nm in "qkvo"}
+    olin = {nm: O.Linear(getattr(bw, nm), O.scales(1, bw.shift[nm], d)) for nm in "qkvo"}
+    x_np = Y.q15_gaussian(Y.tensor_seed(0xC0F1, 1), (B * S, d))
+    x = torch.from_numpy(x_np).cuda()
+    y = torch.empty_like(x)
+    ws = core.workspace(L.nsrl_attention_workspace_size(B, S, d, H))
+    st = core.Status()
+    ps = [lin[n].c() for n in "qkvo"]
+
+    def call():
+        r = L.nsrl_self_attention(core._ptr(x), B, S, d, H, 1, *[C.byref(p) for p in ps], core._ptr(y), core._ptr(ws),
+                                  ws.numel(), core._ptr(st.buf), core._stream())
+        if r != 0:
+            raise RuntimeError(L.nsrl_last_error())
+
+    st.reset()
+    for _ in range(5):
+        call()
+    times = []
+    for _ in range(reps):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        call()
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b))
+    code, _ = st.fetch()
+    if code != 0:
+        raise RuntimeError("config-1 attention rejected")
+    ref = O.self_attention(x_np, B, S, d, H, *[olin[n] for n in "qkvo"], causal=True)
+    eq = ref is not None and bool(np.array_equal(y.cpu().numpy(), ref))
+    if not eq:
+        raise RuntimeError("config-1 attention differs from the oracle")
+    med = statistics.median(times)
+    return {"workload": f"causal attention layer forward (q, k, v, o linears + exact softmax), batch {B}, seq {S}, "
+                        f"d{d} h{H}x{d // H}",
+            "latency_ms_median": med, "latency_ms_min": min(times), "value": B * S / (med / 1000.0),
+            "unit": "tokens/s", "calls": reps, "parity": {"sequences": B, "of": B, "equal": eq}}
+
+
+def run_block_hd16(core, torch, bw, x_np, flush, hbm, tfl, src, steps=5):
+    """The headline block with 16 heads x 16 (the other legal head_dim at
+    d_model 256): tokens/s, the kernel table of a profiled pass, parity on two
+    sequences."""
+    H = 16
+    L = core.lib()
+    lin = {nm: core.Linear(torch.from_numpy(getattr(bw, nm)), core.make_scales(1, bw.shift[nm], bw.out_dim(nm)))
+           for nm in ("q", "k", "v", "o", "up", "gate", "down")}
+    blk = core.TransformerBlock(D_MODEL, H, HIDDEN, *[lin[n] for n in ("q", "k", "v", "o", "up", "gate", "down")],
+                                torch.from_numpy(bw.attn_gamma), torch.from_numpy(bw.mlp_gamma), 1)
+    x = torch.from_numpy(x_np).cuda()
+    y = torch.empty_like(x)
+    ws = core.workspace(blk.workspace_bytes(BATCH, SEQ))
+    st = core.Status()
+
+    def step():
+        if blk.launch(x, y, BATCH, SEQ, ws, st) != 0:
+            raise RuntimeError(L.nsrl_last_error())
+
+    st.reset()
+    for _ in range(3):
+        step()
+    ms = 0.0
+    for _ in range(steps):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        step()
+        b.record()
+        torch.cuda.synchronize()
+        ms += a.elapsed_time(b)
+    L.nsrl_profile_reset()
+    L.nsrl_profile_enable(1)
+    for _ in range(steps):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+    L.nsrl_profile_enable(0)
+    _, rows = kernel_table(L)
+    code, _ = st.fetch()
+    if code != 0:
+        raise RuntimeError("head_dim-16 block rejected")
+    _, _, ref = cpu_sample(bw, x_np, 2, 2, heads=H)
+    eq = bool(np.array_equal(y[:2 * SEQ].cpu().numpy(), ref))
+    if not eq:
+        raise RuntimeError("head_dim-16 block differs from the oracle")
+    total = sum(r["ms"] for r in rows.values())
+    return {"workload": f"the headline block with {H} heads x {D_MODEL // H}", "value": TOKENS * steps / (ms / 1000.0),
+            "unit": "tokens/s", "ms_per_step": ms / steps, "steps": steps, "roofline": roofline(rows, hbm, tfl, src),
+            "kernels": {k: {"launches": v["launches"], "ms": round(v["ms"], 4), "share": round(v["ms"] / total, 4)}
+                        for k, v in sorted(rows.items(), key=lambda kv: -kv[1]["ms"])[:6]},
+            "parity": {"sequences": 2, "of": BATCH, "equal": eq}}
 
 
 def run_secondary(args):
@@ -576,8 +753,6 @@ def main():
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
-    L.nsrl_profile_reset()
-    L.nsrl_profile_enable(1)
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     for i in range(args.steps):
@@ -586,7 +761,6 @@ def main():
         step()
         ends[i].record(stream)
     torch.cuda.synchronize()
-    L.nsrl_profile_enable(0)
     if dist:
         dist.barrier()
     clk = clocks.stop()
@@ -595,10 +769,20 @@ def main():
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     elapsed_ms = float(t.item())
-    n_launches, rows = kernel_table(L)
     code, hs = st.fetch()
     if code != 0:
         raise RuntimeError(f"block rejected in the timed region (flags {hs.flags:#x})")
+    y_timed = y.cpu().numpy()
+    # the same steps again with per-launch events (the in-library profiler) for the
+    # kernel table and the roofline; the timed steps above ran without them
+    L.nsrl_profile_reset()
+    L.nsrl_profile_enable(1)
+    for i in range(args.steps):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+    L.nsrl_profile_enable(0)
+    n_launches, rows = kernel_table(L)
 
     # ---- end to end through the public host-buffer call: pinned host in, host out,
     # the batch in chunks of sequences with copies overlapping compute ----
@@ -674,17 +858,26 @@ def main():
                "roofline": roofline(rows, hbm, tfl, src),
                "kernels": kernels,
                "clocks": clk}
+        # parity: the timed output against the oracle on the first sequences of the
+        # batch (the same sequences the CPU baseline computes)
+        threads = os.cpu_count() or 1
+        seqs = max(1, min(BATCH, threads, 16))
+        _, dt, ref = cpu_sample(bw, x_np, threads, seqs)
+        eq = bool(np.array_equal(y_timed[:seqs * SEQ], ref))
+        out["parity"] = {"sequences": seqs, "of": BATCH, "compared": "block output of the last timed step",
+                         "equal": eq}
+        if not eq:
+            print(json.dumps(out), flush=True)
+            raise RuntimeError("the timed block output differs from the oracle")
         if not args.no_extras and world == 1:
+            out["config1_latency"] = run_config1(core, torch, flush)
+            out["block_hd16"] = run_block_hd16(core, torch, bw, x_np, flush, hbm, tfl, src)
             out["decode"] = run_decode(core, torch, steps=8, warmup=2, hbm=hbm, flush=flush)
             out["linear_sweep"] = run_sweep(core, torch, hbm, tfl, flush)
         if train_out is not None:
             out["train"] = train_out
         if world == 1 and not args.no_cpu_baseline:
-            from oracle import oracle as O
-            O.use_native()
-            threads = os.cpu_count() or 1
-            seqs = max(1, min(BATCH, threads))
-            passes, dt = 0, 0.0
+            passes, dt = 1, dt
             while dt < 10.0 and passes < 64:  # about 10 s of CPU work
                 dt += cpu_sample(bw, x_np, threads, seqs)[1]
                 passes += 1

@@ -98,8 +98,12 @@ nsrl_status nsrl_linear_i16_i8_i16(const int16_t* x, size_t rows, const nsrl_lin
  * nsrl_linear_workspace_size() exceeds the scratch are rejected with
  * NSRL_INVALID_SHAPE and a message.  The first call on a device looks up the
  * scratch address (cudaGetSymbolAddress) and should come before any stream
- * capture.  All calls share the scratch: calls that overlap on the GPU race
- * and must be serialised by the caller. */
+ * capture.  That address is cached per device index for the life of the
+ * process, so it assumes the device's primary context (the runtime API's):
+ * callers that make their own driver-API contexts, or that call
+ * cudaDeviceReset after the first call, are not supported.  All calls share
+ * the scratch: calls that overlap on the GPU race and must be serialised by
+ * the caller. */
 size_t nsrl_linear_noalloc_scratch_bytes(void);
 nsrl_status nsrl_linear_i16_i8_i16_noalloc(const int16_t* x, size_t rows, const nsrl_linear_params* params,
                                            int16_t* y, nsrl_device_status* status, void* stream);
@@ -388,6 +392,19 @@ nsrl_status nsrl_prenorm_transformer_block_host(const int16_t* x_host, size_t ba
                                                 const nsrl_linear_params* up, const nsrl_linear_params* gate,
                                                 const nsrl_linear_params* down, int16_t* y_host, void* workspace,
                                                 size_t workspace_bytes, nsrl_device_status* status, void* stream);
+
+/* ----------------------------------------------------------- diagnostics --
+ * Makes one bounded device wait run out on purpose (no counterpart in the
+ * reference, whose kernels never wait on a device barrier).  Every mbarrier
+ * wait of the library's kernels gives up after a time limit, sets a
+ * WAIT_TIMEOUT bit in the call's status and unwinds, so that a lost arrival
+ * ends the call with NSRL_CORE_REJECTED instead of hanging the GPU.  This
+ * launches one CTA of 32 threads that wait, with the same loop and a limit of
+ * limit_ns (at most 1 s), on a barrier nothing arrives on.  out (3 device
+ * uint64): {threads whose wait gave up, whether the call's timeout bit reads
+ * as set, nanoseconds waited}. */
+nsrl_status nsrl_selftest_bounded_wait(unsigned long long limit_ns, nsrl_device_status* status,
+                                       unsigned long long* out, void* stream);
 
 /* ------------------------------------------------------------ profiling --
  * Per-launch CUDA-event timing of the library's own kernels (no counterpart

@@ -474,19 +474,22 @@ constexpr int HOST_BUFS = 2;  // device buffers per direction of the host-buffer
 // sequences leaves much of the GPU idle at its end (its longest attention
 // tiles run alone).
 struct HostPipe {
-  int device = -1;
   cudaStream_t h2d = nullptr, d2h = nullptr, comp_s[HOST_BUFS] = {nullptr, nullptr};
-  cudaEvent_t in[HOST_BUFS], comp[HOST_BUFS], out[HOST_BUFS], done, fin[HOST_BUFS];
+  cudaEvent_t in[HOST_BUFS], comp[HOST_BUFS], out[HOST_BUFS], done, fin[HOST_BUFS], h2d_fin;
   bool ok = false;
 };
 
+constexpr int kPipeDevices = 64;
+
+// One pipeline (streams and events) per device and host thread, created on
+// the first call on that device and kept for the life of the thread, so a
+// thread that alternates between GPUs reuses each device's own.
 HostPipe* host_pipe() {
-  static thread_local HostPipe p;
+  static thread_local HostPipe pipes[kPipeDevices];
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
-  if (p.ok && p.device == dev) return &p;
-  p = HostPipe{};
-  p.device = dev;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kPipeDevices) return nullptr;
+  HostPipe& p = pipes[dev];
+  if (p.ok) return &p;
   if (cudaStreamCreateWithFlags(&p.h2d, cudaStreamNonBlocking) != cudaSuccess) return nullptr;
   if (cudaStreamCreateWithFlags(&p.d2h, cudaStreamNonBlocking) != cudaSuccess) return nullptr;
   for (int b = 0; b < HOST_BUFS; ++b)
@@ -496,7 +499,9 @@ HostPipe* host_pipe() {
         cudaEventCreateWithFlags(&p.out[b], cudaEventDisableTiming) != cudaSuccess ||
         cudaEventCreateWithFlags(&p.fin[b], cudaEventDisableTiming) != cudaSuccess)
       return nullptr;
-  if (cudaEventCreateWithFlags(&p.done, cudaEventDisableTiming) != cudaSuccess) return nullptr;
+  if (cudaEventCreateWithFlags(&p.done, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&p.h2d_fin, cudaEventDisableTiming) != cudaSuccess)
+    return nullptr;
   p.ok = true;
   return &p;
 }
@@ -532,40 +537,21 @@ std::vector<size_t> host_steps(size_t batch, size_t chunk) {
 }
 }  // namespace
 
-nsrl_status nsrl_prenorm_transformer_block_host(const int16_t* x_host, size_t batch, size_t chunk, size_t seq_len,
-                                                size_t d_model, size_t heads, size_t hidden_dim,
-                                                const int16_t* attn_gamma, const int16_t* mlp_gamma, uint64_t rms_eps,
-                                                const nsrl_linear_params* q, const nsrl_linear_params* k,
-                                                const nsrl_linear_params* v, const nsrl_linear_params* o,
-                                                const nsrl_linear_params* up_p, const nsrl_linear_params* gate,
-                                                const nsrl_linear_params* down, int16_t* y_host, void* workspace,
-                                                size_t workspace_bytes, nsrl_device_status* status, void* stream) {
-  if (chunk == 0 || !x_host || !y_host) return shape_fail("chunk must be nonzero, host buffers non-NULL");
-  if (batch == 0) return NSRL_OK;
-  if (chunk > batch) chunk = batch;
-  if (!workspace ||
-      workspace_bytes < nsrl_transformer_block_host_workspace_size(chunk, seq_len, d_model, heads, hidden_dim))
-    return shape_fail("workspace too small");
-  HostPipe* pp = host_pipe();
-  if (!pp) return cuda_fail(cudaGetLastError(), "copy streams");
-  HostPipe& P = *pp;
-  cudaStream_t s = (cudaStream_t)stream;
-  const size_t elems = chunk * seq_len * d_model;
-  Carver c(workspace);
-  int16_t* xd[HOST_BUFS];
-  int16_t* yd[HOST_BUFS];
-  for (int b = 0; b < HOST_BUFS; ++b) xd[b] = c.take<int16_t>(elems);
-  for (int b = 0; b < HOST_BUFS; ++b) yd[b] = c.take<int16_t>(elems);
-  const size_t bws_bytes = up(nsrl_transformer_block_workspace_size(chunk, seq_len, d_model, heads, hidden_dim));
-  void* bws[HOST_BUFS];
-  for (int b = 0; b < HOST_BUFS; ++b) bws[b] = c.take<uint8_t>(bws_bytes);
-  const std::vector<size_t> steps = host_steps(batch, chunk);
+namespace {
+// The steps of nsrl_prenorm_transformer_block_host after validation: copies
+// in on P.h2d, blocks on the two compute streams, copies out on P.d2h.
+nsrl_status host_pipeline(HostPipe& P, cudaStream_t s, const int16_t* x_host, int16_t* y_host, int16_t* const* xd,
+                          int16_t* const* yd, void* const* bws, size_t bws_bytes, const std::vector<size_t>& steps,
+                          const std::vector<size_t>& first, size_t row, size_t seq_len, size_t d_model, size_t heads,
+                          size_t hidden_dim, const int16_t* attn_gamma, const int16_t* mlp_gamma, uint64_t rms_eps,
+                          const nsrl_linear_params* q, const nsrl_linear_params* k, const nsrl_linear_params* v,
+                          const nsrl_linear_params* o, const nsrl_linear_params* up_p,
+                          const nsrl_linear_params* gate, const nsrl_linear_params* down,
+                          nsrl_device_status* status) {
   const size_t n = steps.size();
-  std::vector<size_t> first(n + 1, 0);  // first sequence of each step
-  for (size_t i = 0; i < n; ++i) first[i + 1] = first[i] + steps[i];
-  const size_t row = seq_len * d_model;
   // the copies may start once the caller's earlier work on `stream` is done
   NSRL_TRY(cudaEventRecord(P.done, s), "event");
+
   NSRL_TRY(cudaStreamWaitEvent(P.h2d, P.done, 0), "event");
   NSRL_TRY(cudaStreamWaitEvent(P.d2h, P.done, 0), "event");
   for (int b = 0; b < HOST_BUFS; ++b) NSRL_TRY(cudaStreamWaitEvent(P.comp_s[b], P.done, 0), "event");
@@ -600,15 +586,60 @@ nsrl_status nsrl_prenorm_transformer_block_host(const int16_t* x_host, size_t ba
              "copy out");
     NSRL_TRY(cudaEventRecord(P.out[b], P.d2h), "event");
   }
-  // the call is complete on `stream` once the last copy out has landed and
-  // both compute streams are idle (the next call reuses their workspaces)
-  NSRL_TRY(cudaEventRecord(P.done, P.d2h), "event");
-  NSRL_TRY(cudaStreamWaitEvent(s, P.done, 0), "event");
-  for (int b = 0; b < HOST_BUFS; ++b) {
-    NSRL_TRY(cudaEventRecord(P.fin[b], P.comp_s[b]), "event");
-    NSRL_TRY(cudaStreamWaitEvent(s, P.fin[b], 0), "event");
-  }
+  // the caller joins the copy and compute streams into `stream`: the call is
+  // complete there once the last copy out has landed and both compute streams
+  // are idle (the next call reuses their workspaces)
   return NSRL_OK;
+}
+}  // namespace
+
+nsrl_status nsrl_prenorm_transformer_block_host(const int16_t* x_host, size_t batch, size_t chunk, size_t seq_len,
+                                                size_t d_model, size_t heads, size_t hidden_dim,
+                                                const int16_t* attn_gamma, const int16_t* mlp_gamma, uint64_t rms_eps,
+                                                const nsrl_linear_params* q, const nsrl_linear_params* k,
+                                                const nsrl_linear_params* v, const nsrl_linear_params* o,
+                                                const nsrl_linear_params* up_p, const nsrl_linear_params* gate,
+                                                const nsrl_linear_params* down, int16_t* y_host, void* workspace,
+                                                size_t workspace_bytes, nsrl_device_status* status, void* stream) {
+  if (chunk == 0 || !x_host || !y_host) return shape_fail("chunk must be nonzero, host buffers non-NULL");
+  if (batch == 0) return NSRL_OK;
+  if (chunk > batch) chunk = batch;
+  if (!workspace ||
+      workspace_bytes < nsrl_transformer_block_host_workspace_size(chunk, seq_len, d_model, heads, hidden_dim))
+    return shape_fail("workspace too small");
+  HostPipe* pp = host_pipe();
+  if (!pp) return cuda_fail(cudaGetLastError(), "copy streams");
+  HostPipe& P = *pp;
+  cudaStream_t s = (cudaStream_t)stream;
+  const size_t elems = chunk * seq_len * d_model;
+  Carver c(workspace);
+  int16_t* xd[HOST_BUFS];
+  int16_t* yd[HOST_BUFS];
+  for (int b = 0; b < HOST_BUFS; ++b) xd[b] = c.take<int16_t>(elems);
+  for (int b = 0; b < HOST_BUFS; ++b) yd[b] = c.take<int16_t>(elems);
+  const size_t bws_bytes = up(nsrl_transformer_block_workspace_size(chunk, seq_len, d_model, heads, hidden_dim));
+  void* bws[HOST_BUFS];
+  for (int b = 0; b < HOST_BUFS; ++b) bws[b] = c.take<uint8_t>(bws_bytes);
+  const std::vector<size_t> steps = host_steps(batch, chunk);
+  const size_t n = steps.size();
+  std::vector<size_t> first(n + 1, 0);  // first sequence of each step
+  for (size_t i = 0; i < n; ++i) first[i + 1] = first[i] + steps[i];
+  const size_t row = seq_len * d_model;
+  // Joins every pipeline stream into the caller's stream.  It runs on every
+  // exit once work may have been enqueued, failures included, so that the
+  // caller never frees the workspace or the host buffers under a copy or a
+  // block still in flight (best effort: its own errors are not reported).
+  auto join = [&]() {
+    if (cudaEventRecord(P.h2d_fin, P.h2d) == cudaSuccess) cudaStreamWaitEvent(s, P.h2d_fin, 0);
+    if (cudaEventRecord(P.done, P.d2h) == cudaSuccess) cudaStreamWaitEvent(s, P.done, 0);
+    for (int b = 0; b < HOST_BUFS; ++b)
+      if (cudaEventRecord(P.fin[b], P.comp_s[b]) == cudaSuccess) cudaStreamWaitEvent(s, P.fin[b], 0);
+  };
+  const nsrl_status res = host_pipeline(P, s, x_host, y_host, xd, yd, bws, bws_bytes, steps, first, row, seq_len,
+                                        d_model, heads, hidden_dim, attn_gamma, mlp_gamma, rms_eps, q, k, v, o, up_p,
+                                        gate, down, status);
+  join();
+  return res;
 }
 
 size_t nsrl_decode_block_workspace_size(size_t batch, size_t d_model, size_t heads) {

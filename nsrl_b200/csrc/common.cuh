@@ -237,20 +237,26 @@ __device__ __forceinline__ unsigned long long global_ns() {
   return t;
 }
 
-// Every wait is bounded in time: after NSRL_WAIT_NS nanoseconds the waiter
+// Every wait is bounded in time: after limit_ns nanoseconds the waiter
 // records NSRL_FLAG_WAIT_TIMEOUT and returns false so that the kernel can
-// unwind (the host then reports the call as failed).
+// unwind (the host then reports the call as failed).  The kernels use
+// NSRL_WAIT_NS; nsrl_selftest_bounded_wait runs the same loop with a short
+// limit on a barrier that never completes.
 #define NSRL_WAIT_NS 2000000000ull
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, nsrl_device_status* st) {
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, nsrl_device_status* st,
+                                              unsigned long long limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;  // the common case reads no timer
   const unsigned long long t0 = global_ns();
   for (uint32_t i = 0;; ++i) {
     if (mbar_try_wait_hint(bar, parity, 20000u)) return true;
-    if ((i & 15u) == 15u && global_ns() - t0 > NSRL_WAIT_NS) {
+    if ((i & 15u) == 15u && global_ns() - t0 > limit_ns) {
       nsrl_flag(st, NSRL_FLAG_WAIT_TIMEOUT);
       return false;
     }
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, nsrl_device_status* st) {
+  return mbar_wait_for(bar, parity, st, NSRL_WAIT_NS);
 }
 
 // True once any bounded wait of the call has timed out (read by one thread,

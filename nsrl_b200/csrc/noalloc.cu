@@ -14,8 +14,10 @@
 // array until the process exits.  Host code cannot use the array's name as a
 // device address (it is a host-side stand-in), so the first call on each
 // device looks the address up once with cudaGetSymbolAddress, with that
-// device current, and caches it; make that first call before any stream
-// capture.  All calls share the array and it keeps the last call's contents:
+// device current, and caches it per device index; make that first call before
+// any stream capture.  The cached address belongs to the device's primary
+// context: a cudaDeviceReset after the first call (which unloads the module
+// and its array) or a caller-made driver-API context is not supported.  All calls share the array and it keeps the last call's contents:
 // the kernels that read it (the linear and the i32 prefix check) only read
 // what the split kernel of the same call wrote, so nothing needs clearing.
 // Calls that overlap on the GPU (two streams, or two host threads) race on the

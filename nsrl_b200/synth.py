@@ -45,6 +45,34 @@ def q15_gaussian(seed: int, shape, sigma_shift: int = 12) -> np.ndarray:
     return np.clip(s >> sigma_shift, -32768, 32767).astype(np.int16).reshape(shape)
 
 
+def _to_i64(v: int) -> int:
+    v &= 0xFFFFFFFFFFFFFFFF
+    return v - (1 << 64) if v >> 63 else v
+
+
+def q15_gaussian_torch(seed: int, shape, device, sigma_shift: int = 12, chunk: int = 1 << 22):
+    """q15_gaussian computed with torch int64 ops on `device` (bit-identical:
+    the same SplitMix64 draws, wrapping multiplies, logical shifts by mask)."""
+    import torch
+    n = int(np.prod(shape))
+    out = torch.empty(n, dtype=torch.int16, device=device)
+    g, m1, m2 = _to_i64(int(GAMMA)), _to_i64(int(M1)), _to_i64(int(M2))
+    s0 = _to_i64(seed)
+
+    def lsr(z, k):
+        return (z >> k) & ((1 << (64 - k)) - 1)
+
+    for c0 in range(0, n, chunk):
+        cn = min(chunk, n - c0)
+        z = torch.arange(12 * c0 + 1, 12 * (c0 + cn) + 1, dtype=torch.int64, device=device) * g + s0
+        z = (z ^ lsr(z, 30)) * m1
+        z = (z ^ lsr(z, 27)) * m2
+        z = z ^ lsr(z, 31)
+        u = lsr(z, 40).view(cn, 12).sum(dim=1) - 6 * (1 << 24)
+        out[c0:c0 + cn] = (u >> sigma_shift).clamp_(-32768, 32767).to(torch.int16)
+    return out.view(tuple(shape) if isinstance(shape, (tuple, list)) else (shape,))
+
+
 def i8_uniform(seed: int, shape) -> np.ndarray:
     n = int(np.prod(shape))
     d = splitmix(seed, n) >> np.uint64(32)

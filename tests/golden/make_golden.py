@@ -1,7 +1,7 @@
 """Writes tests/golden/reference_luts.json from the reference's own LUT source.
 
-Run in a container where the reference tree is mounted (read-only) at
-/root/reference.  The fixture records, for each of the three 8-bit tables of
+Usage: python tests/golden/make_golden.py <reference checkout root>
+(a read-only checkout of atimics/nsrl).  The fixture records, for each of the three 8-bit tables of
 crates/nsrl-core/src/rsqrt_lut_8bit.rs, its length, its FNV-1a-64 hash over
 little-endian bytes and its first and last entries, so that tables derived
 from their mathematical definitions can be pinned to the reference's values
@@ -11,8 +11,9 @@ import json
 import os
 import re
 import struct
+import sys
 
-REF = "/root/reference/crates/nsrl-core/src/rsqrt_lut_8bit.rs"
+LUT_SOURCE = "crates/nsrl-core/src/rsqrt_lut_8bit.rs"
 OUT = os.path.join(os.path.dirname(os.path.abspath(__file__)), "reference_luts.json")
 
 
@@ -28,8 +29,8 @@ def table(src, name):
     return [int(x) for x in m.group(1).replace("\n", " ").split(",") if x.strip()]
 
 
-def main():
-    src = open(REF).read()
+def main(reference_root: str):
+    src = open(os.path.join(reference_root, LUT_SOURCE)).read()
     out = {"source": "crates/nsrl-core/src/rsqrt_lut_8bit.rs"}
     for name, fmt in (("RSQRT_LUT_8BIT", "<h"), ("EXP2_NEG_FRAC_LUT_8BIT", "<h"), ("RECIP_LUT_8BIT_Q31", "<I")):
         vals = table(src, name)
@@ -42,4 +43,6 @@ def main():
 
 
 if __name__ == "__main__":
-    main()
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_golden.py <reference checkout root>")
+    main(sys.argv[1])

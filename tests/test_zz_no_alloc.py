@@ -7,7 +7,8 @@ cudaFree are not allowed because they can synchronise the device or exceed a
 budget owned by another allocator.  The no-alloc entry point serves them from
 a static device scratch array.  This test calls it through the C ABI twice in
 a row, with different shapes, and requires the output to match the workspace
-entry point bit for bit (integer path: tolerance 0).  It also checks that a
+entry point bit for bit (integer path: tolerance 0), and both to match the
+oracle.  It also checks that a
 shape beyond the scratch is rejected.  It runs last (file name) and passes
 both alone and after the other tests.
 """
@@ -15,6 +16,8 @@ import ctypes as C
 
 import numpy as np
 import pytest
+
+from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
 
@@ -40,10 +43,11 @@ def test_noalloc_linear_matches_workspace_linear_on_two_calls():
     torch.cuda.set_device(0)
     cases = [(512, 1024, 384, True), (1000, 256, 256, False)]  # prefix check on / off
     for M, K, N, with_bias in cases:
-        x = torch.from_numpy(Y.q15_gaussian(3 + M, (M, K))).cuda()
-        w = torch.from_numpy(Y.i8_uniform(4 + N, (N, K)))
+        x_np = Y.q15_gaussian(3 + M, (M, K))
+        w_np = Y.i8_uniform(4 + N, (N, K))
+        x = torch.from_numpy(x_np).cuda()
         bias = torch.arange(N, dtype=torch.int32) * 37 - 5000 if with_bias else None
-        lin = core.Linear(w, core.make_scales(1, Y.shift_for(K), N), bias)
+        lin = core.Linear(torch.from_numpy(w_np), core.make_scales(1, Y.shift_for(K), N), bias)
         ref = core.linear_i16_i8_i16_per_channel_checked(x, lin)
         assert ref is not None
         r, y, st = _call_noalloc(core, x, lin)
@@ -51,6 +55,9 @@ def test_noalloc_linear_matches_workspace_linear_on_two_calls():
         code, _ = st.fetch()
         assert code == core.NSRL_OK
         assert torch.equal(y, ref)
+        oref = O.linear(x_np, O.Linear(w_np, O.scales(1, Y.shift_for(K), N),
+                                       None if bias is None else bias.numpy()))
+        assert oref is not None and np.array_equal(y.cpu().numpy(), oref)
 
 
 def test_noalloc_linear_rejects_shapes_beyond_its_scratch():
