@@ -38,7 +38,8 @@ typedef enum nsrl_status {
   NSRL_INVALID_SHAPE = 1,  /* validation `None` (shape / parameter rules) */
   NSRL_CORE_REJECTED = 2,  /* arithmetic `None` detected on the device */
   NSRL_CUDA_ERROR = 3,     /* a CUDA runtime/driver call failed */
-  NSRL_COMM_TIMEOUT = 4,   /* reserved for the data-parallel exchange */
+  NSRL_COMM_TIMEOUT = 4,   /* a collective did not finish before the communicator's deadline */
+  NSRL_COMM_ERROR = 5,     /* the communicator reported an error (a peer failed) or was aborted */
 } nsrl_status;
 
 /* FixedScale{multiplier, right_shift} (crates/nsrl-core/src/numeric.rs:1-5). */
@@ -370,6 +371,125 @@ nsrl_status nsrl_train_windows(const nsrl_train_model* model, const uint8_t* con
                                const int16_t* freq_weights, size_t windows, long long* arena,
                                unsigned long long* counts, unsigned long long* stats, void* workspace,
                                size_t workspace_bytes, nsrl_device_status* status, void* stream);
+
+/* ------------------------------------------------ data-parallel step --
+ * One training batch of the mini transformer on every rank of a
+ * communicator: the reference's map-reduce batch (nsrl-train/src/lib.rs:
+ * 6970-7399) with the ranks as its workers, the ordered merge of the
+ * workers' i64 accumulators (:7401-7471) as an exact NCCL int64 all-reduce,
+ * and the apply of every parameter (:6249-6400 with the shift optimizer, or
+ * the integer-Adam batch apply :4270-4465).  Rank r holds window chunk r of
+ * the batch, as worker r does in the reference, so the weights after a step
+ * are the same for any number of ranks.
+ *
+ * nsrl_comm is an NCCL communicator (non-blocking, NCCL loaded at run time
+ * from libnccl.so.2) whose every wait is bounded by its timeout: a collective
+ * still running at the deadline aborts the communicator and the call returns
+ * NSRL_COMM_TIMEOUT; an error that NCCL reports (a failed peer) aborts it and
+ * returns NSRL_COMM_ERROR.  An aborted communicator fails every later call
+ * with NSRL_COMM_ERROR; destroy it and make a new one.  The reference has no
+ * communicator (its workers are threads, lib.rs:7012-7047). */
+typedef struct nsrl_comm nsrl_comm;
+#define NSRL_COMM_ID_BYTES 128
+
+/* Rank 0 makes the id (ncclGetUniqueId) and hands it to every rank. */
+nsrl_status nsrl_comm_unique_id(uint8_t id[NSRL_COMM_ID_BYTES]);
+/* Joins the communicator on the current CUDA device; timeout_ms bounds the
+ * join and every later wait on it (0 = 120 s). */
+nsrl_status nsrl_comm_init(nsrl_comm** comm, int nranks, int rank, const uint8_t id[NSRL_COMM_ID_BYTES],
+                           uint64_t timeout_ms);
+/* Finalises (or, after a failure, aborts) and frees the communicator. */
+nsrl_status nsrl_comm_destroy(nsrl_comm* comm);
+int nsrl_comm_nranks(const nsrl_comm* comm);
+int nsrl_comm_rank(const nsrl_comm* comm);
+
+enum { NSRL_OPTIMIZER_SHIFT = 0, NSRL_OPTIMIZER_INTEGER_ADAM = 1 };
+/* MiniTransformerAdamTrainScope (nsrl-train/src/lib.rs:188-195). */
+enum {
+  NSRL_ADAM_SCOPE_ALL = 0,
+  NSRL_ADAM_SCOPE_RMS_NORM = 1,
+  NSRL_ADAM_SCOPE_OUTPUT = 2,
+  NSRL_ADAM_SCOPE_FINAL_MLP = 3,
+  NSRL_ADAM_SCOPE_FINAL_MLP_AND_OUTPUT = 4,
+};
+
+/* The learning-rate fields of MiniTransformerMlpTrainConfig (nsrl-train/src/
+ * lib.rs:300-390, defaults :86-91: 1, 18, 16, 14, 24, 18, 18) and the
+ * optimizer.  The shift optimizer subtracts the batch shift
+ * ceil(log2(accepted windows)) from every shift (:13591-13650) and adds the
+ * stacked-layer extra shifts (:15454-15495); integer Adam uses `adam`
+ * (IntegerAdamConfig) for every tensor in `adam_scope`. */
+typedef struct nsrl_train_config {
+  int32_t learning_rate;
+  uint8_t output_learning_rate_shift;
+  uint8_t mlp_learning_rate_shift;
+  uint8_t embedding_learning_rate_shift;
+  uint8_t attention_learning_rate_shift;
+  uint8_t attention_q_learning_rate_shift;
+  uint8_t attention_qk_learning_rate_shift;
+  uint8_t optimizer;  /* NSRL_OPTIMIZER_* */
+  uint8_t adam_scope; /* NSRL_ADAM_SCOPE_* */
+  nsrl_integer_adam_config adam;
+} nsrl_train_config;
+
+/* Optimizer state carried between steps (device arrays, caller-owned).
+ * residuals [nsrl_train_arena_len] int64 (the shift optimizer's carried
+ * remainders, arena order).  With integer Adam: adam_* [nsrl_train_adam_state_len]
+ * in the reference's flat order (token embeddings, positions, attention and
+ * MLP RMS gammas, q, k, v, o, up, gate, down of all layers, output head,
+ * lib.rs:1001-1015, :4165-4196) and adam_step (one uint64, +1 per applied
+ * batch, :4447-4451); NULL otherwise. */
+typedef struct nsrl_train_state {
+  long long* residuals;
+  long long* adam_first_moments;
+  unsigned long long* adam_second_moments;
+  long long* adam_update_residuals;
+  unsigned long long* adam_step;
+} nsrl_train_state;
+
+/* Batch statistics summed over the ranks. */
+typedef struct nsrl_train_step_stats {
+  uint64_t accepted_windows;
+  uint64_t mlp_saturations;
+  uint64_t attention_saturations;
+  uint64_t residual_saturations;
+  uint64_t gradient_saturations; /* of the apply */
+  uint64_t zero_deltas;
+  uint64_t weight_delta_l1;
+} nsrl_train_step_stats;
+
+size_t nsrl_train_adam_state_len(const nsrl_train_model* model);
+size_t nsrl_train_dp_workspace_size(const nsrl_train_model* model, size_t windows, int nranks);
+/* Runs this rank's `windows` windows (contexts [windows][seq_len] uint8,
+ * targets [windows] uint8, freq_weights [256] int16 or NULL), the exchange
+ * with the other ranks of `comm` (NULL = one rank) and the apply; the model's
+ * weights (i8 linears, i16 embeddings, and with Adam the RMS gammas) are
+ * updated in place through its pointers.  The call returns when the step is
+ * complete on the device (it waits on `stream`).  It clears `status` first.
+ * NSRL_CORE_REJECTED: some rank rejected the batch (lib.rs:5371-5375) or the
+ * ordered merge overflowed; the model and the state are unchanged.  Every
+ * rank must call it with the same model shapes and config; rank r's windows
+ * are chunk r of the batch. */
+nsrl_status nsrl_train_dp_step(const nsrl_train_model* model, const uint8_t* contexts, const uint8_t* targets,
+                               const int16_t* freq_weights, size_t windows, const nsrl_train_config* config,
+                               const nsrl_train_state* state, nsrl_comm* comm, nsrl_train_step_stats* stats,
+                               void* workspace, size_t workspace_bytes, nsrl_device_status* status, void* stream);
+
+/* The reference's merge of worker results (mini_transformer_merge_map_reduce_
+ * batch_result, nsrl-train/src/lib.rs:7401-7471) as a primitive: parts is
+ * [workers][len] int64; out[i] = parts[0][i] + parts[1][i] + ... in worker
+ * order, with checked adds for i < checked_len (the i64 accumulators; an
+ * overflow rejects the call) and wrapping adds after (the counts).  The
+ * data-parallel step uses it when the bound of its all-reduce fails. */
+nsrl_status nsrl_merge_worker_parts_i64(const long long* parts, size_t workers, size_t checked_len, size_t len,
+                                        long long* out, nsrl_device_status* status, void* stream);
+
+/* The wait of the communicator against a fake clock and fake completion /
+ * error reports (no GPU, no NCCL): scenario 0 completes after three polls,
+ * 1 never completes, 2 reports a peer error on the third poll.  Returns what
+ * the real wait would (NSRL_OK, NSRL_COMM_TIMEOUT, NSRL_COMM_ERROR); *polls
+ * and *aborted tell how many polls ran and whether the abort was called. */
+nsrl_status nsrl_comm_selftest_wait(int scenario, uint64_t timeout_ms, uint64_t* polls, int* aborted);
 
 /* The transformer block over HOST buffers (pinned host memory for the
  * overlap): the batch runs in steps of at most `chunk` sequences; the copy

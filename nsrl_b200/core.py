@@ -17,7 +17,7 @@ import torch
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libnsrl_b200.so")
 
-NSRL_OK, NSRL_INVALID_SHAPE, NSRL_CORE_REJECTED, NSRL_CUDA_ERROR, NSRL_COMM_TIMEOUT = range(5)
+NSRL_OK, NSRL_INVALID_SHAPE, NSRL_CORE_REJECTED, NSRL_CUDA_ERROR, NSRL_COMM_TIMEOUT, NSRL_COMM_ERROR = range(6)
 
 _lib = None
 

@@ -327,17 +327,23 @@ class TrainModel:
 
 
 class TrainStepBuffers:
-    """Gradient arena, sample counts, stats and workspace of nsrl_train_windows for W windows."""
+    """Workspace of the data-parallel step for W windows per rank over
+    `nranks` ranks (nsrl_train_dp_workspace_size; it also serves
+    nsrl_train_windows alone), and a gradient arena, sample counts and
+    stats for the windows-only call."""
 
-    def __init__(self, model: TrainModel, windows: int):
-        L = _lib_bwd()
+    def __init__(self, model: TrainModel, windows: int, nranks: Optional[int] = None):
+        L = _lib_dp()
         m = model.c()
         dev = core._dev()
+        if nranks is None:
+            import torch.distributed as dist
+            nranks = dist.get_world_size() if dist.is_initialized() else 1
         self.n = L.nsrl_train_arena_len(C.byref(m))
         self.arena = torch.zeros(self.n, dtype=torch.int64, device=dev)
         self.counts = torch.zeros(2 + 9 * len(model.layers), dtype=torch.int64, device=dev)
         self.stats = torch.zeros(4, dtype=torch.int64, device=dev)
-        nbytes = L.nsrl_train_workspace_size(C.byref(m), windows)
+        nbytes = L.nsrl_train_dp_workspace_size(C.byref(m), windows, int(nranks))
         if nbytes == 0:
             raise ValueError(L.nsrl_last_error().decode() or "invalid training-step shape")
         self.ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
@@ -391,6 +397,13 @@ class MiniTransformerTrainConfig:
     attention_learning_rate_shift: int = 24
     attention_q_learning_rate_shift: int = 18
     attention_qk_learning_rate_shift: int = 18
+    # "shift" (the residual-carrying shift apply, lib.rs:6249-6400) or
+    # "integer_adam" (lib.rs:4270-4465) with IntegerAdamConfig fields
+    # (learning_rate, step_shift, beta1_decay_shift, beta2_decay_shift,
+    # epsilon) and a MiniTransformerAdamTrainScope (lib.rs:188-195)
+    optimizer: str = "shift"
+    adam: tuple = (1, 4, 3, 7, 1)
+    adam_scope: str = "all"
 
 
 MAX_RIGHT_SHIFT = 62
@@ -458,19 +471,19 @@ def layer_apply_shifts(cfg: MiniTransformerTrainConfig, accepted_windows: int, l
 class TrainState:
     """Carried residuals of every applied parameter (the residual arrays of
     LinearWeightGradientI64 and MiniTransformerEmbeddingGradientI64), laid
-    out like the gradient arena."""
+    out like the gradient arena; with adam=True also the integer-Adam state
+    (MiniTransformerAdamOptimizerState, lib.rs:1001-1015)."""
 
-    def __init__(self, model: TrainModel):
-        self.residuals = torch.zeros(model.arena_layout()["total"], dtype=torch.int64, device=core._dev())
+    def __init__(self, model: TrainModel, adam: bool = False):
+        dev = core._dev()
+        self.residuals = torch.zeros(model.arena_layout()["total"], dtype=torch.int64, device=dev)
+        self.adam = IntegerAdamState(_lib_dp().nsrl_train_adam_state_len(C.byref(model.c())), dev) if adam else None
 
-
-def _lib_apply():
-    L = _lib_bwd()
-    if not getattr(L, "_apply_bound", False):
-        vp, sz = C.c_void_p, C.c_size_t
-        L.nsrl_apply_embedding_gradient_i64_to_i16.argtypes = [vp, vp, vp, sz, vp, C.c_int32, C.c_uint8, vp, vp, vp]
-        L._apply_bound = True
-    return L
+    def c(self):
+        a = self.adam
+        return _TrainStateC(self.residuals.data_ptr(), *((a.first_moments.data_ptr(), a.second_moments.data_ptr(),
+                                                          a.update_residuals.data_ptr(), a.step.data_ptr())
+                                                         if a is not None else (None,) * 4))
 
 
 def allreduce_flat_i64(flat: torch.Tensor, group=None) -> tuple[torch.Tensor, bool]:
@@ -492,103 +505,164 @@ def allreduce_flat_i64(flat: torch.Tensor, group=None) -> tuple[torch.Tensor, bo
     return merged, not ovf
 
 
-def allreduce_arena_i64(buf: TrainStepBuffers, group=None) -> bool:
-    """Sums the arena, the sample counts and the stats of every rank into every
-    rank, exactly (the ordered merge of lib.rs:7401-7471 with rank r = worker
-    chunk r).  False when that merge overflows i64."""
+class IntegerAdamConfigC(C.Structure):
+    """IntegerAdamConfig (nsrl-train-core/src/lib.rs:279-297) with the reference defaults."""
+    _fields_ = [("learning_rate", C.c_int32), ("step_shift", C.c_uint8), ("beta1_decay_shift", C.c_uint8),
+                ("beta2_decay_shift", C.c_uint8), ("pad", C.c_uint8), ("epsilon", C.c_uint64)]
+
+    def __init__(self, learning_rate=1, step_shift=4, beta1_decay_shift=3, beta2_decay_shift=7, epsilon=1):
+        super().__init__(learning_rate, step_shift, beta1_decay_shift, beta2_decay_shift, 0, epsilon)
+
+
+class _TrainConfigC(C.Structure):
+    _fields_ = [("learning_rate", C.c_int32), ("output_learning_rate_shift", C.c_uint8),
+                ("mlp_learning_rate_shift", C.c_uint8), ("embedding_learning_rate_shift", C.c_uint8),
+                ("attention_learning_rate_shift", C.c_uint8), ("attention_q_learning_rate_shift", C.c_uint8),
+                ("attention_qk_learning_rate_shift", C.c_uint8), ("optimizer", C.c_uint8), ("adam_scope", C.c_uint8),
+                ("adam", IntegerAdamConfigC)]
+
+
+class _TrainStateC(C.Structure):
+    _fields_ = [("residuals", C.c_void_p), ("adam_first_moments", C.c_void_p), ("adam_second_moments", C.c_void_p),
+                ("adam_update_residuals", C.c_void_p), ("adam_step", C.c_void_p)]
+
+
+class _StepStatsC(C.Structure):
+    _fields_ = [(f, C.c_uint64) for f in ("accepted", "mlp_saturation_count", "attention_saturation_count",
+                                          "residual_saturation_count", "gradient_saturation_count",
+                                          "zero_delta_count", "weight_delta_l1")]
+
+
+ADAM_SCOPES = {"all": 0, "rms_norm": 1, "output": 2, "final_mlp": 3, "final_mlp_and_output": 4}
+
+
+def _lib_dp():
+    L = _lib_bwd()
+    if not getattr(L, "_dp_bound", False):
+        vp, sz = C.c_void_p, C.c_size_t
+        L.nsrl_comm_unique_id.argtypes = [vp]
+        L.nsrl_comm_init.argtypes = [C.POINTER(C.c_void_p), C.c_int, C.c_int, vp, C.c_uint64]
+        L.nsrl_comm_destroy.argtypes = [vp]
+        L.nsrl_comm_nranks.argtypes = [vp]
+        L.nsrl_comm_rank.argtypes = [vp]
+        L.nsrl_train_adam_state_len.restype = sz
+        L.nsrl_train_adam_state_len.argtypes = [vp]
+        L.nsrl_train_dp_workspace_size.restype = sz
+        L.nsrl_train_dp_workspace_size.argtypes = [vp, sz, C.c_int]
+        L.nsrl_train_dp_step.argtypes = [vp, vp, vp, vp, sz, C.POINTER(_TrainConfigC), C.POINTER(_TrainStateC), vp,
+                                         C.POINTER(_StepStatsC), vp, sz, vp, vp]
+        L.nsrl_merge_worker_parts_i64.argtypes = [vp, sz, sz, sz, vp, vp, vp]
+        L.nsrl_comm_selftest_wait.argtypes = [C.c_int, C.c_uint64, C.POINTER(C.c_uint64), C.POINTER(C.c_int)]
+        L._dp_bound = True
+    return L
+
+
+class CommError(core.NsrlError):
+    """The communicator timed out or reported a failed peer (it is aborted then)."""
+
+    def __init__(self, code: int, msg: str):
+        super().__init__(msg)
+        self.code = code
+
+
+class Communicator:
+    """nsrl_comm: an NCCL communicator of the library over the ranks of a
+    torch.distributed group (any backend: the group only carries rank 0's
+    128-byte NCCL id to the other ranks).  Every wait on it is bounded by
+    timeout_ms; a collective that misses the deadline aborts it (CommError)."""
+
+    def __init__(self, group=None, timeout_ms: int = 120_000):
+        import torch.distributed as dist
+        L = _lib_dp()
+        self.handle = None
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        uid = (C.c_uint8 * 128)()
+        if self.rank == 0:
+            r = L.nsrl_comm_unique_id(uid)
+            if r != core.NSRL_OK:
+                raise CommError(r, L.nsrl_last_error().decode())
+        obj = [bytes(uid) if self.rank == 0 else None]
+        src = 0 if group is None else dist.get_global_rank(group, 0)
+        dist.broadcast_object_list(obj, src=src, group=group)
+        uid = (C.c_uint8 * 128).from_buffer_copy(obj[0])
+        h = C.c_void_p()
+        r = L.nsrl_comm_init(C.byref(h), self.world, self.rank, uid, int(timeout_ms))
+        if r != core.NSRL_OK:
+            raise CommError(r, L.nsrl_last_error().decode())
+        self.handle = h
+
+    def close(self):
+        if self.handle:
+            _lib_dp().nsrl_comm_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+_COMMS = {}
+
+
+def default_communicator(group=None) -> Optional[Communicator]:
+    """One Communicator per torch.distributed group (None for a single rank)."""
     import torch.distributed as dist
     if not dist.is_initialized() or dist.get_world_size(group) == 1:
-        return True
-    flat, ok = allreduce_flat_i64(torch.cat([buf.arena, buf.counts, buf.stats]), group)
-    n, c = buf.arena.numel(), buf.counts.numel()
-    buf.arena.copy_(flat[:n])
-    buf.counts.copy_(flat[n:n + c])
-    buf.stats.copy_(flat[n + c:])
-    return ok
-
-
-def apply_batch(model: TrainModel, state: TrainState, buf: TrainStepBuffers, cfg: MiniTransformerTrainConfig,
-                accepted_windows: int) -> Optional[dict]:
-    """Applies the merged batch gradients to every parameter (lib.rs:6249-6400):
-    i8 weights with carried residuals, then the i16 embeddings.  Returns the
-    summed update stats, or None on an arithmetic rejection."""
-    L = _lib_apply()
-    lay = model.arena_layout()
-    sh = layer_apply_shifts(cfg, accepted_windows, len(model.layers))
-    st = core.Status()
-    st.reset()
-    stats = torch.zeros(3, dtype=torch.int64, device=buf.arena.device)
-    total = torch.zeros(3, dtype=torch.int64, device=buf.arena.device)
-    lr = int(cfg.learning_rate)
-
-    def apply_i8(key, weights, count_idx):
-        o, n = lay[key]
-        r = L.nsrl_apply_linear_weight_gradient_i64_to_i8(
-            core._ptr(buf.arena[o:o + n]), core._ptr(state.residuals[o:o + n]), core._ptr(weights), n,
-            core._ptr(buf.counts[count_idx:count_idx + 1]), lr, int(sh[key]), 1, core._ptr(stats), core._ptr(st.buf),
-            core._stream())
-        core._check(r)
-        total.add_(stats)
-
-    apply_i8("head", model.head.weights, 0)
-    for li, ly in enumerate(model.layers):
-        for j, nm in enumerate(LAYER_LINEARS):
-            apply_i8((li, nm), ly[nm].weights, 1 + 9 * li + j)
-    ce = 1 + 9 * len(model.layers)
-    stats.zero_()
-    for key, emb in (("emb", model.embeddings), ("pos", model.positions)):
-        if emb is None:
-            continue
-        o, n = lay[key]
-        r = L.nsrl_apply_embedding_gradient_i64_to_i16(
-            core._ptr(buf.arena[o:o + n]), core._ptr(state.residuals[o:o + n]), core._ptr(emb), n,
-            core._ptr(buf.counts[ce:ce + 1]), lr, int(sh["emb"]), core._ptr(stats), core._ptr(st.buf), core._stream())
-        core._check(r)
-    total.add_(stats)
-    o, n = lay["emb"]
-    buf.arena[o:o + n + lay["pos"][1]].zero_()
-    buf.counts[ce].zero_()
-    code, _ = st.fetch()
-    if code != core.NSRL_OK:
         return None
-    t = total.cpu().tolist()
-    return {"gradient_saturation_count": t[0], "zero_delta_count": t[1], "weight_delta_l1": t[2]}
+    key = id(group)
+    if key not in _COMMS:
+        _COMMS[key] = Communicator(group)
+    return _COMMS[key]
+
+
+def close_communicators():
+    for c in _COMMS.values():
+        c.close()
+    _COMMS.clear()
+
+
+def _config_c(cfg: "MiniTransformerTrainConfig") -> _TrainConfigC:
+    return _TrainConfigC(int(cfg.learning_rate), cfg.output_learning_rate_shift, cfg.mlp_learning_rate_shift,
+                         cfg.embedding_learning_rate_shift, cfg.attention_learning_rate_shift,
+                         cfg.attention_q_learning_rate_shift, cfg.attention_qk_learning_rate_shift,
+                         1 if cfg.optimizer == "integer_adam" else 0, ADAM_SCOPES[cfg.adam_scope],
+                         IntegerAdamConfigC(*cfg.adam))
 
 
 def mini_transformer_train_step(model: TrainModel, state: TrainState, contexts: torch.Tensor, targets: torch.Tensor,
                                 cfg: MiniTransformerTrainConfig, buf: TrainStepBuffers, group=None,
-                                freq_weights: Optional[torch.Tensor] = None) -> Optional[dict]:
-    """One data-parallel batch: this rank's windows forward + backward into i64
-    accumulators (lib.rs:7051-7399), the exact int64 all-reduce (:7401-7471),
-    and the requantising apply of every parameter (:6249-6400).  Returns the
-    batch stats, or None when the batch is rejected on any rank (:5371-5375).
-    A batch rejected before the apply leaves the model unchanged; the apply's
-    own checks (i64 overflow of avg * lr + residual) cannot fail for sums of
-    int16 products and are reported, not rolled back.  Every rank takes the
-    same collective steps."""
-    import torch.distributed as dist
-    buf.clear()
-    buf.status.reset()
-    r = launch_train_windows(model, contexts, targets, buf, freq_weights)
+                                freq_weights: Optional[torch.Tensor] = None,
+                                comm: Optional[Communicator] = None) -> Optional[dict]:
+    """One data-parallel batch through nsrl_train_dp_step: this rank's windows
+    forward + backward into i64 accumulators (lib.rs:7051-7399), the exact
+    int64 exchange with the other ranks (:7401-7471) and the apply of every
+    parameter (:6249-6400, or integer Adam :4270-4465), with no host round
+    trip in between.  Returns the batch stats, or None when the batch is
+    rejected on any rank (:5371-5375; the model is unchanged then).  Raises
+    CommError when the exchange times out or a peer fails."""
+    L = _lib_dp()
+    if comm is None:
+        comm = default_communicator(group)
+    m = model.c()
+    st = _StepStatsC()
+    cc = _config_c(cfg)
+    sc = state.c()
+    ctx = contexts.to(core._dev(), torch.uint8).contiguous()
+    tgt = targets.to(core._dev(), torch.uint8).contiguous()
+    r = L.nsrl_train_dp_step(C.byref(m), core._ptr(ctx), core._ptr(tgt), core._ptr(freq_weights), ctx.shape[0],
+                             C.byref(cc), C.byref(sc), comm.handle if comm else None, C.byref(st),
+                             core._ptr(buf.ws), buf.ws.numel(), core._ptr(buf.status.buf), core._stream())
     if r == core.NSRL_INVALID_SHAPE:
-        raise ValueError(_lib().nsrl_last_error().decode())
+        raise ValueError(L.nsrl_last_error().decode())
+    if r in (core.NSRL_COMM_TIMEOUT, core.NSRL_COMM_ERROR):
+        raise CommError(r, L.nsrl_last_error().decode())
+    if r == core.NSRL_CORE_REJECTED:
+        return None
     core._check(r)
-    code, _ = buf.status.fetch()
-    rejected = torch.tensor([0 if code == core.NSRL_OK else 1], dtype=torch.int64, device=buf.arena.device)
-    if dist.is_initialized() and dist.get_world_size(group) > 1:
-        dist.all_reduce(rejected, op=dist.ReduceOp.MAX, group=group)
-    if int(rejected.item()):
-        return None
-    if not allreduce_arena_i64(buf, group):
-        return None
-    s = buf.stats.cpu().tolist()
-    upd = apply_batch(model, state, buf, cfg, int(s[0]))
-    if upd is None:
-        return None
-    out = {"accepted": s[0], "mlp_saturation_count": s[1], "attention_saturation_count": s[2],
-           "residual_saturation_count": s[3]}
-    out.update(upd)
-    return out
+    return {f: int(getattr(st, f)) for f, _ in _StepStatsC._fields_}
 
 
 def accumulate_weight_gradient_i16(x: torch.Tensor, grad_output: torch.Tensor, scales: torch.Tensor,
@@ -615,15 +689,6 @@ def accumulate_weight_gradient_i16(x: torch.Tensor, grad_output: torch.Tensor, s
 
 
 # ------------------------------------------------------------ integer Adam --
-class IntegerAdamConfigC(C.Structure):
-    """IntegerAdamConfig (nsrl-train-core/src/lib.rs:279-297) with the reference defaults."""
-    _fields_ = [("learning_rate", C.c_int32), ("step_shift", C.c_uint8), ("beta1_decay_shift", C.c_uint8),
-                ("beta2_decay_shift", C.c_uint8), ("pad", C.c_uint8), ("epsilon", C.c_uint64)]
-
-    def __init__(self, learning_rate=1, step_shift=4, beta1_decay_shift=3, beta2_decay_shift=7, epsilon=1):
-        super().__init__(learning_rate, step_shift, beta1_decay_shift, beta2_decay_shift, 0, epsilon)
-
-
 class IntegerAdamState:
     """IntegerAdamStateWorkspace on the device: step, moments, update residuals."""
 

@@ -560,3 +560,89 @@ def integer_adam(acc, count, weights, cfg: AdamConfig, state: AdamState):
         return None
     state.step = st.value
     return [int(s) for s in stats]
+
+
+ADAM_SCOPES = ("all", "rms_norm", "output", "final_mlp", "final_mlp_and_output")
+
+
+def adam_state_layout(model: TrainModel):
+    """mini_transformer_adam_state_ranges (nsrl-train/src/lib.rs:4165-4196):
+    embeddings, positions, attention RMS, MLP RMS, then q, k, v, o, up, gate,
+    down over all layers, then the output head."""
+    d, F, L, S = model.d, model.F, len(model.layers), model.S
+    rms = model.layers[0].get("attn_gamma") is not None
+    lay, off = {}, 0
+    for key, n in (("emb", 256 * d), ("pos", S * d if model.positions is not None else 0),
+                   ("rms_attn", L * d if rms else 0), ("rms_mlp", L * d if rms else 0)):
+        lay[key] = off
+        off += n
+    for nm, n in zip(LAYER_LINEARS, [d * d] * 4 + [F * d] * 3):
+        lay[nm] = off
+        off += L * n
+    lay["output"] = off
+    lay["total"] = off + 256 * d
+    return lay
+
+
+def adam_train_step(model: TrainModel, state: AdamState, contexts, targets, cfg: AdamConfig, scope="all",
+                    workers=1):
+    """One map-reduce batch and the integer-Adam batch apply
+    (mini_transformer_apply_integer_adam_batch, lib.rs:4270-4465) in place on
+    the model's numpy weights and `state` (one flat state in adam_state_layout
+    order; its step advances once per batch, the slices' own steps are
+    ignored, lib.rs:4447-4451).  Returns the stats dict, or None when the
+    batch is rejected."""
+    r = train_windows(model, contexts, targets, workers=workers)
+    if r is None:
+        return None
+    acc, counts, stats = r
+    lay = model.arena_layout()
+    sl = adam_state_layout(model)
+    L = len(model.layers)
+    rms = model.layers[0].get("attn_gamma") is not None
+    tot = [0, 0, 0]
+
+    def apply(arena_key, weights, count, state_off):
+        o, n = lay[arena_key]
+        flat = weights.reshape(-1)
+        a = np.ascontiguousarray(acc[o:o + n])
+        st = np.zeros(3, np.uint64)
+        stp = C.c_uint64(0)
+        fn = lib().orc_integer_adam_i8 if flat.dtype == np.int8 else lib().orc_integer_adam_i16
+        rr = fn(_p(a), C.c_uint64(int(count)), _p(flat), C.c_size_t(n), C.byref(cfg),
+                C.c_void_p(state.first.ctypes.data + 8 * state_off),
+                C.c_void_p(state.second.ctypes.data + 8 * state_off),
+                C.c_void_p(state.residuals.ctypes.data + 8 * state_off), C.byref(stp), _p(st))
+        if rr:
+            return False
+        for i in range(3):
+            tot[i] += int(st[i])
+        return True
+
+    ok = True
+    if scope in ("all", "output", "final_mlp_and_output"):
+        ok &= apply("head", model.head.weights, counts[0], sl["output"])
+    d, F = model.d, model.F
+    sizes = dict(zip(LAYER_LINEARS, [d * d] * 4 + [F * d] * 3))
+    for li, ly in enumerate(model.layers):
+        if scope == "all":
+            for j, nm in enumerate(("q", "k", "v", "o")):
+                ok &= apply((li, nm), ly[nm].weights, counts[1 + 9 * li + j], sl[nm] + li * sizes[nm])
+        if scope == "all" or (scope in ("final_mlp", "final_mlp_and_output") and li + 1 == L):
+            for nm in ("down", "up", "gate"):
+                j = LAYER_LINEARS.index(nm)
+                ok &= apply((li, nm), ly[nm].weights, counts[1 + 9 * li + j], sl[nm] + li * sizes[nm])
+        if scope in ("all", "rms_norm") and rms:
+            ok &= apply((li, "rms_attn"), ly["attn_gamma"], counts[1 + 9 * li + 7], sl["rms_attn"] + li * d)
+            ok &= apply((li, "rms_mlp"), ly["mlp_gamma"], counts[1 + 9 * li + 8], sl["rms_mlp"] + li * d)
+    if scope == "all":
+        ce = counts[1 + 9 * L]
+        ok &= apply("emb", model.embeddings, ce, sl["emb"])
+        if model.positions is not None:
+            ok &= apply("pos", model.positions, ce, sl["pos"])
+    if not ok:
+        return None
+    state.step += 1
+    stats = dict(stats)
+    stats.update({"gradient_saturation_count": tot[0], "zero_delta_count": tot[1], "weight_delta_l1": tot[2]})
+    return stats

@@ -1,0 +1,138 @@
+"""The data-parallel step behind the C ABI (nsrl_train_dp_step) on one GPU:
+the integer-Adam optimizer in every train scope, a rejected batch, an
+invalid learning-rate config, and the ordered worker merge it falls back
+to, each against the oracle bit for bit."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+
+from train_models import random_model, random_windows
+
+pytestmark = pytest.mark.gpu
+
+
+def _train():
+    from nsrl_b200 import build, train
+    build.build()
+    return train
+
+
+def _gpu_model(m):
+    from test_gpu_train_step import to_gpu
+    return to_gpu(m)
+
+
+def _check_model(m, gm):
+    assert np.array_equal(gm.head.weights.cpu().numpy(), m.head.weights)
+    for ly, gly in zip(m.layers, gm.layers):
+        for nm in O.LAYER_LINEARS:
+            assert np.array_equal(gly[nm].weights.cpu().numpy(), ly[nm].weights), nm
+        for g in ("attn_gamma", "mlp_gamma"):
+            if ly.get(g) is not None:
+                assert np.array_equal(gly[g].cpu().numpy(), ly[g]), g
+    assert np.array_equal(gm.embeddings.cpu().numpy(), m.embeddings)
+    if m.positions is not None:
+        assert np.array_equal(gm.positions.cpu().numpy(), m.positions)
+
+
+@pytest.mark.parametrize("scope", ["all", "rms_norm", "output", "final_mlp", "final_mlp_and_output"])
+def test_integer_adam_step_every_scope(scope):
+    """Three batches with integer Adam as the optimizer (lib.rs:4270-4465):
+    weights, RMS gammas, embeddings, the moments, the update residuals and
+    the step, against the oracle's map-reduce batch and Adam batch apply."""
+    T = _train()
+    d, H, F, L, S, W = 64, 4, 128, 2, 16, 4
+    m = random_model(d, H, F, L, S, rms=True, positions=True, seed=51)
+    gm = _gpu_model(m)
+    acfg = (1, 4, 3, 7, 1)
+    ocfg = O.AdamConfig(*acfg)
+    ostate = O.AdamState(O.adam_state_layout(m)["total"])
+    state = T.TrainState(gm, adam=True)
+    assert state.adam.first_moments.numel() == ostate.first.size
+    cfg = T.MiniTransformerTrainConfig(optimizer="integer_adam", adam=acfg, adam_scope=scope)
+    buf = T.TrainStepBuffers(gm, W)
+    for step in range(3):
+        ctx, tgt = random_windows(W, S, seed=60 + step)
+        ref = O.adam_train_step(m, ostate, ctx, tgt, ocfg, scope=scope)
+        got = T.mini_transformer_train_step(gm, state, torch.from_numpy(ctx).cuda(), torch.from_numpy(tgt).cuda(),
+                                            cfg, buf)
+        assert ref is not None and got == ref, (step, got, ref)
+        _check_model(m, gm)
+        assert np.array_equal(state.adam.first_moments.cpu().numpy(), ostate.first)
+        assert np.array_equal(state.adam.second_moments.cpu().numpy().view(np.uint64), ostate.second)
+        assert np.array_equal(state.adam.update_residuals.cpu().numpy(), ostate.residuals)
+        assert int(state.adam.step.item()) == ostate.step == step + 1
+
+
+def test_rejected_batch_leaves_the_model_unchanged():
+    """A forward multiplier other than 1 is a rejection of the training step
+    (the reference's scale tables all have multiplier 1): the whole batch is
+    rejected and nothing is applied (lib.rs:5371-5375)."""
+    T = _train()
+    from nsrl_b200 import core
+    d, H, F, L, S, W = 64, 4, 128, 1, 16, 2
+    m = random_model(d, H, F, L, S, seed=5)
+    gm = _gpu_model(m)
+    gm.layers[0]["up"] = core.Linear(gm.layers[0]["up"].weights, core.make_scales(2, 10, F))
+    before = [gm.head.weights.clone()] + [gm.layers[0][n].weights.clone() for n in O.LAYER_LINEARS]
+    emb = gm.embeddings.clone()
+    state = T.TrainState(gm)
+    ctx, tgt = random_windows(W, S, seed=3)
+    out = T.mini_transformer_train_step(gm, state, torch.from_numpy(ctx).cuda(), torch.from_numpy(tgt).cuda(),
+                                        T.MiniTransformerTrainConfig(), T.TrainStepBuffers(gm, W))
+    assert out is None
+    after = [gm.head.weights] + [gm.layers[0][n].weights for n in O.LAYER_LINEARS]
+    assert all(torch.equal(a, b) for a, b in zip(before, after))
+    assert torch.equal(emb, gm.embeddings) and int(state.residuals.abs().sum()) == 0
+
+
+def test_shift_below_the_batch_shift_is_an_invalid_config():
+    """mini_transformer_batch_component_shift_config (lib.rs:13607-13650):
+    8 windows make a batch shift of 3, above an output shift of 2."""
+    T = _train()
+    d, H, F, L, S, W = 64, 4, 128, 1, 16, 8
+    m = random_model(d, H, F, L, S, seed=8)
+    gm = _gpu_model(m)
+    ctx, tgt = random_windows(W, S, seed=4)
+    cfg = T.MiniTransformerTrainConfig(output_learning_rate_shift=2)
+    with pytest.raises(ValueError, match="batch shift"):
+        T.mini_transformer_train_step(gm, T.TrainState(gm), torch.from_numpy(ctx).cuda(),
+                                      torch.from_numpy(tgt).cuda(), cfg, T.TrainStepBuffers(gm, W))
+
+
+@pytest.mark.parametrize("case", ["random", "overflow", "large_ok"])
+def test_ordered_worker_merge(case):
+    """nsrl_merge_worker_parts_i64 against the oracle's merge (lib.rs:7443-7471):
+    checked adds in worker order, including an overflow that only a prefix sees."""
+    T = _train()
+    from nsrl_b200 import core
+    L = T._lib_dp()
+    rng = np.random.default_rng(7)
+    workers, n = 4, 100_003
+    if case == "random":
+        parts = rng.integers(-2**50, 2**50, size=(workers, n), dtype=np.int64)
+    elif case == "overflow":  # 2^62 + 2^62 leaves i64 at the second worker; the total would come back
+        parts = np.zeros((workers, n), np.int64)
+        parts[:, 77] = [2**62, 2**62, -2**62, -2**62]
+    else:  # the all-reduce bound fails, no prefix overflows
+        parts = np.zeros((workers, n), np.int64)
+        parts[:, 5] = [2**62, -2**62, 2**62, -2**62]
+    counts = rng.integers(0, 1000, size=(workers, 9), dtype=np.uint64)
+    ref = O.merge_i64(parts, counts.sum(axis=1))
+    both = torch.from_numpy(np.concatenate([parts, counts.astype(np.int64)], axis=1)).cuda()
+    out = torch.empty(n + 9, dtype=torch.int64, device="cuda")
+    st = core.Status()
+    st.reset()
+    r = L.nsrl_merge_worker_parts_i64(core._ptr(both), workers, n, n + 9, core._ptr(out), core._ptr(st.buf),
+                                      core._stream())
+    assert r == core.NSRL_OK
+    code, _ = st.fetch()
+    if ref is None:
+        assert code == core.NSRL_CORE_REJECTED
+        return
+    assert code == core.NSRL_OK
+    got = out.cpu().numpy()
+    assert np.array_equal(got[:n], ref[0])
+    assert np.array_equal(got[n:].view(np.uint64), counts.sum(axis=0))
