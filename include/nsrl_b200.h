@@ -400,6 +400,10 @@ nsrl_status nsrl_comm_init(nsrl_comm** comm, int nranks, int rank, const uint8_t
                            uint64_t timeout_ms);
 /* Finalises (or, after a failure, aborts) and frees the communicator. */
 nsrl_status nsrl_comm_destroy(nsrl_comm* comm);
+/* Aborts the communicator now (ncclCommAbort): for a caller that learned on
+ * the host that a peer has left; every later step on it fails with
+ * NSRL_COMM_ERROR.  Free it with nsrl_comm_destroy. */
+nsrl_status nsrl_comm_abort(nsrl_comm* comm);
 int nsrl_comm_nranks(const nsrl_comm* comm);
 int nsrl_comm_rank(const nsrl_comm* comm);
 

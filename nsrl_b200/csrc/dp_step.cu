@@ -792,6 +792,15 @@ nsrl_status nsrl_comm_destroy(nsrl_comm* c) {
   return s;
 }
 
+nsrl_status nsrl_comm_abort(nsrl_comm* c) {
+  if (!c) return fail("null communicator");
+  if (!c->dead) {
+    c->dead = true;
+    nccl().CommAbort(c->comm);
+  }
+  return NSRL_OK;
+}
+
 int nsrl_comm_nranks(const nsrl_comm* c) { return c ? c->nranks : 0; }
 int nsrl_comm_rank(const nsrl_comm* c) { return c ? c->rank : -1; }
 

@@ -15,6 +15,7 @@ detection (a rejection, like the reference's `CoreRejected`).
 from __future__ import annotations
 
 import ctypes as C
+import datetime
 from typing import Optional, Sequence
 
 import torch
@@ -543,6 +544,7 @@ def _lib_dp():
         L.nsrl_comm_unique_id.argtypes = [vp]
         L.nsrl_comm_init.argtypes = [C.POINTER(C.c_void_p), C.c_int, C.c_int, vp, C.c_uint64]
         L.nsrl_comm_destroy.argtypes = [vp]
+        L.nsrl_comm_abort.argtypes = [vp]
         L.nsrl_comm_nranks.argtypes = [vp]
         L.nsrl_comm_rank.argtypes = [vp]
         L.nsrl_train_adam_state_len.restype = sz
@@ -563,6 +565,45 @@ class CommError(core.NsrlError):
     def __init__(self, code: int, msg: str):
         super().__init__(msg)
         self.code = code
+
+
+class PeerCheck:
+    """A host-side check, before every step, that all ranks of the group are
+    still there: each rank sets its key for the step in the group's store and
+    waits (bounded) for the others'.  A rank that has left is noticed here,
+    before any collective of the step is launched, so that no kernel waits on
+    or writes to a peer that is gone."""
+
+    def __init__(self, group=None, timeout_ms: int = 120_000, namespace: str = "nsrl"):
+        import torch.distributed as dist
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.timeout = datetime.timedelta(milliseconds=int(timeout_ms))
+        self.store = dist.PrefixStore(f"{namespace}/peers/", dist.distributed_c10d._get_default_store())
+        self.step = 0
+
+    def wait(self):
+        """Raises CommError when some rank does not arrive in time."""
+        k = self.step
+        self.step += 1
+        self.store.set(f"{k}/{self.rank}", "1")
+        try:
+            self.store.wait([f"{k}/{r}" for r in range(self.world)], self.timeout)
+        except Exception as e:  # the store's timeout, or its server gone with rank 0
+            missing = [r for r in range(self.world) if r != self.rank and not self._has(f"{k}/{r}")]
+            raise CommError(core.NSRL_COMM_ERROR, f"ranks {missing} did not arrive before step {k} "
+                                                  f"({type(e).__name__})") from e
+        if k >= 2:
+            try:
+                self.store.delete_key(f"{k - 2}/{self.rank}")
+            except Exception:
+                pass
+
+    def _has(self, key):
+        try:
+            return self.store.check([key])
+        except Exception:
+            return False
 
 
 class Communicator:
@@ -591,6 +632,17 @@ class Communicator:
         if r != core.NSRL_OK:
             raise CommError(r, L.nsrl_last_error().decode())
         self.handle = h
+        self.peers = PeerCheck(group, timeout_ms, namespace="nsrl/" + bytes(uid)[:8].hex())
+
+    def check_peers(self):
+        """The host-side peer check before a step; on failure the communicator
+        is aborted (nothing of the step has been launched) and CommError raised."""
+        try:
+            self.peers.wait()
+        except CommError:
+            if self.handle:
+                _lib_dp().nsrl_comm_abort(self.handle)
+            raise
 
     def close(self):
         if self.handle:
@@ -646,6 +698,8 @@ def mini_transformer_train_step(model: TrainModel, state: TrainState, contexts: 
     L = _lib_dp()
     if comm is None:
         comm = default_communicator(group)
+    if comm is not None:
+        comm.check_peers()
     m = model.c()
     st = _StepStatsC()
     cc = _config_c(cfg)

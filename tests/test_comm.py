@@ -95,3 +95,39 @@ def test_communicator_bootstrap_with_an_absent_rank(tmp_path):
     r0 = np.load(tmp_path / "boot0.npy", allow_pickle=True).item()
     assert r0["outcome"].startswith("group-error")
     assert r0["id"] is None and r0["elapsed"] < 60
+
+
+def _peers(rank, world, port, out_dir):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import torch.distributed as dist
+    from nsrl_b200 import train as T
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    pc = T.PeerCheck(timeout_ms=2000, namespace="test")
+    outcome = []
+    for step in range(3):
+        if rank == 1 and step == 2:
+            break  # rank 1 leaves between steps
+        t0 = time.time()
+        try:
+            pc.wait()
+            outcome.append(("ok", time.time() - t0))
+        except T.CommError as e:
+            outcome.append((f"comm-error-{e.code}: {e}", time.time() - t0))
+            break
+    np.save(os.path.join(out_dir, f"peers{rank}.npy"), np.array(outcome, dtype=object), allow_pickle=True)
+    if rank == 0:
+        time.sleep(0.5)  # keep the store (served by rank 0) up until rank 1 has saved
+
+
+def test_peer_check_notices_a_rank_that_left(tmp_path):
+    """Both ranks pass two steps; rank 1 then leaves and rank 0's check for the
+    third step fails with NSRL_COMM_ERROR after its 2 s limit, before anything
+    of that step would be launched."""
+    mp.start_processes(_peers, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True, start_method="spawn")
+    r0 = list(np.load(tmp_path / "peers0.npy", allow_pickle=True))
+    r1 = list(np.load(tmp_path / "peers1.npy", allow_pickle=True))
+    assert [o[0] for o in r1] == ["ok", "ok"]
+    assert [o[0] for o in r0[:2]] == ["ok", "ok"]
+    assert r0[2][0].startswith("comm-error-5") and "[1]" in r0[2][0]
+    assert 1.5 < r0[2][1] < 30

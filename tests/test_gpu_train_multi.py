@@ -84,3 +84,62 @@ def test_two_gpu_training_step_matches_one_worker(tmp_path):
                 assert np.array_equal(ly[nm], oly[nm].weights), nm
         assert np.array_equal(out["emb"], m.embeddings) and np.array_equal(out["pos"], m.positions)
         assert np.array_equal(out["res"], res)
+
+
+def _leaving_rank(rank, world, port, out_dir):
+    """Two data-parallel steps, then rank 1 leaves between steps (none of its
+    work in flight: the step call returns only when its GPU work is done).
+    Rank 0 learns of it on the host, in the peer check before its third step,
+    so nothing of that step is launched; the communicator is aborted and the
+    GPU stays usable.  NVLS is off (a rank leaving while bound to an NVLink
+    multicast object is to be avoided)."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    import datetime
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    from nsrl_b200 import core, train as T
+    from test_gpu_train_step import to_gpu
+    m = random_model(D, H, F, L, S, seed=77)
+    gm = to_gpu(m)
+    state = T.TrainState(gm)
+    per = W // world
+    buf = T.TrainStepBuffers(gm, per, nranks=world)
+    cfg = T.MiniTransformerTrainConfig(**SHIFTS)
+    comm = T.Communicator(timeout_ms=4000)
+    out = []
+    for step in range(3):
+        if rank == 1 and step == 2:
+            T._lib_dp().nsrl_comm_abort(comm.handle)  # leaves as a failed rank would: no finalize handshake
+            comm.close()
+            break
+        ctx, tgt = random_windows(W, S, seed=90 + step)
+        lo, hi = rank * per, (rank + 1) * per
+        try:
+            r = T.mini_transformer_train_step(gm, state, torch.from_numpy(ctx[lo:hi]).cuda(),
+                                              torch.from_numpy(tgt[lo:hi]).cuda(), cfg, buf, comm=comm)
+            out.append("ok" if r is not None else "rejected")
+        except T.CommError as e:
+            out.append(f"comm-error-{e.code}")
+            break
+    if rank == 0:
+        comm.close()  # aborted already: frees it
+        lin = core.Linear(torch.eye(64, dtype=torch.int8), core.make_scales(1, 0, 64))
+        x = torch.arange(64 * 64, dtype=torch.int16).reshape(64, 64).cuda()
+        y = core.linear_i16_i8_i16_per_channel_checked(x, lin)
+        out.append("gpu-ok" if y is not None and torch.equal(y, x) else "gpu-bad")
+    np.save(os.path.join(out_dir, f"leave{rank}.npy"), np.array(out, dtype=object), allow_pickle=True)
+    if rank == 0:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_gpu_rank_leaving_between_steps(tmp_path):
+    mp.start_processes(_leaving_rank, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True,
+                       start_method="spawn")
+    r0 = list(np.load(tmp_path / "leave0.npy", allow_pickle=True))
+    r1 = list(np.load(tmp_path / "leave1.npy", allow_pickle=True))
+    assert r1 == ["ok", "ok"]
+    assert r0 == ["ok", "ok", "comm-error-5", "gpu-ok"]
