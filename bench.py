@@ -667,6 +667,67 @@ def run_block_hd16(core, torch, bw, x_np, flush, hbm, tfl, src, steps=5):
             "parity": {"sequences": 2, "of": BATCH, "equal": eq}}
 
 
+def run_generate(core, torch, batch=64, steps=16, prompt_len=256, warmup=1):
+    """Byte generation with the training workload's model (4 layers, d256,
+    4 x 64 heads, seq 512): `batch` prompts of `prompt_len` bytes, `steps`
+    sampled bytes each (top-k 40), every step the full forward of each
+    512-byte window as the reference computes it.  Tokens/s = batch * steps
+    / time; parity: sequence 0's first 4 bytes against the oracle."""
+    from nsrl_b200 import generate as G
+    from nsrl_b200 import synth as Y
+    O = oracle_module()
+    tw = Y.TrainWeights(seed=4040, layers=TR_LAYERS, d=TR_D, hidden=TR_F, seq_len=TR_S)
+    head_shift = 15  # a live byte softmax at this model's feature scale
+    layers = []
+    olayers = []
+    for bw in tw.blocks:
+        e = {nm: core.Linear(torch.from_numpy(getattr(bw, nm)), core.make_scales(1, bw.shift[nm], bw.out_dim(nm)))
+             for nm in LINEARS}
+        e["attn_gamma"], e["mlp_gamma"] = torch.from_numpy(bw.attn_gamma), torch.from_numpy(bw.mlp_gamma)
+        layers.append(e)
+        o = {nm: O.Linear(getattr(bw, nm), O.scales(1, bw.shift[nm], bw.out_dim(nm))) for nm in LINEARS}
+        o["attn_gamma"], o["mlp_gamma"] = bw.attn_gamma, bw.mlp_gamma
+        olayers.append(o)
+    from nsrl_b200 import train as TT
+    gm = TT.TrainModel(torch.from_numpy(tw.embeddings), torch.from_numpy(tw.positions), layers,
+                       core.Linear(torch.from_numpy(tw.head), core.make_scales(1, head_shift, 256)), TR_D, TR_H, TR_F,
+                       TR_S)
+    draws = Y.splitmix(0x6E4E, batch * prompt_len) >> np.uint64(57)
+    prompts = [bytes((draws[b * prompt_len:(b + 1) * prompt_len] + 32).astype(np.uint8)) for b in range(batch)]
+    gen = G.Generator(gm, batch, prompt_len, steps)
+    host = torch.from_numpy(np.frombuffer(b"".join(prompts), np.uint8).reshape(batch, prompt_len).copy())
+    for _ in range(warmup):
+        gen(prompts, "sample", 40, 7)
+    gen.contexts[:, :prompt_len].copy_(host)
+    gen.status.reset()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    r = gen.launch([prompt_len] * batch, "sample", 40, 7)
+    b.record()
+    torch.cuda.synchronize()
+    if r != 0 or gen.status.fetch()[0] != 0:
+        raise RuntimeError("generation rejected")
+    ms = a.elapsed_time(b)
+    toks = gen.tokens.cpu().numpy()
+    om = O.TrainModel(tw.embeddings, tw.positions, olayers, O.Linear(tw.head, O.scales(1, head_shift, 256)), TR_D,
+                      TR_H, TR_F, TR_S)
+    t0 = time.perf_counter()
+    ref = O.generate(om, prompts[0], 4, "sample", 40, 7)
+    cpu_s = time.perf_counter() - t0
+    eq = ref is not None and bool(np.array_equal(toks[0, :4], ref[0]))
+    if not eq:
+        raise RuntimeError("generated bytes differ from the oracle")
+    return {"workload": f"byte generation, {TR_LAYERS}-layer d{TR_D} h{TR_H}x{TR_D // TR_H} ff{TR_F} window {TR_S}, "
+                        f"batch {batch}, prompts of {prompt_len} bytes, {steps} sampled bytes (top-k 40), full "
+                        f"window forward per step",
+            "value": batch * steps / (ms / 1000.0), "unit": "generated tokens/s", "ms_per_step": ms / steps,
+            "steps": steps, "batch": batch,
+            "cpu_oracle": {"value": 4 / cpu_s, "unit": "generated tokens/s", "cores": 1,
+                           "sample": "4 bytes of one sequence"},
+            "parity": {"sequences": 1, "bytes": 4, "equal": eq}}
+
+
 def run_secondary(args):
     """One secondary measurement alone on cuda:0 (its JSON object on one line)."""
     import torch
@@ -677,6 +738,8 @@ def run_secondary(args):
     if args.case == "decode":
         out = run_decode(core, torch, steps=args.steps, warmup=args.warmup, hbm=hbm, flush=flush,
                          batch=args.decode_batch)
+    elif args.case == "generate":
+        out = run_generate(core, torch)
     elif args.case == "train":
         out = run_train(core, torch, None, 1, 0, steps=args.steps, warmup=args.warmup, flush=flush, hbm=hbm, tfl=tfl,
                         src=peaks()[2], cpu_baseline=not args.no_cpu_baseline, batch=args.train_windows)
@@ -694,7 +757,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip the decode and linear-sweep measurements")
-    ap.add_argument("--case", default="block", choices=["block", "decode", "sweep", "train"],
+    ap.add_argument("--case", default="block", choices=["block", "decode", "sweep", "train", "generate"],
                     help="decode / sweep / train: run only that secondary measurement on one GPU")
     ap.add_argument("--decode-batch", type=int, default=DEC_B)
     ap.add_argument("--train-steps", type=int, default=3, help="timed steps of the training-step measurement")
@@ -873,6 +936,7 @@ def main():
             out["config1_latency"] = run_config1(core, torch, flush)
             out["block_hd16"] = run_block_hd16(core, torch, bw, x_np, flush, hbm, tfl, src)
             out["decode"] = run_decode(core, torch, steps=8, warmup=2, hbm=hbm, flush=flush)
+            out["generate"] = run_generate(core, torch)
             out["linear_sweep"] = run_sweep(core, torch, hbm, tfl, flush)
         if train_out is not None:
             out["train"] = train_out

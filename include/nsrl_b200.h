@@ -495,6 +495,42 @@ nsrl_status nsrl_merge_worker_parts_i64(const long long* parts, size_t workers, 
  * and *aborted tell how many polls ran and whether the abort was called. */
 nsrl_status nsrl_comm_selftest_wait(int scenario, uint64_t timeout_ms, uint64_t* polls, int* aborted);
 
+/* ------------------------------------------------------------ generation --
+ * Byte generation with the mini transformer (softmax attention), the
+ * reference's generate_mini_transformer (nsrl-train/src/lib.rs:12702-12800)
+ * batched over sequences and kept on the device: every step takes the last
+ * seq_len bytes of each context, left-padded with ' ', runs the full forward
+ * (:14911-15008), the byte head and its base-2 softmax on the last position
+ * (:17455-17490), and picks the next byte (:18979-19100).  The reference's
+ * window slides (and its positions shift) every step, so the whole window is
+ * recomputed, as the reference does: a KV cache cannot reproduce these
+ * steps; nsrl_prenorm_attention_decode_block serves callers whose context
+ * does not slide.  `model` is the training model struct (only read). */
+typedef struct nsrl_decode_config {
+  int32_t strategy;     /* 0: greedy (argmax, lowest index on ties); 1: sample */
+  uint32_t top_k;       /* sample among the top_k logits (0 = all 256) */
+  uint64_t sample_seed; /* decode_sample_u64 seed (lib.rs:19334-19340) */
+} nsrl_decode_config;
+
+size_t nsrl_generate_workspace_size(const nsrl_train_model* model, size_t batch);
+/* windows [batch][seq_len] uint8 (device) -> logits_q8 [batch][256] int32
+ * and probs_q15 [batch][256] int16 of each window's last position. */
+nsrl_status nsrl_mini_transformer_output_rows(const nsrl_train_model* model, const uint8_t* windows, size_t batch,
+                                              int32_t* logits_q8, int16_t* probs_q15, void* workspace,
+                                              size_t workspace_bytes, nsrl_device_status* status, void* stream);
+/* contexts [batch][capacity] uint8 (device) hold each prompt at the start;
+ * prompt_lens [batch] (HOST int32, 1..capacity-steps).  Runs `steps` steps:
+ * the chosen byte of step i is appended to each context and written to
+ * tokens [batch][steps]; pick_logits / pick_probs [batch][steps] (device, or
+ * NULL) get its logit and probability.  Asynchronous on `stream`.  The
+ * decode options beyond greedy and seeded top-k sampling (priors,
+ * penalties, printable filters) are not offered. */
+nsrl_status nsrl_mini_transformer_generate(const nsrl_train_model* model, uint8_t* contexts, size_t capacity,
+                                           const int32_t* prompt_lens, size_t batch, size_t steps,
+                                           const nsrl_decode_config* decode, uint8_t* tokens, int32_t* pick_logits,
+                                           int16_t* pick_probs, void* workspace, size_t workspace_bytes,
+                                           nsrl_device_status* status, void* stream);
+
 /* The transformer block over HOST buffers (pinned host memory for the
  * overlap): the batch runs in steps of at most `chunk` sequences; the copy
  * in of step i+1, the block of step i and the copy out of step i-1 overlap

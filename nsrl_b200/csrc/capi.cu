@@ -222,7 +222,10 @@ nsrl_status mlp_block(const int16_t* x, size_t T, size_t d, size_t F, const int1
   Planes gated = c.planes(T, F, true);
   if (!needs_l1(d, upp, gatep)) xn.l1 = nullptr;
   if (!needs_l1(F, downp)) gated.l1 = nullptr;
-  NSRL_TRY(launch_rms_norm(x, T, d, gamma, eps, nullptr, xn, st, stream), "rms norm");
+  if (gamma)
+    NSRL_TRY(launch_rms_norm(x, T, d, gamma, eps, nullptr, xn, st, stream), "rms norm");
+  else  // the mini transformer without RMS norm: the block reads x itself
+    NSRL_TRY(launch_split_planes(x, T, d, d, xn, stream), "split");
   if (gated.l1) NSRL_TRY(cudaMemsetAsync(gated.l1, 0, T * sizeof(unsigned long long), stream), "memset");
   GemmArgs g{};
   g.a_hi = xn.hi;
@@ -273,7 +276,10 @@ nsrl_status attention_block(const int16_t* x, size_t B, size_t S, size_t d, size
     ctx16 = c.take<int16_t>(T * d);
   }
   if (!needs_l1(d, q, k, v)) xn.l1 = nullptr;
-  NSRL_TRY(launch_rms_norm(x, T, d, gamma, eps, nullptr, xn, st, stream), "rms norm");
+  if (gamma)
+    NSRL_TRY(launch_rms_norm(x, T, d, gamma, eps, nullptr, xn, st, stream), "rms norm");
+  else  // the mini transformer without RMS norm: the block reads x itself
+    NSRL_TRY(launch_split_planes(x, T, d, d, xn, stream), "split");
   return attention_core(xn, B, S, d, H, causal, q, k, v, o, qkv, ctx, vt, qkv16, ctx16, Epi::RESID, x, y,
                         &st->attention_saturations, st, stream);
 }
@@ -737,6 +743,132 @@ nsrl_status nsrl_attention_decode(const int16_t* q, const int16_t* k_cache, cons
   NSRL_TRY(launch_decode_attention(q, k_cache, v_cache, lens, batch, heads, head_dim, max_len, ctx, status,
                                    (cudaStream_t)stream),
            "decode attention");
+  return NSRL_OK;
+}
+
+// ------------------------------------------------------------- generation --
+namespace {
+// The forward of B windows of the mini transformer (softmax attention): the
+// embedding, then per layer the prenorm attention block and the prenorm
+// gated-MLP block (the training model's block, nsrl-train/src/lib.rs:
+// 15079-15294; RMS norm off when the layer has no gammas), then the byte
+// head and its softmax on the last position of every window.
+size_t gen_ws(const nsrl_train_model* m, size_t B, Carver* c) {
+  Carver local(nullptr);
+  Carver& k = c ? *c : local;
+  const size_t start = k.off;
+  const size_t T = B * m->seq_len;
+  k.take<uint8_t>(T);                 // windows
+  k.take<int16_t>(T * m->d_model);    // x
+  k.take<int16_t>(T * m->d_model);    // h
+  k.take<int32_t>(B * 256);           // logits
+  k.take<int16_t>(B * 256);           // probabilities
+  k.take<int32_t>(B);                 // context lengths
+  k.off += std::max(attention_ws(B, m->seq_len, m->d_model, m->heads), mlp_ws(T, m->d_model, m->hidden_dim));
+  return k.off - start;
+}
+
+nsrl_status validate_gen_model(const nsrl_train_model* m) {
+  if (!m || !m->layer || m->layers == 0 || !m->embeddings) return shape_fail("model with embeddings and layers");
+  const size_t d = m->d_model, S = m->seq_len;
+  nsrl_status r = validate_attention(S, d, m->heads, &m->layer[0].lin[0], &m->layer[0].lin[1], &m->layer[0].lin[2],
+                                     &m->layer[0].lin[3]);
+  if (r != NSRL_OK) return r;
+  if (d > 4096) return shape_fail("d_model <= 4096 for the byte head");
+  if (!linear_ok(&m->head, d, 256)) return shape_fail("head must be [256][d_model]");
+  const bool rms = m->layer[0].attn_gamma != nullptr;
+  for (size_t l = 0; l < m->layers; ++l) {
+    const nsrl_train_layer& L = m->layer[l];
+    if ((L.attn_gamma != nullptr) != rms || (L.mlp_gamma != nullptr) != rms)
+      return shape_fail("RMS gammas: both or neither, the same in every layer");
+    if ((r = validate_attention(S, d, m->heads, &L.lin[0], &L.lin[1], &L.lin[2], &L.lin[3])) != NSRL_OK) return r;
+    if ((r = validate_mlp(S, d, m->hidden_dim, &L.lin[4], &L.lin[5], &L.lin[6])) != NSRL_OK) return r;
+  }
+  return NSRL_OK;
+}
+
+// windows (device [B][S]) -> logits / probabilities [B][256] through the workspace carver.
+nsrl_status gen_forward(const nsrl_train_model* m, const uint8_t* win, size_t B, int32_t* logits, int16_t* probs,
+                        Carver& c, int16_t* x, int16_t* h, nsrl_device_status* st, cudaStream_t s) {
+  const size_t S = m->seq_len, d = m->d_model, T = B * S;
+  NSRL_TRY(launch_embed(win, T, S, d, m->embeddings, m->positions, x, s), "embedding");
+  const size_t mark = c.off;
+  for (size_t l = 0; l < m->layers; ++l) {
+    const nsrl_train_layer& L = m->layer[l];
+    c.off = mark;
+    nsrl_status r = attention_block(x, B, S, d, m->heads, true, L.attn_gamma, 1, &L.lin[0], &L.lin[1], &L.lin[2],
+                                    &L.lin[3], h, c, st, s);
+    if (r != NSRL_OK) return r;
+    c.off = mark;
+    r = mlp_block(h, T, d, m->hidden_dim, L.mlp_gamma, 1, &L.lin[4], &L.lin[5], &L.lin[6], x, c, st, s);
+    if (r != NSRL_OK) return r;
+  }
+  NSRL_TRY(launch_head_rows(x, S * d, (S - 1) * d, B, d, &m->head, logits, probs, st, s), "byte head");
+  return NSRL_OK;
+}
+}  // namespace
+
+size_t nsrl_generate_workspace_size(const nsrl_train_model* model, size_t batch) {
+  if (validate_gen_model(model) != NSRL_OK || batch == 0) return 0;
+  return gen_ws(model, batch, nullptr);
+}
+
+nsrl_status nsrl_mini_transformer_output_rows(const nsrl_train_model* m, const uint8_t* windows, size_t batch,
+                                              int32_t* logits_q8, int16_t* probs_q15, void* workspace,
+                                              size_t workspace_bytes, nsrl_device_status* status, void* stream) {
+  nsrl_status r = validate_gen_model(m);
+  if (r != NSRL_OK) return r;
+  if (!windows || !logits_q8 || !probs_q15 || !status) return shape_fail("NULL argument");
+  if (batch == 0) return NSRL_OK;
+  if (!workspace || workspace_bytes < gen_ws(m, batch, nullptr)) return shape_fail("workspace too small");
+  cudaStream_t s = (cudaStream_t)stream;
+  const size_t T = batch * m->seq_len;
+  Carver c(workspace);
+  c.take<uint8_t>(T);
+  int16_t* x = c.take<int16_t>(T * m->d_model);
+  int16_t* h = c.take<int16_t>(T * m->d_model);
+  c.take<int32_t>(batch * 256);
+  c.take<int16_t>(batch * 256);
+  c.take<int32_t>(batch);
+  return gen_forward(m, windows, batch, logits_q8, probs_q15, c, x, h, status, s);
+}
+
+nsrl_status nsrl_mini_transformer_generate(const nsrl_train_model* m, uint8_t* contexts, size_t capacity,
+                                           const int32_t* prompt_lens, size_t batch, size_t steps,
+                                           const nsrl_decode_config* decode, uint8_t* tokens, int32_t* pick_logits,
+                                           int16_t* pick_probs, void* workspace, size_t workspace_bytes,
+                                           nsrl_device_status* status, void* stream) {
+  nsrl_status r = validate_gen_model(m);
+  if (r != NSRL_OK) return r;
+  if (!contexts || !prompt_lens || !decode || !tokens || !status) return shape_fail("NULL argument");
+  if (decode->strategy != 0 && decode->strategy != 1) return shape_fail("decode strategy: 0 greedy, 1 sample");
+  if (batch == 0 || steps == 0) return NSRL_OK;
+  if (steps > (size_t)INT32_MAX || capacity > (size_t)INT32_MAX) return shape_fail("steps / capacity too large");
+  for (size_t b = 0; b < batch; ++b)  // lib.rs:12735: an empty prompt is InvalidConfig
+    if (prompt_lens[b] <= 0 || (size_t)prompt_lens[b] + steps > capacity)
+      return shape_fail("every prompt needs 1..capacity-steps bytes");
+  if (!workspace || workspace_bytes < gen_ws(m, batch, nullptr)) return shape_fail("workspace too small");
+  cudaStream_t s = (cudaStream_t)stream;
+  const size_t T = batch * m->seq_len;
+  Carver c(workspace);
+  uint8_t* win = c.take<uint8_t>(T);
+  int16_t* x = c.take<int16_t>(T * m->d_model);
+  int16_t* h = c.take<int16_t>(T * m->d_model);
+  int32_t* logits = c.take<int32_t>(batch * 256);
+  int16_t* probs = c.take<int16_t>(batch * 256);
+  int32_t* lens = c.take<int32_t>(batch);
+  // from pageable memory: staged before the call returns
+  NSRL_TRY(cudaMemcpyAsync(lens, prompt_lens, batch * sizeof(int32_t), cudaMemcpyHostToDevice, s), "lengths");
+  const size_t mark = c.off;
+  for (size_t step = 0; step < steps; ++step) {
+    c.off = mark;
+    NSRL_TRY(launch_gen_windows(contexts, capacity, lens, m->seq_len, batch, win, s), "windows");
+    r = gen_forward(m, win, batch, logits, probs, c, x, h, status, s);
+    if (r != NSRL_OK) return r;
+    NSRL_TRY(launch_select(logits, probs, batch, decode->strategy, (int)decode->top_k, decode->sample_seed, (int)step,
+                           contexts, capacity, lens, (int)steps, tokens, pick_logits, pick_probs, s),
+             "select");
+  }
   return NSRL_OK;
 }
 

@@ -189,6 +189,20 @@ class ProfScope {
   cudaEvent_t ev_;
 };
 
+// Generation (generate.cu): context windows [B][S] (last bytes, left-padded
+// with ' '), embeddings + positions, the byte head with its softmax on one row
+// per sequence, and the device-side choice of the next byte.
+cudaError_t launch_gen_windows(const uint8_t* ctx, size_t cap, const int32_t* lens, size_t S, size_t B, uint8_t* win,
+                               cudaStream_t s);
+cudaError_t launch_embed(const uint8_t* win, size_t rows, size_t S, size_t d, const int16_t* emb,
+                         const int16_t* pos, int16_t* x, cudaStream_t s);
+cudaError_t launch_head_rows(const int16_t* x, size_t row_stride, size_t row0, size_t B, size_t d,
+                             const nsrl_linear_params* head, int32_t* logits, int16_t* probs, nsrl_device_status* st,
+                             cudaStream_t s);
+cudaError_t launch_select(const int32_t* logits, const int16_t* probs, size_t B, int strategy, int top_k,
+                          uint64_t seed, int step, uint8_t* ctx, size_t cap, int32_t* lens, int steps,
+                          uint8_t* tokens, int32_t* pick_logit, int16_t* pick_prob, cudaStream_t s);
+
 void set_error(const char* fmt, ...);
 bool tma_supported();
 

@@ -1306,9 +1306,121 @@ static bool train_window(const TrainModel& m, const uint8_t* ctx, uint8_t target
   return true;
 }
 
+// nsrl-train/src/lib.rs:14911-15008 (softmax attention, learned or no
+// positions) and :17455-17490: the forward of one window and the byte-head
+// row of its last position.  false = CoreRejected.
+static bool output_row(const TrainModel& m, const uint8_t* window, int32_t* logits_q8, int16_t* probs_q15) {
+  const size_t S = m.S, d = m.d, T = S * d;
+  std::vector<int16_t> x(T);
+  for (size_t t = 0; t < S; ++t)
+    for (size_t i = 0; i < d; ++i) {
+      int64_t v = m.embeddings[(size_t)window[t] * d + i];
+      if (m.positions) v += m.positions[t * d + i];
+      x[t * d + i] = saturate_i16(v);
+    }
+  BlockCache c;
+  uint64_t sat = 0;
+  std::vector<int16_t> cur = x;
+  for (size_t l = 0; l < m.layers; ++l) {
+    if (!block_forward_cache(m, m.layer[l], cur.data(), c, &sat)) return false;
+    cur = c.out;
+  }
+  int16_t logits16[VOCAB];
+  if (!linear_row(cur.data() + (S - 1) * d, m.head, logits16)) return false;
+  for (size_t i = 0; i < VOCAB; ++i) logits_q8[i] = logits16[i];
+  return base2_softmax(logits_q8, VOCAB, probs_q15, nullptr);
+}
+
+static uint64_t splitmix64(uint64_t v) {  // lib.rs:19342-19347
+  v += 0x9e3779b97f4a7c15ull;
+  v = (v ^ (v >> 30)) * 0xbf58476d1ce4e5b9ull;
+  v = (v ^ (v >> 27)) * 0x94d049bb133111ebull;
+  return v ^ (v >> 31);
+}
+
+// decode_sample_u64 (lib.rs:19334-19340) over the StableHasher (FNV-1a,
+// :19468-19519; usize values as 8 little-endian bytes, slices length-prefixed).
+static uint64_t decode_sample_u64(uint64_t seed, size_t step, const uint8_t* ctx, size_t n) {
+  Fnv f;
+  f.usize(seed);
+  f.usize((uint64_t)step);
+  f.usize((uint64_t)n);
+  f.bytes(ctx, n);
+  return splitmix64(f.h);
+}
+
+// select_byte_from_row_with_priors (lib.rs:18979-19083) with no priors and no
+// constraints: greedy = byte_argmax_i32 (lowest index among equal logits,
+// :18951-18958); sample = the top_k candidates by (logit desc, index asc),
+// weights max(p, 0), threshold = decode_sample_u64 % mass, walked in that
+// order; a zero mass falls back to the first candidate (:19085-19100).
+static uint8_t select_byte(const int32_t* logits, const int16_t* probs, int strategy, size_t top_k, uint64_t seed,
+                           size_t step, const uint8_t* ctx, size_t n) {
+  int best = 0;
+  for (int i = 1; i < (int)VOCAB; ++i)
+    if (logits[i] > logits[best]) best = i;
+  if (strategy == 0) return (uint8_t)best;
+  const size_t k = (top_k == 0 || top_k > VOCAB) ? VOCAB : top_k;
+  std::vector<int> cand(VOCAB);
+  for (int i = 0; i < (int)VOCAB; ++i) cand[i] = i;
+  std::stable_sort(cand.begin(), cand.end(), [&](int a, int b) { return logits[a] > logits[b]; });
+  cand.resize(k);
+  uint64_t mass = 0;
+  for (int c : cand) mass += (uint64_t)std::max<int>(probs[c], 0);
+  if (mass == 0) return (uint8_t)cand[0];
+  uint64_t th = decode_sample_u64(seed, step, ctx, n) % mass;
+  for (int c : cand) {
+    const uint64_t w = (uint64_t)std::max<int>(probs[c], 0);
+    if (th < w) return (uint8_t)c;
+    th -= w;
+  }
+  return (uint8_t)cand[0];
+}
+
 }  // namespace orc
 
 extern "C" {
+
+// The byte-head rows of B windows [B][S] (one per thread of `threads`).
+int orc_output_rows(const TrainModel* m, const uint8_t* windows, size_t B, int32_t* logits_q8, int16_t* probs_q15,
+                    int threads) {
+  std::atomic<int> bad{0};
+  std::atomic<size_t> next{0};
+  auto run = [&]() {
+    for (size_t b; (b = next++) < B;)
+      if (!output_row(*m, windows + b * m->S, logits_q8 + b * VOCAB, probs_q15 + b * VOCAB)) bad = 1;
+  };
+  std::vector<std::thread> pool;
+  for (int t = 1; t < std::max(1, threads); ++t) pool.emplace_back(run);
+  run();
+  for (auto& t : pool) t.join();
+  return bad ? 2 : 0;
+}
+
+// generate_mini_transformer_with_attention_kind_position_policy_priors_and_ttt_shift
+// (nsrl-train/src/lib.rs:12702-12800), base-2 softmax attention, no priors:
+// per step the last S bytes of the context, left-padded with ' ', run the
+// full forward; the selected byte is appended.  ctx holds the prompt (n
+// bytes) and has room for `steps` more; tokens, logit, prob: [steps].
+int orc_generate(const TrainModel* m, uint8_t* ctx, size_t n, size_t steps, int strategy, size_t top_k,
+                 uint64_t seed, uint8_t* tokens, int32_t* logit_out, int16_t* prob_out) {
+  if (n == 0 || m->S == 0) return 1;
+  std::vector<uint8_t> win(m->S);
+  int32_t logits[VOCAB];
+  int16_t probs[VOCAB];
+  for (size_t step = 0; step < steps; ++step) {
+    const size_t len = std::min(m->S, n);
+    std::fill(win.begin(), win.end(), (uint8_t)' ');
+    memcpy(win.data() + (m->S - len), ctx + (n - len), len);
+    if (!output_row(*m, win.data(), logits, probs)) return 2;
+    const uint8_t tok = select_byte(logits, probs, strategy, top_k, seed, step, ctx, n);
+    tokens[step] = tok;
+    if (logit_out) logit_out[step] = logits[tok];
+    if (prob_out) prob_out[step] = probs[tok];
+    ctx[n++] = tok;
+  }
+  return 0;
+}
 
 size_t orc_train_arena_len(const TrainModel* m) { return Arena(*m).total; }
 

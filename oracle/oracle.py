@@ -646,3 +646,35 @@ def adam_train_step(model: TrainModel, state: AdamState, contexts, targets, cfg:
     stats = dict(stats)
     stats.update({"gradient_saturation_count": tot[0], "zero_delta_count": tot[1], "weight_delta_l1": tot[2]})
     return stats
+
+
+# ------------------------------------------------------------- generation --
+def output_rows(model: TrainModel, windows, threads=1):
+    """The byte-head row (logits Q8 i32, probabilities Q15 i16) of the last
+    position of each window [B][S] (nsrl-train/src/lib.rs:14911-15008,
+    :17455-17490); None when a window is rejected."""
+    w = _c(windows, np.uint8)
+    B = w.shape[0]
+    logits = np.zeros((B, 256), np.int32)
+    probs = np.zeros((B, 256), np.int16)
+    ms = model.struct()
+    if lib().orc_output_rows(C.byref(ms), _p(w), C.c_size_t(B), _p(logits), _p(probs), C.c_int(threads)):
+        return None
+    return logits, probs
+
+
+def generate(model: TrainModel, prompt: bytes, steps: int, strategy="greedy", top_k=0, seed=0):
+    """generate_mini_transformer (lib.rs:12702-12800) with greedy or seeded
+    top-k sampling and no priors: (tokens, logits of the picks, probabilities
+    of the picks), or None on a rejection."""
+    ctx = np.zeros(len(prompt) + steps, np.uint8)
+    ctx[:len(prompt)] = np.frombuffer(bytes(prompt), np.uint8)
+    tok = np.zeros(steps, np.uint8)
+    lg = np.zeros(steps, np.int32)
+    pr = np.zeros(steps, np.int16)
+    ms = model.struct()
+    if lib().orc_generate(C.byref(ms), _p(ctx), C.c_size_t(len(prompt)), C.c_size_t(steps),
+                          C.c_int(0 if strategy == "greedy" else 1), C.c_size_t(top_k), C.c_uint64(seed), _p(tok),
+                          _p(lg), _p(pr)):
+        return None
+    return tok, lg, pr
