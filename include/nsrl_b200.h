@@ -237,6 +237,16 @@ nsrl_status nsrl_apply_embedding_gradient_i64_to_i16(const long long* accumulato
                                                      uint8_t learning_rate_shift, unsigned long long* stats,
                                                      nsrl_device_status* status, void* stream);
 
+/* The movement average of the per-window (serial) training mode
+ * (average_mini_transformer_batch_movement, nsrl-train/src/lib.rs:14515-14583):
+ * values[i] = sat(base[i] + round_div(values[i] - base[i], divisor)), the
+ * movement since the batch's checkpoint `base` divided by the accepted windows
+ * (half away from zero).  A tensor that the batch updates through i64
+ * accumulators (every tensor of nsrl_train_dp_step) is not averaged. */
+nsrl_status nsrl_average_movement_i8(const int8_t* base, int8_t* values, size_t len, uint64_t divisor, void* stream);
+nsrl_status nsrl_average_movement_i16(const int16_t* base, int16_t* values, size_t len, uint64_t divisor,
+                                      void* stream);
+
 /* Integer Adam (crates/nsrl-train-core/src/lib.rs:276-661): IntegerAdamConfig
  * with beta1 = 1 - 2^-beta1_decay_shift, beta2 = 1 - 2^-beta2_decay_shift. */
 typedef struct nsrl_integer_adam_config {

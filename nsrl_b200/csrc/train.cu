@@ -293,6 +293,20 @@ __global__ void apply_embedding_kernel(const long long* __restrict__ acc, long l
   }
 }
 
+// average_i8_movement / average_i16_movement (nsrl-train/src/lib.rs:14552-14583):
+// w = sat(base + round_div(w - base, divisor)), half away from zero.
+template <class W>
+__global__ void average_movement_kernel(const W* __restrict__ base, W* __restrict__ w, long long len, long long div,
+                                        int lo, int hi) {
+  const long long half = div / 2;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < len; i += (long long)gridDim.x * blockDim.x) {
+    const long long b = base[i], m = (long long)w[i] - b;  // |m| < 2^17: no overflow anywhere
+    const long long avg = m >= 0 ? (m + half) / div : -((-m + half) / div);
+    const long long v = b + avg;
+    w[i] = (W)(v < lo ? lo : (v > hi ? hi : v));
+  }
+}
+
 // ---------------------------------------------------------- integer Adam --
 // crates/nsrl-train-core/src/lib.rs:602-661 (integer_adam_delta) with the
 // reference's i128 intermediates as __int128.  Returns false on a rejection.
@@ -510,6 +524,44 @@ nsrl_status nsrl_apply_linear_weight_gradient_i64_to_i8(long long* accumulators,
   if (e == cudaSuccess) e = cudaMemsetAsync(sample_count, 0, sizeof(unsigned long long), s);
   if (e != cudaSuccess) {
     set_error("apply: %s", cudaGetErrorString(e));
+    return NSRL_CUDA_ERROR;
+  }
+  return NSRL_OK;
+}
+
+nsrl_status nsrl_average_movement_i8(const int8_t* base, int8_t* values, size_t len, uint64_t divisor, void* stream) {
+  if (!base || !values || divisor == 0 || divisor > (uint64_t)LLONG_MAX) {
+    set_error("invalid config: movement average (divisor must be nonzero)");
+    return NSRL_INVALID_SHAPE;
+  }
+  if (len == 0) return NSRL_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  const unsigned blocks = (unsigned)std::min<size_t>((len + 255) / 256, 148 * 8);
+  ProfScope prof("average_movement_i8", s, 0.0, 3.0 * (double)len);
+  average_movement_kernel<int8_t><<<blocks, 256, 0, s>>>(base, values, (long long)len, (long long)divisor, -128, 127);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("movement average: %s", cudaGetErrorString(e));
+    return NSRL_CUDA_ERROR;
+  }
+  return NSRL_OK;
+}
+
+nsrl_status nsrl_average_movement_i16(const int16_t* base, int16_t* values, size_t len, uint64_t divisor,
+                                      void* stream) {
+  if (!base || !values || divisor == 0 || divisor > (uint64_t)LLONG_MAX) {
+    set_error("invalid config: movement average (divisor must be nonzero)");
+    return NSRL_INVALID_SHAPE;
+  }
+  if (len == 0) return NSRL_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  const unsigned blocks = (unsigned)std::min<size_t>((len + 255) / 256, 148 * 8);
+  ProfScope prof("average_movement_i16", s, 0.0, 6.0 * (double)len);
+  average_movement_kernel<int16_t><<<blocks, 256, 0, s>>>(base, values, (long long)len, (long long)divisor, -32768,
+                                                          32767);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("movement average: %s", cudaGetErrorString(e));
     return NSRL_CUDA_ERROR;
   }
   return NSRL_OK;

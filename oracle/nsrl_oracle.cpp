@@ -1075,6 +1075,7 @@ struct TrainModel {
   const int16_t* positions;   // [S][d], or null for the position-free policy
   const TrainLayer* layer;
   LinearParams head;          // [256][d]
+  int32_t attention_kind;     // 0: base-2 softmax, 1: linear (MiniTransformerAttentionKind, lib.rs:1017-1023)
 };
 
 // Offsets of the i64 gradient arena: head, per layer (q k v o up gate down
@@ -1099,6 +1100,160 @@ struct Arena {
   // counts: [0] head, [1 + 9 l + i] layer l item i, [1 + 9 L] embeddings
 };
 
+// ------------------------------------------------------ linear attention --
+// crates/nsrl-core/src/attention.rs:1391-1466: phi(x) = x + 32769, the
+// per-head state S[key][value] = sum phi(k) v and key sums sum phi(k) in
+// checked i64, the projection round_div(sum phi(q) S, sum phi(q) K_s).
+static inline int64_t la_phi(int16_t v) { return (int64_t)v + 32769; }
+
+// attention.rs:1468-1477 (denominator > 0; saturating +- half, truncating division)
+static int64_t la_round_div(int64_t num, int64_t den) {
+  const int64_t half = den >> 1;
+  int64_t t;
+  if (num >= 0) {
+    if (__builtin_add_overflow(num, half, &t)) t = INT64_MAX;
+  } else {
+    if (__builtin_sub_overflow(num, half, &t)) t = INT64_MIN;
+  }
+  return t / den;
+}
+
+// attention.rs:1346-1396 (decay of the state; identity is a no-op)
+static bool la_decay(int64_t* S, int64_t* ks, size_t hd, FixedScale decay) {
+  if (decay.multiplier == 1 && decay.right_shift == 0) return true;
+  for (size_t i = 0; i < hd; ++i) {
+    int64_t w;
+    if (__builtin_mul_overflow(ks[i], (int64_t)decay.multiplier, &w)) return false;
+    ks[i] = rhu(w, decay.right_shift);
+  }
+  for (size_t i = 0; i < hd * hd; ++i) {
+    int64_t w;
+    if (__builtin_mul_overflow(S[i], (int64_t)decay.multiplier, &w)) return false;
+    S[i] = rhu(w, decay.right_shift);
+  }
+  return true;
+}
+
+// attention.rs:1398-1430
+static bool la_accumulate(const int16_t* k, const int16_t* v, int64_t* S, int64_t* ks, size_t hd, FixedScale decay) {
+  if (!la_decay(S, ks, hd, decay)) return false;
+  for (size_t i = 0; i < hd; ++i) {
+    const int64_t pk = la_phi(k[i]);
+    if (__builtin_add_overflow(ks[i], pk, &ks[i])) return false;
+    for (size_t j = 0; j < hd; ++j) {
+      const int64_t p = pk * (int64_t)v[j];  // |p| <= 2^31
+      if (__builtin_add_overflow(S[i * hd + j], p, &S[i * hd + j])) return false;
+    }
+  }
+  return true;
+}
+
+// attention.rs:1432-1466
+static bool la_project(const int16_t* q, const int64_t* S, const int64_t* ks, size_t hd, int16_t* out) {
+  int64_t den = 0;
+  for (size_t i = 0; i < hd; ++i) {
+    int64_t p;
+    if (__builtin_mul_overflow(la_phi(q[i]), ks[i], &p) || __builtin_add_overflow(den, p, &den)) return false;
+  }
+  if (den <= 0) return false;
+  for (size_t j = 0; j < hd; ++j) {
+    int64_t num = 0;
+    for (size_t i = 0; i < hd; ++i) {
+      int64_t p;
+      if (__builtin_mul_overflow(la_phi(q[i]), S[i * hd + j], &p) || __builtin_add_overflow(num, p, &num))
+        return false;
+    }
+    out[j] = saturate_i16(la_round_div(num, den));
+  }
+  return true;
+}
+
+// attention.rs:1290-1344 (linear_attention_ttt_delta_state_i16_q15_checked)
+static bool la_ttt_delta(const int16_t* k, const int16_t* v, int64_t* S, const int64_t* ks, size_t hd,
+                         uint8_t lr_shift, int16_t* pred, uint64_t* delta_l1) {
+  int64_t den = 0;
+  for (size_t i = 0; i < hd; ++i) {
+    int64_t p;
+    if (__builtin_mul_overflow(la_phi(k[i]), ks[i], &p) || __builtin_add_overflow(den, p, &den)) return false;
+  }
+  for (size_t j = 0; j < hd; ++j) {
+    if (den > 0) {
+      int64_t num = 0;
+      for (size_t i = 0; i < hd; ++i) {
+        int64_t p;
+        if (__builtin_mul_overflow(la_phi(k[i]), S[i * hd + j], &p) || __builtin_add_overflow(num, p, &num))
+          return false;
+      }
+      pred[j] = saturate_i16(la_round_div(num, den));
+    } else {
+      pred[j] = 0;
+    }
+  }
+  uint64_t l1 = 0;
+  for (size_t i = 0; i < hd; ++i) {
+    const int64_t pk = la_phi(k[i]);
+    for (size_t j = 0; j < hd; ++j) {
+      const int64_t err = (int64_t)v[j] - (int64_t)pred[j];
+      const int64_t upd = rhu(pk * err, lr_shift);
+      if (__builtin_add_overflow(S[i * hd + j], upd, &S[i * hd + j])) return false;
+      const uint64_t a = upd < 0 ? (uint64_t)(-(upd + 1)) + 1 : (uint64_t)upd;
+      if (__builtin_add_overflow(l1, a, &l1)) return false;
+    }
+  }
+  *delta_l1 += l1;
+  return true;
+}
+
+// attention.rs:911-1041: q, k, v of every token, then per token and head the
+// state update and (causal) the projection; non-causal accumulates every
+// token first.  x, out [S][d]; q, k, v, ctx scratch [S][d].
+static bool linear_attention_seq(const int16_t* x, size_t S, size_t d, size_t H, bool causal, const LinearParams* lp,
+                                 FixedScale decay, int16_t* out) {
+  if (S == 0 || d == 0 || H == 0 || d % H) return false;
+  const size_t hd = d / H, T = S * d;
+  std::vector<int16_t> q(T), k(T), v(T), ctx(T);
+  std::vector<int64_t> st(H * hd * hd, 0), ks(H * hd, 0);
+  for (size_t t = 0; t < S; ++t)
+    if (!linear_row(x + t * d, lp[0], &q[t * d]) || !linear_row(x + t * d, lp[1], &k[t * d]) ||
+        !linear_row(x + t * d, lp[2], &v[t * d]))
+      return false;
+  for (size_t t = 0; t < S; ++t)
+    for (size_t h = 0; h < H; ++h) {
+      const size_t rb = t * d + h * hd;
+      if (!la_accumulate(&k[rb], &v[rb], &st[h * hd * hd], &ks[h * hd], hd, decay)) return false;
+      if (causal && !la_project(&q[rb], &st[h * hd * hd], &ks[h * hd], hd, &ctx[rb])) return false;
+    }
+  if (!causal)
+    for (size_t t = 0; t < S; ++t)
+      for (size_t h = 0; h < H; ++h) {
+        const size_t rb = t * d + h * hd;
+        if (!la_project(&q[rb], &st[h * hd * hd], &ks[h * hd], hd, &ctx[rb])) return false;
+      }
+  for (size_t t = 0; t < S; ++t)
+    if (!linear_row(&ctx[t * d], lp[3], out + t * d)) return false;
+  return true;
+}
+
+// attention.rs:1085-1158 / :1186-1283: one row through q, k, v, the state
+// update (+ the TTT delta when ttt) and the projection, then o.
+static bool linear_attention_row_step(const int16_t* x, size_t d, size_t H, const LinearParams* lp, int64_t* st,
+                                      int64_t* ks, bool ttt, uint8_t lr_shift, int16_t* out, uint64_t* delta_l1) {
+  if (d == 0 || H == 0 || d % H) return false;
+  const size_t hd = d / H;
+  std::vector<int16_t> q(d), k(d), v(d), ctx(d), pred(d);
+  if (!linear_row(x, lp[0], q.data()) || !linear_row(x, lp[1], k.data()) || !linear_row(x, lp[2], v.data()))
+    return false;
+  const FixedScale id{1, 0, {0, 0, 0}};
+  for (size_t h = 0; h < H; ++h) {
+    const size_t o = h * hd;
+    if (!la_accumulate(&k[o], &v[o], &st[h * hd * hd], &ks[h * hd], hd, id)) return false;
+    if (ttt && !la_ttt_delta(&k[o], &v[o], &st[h * hd * hd], &ks[h * hd], hd, lr_shift, &pred[o], delta_l1))
+      return false;
+    if (!la_project(&q[o], &st[h * hd * hd], &ks[h * hd], hd, &ctx[o])) return false;
+  }
+  return linear_row(ctx.data(), lp[3], out);
+}
+
 struct BlockCache {
   std::vector<int16_t> in, an, q, k, v, ctx, P, ares, mn, up, gate, gated, out;
 };
@@ -1107,22 +1262,13 @@ static bool sat_add_rows(const int16_t* a, const int16_t* b, int16_t* out, size_
   return residual_add(a, b, out, n, sat);
 }
 
-// nsrl-train/src/lib.rs:15079-15300 (base-2 softmax attention kind)
-static bool block_forward_cache(const TrainModel& m, const TrainLayer& L, const int16_t* x, BlockCache& c,
-                                uint64_t* res_sat) {
-  const size_t S = m.S, d = m.d, F = m.F, H = m.H, T = S * d;
-  c.in.assign(x, x + T);
-  c.an.resize(T);
-  if (L.attn_gamma) {
-    for (size_t t = 0; t < S; ++t)
-      if (!rms_norm_row(x + t * d, L.attn_gamma, d, TRAIN_RMS_EPS, &c.an[t * d])) return false;
-  } else {
-    c.an = c.in;
-  }
+// The base-2 softmax attention of a block with its caches (q, k, v, context, P).
+static bool softmax_attention_part(const TrainModel& m, const TrainLayer& L, const int16_t* x, BlockCache& c,
+                                   std::vector<int16_t>& aout, std::vector<int16_t>& probs, uint64_t* res_sat) {
+  const size_t S = m.S, d = m.d, H = m.H, T = S * d;
+  std::vector<int32_t> logits(S);
   if (!attention_shapes_valid(S, d, H, L.lin)) return false;
   c.q.resize(T), c.k.resize(T), c.v.resize(T), c.ctx.resize(T);
-  std::vector<int16_t> aout(T), probs(S);
-  std::vector<int32_t> logits(S);
   for (size_t t = 0; t < S; ++t) {
     if (!linear_row(&c.an[t * d], L.lin[0], &c.q[t * d])) return false;
     if (!linear_row(&c.an[t * d], L.lin[1], &c.k[t * d])) return false;
@@ -1148,6 +1294,31 @@ static bool block_forward_cache(const TrainModel& m, const TrainLayer& L, const 
   if (!attention_probabilities(c.q.data(), c.k.data(), S, d, H, c.P.data())) return false;
   c.ares.resize(T);
   sat_add_rows(x, aout.data(), c.ares.data(), T, res_sat);
+  return true;
+}
+
+// nsrl-train/src/lib.rs:15079-15300 (base-2 softmax attention kind)
+static bool block_forward_cache(const TrainModel& m, const TrainLayer& L, const int16_t* x, BlockCache& c,
+                                uint64_t* res_sat) {
+  const size_t S = m.S, d = m.d, F = m.F, H = m.H, T = S * d;
+  c.in.assign(x, x + T);
+  c.an.resize(T);
+  if (L.attn_gamma) {
+    for (size_t t = 0; t < S; ++t)
+      if (!rms_norm_row(x + t * d, L.attn_gamma, d, TRAIN_RMS_EPS, &c.an[t * d])) return false;
+  } else {
+    c.an = c.in;
+  }
+  std::vector<int16_t> aout(T), probs(S);
+  if (m.attention_kind == 1) {
+    // the Linear kind of mini_transformer_forward_block_for_attention_kind (lib.rs:15079-15294)
+    const FixedScale id{1, 0, {0, 0, 0}};
+    if (!linear_attention_seq(c.an.data(), S, d, H, true, L.lin, id, aout.data())) return false;
+    c.ares.resize(T);
+    sat_add_rows(x, aout.data(), c.ares.data(), T, res_sat);
+  } else if (!softmax_attention_part(m, L, x, c, aout, probs, res_sat)) {
+    return false;
+  }
   c.mn.resize(T);
   if (L.mlp_gamma) {
     for (size_t t = 0; t < S; ++t)
@@ -1380,6 +1551,95 @@ static uint8_t select_byte(const int32_t* logits, const int16_t* probs, int stra
 }  // namespace orc
 
 extern "C" {
+
+// linear_attention_i16_q15_checked (attention.rs:879-1041) over `batch`
+// sequences [batch][S][d]; 0 = ok, 2 = rejected.
+int orc_linear_attention(const int16_t* x, size_t batch, size_t S, size_t d, size_t H, int causal,
+                         const LinearParams* lp, int16_t* out) {
+  const FixedScale id{1, 0, {0, 0, 0}};
+  for (size_t b = 0; b < batch; ++b)
+    if (!linear_attention_seq(x + b * S * d, S, d, H, causal != 0, lp, id, out + b * S * d)) return 2;
+  return 0;
+}
+
+// linear_attention_step_i16_q15_checked / linear_attention_ttt_step_i16_q15_checked
+// (attention.rs:1045-1283) for `batch` independent streams: rows x [batch][d],
+// states [batch][H][hd][hd] and key sums [batch][H][hd] updated in place,
+// delta_l1 [batch] (TTT only, added to).
+int orc_linear_attention_step(const int16_t* x, size_t batch, size_t d, size_t H, const LinearParams* lp,
+                              int64_t* state, int64_t* key_sums, int ttt, uint8_t lr_shift, int16_t* out,
+                              uint64_t* delta_l1) {
+  if (H == 0 || d % H) return 1;
+  const size_t hd = d / H;
+  for (size_t b = 0; b < batch; ++b) {
+    uint64_t dl = 0;
+    if (!linear_attention_row_step(x + b * d, d, H, lp, state + b * H * hd * hd, key_sums + b * H * hd, ttt != 0,
+                                   lr_shift, out + b * d, &dl))
+      return 2;
+    if (delta_l1) delta_l1[b] += dl;
+  }
+  return 0;
+}
+
+// mini_transformer_streaming_linear_nope_step / _ttt_nope_step (nsrl-train/src/
+// lib.rs:13035-13150): the token's embedding, the linear-attention step of
+// layer 0 with its state, the residual, the gated MLP (no RMS norm: the
+// streaming step applies none), the residual and the byte-head row.
+static bool streaming_step(const TrainModel& m, uint8_t token, int64_t* st, int64_t* ks, bool ttt, uint8_t lr_shift,
+                           int32_t* logits, int16_t* probs) {
+  const size_t d = m.d, F = m.F;
+  const TrainLayer& L = m.layer[0];
+  std::vector<int16_t> e(m.embeddings + (size_t)token * d, m.embeddings + (size_t)token * d + d);
+  std::vector<int16_t> a(d), r(d), up(F), gate(F), gated(F), mo(d), out(d);
+  uint64_t dl = 0, sat = 0;
+  if (!linear_attention_row_step(e.data(), d, m.H, L.lin, st, ks, ttt, lr_shift, a.data(), &dl)) return false;
+  sat_add_rows(e.data(), a.data(), r.data(), d, &sat);
+  if (!linear_row(r.data(), L.lin[4], up.data()) || !linear_row(r.data(), L.lin[5], gate.data())) return false;
+  for (size_t f = 0; f < F; ++f) gated[f] = gated_activation(up[f], gate[f]);
+  if (!linear_row(gated.data(), L.lin[6], mo.data())) return false;
+  sat_add_rows(r.data(), mo.data(), out.data(), d, &sat);
+  int16_t l16[VOCAB];
+  if (!linear_row(out.data(), m.head, l16)) return false;
+  for (size_t i = 0; i < VOCAB; ++i) logits[i] = l16[i];
+  return base2_softmax(logits, VOCAB, probs, nullptr);
+}
+
+// generate_mini_transformer_streaming_linear_nope_with_priors (lib.rs:12802-12878)
+// and its TTT variant (:12880-12980), no priors: the prompt runs through the
+// step token by token, then each chosen byte.
+int orc_generate_streaming(const TrainModel* m, uint8_t* ctx, size_t n, size_t steps, int strategy, size_t top_k,
+                           uint64_t seed, int ttt, uint8_t lr_shift, uint8_t* tokens, int32_t* logit_out,
+                           int16_t* prob_out) {
+  if (n == 0 || m->H == 0 || m->d % m->H) return 1;
+  const size_t hd = m->d / m->H;
+  std::vector<int64_t> st(m->H * hd * hd, 0), ks(m->H * hd, 0);
+  int32_t logits[VOCAB];
+  int16_t probs[VOCAB];
+  for (size_t i = 0; i < n; ++i)
+    if (!streaming_step(*m, ctx[i], st.data(), ks.data(), ttt != 0, lr_shift, logits, probs)) return 2;
+  for (size_t step = 0; step < steps; ++step) {
+    const uint8_t tok = select_byte(logits, probs, strategy, top_k, seed, step, ctx, n);
+    tokens[step] = tok;
+    if (logit_out) logit_out[step] = logits[tok];
+    if (prob_out) prob_out[step] = probs[tok];
+    ctx[n++] = tok;
+    if ((step + 1 < steps || ttt) && !streaming_step(*m, tok, st.data(), ks.data(), ttt != 0, lr_shift, logits, probs))
+      return 2;
+  }
+  return 0;
+}
+
+// linear_attention_ttt_delta_state_i16_q15_checked and the state projection
+// (attention.rs:1290-1344, :1432-1466) on one head, for known-answer tests.
+int orc_linear_attention_ttt_delta(const int16_t* k, const int16_t* v, int64_t* S, int64_t* ks, size_t hd,
+                                   uint8_t lr_shift, int16_t* pred, uint64_t* delta_l1) {
+  if (hd == 0 || lr_shift > MAX_RIGHT_SHIFT) return 1;
+  *delta_l1 = 0;
+  return la_ttt_delta(k, v, S, ks, hd, lr_shift, pred, delta_l1) ? 0 : 2;
+}
+int orc_linear_attention_project(const int16_t* q, const int64_t* S, const int64_t* ks, size_t hd, int16_t* out) {
+  return la_project(q, S, ks, hd, out) ? 0 : 2;
+}
 
 // The byte-head rows of B windows [B][S] (one per thread of `threads`).
 int orc_output_rows(const TrainModel* m, const uint8_t* windows, size_t B, int32_t* logits_q8, int16_t* probs_q15,

@@ -293,7 +293,7 @@ class _TrainLayer(C.Structure):
 class _TrainModel(C.Structure):
     _fields_ = [("d", C.c_size_t), ("H", C.c_size_t), ("F", C.c_size_t), ("layers", C.c_size_t),
                 ("S", C.c_size_t), ("embeddings", C.c_void_p), ("positions", C.c_void_p),
-                ("layer", C.c_void_p), ("head", LinearParams)]
+                ("layer", C.c_void_p), ("head", LinearParams), ("attention_kind", C.c_int32)]
 
 
 LAYER_LINEARS = ("q", "k", "v", "o", "up", "gate", "down")
@@ -305,7 +305,8 @@ class TrainModel:
     layers: list of dicts with Linear entries q k v o up gate down and optional
     int16 attn_gamma / mlp_gamma (RMS norm enabled when present)."""
 
-    def __init__(self, embeddings, positions, layers, head, d, H, F, S):
+    def __init__(self, embeddings, positions, layers, head, d, H, F, S, attention_kind="softmax"):
+        self.attention_kind = attention_kind  # "softmax" (base-2) or "linear"
         self.embeddings = _c(embeddings, np.int16)
         self.positions = None if positions is None else _c(positions, np.int16)
         self.layers = layers
@@ -326,7 +327,7 @@ class TrainModel:
         self._keep = arr
         return _TrainModel(self.d, self.H, self.F, len(self.layers), self.S, self.embeddings.ctypes.data,
                            None if self.positions is None else self.positions.ctypes.data,
-                           C.cast(arr, C.c_void_p), self.head.struct())
+                           C.cast(arr, C.c_void_p), self.head.struct(), 1 if self.attention_kind == "linear" else 0)
 
     def arena_layout(self):
         """Offsets of the i64 gradient arena, in the order the CUDA path uses too."""
@@ -676,5 +677,66 @@ def generate(model: TrainModel, prompt: bytes, steps: int, strategy="greedy", to
     if lib().orc_generate(C.byref(ms), _p(ctx), C.c_size_t(len(prompt)), C.c_size_t(steps),
                           C.c_int(0 if strategy == "greedy" else 1), C.c_size_t(top_k), C.c_uint64(seed), _p(tok),
                           _p(lg), _p(pr)):
+        return None
+    return tok, lg, pr
+
+
+def average_movement(base, values, divisor):
+    """average_i8_movement / average_i16_movement (nsrl-train/src/lib.rs:14552-14583):
+    sat(base + round_div(values - base, divisor)) with half-away-from-zero rounding."""
+    b = base.astype(np.int64)
+    m = values.astype(np.int64) - b
+    half = divisor // 2
+    avg = np.where(m >= 0, (m + half) // divisor, -((-m + half) // divisor))
+    info = np.iinfo(values.dtype)
+    return np.clip(b + avg, info.min, info.max).astype(values.dtype)
+
+
+# -------------------------------------------------------- linear attention --
+def linear_attention(x, B, S, d, H, q, k, v, o, causal=True):
+    """linear_attention_i16_q15_checked (crates/nsrl-core/src/attention.rs:879-1041)
+    per sequence of x [B*S, d]; None on a rejection."""
+    x = _c(x, np.int16)
+    out = np.zeros((B * S, d), np.int16)
+    if lib().orc_linear_attention(_p(x), C.c_size_t(B), C.c_size_t(S), C.c_size_t(d), C.c_size_t(H),
+                                  C.c_int(int(causal)), _lp_array([q, k, v, o]), _p(out)):
+        return None
+    return out
+
+
+def linear_attention_step(x, H, q, k, v, o, state, key_sums, ttt_shift=None, delta_l1=None):
+    """linear_attention_step_i16_q15_checked / _ttt_step (attention.rs:1045-1283)
+    for rows x [B, d] of B streams; state [B, H*hd*hd] and key_sums [B, H*hd]
+    int64 updated in place; delta_l1 [B] uint64 added to (TTT).  The output
+    rows, or None on a rejection."""
+    x = _c(x, np.int16)
+    B, d = x.shape
+    out = np.zeros((B, d), np.int16)
+    dl = _c(np.zeros(B, np.uint64) if delta_l1 is None else delta_l1, np.uint64)
+    if lib().orc_linear_attention_step(_p(x), C.c_size_t(B), C.c_size_t(d), C.c_size_t(H),
+                                       _lp_array([q, k, v, o]), _p(state), _p(key_sums),
+                                       C.c_int(0 if ttt_shift is None else 1),
+                                       C.c_uint8(0 if ttt_shift is None else ttt_shift), _p(out), _p(dl)):
+        return None
+    if delta_l1 is not None:
+        delta_l1[...] = dl
+    return out
+
+
+def generate_streaming(model: TrainModel, prompt: bytes, steps: int, strategy="greedy", top_k=0, seed=0,
+                       ttt_shift=None):
+    """generate_mini_transformer_streaming_linear_nope_with_priors (or its TTT
+    variant, nsrl-train/src/lib.rs:12802-12980): (tokens, picked logits,
+    picked probabilities), or None on a rejection."""
+    ctx = np.zeros(len(prompt) + steps, np.uint8)
+    ctx[:len(prompt)] = np.frombuffer(bytes(prompt), np.uint8)
+    tok = np.zeros(steps, np.uint8)
+    lg = np.zeros(steps, np.int32)
+    pr = np.zeros(steps, np.int16)
+    ms = model.struct()
+    if lib().orc_generate_streaming(C.byref(ms), _p(ctx), C.c_size_t(len(prompt)), C.c_size_t(steps),
+                                    C.c_int(0 if strategy == "greedy" else 1), C.c_size_t(top_k), C.c_uint64(seed),
+                                    C.c_int(0 if ttt_shift is None else 1),
+                                    C.c_uint8(0 if ttt_shift is None else ttt_shift), _p(tok), _p(lg), _p(pr)):
         return None
     return tok, lg, pr

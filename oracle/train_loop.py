@@ -92,7 +92,8 @@ def _copy_model(m):
                 e[g] = ly[g].copy()
         layers.append(e)
     return O.TrainModel(m.embeddings.copy(), None if m.positions is None else m.positions.copy(), layers,
-                        O.Linear(m.head.weights.copy(), m.head.scales.copy()), m.d, m.H, m.F, m.S)
+                        O.Linear(m.head.weights.copy(), m.head.scales.copy()), m.d, m.H, m.F, m.S,
+                        attention_kind=m.attention_kind)
 
 
 def run_integer_adam_training(tokens: bytes, model: O.TrainModel, epochs=1, stride=1, window_offset=0,

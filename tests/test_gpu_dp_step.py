@@ -136,3 +136,27 @@ def test_ordered_worker_merge(case):
     got = out.cpu().numpy()
     assert np.array_equal(got[:n], ref[0])
     assert np.array_equal(got[n:].view(np.uint64), counts.sum(axis=0))
+
+
+@pytest.mark.parametrize("dtype,divisor", [(np.int8, 1), (np.int8, 3), (np.int8, 8), (np.int16, 5), (np.int16, 2)])
+def test_average_batch_movement(dtype, divisor):
+    """average_mini_transformer_batch_movement's per-tensor rule (lib.rs:14552-14583)
+    against the oracle, saturation at both rails included."""
+    T = _train()
+    import ctypes as C
+    from nsrl_b200 import core
+    L = T._lib_dp()
+    info = np.iinfo(dtype)
+    rng = np.random.default_rng(divisor)
+    n = 70_001
+    base = rng.integers(info.min, info.max + 1, n).astype(dtype)
+    vals = rng.integers(info.min, info.max + 1, n).astype(dtype)
+    base[:4] = [info.max, info.min, info.max, 0]
+    vals[:4] = [info.min, info.max, info.max, info.min]
+    ref = O.average_movement(base, vals, divisor)
+    fn = L.nsrl_average_movement_i8 if dtype == np.int8 else L.nsrl_average_movement_i16
+    fn.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.c_uint64, C.c_void_p]
+    b, v = torch.from_numpy(base).cuda(), torch.from_numpy(vals).cuda()
+    assert fn(core._ptr(b), core._ptr(v), n, divisor, core._stream()) == core.NSRL_OK
+    assert np.array_equal(v.cpu().numpy(), ref)
+    assert fn(core._ptr(b), core._ptr(v), n, 0, core._stream()) == core.NSRL_INVALID_SHAPE
