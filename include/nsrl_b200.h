@@ -364,6 +364,8 @@ typedef struct nsrl_train_model {
   const int16_t* positions;  /* [seq_len][d], or NULL for the position-free policy */
   const nsrl_train_layer* layer; /* host array of `layers` blocks */
   nsrl_linear_params head;   /* [256][d] byte head */
+  int32_t attention_kind;    /* MiniTransformerAttentionKind (lib.rs:1017-1023): 0 base-2
+                                softmax, 1 linear (generation and output rows only) */
 } nsrl_train_model;
 
 /* Length (int64 elements) of the gradient arena: head [256][d]; per layer
@@ -505,6 +507,36 @@ nsrl_status nsrl_merge_worker_parts_i64(const long long* parts, size_t workers, 
  * and *aborted tell how many polls ran and whether the abort was called. */
 nsrl_status nsrl_comm_selftest_wait(int scenario, uint64_t timeout_ms, uint64_t* polls, int* aborted);
 
+/* ------------------------------------------------------ linear attention --
+ * Causal (or full) integer linear attention over `batch` sequences of
+ * seq_len tokens, x and out [batch*seq_len][d]: q, k, v linears, per head the
+ * state S = sum phi(k) v^T and key sums sum phi(k) (phi(x) = x + 32769,
+ * checked i64), the projection round_div(phi(q) S, phi(q) . key sums), then
+ * the o linear.  Replaces linear_attention_i16_q15_checked
+ * (crates/nsrl-core/src/attention.rs:879-1041), one sequence per reference
+ * call.  head_dim = d / heads <= 64 (any value, not only powers of four). */
+size_t nsrl_linear_attention_workspace_size(size_t batch, size_t seq_len, size_t d_model);
+nsrl_status nsrl_linear_attention(const int16_t* x, size_t batch, size_t seq_len, size_t d_model, size_t heads,
+                                  int causal, const nsrl_linear_params* q, const nsrl_linear_params* k,
+                                  const nsrl_linear_params* v, const nsrl_linear_params* o, int16_t* out,
+                                  void* workspace, size_t workspace_bytes, nsrl_device_status* status,
+                                  void* stream);
+
+/* One streaming step of `batch` independent streams: row b of x [batch][d]
+ * updates stream b's state (state [batch][heads][hd][hd], key_sums
+ * [batch][heads][hd], int64, zero at the start of a stream) and projects its
+ * query; out [batch][d].  ttt_shift < 0: linear_attention_step_i16_q15_checked
+ * (attention.rs:1045-1158); ttt_shift in 0..62: the test-time-training step
+ * (:1160-1344), which also adds each stream's sum |state update| to
+ * delta_l1[b] (device uint64, may be NULL). */
+size_t nsrl_linear_attention_step_workspace_size(size_t batch, size_t d_model);
+nsrl_status nsrl_linear_attention_step(const int16_t* x, size_t batch, size_t d_model, size_t heads,
+                                       const nsrl_linear_params* q, const nsrl_linear_params* k,
+                                       const nsrl_linear_params* v, const nsrl_linear_params* o, long long* state,
+                                       long long* key_sums, int ttt_shift, unsigned long long* delta_l1,
+                                       int16_t* out, void* workspace, size_t workspace_bytes,
+                                       nsrl_device_status* status, void* stream);
+
 /* ------------------------------------------------------------ generation --
  * Byte generation with the mini transformer (softmax attention), the
  * reference's generate_mini_transformer (nsrl-train/src/lib.rs:12702-12800)
@@ -540,6 +572,23 @@ nsrl_status nsrl_mini_transformer_generate(const nsrl_train_model* model, uint8_
                                            const nsrl_decode_config* decode, uint8_t* tokens, int32_t* pick_logits,
                                            int16_t* pick_probs, void* workspace, size_t workspace_bytes,
                                            nsrl_device_status* status, void* stream);
+
+/* Incremental generation with a one-layer linear-attention model without
+ * positions: generate_mini_transformer_streaming_linear_nope_with_priors and
+ * its TTT variant (nsrl-train/src/lib.rs:12802-12980), batched.  Every
+ * prompt byte and then every chosen byte runs one streaming step (the
+ * token's embedding, the linear-attention step with the stream's carried
+ * state, the residual, the gated MLP, the residual, the byte head); the
+ * reference's streaming step applies no RMS norm, and neither does this.
+ * All prompts have prompt_len bytes (contexts [batch][capacity], device).
+ * ttt_shift < 0: the plain step; else the TTT step with that shift. */
+size_t nsrl_generate_streaming_workspace_size(const nsrl_train_model* model, size_t batch);
+nsrl_status nsrl_mini_transformer_generate_streaming(const nsrl_train_model* model, uint8_t* contexts,
+                                                     size_t capacity, size_t prompt_len, size_t batch, size_t steps,
+                                                     const nsrl_decode_config* decode, int ttt_shift,
+                                                     uint8_t* tokens, int32_t* pick_logits, int16_t* pick_probs,
+                                                     void* workspace, size_t workspace_bytes,
+                                                     nsrl_device_status* status, void* stream);
 
 /* The transformer block over HOST buffers (pinned host memory for the
  * overlap): the batch runs in steps of at most `chunk` sequences; the copy

@@ -324,3 +324,59 @@ def attention_decode(q, k_cache, v_cache, lens, heads, head_dim):
     h = _run(lambda: lib().nsrl_attention_decode(_ptr(q), _ptr(kc), _ptr(vc), _ptr(ln), B, heads, head_dim, Lmax,
                                                  _ptr(ctx), _ptr(st.buf), _stream()), st)
     return None if h is None else ctx
+
+
+# ------------------------------------------------------- linear attention ---
+def _bind_linear_attention(L):
+    if not getattr(L, "_la_bound", False):
+        vp, sz, lp = C.c_void_p, C.c_size_t, C.POINTER(LinearParamsC)
+        L.nsrl_linear_attention_workspace_size.restype = sz
+        L.nsrl_linear_attention_workspace_size.argtypes = [sz, sz, sz]
+        L.nsrl_linear_attention.argtypes = [vp, sz, sz, sz, sz, C.c_int, lp, lp, lp, lp, vp, vp, sz, vp, vp]
+        L.nsrl_linear_attention_step_workspace_size.restype = sz
+        L.nsrl_linear_attention_step_workspace_size.argtypes = [sz, sz]
+        L.nsrl_linear_attention_step.argtypes = [vp, sz, sz, sz, lp, lp, lp, lp, vp, vp, C.c_int, vp, vp, vp, sz, vp,
+                                                 vp]
+        L._la_bound = True
+    return L
+
+
+def linear_attention_i16_q15_checked(x, batch, seq_len, d_model, heads, q, k, v, o, causal=True):
+    """attention.rs:879-1041 over `batch` sequences of x [batch*seq_len, d]; None on a rejection."""
+    L = _bind_linear_attention(lib())
+    x = _i16(x)
+    out = torch.empty((batch * seq_len, d_model), dtype=torch.int16, device=x.device)
+    ws = workspace(L.nsrl_linear_attention_workspace_size(batch, seq_len, d_model))
+    st = Status()
+    ps = [l.c() for l in (q, k, v, o)]
+    h = _run(lambda: L.nsrl_linear_attention(_ptr(x), batch, seq_len, d_model, heads, int(causal),
+                                             *[C.byref(p) for p in ps], _ptr(out), _ptr(ws), ws.numel(),
+                                             _ptr(st.buf), _stream()), st)
+    return None if h is None else out
+
+
+class LinearAttentionStreams:
+    """Carried states of `batch` linear-attention streams ([batch][heads][hd][hd]
+    and [batch][heads][hd] int64, zero at the start)."""
+
+    def __init__(self, batch, d_model, heads, device=None):
+        dev = device if device is not None else _dev()
+        hd = d_model // heads
+        self.batch, self.d_model, self.heads = batch, d_model, heads
+        self.state = torch.zeros((batch, heads * hd * hd), dtype=torch.int64, device=dev)
+        self.key_sums = torch.zeros((batch, heads * hd), dtype=torch.int64, device=dev)
+        self.delta_l1 = torch.zeros(batch, dtype=torch.int64, device=dev)
+
+    def step(self, x, q, k, v, o, ttt_shift=None):
+        """attention.rs:1045-1283 on rows x [batch, d]; the output rows or None."""
+        L = _bind_linear_attention(lib())
+        x = _i16(x)
+        out = torch.empty_like(x)
+        ws = workspace(L.nsrl_linear_attention_step_workspace_size(self.batch, self.d_model))
+        st = Status()
+        ps = [l.c() for l in (q, k, v, o)]
+        h = _run(lambda: L.nsrl_linear_attention_step(
+            _ptr(x), self.batch, self.d_model, self.heads, *[C.byref(p) for p in ps], _ptr(self.state),
+            _ptr(self.key_sums), -1 if ttt_shift is None else int(ttt_shift), _ptr(self.delta_l1), _ptr(out),
+            _ptr(ws), ws.numel(), _ptr(st.buf), _stream()), st)
+        return None if h is None else out

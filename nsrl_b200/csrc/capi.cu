@@ -284,6 +284,98 @@ nsrl_status attention_block(const int16_t* x, size_t B, size_t S, size_t d, size
                         &st->attention_saturations, st, stream);
 }
 
+// Linear attention core: input planes -> q|k|v planes -> linear attention ->
+// context planes -> O linear (epilogue out_epi).
+size_t linear_attention_ws(size_t T, size_t d, Carver* c = nullptr) {
+  Carver local(nullptr);
+  Carver& k = c ? *c : local;
+  const size_t start = k.off;
+  k.planes(T, d, true);
+  k.planes(T, 3 * d, false);
+  k.planes(T, d, true);
+  return k.off - start;
+}
+
+nsrl_status linear_attention_core(const Planes& xin, size_t B, size_t S, size_t d, size_t H, bool causal,
+                                  const nsrl_linear_params* q, const nsrl_linear_params* k,
+                                  const nsrl_linear_params* v, const nsrl_linear_params* o, Planes qkv, Planes ctx,
+                                  Epi out_epi, const int16_t* skip, int16_t* out, unsigned long long* sat,
+                                  nsrl_device_status* st, cudaStream_t stream, long long* state = nullptr,
+                                  long long* key_sums = nullptr, int ttt_shift = -1,
+                                  unsigned long long* delta_l1 = nullptr) {
+  const size_t T = B * S;
+  GemmArgs g{};
+  g.a_hi = xin.hi;
+  g.a_lo = xin.lo;
+  g.a_l1 = xin.l1;
+  g.lda = xin.ld;
+  g.M = T;
+  g.K = d;
+  g.nseg = 3;
+  g.seg[0] = seg_of(q);
+  g.seg[1] = seg_of(k);
+  g.seg[2] = seg_of(v);
+  g.epi = Epi::PLANES;
+  g.yp = qkv;
+  g.st = st;
+  NSRL_TRY(launch_gemm(g, stream), "qkv projection");
+  if (!needs_l1(d, o)) ctx.l1 = nullptr;
+  if (ctx.l1) NSRL_TRY(cudaMemsetAsync(ctx.l1, 0, T * sizeof(unsigned long long), stream), "memset");
+  if (state)
+    NSRL_TRY(launch_linear_attention_step(qkv, B, d, H, state, key_sums, ttt_shift, delta_l1, ctx, st, stream),
+             "linear attention step");
+  else
+    NSRL_TRY(launch_linear_attention(qkv, B, S, d, H, causal, ctx, st, stream), "linear attention");
+  GemmArgs og{};
+  og.a_hi = ctx.hi;
+  og.a_lo = ctx.lo;
+  og.a_l1 = ctx.l1;
+  og.lda = ctx.ld;
+  og.M = T;
+  og.K = d;
+  og.nseg = 1;
+  og.seg[0] = seg_of(o);
+  og.epi = out_epi;
+  og.y = out;
+  og.ldy = d;
+  og.skip = skip;
+  og.ldskip = d;
+  og.sat_counter = sat;
+  og.st = st;
+  NSRL_TRY(launch_gemm(og, stream), "output projection");
+  return NSRL_OK;
+}
+
+// y = x + linear_attention(rms(x) or x): the Linear kind of the mini
+// transformer's block (nsrl-train/src/lib.rs:15079-15294).
+nsrl_status linear_attention_block(const int16_t* x, size_t B, size_t S, size_t d, size_t H, const int16_t* gamma,
+                                   uint64_t eps, const nsrl_linear_params* q, const nsrl_linear_params* k,
+                                   const nsrl_linear_params* v, const nsrl_linear_params* o, int16_t* y, Carver& c,
+                                   nsrl_device_status* st, cudaStream_t stream) {
+  const size_t T = B * S;
+  Planes xn = c.planes(T, d, true);
+  Planes qkv = c.planes(T, 3 * d, false);
+  Planes ctx = c.planes(T, d, true);
+  if (!needs_l1(d, q, k, v)) xn.l1 = nullptr;
+  if (gamma)
+    NSRL_TRY(launch_rms_norm(x, T, d, gamma, eps, nullptr, xn, st, stream), "rms norm");
+  else
+    NSRL_TRY(launch_split_planes(x, T, d, d, xn, stream), "split");
+  return linear_attention_core(xn, B, S, d, H, true, q, k, v, o, qkv, ctx, Epi::RESID, x, y,
+                               &st->attention_saturations, st, stream);
+}
+
+nsrl_status validate_linear_attention(size_t d, size_t H, const nsrl_linear_params* q, const nsrl_linear_params* k,
+                                      const nsrl_linear_params* v, const nsrl_linear_params* o) {
+  // attention.rs:1636-1684 (any head_dim; this path takes head_dim <= 64)
+  if (d == 0 || H == 0 || d % H != 0) return shape_fail("d_model must be a nonzero multiple of heads");
+  if (!linear_attention_supported(d, H)) return shape_fail("linear attention: head_dim <= 64");
+  if (!linear_ok(q, d, d) || !linear_ok(k, d, d) || !linear_ok(v, d, d) || !linear_ok(o, d, d))
+    return shape_fail("q/k/v/o must be d_model x d_model linears");
+  if (d > (size_t)INT32_MAX / 3) return shape_fail("dimension too large");
+  return NSRL_OK;
+}
+
 }  // namespace
 }  // namespace nsrl
 
@@ -764,15 +856,22 @@ size_t gen_ws(const nsrl_train_model* m, size_t B, Carver* c) {
   k.take<int32_t>(B * 256);           // logits
   k.take<int16_t>(B * 256);           // probabilities
   k.take<int32_t>(B);                 // context lengths
-  k.off += std::max(attention_ws(B, m->seq_len, m->d_model, m->heads), mlp_ws(T, m->d_model, m->hidden_dim));
+  const size_t aws = m->attention_kind == 1 ? linear_attention_ws(T, m->d_model)
+                                             : attention_ws(B, m->seq_len, m->d_model, m->heads);
+  k.off += std::max(aws, mlp_ws(T, m->d_model, m->hidden_dim));
   return k.off - start;
 }
 
 nsrl_status validate_gen_model(const nsrl_train_model* m) {
   if (!m || !m->layer || m->layers == 0 || !m->embeddings) return shape_fail("model with embeddings and layers");
   const size_t d = m->d_model, S = m->seq_len;
-  nsrl_status r = validate_attention(S, d, m->heads, &m->layer[0].lin[0], &m->layer[0].lin[1], &m->layer[0].lin[2],
-                                     &m->layer[0].lin[3]);
+  if (m->attention_kind != 0 && m->attention_kind != 1) return shape_fail("attention_kind: 0 softmax, 1 linear");
+  const bool lin = m->attention_kind == 1;
+  auto vattn = [&](const nsrl_train_layer& L) {
+    return lin ? validate_linear_attention(d, m->heads, &L.lin[0], &L.lin[1], &L.lin[2], &L.lin[3])
+               : validate_attention(S, d, m->heads, &L.lin[0], &L.lin[1], &L.lin[2], &L.lin[3]);
+  };
+  nsrl_status r = vattn(m->layer[0]);
   if (r != NSRL_OK) return r;
   if (d > 4096) return shape_fail("d_model <= 4096 for the byte head");
   if (!linear_ok(&m->head, d, 256)) return shape_fail("head must be [256][d_model]");
@@ -781,7 +880,7 @@ nsrl_status validate_gen_model(const nsrl_train_model* m) {
     const nsrl_train_layer& L = m->layer[l];
     if ((L.attn_gamma != nullptr) != rms || (L.mlp_gamma != nullptr) != rms)
       return shape_fail("RMS gammas: both or neither, the same in every layer");
-    if ((r = validate_attention(S, d, m->heads, &L.lin[0], &L.lin[1], &L.lin[2], &L.lin[3])) != NSRL_OK) return r;
+    if ((r = vattn(L)) != NSRL_OK) return r;
     if ((r = validate_mlp(S, d, m->hidden_dim, &L.lin[4], &L.lin[5], &L.lin[6])) != NSRL_OK) return r;
   }
   return NSRL_OK;
@@ -796,8 +895,11 @@ nsrl_status gen_forward(const nsrl_train_model* m, const uint8_t* win, size_t B,
   for (size_t l = 0; l < m->layers; ++l) {
     const nsrl_train_layer& L = m->layer[l];
     c.off = mark;
-    nsrl_status r = attention_block(x, B, S, d, m->heads, true, L.attn_gamma, 1, &L.lin[0], &L.lin[1], &L.lin[2],
-                                    &L.lin[3], h, c, st, s);
+    nsrl_status r = m->attention_kind == 1
+                        ? linear_attention_block(x, B, S, d, m->heads, L.attn_gamma, 1, &L.lin[0], &L.lin[1],
+                                                 &L.lin[2], &L.lin[3], h, c, st, s)
+                        : attention_block(x, B, S, d, m->heads, true, L.attn_gamma, 1, &L.lin[0], &L.lin[1],
+                                          &L.lin[2], &L.lin[3], h, c, st, s);
     if (r != NSRL_OK) return r;
     c.off = mark;
     r = mlp_block(h, T, d, m->hidden_dim, L.mlp_gamma, 1, &L.lin[4], &L.lin[5], &L.lin[6], x, c, st, s);
@@ -868,6 +970,164 @@ nsrl_status nsrl_mini_transformer_generate(const nsrl_train_model* m, uint8_t* c
     NSRL_TRY(launch_select(logits, probs, batch, decode->strategy, (int)decode->top_k, decode->sample_seed, (int)step,
                            contexts, capacity, lens, (int)steps, tokens, pick_logits, pick_probs, s),
              "select");
+  }
+  return NSRL_OK;
+}
+
+// ------------------------------------------------------- linear attention --
+size_t nsrl_linear_attention_workspace_size(size_t batch, size_t seq_len, size_t d_model) {
+  return linear_attention_ws(batch * seq_len, d_model);
+}
+
+nsrl_status nsrl_linear_attention(const int16_t* x, size_t batch, size_t seq_len, size_t d_model, size_t heads,
+                                  int causal, const nsrl_linear_params* q, const nsrl_linear_params* k,
+                                  const nsrl_linear_params* v, const nsrl_linear_params* o, int16_t* out,
+                                  void* workspace, size_t workspace_bytes, nsrl_device_status* status,
+                                  void* stream) {
+  nsrl_status r = validate_linear_attention(d_model, heads, q, k, v, o);
+  if (r != NSRL_OK) return r;
+  if (seq_len == 0) return shape_fail("seq_len must be nonzero");
+  if (!x || !out || !status) return shape_fail("NULL argument");
+  if (batch == 0) return NSRL_OK;
+  if (!workspace || workspace_bytes < linear_attention_ws(batch * seq_len, d_model))
+    return shape_fail("workspace too small");
+  cudaStream_t s = (cudaStream_t)stream;
+  const size_t T = batch * seq_len;
+  Carver c(workspace);
+  Planes xp = c.planes(T, d_model, true);
+  Planes qkv = c.planes(T, 3 * d_model, false);
+  Planes ctx = c.planes(T, d_model, true);
+  if (!needs_l1(d_model, q, k, v)) xp.l1 = nullptr;
+  NSRL_TRY(launch_split_planes(x, T, d_model, d_model, xp, s), "split");
+  return linear_attention_core(xp, batch, seq_len, d_model, heads, causal != 0, q, k, v, o, qkv, ctx, Epi::I16,
+                               nullptr, out, nullptr, status, s);
+}
+
+size_t nsrl_linear_attention_step_workspace_size(size_t batch, size_t d_model) {
+  return linear_attention_ws(batch, d_model);
+}
+
+nsrl_status nsrl_linear_attention_step(const int16_t* x, size_t batch, size_t d_model, size_t heads,
+                                       const nsrl_linear_params* q, const nsrl_linear_params* k,
+                                       const nsrl_linear_params* v, const nsrl_linear_params* o, long long* state,
+                                       long long* key_sums, int ttt_shift, unsigned long long* delta_l1,
+                                       int16_t* out, void* workspace, size_t workspace_bytes,
+                                       nsrl_device_status* status, void* stream) {
+  nsrl_status r = validate_linear_attention(d_model, heads, q, k, v, o);
+  if (r != NSRL_OK) return r;
+  if (!x || !out || !status || !state || !key_sums) return shape_fail("NULL argument");
+  if (ttt_shift > 62) return shape_fail("TTT learning-rate shift <= 62");
+  if (ttt_shift >= 0 && !delta_l1) return shape_fail("the TTT step needs delta_l1");
+  if (batch == 0) return NSRL_OK;
+  if (!workspace || workspace_bytes < linear_attention_ws(batch, d_model)) return shape_fail("workspace too small");
+  cudaStream_t s = (cudaStream_t)stream;
+  Carver c(workspace);
+  Planes xp = c.planes(batch, d_model, true);
+  Planes qkv = c.planes(batch, 3 * d_model, false);
+  Planes ctx = c.planes(batch, d_model, true);
+  if (!needs_l1(d_model, q, k, v)) xp.l1 = nullptr;
+  NSRL_TRY(launch_split_planes(x, batch, d_model, d_model, xp, s), "split");
+  return linear_attention_core(xp, batch, 1, d_model, heads, true, q, k, v, o, qkv, ctx, Epi::I16, nullptr, out,
+                               nullptr, status, s, state, key_sums, ttt_shift < 0 ? -1 : ttt_shift, delta_l1);
+}
+
+// ------------------------------------------------- streaming generation --
+namespace {
+size_t stream_gen_ws(const nsrl_train_model* m, size_t B, Carver* c) {
+  Carver local(nullptr);
+  Carver& k = c ? *c : local;
+  const size_t start = k.off;
+  const size_t d = m->d_model, H = m->heads, hd = d / H;
+  k.take<int16_t>(B * d);              // x
+  k.take<int16_t>(B * d);              // h
+  k.take<int16_t>(B * d);              // y
+  k.take<int32_t>(B * 256);            // logits
+  k.take<int16_t>(B * 256);            // probabilities
+  k.take<int32_t>(B);                  // context lengths
+  k.take<long long>(B * H * hd * hd);  // states
+  k.take<long long>(B * H * hd);       // key sums
+  k.take<unsigned long long>(B);       // TTT delta L1
+  k.off += std::max(linear_attention_ws(B, d), mlp_ws(B, d, m->hidden_dim));
+  return k.off - start;
+}
+
+nsrl_status validate_stream_model(const nsrl_train_model* m) {
+  if (!m || !m->layer || m->layers != 1 || !m->embeddings || m->attention_kind != 1)
+    return shape_fail("streaming generation: a one-layer linear-attention model");
+  const nsrl_train_layer& L = m->layer[0];
+  nsrl_status r = validate_linear_attention(m->d_model, m->heads, &L.lin[0], &L.lin[1], &L.lin[2], &L.lin[3]);
+  if (r != NSRL_OK) return r;
+  if ((r = validate_mlp(1, m->d_model, m->hidden_dim, &L.lin[4], &L.lin[5], &L.lin[6])) != NSRL_OK) return r;
+  if (m->d_model > 4096 || !linear_ok(&m->head, m->d_model, 256)) return shape_fail("head must be [256][d_model]");
+  return NSRL_OK;
+}
+}  // namespace
+
+size_t nsrl_generate_streaming_workspace_size(const nsrl_train_model* model, size_t batch) {
+  if (validate_stream_model(model) != NSRL_OK || batch == 0) return 0;
+  return stream_gen_ws(model, batch, nullptr);
+}
+
+nsrl_status nsrl_mini_transformer_generate_streaming(const nsrl_train_model* m, uint8_t* contexts, size_t capacity,
+                                                     size_t prompt_len, size_t batch, size_t steps,
+                                                     const nsrl_decode_config* decode, int ttt_shift,
+                                                     uint8_t* tokens, int32_t* pick_logits, int16_t* pick_probs,
+                                                     void* workspace, size_t workspace_bytes,
+                                                     nsrl_device_status* status, void* stream) {
+  nsrl_status r = validate_stream_model(m);
+  if (r != NSRL_OK) return r;
+  if (!contexts || !decode || !tokens || !status) return shape_fail("NULL argument");
+  if (decode->strategy != 0 && decode->strategy != 1) return shape_fail("decode strategy: 0 greedy, 1 sample");
+  if (ttt_shift > 62) return shape_fail("TTT learning-rate shift <= 62");
+  if (batch == 0 || steps == 0) return NSRL_OK;
+  if (prompt_len == 0 || prompt_len + steps > capacity || capacity > (size_t)INT32_MAX)
+    return shape_fail("prompts need 1..capacity-steps bytes");
+  if (!workspace || workspace_bytes < stream_gen_ws(m, batch, nullptr)) return shape_fail("workspace too small");
+  cudaStream_t s = (cudaStream_t)stream;
+  const size_t d = m->d_model, H = m->heads, hd = d / H, F = m->hidden_dim;
+  const nsrl_train_layer& L = m->layer[0];
+  Carver c(workspace);
+  int16_t* x = c.take<int16_t>(batch * d);
+  int16_t* h = c.take<int16_t>(batch * d);
+  int16_t* y = c.take<int16_t>(batch * d);
+  int32_t* logits = c.take<int32_t>(batch * 256);
+  int16_t* probs = c.take<int16_t>(batch * 256);
+  int32_t* lens = c.take<int32_t>(batch);
+  long long* state = c.take<long long>(batch * H * hd * hd);
+  long long* ks = c.take<long long>(batch * H * hd);
+  unsigned long long* dl1 = c.take<unsigned long long>(batch);
+  const size_t mark = c.off;
+  NSRL_TRY(cudaMemsetAsync(state, 0, batch * H * hd * hd * sizeof(long long), s), "state");
+  NSRL_TRY(cudaMemsetAsync(ks, 0, batch * H * hd * sizeof(long long), s), "state");
+  NSRL_TRY(cudaMemsetAsync(dl1, 0, batch * sizeof(unsigned long long), s), "state");
+  std::vector<int32_t> hl(batch, (int32_t)prompt_len);
+  NSRL_TRY(cudaMemcpyAsync(lens, hl.data(), batch * sizeof(int32_t), cudaMemcpyHostToDevice, s), "lengths");
+  // mini_transformer_streaming_linear_nope_step (lib.rs:13035-13150): one token of every stream
+  auto step = [&](int fixed_pos) -> nsrl_status {
+    c.off = mark;
+    NSRL_TRY(launch_embed_token(contexts, capacity, lens, fixed_pos, m->embeddings, d, batch, x, s), "embedding");
+    Planes xp = c.planes(batch, d, true);
+    Planes qkv = c.planes(batch, 3 * d, false);
+    Planes ctx = c.planes(batch, d, true);
+    if (!needs_l1(d, &L.lin[0], &L.lin[1], &L.lin[2])) xp.l1 = nullptr;
+    NSRL_TRY(launch_split_planes(x, batch, d, d, xp, s), "split");
+    nsrl_status rr = linear_attention_core(xp, batch, 1, d, H, true, &L.lin[0], &L.lin[1], &L.lin[2], &L.lin[3], qkv,
+                                           ctx, Epi::RESID, x, h, &status->attention_saturations, status, s, state,
+                                           ks, ttt_shift < 0 ? -1 : ttt_shift, dl1);
+    if (rr != NSRL_OK) return rr;
+    c.off = mark;
+    rr = mlp_block(h, batch, d, F, nullptr, 1, &L.lin[4], &L.lin[5], &L.lin[6], y, c, status, s);
+    if (rr != NSRL_OK) return rr;
+    NSRL_TRY(launch_head_rows(y, d, 0, batch, d, &m->head, logits, probs, status, s), "byte head");
+    return NSRL_OK;
+  };
+  for (size_t i = 0; i < prompt_len; ++i)
+    if ((r = step((int)i)) != NSRL_OK) return r;
+  for (size_t t = 0; t < steps; ++t) {
+    NSRL_TRY(launch_select(logits, probs, batch, decode->strategy, (int)decode->top_k, decode->sample_seed, (int)t,
+                           contexts, capacity, lens, (int)steps, tokens, pick_logits, pick_probs, s),
+             "select");
+    if (t + 1 < steps && (r = step(-1)) != NSRL_OK) return r;
   }
   return NSRL_OK;
 }

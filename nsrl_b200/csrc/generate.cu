@@ -97,6 +97,18 @@ __global__ void __launch_bounds__(VOCAB) head_row_kernel(const int16_t* __restri
   probs_out[b * VOCAB + c] = (int16_t)p;
 }
 
+// x[b] = emb[ctx[b][pos]] with pos = fixed_pos >= 0 ? fixed_pos : lens[b] - 1
+// (the token embedding without positions, lib.rs:13275-13289).
+__global__ void embed_token_kernel(const uint8_t* __restrict__ ctx, long long cap, const int32_t* __restrict__ lens,
+                                   int fixed_pos, const int16_t* __restrict__ emb, int d, int B, int16_t* __restrict__ x) {
+  const long long n = (long long)B * d;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const int b = (int)(i / d), c = (int)(i % d);
+    const int pos = fixed_pos >= 0 ? fixed_pos : lens[b] - 1;
+    x[i] = emb[(int)ctx[(long long)b * cap + pos] * d + c];
+  }
+}
+
 __device__ __forceinline__ uint64_t fnv_byte(uint64_t h, uint8_t v) { return (h ^ v) * 0x100000001b3ull; }
 __device__ __forceinline__ uint64_t fnv_u64(uint64_t h, uint64_t v) {
 #pragma unroll
@@ -192,6 +204,15 @@ cudaError_t launch_embed(const uint8_t* win, size_t rows, size_t S, size_t d, co
   const unsigned blocks = (unsigned)std::min<size_t>((n + 255) / 256, 148 * 16);
   ProfScope prof("embed", s, 0.0, 6.0 * (double)n);
   embed_kernel<<<blocks, 256, 0, s>>>(win, (int)S, (int)d, emb, pos, (long long)rows, x);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_embed_token(const uint8_t* ctx, size_t cap, const int32_t* lens, int fixed_pos,
+                               const int16_t* emb, size_t d, size_t B, int16_t* x, cudaStream_t s) {
+  const size_t n = B * d;
+  const unsigned blocks = (unsigned)std::min<size_t>((n + 255) / 256, 148 * 8);
+  ProfScope prof("embed_token", s, 0.0, 4.0 * (double)n);
+  embed_token_kernel<<<blocks, 256, 0, s>>>(ctx, (long long)cap, lens, fixed_pos, emb, (int)d, (int)B, x);
   return cudaGetLastError();
 }
 

@@ -196,12 +196,27 @@ cudaError_t launch_gen_windows(const uint8_t* ctx, size_t cap, const int32_t* le
                                cudaStream_t s);
 cudaError_t launch_embed(const uint8_t* win, size_t rows, size_t S, size_t d, const int16_t* emb,
                          const int16_t* pos, int16_t* x, cudaStream_t s);
+cudaError_t launch_embed_token(const uint8_t* ctx, size_t cap, const int32_t* lens, int fixed_pos,
+                               const int16_t* emb, size_t d, size_t B, int16_t* x, cudaStream_t s);
 cudaError_t launch_head_rows(const int16_t* x, size_t row_stride, size_t row0, size_t B, size_t d,
                              const nsrl_linear_params* head, int32_t* logits, int16_t* probs, nsrl_device_status* st,
                              cudaStream_t s);
 cudaError_t launch_select(const int32_t* logits, const int16_t* probs, size_t B, int strategy, int top_k,
                           uint64_t seed, int step, uint8_t* ctx, size_t cap, int32_t* lens, int steps,
                           uint8_t* tokens, int32_t* pick_logit, int16_t* pick_prob, cudaStream_t s);
+
+// Linear attention (linear_attention.cu) on the byte planes of the q|k|v
+// projection [rows][3d] -> context planes [rows][d] (+ row L1, zeroed by the
+// caller).  Head dims up to 64.
+bool linear_attention_supported(size_t d, size_t H);
+cudaError_t launch_linear_attention(const Planes& qkv, size_t B, size_t S, size_t d, size_t H, bool causal,
+                                    Planes ctx, nsrl_device_status* st, cudaStream_t stream);
+// One step of B streams (one q|k|v row each) with carried states [B][H][hd][hd]
+// and key sums [B][H][hd] (int64); ttt_shift >= 0 applies the TTT delta with
+// that shift and adds each stream's |update| to delta_l1[b].
+cudaError_t launch_linear_attention_step(const Planes& qkv, size_t B, size_t d, size_t H, long long* state,
+                                         long long* key_sums, int ttt_shift, unsigned long long* delta_l1,
+                                         Planes ctx, nsrl_device_status* st, cudaStream_t stream);
 
 void set_error(const char* fmt, ...);
 bool tma_supported();

@@ -438,6 +438,7 @@ size_t arena_len(const nsrl_train_model* m) {
 
 nsrl_status validate_model(const nsrl_train_model* m, bool* rms) {
   if (!m || !m->layer || m->layers == 0) return fail_shape("model with at least one layer");
+  if (m->attention_kind != 0) return fail_shape("the training step takes base-2 softmax attention (attention_kind 0)");
   const size_t d = m->d_model, H = m->heads, F = m->hidden_dim, S = m->seq_len;
   if (d == 0 || H == 0 || F == 0 || S == 0 || d % H != 0) return fail_shape("d_model, heads, hidden_dim, seq_len");
   const size_t hd = d / H;

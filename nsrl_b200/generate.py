@@ -105,3 +105,53 @@ class Generator:
         if not T._run_status(r, self.status):
             return None
         return self.tokens.cpu(), self.pick_logits.cpu(), self.pick_probs.cpu()
+
+
+class StreamingGenerator:
+    """Incremental generation with a one-layer linear-attention model without
+    positions (generate_mini_transformer_streaming_linear_nope_with_priors and
+    its TTT variant, lib.rs:12802-12980): each stream carries its linear
+    attention state; prompts of one length per batch."""
+
+    def __init__(self, model: T.TrainModel, batch: int, prompt_len: int, steps: int):
+        L = _lib()
+        if not getattr(L, "_sgen_bound", False):
+            vp, sz = C.c_void_p, C.c_size_t
+            L.nsrl_generate_streaming_workspace_size.restype = sz
+            L.nsrl_generate_streaming_workspace_size.argtypes = [vp, sz]
+            L.nsrl_mini_transformer_generate_streaming.argtypes = [vp, vp, sz, sz, sz, sz, C.POINTER(DecodeConfigC),
+                                                                   C.c_int, vp, vp, vp, vp, sz, vp, vp]
+            L._sgen_bound = True
+        self.model, self.batch, self.prompt_len, self.steps = model, batch, prompt_len, steps
+        self.capacity = prompt_len + steps
+        m = model.c()
+        nbytes = L.nsrl_generate_streaming_workspace_size(C.byref(m), batch)
+        if nbytes == 0:
+            raise ValueError(L.nsrl_last_error().decode() or "invalid streaming-generation shape")
+        dev = core._dev()
+        self.ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        self.contexts = torch.empty((batch, self.capacity), dtype=torch.uint8, device=dev)
+        self.tokens = torch.empty((batch, steps), dtype=torch.uint8, device=dev)
+        self.pick_logits = torch.empty((batch, steps), dtype=torch.int32, device=dev)
+        self.pick_probs = torch.empty((batch, steps), dtype=torch.int16, device=dev)
+        self.status = core.Status()
+
+    def __call__(self, prompts: Sequence[bytes], strategy="greedy", top_k=0, seed=0, ttt_shift=None):
+        if len(prompts) != self.batch or any(len(p) != self.prompt_len for p in prompts):
+            raise ValueError("one prompt of prompt_len bytes per stream")
+        L = _lib()
+        host = torch.zeros((self.batch, self.capacity), dtype=torch.uint8)
+        for b, p in enumerate(prompts):
+            host[b, :len(p)] = torch.frombuffer(bytearray(p), dtype=torch.uint8)
+        self.contexts.copy_(host)
+        self.status.reset()
+        cfg = DecodeConfigC(STRATEGIES[strategy], int(top_k), int(seed))
+        m = self.model.c()
+        r = L.nsrl_mini_transformer_generate_streaming(
+            C.byref(m), core._ptr(self.contexts), self.capacity, self.prompt_len, self.batch, self.steps,
+            C.byref(cfg), -1 if ttt_shift is None else int(ttt_shift), core._ptr(self.tokens),
+            core._ptr(self.pick_logits), core._ptr(self.pick_probs), core._ptr(self.ws), self.ws.numel(),
+            core._ptr(self.status.buf), core._stream())
+        if not T._run_status(r, self.status):
+            return None
+        return self.tokens.cpu(), self.pick_logits.cpu(), self.pick_probs.cpu()

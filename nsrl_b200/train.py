@@ -159,7 +159,7 @@ class _TrainLayerC(C.Structure):
 class _TrainModelC(C.Structure):
     _fields_ = [("d_model", C.c_size_t), ("heads", C.c_size_t), ("hidden_dim", C.c_size_t), ("layers", C.c_size_t),
                 ("seq_len", C.c_size_t), ("embeddings", C.c_void_p), ("positions", C.c_void_p),
-                ("layer", C.c_void_p), ("head", core.LinearParamsC)]
+                ("layer", C.c_void_p), ("head", core.LinearParamsC), ("attention_kind", C.c_int32)]
 
 
 LAYER_LINEARS = ("q", "k", "v", "o", "up", "gate", "down")
@@ -283,8 +283,10 @@ class TrainModel:
     layers: list of dicts with core.Linear entries q k v o up gate down and
     optional int16 attn_gamma / mlp_gamma (RMS norm on when present)."""
 
-    def __init__(self, embeddings, positions, layers, head, d_model, heads, hidden_dim, seq_len):
+    def __init__(self, embeddings, positions, layers, head, d_model, heads, hidden_dim, seq_len,
+                 attention_kind: str = "softmax"):
         dev = core._dev()
+        self.attention_kind = attention_kind  # "softmax" (base-2) or "linear"
         self.embeddings = embeddings.to(dev, torch.int16).contiguous()
         self.positions = None if positions is None else positions.to(dev, torch.int16).contiguous()
         self.layers = []
@@ -306,7 +308,7 @@ class TrainModel:
                 arr[i].lin[j] = ly[nm].c()
         m = _TrainModelC(self.d_model, self.heads, self.hidden_dim, len(self.layers), self.seq_len,
                          self.embeddings.data_ptr(), None if self.positions is None else self.positions.data_ptr(),
-                         C.cast(arr, C.c_void_p), self.head.c())
+                         C.cast(arr, C.c_void_p), self.head.c(), 1 if self.attention_kind == "linear" else 0)
         m._keep = arr
         return m
 
