@@ -728,6 +728,175 @@ def run_generate(core, torch, batch=64, steps=16, prompt_len=256, warmup=1):
             "parity": {"sequences": 1, "bytes": 4, "equal": eq}}
 
 
+def run_sharded(args):
+    """The config-3 block with heads and batch sharded: ranks form batch groups
+    of G ranks (G = --shard-heads, default min(N, heads)); each group runs its
+    share of the global batch with positions split G ways for the token-wise
+    work and heads split G ways for attention (nsrl_sharded_transformer_block:
+    q|k|v and context rows cross NVLink as peer stores from the kernels'
+    epilogues).  Total work is fixed as N grows (strong scaling)."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", str(29500 + os.getpid() % 1000))
+        dist.init_process_group("gloo", rank=0, world_size=1)
+    from nsrl_b200 import build, core, shard
+    from nsrl_b200 import synth as Y
+    build.build()
+    L = core.lib()
+    G = args.shard_heads or min(world, HEADS)
+    Bg_total = args.shard_batch
+    if world % G or HEADS % G or SEQ % G or Bg_total % (world // G):
+        raise SystemExit(f"--shard-heads {G} does not split {world} ranks / {HEADS} heads / batch {Bg_total}")
+    ngroups = world // G
+    grp_id, grank = rank // G, rank % G
+    groups = [dist.new_group(list(range(g * G, (g + 1) * G))) for g in range(ngroups)] if world > 1 else [None]
+    pg = groups[grp_id]
+    Bg = Bg_total // ngroups
+    bw = Y.BlockWeights(seed=2024, d=D_MODEL, hidden=HIDDEN)
+    lin = {nm: core.Linear(torch.from_numpy(getattr(bw, nm)), core.make_scales(1, bw.shift[nm], bw.out_dim(nm)))
+           for nm in ("q", "k", "v", "o", "up", "gate", "down")}
+    blk = core.TransformerBlock(D_MODEL, HEADS, HIDDEN, *[lin[n] for n in ("q", "k", "v", "o", "up", "gate", "down")],
+                                torch.from_numpy(bw.attn_gamma), torch.from_numpy(bw.mlp_gamma), 1)
+    # the group's sequences (seeded by sequence index), this rank's positions of each
+    seqs = [Y.q15_gaussian(Y.tensor_seed(0x5A4D, grp_id * Bg + b), (SEQ, D_MODEL)) for b in range(Bg)]
+    a, b_ = shard.positions(SEQ, G, grank)
+    x_np = np.ascontiguousarray(np.stack([q[a:b_] for q in seqs]).reshape(-1, D_MODEL))
+    x = torch.from_numpy(x_np).cuda()
+    y = torch.empty_like(x)
+    g = shard.ShardGroup(Bg, SEQ, D_MODEL, HEADS, group=pg, timeout_ms=20000)
+    ws = core.workspace(g.workspace_bytes(HIDDEN))
+    st = core.Status()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def step(xin, yout):
+        r = g.block(blk, xin, yout, ws, st)
+        if r != 0:
+            raise RuntimeError(f"sharded block failed: {r} {L.nsrl_last_error()}")
+        core._check(g.post_status(st))
+        core._check(g.combine_status(st))
+
+    for _ in range(args.warmup):
+        st.reset()
+        flush.zero_()
+        step(x, y)
+    code, hs = st.fetch()
+    if code != 0:
+        raise RuntimeError(f"sharded block rejected during warm-up (flags {hs.flags:#x})")
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    dist.barrier()
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    for i in range(args.steps):
+        flush.zero_()
+        starts[i].record(stream)
+        st.buf.zero_()
+        step(x, y)
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    clk = clocks.stop()
+    ms = torch.tensor([sum(s_.elapsed_time(e_) for s_, e_ in zip(starts, ends))], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    elapsed_ms = float(ms.item())
+    code, hs = st.fetch()
+    if code != 0:
+        raise RuntimeError(f"sharded block rejected in the timed region (flags {hs.flags:#x})")
+    L.nsrl_profile_reset()
+    L.nsrl_profile_enable(1)
+    for _ in range(3):
+        flush.zero_()
+        st.buf.zero_()
+        step(x, y)
+    torch.cuda.synchronize()
+    L.nsrl_profile_enable(0)
+    n_launches, rows = kernel_table(L)
+    launches_per_step = n_launches // 3
+    # end to end: this rank's rows from pinned host memory, the block, the rows and the status back
+    xh = torch.from_numpy(x_np).pin_memory()
+    yh = torch.empty_like(xh).pin_memory()
+    sh = torch.empty(8, dtype=torch.int64).pin_memory()
+    xd, yd = torch.empty_like(x), torch.empty_like(y)
+    e2e_steps = max(3, min(args.steps, 20))
+    e_s = [torch.cuda.Event(enable_timing=True) for _ in range(e2e_steps)]
+    e_e = [torch.cuda.Event(enable_timing=True) for _ in range(e2e_steps)]
+    dist.barrier()
+    torch.cuda.synchronize()
+    for i in range(e2e_steps):
+        flush.zero_()
+        e_s[i].record(stream)
+        xd.copy_(xh, non_blocking=True)
+        st.buf.zero_()
+        step(xd, yd)
+        yh.copy_(yd, non_blocking=True)
+        sh.copy_(st.buf, non_blocking=True)
+        e_e[i].record(stream)
+    torch.cuda.synchronize()
+    if int(sh[0]) != 0 or not torch.equal(yh, y.cpu()):
+        raise RuntimeError("end-to-end sharded output differs from the device run")
+    t = torch.tensor([sum(a_.elapsed_time(b2) for a_, b2 in zip(e_s, e_e))], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t.item())
+    # parity: every rank checks its rows of its group's first sequence against the oracle
+    O = oracle_module()
+    ol = {nm: O.Linear(getattr(bw, nm), O.scales(1, bw.shift[nm], bw.out_dim(nm)))
+          for nm in ("q", "k", "v", "o", "up", "gate", "down")}
+    threads = max(1, (os.cpu_count() or 1) // max(1, min(world, 8)))
+    y1, _ = O.prenorm_attention_block(seqs[0], 1, SEQ, D_MODEL, HEADS, bw.attn_gamma, 1, ol["q"], ol["k"], ol["v"],
+                                      ol["o"], threads=threads)
+    ref, _ = O.prenorm_mlp_block(y1, SEQ, D_MODEL, HIDDEN, bw.mlp_gamma, 1, ol["up"], ol["gate"], ol["down"],
+                                 threads=threads)
+    eq = torch.tensor([int(np.array_equal(y.cpu().numpy()[:b_ - a], ref[a:b_]))], device="cuda")
+    if world > 1:
+        dist.all_reduce(eq, op=dist.ReduceOp.MIN)
+    g.close()
+    if rank == 0:
+        hbm, tfl, src = peaks()
+        tokens = Bg_total * SEQ
+        total_ms = sum(r["ms"] for r in rows.values())
+        kernels = {k: {"launches": v["launches"] // 3, "ms": round(v["ms"] / 3, 4), "share": round(v["ms"] / total_ms, 4)}
+                   for k, v in sorted(rows.items(), key=lambda kv: -kv[1]["ms"])}
+        out = {"metric": METRIC, "value": tokens * args.steps / (elapsed_ms / 1000.0), "unit": "tokens/s",
+               "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps,
+               "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+               "dtype": "int16xint8->int32/int64",
+               "data": "synthetic (seeded SplitMix64: Irwin-Hall Q15 sigma 4096, uniform i8 weights)",
+               "config": {"workload": f"prenorm causal attention + gated-MLP block forward, d{D_MODEL} "
+                                      f"h{HEADS}x{HEAD_DIM} ff{HIDDEN} s{SEQ}, global batch {Bg_total}",
+                          "global_batch": Bg_total, "seq_len": SEQ,
+                          "parallelism": f"heads/positions x{G}, batch x{ngroups}",
+                          "l2": "flushed before every step (256 MiB memset, outside the timed events)"},
+               "e2e": {"value": tokens * e2e_steps / (e2e_ms / 1000.0), "unit": "tokens/s",
+                       "h2d_bytes_per_step": int(x.numel() * 2) * world,
+                       "d2h_bytes_per_step": int(y.numel() * 2 + 64) * world, "steps": e2e_steps},
+               "gpu_launches": launches_per_step * args.steps,
+               "roofline": roofline(rows, hbm, tfl, src),
+               "kernels": kernels, "clocks": clk,
+               "parity": {"compared": "each rank's rows of its group's first sequence, last timed step",
+                          "equal": bool(int(eq.item()))}}
+        print(json.dumps(out), flush=True)
+        if not int(eq.item()):
+            raise RuntimeError("the sharded block output differs from the oracle")
+    dist.barrier()
+    dist.destroy_process_group()
+    return 0
+
+
 def run_secondary(args):
     """One secondary measurement alone on cuda:0 (its JSON object on one line)."""
     import torch
@@ -757,8 +926,12 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip the decode and linear-sweep measurements")
-    ap.add_argument("--case", default="block", choices=["block", "decode", "sweep", "train", "generate"],
-                    help="decode / sweep / train: run only that secondary measurement on one GPU")
+    ap.add_argument("--case", default="block", choices=["block", "decode", "sweep", "train", "generate", "sharded"],
+                    help="decode / sweep / train / generate: run only that secondary measurement on one GPU; "
+                         "sharded: the block with heads and batch sharded over the ranks")
+    ap.add_argument("--shard-heads", type=int, default=0, help="--case sharded: ranks per head group (default "
+                                                                 "min(N, heads))")
+    ap.add_argument("--shard-batch", type=int, default=BATCH, help="--case sharded: global batch (sequences)")
     ap.add_argument("--decode-batch", type=int, default=DEC_B)
     ap.add_argument("--train-steps", type=int, default=3, help="timed steps of the training-step measurement")
     ap.add_argument("--train-windows", type=int, default=TR_BATCH,
@@ -766,6 +939,8 @@ def main():
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.case == "sharded":
+        return run_sharded(args)
     if args.case != "block":
         return run_secondary(args)
 

@@ -625,6 +625,107 @@ nsrl_status nsrl_prenorm_transformer_block_host(const int16_t* x_host, size_t ba
 nsrl_status nsrl_selftest_bounded_wait(unsigned long long limit_ns, nsrl_device_status* status,
                                        unsigned long long* out, void* stream);
 
+/* ------------------------------------------------- head-sharded forward --
+ * The transformer block of nsrl_prenorm_transformer_block (or, without the
+ * MLP, nsrl_prenorm_attention_residual_block) split over n ranks, one GPU
+ * each, with results identical to the one-GPU block.  The reference computes
+ * this block on one CPU (attention.rs:1522-1583, mlp.rs:541-594); the split
+ * has no counterpart there.
+ *
+ * Rank r owns positions [r S/n, (r+1) S/n) of every sequence for the work
+ * done token by token -- the RMS norms, the Q|K|V, O, up, gate and down
+ * linears, the residual adds -- and heads [r H/n, (r+1) H/n) for attention.
+ * The Q|K|V projection of a rank's positions stores each head's q, k and v
+ * straight into the exchange buffer of the rank that owns the head, over
+ * NVLink (peer stores from the GEMM's epilogue); attention on a rank's heads
+ * stores each context row straight into the buffer of the rank that owns the
+ * position.  Every value is computed by the same kernel and operation
+ * order as on one GPU; only where it is stored changes, so the split is
+ * exact.  Weights are whole on every rank.
+ *
+ * x and y are the rank's rows [batch][S/n][d_model] (position-major within
+ * each sequence).  Shape rules: those of the one-GPU block, n <= 8, S and
+ * heads multiples of n, head_dim 64 and S <= 16384 (the tensor-core
+ * attention); d_model a multiple of 128 keeps the Q|K|V projection on the
+ * tensor cores (other sizes use the SIMT linear).
+ *
+ * Exchange buffers: every rank allocates one buffer of
+ * nsrl_shard_exchange_bytes with nsrl_shard_alloc, shares its IPC handle, and
+ * opens the others' with nsrl_ipc_open; nsrl_shard_group_create then takes
+ * all n buffers (index = rank; its own as allocated).  Every rank must have
+ * returned from nsrl_shard_group_create before any rank runs a phase (a host
+ * barrier), and all ranks run the same phases in the same order.
+ *
+ * Synchronisation is on the device: a phase that feeds other ranks ends with
+ * a signal (a release store of an epoch count into every rank's signal
+ * words); the phase that reads the exchange starts with a wait for every
+ * rank's signal of that epoch, bounded by the group's timeout.  A wait that
+ * runs out sets NSRL_FLAG_WAIT_TIMEOUT in the status (nsrl_status_fetch then
+ * returns NSRL_CORE_REJECTED), and the group is unusable afterwards: destroy
+ * it and create a new one on every rank.
+ *
+ * Status: each rank's status sees its own positions' saturations and its own
+ * heads' rejections.  nsrl_shard_status_post followed by
+ * nsrl_shard_status_combine adds every other rank's words into the status,
+ * so that each rank holds the status of the whole block (flags OR-ed,
+ * saturation counts summed); run the pair once per forward, after the last
+ * phase. */
+typedef struct nsrl_shard_group nsrl_shard_group;
+#define NSRL_IPC_HANDLE_BYTES 64
+
+size_t nsrl_shard_exchange_bytes(size_t batch, size_t seq_len, size_t d_model, size_t heads, size_t nranks);
+/* cudaMalloc'd, zeroed exchange buffer on the current device; free with nsrl_shard_free. */
+nsrl_status nsrl_shard_alloc(size_t bytes, void** buffer);
+nsrl_status nsrl_shard_free(void* buffer);
+/* CUDA IPC handle of a buffer from nsrl_shard_alloc, and its mapping in another process. */
+nsrl_status nsrl_ipc_get_handle(const void* buffer, uint8_t handle[NSRL_IPC_HANDLE_BYTES]);
+nsrl_status nsrl_ipc_open(const uint8_t handle[NSRL_IPC_HANDLE_BYTES], void** buffer);
+nsrl_status nsrl_ipc_close(void* buffer);
+
+/* Binds rank `rank` of `nranks` to the shape and the n exchange buffers (as
+ * mapped in this process), zeroes its own buffer's header and synchronises
+ * the device.  timeout_ms bounds every device wait (0 = 10 s). */
+nsrl_status nsrl_shard_group_create(nsrl_shard_group** group, int nranks, int rank, void* const* exchange,
+                                    size_t exchange_bytes, size_t batch, size_t seq_len, size_t d_model,
+                                    size_t heads, uint64_t timeout_ms);
+nsrl_status nsrl_shard_group_destroy(nsrl_shard_group* group);
+
+/* Scratch of the three phases on one rank (MLP hidden size hidden_dim; 0 when
+ * the MLP is left out). */
+size_t nsrl_sharded_block_workspace_size(const nsrl_shard_group* group, size_t hidden_dim);
+
+/* Phase 1: n = rms_norm(x) (or x itself with rms_gamma NULL), the Q|K|V
+ * projection of the rank's positions into the head owners' buffers, signal. */
+nsrl_status nsrl_sharded_block_qkv(const nsrl_shard_group* group, const int16_t* x, const int16_t* rms_gamma,
+                                   uint64_t rms_eps, const nsrl_linear_params* q, const nsrl_linear_params* k,
+                                   const nsrl_linear_params* v, const nsrl_linear_params* o, void* workspace,
+                                   size_t workspace_bytes, nsrl_device_status* status, void* stream);
+/* Phase 2: wait, causal attention of the rank's heads over all positions into
+ * the position owners' buffers, signal.  o is the block's output projection:
+ * the context's row L1 norms are kept when its i32 prefix check needs them. */
+nsrl_status nsrl_sharded_block_attention(const nsrl_shard_group* group, const nsrl_linear_params* o, void* workspace,
+                                         size_t workspace_bytes, nsrl_device_status* status, void* stream);
+/* Phase 3: wait, h = x + O(context) for the rank's positions, then (up not
+ * NULL) y = h + down(gated(up(n), gate(n))) with n = rms_norm(h), else y = h. */
+nsrl_status nsrl_sharded_block_output(const nsrl_shard_group* group, const int16_t* x, const nsrl_linear_params* o,
+                                      const int16_t* mlp_gamma, uint64_t rms_eps, const nsrl_linear_params* up,
+                                      const nsrl_linear_params* gate, const nsrl_linear_params* down, size_t hidden_dim,
+                                      int16_t* y, void* workspace, size_t workspace_bytes,
+                                      nsrl_device_status* status, void* stream);
+/* The three phases in order: one transformer block (MLP when up is not NULL). */
+nsrl_status nsrl_sharded_transformer_block(const nsrl_shard_group* group, const int16_t* x,
+                                           const int16_t* attn_gamma, const int16_t* mlp_gamma, uint64_t rms_eps,
+                                           const nsrl_linear_params* q, const nsrl_linear_params* k,
+                                           const nsrl_linear_params* v, const nsrl_linear_params* o,
+                                           const nsrl_linear_params* up, const nsrl_linear_params* gate,
+                                           const nsrl_linear_params* down, size_t hidden_dim, int16_t* y,
+                                           void* workspace, size_t workspace_bytes, nsrl_device_status* status,
+                                           void* stream);
+/* Posts this rank's status words to every rank and signals; then (combine)
+ * waits and adds the other ranks' posted words into *status. */
+nsrl_status nsrl_shard_status_post(const nsrl_shard_group* group, const nsrl_device_status* status, void* stream);
+nsrl_status nsrl_shard_status_combine(const nsrl_shard_group* group, nsrl_device_status* status, void* stream);
+
 /* ------------------------------------------------------------ profiling --
  * Per-launch CUDA-event timing of the library's own kernels (no counterpart
  * in the reference, whose only timer is a wall clock around the block loop,

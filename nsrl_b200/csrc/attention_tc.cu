@@ -85,6 +85,7 @@ struct Args {
   long long ldc;
   int16_t* probs;    // optional P [B][H][S][S]: the visited key tiles only, zeros above the diagonal
   int pstore;        // write P as byte planes [B][H][S][S] (the same entries) through maps.p_hi / p_lo
+  CtxRoute rt;       // head-sharded context destinations (rt.nranks > 0)
   nsrl_device_status* st;
 };
 
@@ -663,6 +664,19 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
     // and rhu(tot, 15) = (tot + 2^14) >> 15 cannot overflow.
     wait_bar(&ctl->o_full, 0, ctl, a.st);
     tc_fence_after();
+    // Destination row: this rank's context rows, or (head-sharded) the rows
+    // of the rank that owns position qi.
+    int8_t* chi = a.ctx_hi;
+    uint8_t* clo = a.ctx_lo;
+    unsigned long long* cl1 = a.ctx_l1;
+    long long crow = (long long)row0 + qi;
+    if (a.rt.nranks && row_live) {  // rows past the sequence store nothing
+      const int own = qi / a.rt.s_loc;
+      chi = a.rt.tab->ctx_hi[own];
+      clo = a.rt.tab->ctx_lo[own];
+      cl1 = a.ctx_l1 ? a.rt.tab->ctx_l1[own] : nullptr;
+      crow = (long long)b * a.rt.s_loc + (qi - own * a.rt.s_loc);
+    }
     unsigned l1 = 0;
 #pragma unroll
     for (int c = 0; c < 2; ++c) {  // dims [32g + 16c, +16)
@@ -689,12 +703,12 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
           hw[k] = __byte_perm(pk[2 * k], pk[2 * k + 1], 0x7531);
           lw[k] = __byte_perm(pk[2 * k], pk[2 * k + 1], 0x6420);
         }
-        const long long off = (long long)(row0 + qi) * a.ldc + h * HD + col;
-        *reinterpret_cast<uint4*>(a.ctx_hi + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-        *reinterpret_cast<uint4*>(a.ctx_lo + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        const long long off = crow * a.ldc + a.rt.col0 + h * HD + col;
+        *reinterpret_cast<uint4*>(chi + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        *reinterpret_cast<uint4*>(clo + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
       }
     }
-    if (row_live && a.ctx_l1) atomicAdd(&a.ctx_l1[row0 + qi], (unsigned long long)l1);
+    if (row_live && cl1) atomicAdd(&cl1[crow], (unsigned long long)l1);
   }
   tc_fence_before();
   __syncthreads();
@@ -781,15 +795,19 @@ size_t attention_tc_scratch_bytes(size_t B, size_t S, size_t d, size_t H) {
 
 cudaError_t launch_attention_tc(const Planes& qkv, const VtPlanes& vt, size_t B, size_t S, size_t d, size_t H,
                                 bool causal, Planes ctx, int16_t* wscr, nsrl_device_status* st,
-                                cudaStream_t stream, int16_t* probs, const Planes* probs_planes) {
+                                cudaStream_t stream, int16_t* probs, const Planes* probs_planes,
+                                const CtxRoute* route) {
   if (!attention_tc_supported(S, d, H) || encode_fn() == nullptr || wscr == nullptr) return cudaErrorNotSupported;
   if (probs_planes && (!causal || probs_planes->ld != S)) return cudaErrorInvalidValue;
+  if (route && route->nranks &&
+      (route->tab == nullptr || route->s_loc <= 0 || S % (size_t)route->s_loc != 0 || probs || probs_planes))
+    return cudaErrorInvalidValue;
   if (B == 0) return cudaSuccess;
   const size_t T = B * S;
   Maps m;
   const bool ok =
-      make_map(&m.q_hi, qkv.hi, 3 * d, T, qkv.ld, 64, QT) && make_map(&m.q_lo, qkv.lo, 3 * d, T, qkv.ld, 64, QT) &&
-      make_map(&m.k_hi, qkv.hi, 3 * d, T, qkv.ld, 64, KT) && make_map(&m.k_lo, qkv.lo, 3 * d, T, qkv.ld, 64, KT) &&
+      make_map(&m.q_hi, qkv.hi, 2 * d, T, qkv.ld, 64, QT) && make_map(&m.q_lo, qkv.lo, 2 * d, T, qkv.ld, 64, QT) &&
+      make_map(&m.k_hi, qkv.hi, 2 * d, T, qkv.ld, 64, KT) && make_map(&m.k_lo, qkv.lo, 2 * d, T, qkv.ld, 64, KT) &&
       make_map(&m.vt_hi, vt.hi, S, B * H * HD, S, KT, HD) && make_map(&m.vt_lo, vt.lo, S, B * H * HD, S, KT, HD) &&
       (!probs_planes || (make_p_map(&m.p_hi, probs_planes->hi, S, B * H) && make_p_map(&m.p_lo, probs_planes->lo, S, B * H))) &&
       make_map(&m.w, wscr, 2 * attention_tc_wstride(S), chunk_seqs(B, S, H) * H * ((S + QT - 1) / QT) * QT,
@@ -810,6 +828,7 @@ cudaError_t launch_attention_tc(const Planes& qkv, const VtPlanes& vt, size_t B,
   a.ldc = (long long)ctx.ld;
   a.probs = probs;
   a.pstore = probs_planes ? 1 : 0;
+  if (route) a.rt = *route;
   a.st = st;
   a.wscr = wscr;
   a.wstride = (long long)attention_tc_wstride(S);

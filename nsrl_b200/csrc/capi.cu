@@ -1132,4 +1132,194 @@ nsrl_status nsrl_mini_transformer_generate_streaming(const nsrl_train_model* m, 
   return NSRL_OK;
 }
 
+// ---- head-sharded forward: the three phases of one block on one rank ----
+namespace {
+// Workspace: input planes of the Q|K|V projection, the attention's weight
+// scratch, then the attention block's output h and the MLP scratch.
+struct ShardWs {
+  Planes xn;
+  int16_t* wscr;
+  int16_t* h;
+  size_t mlp_off;
+};
+
+ShardWs shard_ws(Carver& c, const ShardLayout& L) {
+  ShardWs w;
+  const size_t T = L.B * L.s_loc;
+  w.xn = c.planes(T, L.d, true);
+  const size_t ws = attention_tc_scratch_bytes(L.B, L.S, L.d_loc, L.h_loc);
+  w.wscr = c.take<int16_t>(ws / sizeof(int16_t));
+  w.h = c.take<int16_t>(T * L.d);
+  w.mlp_off = c.off;
+  return w;
+}
+
+size_t shard_ws_bytes(const ShardLayout& L, size_t F) {
+  Carver c(nullptr);
+  shard_ws(c, L);
+  if (F) mlp_ws(L.B * L.s_loc, L.d, F, &c);
+  return c.off;
+}
+
+nsrl_status shard_check(const nsrl_shard_group* g, void* ws, size_t bytes, size_t F, nsrl_device_status* st,
+                        const char* what) {
+  if (!g || !st) return shape_fail("sharded block: NULL group or status");
+  if (!ws || bytes < shard_ws_bytes(g->L, F)) {
+    set_error("%s: workspace too small", what);
+    return NSRL_INVALID_SHAPE;
+  }
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev != g->device) return shape_fail("sharded block: wrong device");
+  return NSRL_OK;
+}
+
+Planes own_ctx(const nsrl_shard_group* g, bool l1) {
+  uint8_t* b = g->base[g->rank];
+  Planes p;
+  p.hi = reinterpret_cast<int8_t*>(b + g->L.ctx_hi);
+  p.lo = b + g->L.ctx_lo;
+  p.l1 = l1 ? reinterpret_cast<unsigned long long*>(b + g->L.ctx_l1) : nullptr;
+  p.ld = g->L.d;
+  return p;
+}
+}  // namespace
+
+size_t nsrl_sharded_block_workspace_size(const nsrl_shard_group* group, size_t hidden_dim) {
+  return group ? shard_ws_bytes(group->L, hidden_dim) : 0;
+}
+
+nsrl_status nsrl_sharded_block_qkv(const nsrl_shard_group* g, const int16_t* x, const int16_t* rms_gamma,
+                                   uint64_t rms_eps, const nsrl_linear_params* q, const nsrl_linear_params* k,
+                                   const nsrl_linear_params* v, const nsrl_linear_params* o, void* workspace,
+                                   size_t workspace_bytes, nsrl_device_status* status, void* stream) {
+  nsrl_status r = shard_check(g, workspace, workspace_bytes, 0, status, "nsrl_sharded_block_qkv");
+  if (r != NSRL_OK) return r;
+  const ShardLayout& L = g->L;
+  if ((r = validate_attention(L.S, L.d, L.H, q, k, v, o)) != NSRL_OK) return r;
+  if (!x) return shape_fail("x is NULL");
+  cudaStream_t s = (cudaStream_t)stream;
+  const size_t T = L.B * L.s_loc;
+  Carver c(workspace);
+  ShardWs w = shard_ws(c, L);
+  if (!needs_l1(L.d, q, k, v)) w.xn.l1 = nullptr;
+  if (rms_gamma)
+    NSRL_TRY(launch_rms_norm(x, T, L.d, rms_gamma, rms_eps, nullptr, w.xn, status, s), "rms norm");
+  else
+    NSRL_TRY(launch_split_planes(x, T, L.d, L.d, w.xn, s), "split");
+  // The context's row L1 is summed by every rank's attention: zero it before the signal.
+  if (needs_l1(L.d, o))
+    NSRL_TRY(cudaMemsetAsync(own_ctx(g, true).l1, 0, T * sizeof(unsigned long long), s), "memset");
+  GemmArgs ga{};
+  ga.a_hi = w.xn.hi;
+  ga.a_lo = w.xn.lo;
+  ga.a_l1 = w.xn.l1;
+  ga.lda = L.d;
+  ga.M = T;
+  ga.K = L.d;
+  ga.nseg = 3;
+  ga.seg[0] = seg_of(q);
+  ga.seg[1] = seg_of(k);
+  ga.seg[2] = seg_of(v);
+  ga.epi = Epi::QKV_VT;
+  ga.vt = VtPlanes{nullptr, nullptr, (int)L.S, (int)L.h_loc, (int)(L.d / L.H), nullptr};
+  ga.route.nranks = g->nranks;
+  ga.route.rank = g->rank;
+  ga.route.S = (int)L.S;
+  ga.route.s_loc = (int)L.s_loc;
+  ga.route.d_loc = (int)L.d_loc;
+  ga.route.tab = g->tab;
+  ga.st = status;
+  NSRL_TRY(launch_gemm(ga, s), "qkv projection");
+  NSRL_TRY(launch_shard_post(g, nullptr, s), "signal");
+  return NSRL_OK;
+}
+
+nsrl_status nsrl_sharded_block_attention(const nsrl_shard_group* g, const nsrl_linear_params* o, void* workspace,
+                                         size_t workspace_bytes, nsrl_device_status* status, void* stream) {
+  nsrl_status r = shard_check(g, workspace, workspace_bytes, 0, status, "nsrl_sharded_block_attention");
+  if (r != NSRL_OK) return r;
+  const ShardLayout& L = g->L;
+  if (!linear_ok(o, L.d, L.d)) return shape_fail("o must be a d_model x d_model linear");
+  cudaStream_t s = (cudaStream_t)stream;
+  Carver c(workspace);
+  ShardWs w = shard_ws(c, L);
+  NSRL_TRY(launch_shard_wait(g, false, status, s), "wait");
+  uint8_t* b = g->base[g->rank];
+  Planes qk{reinterpret_cast<int8_t*>(b + L.qk_hi), b + L.qk_lo, nullptr, 2 * L.d_loc};
+  VtPlanes vt{reinterpret_cast<int8_t*>(b + L.vt_hi), b + L.vt_lo, (int)L.S, (int)L.h_loc, (int)(L.d / L.H), w.wscr};
+  Planes ctx{nullptr, nullptr, needs_l1(L.d, o) ? own_ctx(g, true).l1 : nullptr, L.d};
+  CtxRoute rt;
+  rt.nranks = g->nranks;
+  rt.s_loc = (int)L.s_loc;
+  rt.col0 = (int)(g->rank * L.d_loc);
+  rt.tab = g->tab;
+  NSRL_TRY(launch_attention_tc(qk, vt, L.B, L.S, L.d_loc, L.h_loc, true, ctx, w.wscr, status, s, nullptr, nullptr,
+                               &rt),
+           "attention");
+  NSRL_TRY(launch_shard_post(g, nullptr, s), "signal");
+  return NSRL_OK;
+}
+
+nsrl_status nsrl_sharded_block_output(const nsrl_shard_group* g, const int16_t* x, const nsrl_linear_params* o,
+                                      const int16_t* mlp_gamma, uint64_t rms_eps, const nsrl_linear_params* up_p,
+                                      const nsrl_linear_params* gate, const nsrl_linear_params* down,
+                                      size_t hidden_dim, int16_t* y, void* workspace, size_t workspace_bytes,
+                                      nsrl_device_status* status, void* stream) {
+  nsrl_status r = shard_check(g, workspace, workspace_bytes, up_p ? hidden_dim : 0, status,
+                              "nsrl_sharded_block_output");
+  if (r != NSRL_OK) return r;
+  const ShardLayout& L = g->L;
+  const size_t T = L.B * L.s_loc;
+  if (!linear_ok(o, L.d, L.d)) return shape_fail("o must be a d_model x d_model linear");
+  if (up_p && (r = validate_mlp(L.S, L.d, hidden_dim, up_p, gate, down)) != NSRL_OK) return r;
+  if (!x || !y) return shape_fail("x / y is NULL");
+  if (x == y) return shape_fail("x and y may not alias");
+  cudaStream_t s = (cudaStream_t)stream;
+  Carver c(workspace);
+  ShardWs w = shard_ws(c, L);
+  NSRL_TRY(launch_shard_wait(g, false, status, s), "wait");
+  const Planes ctx = own_ctx(g, needs_l1(L.d, o));
+  int16_t* h = up_p ? w.h : y;
+  GemmArgs og{};
+  og.a_hi = ctx.hi;
+  og.a_lo = ctx.lo;
+  og.a_l1 = ctx.l1;
+  og.lda = L.d;
+  og.M = T;
+  og.K = L.d;
+  og.nseg = 1;
+  og.seg[0] = seg_of(o);
+  og.epi = Epi::RESID;
+  og.y = h;
+  og.ldy = L.d;
+  og.skip = x;
+  og.ldskip = L.d;
+  og.sat_counter = &status->attention_saturations;
+  og.st = status;
+  NSRL_TRY(launch_gemm(og, s), "output projection");
+  if (!up_p) return NSRL_OK;
+  c.off = w.mlp_off;
+  return mlp_block(h, T, L.d, hidden_dim, mlp_gamma, rms_eps, up_p, gate, down, y, c, status, s);
+}
+
+nsrl_status nsrl_sharded_transformer_block(const nsrl_shard_group* g, const int16_t* x, const int16_t* attn_gamma,
+                                           const int16_t* mlp_gamma, uint64_t rms_eps, const nsrl_linear_params* q,
+                                           const nsrl_linear_params* k, const nsrl_linear_params* v,
+                                           const nsrl_linear_params* o, const nsrl_linear_params* up_p,
+                                           const nsrl_linear_params* gate, const nsrl_linear_params* down,
+                                           size_t hidden_dim, int16_t* y, void* workspace, size_t workspace_bytes,
+                                           nsrl_device_status* status, void* stream) {
+  nsrl_status r = shard_check(g, workspace, workspace_bytes, up_p ? hidden_dim : 0, status,
+                              "nsrl_sharded_transformer_block");
+  if (r != NSRL_OK) return r;
+  if (up_p && (r = validate_mlp(g->L.S, g->L.d, hidden_dim, up_p, gate, down)) != NSRL_OK) return r;
+  if (!x || !y || x == y) return shape_fail("x / y is NULL or they alias");
+  r = nsrl_sharded_block_qkv(g, x, attn_gamma, rms_eps, q, k, v, o, workspace, workspace_bytes, status, stream);
+  if (r == NSRL_OK) r = nsrl_sharded_block_attention(g, o, workspace, workspace_bytes, status, stream);
+  if (r == NSRL_OK)
+    r = nsrl_sharded_block_output(g, x, o, mlp_gamma, rms_eps, up_p, gate, down, hidden_dim, y, workspace,
+                                  workspace_bytes, status, stream);
+  return r;
+}
+
 }  // extern "C"

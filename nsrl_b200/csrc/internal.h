@@ -44,6 +44,38 @@ struct VtPlanes {
   int16_t* wscr;  // weight scratch of the tensor-core attention (may be null)
 };
 
+// ---- head-sharded forward (shard.cu) ----
+// Ranks r = 0..n-1 own the positions [r s_loc, (r+1) s_loc) of every sequence
+// for the token-wise work (norms, linears, MLP) and the heads [r Hr, (r+1) Hr)
+// for attention.  Every rank's exchange buffer has the same layout; the
+// table holds each rank's regions as mapped in this process (device memory).
+constexpr int kMaxShardRanks = 8;
+struct ShardTable {
+  int8_t* qk_hi[kMaxShardRanks];  // [B*S][2 d_loc]: q | k of the rank's heads, all positions
+  uint8_t* qk_lo[kMaxShardRanks];
+  int8_t* vt_hi[kMaxShardRanks];  // [B][d_loc][S]: v of the rank's heads, transposed per head
+  uint8_t* vt_lo[kMaxShardRanks];
+  int8_t* ctx_hi[kMaxShardRanks];  // [B*s_loc][d]: the context of the rank's positions, all heads
+  uint8_t* ctx_lo[kMaxShardRanks];
+  unsigned long long* ctx_l1[kMaxShardRanks];  // [B*s_loc]
+  unsigned long long* signal[kMaxShardRanks];  // [kMaxShardRanks]: epoch last signalled by each rank
+  unsigned long long* slots[kMaxShardRanks];   // [kMaxShardRanks][4]: status words posted by each rank
+};
+// Q|K|V projection of the rank's positions: columns go to the head owner's
+// q|k planes and transposed v planes instead of local planes.
+struct QkvRoute {
+  int nranks = 0;  // 0: local stores
+  int rank = 0, S = 0, s_loc = 0, d_loc = 0;
+  const ShardTable* tab = nullptr;
+};
+// Context of the rank's heads: rows go to the position owner's context planes
+// at column col0 + h * hd (and its row L1).
+struct CtxRoute {
+  int nranks = 0;  // 0: local stores
+  int s_loc = 0, col0 = 0;
+  const ShardTable* tab = nullptr;
+};
+
 struct GemmArgs {
   const int8_t* a_hi;
   const uint8_t* a_lo;
@@ -62,6 +94,7 @@ struct GemmArgs {
   unsigned long long* sat_counter;
   VtPlanes vt;
   bool v_rows = false;  // QKV_VT: the v columns also go to yp (row-major q|k|v planes)
+  QkvRoute route;       // QKV_VT: the head-sharded destinations (route.nranks > 0)
   nsrl_device_status* st;
   // Backward-input form (linear.rs:594-640): the sum is an i64 (no prefix
   // rule) requantised by requantize_i64_to_i16; A holds the prescaled grads.
@@ -96,10 +129,12 @@ cudaError_t launch_attention(const Planes& qkv, size_t B, size_t S, size_t d, si
 // probs_planes (optional, causal only, ld S): the same entries as byte planes;
 // row t is written for keys below the end of its 128-key block, zeros above
 // the diagonal, which is the causal plane form the backward reads.
+// route (optional): the head-sharded context destinations; d and H are then
+// the rank's columns and heads, and qkv holds q | k only (ld >= 2 d).
 cudaError_t launch_attention_tc(const Planes& qkv, const VtPlanes& vt, size_t B, size_t S, size_t d, size_t H,
                                 bool causal, Planes ctx, int16_t* wscr, nsrl_device_status* st,
                                 cudaStream_t stream, int16_t* probs = nullptr,
-                                const Planes* probs_planes = nullptr);
+                                const Planes* probs_planes = nullptr, const CtxRoute* route = nullptr);
 size_t attention_tc_wstride(size_t S);
 size_t attention_tc_scratch_bytes(size_t B, size_t S, size_t d, size_t H);
 // Shape rule of the tensor-core attention (head_dim 64, seq_len % 16 == 0,
@@ -221,4 +256,36 @@ cudaError_t launch_linear_attention_step(const Planes& qkv, size_t B, size_t d, 
 void set_error(const char* fmt, ...);
 bool tma_supported();
 
+// Byte offsets of one exchange buffer of a head-sharded forward (the same on
+// every rank): a 4 KiB header (signal words, the epoch counter, posted status
+// slots), then the q|k planes, the transposed v planes, and the context planes
+// with their row L1, each 256-byte aligned.
+struct ShardLayout {
+  size_t B = 0, S = 0, d = 0, H = 0, n = 0, s_loc = 0, d_loc = 0, h_loc = 0;
+  size_t qk_hi = 0, qk_lo = 0, vt_hi = 0, vt_lo = 0, ctx_hi = 0, ctx_lo = 0, ctx_l1 = 0, total = 0;
+};
+constexpr size_t kShardSignalOff = 0;    // u64 [kMaxShardRanks]
+constexpr size_t kShardEpochOff = 64;    // u64: this rank's signals so far
+constexpr size_t kShardSlotsOff = 256;   // u64 [kMaxShardRanks][4]
+constexpr size_t kShardHeaderBytes = 4096;
+// false when the shape does not split over n ranks.
+bool shard_layout(size_t B, size_t S, size_t d, size_t H, size_t n, ShardLayout* L);
+
+// Signal every rank that this rank's stores so far are complete (epoch + 1).
+cudaError_t launch_shard_post(const nsrl_shard_group* g, const nsrl_device_status* post_status, cudaStream_t s);
+// Wait (bounded) until every rank has signalled this rank's current epoch;
+// with combine, add the status words the ranks posted into *st.
+cudaError_t launch_shard_wait(const nsrl_shard_group* g, bool combine, nsrl_device_status* st, cudaStream_t s);
+
 }  // namespace nsrl
+
+// One rank's view of a head-sharded forward: the shape it is bound to, the
+// exchange buffers of all ranks as mapped in this process, and the device
+// copy of their route table.
+struct nsrl_shard_group {
+  int nranks = 0, rank = 0, device = 0;
+  nsrl::ShardLayout L;
+  unsigned long long timeout_ns = 0;
+  uint8_t* base[nsrl::kMaxShardRanks] = {};
+  nsrl::ShardTable* tab = nullptr;  // device memory
+};

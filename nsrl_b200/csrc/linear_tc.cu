@@ -69,6 +69,7 @@ struct TcParams {
   uint8_t* vtl;
   int vt_S, vt_H, vt_hd, vt_col0;  // QKV_VT: output columns >= vt_col0 go to the transposed planes
   bool v_rows;                      // QKV_VT: and to the row-major planes as well
+  QkvRoute route;                   // QKV_VT: head-sharded destinations (route.nranks > 0)
   bool small_acc;                   // K * 127 * 32767 < 2^30: every accumulator is below 2^30
   bool wide;                        // i64 accumulator, requantize_i64_to_i16 (backward-input linears)
   nsrl_device_status* st;
@@ -217,6 +218,63 @@ __device__ __forceinline__ void store16_planes_nol1(int8_t* dh, uint8_t* dl, con
       }
     }
   }
+}
+
+// Head-sharded Q|K|V stores.  Row m of this rank's projection is position
+// rank * s_loc + (m % s_loc) of sequence m / s_loc; column c of segment seg
+// (q, k, v) belongs to rank c / d_loc.  q and k go to that rank's planes
+// [B*S][2 d_loc] (q at column 0, k at d_loc), v to its transposed planes
+// [B][d_loc][S].  Sixteen columns starting at a multiple of 16 never cross
+// a rank (d_loc is a multiple of the head dim, itself a multiple of 16).
+__device__ __forceinline__ void qkv_route_store16(const TcParams& p, int m, int n, const int (&v)[16],
+                                                  const uint32_t (&o)[8], int nv) {
+  const QkvRoute& R = p.route;
+  const int d = p.seg_rows;
+  const int b = m / R.s_loc;
+  const int pos = R.rank * R.s_loc + (m - b * R.s_loc);
+  const int seg = n / d, c = n - seg * d;
+  const int own = c / R.d_loc, cl = c - own * R.d_loc;
+  if (seg < 2) {
+    const long long ld = 2LL * R.d_loc;
+    const long long col = (long long)seg * R.d_loc + cl;
+    const long long off = ((long long)b * R.S + pos) * ld + col;
+    store16_planes_nol1(R.tab->qk_hi[own] + off, R.tab->qk_lo[own] + off, o, nv, ((ld | col) & 15) == 0);
+  } else {
+    int8_t* vh = R.tab->vt_hi[own];
+    uint8_t* vl = R.tab->vt_lo[own];
+    const long long off0 = ((long long)b * R.d_loc + cl) * R.S + pos;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      if (i < nv) {
+        const long long off = off0 + (long long)i * R.S;
+        vh[off] = (int8_t)(v[i] >> 8);
+        vl[off] = (uint8_t)(v[i] & 255);
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void qkv_route_store1(const TcParams& p, int m, int n, int v) {
+  const QkvRoute& R = p.route;
+  const int d = p.seg_rows;
+  const int b = m / R.s_loc;
+  const int pos = R.rank * R.s_loc + (m - b * R.s_loc);
+  const int seg = n / d, c = n - seg * d;
+  const int own = c / R.d_loc, cl = c - own * R.d_loc;
+  long long off;
+  int8_t* h;
+  uint8_t* l;
+  if (seg < 2) {
+    off = ((long long)b * R.S + pos) * (2LL * R.d_loc) + (long long)seg * R.d_loc + cl;
+    h = R.tab->qk_hi[own];
+    l = R.tab->qk_lo[own];
+  } else {
+    off = ((long long)b * R.d_loc + cl) * R.S + pos;
+    h = R.tab->vt_hi[own];
+    l = R.tab->vt_lo[own];
+  }
+  h[off] = (int8_t)(v >> 8);
+  l[off] = (uint8_t)(v & 255);
 }
 
 // mlp.rs:150-170 on values already in [-32768, 32767] (int arguments, no
@@ -484,6 +542,10 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
           } else {
 #pragma unroll
             for (int i = 0; i < 8; ++i) o[i] = __byte_perm((uint32_t)v[2 * i], (uint32_t)v[2 * i + 1], 0x5410);
+            if (EPI == (int)Epi::QKV_VT && p.route.nranks) {
+              qkv_route_store16(p, r, nh, v, o, nv);
+              continue;
+            }
             if (EPI == (int)Epi::I16 || (EPI == (int)Epi::QKV_VT && p.y))  // QKV_VT: the training step's int16 cache
               store16_i16(p.y + (long long)r * p.ldy + nh, o, nv, ((p.ldy | nh) & 7) == 0);
             if (EPI == (int)Epi::I16) continue;
@@ -593,6 +655,10 @@ __global__ void gemm_simt_kernel(const SimtParams s) {
     } else {
       v = finish1(h, l, p.bias[sg], p.scales[sg], nl);
     }
+  }
+  if (s.epi == (int)Epi::QKV_VT && p.route.nranks) {
+    qkv_route_store1(p, m, n, v);
+    return;
   }
   if (s.epi == (int)Epi::I16) {
     p.y[(long long)m * p.ldy + n] = v;
@@ -869,6 +935,10 @@ cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t stream) {
   p.vt_hd = a.vt.hd;
   p.vt_col0 = a.epi == Epi::QKV_VT ? 2 * (int)a.seg[0].rows : INT_MAX;
   p.v_rows = a.v_rows;
+  p.route = a.route;
+  if (a.route.nranks && (a.epi != Epi::QKV_VT || a.nseg != 3 || a.route.tab == nullptr || a.route.s_loc <= 0 ||
+                         a.route.d_loc <= 0 || a.route.d_loc % 16 != 0 || a.M % (size_t)a.route.s_loc != 0))
+    return cudaErrorInvalidValue;
   p.small_acc = (unsigned long long)a.K * 127ull * 32767ull < (1ull << 30);
   p.wide = a.wide;
   p.st = a.st;
