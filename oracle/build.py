@@ -22,10 +22,10 @@ def needs_build() -> bool:
 
 def build(force: bool = False) -> str:
     if force or needs_build():
-        cmd = ["g++", "-std=c++17", "-O3", "-fPIC", "-shared", "-pthread", "-Wall",
-               "-o", OUT + ".tmp"] + SRC
+        tmp = f"{OUT}.{os.getpid()}.tmp"  # one temporary per process: ranks may build at once
+        cmd = ["g++", "-std=c++17", "-O3", "-fPIC", "-shared", "-pthread", "-Wall", "-o", tmp] + SRC
         subprocess.check_call(cmd)
-        os.replace(OUT + ".tmp", OUT)
+        os.replace(tmp, OUT)
     return OUT
 
 
@@ -39,11 +39,11 @@ NATIVE_OUT = os.path.join(HERE, "liboracle_native.so")
 def build_native() -> str:
     """Same sources with -march=native for timing the CPU baseline on the host it runs on."""
     if not os.path.exists(NATIVE_OUT) or os.path.getmtime(NATIVE_OUT) < max(os.path.getmtime(p) for p in SRC + HDR):
-        cmd = ["g++", "-std=c++17", "-O3", "-march=native", "-fPIC", "-shared", "-pthread",
-               "-o", NATIVE_OUT + ".tmp"] + SRC
+        tmp = f"{NATIVE_OUT}.{os.getpid()}.tmp"
+        cmd = ["g++", "-std=c++17", "-O3", "-march=native", "-fPIC", "-shared", "-pthread", "-o", tmp] + SRC
         try:
             subprocess.check_call(cmd)
         except (subprocess.CalledProcessError, OSError):
             return build()
-        os.replace(NATIVE_OUT + ".tmp", NATIVE_OUT)
+        os.replace(tmp, NATIVE_OUT)
     return NATIVE_OUT
