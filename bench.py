@@ -783,8 +783,7 @@ def run_sharded(args):
         r = g.block(blk, xin, yout, ws, st)
         if r != 0:
             raise RuntimeError(f"sharded block failed: {r} {L.nsrl_last_error()}")
-        core._check(g.post_status(st))
-        core._check(g.combine_status(st))
+        core._check(g.allreduce_status(st))
 
     for _ in range(args.warmup):
         st.reset()

@@ -712,7 +712,10 @@ nsrl_status nsrl_sharded_block_output(const nsrl_shard_group* group, const int16
                                       const nsrl_linear_params* gate, const nsrl_linear_params* down, size_t hidden_dim,
                                       int16_t* y, void* workspace, size_t workspace_bytes,
                                       nsrl_device_status* status, void* stream);
-/* The three phases in order: one transformer block (MLP when up is not NULL). */
+/* The three phases in order: one transformer block (MLP when up is not NULL),
+ * each signal fused with the wait that follows it (one launch), which needs
+ * every rank's phases to run at the same time: ranks in separate processes,
+ * one GPU each.  Ranks emulated on one GPU call the phases one by one. */
 nsrl_status nsrl_sharded_transformer_block(const nsrl_shard_group* group, const int16_t* x,
                                            const int16_t* attn_gamma, const int16_t* mlp_gamma, uint64_t rms_eps,
                                            const nsrl_linear_params* q, const nsrl_linear_params* k,
@@ -722,9 +725,11 @@ nsrl_status nsrl_sharded_transformer_block(const nsrl_shard_group* group, const 
                                            void* workspace, size_t workspace_bytes, nsrl_device_status* status,
                                            void* stream);
 /* Posts this rank's status words to every rank and signals; then (combine)
- * waits and adds the other ranks' posted words into *status. */
+ * waits and adds the other ranks' posted words into *status.  The pair in
+ * one launch, for ranks in separate processes: nsrl_shard_status_allreduce. */
 nsrl_status nsrl_shard_status_post(const nsrl_shard_group* group, const nsrl_device_status* status, void* stream);
 nsrl_status nsrl_shard_status_combine(const nsrl_shard_group* group, nsrl_device_status* status, void* stream);
+nsrl_status nsrl_shard_status_allreduce(const nsrl_shard_group* group, nsrl_device_status* status, void* stream);
 
 /* ------------------------------------------------------------ profiling --
  * Per-launch CUDA-event timing of the library's own kernels (no counterpart

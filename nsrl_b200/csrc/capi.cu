@@ -1188,16 +1188,12 @@ size_t nsrl_sharded_block_workspace_size(const nsrl_shard_group* group, size_t h
   return group ? shard_ws_bytes(group->L, hidden_dim) : 0;
 }
 
-nsrl_status nsrl_sharded_block_qkv(const nsrl_shard_group* g, const int16_t* x, const int16_t* rms_gamma,
-                                   uint64_t rms_eps, const nsrl_linear_params* q, const nsrl_linear_params* k,
-                                   const nsrl_linear_params* v, const nsrl_linear_params* o, void* workspace,
-                                   size_t workspace_bytes, nsrl_device_status* status, void* stream) {
-  nsrl_status r = shard_check(g, workspace, workspace_bytes, 0, status, "nsrl_sharded_block_qkv");
-  if (r != NSRL_OK) return r;
+namespace {
+// The phases' work without their signal and wait.
+nsrl_status qkv_body(const nsrl_shard_group* g, const int16_t* x, const int16_t* rms_gamma, uint64_t rms_eps,
+                     const nsrl_linear_params* q, const nsrl_linear_params* k, const nsrl_linear_params* v,
+                     const nsrl_linear_params* o, void* workspace, nsrl_device_status* status, cudaStream_t s) {
   const ShardLayout& L = g->L;
-  if ((r = validate_attention(L.S, L.d, L.H, q, k, v, o)) != NSRL_OK) return r;
-  if (!x) return shape_fail("x is NULL");
-  cudaStream_t s = (cudaStream_t)stream;
   const size_t T = L.B * L.s_loc;
   Carver c(workspace);
   ShardWs w = shard_ws(c, L);
@@ -1227,23 +1223,20 @@ nsrl_status nsrl_sharded_block_qkv(const nsrl_shard_group* g, const int16_t* x, 
   ga.route.S = (int)L.S;
   ga.route.s_loc = (int)L.s_loc;
   ga.route.d_loc = (int)L.d_loc;
-  ga.route.tab = g->tab;
+  // other ranks' rows: into this rank's staging slots, then one coalesced push
+  // over NVLink (or, without staging, peer stores from the epilogue)
+  ga.route.tab = g->stab ? g->stab : g->tab;
   ga.st = status;
   NSRL_TRY(launch_gemm(ga, s), "qkv projection");
-  NSRL_TRY(launch_shard_post(g, nullptr, s), "signal");
+  NSRL_TRY(launch_shard_push(g, s), "qkv push");
   return NSRL_OK;
 }
 
-nsrl_status nsrl_sharded_block_attention(const nsrl_shard_group* g, const nsrl_linear_params* o, void* workspace,
-                                         size_t workspace_bytes, nsrl_device_status* status, void* stream) {
-  nsrl_status r = shard_check(g, workspace, workspace_bytes, 0, status, "nsrl_sharded_block_attention");
-  if (r != NSRL_OK) return r;
+nsrl_status attention_body(const nsrl_shard_group* g, const nsrl_linear_params* o, void* workspace,
+                           nsrl_device_status* status, cudaStream_t s) {
   const ShardLayout& L = g->L;
-  if (!linear_ok(o, L.d, L.d)) return shape_fail("o must be a d_model x d_model linear");
-  cudaStream_t s = (cudaStream_t)stream;
   Carver c(workspace);
   ShardWs w = shard_ws(c, L);
-  NSRL_TRY(launch_shard_wait(g, false, status, s), "wait");
   uint8_t* b = g->base[g->rank];
   Planes qk{reinterpret_cast<int8_t*>(b + L.qk_hi), b + L.qk_lo, nullptr, 2 * L.d_loc};
   VtPlanes vt{reinterpret_cast<int8_t*>(b + L.vt_hi), b + L.vt_lo, (int)L.S, (int)L.h_loc, (int)(L.d / L.H), w.wscr};
@@ -1256,28 +1249,17 @@ nsrl_status nsrl_sharded_block_attention(const nsrl_shard_group* g, const nsrl_l
   NSRL_TRY(launch_attention_tc(qk, vt, L.B, L.S, L.d_loc, L.h_loc, true, ctx, w.wscr, status, s, nullptr, nullptr,
                                &rt),
            "attention");
-  NSRL_TRY(launch_shard_post(g, nullptr, s), "signal");
   return NSRL_OK;
 }
 
-nsrl_status nsrl_sharded_block_output(const nsrl_shard_group* g, const int16_t* x, const nsrl_linear_params* o,
-                                      const int16_t* mlp_gamma, uint64_t rms_eps, const nsrl_linear_params* up_p,
-                                      const nsrl_linear_params* gate, const nsrl_linear_params* down,
-                                      size_t hidden_dim, int16_t* y, void* workspace, size_t workspace_bytes,
-                                      nsrl_device_status* status, void* stream) {
-  nsrl_status r = shard_check(g, workspace, workspace_bytes, up_p ? hidden_dim : 0, status,
-                              "nsrl_sharded_block_output");
-  if (r != NSRL_OK) return r;
+nsrl_status output_body(const nsrl_shard_group* g, const int16_t* x, const nsrl_linear_params* o,
+                        const int16_t* mlp_gamma, uint64_t rms_eps, const nsrl_linear_params* up_p,
+                        const nsrl_linear_params* gate, const nsrl_linear_params* down, size_t hidden_dim,
+                        int16_t* y, void* workspace, nsrl_device_status* status, cudaStream_t s) {
   const ShardLayout& L = g->L;
   const size_t T = L.B * L.s_loc;
-  if (!linear_ok(o, L.d, L.d)) return shape_fail("o must be a d_model x d_model linear");
-  if (up_p && (r = validate_mlp(L.S, L.d, hidden_dim, up_p, gate, down)) != NSRL_OK) return r;
-  if (!x || !y) return shape_fail("x / y is NULL");
-  if (x == y) return shape_fail("x and y may not alias");
-  cudaStream_t s = (cudaStream_t)stream;
   Carver c(workspace);
   ShardWs w = shard_ws(c, L);
-  NSRL_TRY(launch_shard_wait(g, false, status, s), "wait");
   const Planes ctx = own_ctx(g, needs_l1(L.d, o));
   int16_t* h = up_p ? w.h : y;
   GemmArgs og{};
@@ -1302,6 +1284,68 @@ nsrl_status nsrl_sharded_block_output(const nsrl_shard_group* g, const int16_t* 
   return mlp_block(h, T, L.d, hidden_dim, mlp_gamma, rms_eps, up_p, gate, down, y, c, status, s);
 }
 
+nsrl_status check_qkv(const nsrl_shard_group* g, const int16_t* x, const nsrl_linear_params* q,
+                      const nsrl_linear_params* k, const nsrl_linear_params* v, const nsrl_linear_params* o) {
+  const ShardLayout& L = g->L;
+  nsrl_status r = validate_attention(L.S, L.d, L.H, q, k, v, o);
+  if (r != NSRL_OK) return r;
+  return x ? NSRL_OK : shape_fail("x is NULL");
+}
+
+nsrl_status check_output(const nsrl_shard_group* g, const int16_t* x, const nsrl_linear_params* o,
+                         const nsrl_linear_params* up_p, const nsrl_linear_params* gate,
+                         const nsrl_linear_params* down, size_t hidden_dim, const int16_t* y) {
+  const ShardLayout& L = g->L;
+  if (!linear_ok(o, L.d, L.d)) return shape_fail("o must be a d_model x d_model linear");
+  if (up_p) {
+    nsrl_status r = validate_mlp(L.S, L.d, hidden_dim, up_p, gate, down);
+    if (r != NSRL_OK) return r;
+  }
+  if (!x || !y) return shape_fail("x / y is NULL");
+  if (x == y) return shape_fail("x and y may not alias");
+  return NSRL_OK;
+}
+}  // namespace
+
+nsrl_status nsrl_sharded_block_qkv(const nsrl_shard_group* g, const int16_t* x, const int16_t* rms_gamma,
+                                   uint64_t rms_eps, const nsrl_linear_params* q, const nsrl_linear_params* k,
+                                   const nsrl_linear_params* v, const nsrl_linear_params* o, void* workspace,
+                                   size_t workspace_bytes, nsrl_device_status* status, void* stream) {
+  nsrl_status r = shard_check(g, workspace, workspace_bytes, 0, status, "nsrl_sharded_block_qkv");
+  if (r == NSRL_OK) r = check_qkv(g, x, q, k, v, o);
+  if (r != NSRL_OK) return r;
+  cudaStream_t s = (cudaStream_t)stream;
+  if ((r = qkv_body(g, x, rms_gamma, rms_eps, q, k, v, o, workspace, status, s)) != NSRL_OK) return r;
+  NSRL_TRY(launch_shard_post(g, nullptr, s), "signal");
+  return NSRL_OK;
+}
+
+nsrl_status nsrl_sharded_block_attention(const nsrl_shard_group* g, const nsrl_linear_params* o, void* workspace,
+                                         size_t workspace_bytes, nsrl_device_status* status, void* stream) {
+  nsrl_status r = shard_check(g, workspace, workspace_bytes, 0, status, "nsrl_sharded_block_attention");
+  if (r != NSRL_OK) return r;
+  if (!linear_ok(o, g->L.d, g->L.d)) return shape_fail("o must be a d_model x d_model linear");
+  cudaStream_t s = (cudaStream_t)stream;
+  NSRL_TRY(launch_shard_wait(g, false, status, s), "wait");
+  if ((r = attention_body(g, o, workspace, status, s)) != NSRL_OK) return r;
+  NSRL_TRY(launch_shard_post(g, nullptr, s), "signal");
+  return NSRL_OK;
+}
+
+nsrl_status nsrl_sharded_block_output(const nsrl_shard_group* g, const int16_t* x, const nsrl_linear_params* o,
+                                      const int16_t* mlp_gamma, uint64_t rms_eps, const nsrl_linear_params* up_p,
+                                      const nsrl_linear_params* gate, const nsrl_linear_params* down,
+                                      size_t hidden_dim, int16_t* y, void* workspace, size_t workspace_bytes,
+                                      nsrl_device_status* status, void* stream) {
+  nsrl_status r = shard_check(g, workspace, workspace_bytes, up_p ? hidden_dim : 0, status,
+                              "nsrl_sharded_block_output");
+  if (r == NSRL_OK) r = check_output(g, x, o, up_p, gate, down, hidden_dim, y);
+  if (r != NSRL_OK) return r;
+  cudaStream_t s = (cudaStream_t)stream;
+  NSRL_TRY(launch_shard_wait(g, false, status, s), "wait");
+  return output_body(g, x, o, mlp_gamma, rms_eps, up_p, gate, down, hidden_dim, y, workspace, status, s);
+}
+
 nsrl_status nsrl_sharded_transformer_block(const nsrl_shard_group* g, const int16_t* x, const int16_t* attn_gamma,
                                            const int16_t* mlp_gamma, uint64_t rms_eps, const nsrl_linear_params* q,
                                            const nsrl_linear_params* k, const nsrl_linear_params* v,
@@ -1311,15 +1355,15 @@ nsrl_status nsrl_sharded_transformer_block(const nsrl_shard_group* g, const int1
                                            nsrl_device_status* status, void* stream) {
   nsrl_status r = shard_check(g, workspace, workspace_bytes, up_p ? hidden_dim : 0, status,
                               "nsrl_sharded_transformer_block");
+  if (r == NSRL_OK) r = check_qkv(g, x, q, k, v, o);
+  if (r == NSRL_OK) r = check_output(g, x, o, up_p, gate, down, hidden_dim, y);
   if (r != NSRL_OK) return r;
-  if (up_p && (r = validate_mlp(g->L.S, g->L.d, hidden_dim, up_p, gate, down)) != NSRL_OK) return r;
-  if (!x || !y || x == y) return shape_fail("x / y is NULL or they alias");
-  r = nsrl_sharded_block_qkv(g, x, attn_gamma, rms_eps, q, k, v, o, workspace, workspace_bytes, status, stream);
-  if (r == NSRL_OK) r = nsrl_sharded_block_attention(g, o, workspace, workspace_bytes, status, stream);
-  if (r == NSRL_OK)
-    r = nsrl_sharded_block_output(g, x, o, mlp_gamma, rms_eps, up_p, gate, down, hidden_dim, y, workspace,
-                                  workspace_bytes, status, stream);
-  return r;
+  cudaStream_t s = (cudaStream_t)stream;
+  if ((r = qkv_body(g, x, attn_gamma, rms_eps, q, k, v, o, workspace, status, s)) != NSRL_OK) return r;
+  NSRL_TRY(launch_shard_barrier(g, nullptr, false, status, s), "barrier");
+  if ((r = attention_body(g, o, workspace, status, s)) != NSRL_OK) return r;
+  NSRL_TRY(launch_shard_barrier(g, nullptr, false, status, s), "barrier");
+  return output_body(g, x, o, mlp_gamma, rms_eps, up_p, gate, down, hidden_dim, y, workspace, status, s);
 }
 
 }  // extern "C"

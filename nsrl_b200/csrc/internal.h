@@ -259,10 +259,16 @@ bool tma_supported();
 // Byte offsets of one exchange buffer of a head-sharded forward (the same on
 // every rank): a 4 KiB header (signal words, the epoch counter, posted status
 // slots), then the q|k planes, the transposed v planes, and the context planes
-// with their row L1, each 256-byte aligned.
+// with their row L1, each 256-byte aligned.  When every rank's positions make
+// 16-byte runs (S / n a multiple of 16), n staging slots follow, each with the
+// q|k and v regions of one destination rank at the same relative offsets: the
+// Q|K|V projection writes the parts of other ranks there, and one copy kernel
+// pushes them over NVLink in long contiguous runs.
 struct ShardLayout {
   size_t B = 0, S = 0, d = 0, H = 0, n = 0, s_loc = 0, d_loc = 0, h_loc = 0;
-  size_t qk_hi = 0, qk_lo = 0, vt_hi = 0, vt_lo = 0, ctx_hi = 0, ctx_lo = 0, ctx_l1 = 0, total = 0;
+  size_t qk_hi = 0, qk_lo = 0, vt_hi = 0, vt_lo = 0, ctx_hi = 0, ctx_lo = 0, ctx_l1 = 0;
+  size_t stage = 0, stage_stride = 0;  // slot p's q|k hi plane at stage + p * stage_stride (0: no staging)
+  size_t total = 0;
 };
 constexpr size_t kShardSignalOff = 0;    // u64 [kMaxShardRanks]
 constexpr size_t kShardEpochOff = 64;    // u64: this rank's signals so far
@@ -276,6 +282,14 @@ cudaError_t launch_shard_post(const nsrl_shard_group* g, const nsrl_device_statu
 // Wait (bounded) until every rank has signalled this rank's current epoch;
 // with combine, add the status words the ranks posted into *st.
 cudaError_t launch_shard_wait(const nsrl_shard_group* g, bool combine, nsrl_device_status* st, cudaStream_t s);
+// Signal and wait in one launch (ranks in separate processes only); with post,
+// the status words go out with the signal, and with combine the other ranks'
+// posted words are added into *st.
+cudaError_t launch_shard_barrier(const nsrl_shard_group* g, const nsrl_device_status* post, bool combine,
+                                 nsrl_device_status* st, cudaStream_t s);
+// Copies this rank's staged q|k and v rows of every other rank into that
+// rank's exchange buffer (no-op without staging).
+cudaError_t launch_shard_push(const nsrl_shard_group* g, cudaStream_t s);
 
 }  // namespace nsrl
 
@@ -287,5 +301,6 @@ struct nsrl_shard_group {
   nsrl::ShardLayout L;
   unsigned long long timeout_ns = 0;
   uint8_t* base[nsrl::kMaxShardRanks] = {};
-  nsrl::ShardTable* tab = nullptr;  // device memory
+  nsrl::ShardTable* tab = nullptr;    // device memory: every rank's regions
+  nsrl::ShardTable* stab = nullptr;   // device memory: the same, other ranks' q|k, v in the staging slots (or null)
 };

@@ -13,6 +13,7 @@
 // Every wait is bounded by the group's timeout; when it runs out the waiter
 // sets NSRL_FLAG_WAIT_TIMEOUT and returns, so a rank that never signals
 // ends the call with an error instead of a hung GPU.
+#include <algorithm>
 #include <cstring>
 
 #include "common.cuh"
@@ -41,30 +42,6 @@ struct PostArgs {
   const nsrl_device_status* post;  // optional: status words to post
 };
 
-// One warp.  Thread t < n posts (optionally) the status words into rank t's
-// slot of this rank and then signals rank t.  The kernel boundary orders the
-// stores of the kernels before it; the system-scope fence makes them visible
-// to the other GPUs before the release store of the signal.
-__global__ void shard_post_kernel(const PostArgs a) {
-  __shared__ unsigned long long e;
-  if (threadIdx.x == 0) {
-    e = *a.epoch + 1;
-    *a.epoch = e;
-  }
-  __syncwarp();
-  const int t = threadIdx.x;
-  if (t < a.nranks) {
-    if (a.post) {
-      unsigned long long* slot = a.tab->slots[t] + 4 * a.rank;
-      slot[0] = a.post->flags;
-      slot[1] = a.post->attention_saturations;
-      slot[2] = a.post->mlp_saturations;
-    }
-    __threadfence_system();
-    st_release_sys(a.tab->signal[t] + a.rank, e);
-  }
-}
-
 struct WaitArgs {
   const ShardTable* tab;
   const unsigned long long* epoch;
@@ -73,43 +50,123 @@ struct WaitArgs {
   nsrl_device_status* st;
 };
 
-__global__ void shard_wait_kernel(const WaitArgs a) {
-  __shared__ unsigned long long got[kMaxShardRanks][3];
-  __shared__ int ok[kMaxShardRanks];
-  const int t = threadIdx.x;
-  if (t < a.nranks) {
-    const unsigned long long e = *a.epoch;
-    const unsigned long long* sig = a.tab->signal[a.rank] + t;
-    bool done = ld_acquire_sys(sig) >= e;
-    if (!done) {
-      const unsigned long long t0 = global_ns();
-      while (!done) {
-        __nanosleep(200);
-        done = ld_acquire_sys(sig) >= e;
-        if (!done && global_ns() - t0 > a.limit_ns) break;
-      }
-    }
-    ok[t] = done ? 1 : 0;
-    if (!done) nsrl_flag(a.st, NSRL_FLAG_WAIT_TIMEOUT);
-    if (done && a.combine && t != a.rank) {
-      const unsigned long long* slot = a.tab->slots[a.rank] + 4 * t;
-      got[t][0] = slot[0];
-      got[t][1] = slot[1];
-      got[t][2] = slot[2];
+// Thread t < n of one warp: post (optionally) the status words into this
+// rank's slot of rank t, then signal rank t with epoch e.  The kernel boundary
+// orders the stores of the kernels before it; the system-scope fence makes
+// them visible to the other GPUs before the release store of the signal.
+__device__ __forceinline__ void post_one(const PostArgs& a, int t, unsigned long long e) {
+  if (a.post) {
+    unsigned long long* slot = a.tab->slots[t] + 4 * a.rank;
+    slot[0] = a.post->flags;
+    slot[1] = a.post->attention_saturations;
+    slot[2] = a.post->mlp_saturations;
+  }
+  __threadfence_system();
+  st_release_sys(a.tab->signal[t] + a.rank, e);
+}
+
+// Thread t < n: wait (bounded) for rank t's signal of epoch e; with combine,
+// fetch the status words rank t posted.  Returns whether the signal came.
+__device__ __forceinline__ bool wait_one(const WaitArgs& a, int t, unsigned long long e,
+                                         unsigned long long (&got)[kMaxShardRanks][3]) {
+  const unsigned long long* sig = a.tab->signal[a.rank] + t;
+  bool done = ld_acquire_sys(sig) >= e;
+  if (!done) {
+    const unsigned long long t0 = global_ns();
+    while (!done) {
+      __nanosleep(100);
+      done = ld_acquire_sys(sig) >= e;
+      if (!done && global_ns() - t0 > a.limit_ns) break;
     }
   }
+  if (!done) nsrl_flag(a.st, NSRL_FLAG_WAIT_TIMEOUT);
+  if (done && a.combine && t != a.rank) {
+    const unsigned long long* slot = a.tab->slots[a.rank] + 4 * t;
+    got[t][0] = slot[0];
+    got[t][1] = slot[1];
+    got[t][2] = slot[2];
+  }
+  return done;
+}
+
+// Adds the other ranks' posted status words into this rank's status (thread 0).
+__device__ __forceinline__ void combine(const WaitArgs& a, const int (&ok)[kMaxShardRanks],
+                                        const unsigned long long (&got)[kMaxShardRanks][3]) {
+  unsigned long long f = 0, as = 0, ms = 0;
+  for (int p = 0; p < a.nranks; ++p) {
+    if (p == a.rank || !ok[p]) continue;
+    f |= got[p][0];
+    as += got[p][1];
+    ms += got[p][2];
+  }
+  if (f) nsrl_flag(a.st, f);
+  if (as) atomicAdd(&a.st->attention_saturations, as);
+  if (ms) atomicAdd(&a.st->mlp_saturations, ms);
+}
+
+// mode 1: post; mode 2: wait (the epoch of this rank's last post); mode 3:
+// post, then wait -- the form for ranks in separate processes.
+__global__ void shard_sync_kernel(const PostArgs pa, const WaitArgs wa, int mode) {
+  __shared__ unsigned long long e;
+  __shared__ unsigned long long got[kMaxShardRanks][3];
+  __shared__ int ok[kMaxShardRanks];
+  if (threadIdx.x == 0) {
+    e = *pa.epoch + ((mode & 1) ? 1 : 0);
+    if (mode & 1) *pa.epoch = e;
+  }
   __syncwarp();
-  if (t == 0 && a.combine) {
-    unsigned long long f = 0, as = 0, ms = 0;
-    for (int p = 0; p < a.nranks; ++p) {
-      if (p == a.rank || !ok[p]) continue;
-      f |= got[p][0];
-      as += got[p][1];
-      ms += got[p][2];
+  const int t = threadIdx.x;
+  if (t < pa.nranks) {
+    if (mode & 1) post_one(pa, t, e);
+    if (mode & 2) ok[t] = wait_one(wa, t, e, got) ? 1 : 0;
+  }
+  __syncwarp();
+  if (t == 0 && (mode & 2) && wa.combine) combine(wa, ok, got);
+}
+
+struct PushArgs {
+  const ShardTable* tab;   // destinations: every rank's exchange regions
+  const uint8_t* own;      // this rank's exchange buffer (its staging slots)
+  size_t stage, stride;    // slot p at own + stage + p * stride
+  size_t slot_qk_lo, slot_vt_hi, slot_vt_lo;  // regions within a slot (q|k hi at 0)
+  long long S, s_loc, d_loc, B;
+  int nranks, rank;
+  long long qk_chunks, vt_chunks, per_peer;  // 16-byte chunks of one plane of q|k and of v, and per peer
+};
+
+// Grid-stride copy in 16-byte chunks: for each other rank p, its q|k rows of
+// this rank's positions (one run of s_loc * 2 d_loc bytes per sequence) and
+// its v rows (one run of s_loc bytes per (sequence, column)), hi and lo
+// planes, from the staging slot to the same offsets of p's regions.
+__global__ void shard_push_kernel(const PushArgs a) {
+  const long long total = (long long)(a.nranks - 1) * a.per_peer;
+  const long long qk_run = a.s_loc * 2 * a.d_loc / 16;
+  const long long vt_run = a.s_loc / 16;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int q = (int)(i / a.per_peer);
+    const int p = q < a.rank ? q : q + 1;
+    long long j = i - (long long)q * a.per_peer;
+    const uint8_t* slot = a.own + a.stage + (size_t)p * a.stride;
+    const uint8_t* src;
+    uint8_t* dst;
+    if (j < 2 * a.qk_chunks) {
+      const int plane = (int)(j / a.qk_chunks);
+      const long long k = j - plane * a.qk_chunks;
+      const long long b = k / qk_run, c = k - b * qk_run;
+      const long long off = (b * a.S + a.rank * a.s_loc) * 2 * a.d_loc + c * 16;
+      src = slot + (plane ? a.slot_qk_lo : 0) + off;
+      dst = (plane ? a.tab->qk_lo[p] : reinterpret_cast<uint8_t*>(a.tab->qk_hi[p])) + off;
+    } else {
+      j -= 2 * a.qk_chunks;
+      const int plane = (int)(j / a.vt_chunks);
+      const long long k = j - plane * a.vt_chunks;
+      const long long row = k / vt_run, c = k - row * vt_run;
+      const long long off = row * a.S + a.rank * a.s_loc + c * 16;
+      src = slot + (plane ? a.slot_vt_lo : a.slot_vt_hi) + off;
+      dst = (plane ? a.tab->vt_lo[p] : reinterpret_cast<uint8_t*>(a.tab->vt_hi[p])) + off;
     }
-    if (f) nsrl_flag(a.st, f);
-    if (as) atomicAdd(&a.st->attention_saturations, as);
-    if (ms) atomicAdd(&a.st->mlp_saturations, ms);
+    *reinterpret_cast<uint4*>(dst) = __ldg(reinterpret_cast<const uint4*>(src));
   }
 }
 
@@ -140,34 +197,77 @@ bool shard_layout(size_t B, size_t S, size_t d, size_t H, size_t n, ShardLayout*
   l.ctx_hi = take(B * l.s_loc * d);
   l.ctx_lo = take(B * l.s_loc * d);
   l.ctx_l1 = take(B * l.s_loc * sizeof(unsigned long long));
+  if (n > 1 && l.s_loc % 16 == 0) {  // staging slots: q|k hi, lo, v hi, lo of one destination each
+    l.stage = off;
+    const size_t slot = al256(B * S * 2 * l.d_loc) * 2 + al256(B * l.d_loc * S) * 2;
+    l.stage_stride = slot;
+    off += n * slot;
+  }
   l.total = off;
   *L = l;
   return true;
 }
 
-cudaError_t launch_shard_post(const nsrl_shard_group* g, const nsrl_device_status* post_status, cudaStream_t s) {
-  PostArgs a;
-  a.tab = g->tab;
-  a.epoch = reinterpret_cast<unsigned long long*>(g->base[g->rank] + kShardEpochOff);
-  a.nranks = g->nranks;
-  a.rank = g->rank;
-  a.post = post_status;
-  ProfScope prof("shard_post", s, 0.0, 0.0);
-  shard_post_kernel<<<1, 32, 0, s>>>(a);
+namespace {
+cudaError_t launch_sync(const nsrl_shard_group* g, int mode, const nsrl_device_status* post, bool combine,
+                        nsrl_device_status* st, cudaStream_t s, const char* name) {
+  PostArgs pa;
+  pa.tab = g->tab;
+  pa.epoch = reinterpret_cast<unsigned long long*>(g->base[g->rank] + kShardEpochOff);
+  pa.nranks = g->nranks;
+  pa.rank = g->rank;
+  pa.post = post;
+  WaitArgs wa;
+  wa.tab = g->tab;
+  wa.epoch = pa.epoch;
+  wa.nranks = g->nranks;
+  wa.rank = g->rank;
+  wa.combine = combine ? 1 : 0;
+  wa.limit_ns = g->timeout_ns;
+  wa.st = st;
+  ProfScope prof(name, s, 0.0, 0.0);
+  shard_sync_kernel<<<1, 32, 0, s>>>(pa, wa, mode);
   return cudaGetLastError();
+}
+}  // namespace
+
+cudaError_t launch_shard_post(const nsrl_shard_group* g, const nsrl_device_status* post_status, cudaStream_t s) {
+  return launch_sync(g, 1, post_status, false, nullptr, s, "shard_post");
 }
 
 cudaError_t launch_shard_wait(const nsrl_shard_group* g, bool combine, nsrl_device_status* st, cudaStream_t s) {
-  WaitArgs a;
+  return launch_sync(g, 2, nullptr, combine, st, s, "shard_wait");
+}
+
+cudaError_t launch_shard_barrier(const nsrl_shard_group* g, const nsrl_device_status* post, bool combine,
+                                 nsrl_device_status* st, cudaStream_t s) {
+  return launch_sync(g, 3, post, combine, st, s, "shard_barrier");
+}
+
+cudaError_t launch_shard_push(const nsrl_shard_group* g, cudaStream_t s) {
+  const ShardLayout& L = g->L;
+  if (!g->stab || g->nranks < 2) return cudaSuccess;
+  PushArgs a;
   a.tab = g->tab;
-  a.epoch = reinterpret_cast<const unsigned long long*>(g->base[g->rank] + kShardEpochOff);
+  a.own = g->base[g->rank];
+  a.stage = L.stage;
+  a.stride = L.stage_stride;
+  a.slot_qk_lo = al256(L.B * L.S * 2 * L.d_loc);
+  a.slot_vt_hi = 2 * a.slot_qk_lo;
+  a.slot_vt_lo = a.slot_vt_hi + al256(L.B * L.d_loc * L.S);
+  a.S = (long long)L.S;
+  a.s_loc = (long long)L.s_loc;
+  a.d_loc = (long long)L.d_loc;
+  a.B = (long long)L.B;
   a.nranks = g->nranks;
   a.rank = g->rank;
-  a.combine = combine ? 1 : 0;
-  a.limit_ns = g->timeout_ns;
-  a.st = st;
-  ProfScope prof("shard_wait", s, 0.0, 0.0);
-  shard_wait_kernel<<<1, 32, 0, s>>>(a);
+  a.qk_chunks = a.B * a.s_loc * 2 * a.d_loc / 16;
+  a.vt_chunks = a.B * a.d_loc * a.s_loc / 16;
+  a.per_peer = 2 * a.qk_chunks + 2 * a.vt_chunks;
+  const long long total = (long long)(g->nranks - 1) * a.per_peer;
+  const unsigned blocks = (unsigned)std::min<long long>((total + 255) / 256, 148 * 8);
+  ProfScope prof("shard_push", s, 0.0, 2.0 * 16.0 * (double)total);
+  shard_push_kernel<<<blocks, 256, 0, s>>>(a);
   return cudaGetLastError();
 }
 
@@ -297,10 +397,27 @@ nsrl_status nsrl_shard_group_create(nsrl_shard_group** group, int nranks, int ra
   }
   cudaError_t e = cudaMalloc(&g->tab, sizeof(ShardTable));
   if (e == cudaSuccess) e = cudaMemcpy(g->tab, &t, sizeof(t), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess && L.stage) {
+    // the projection's view: other ranks' q|k and v in this rank's staging slots
+    ShardTable st = t;
+    uint8_t* own = g->base[rank];
+    const size_t qk = al256(L.B * L.S * 2 * L.d_loc), vt = al256(L.B * L.d_loc * L.S);
+    for (int r = 0; r < nranks; ++r) {
+      if (r == rank) continue;
+      uint8_t* slot = own + L.stage + (size_t)r * L.stage_stride;
+      st.qk_hi[r] = reinterpret_cast<int8_t*>(slot);
+      st.qk_lo[r] = slot + qk;
+      st.vt_hi[r] = reinterpret_cast<int8_t*>(slot + 2 * qk);
+      st.vt_lo[r] = slot + 2 * qk + vt;
+    }
+    e = cudaMalloc(&g->stab, sizeof(ShardTable));
+    if (e == cudaSuccess) e = cudaMemcpy(g->stab, &st, sizeof(st), cudaMemcpyHostToDevice);
+  }
   if (e == cudaSuccess) e = cudaMemset(g->base[rank], 0, kShardHeaderBytes);
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) {
     if (g->tab) cudaFree(g->tab);
+    if (g->stab) cudaFree(g->stab);
     delete g;
     return shard_cuda_fail(e, "shard group");
   }
@@ -312,6 +429,7 @@ nsrl_status nsrl_shard_group_destroy(nsrl_shard_group* group) {
   if (!group) return NSRL_OK;
   cudaError_t e = cudaSuccess;
   if (group->tab) e = cudaFree(group->tab);
+  if (group->stab && e == cudaSuccess) e = cudaFree(group->stab);
   delete group;
   return e == cudaSuccess ? NSRL_OK : shard_cuda_fail(e, "shard group free");
 }
@@ -323,6 +441,15 @@ nsrl_status nsrl_shard_status_post(const nsrl_shard_group* group, const nsrl_dev
   }
   const cudaError_t e = launch_shard_post(group, status, (cudaStream_t)stream);
   return e == cudaSuccess ? NSRL_OK : shard_cuda_fail(e, "status post");
+}
+
+nsrl_status nsrl_shard_status_allreduce(const nsrl_shard_group* group, nsrl_device_status* status, void* stream) {
+  if (!group || !status) {
+    set_error("nsrl_shard_status_allreduce: NULL argument");
+    return NSRL_INVALID_SHAPE;
+  }
+  const cudaError_t e = launch_shard_barrier(group, status, true, status, (cudaStream_t)stream);
+  return e == cudaSuccess ? NSRL_OK : shard_cuda_fail(e, "status all-reduce");
 }
 
 nsrl_status nsrl_shard_status_combine(const nsrl_shard_group* group, nsrl_device_status* status, void* stream) {

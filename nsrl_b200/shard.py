@@ -84,6 +84,7 @@ def _bind():
                                                  vp, sz, vp, vp]
     L.nsrl_shard_status_post.argtypes = [vp, vp, vp]
     L.nsrl_shard_status_combine.argtypes = [vp, vp, vp]
+    L.nsrl_shard_status_allreduce.argtypes = [vp, vp, vp]
     L._shard_bound = True
     return L
 
@@ -174,6 +175,11 @@ class _Rank:
         return _bind().nsrl_shard_status_post(C.c_void_p(self.g), core._ptr(status.buf),
                                               stream if stream is not None else core._stream())
 
+    def allreduce_status(self, status: core.Status, stream=None) -> int:
+        """post_status and combine_status in one launch (ranks in separate processes)."""
+        return _bind().nsrl_shard_status_allreduce(C.c_void_p(self.g), core._ptr(status.buf),
+                                                   stream if stream is not None else core._stream())
+
     def combine_status(self, status: core.Status, stream=None) -> int:
         return _bind().nsrl_shard_status_combine(C.c_void_p(self.g), core._ptr(status.buf),
                                                  stream if stream is not None else core._stream())
@@ -254,8 +260,7 @@ class ShardGroup(_Rank):
         if r == core.NSRL_INVALID_SHAPE:
             return None
         core._check(r)
-        core._check(self.post_status(st))
-        core._check(self.combine_status(st))
+        core._check(self.allreduce_status(st))
         h = _result(st)
         return None if h is None else (y, h.attention_saturations, h.mlp_saturations)
 

@@ -38,6 +38,7 @@ def _block(core, d, F, seed, qk_extra=7):
     (3, 1, 48, 192, 256, True),     # d_model not a multiple of 128: SIMT Q|K|V projection
     (4, 1, 128, 1024, 512, True),   # d_model > 516: the exact prefix check reads the summed context L1
     (8, 1, 256, 512, 512, True),    # eight ranks, one head each
+    (2, 2, 48, 128, 256, True),     # 24 positions per rank: peer stores from the epilogue, no staging
 ])
 def test_sharded_block_matches_one_gpu_and_oracle(mods, n, B, S, d, F, mlp):
     core, shard = mods

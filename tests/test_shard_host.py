@@ -32,6 +32,8 @@ def _layout_bytes(B, S, d, H, n):
     off = 4096
     for size in (B * S * 2 * dl, B * S * 2 * dl, B * dl * S, B * dl * S, B * sl * d, B * sl * d, 8 * B * sl):
         off = _al(off + size)
+    if n > 1 and sl % 16 == 0:  # one staging slot per destination rank: q|k hi, lo and v hi, lo
+        off += n * (2 * _al(B * S * 2 * dl) + 2 * _al(B * dl * S))
     return off
 
 
