@@ -10,7 +10,7 @@
 // other.  The warps of a group:
 //   warp 0     TMA producer: Q planes once, then per 32-key tile the K planes
 //              (max and sum passes) or the transposed V planes (last pass)
-//   warp 1     TMEM allocator + single-thread MMA issuer
+//   warp 1     TMEM allocator + MMA issuer (the whole warp runs the loop, one elected lane issues)
 //   warps 2..9 softmax: warp w owns query rows 32*(w%4) .. +31 (its TMEM lane
 //              quarter) and keys [16*g, 16*g+16) of each 32-key tile,
 //              g = (w-2)/4
@@ -361,7 +361,9 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
     }
   } else if (warp == 1) {
     // ----------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+    // The whole warp runs the loop (warp-uniform operands); one elected lane
+    // issues each MMA and commit, lane 0 the P stores.
+    {
       const uint32_t id_ss = idesc_i8(QT, KT, 1, 1), id_su = idesc_i8(QT, KT, 1, 0);
       const uint32_t id_us = idesc_i8(QT, KT, 0, 1), id_uu = idesc_i8(QT, KT, 0, 0);
       const uint32_t pv_us = idesc_i8(QT, HD, 0, 1), pv_uu = idesc_i8(QT, HD, 0, 0);
@@ -384,13 +386,13 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
             const uint64_t aqh = sdesc_k64(qh + 32 * ks), aql = sdesc_k64(ql + 32 * ks);
             const uint64_t bkh = sdesc_k64(kh + 32 * ks), bkl = sdesc_k64(kl + 32 * ks);
             const uint32_t acc = ks > 0 ? 1u : 0u;
-            umma_i8(d + S_HH, aqh, bkh, id_ss, acc);
-            umma_i8(d + S_MID, aqh, bkl, id_su, acc);
-            umma_i8(d + S_MID, aql, bkh, id_us, 1u);
-            umma_i8(d + S_LL, aql, bkl, id_uu, acc);
+            umma_i8_warp(d + S_HH, aqh, bkh, id_ss, acc);
+            umma_i8_warp(d + S_MID, aqh, bkl, id_su, acc);
+            umma_i8_warp(d + S_MID, aql, bkh, id_us, 1u);
+            umma_i8_warp(d + S_LL, aql, bkl, id_uu, acc);
           }
-          umma_commit(&ctl->s_full[sb]);
-          umma_commit(&ctl->empty[s]);
+          umma_commit_warp(&ctl->s_full[sb]);
+          umma_commit_warp(&ctl->empty[s]);
           if (sb)
             ++use1;
           else
@@ -405,7 +407,7 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
         const int pb = j & 1;
         wait_bar(&ctl->p_full[pb], (j >> 1) & 1, ctl, a.st);
         tc_fence_after();
-        if (a.pstore) {  // the cached P of rows q0.. (keys j*32 ..): straight from the MMA's P tile
+        if (a.pstore && lane == 0) {  // the cached P of rows q0.. (keys j*32 ..): straight from the MMA's P tile
           const uint8_t* pt = sm + OFF_P + pb * 2 * PLANE_P;
           tma_store_3d(&maps.p_hi, pt, j * KT, q0, pz);
           tma_store_3d(&maps.p_lo, pt + PLANE_P, j * KT, q0, pz);
@@ -416,19 +418,19 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
         const uint64_t aph = sdesc_k32(ph), apl = sdesc_k32(pl);
         const uint64_t bvh = sdesc_k32(vh), bvl = sdesc_k32(vl);
         const uint32_t acc = j > 0 ? 1u : 0u;
-        umma_i8(tmem + O_HH, aph, bvh, pv_us, acc);
-        umma_i8(tmem + O_MID, aph, bvl, pv_uu, acc);
-        umma_i8(tmem + O_MID, apl, bvh, pv_us, 1u);
-        umma_i8(tmem + O_LL, apl, bvl, pv_uu, acc);
-        umma_commit(&ctl->p_empty[pb]);
-        umma_commit(&ctl->empty[s]);
-        if (a.pstore && j > 0) {  // the previous tile's store has read its P buffer
+        umma_i8_warp(tmem + O_HH, aph, bvh, pv_us, acc);
+        umma_i8_warp(tmem + O_MID, aph, bvl, pv_uu, acc);
+        umma_i8_warp(tmem + O_MID, apl, bvh, pv_us, 1u);
+        umma_i8_warp(tmem + O_LL, apl, bvl, pv_uu, acc);
+        umma_commit_warp(&ctl->p_empty[pb]);
+        umma_commit_warp(&ctl->empty[s]);
+        if (a.pstore && j > 0 && lane == 0) {  // the previous tile's store has read its P buffer
           bulk_wait_read<1>();
           mbar_arrive(&ctl->p_empty[pb ^ 1]);
         }
       }
-      umma_commit(&ctl->o_full);
-      if (a.pstore) bulk_wait_all();  // the P stores are complete before the CTA (and its shared memory) ends
+      umma_commit_warp(&ctl->o_full);
+      if (a.pstore && lane == 0) bulk_wait_all();  // the P stores are complete before the CTA (and its shared memory) ends
       // every MMA of this CTA completes before TMEM is released
       mbar_wait(&ctl->o_full, 0, a.st);
     }
