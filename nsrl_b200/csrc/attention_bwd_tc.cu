@@ -201,7 +201,7 @@ __global__ void __launch_bounds__(KTHREADS, 1) attn_kv_tc_kernel(const __grid_co
       for (uint32_t j = (it > KST ? it - KST : 0); j < it; ++j) mbar_wait(&full[j % KST], (j / KST) & 1, a.st);
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    {  // the whole warp runs the loop (warp-uniform operands), one elected lane issues
       // dK: dL (s8 hi / u8 lo) x Q (s8 / u8); dV: P (hi <= 127, as u8) x dC (s8 / u8);
       // dQ: dL x K (s8 / u8), A K-major
       const uint32_t id_ss = idesc_mn(1, 1), id_su = idesc_mn(1, 0), id_us = idesc_mn(0, 1), id_uu = idesc_mn(0, 0);
@@ -236,14 +236,14 @@ __global__ void __launch_bounds__(KTHREADS, 1) attn_kv_tc_kernel(const __grid_co
             const uint64_t bhd = sdesc_mn(base + OFF_BH + 2048 * j, 512, LAYOUT_SW64);
             const uint64_t bld = sdesc_mn(base + OFF_BL + 2048 * j, 512, LAYOUT_SW64);
             const uint32_t acc = (x > w.x0 || j > 0) ? 1u : 0u;
-            umma_i8(d, ah, bhd, i_hh, acc);            // hh
-            umma_i8(d + 64, ah, bld, i_hl, acc);       // mid: hi x lo
-            umma_i8(d + 64, al, bhd, i_lh, 1u);        //      lo x hi
-            umma_i8(d + 128, al, bld, i_ll, acc);      // ll
+            umma_i8_warp(d, ah, bhd, i_hh, acc);            // hh
+            umma_i8_warp(d + 64, ah, bld, i_hl, acc);       // mid: hi x lo
+            umma_i8_warp(d + 64, al, bhd, i_lh, 1u);        //      lo x hi
+            umma_i8_warp(d + 128, al, bld, i_ll, acc);      // ll
           }
-          umma_commit(&empty[s]);
+          umma_commit_warp(&empty[s]);
         }
-        umma_commit(&acc_full[buf]);
+        umma_commit_warp(&acc_full[buf]);
       }
     }
   } else {

@@ -72,7 +72,8 @@ constexpr size_t SMEM_BYTES = (size_t)GROUPS * GROUP_BYTES + 1024;
 struct Maps {
   CUtensorMap q_hi, q_lo, k_hi, k_lo, vt_hi, vt_lo;  // q: 128-row boxes, k: 32-row boxes, vt: 64 x 32-byte boxes
   CUtensorMap p_hi, p_lo;  // P planes [B*H][S][S], 128 x 32-byte boxes (stores of the cached P)
-  CUtensorMap w;           // weight scratch as bytes [rows][2 wstride], 128 x 64-byte boxes (sum-pass stores)
+  CUtensorMap w;           // weight scratch as bytes [rows][2 wstride], 128 x 64-byte boxes (last-pass loads)
+  CUtensorMap ws;          // the same, 32 x 32-byte boxes: one softmax warp's weights of a tile (sum-pass stores)
 };
 
 struct Args {
@@ -300,7 +301,7 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
       mbar_init(&ctl->p_empty[i], a.pstore ? 2 : 1);
     }
     mbar_init(&ctl->o_full, 1);
-    mbar_init(&ctl->w_ready, 1);
+    mbar_init(&ctl->w_ready, SOFTMAX_WARPS);
     for (int i = 0; i < WPF_N; ++i) {
       mbar_init(&ctl->w_full[i], 1);
       mbar_init(&ctl->w_empty[i], SOFTMAX_WARPS);
@@ -563,37 +564,39 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
     };
 
     // ---- pass 1: weights and the row sum ----
-    // Each 128 x 32 tile of weights goes through shared memory (three 8 KB
-    // buffers in the last pass's prefetch region, [row][64 bytes] with the
-    // 64-byte swizzle) and out with one TMA store, instead of 32 row-strided
-    // 16-byte stores per warp.  A buffer is rewritten three tiles later: the
-    // storing thread waits for all but its newest store to have read shared
-    // memory before it reaches the next tile's barrier, which the writers of
-    // that buffer pass only afterwards.
-    uint8_t* wst = sm + OFF_WPF;
-    const uint32_t wsw = ((uint32_t)row >> 1) & 3u;
+    // Each warp's 32 rows x 16 weights of a tile go through its own 1 KB of
+    // shared memory (32-byte rows, 32-byte swizzle: conflict-free 16-byte
+    // stores) and out with one TMA store of that box, so the warps never wait
+    // on one another.  Three slots per warp, in the last pass's prefetch
+    // region: before slot j % 3 is rewritten, lane 0 waits until all but its
+    // two newest stores have read shared memory.
+    uint8_t* wst = sm + OFF_WPF + (q * 2 + g) * 1024;
     uint32_t rsum = 0;  // this thread's keys: at most 16384 / 2 weights below 2^15
+    const uint32_t c0 = swz32_chunk((uint32_t)lane, 0u), c1 = swz32_chunk((uint32_t)lane, 1u);
     for (int j = 0; j < ntiles; ++j, ++it) {
       uint32_t hh[16], mid[16], ll[16], w[16];
       fetch_s((int)(it & 1), hh, mid, ll);
       weights(hh, mid, ll, live_keys(j), w);
       rsum += sum16(w);
       uint8_t* tb = wst + (j % 3) * (QT * 64);
-      *reinterpret_cast<uint4*>(tb + row * 64 + (((2u * g) ^ wsw) << 4)) =
+      if (j >= 3) {
+        if (lane == 0) bulk_wait_read<2>();
+        __syncwarp();
+      }
+      *reinterpret_cast<uint4*>(tb + c0) =
           make_uint4(__byte_perm(w[0], w[1], 0x5410), __byte_perm(w[2], w[3], 0x5410),
                      __byte_perm(w[4], w[5], 0x5410), __byte_perm(w[6], w[7], 0x5410));
-      *reinterpret_cast<uint4*>(tb + row * 64 + (((2u * g + 1u) ^ wsw) << 4)) =
+      *reinterpret_cast<uint4*>(tb + c1) =
           make_uint4(__byte_perm(w[8], w[9], 0x5410), __byte_perm(w[10], w[11], 0x5410),
                      __byte_perm(w[12], w[13], 0x5410), __byte_perm(w[14], w[15], 0x5410));
       fence_proxy_async_smem();
-      named_sync_softmax(grp);
-      if (gtid == 64) {
-        tma_store_2d(&maps.w, tb, j * KT * 2, wy);
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(&maps.ws, tb, j * KT * 2 + 32 * g, wy + 32 * q);
         bulk_commit();
-        bulk_wait_read<1>();
       }
     }
-    if (gtid == 64) {  // the stores are complete before the producer loads the tiles back
+    if (lane == 0) {  // this warp's stores are complete before the producer loads the tiles back
       bulk_wait_all();
       fence_proxy_async_global();
       mbar_arrive(&ctl->w_ready);
@@ -609,7 +612,8 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
 
     // ---- pass 2: P = sat_i16(rhu(w * inv, 16)) as byte planes, O += P V ----
     // The weights come back as 128 x 32 tiles that the producer loads by TMA
-    // into a WPF_N-slot ring (the layout the sum pass stored them from).
+    // into a WPF_N-slot ring ([row][64 bytes], 64-byte swizzle).
+    const uint32_t wsw = ((uint32_t)row >> 1) & 3u;
     for (int j = 0; j < ntiles; ++j) {
       const int key0 = j * KT + 16 * g;
       uint32_t w[16];
@@ -813,7 +817,9 @@ cudaError_t launch_attention_tc(const Planes& qkv, const VtPlanes& vt, size_t B,
       make_map(&m.vt_hi, vt.hi, S, B * H * HD, S, KT, HD) && make_map(&m.vt_lo, vt.lo, S, B * H * HD, S, KT, HD) &&
       (!probs_planes || (make_p_map(&m.p_hi, probs_planes->hi, S, B * H) && make_p_map(&m.p_lo, probs_planes->lo, S, B * H))) &&
       make_map(&m.w, wscr, 2 * attention_tc_wstride(S), chunk_seqs(B, S, H) * H * ((S + QT - 1) / QT) * QT,
-               2 * attention_tc_wstride(S), 64, QT);
+               2 * attention_tc_wstride(S), 64, QT) &&
+      make_map(&m.ws, wscr, 2 * attention_tc_wstride(S), chunk_seqs(B, S, H) * H * ((S + QT - 1) / QT) * QT,
+               2 * attention_tc_wstride(S), 32, 32);
   if (!ok) return cudaErrorNotSupported;
   if (!probs_planes) {
     m.p_hi = m.q_hi;  // unused

@@ -18,7 +18,7 @@
 // Persistent kernel, one CTA per SM, 18 warps:
 //   warp 0      TMA producer: A hi/lo planes + W tile per 128-wide K block,
 //               through a 4-stage shared-memory ring
-//   warp 1      TMEM allocator + single-thread MMA issuer
+//   warp 1      TMEM allocator + MMA issuer (whole warp, one elected lane issues)
 //   warps 2..17 epilogue: TMEM -> registers -> requant -> global; four
 //               warps per TMEM lane quarter, 32 columns each
 // The two accumulator pairs (hi, lo) of a 128 x 128 tile take 256 TMEM
@@ -375,7 +375,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
         mbar_wait(&full[j % STAGES], (j / STAGES) & 1, p.st);
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    {  // the whole warp runs the loop (warp-uniform operands), one elected lane issues
       const uint32_t id_hi = idesc_i8(BM, BN, 1, 1);  // s8 x s8
       const uint32_t id_lo = idesc_i8(BM, BN, 0, 1);  // u8 x s8
       uint32_t it = 0, local = 0;
@@ -400,12 +400,12 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
             const uint64_t al = sdesc_k128(base + TILE_A + 32 * j);
             const uint64_t bd = sdesc_k128(base + 2 * TILE_A + 32 * j);
             const uint32_t acc = (kb > 0 || j > 0) ? 1u : 0u;
-            umma_i8(d, ah, bd, id_hi, acc);
-            umma_i8(d + BN, al, bd, id_lo, acc);
+            umma_i8_warp(d, ah, bd, id_hi, acc);
+            umma_i8_warp(d + BN, al, bd, id_lo, acc);
           }
-          umma_commit(&empty[s]);
+          umma_commit_warp(&empty[s]);
         }
-        umma_commit(&acc_full[buf]);
+        umma_commit_warp(&acc_full[buf]);
       }
     }
   } else {

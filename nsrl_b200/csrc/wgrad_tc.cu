@@ -139,7 +139,7 @@ __global__ void __launch_bounds__(WTHREADS, 1) wgrad_tc_kernel(const __grid_cons
         mbar_wait(&full[j % WSTAGES], (j / WSTAGES) & 1, p.st);
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    {  // the whole warp runs the loop (warp-uniform operands), one elected lane issues
       const uint32_t id_ss = idesc_i8_mn(WB, WB, 1, 1);
       const uint32_t id_su = idesc_i8_mn(WB, WB, 1, 0);
       const uint32_t id_us = idesc_i8_mn(WB, WB, 0, 1);
@@ -167,14 +167,14 @@ __global__ void __launch_bounds__(WTHREADS, 1) wgrad_tc_kernel(const __grid_cons
             const uint64_t xh = sdesc_mn128(base + 2 * WTILE + 4096 * j);
             const uint64_t xl = sdesc_mn128(base + 3 * WTILE + 4096 * j);
             const uint32_t acc = (b > b0 || j > 0) ? 1u : 0u;
-            umma_i8(tmem, xh, gh, id_ss, acc);
-            umma_i8(tmem + WB, xh, gl, id_su, acc);
-            umma_i8(tmem + WB, xl, gh, id_us, 1u);
-            umma_i8(tmem + 2 * WB, xl, gl, id_uu, acc);
+            umma_i8_warp(tmem, xh, gh, id_ss, acc);
+            umma_i8_warp(tmem + WB, xh, gl, id_su, acc);
+            umma_i8_warp(tmem + WB, xl, gh, id_us, 1u);
+            umma_i8_warp(tmem + 2 * WB, xl, gl, id_uu, acc);
           }
-          umma_commit(&empty[s]);
+          umma_commit_warp(&empty[s]);
         }
-        umma_commit(acc_full);
+        umma_commit_warp(acc_full);
       }
     }
   } else {
