@@ -118,6 +118,32 @@ __device__ __forceinline__ ColScale load_scales(const nsrl_fixed_scale* sc, cons
   return c;
 }
 
+// The scale of a segment whose every column has multiplier 1, one right
+// shift and no bias (the reference's per-layer tables): no table reads.
+__device__ __forceinline__ ColScale uniform_scale(int shift) {
+  ColScale c;
+  c.mult = 1;
+  c.shift = shift;
+  c.bias = 0;
+  c.ushift = shift;
+  c.uniform = true;
+  return c;
+}
+
+// AND of v over the epilogue warps (named barrier 1, their threads only).
+__device__ __forceinline__ bool epilogue_all(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "barrier.cta.red.and.pred q, 1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "n"(32 * EPI_WARPS)
+      : "memory");
+  return r != 0;
+}
+
 // requantize_i32_to_i16 of W columns: acc = 256*hi + lo (+ bias), wrapping
 // u32 arithmetic (exact whenever the true i32 sum fits).
 // `small`: |acc| < 2^30 (K * 127 * 32767 < 2^30, no bias), so acc + 2^(s-1)
@@ -416,6 +442,24 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
     const int cg = (warp - 2) >> 2;
     uint32_t local = 0;
     unsigned long long sat = 0;
+    // Every segment's scales uniform (multiplier 1, one shift, no bias)?  Then
+    // the tiles take that shift and read no table: checked once per CTA by the
+    // epilogue warps, each column by one thread.
+    int ush0 = 0, ush1 = 0, ush2 = 0;
+    bool uni = true;
+    for (int sg = 0; sg < p.nseg; ++sg) {
+      const nsrl_fixed_scale s0 = p.scales[sg][0];
+      bool ok = p.bias[sg] == nullptr && s0.multiplier == 1;
+      for (int i = (int)threadIdx.x - 64; i < p.seg_rows && ok; i += 32 * EPI_WARPS) {
+        const nsrl_fixed_scale si = p.scales[sg][i];
+        ok = si.multiplier == 1 && si.right_shift == s0.right_shift;
+      }
+      uni = uni && ok;
+      if (sg == 0) ush0 = s0.right_shift;
+      if (sg == 1) ush1 = s0.right_shift;
+      if (sg == 2) ush2 = s0.right_shift;
+    }
+    uni = epilogue_all(uni);
     for (int t = blockIdx.x; t < p.tiles; t += gridDim.x, ++local) {
       const uint32_t buf = local & 1, use = local >> 1;
       const int m0 = (t / p.tiles_n) * BM, nt = t % p.tiles_n;
@@ -426,8 +470,10 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
       if (EPI == (int)Epi::GATED) {
         const int fb = nt * (BN / 2) + 16 * cg;
         const int nvalid = max(0, min(16, p.N - fb));
-        const ColScale su = load_scales(p.scales[0], p.bias[0], fb + (lane & 15), (lane & 15) < nvalid);
-        const ColScale sg = load_scales(p.scales[1], p.bias[1], fb + (lane & 15), (lane & 15) < nvalid);
+        const ColScale su =
+            uni ? uniform_scale(ush0) : load_scales(p.scales[0], p.bias[0], fb + (lane & 15), (lane & 15) < nvalid);
+        const ColScale sg =
+            uni ? uniform_scale(ush1) : load_scales(p.scales[1], p.bias[1], fb + (lane & 15), (lane & 15) < nvalid);
         uint32_t hu[16], lu[16], hg[16], lg[16];
         if (!mbar_wait(&acc_full[buf], use & 1, p.st)) break;
         tc_fence_after();
@@ -477,7 +523,8 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
         const int nloc = ((p.nseg == 3) ? nb % p.seg_rows : nb) + 32 * cg;
         const int n = nb + 32 * cg;
         const int nvalid = max(0, min(32, p.N - n));
-        const ColScale sc = load_scales(p.scales[sseg], p.bias[sseg], nloc + lane, lane < nvalid);
+        const ColScale sc = uni ? uniform_scale(sseg == 0 ? ush0 : sseg == 1 ? ush1 : ush2)
+                                : load_scales(p.scales[sseg], p.bias[sseg], nloc + lane, lane < nvalid);
         // The residual rows do not depend on the accumulator: fetch them first.
         uint32_t s16[16];
         const bool vec_skip = EPI == (int)Epi::RESID && ((p.ldskip | p.ldy | n) & 7) == 0 && nvalid == 32;  // both halves full
