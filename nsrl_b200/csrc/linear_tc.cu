@@ -550,18 +550,35 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
         }
         if (!mbar_wait(&acc_full[buf], use & 1, p.st)) break;
         tc_fence_after();
-        // Two halves of 16 columns keep the live registers low; the buffer is
-        // released once the second half is loaded.
+        // All 32 columns come out of TMEM at once and the buffer is released
+        // before any arithmetic, so the next tile's MMAs overlap this
+        // epilogue; the columns are then finished in two halves of 16.  The
+        // residual form, which also holds the skip rows, loads and releases
+        // half by half to keep its registers.
+        constexpr bool kOnce = EPI != (int)Epi::RESID;
+        uint32_t hq[2][16], lq[2][16];
+        if (kOnce) {
+          tmem_ld16(lrow + 32 * cg, hq[0]);
+          tmem_ld16(lrow + BN + 32 * cg, lq[0]);
+          tmem_ld16(lrow + 32 * cg + 16, hq[1]);
+          tmem_ld16(lrow + BN + 32 * cg + 16, lq[1]);
+          tmem_wait_ld();
+          tc_fence_before();
+          if (lane == 0) mbar_arrive(&acc_empty[buf]);
+        }
 #pragma unroll
         for (int hf = 0; hf < 2; ++hf) {
-          uint32_t h[16], l[16];
-          tmem_ld16(lrow + 32 * cg + 16 * hf, h);
-          tmem_ld16(lrow + BN + 32 * cg + 16 * hf, l);
-          tmem_wait_ld();
-          if (hf == 1) {
-            tc_fence_before();
-            if (lane == 0) mbar_arrive(&acc_empty[buf]);
+          if (!kOnce) {
+            tmem_ld16(lrow + 32 * cg + 16 * hf, hq[hf]);
+            tmem_ld16(lrow + BN + 32 * cg + 16 * hf, lq[hf]);
+            tmem_wait_ld();
+            if (hf == 1) {
+              tc_fence_before();
+              if (lane == 0) mbar_arrive(&acc_empty[buf]);
+            }
           }
+          const uint32_t(&h)[16] = hq[hf];
+          const uint32_t(&l)[16] = lq[hf];
           const int nv = max(0, min(16, nvalid - 16 * hf));
           const int nh = n + 16 * hf;
           int v[16];
