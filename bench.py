@@ -468,6 +468,12 @@ def run_train(core, torch, dist, world, rank, steps, warmup, flush, hbm, tfl, sr
            "kernel_table": f"{prof_steps} further step with per-launch events (the timed steps run without them)",
            "kernels": {k: {"launches": v["launches"], "ms": round(v["ms"], 3), "share": round(v["ms"] / total, 4)}
                        for k, v in sorted(rows.items(), key=lambda kv: -kv[1]["ms"])[:12]}}
+    ap = rows.get("dp_apply")
+    if ap:  # the requantising apply: algorithmic bytes (34 per arena element) per launch over its time
+        per = ap["ms"] / ap["launches"]
+        gbs = ap["bytes"] / ap["launches"] / (per / 1000.0) / 1e9
+        out["apply"] = {"ms_per_launch": round(per, 4), "algorithmic_bytes_per_launch": ap["bytes"] / ap["launches"],
+                        "achieved_gbs": round(gbs, 1), "frac_of_hbm": round(gbs / hbm, 4)}
     if world == 1:
         out["parity"] = train_parity(core, torch)
         if not out["parity"]["equal"]:

@@ -625,6 +625,13 @@ nsrl_status nsrl_prenorm_transformer_block_host(const int16_t* x_host, size_t ba
 nsrl_status nsrl_selftest_bounded_wait(unsigned long long limit_ns, nsrl_device_status* status,
                                        unsigned long long* out, void* stream);
 
+/* Runs the divider of the data-parallel apply over n numerators: out[i] =
+ * round_div(num[i], den) (the reference's rounding of an i64 gradient sum by
+ * its count, half away from zero), ok[i] = 0 where the reference's checked
+ * arithmetic fails.  Device arrays; no counterpart in the reference. */
+nsrl_status nsrl_selftest_round_div(const long long* num, size_t n, long long den, long long* out,
+                                    unsigned char* ok, void* stream);
+
 /* ------------------------------------------------- head-sharded forward --
  * The transformer block of nsrl_prenorm_transformer_block (or, without the
  * MLP, nsrl_prenorm_attention_residual_block) split over n ranks, one GPU

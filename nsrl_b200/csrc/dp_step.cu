@@ -278,6 +278,60 @@ __device__ __forceinline__ bool round_div(long long num, long long den, long lon
   return true;
 }
 
+// round_div by one divisor over many numerators: den / 2 and the correctly
+// rounded double 1 / den are computed once.  floor(u / den) for u < 2^52 and
+// den < 2^52 comes from the double product u * (1 / den): u is exact as a
+// double and the product is within a relative 2^-52 of u / den, so it is
+// within one of the quotient, and one exact integer step (r = u - q den, then
+// q - 1 for r < 0 or q + 1 for r >= den) gives it; larger values divide as
+// integers.  Same results as round_div.
+struct RoundDiv {
+  long long den, half;
+  double rd;
+};
+__device__ __forceinline__ RoundDiv round_div_by(long long den) {
+  RoundDiv d;
+  d.den = den;
+  d.half = den / 2;
+  d.rd = 1.0 / (double)den;
+  return d;
+}
+__device__ __forceinline__ long long udiv(unsigned long long u, const RoundDiv& d) {
+  if (u < (1ull << 52) && d.den < (1ll << 52)) {
+    long long q = (long long)((double)u * d.rd);
+    const long long r = (long long)u - q * d.den;
+    if (r < 0)
+      --q;
+    else if (r >= d.den)
+      ++q;
+    return q;
+  }
+  return (long long)(u / (unsigned long long)d.den);
+}
+__device__ __forceinline__ bool round_div(long long num, const RoundDiv& d, long long& out) {
+  if (num >= 0) {
+    if (num > LLONG_MAX - d.half) return false;
+    out = udiv((unsigned long long)(num + d.half), d);
+  } else {
+    if (num == LLONG_MIN) return false;
+    const long long m = -num;
+    if (m > LLONG_MAX - d.half) return false;
+    out = -udiv((unsigned long long)(m + d.half), d);
+  }
+  return true;
+}
+
+// The apply's divider over an array (nsrl_selftest_round_div).
+__global__ void round_div_selftest_kernel(const long long* num, long long n, long long den, long long* out,
+                                          unsigned char* ok) {
+  const RoundDiv d = round_div_by(den);
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    long long q = 0;
+    ok[i] = round_div(num[i], d, q) ? 1 : 0;
+    out[i] = q;
+  }
+}
+
 __device__ __forceinline__ unsigned long long mag(long long v) {
   return v == LLONG_MIN ? (unsigned long long)LLONG_MAX + 1ull : (unsigned long long)(v < 0 ? -v : v);
 }
@@ -456,7 +510,7 @@ __global__ void __launch_bounds__(256)
       bad = true;
       continue;
     }
-    const long long den = (long long)count;
+    const RoundDiv den = round_div_by((long long)count);
     const long long e0 = (long long)(t - sg.tile0) * APPLY_TILE;
     const long long e1 = min(sg.len, e0 + APPLY_TILE);
     const int shift = sg.shift_class >= 0 ? shifts[sg.shift_class] : 0;
@@ -828,6 +882,21 @@ nsrl_status nsrl_comm_selftest_wait(int scenario, uint64_t timeout_ms, uint64_t*
   const nsrl_status s = wait_bounded(o, timeout_ms * 1000000ull, "self-test", polls);
   *aborted = f.aborted;
   return s;
+}
+
+nsrl_status nsrl_selftest_round_div(const long long* num, size_t n, long long den, long long* out,
+                                    unsigned char* ok, void* stream) {
+  if (!num || !out || !ok || den <= 0) {
+    set_error("nsrl_selftest_round_div: NULL argument or den <= 0");
+    return NSRL_INVALID_SHAPE;
+  }
+  if (n == 0) return NSRL_OK;
+  const unsigned blocks = (unsigned)std::min<size_t>((n + 255) / 256, 148 * 8);
+  round_div_selftest_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(num, (long long)n, den, out, ok);
+  const cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) return NSRL_OK;
+  set_error("round_div selftest: %s", cudaGetErrorString(e));
+  return NSRL_CUDA_ERROR;
 }
 
 nsrl_status nsrl_merge_worker_parts_i64(const long long* parts, size_t workers, size_t checked_len, size_t len,

@@ -160,3 +160,44 @@ def test_average_batch_movement(dtype, divisor):
     assert fn(core._ptr(b), core._ptr(v), n, divisor, core._stream()) == core.NSRL_OK
     assert np.array_equal(v.cpu().numpy(), ref)
     assert fn(core._ptr(b), core._ptr(v), n, 0, core._stream()) == core.NSRL_INVALID_SHAPE
+
+
+def test_apply_divider_matches_integer_division():
+    """The apply's divider (a double reciprocal of the count with one exact
+    integer correction below 2^52, integer division above) against Python's
+    exact round-half-away-from-zero division, at the edges: halves, the 2^52
+    boundary, i64 extremes, counts of 1, 3, 7, 2^31 - 1 and near 2^52."""
+    import ctypes as C
+    from nsrl_b200 import core
+    T = _train()
+    L = T._lib_dp()
+    L.nsrl_selftest_round_div.argtypes = [C.c_void_p, C.c_size_t, C.c_longlong, C.c_void_p, C.c_void_p, C.c_void_p]
+    rng = np.random.default_rng(11)
+    edge = [0, 1, -1, 2, -2, 3, -3, (1 << 52) - 1, 1 << 52, (1 << 52) + 1, -(1 << 52), (1 << 62), -(1 << 62),
+            (1 << 63) - 1, -(1 << 63) + 1, -(1 << 63)]
+
+    def ref(n, d):
+        half = d // 2
+        m = abs(n)
+        if n == -(1 << 63) or m > (1 << 63) - 1 - half:
+            return None
+        q = (m + half) // d
+        return q if n >= 0 else -q
+
+    for den in (1, 2, 3, 7, 1000, (1 << 31) - 1, (1 << 52) - 1, 1 << 52, (1 << 60) + 7):
+        nums = list(edge)
+        nums += [k * den + den // 2 + o for k in (0, 1, 5, 12345) for o in (-1, 0, 1) if abs(k * den) < (1 << 62)]
+        nums += list(rng.integers(-(1 << 53), 1 << 53, 2000))
+        nums += list(rng.integers(-(1 << 62), 1 << 62, 2000))
+        a = np.array(nums, dtype=np.int64)
+        num = torch.from_numpy(a).cuda()
+        out = torch.empty_like(num)
+        ok = torch.empty(len(nums), dtype=torch.uint8, device="cuda")
+        assert L.nsrl_selftest_round_div(core._ptr(num), len(nums), den, core._ptr(out), core._ptr(ok),
+                                         core._stream()) == core.NSRL_OK
+        got, good = out.cpu().numpy(), ok.cpu().numpy()
+        for i, n in enumerate(nums):
+            r = ref(int(n), den)
+            assert (r is None) == (good[i] == 0), (n, den)
+            if r is not None:
+                assert int(got[i]) == r, (n, den, int(got[i]), r)
