@@ -38,9 +38,9 @@ E2E_CHUNKS = (8, 16, 32)  # sequences per chunk of the host-buffer pipeline: eac
 METRIC = "int attention-block tokens/s @1/2/4/8 B200, %INT8/HBM roofline, bit-exact"
 WORKLOAD = "prenorm causal attention + gated-MLP block forward, d256 h4x64 ff1024 s1024 b64/gpu"
 # dram__bytes_read.sum + dram__bytes_write.sum per launch, from the ncu captures
-# summarised in profiles/ (attention: 322.9 MB read + 290.1 MB written; the gated
-# linear: 37.0 MB + 83.4 MB; decode at batch 32: 544.6 MB + 3.8 MB).
-NCU_TRAFFIC = {"attention_tc_hd64": 637143296, "linear_tc_gated": 120378880, "attention_decode": 548445696}
+# summarised in profiles/ (attention: 342.1 MB read + 289.8 MB written; the gated
+# linear: 35.9 MB + 81.6 MB; decode at batch 32: 544.6 MB + 3.8 MB).
+NCU_TRAFFIC = {"attention_tc_hd64": 631958272, "linear_tc_gated": 117480704, "attention_decode": 548445696}
 
 
 def peaks():
