@@ -426,10 +426,7 @@ nsrl_status nsrl_linear_i16_i8_i16(const int16_t* x, size_t rows, const nsrl_lin
   cudaStream_t s = (cudaStream_t)stream;
   Carver c(workspace);
   Planes xp = c.planes(rows, K, true);
-  NSRL_TRY(launch_split_planes(x, rows, K, K, xp, s), "split planes");
   GemmArgs g{};
-  g.a_hi = xp.hi;
-  g.a_lo = xp.lo;
   g.a_l1 = xp.l1;
   g.lda = K;
   g.M = rows;
@@ -440,7 +437,21 @@ nsrl_status nsrl_linear_i16_i8_i16(const int16_t* x, size_t rows, const nsrl_lin
   g.y = y;
   g.ldy = N;
   g.st = status;
-  NSRL_TRY(launch_gemm(g, s), "linear");
+  // With at most two 128-column output tiles the tensor-core kernel splits
+  // the int16 rows into planes itself (K % 8 == 0, 16-byte aligned rows): it
+  // converts each A tile once per output tile, which costs less than a split
+  // pass over A only while there are few of them.  Otherwise a split pass first.
+  g.a16 = N <= 256 ? x : nullptr;
+  cudaError_t e = g.a16 ? launch_gemm(g, s) : cudaErrorInvalidValue;
+  if (e == cudaErrorInvalidValue) {
+    cudaGetLastError();  // nothing was launched
+    g.a16 = nullptr;
+    NSRL_TRY(launch_split_planes(x, rows, K, K, xp, s), "split planes");
+    g.a_hi = xp.hi;
+    g.a_lo = xp.lo;
+    e = launch_gemm(g, s);
+  }
+  NSRL_TRY(e, "linear");
   return NSRL_OK;
 }
 

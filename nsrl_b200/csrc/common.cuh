@@ -405,6 +405,13 @@ __device__ __forceinline__ uint64_t sdesc_k128(uint32_t saddr) {
          ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
+// The same layout with the 8-row atoms `sbo` bytes apart (e.g. two planes
+// interleaved atom by atom).
+__device__ __forceinline__ uint64_t sdesc_k128_sbo(uint32_t saddr, uint32_t sbo) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
 // Instruction descriptor: kind::i8, D = s32, K-major A and B, shape M x N.
 // a_signed / b_signed select s8 (1) or u8 (0) per operand.
 __host__ __device__ constexpr uint32_t idesc_i8(uint32_t M, uint32_t N, uint32_t a_signed, uint32_t b_signed) {

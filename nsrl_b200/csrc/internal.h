@@ -95,6 +95,11 @@ struct GemmArgs {
   VtPlanes vt;
   bool v_rows = false;  // QKV_VT: the v columns also go to yp (row-major q|k|v planes)
   QkvRoute route;       // QKV_VT: the head-sharded destinations (route.nranks > 0)
+  // int16 A [M][lda] instead of the planes (Epi::I16 only): the kernel splits
+  // it into planes in shared memory and writes the row L1 into a_l1 when the
+  // i32 prefix check needs it.  cudaErrorInvalidValue when the shape or
+  // alignment does not allow it (the caller then splits A itself).
+  const int16_t* a16 = nullptr;
   nsrl_device_status* st;
   // Backward-input form (linear.rs:594-640): the sum is an i64 (no prefix
   // rule) requantised by requantize_i64_to_i16; A holds the prescaled grads.

@@ -43,6 +43,10 @@ constexpr int ACC_COLS = 2 * BN;                  // acc_hi: [0,128), acc_lo: [1
 constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;      // two tiles in flight
 constexpr int EPI_WARPS = 16;
 constexpr int THREADS = 64 + 32 * EPI_WARPS;      // 576
+// The int16-input form: four more warps turn each stage's int16 A tile into the
+// two byte planes in place (see the converter below).
+constexpr int CONV_WARPS = 4;
+constexpr int threads_for(bool a16) { return THREADS + (a16 ? 32 * CONV_WARPS : 0); }
 constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE_BYTES + 1024 + 256;
 
 struct TcMaps {
@@ -325,15 +329,23 @@ __device__ __forceinline__ void store16_i16(int16_t* dst, const uint32_t (&o)[8]
 
 // WIDE (= p.wide) is a template parameter so that each kernel holds only one
 // requantisation form: a smaller epilogue for the instruction cache.
-template <int EPI, bool WIDE>
-__global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_constant__ TcMaps maps, const TcParams p) {
+// A16: A is int16 [M][K] in global memory.  TMA loads each 128 x 128 int16
+// tile into the stage (the 32 KB the two planes take); warps 2 + EPI_WARPS ..
+// turn it in place into the hi and lo planes in the MMA's K-major
+// 128-byte-swizzled layout, and only then hand the stage to the MMA.  The
+// separate split pass over A disappears; the i32 prefix check, where K or a
+// bias needs it, takes the rows' L1 from the int16 rows itself.
+template <int EPI, bool WIDE, bool A16>
+__global__ void __launch_bounds__(threads_for(A16), 1)
+    gemm_tc_kernel(const __grid_constant__ TcMaps maps, const TcParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;  // [2]: MMA -> epilogue
   uint64_t* acc_empty = acc_full + 2;   // [2]: epilogue -> MMA
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* ready = acc_empty + 2;      // [STAGES]: converter -> MMA (A16)
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(ready + STAGES);
   uint32_t* skip_flag = tslot + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -350,6 +362,8 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], EPI_WARPS);
     }
+    if (A16)
+      for (int s = 0; s < STAGES; ++s) mbar_init(&ready[s], CONV_WARPS);
     fence_barrier_init();
     prefetch_tmap(&maps.a_hi);
     prefetch_tmap(&maps.a_lo);
@@ -386,8 +400,12 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
           }
           mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
           uint8_t* sa = smem + s * STAGE_BYTES;
-          tma_load_2d(sa, &maps.a_hi, &full[s], kb * BK, m0);
-          tma_load_2d(sa + TILE_A, &maps.a_lo, &full[s], kb * BK, m0);
+          if (A16) {  // the int16 tile [128 rows][128 k] (32 KB) where the planes will be
+            tma_load_2d(sa, &maps.a_hi, &full[s], kb * BK, m0);
+          } else {
+            tma_load_2d(sa, &maps.a_hi, &full[s], kb * BK, m0);
+            tma_load_2d(sa + TILE_A, &maps.a_lo, &full[s], kb * BK, m0);
+          }
           if (EPI == (int)Epi::GATED) {
             tma_load_2d(sa + 2 * TILE_A, &maps.b[0], &full[s], kb * BK, brow);
             tma_load_2d(sa + 2 * TILE_A + TILE_B / 2, &maps.b[1], &full[s], kb * BK, brow);
@@ -414,7 +432,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
         for (int kb = 0; kb < nkb; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
-          if (!mbar_wait(&full[s], ph, p.st)) {
+          if (!mbar_wait(A16 ? &ready[s] : &full[s], ph, p.st)) {
             ok = false;
             break;
           }
@@ -422,8 +440,9 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
           const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
 #pragma unroll
           for (int j = 0; j < BK / 32; ++j) {
-            const uint64_t ah = sdesc_k128(base + 32 * j);
-            const uint64_t al = sdesc_k128(base + TILE_A + 32 * j);
+            // int16 input: the converter interleaves the planes atom by atom
+            const uint64_t ah = A16 ? sdesc_k128_sbo(base + 32 * j, 2048) : sdesc_k128(base + 32 * j);
+            const uint64_t al = A16 ? sdesc_k128_sbo(base + 1024 + 32 * j, 2048) : sdesc_k128(base + TILE_A + 32 * j);
             const uint64_t bd = sdesc_k128(base + 2 * TILE_A + 32 * j);
             const uint32_t acc = (kb > 0 || j > 0) ? 1u : 0u;
             umma_i8_warp(d, ah, bd, id_hi, acc);
@@ -432,6 +451,54 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
           umma_commit_warp(&empty[s]);
         }
         umma_commit_warp(&acc_full[buf]);
+      }
+    }
+  } else if (A16 && warp >= 2 + EPI_WARPS) {
+    // --------------------------------------------------------- converter
+    // The int16 tile is [128 rows][256 bytes]; its 8-row group g (2 KB at
+    // 2048 g) becomes, in place, the hi plane's 8-row swizzle atom g (the
+    // first 1 KB) and the lo plane's (the second): the MMA reads both planes
+    // with 2048-byte atom strides.  A group's bytes hold only that group's
+    // rows before and after, so each warp converts its own four groups (rows
+    // 32 cw .. +31) with no barrier but its own: all eight rows are read
+    // before any is written.  Each lane reads 16 bytes (8 int16) of a
+    // row pair (a warp reads 512 bytes at once) and writes its 8 bytes of
+    // each plane row at the chunk's swizzled place (chunk ^ (row & 7)).
+    const int cw = warp - (2 + EPI_WARPS);
+    uint32_t it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
+      for (int kb = 0; kb < nkb; ++kb, ++it) {
+        const int s = it % STAGES;
+        if (!mbar_wait(&full[s], (it / STAGES) & 1, p.st)) {
+          ok = false;
+          break;
+        }
+        uint8_t* sa = smem + s * STAGE_BYTES;
+        // lane l: row (l >> 4) of each row pair, int16 elements 8 (l & 15) ..
+        // +7, i.e. plane bytes 8 (l & 15) .. +7 = half (l & 1) of 16-byte
+        // chunk (l & 15) >> 1
+        const uint32_t hr = (uint32_t)lane >> 4, ch = ((uint32_t)lane & 15u) >> 1, hb = ((uint32_t)lane & 1u) * 8u;
+#pragma unroll
+        for (int grp = 0; grp < 4; ++grp) {
+          uint8_t* gb = sa + 2048 * (4 * cw + grp);
+          uint4 raw[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) raw[q] = *reinterpret_cast<const uint4*>(gb + 512 * q + lane * 16);
+          __syncwarp();
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t r = 2u * (uint32_t)q + hr;  // row within the 8-row group
+            const uint32_t off = r * 128u + ((ch ^ r) << 4) + hb;
+            *reinterpret_cast<uint2*>(gb + off) =
+                make_uint2(__byte_perm(raw[q].x, raw[q].y, 0x7531), __byte_perm(raw[q].z, raw[q].w, 0x7531));
+            *reinterpret_cast<uint2*>(gb + 1024 + off) =
+                make_uint2(__byte_perm(raw[q].x, raw[q].y, 0x6420), __byte_perm(raw[q].z, raw[q].w, 0x6420));
+          }
+        }
+        fence_proxy_async_smem();  // the planes, written by the threads, are read by the tensor cores
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ready[s]);
       }
     }
   } else {
@@ -553,9 +620,10 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_tc_kernel(const __grid_consta
         // All 32 columns come out of TMEM at once and the buffer is released
         // before any arithmetic, so the next tile's MMAs overlap this
         // epilogue; the columns are then finished in two halves of 16.  The
-        // residual form, which also holds the skip rows, loads and releases
-        // half by half to keep its registers.
-        constexpr bool kOnce = EPI != (int)Epi::RESID;
+        // residual form, which also holds the skip rows, and the int16-input
+        // form, which has fewer registers per thread, load and release half
+        // by half.
+        constexpr bool kOnce = EPI != (int)Epi::RESID && !A16;
         uint32_t hq[2][16], lq[2][16];
         if (kOnce) {
           tmem_ld16(lrow + 32 * cg, hq[0]);
@@ -757,6 +825,7 @@ __global__ void gemm_simt_kernel(const SimtParams s) {
 struct CheckParams {
   const int8_t* a_hi;
   const uint8_t* a_lo;
+  const int16_t* a16;  // int16 A instead of the planes (row stride lda elements)
   long long lda;
   const unsigned long long* l1;
   int M, K;
@@ -772,15 +841,16 @@ constexpr int PREFIX_CHECK_THREADS = 256;
 // Rescans row m of the linear in the reference's order (bias, then k = 0, 1,
 // ...): any i32 prefix outside the range flags the call (linear.rs:282-296).
 __device__ void prefix_rescan_row(const CheckParams& c, int m, int lane) {
-  const int8_t* ah = c.a_hi + (long long)m * c.lda;
-  const uint8_t* al = c.a_lo + (long long)m * c.lda;
+  const int8_t* ah = c.a16 ? nullptr : c.a_hi + (long long)m * c.lda;
+  const uint8_t* al = c.a16 ? nullptr : c.a_lo + (long long)m * c.lda;
+  const int16_t* a16 = c.a16 ? c.a16 + (long long)m * c.lda : nullptr;
   for (int sg = 0; sg < c.nseg; ++sg) {
     for (int n = lane; n < c.rows[sg]; n += 32) {
       const int8_t* w = c.w[sg] + (long long)n * c.K;
       int acc = c.bias[sg] ? c.bias[sg][n] : 0;
       bool bad = false;
       for (int k = 0; k < c.K && !bad; ++k) {
-        int x = (int)ah[k] * 256 + (int)al[k];
+        const int x = a16 ? (int)a16[k] : (int)ah[k] * 256 + (int)al[k];
         long long t = (long long)acc + (long long)(x * (int)w[k]);
         if (t < INT_MIN || t > INT_MAX) bad = true;
         acc = (int)t;
@@ -796,6 +866,7 @@ __device__ void prefix_rescan_row(const CheckParams& c, int m, int lane) {
 __global__ void __launch_bounds__(PREFIX_CHECK_THREADS) prefix_check_kernel(const CheckParams c) {
   __shared__ long long s_maxb;
   __shared__ int s_rows[PREFIX_CHECK_THREADS];
+  __shared__ unsigned long long s_l1[PREFIX_CHECK_THREADS];  // int16 rows: their L1, computed here
   __shared__ int s_n;
   if (threadIdx.x == 0) s_maxb = 0;
   __syncthreads();
@@ -811,7 +882,28 @@ __global__ void __launch_bounds__(PREFIX_CHECK_THREADS) prefix_check_kernel(cons
     if (threadIdx.x == 0) s_n = 0;
     __syncthreads();
     const int m = base + (int)threadIdx.x;
-    if (m < c.M && 127ll * (long long)c.l1[m] + maxb > (long long)INT_MAX) s_rows[atomicAdd(&s_n, 1)] = m;
+    if (c.a16) {
+      // int16 rows: each warp sums |x| of 32 rows, one 512-byte stretch of a row per step
+      for (int j = 0; j < 32; ++j) {
+        const int mr = base + (threadIdx.x >> 5) * 32 + j;
+        unsigned long long sum = 0;
+        if (mr < c.M) {
+          const int16_t* xr = c.a16 + (long long)mr * c.lda;
+          for (int k = lane * 8; k < c.K; k += 256) {
+            const uint4 v = *reinterpret_cast<const uint4*>(xr + k);
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) sum += (unsigned)(abs((int)(int16_t)(w[q] & 0xFFFFu)) + abs((int)w[q] >> 16));
+          }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if (lane == j) s_l1[threadIdx.x] = sum;
+      }
+      __syncwarp();
+    }
+    const unsigned long long l1m = c.a16 ? s_l1[threadIdx.x] : (m < c.M ? c.l1[m] : 0ull);
+    if (m < c.M && 127ll * (long long)l1m + maxb > (long long)INT_MAX) s_rows[atomicAdd(&s_n, 1)] = m;
     __syncthreads();
     const int nq = s_n;
     for (int qi = threadIdx.x >> 5; qi < nq; qi += warps) prefix_rescan_row(c, s_rows[qi], lane);
@@ -902,6 +994,20 @@ EncodeTiledFn encode_fn() {
 
 // 2-D uint8 tensor map [rows][inner] with row stride `ld` bytes, box
 // [box_rows][128 bytes], 128-byte swizzle, zero fill out of bounds.
+// int16 [rows][inner] (row stride ld bytes), box [box_rows][BK elements], no
+// swizzle: the int16-input form's A tiles, rows of 256 bytes in shared memory.
+bool make_map16(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t rows, uint64_t ld, uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {ld};
+  cuuint32_t box[2] = {(cuuint32_t)BK, box_rows};
+  cuuint32_t es[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(ptr), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool make_map(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t rows, uint64_t ld, uint32_t box_rows) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
@@ -914,16 +1020,16 @@ bool make_map(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t rows, ui
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int EPI, bool WIDE>
+template <int EPI, bool WIDE, bool A16 = false>
 cudaError_t launch_tc(const TcMaps& maps, const TcParams& p, int grid, cudaStream_t stream) {
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<EPI, WIDE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)SMEM_BYTES);
+    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<EPI, WIDE, A16>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  gemm_tc_kernel<EPI, WIDE><<<grid, THREADS, SMEM_BYTES, stream>>>(maps, p);
+  gemm_tc_kernel<EPI, WIDE, A16><<<grid, threads_for(A16), SMEM_BYTES, stream>>>(maps, p);
   return cudaGetLastError();
 }
 
@@ -1006,10 +1112,22 @@ cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t stream) {
   p.small_acc = (unsigned long long)a.K * 127ull * 32767ull < (1ull << 30);
   p.wide = a.wide;
   p.st = a.st;
+  const bool a16 = a.a16 != nullptr;
+  const bool need_check = [&] {
+    bool b = false;
+    for (int i = 0; i < a.nseg; ++i) b = b || a.seg[i].bias != nullptr;
+    return !a.wide && (b || (unsigned long long)a.K * 127ull * 32767ull > 2147483647ull);
+  }();
+  // int16 A: only the plain int16 epilogue, on the tensor-core path (the
+  // caller splits A into planes itself otherwise)
+  if (a16 && (a.epi != Epi::I16 || a.wide || a.nseg != 1 || !tma_supported() || (a.K % 8) != 0 ||
+              ((a.lda * 2) % 16) != 0 || !aligned16(a.a16)))
+    return cudaErrorInvalidValue;
+
   // The wide form keeps each plane's s32 sum exact: K * 255 * 127 < 2^31.
   if (a.wide && (a.K > 66000 || gated || a.epi == Epi::QKV_VT || a.nseg != 1)) return cudaErrorInvalidValue;
 
-  bool tc = tma_supported() && (a.K % 16) == 0 && (a.lda % 16) == 0 && aligned16(a.a_hi) && aligned16(a.a_lo);
+  bool tc = a16 || (tma_supported() && (a.K % 16) == 0 && (a.lda % 16) == 0 && aligned16(a.a_hi) && aligned16(a.a_lo));
   for (int i = 0; i < a.nseg; ++i) tc = tc && aligned16(a.seg[i].w);
   if (a.nseg == 3 && (a.seg[0].rows % BN) != 0) tc = false;
   if (a.nseg == 3 && (a.seg[1].rows != a.seg[0].rows || a.seg[2].rows != a.seg[0].rows)) tc = false;
@@ -1025,18 +1143,22 @@ cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t stream) {
   cudaError_t err = cudaSuccess;
   if (tc) {
     TcMaps maps;
-    bool ok = make_map(&maps.a_hi, a.a_hi, a.K, a.M, a.lda, BM) && make_map(&maps.a_lo, a.a_lo, a.K, a.M, a.lda, BM);
+    bool ok = a16 ? make_map16(&maps.a_hi, a.a16, a.K, a.M, a.lda * 2, BM)
+                  : make_map(&maps.a_hi, a.a_hi, a.K, a.M, a.lda, BM) && make_map(&maps.a_lo, a.a_lo, a.K, a.M, a.lda, BM);
+    if (a16) maps.a_lo = maps.a_hi;  // unused
     const uint32_t brows = gated ? BN / 2 : BN;
     for (int i = 0; i < a.nseg && ok; ++i) ok = make_map(&maps.b[i], a.seg[i].w, a.K, a.seg[i].rows, a.K, brows);
     for (int i = a.nseg; i < 3; ++i) maps.b[i] = maps.b[0];
     if (!ok) {
+      if (a16) return cudaErrorInvalidValue;
       tc = false;
     } else {
       p.tiles_n = gated ? (N + BN / 2 - 1) / (BN / 2) : (N + BN - 1) / BN;
       p.tiles = p.tiles_n * (int)((a.M + BM - 1) / BM);
       const int grid = std::min(p.tiles, sm_count());
       ProfScope prof(names[1][(int)a.epi], stream, 2.0 * Mx * nw * Kx, 2.0 * Mx * Kx + nw * Kx + out_bytes);
-      err = launch_tc_epi(a.epi, maps, p, grid, stream);
+      err = a16 ? launch_tc<(int)Epi::I16, false, true>(maps, p, grid, stream)
+                : launch_tc_epi(a.epi, maps, p, grid, stream);
     }
   }
   if (!tc) {
@@ -1061,13 +1183,12 @@ cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t stream) {
 
   // The i32 prefix can only overflow when |bias| + K * 127 * 32767 > i32::MAX
   // (linear.rs:144-173); then rows outside the L1 bound are rescanned.
-  bool any_bias = false;
-  for (int i = 0; i < a.nseg; ++i) any_bias = any_bias || a.seg[i].bias != nullptr;
-  if (!a.wide && (any_bias || (unsigned long long)a.K * 127ull * 32767ull > 2147483647ull)) {
+  if (need_check) {
     if (!a.a_l1) return cudaErrorInvalidValue;
     CheckParams c{};
     c.a_hi = a.a_hi;
     c.a_lo = a.a_lo;
+    c.a16 = a.a16;
     c.lda = (long long)a.lda;
     c.l1 = a.a_l1;
     c.M = (int)a.M;
