@@ -1,5 +1,6 @@
 // Integer causal self-attention on the B200 tensor cores (tcgen05, kind::i8),
-// head_dim 64.
+// head_dim 64, or 16 for the forward alone (Q and K rows padded to the MMA's
+// 32-byte K step, logit shift 2).
 //
 // Reference: crates/nsrl-core/src/attention.rs:742-877 (full attention),
 // :261-293 (base-2 softmax), :117-140 (QK dot), :596-668 (AV).
@@ -36,7 +37,7 @@
 namespace nsrl {
 namespace {
 
-constexpr int QT = 128, KT = 32, HD = 64;
+constexpr int QT = 128, KT = 32, HD = 64;  // HD: the largest head dim (it sizes the shared-memory layout)
 constexpr int ST = 4;                 // K / V^T stage ring
 constexpr int PLANE_Q = QT * HD;      // 8 KB per plane
 constexpr int PLANE_K = KT * HD;      // 2 KB: 32 keys x 64 dims
@@ -53,8 +54,20 @@ constexpr uint32_t TMEM_COLS = 512;                     // 256 per group
 constexpr uint32_t S_HH = 0, S_MID = 32, S_LL = 64, S_BUF1 = 96;
 constexpr uint32_t O_HH = 0, O_MID = 64, O_LL = 128;
 // Bound on |256 * mid + ll| of one 64-dim dot product: |mid| <= 64 * 2 * 128 * 255,
-// 0 <= ll <= 64 * 255 * 255.
+// 0 <= ll <= 64 * 255 * 255 (a 16-dim product stays below it too).
 constexpr long long B_MID = 64LL * 2 * 128 * 255 * 256 + 64LL * 255 * 255;
+
+// Per head dim (64 or 16): Q and K rows in shared memory are ROW bytes (16
+// dims are padded to the MMA's 32-byte K step: Q's upper 16 bytes are zeroed,
+// so whatever K holds there adds nothing), the logit shift is
+// log2(sqrt(head_dim)) (attention.rs:77-87), and the transfer sizes.
+template <int HDIM>
+struct HeadDim {
+  static constexpr int ROW = HDIM < 32 ? 32 : HDIM;
+  static constexpr int SH = HDIM == 64 ? 3 : 2;
+  static constexpr int PQ = QT * ROW, PK = KT * ROW, PV = HDIM * KT;
+  static_assert(HDIM == 64 || HDIM == 16, "head dims 64 and 16");
+};
 
 constexpr int OFF_Q = 0;
 constexpr int OFF_STAGE = OFF_Q + 2 * PLANE_Q;
@@ -108,6 +121,7 @@ __device__ __forceinline__ uint32_t swz32_chunk(uint32_t r, uint32_t c) { return
 struct Ctl {
   uint64_t q_full, full[ST], empty[ST], s_full[2], s_empty[2], p_full[2], p_empty[2], o_full;
   uint64_t w_ready, w_full[WPF_N], w_empty[WPF_N];  // the weight scratch written / its last-pass tile ring
+  uint64_t q_ready;  // head dim 16: Q's padding zeroed by the softmax warps
   uint32_t tslot, abort;
 };
 static_assert(sizeof(Ctl) <= 256, "barrier area");
@@ -149,10 +163,10 @@ __device__ __forceinline__ void scores_max(const uint32_t (&hh)[16], const uint3
 }
 
 // Base-2 weights w = LUT(lg - lgmax) (attention.rs:142-158) of 16 scores.  w
-// != 0 needs mag = lgmax - lg < 3840, i.e. raw > rawmax - 30720; that needs
-// hh > hh_floor, and then rawmax - raw < 2^32 is exact in u32, with
-// mag = (diff + cround) >> 3.
-template <bool FULL>
+// != 0 needs mag = lgmax - lg < 3840, i.e. raw > rawmax - (3840 << SH); that
+// needs hh > hh_floor, and then rawmax - raw < 2^32 is exact in u32, with
+// mag = (diff + cround) >> SH (SH = 3 for head dim 64: the logit is raw >> 3).
+template <bool FULL, int SH>
 __device__ __forceinline__ void scores_weight(const uint32_t (&hh)[16], const uint32_t (&mid)[16],
                                               const uint32_t (&ll)[16], int nlive, int hh_floor, uint32_t rawmax_lo,
                                               uint32_t cround, const int16_t* lut, int (&w)[16]) {
@@ -161,8 +175,8 @@ __device__ __forceinline__ void scores_weight(const uint32_t (&hh)[16], const ui
     int wi = 0;
     if ((FULL || i < nlive) && (int)hh[i] > hh_floor) {
       const uint32_t diff = rawmax_lo - (hh[i] * 65536u + mid[i] * 256u + ll[i]);
-      if (diff < 30720u - cround) {
-        const uint32_t mag = (diff + cround) >> 3;
+      if (diff < (3840u << SH) - cround) {
+        const uint32_t mag = (diff + cround) >> SH;
         wi = (int)lut[mag & 255u] >> (mag >> 8);
       }
     }
@@ -234,11 +248,11 @@ __device__ __forceinline__ void tile_max(const uint32_t (&hh)[16], const uint32_
 // Pass-1 weights of a warp whose 32 rows all have exact i32 raw values
 // (|raw| <= 2^30 + B_MID).  With C = rawmax + cround (mod 2^32),
 // t = C - raw = (rawmax - raw) + cround < 2^32 exactly, mag = lgmax - lg =
-// t >> 3, and w = LUT[mag & 255] >> (mag >> 8) = lutr[(t >> 3) & 255] >> (t >> 11):
-// t >= 30720 (mag >= 3840) shifts by 15 or more and gives 0 as the
+// t >> SH, and w = LUT[mag & 255] >> (mag >> 8) = lutr[(t >> SH) & 255] >> (t >> (SH + 8)):
+// t >= 3840 << SH (mag >= 3840) shifts by 15 or more and gives 0 as the
 // reference's `shift >= 15` test does, since every table value is below 2^15.
 // Masked keys get t = 2^32 - 1, hence w = 0.
-template <bool FULL>
+template <bool FULL, int SH>
 __device__ __forceinline__ void weights_fast(const uint32_t (&hh)[16], const uint32_t (&mid)[16],
                                              const uint32_t (&ll)[16], int nlive, uint32_t C, uint32_t lane4,
                                              uint32_t (&w)[16]) {
@@ -247,8 +261,8 @@ __device__ __forceinline__ void weights_fast(const uint32_t (&hh)[16], const uin
   for (int i = 0; i < 16; ++i) {
     uint32_t t = C - (hh[i] * 65536u + mid[i] * 256u + ll[i]);
     if (!FULL && i >= nlive) t = 0xFFFFFFFFu;
-    const uint32_t v = *reinterpret_cast<const uint32_t*>(tab + (((t << 4) & 0x7F80u) | lane4));
-    w[i] = shr_clamp(v, t >> 11);
+    const uint32_t v = *reinterpret_cast<const uint32_t*>(tab + (((t << (7 - SH)) & 0x7F80u) | lane4));
+    w[i] = shr_clamp(v, t >> (SH + 8));
   }
 }
 
@@ -257,7 +271,9 @@ __device__ __forceinline__ void weights_fast(const uint32_t (&hh)[16], const uin
 // on its own sequence with its own shared-memory region, barriers and 256 TMEM
 // columns: the row exchanges, first-tile latency and tail of one group overlap
 // the steady state of the other.
+template <int HDIM>
 __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_constant__ Maps maps, const Args a) {
+  using Hd = HeadDim<HDIM>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint32_t s_abort, s_tslot;
   const int gw = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -302,6 +318,7 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
     }
     mbar_init(&ctl->o_full, 1);
     mbar_init(&ctl->w_ready, SOFTMAX_WARPS);
+    mbar_init(&ctl->q_ready, SOFTMAX_WARPS);
     for (int i = 0; i < WPF_N; ++i) {
       mbar_init(&ctl->w_full[i], 1);
       mbar_init(&ctl->w_empty[i], SOFTMAX_WARPS);
@@ -323,9 +340,9 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
   } else if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      mbar_arrive_expect_tx(&ctl->q_full, 2 * PLANE_Q);
-      tma_load_2d(sm + OFF_Q, &maps.q_hi, &ctl->q_full, h * HD, row0 + q0);
-      tma_load_2d(sm + OFF_Q + PLANE_Q, &maps.q_lo, &ctl->q_full, h * HD, row0 + q0);
+      mbar_arrive_expect_tx(&ctl->q_full, 2 * Hd::PQ);
+      tma_load_2d(sm + OFF_Q, &maps.q_hi, &ctl->q_full, h * HDIM, row0 + q0);
+      tma_load_2d(sm + OFF_Q + PLANE_Q, &maps.q_lo, &ctl->q_full, h * HDIM, row0 + q0);
       uint32_t it = 0;
       bool ok = true;
       for (int pass = 0; pass < 3 && ok; ++pass) {
@@ -336,12 +353,12 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
             break;
           }
           uint8_t* stg = sm + OFF_STAGE + s * STAGE_BYTES;
-          mbar_arrive_expect_tx(&ctl->full[s], STAGE_BYTES);
+          mbar_arrive_expect_tx(&ctl->full[s], pass < 2 ? 2 * Hd::PK : 2 * Hd::PV);
           if (pass < 2) {  // K rows j*32 .. +31 of this head
-            tma_load_2d(stg, &maps.k_hi, &ctl->full[s], a.d + h * HD, row0 + j * KT);
-            tma_load_2d(stg + PLANE_K, &maps.k_lo, &ctl->full[s], a.d + h * HD, row0 + j * KT);
-          } else {         // V^T: 64 dims x keys j*32 .. +31
-            const int vrow = (b * a.H + h) * HD;
+            tma_load_2d(stg, &maps.k_hi, &ctl->full[s], a.d + h * HDIM, row0 + j * KT);
+            tma_load_2d(stg + PLANE_K, &maps.k_lo, &ctl->full[s], a.d + h * HDIM, row0 + j * KT);
+          } else {         // V^T: the head's dims x keys j*32 .. +31
+            const int vrow = (b * a.H + h) * HDIM;
             tma_load_2d(stg, &maps.vt_hi, &ctl->full[s], j * KT, vrow);
             tma_load_2d(stg + PLANE_V, &maps.vt_lo, &ctl->full[s], j * KT, vrow);
             // the sum pass's weights of tile j, into ring slot j % WPF_N, once
@@ -367,10 +384,10 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
     {
       const uint32_t id_ss = idesc_i8(QT, KT, 1, 1), id_su = idesc_i8(QT, KT, 1, 0);
       const uint32_t id_us = idesc_i8(QT, KT, 0, 1), id_uu = idesc_i8(QT, KT, 0, 0);
-      const uint32_t pv_us = idesc_i8(QT, HD, 0, 1), pv_uu = idesc_i8(QT, HD, 0, 0);
+      const uint32_t pv_us = idesc_i8(QT, HDIM, 0, 1), pv_uu = idesc_i8(QT, HDIM, 0, 0);
       const uint32_t qh = smem_u32(sm + OFF_Q), ql = qh + PLANE_Q;
       uint32_t use0 = 0, use1 = 0;  // uses of each S buffer
-      wait_bar(&ctl->q_full, 0, ctl, a.st);
+      wait_bar(HDIM < 32 ? &ctl->q_ready : &ctl->q_full, 0, ctl, a.st);
       uint32_t it = 0;
       for (int pass = 0; pass < 2; ++pass) {
         for (int j = 0; j < ntiles; ++j, ++it) {
@@ -383,9 +400,12 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
           const uint32_t kh = smem_u32(sm + OFF_STAGE + s * STAGE_BYTES), kl = kh + PLANE_K;
           const uint32_t d = tmem + (uint32_t)sb * S_BUF1;
 #pragma unroll
-          for (int ks = 0; ks < HD / 32; ++ks) {
-            const uint64_t aqh = sdesc_k64(qh + 32 * ks), aql = sdesc_k64(ql + 32 * ks);
-            const uint64_t bkh = sdesc_k64(kh + 32 * ks), bkl = sdesc_k64(kl + 32 * ks);
+          for (int ks = 0; ks < Hd::ROW / 32; ++ks) {
+            // 64-byte rows (64-byte swizzle) for head dim 64, 32-byte rows for 16
+            const uint64_t aqh = Hd::ROW == 64 ? sdesc_k64(qh + 32 * ks) : sdesc_k32(qh);
+            const uint64_t aql = Hd::ROW == 64 ? sdesc_k64(ql + 32 * ks) : sdesc_k32(ql);
+            const uint64_t bkh = Hd::ROW == 64 ? sdesc_k64(kh + 32 * ks) : sdesc_k32(kh);
+            const uint64_t bkl = Hd::ROW == 64 ? sdesc_k64(kl + 32 * ks) : sdesc_k32(kl);
             const uint32_t acc = ks > 0 ? 1u : 0u;
             umma_i8_warp(d + S_HH, aqh, bkh, id_ss, acc);
             umma_i8_warp(d + S_MID, aqh, bkl, id_su, acc);
@@ -448,6 +468,18 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
       const uint32_t v = (uint32_t)(uint16_t)d_exp2_lut[i >> 3];
       reinterpret_cast<uint4*>(s_lutr)[i] = make_uint4(v, v, v, v);
     }
+    if (HDIM < 32) {
+      // Head dim 16: each Q row was loaded as 32 bytes (this head's 16, then
+      // the next 16 of the row); the upper 16 become zeros, so the 32-byte MMA
+      // K step adds nothing for them.  Thread t zeroes row t & 127 of plane
+      // t >> 7: logical chunk 1 of the 32-byte-swizzled row.
+      wait_bar(&ctl->q_full, 0, ctl, a.st);
+      const uint32_t t = (uint32_t)(gtid - 64), r = t & 127u;
+      *reinterpret_cast<uint4*>(sm + OFF_Q + (t >> 7) * PLANE_Q + swz32_chunk(r, 1u)) = make_uint4(0u, 0u, 0u, 0u);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ctl->q_ready);
+    }
     const int q = gw & 3, g = (warp - 2) >> 2;  // TMEM lane quarter follows the warp's index in the CTA
     const int row = q * 32 + lane;
     const int qi = q0 + row;
@@ -508,14 +540,14 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
       rmn = min(rmn, xmin[(g ^ 1) * QT + row]);
       if (row_live) {
         rawmax = rmx;
-        lgmax = rawmax >> 3;
-        if (lgmax > INT_MAX || (rmn != LLONG_MAX && (rmn >> 3) < INT_MIN)) range_bad = true;
+        lgmax = rawmax >> Hd::SH;
+        if (lgmax > INT_MAX || (rmn != LLONG_MAX && (rmn >> Hd::SH) < INT_MIN)) range_bad = true;
         if (lgmax <= (long long)INT_MIN) masked_bad = true;  // every live logit masked or out of range
         slow_row = lgmax < (long long)INT_MIN + 15 * 256;
         rawmax_lo = (uint32_t)rawmax;
-        cround = 7u - (uint32_t)(rawmax & 7);
-        // candidates for w != 0: 65536*hh + B_MID > rawmax - 30720
-        const long long fl = (rawmax - 30720 - B_MID) >> 16;
+        cround = ((1u << Hd::SH) - 1u) - (uint32_t)(rawmax & ((1 << Hd::SH) - 1));
+        // candidates for w != 0: 65536*hh + B_MID > rawmax - (3840 << SH)
+        const long long fl = (rawmax - (3840LL << Hd::SH) - B_MID) >> 16;
         hh_floor = (int)max((long long)INT_MIN, min((long long)INT_MAX, fl));
         // no element of the row took the i64 path: every raw value of the
         // row, rawmax included, is an exact i32 of magnitude <= 2^30 + B_MID
@@ -530,17 +562,17 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
       const bool full = __all_sync(FULLMASK, nlive == 16);
       if (warp_fast) {
         if (full)
-          weights_fast<true>(hh, mid, ll, nlive, cfast, lane4, w);
+          weights_fast<true, Hd::SH>(hh, mid, ll, nlive, cfast, lane4, w);
         else
-          weights_fast<false>(hh, mid, ll, nlive, cfast, lane4, w);
+          weights_fast<false, Hd::SH>(hh, mid, ll, nlive, cfast, lane4, w);
         return;
       }
       int wi[16];
       if (!slow_row) {
         if (full)
-          scores_weight<true>(hh, mid, ll, nlive, hh_floor, rawmax_lo, cround, lut, wi);
+          scores_weight<true, Hd::SH>(hh, mid, ll, nlive, hh_floor, rawmax_lo, cround, lut, wi);
         else
-          scores_weight<false>(hh, mid, ll, nlive, hh_floor, rawmax_lo, cround, lut, wi);
+          scores_weight<false, Hd::SH>(hh, mid, ll, nlive, hh_floor, rawmax_lo, cround, lut, wi);
       } else {
         // Rows whose max logit lies within 15 * 256 of i32::MIN: exact i64
         // path, with logits equal to MASKED_LOGIT excluded (attention.rs:266-276).
@@ -549,7 +581,7 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
           int v = 0;
           if (i < nlive) {
             const long long raw = (long long)(int)hh[i] * 65536 + (long long)(int)mid[i] * 256 + (long long)(int)ll[i];
-            const long long lg = raw >> 3;
+            const long long lg = raw >> Hd::SH;
             const long long delta = lg - lgmax;
             if (delta > -15 * 256 && lg != (long long)INT_MIN) {
               const int mag = (int)(-delta);
@@ -685,9 +717,10 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
     }
     unsigned l1 = 0;
 #pragma unroll
-    for (int c = 0; c < 2; ++c) {  // dims [32g + 16c, +16)
+    for (int c = 0; c < 2; ++c) {  // dims [32g + 16c, +16) of the head's HDIM
       uint32_t oh[16], om[16], ol[16];
       const uint32_t col = (uint32_t)(32 * g + 16 * c);
+      if (col >= (uint32_t)HDIM) continue;
       tmem_ld16(trow + O_HH + col, oh);
       tmem_ld16(trow + O_MID + col, om);
       tmem_ld16(trow + O_LL + col, ol);
@@ -709,12 +742,12 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
           hw[k] = __byte_perm(pk[2 * k], pk[2 * k + 1], 0x7531);
           lw[k] = __byte_perm(pk[2 * k], pk[2 * k + 1], 0x6420);
         }
-        const long long off = crow * a.ldc + a.rt.col0 + h * HD + col;
+        const long long off = crow * a.ldc + a.rt.col0 + h * HDIM + col;
         *reinterpret_cast<uint4*>(chi + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
         *reinterpret_cast<uint4*>(clo + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
       }
     }
-    if (row_live && cl1) atomicAdd(&cl1[crow], (unsigned long long)l1);
+    if (row_live && cl1 && 32 * g < HDIM) atomicAdd(&cl1[crow], (unsigned long long)l1);
   }
   tc_fence_before();
   __syncthreads();
@@ -792,10 +825,14 @@ bool attention_tc_supported(size_t S, size_t d, size_t H) {
   return H != 0 && d / H == (size_t)HD && d % H == 0 && S % 16 == 0 && S <= 16384 && (3 * d) % 16 == 0;
 }
 
+bool attention_tc_forward_supported(size_t S, size_t d, size_t H) {
+  return H != 0 && d % H == 0 && (d / H == 64 || d / H == 16) && S % 16 == 0 && S <= 16384 && (3 * d) % 16 == 0;
+}
+
 size_t attention_tc_wstride(size_t S) { return (S + 63) / 64 * 64; }
 
 size_t attention_tc_scratch_bytes(size_t B, size_t S, size_t d, size_t H) {
-  if (!attention_tc_supported(S, d, H) || B == 0) return 0;
+  if (!attention_tc_forward_supported(S, d, H) || B == 0) return 0;
   return chunk_seqs(B, S, H) * scratch_per_seq(S, H);
 }
 
@@ -803,7 +840,11 @@ cudaError_t launch_attention_tc(const Planes& qkv, const VtPlanes& vt, size_t B,
                                 bool causal, Planes ctx, int16_t* wscr, nsrl_device_status* st,
                                 cudaStream_t stream, int16_t* probs, const Planes* probs_planes,
                                 const CtxRoute* route) {
-  if (!attention_tc_supported(S, d, H) || encode_fn() == nullptr || wscr == nullptr) return cudaErrorNotSupported;
+  if (!attention_tc_forward_supported(S, d, H) || encode_fn() == nullptr || wscr == nullptr)
+    return cudaErrorNotSupported;
+  const size_t hd = d / H;
+  // head dim 16: the forward only (no P for a backward, no head-sharded routing)
+  if (hd == 16 && (probs || probs_planes || (route && route->nranks))) return cudaErrorNotSupported;
   if (probs_planes && (!causal || probs_planes->ld != S)) return cudaErrorInvalidValue;
   if (route && route->nranks &&
       (route->tab == nullptr || route->s_loc <= 0 || S % (size_t)route->s_loc != 0 || probs || probs_planes))
@@ -812,9 +853,15 @@ cudaError_t launch_attention_tc(const Planes& qkv, const VtPlanes& vt, size_t B,
   const size_t T = B * S;
   Maps m;
   const bool ok =
-      make_map(&m.q_hi, qkv.hi, 2 * d, T, qkv.ld, 64, QT) && make_map(&m.q_lo, qkv.lo, 2 * d, T, qkv.ld, 64, QT) &&
-      make_map(&m.k_hi, qkv.hi, 2 * d, T, qkv.ld, 64, KT) && make_map(&m.k_lo, qkv.lo, 2 * d, T, qkv.ld, 64, KT) &&
-      make_map(&m.vt_hi, vt.hi, S, B * H * HD, S, KT, HD) && make_map(&m.vt_lo, vt.lo, S, B * H * HD, S, KT, HD) &&
+      // q and k rows of a head: 64 bytes (64-byte swizzle), or for head dim 16
+      // 32 bytes from the head's first (32-byte swizzle; Q's extra 16 zeroed
+      // in the kernel)
+      make_map(&m.q_hi, qkv.hi, 2 * d, T, qkv.ld, hd == 64 ? 64 : 32, QT) &&
+      make_map(&m.q_lo, qkv.lo, 2 * d, T, qkv.ld, hd == 64 ? 64 : 32, QT) &&
+      make_map(&m.k_hi, qkv.hi, 2 * d, T, qkv.ld, hd == 64 ? 64 : 32, KT) &&
+      make_map(&m.k_lo, qkv.lo, 2 * d, T, qkv.ld, hd == 64 ? 64 : 32, KT) &&
+      make_map(&m.vt_hi, vt.hi, S, B * H * hd, S, KT, (uint32_t)hd) &&
+      make_map(&m.vt_lo, vt.lo, S, B * H * hd, S, KT, (uint32_t)hd) &&
       (!probs_planes || (make_p_map(&m.p_hi, probs_planes->hi, S, B * H) && make_p_map(&m.p_lo, probs_planes->lo, S, B * H))) &&
       make_map(&m.w, wscr, 2 * attention_tc_wstride(S), chunk_seqs(B, S, H) * H * ((S + QT - 1) / QT) * QT,
                2 * attention_tc_wstride(S), 64, QT) &&
@@ -840,21 +887,25 @@ cudaError_t launch_attention_tc(const Planes& qkv, const VtPlanes& vt, size_t B,
   a.st = st;
   a.wscr = wscr;
   a.wstride = (long long)attention_tc_wstride(S);
-  static bool configured = false;
-  if (!configured) {
-    const cudaError_t e =
-        cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
+  static bool configured[2] = {false, false};
+  if (!configured[hd == 16]) {
+    const cudaError_t e = cudaFuncSetAttribute(hd == 16 ? attention_tc_kernel<16> : attention_tc_kernel<64>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
     if (e != cudaSuccess) return e;
-    configured = true;
+    configured[hd == 16] = true;
   }
   const double pairs = causal ? (double)S * (S + 1) / 2.0 : (double)S * S;
-  ProfScope prof("attention_tc_hd64", stream, 4.0 * HD * (double)H * (double)B * pairs, 8.0 * (double)T * (double)d);
+  ProfScope prof(hd == 16 ? "attention_tc_hd16" : "attention_tc_hd64", stream,
+                 4.0 * (double)hd * (double)H * (double)B * pairs, 8.0 * (double)T * (double)d);
   const size_t chunk = chunk_seqs(B, S, H);
   for (size_t b0 = 0; b0 < B; b0 += chunk) {
     a.b0 = (int)b0;
     a.nb = (int)std::min(chunk, B - b0);
     const dim3 grid((unsigned)H, (unsigned)((a.nb + GROUPS - 1) / GROUPS), (unsigned)((S + QT - 1) / QT));
-    attention_tc_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(m, a);
+    if (hd == 16)
+      attention_tc_kernel<16><<<grid, THREADS, SMEM_BYTES, stream>>>(m, a);
+    else
+      attention_tc_kernel<64><<<grid, THREADS, SMEM_BYTES, stream>>>(m, a);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }

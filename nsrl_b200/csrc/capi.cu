@@ -95,7 +95,7 @@ bool attention_prefill_native(size_t d, size_t H, size_t S) {
 // Transposed V planes for the tensor-core attention (empty when it does not apply).
 VtPlanes carve_vt(Carver& c, size_t B, size_t S, size_t d, size_t H) {
   VtPlanes vt{nullptr, nullptr, (int)S, (int)H, (int)(d / H), nullptr};
-  if (attention_tc_supported(S, d, H)) {
+  if (attention_tc_forward_supported(S, d, H)) {
     vt.hi = c.take<int8_t>(B * S * d);
     vt.lo = c.take<uint8_t>(B * S * d);
     const size_t ws = attention_tc_scratch_bytes(B, S, d, H);
@@ -113,7 +113,7 @@ size_t attention_ws(size_t B, size_t S, size_t d, size_t H, Carver* c = nullptr)
   k.planes(T, d, true);
   k.planes(T, 3 * d, false);
   k.planes(T, d, true);
-  if (attention_tc_supported(S, d, H)) {
+  if (attention_tc_forward_supported(S, d, H)) {
     k.take<int8_t>(T * d);
     k.take<uint8_t>(T * d);
     const size_t ws = attention_tc_scratch_bytes(B, S, d, H);

@@ -96,8 +96,8 @@ struct GemmArgs {
   bool v_rows = false;  // QKV_VT: the v columns also go to yp (row-major q|k|v planes)
   QkvRoute route;       // QKV_VT: the head-sharded destinations (route.nranks > 0)
   // int16 A [M][lda] instead of the planes (Epi::I16 only): the kernel splits
-  // it into planes in shared memory and writes the row L1 into a_l1 when the
-  // i32 prefix check needs it.  cudaErrorInvalidValue when the shape or
+  // it into planes in shared memory, and the i32 prefix check, where needed,
+  // takes row L1 from the int16 rows.  cudaErrorInvalidValue when the shape or
   // alignment does not allow it (the caller then splits A itself).
   const int16_t* a16 = nullptr;
   nsrl_device_status* st;
@@ -124,8 +124,9 @@ cudaError_t launch_rms_norm(const int16_t* x, size_t rows, size_t d, const int16
 cudaError_t launch_attention(const Planes& qkv, size_t B, size_t S, size_t d, size_t H, bool causal, Planes ctx,
                              nsrl_device_status* st, cudaStream_t stream);
 
-// Tensor-core (tcgen05) attention core for head_dim 64: q, k from the q|k|v
-// planes, v from the transposed planes of Epi::QKV_VT.  Returns
+// Tensor-core (tcgen05) attention core for head_dim 64 (or 16: the forward
+// only): q, k from the q|k|v planes, v from the transposed planes of
+// Epi::QKV_VT.  Returns
 // cudaErrorNotSupported when the shape is outside what it takes.
 // wscr (optional, attention_tc_scratch_bytes): weights of the sum pass, so
 // that the last pass does not recompute Q K^T.
@@ -145,6 +146,8 @@ size_t attention_tc_scratch_bytes(size_t B, size_t S, size_t d, size_t H);
 // Shape rule of the tensor-core attention (head_dim 64, seq_len % 16 == 0,
 // seq_len <= 16384); the workspace reserves the transposed V planes for it.
 bool attention_tc_supported(size_t S, size_t d, size_t H);
+// The forward alone (no cached P, no head-sharded routing) also takes head_dim 16.
+bool attention_tc_forward_supported(size_t S, size_t d, size_t H);
 
 // KV-cache decode attention (int16 operands).
 // Caches are [B][Lmax][H*hd] (the reference's row layout) or, head_major,

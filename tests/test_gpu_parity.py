@@ -139,6 +139,9 @@ def attn_weights(core, d, seed, qk_extra=7, qk_shift=None):
     (2, 128, 128, 2, False, 5),    # tensor-core path, full attention
     (1, 1024, 256, 4, True, 7),    # tensor-core path at the benchmark length
     (1, 320, 64, 1, True, 0),      # tensor-core path, peaked softmax, one head
+    (2, 256, 256, 16, True, 7),    # tensor-core path at head_dim 16 (the alt 16 x 16 shape)
+    (1, 144, 128, 8, False, 5),    # head_dim 16, full attention, ragged tiles
+    (1, 1024, 256, 16, True, 0),   # head_dim 16 at the benchmark length, peaked softmax
 ])
 def test_self_attention_parity(core, B, S, d, H, causal, qk_extra):
     P = attn_weights(core, d, 100 + d + H, qk_extra)
