@@ -469,7 +469,7 @@ def run_train(core, torch, dist, world, rank, steps, warmup, flush, hbm, tfl, sr
            "kernels": {k: {"launches": v["launches"], "ms": round(v["ms"], 3), "share": round(v["ms"] / total, 4)}
                        for k, v in sorted(rows.items(), key=lambda kv: -kv[1]["ms"])[:12]}}
     ap = rows.get("dp_apply")
-    if ap:  # the requantising apply: algorithmic bytes (34 per arena element) per launch over its time
+    if ap:  # the requantising apply: algorithmic bytes (gradient, residual or Adam state, weight) over its time
         per = ap["ms"] / ap["launches"]
         gbs = ap["bytes"] / ap["launches"] / (per / 1000.0) / 1e9
         out["apply"] = {"ms_per_launch": round(per, 4), "algorithmic_bytes_per_launch": ap["bytes"] / ap["launches"],

@@ -632,6 +632,19 @@ nsrl_status nsrl_selftest_bounded_wait(unsigned long long limit_ns, nsrl_device_
 nsrl_status nsrl_selftest_round_div(const long long* num, size_t n, long long den, long long* out,
                                     unsigned char* ok, void* stream);
 
+/* Runs the element rule of the data-parallel apply's SGD segments over n
+ * entries: weights_i8 != 0 is apply_linear_weight_gradient_i64_to_i8 with the
+ * residual carried (crates/nsrl-train-core/src/lib.rs:386-465), 0 the i16
+ * embedding rule (nsrl-train/src/lib.rs:14457-14510), with the gradient sums,
+ * count, learning rate and shift given.  residuals and weights (int8 or
+ * int16) are updated in place; stats (3 device uint64, zeroed by the caller)
+ * gain {saturations, zero deltas, weight L1}; *bad is set to 1 where the
+ * reference's checked arithmetic fails (the apply would be rejected).  The
+ * sums are not cleared.  Device arrays; no counterpart in the reference. */
+nsrl_status nsrl_selftest_sgd_apply(const long long* sums, long long* residuals, void* weights, int weights_i8,
+                                    size_t n, unsigned long long count, int learning_rate, int shift,
+                                    unsigned long long* stats, unsigned char* bad, void* stream);
+
 /* ------------------------------------------------- head-sharded forward --
  * The transformer block of nsrl_prenorm_transformer_block (or, without the
  * MLP, nsrl_prenorm_attention_residual_block) split over n ranks, one GPU

@@ -226,7 +226,10 @@ enum Decision : int { DEC_APPLY = 0, DEC_REJECT = 1, DEC_MERGE = 2, DEC_INVALID 
 enum SegKind : int { SEG_SGD_I8 = 0, SEG_SGD_EMB_I16 = 1, SEG_ADAM_I8 = 2, SEG_ADAM_I16 = 3 };
 
 constexpr int MAX_SEGS = 128;
-constexpr int APPLY_TILE = 4096;  // elements of one apply tile (256 threads x 16)
+constexpr int APPLY_THREADS = 256;
+constexpr int APPLY_PER = 16;
+constexpr int APPLY_BATCH = 8;  // loads a thread issues before their arithmetic
+constexpr int APPLY_TILE = APPLY_THREADS * APPLY_PER;  // elements of one apply tile
 
 struct ApplySeg {
   long long off;        // first element in the arena
@@ -278,25 +281,50 @@ __device__ __forceinline__ bool round_div(long long num, long long den, long lon
   return true;
 }
 
-// round_div by one divisor over many numerators: den / 2 and the correctly
-// rounded double 1 / den are computed once.  floor(u / den) for u < 2^52 and
-// den < 2^52 comes from the double product u * (1 / den): u is exact as a
-// double and the product is within a relative 2^-52 of u / den, so it is
-// within one of the quotient, and one exact integer step (r = u - q den, then
-// q - 1 for r < 0 or q + 1 for r >= den) gives it; larger values divide as
-// integers.  Same results as round_div.
+// round_div by one divisor over many numerators, with the divisor's
+// constants computed once.  Three quotient paths, all exact:
+//  - u < 2^32 and den < 2^32: Granlund and Montgomery's division by an
+//    invariant integer ("Division by Invariant Integers using Multiplication",
+//    PLDI 1994, figure 4.1): with l = ceil(log2 den) and
+//    m = floor(2^32 (2^l - den) / den) + 1 (< 2^32), t = hi32(m u) and
+//    floor(u / den) = (t + ((u - t) >> min(l, 1))) >> max(l - 1, 0);
+//  - u < 2^52 and den < 2^52: the double product u * (1 / den), within one of
+//    the quotient (u is exact as a double and the correctly rounded 1 / den
+//    is within a relative 2^-53), then one exact integer step (r = u - q den,
+//    then q - 1 for r < 0 or q + 1 for r >= den);
+//  - otherwise 64-bit integer division.
+// Same results as round_div.
 struct RoundDiv {
   long long den, half;
   double rd;
+  uint32_t m32;  // the 32-bit path's multiplier and shifts (den < 2^32)
+  int sh1, sh2;
+  bool d32;
 };
 __device__ __forceinline__ RoundDiv round_div_by(long long den) {
   RoundDiv d;
   d.den = den;
   d.half = den / 2;
   d.rd = 1.0 / (double)den;
+  d.d32 = den <= 0xFFFFFFFFll;
+  d.m32 = 0;
+  d.sh1 = d.sh2 = 0;
+  if (d.d32) {
+    const unsigned long long ud = (unsigned long long)den;
+    const int l = ud <= 1 ? 0 : 64 - __clzll((long long)(ud - 1));  // ceil(log2 den), 0..32
+    d.m32 = (uint32_t)((((1ull << l) - ud) << 32) / ud + 1);        // (2^l - den) < den <= 2^32
+    d.sh1 = l < 1 ? l : 1;
+    d.sh2 = l > 1 ? l - 1 : 0;
+  }
   return d;
 }
+// floor(u / den) for den < 2^32 (the first path of udiv).
+__device__ __forceinline__ uint32_t div32(uint32_t u, const RoundDiv& d) {
+  const uint32_t t = __umulhi(d.m32, u);
+  return (t + ((u - t) >> d.sh1)) >> d.sh2;
+}
 __device__ __forceinline__ long long udiv(unsigned long long u, const RoundDiv& d) {
+  if (d.d32 && (u >> 32) == 0) return (long long)div32((uint32_t)u, d);
   if (u < (1ull << 52) && d.den < (1ll << 52)) {
     long long q = (long long)((double)u * d.rd);
     const long long r = (long long)u - q * d.den;
@@ -309,15 +337,13 @@ __device__ __forceinline__ long long udiv(unsigned long long u, const RoundDiv& 
   return (long long)(u / (unsigned long long)d.den);
 }
 __device__ __forceinline__ bool round_div(long long num, const RoundDiv& d, long long& out) {
-  if (num >= 0) {
-    if (num > LLONG_MAX - d.half) return false;
-    out = udiv((unsigned long long)(num + d.half), d);
-  } else {
-    if (num == LLONG_MIN) return false;
-    const long long m = -num;
-    if (m > LLONG_MAX - d.half) return false;
-    out = -udiv((unsigned long long)(m + d.half), d);
-  }
+  // one quotient for either sign: rounding half away from zero is the
+  // magnitude's rounding with the sign put back
+  if (num == LLONG_MIN) return false;
+  const long long m = num < 0 ? -num : num;
+  if (m > LLONG_MAX - d.half) return false;
+  const long long q = udiv((unsigned long long)(m + d.half), d);
+  out = num < 0 ? -q : q;
   return true;
 }
 
@@ -477,9 +503,163 @@ __device__ __forceinline__ bool adam_delta(long long g, const AdamRule& c, long 
   return true;
 }
 
+// Constants of the SGD rules for one segment: the divider, the learning
+// rate, the shift and the uniform conditions of the 32-bit fast path (a
+// 32-bit divisor and a shift in [0, 30]; bias = 2^(shift-1), or 0).
+struct SgdRule {
+  RoundDiv den;
+  int lr, shift, sh;
+  long long bias;
+  uint32_t half32;
+  bool fast;
+};
+__device__ __forceinline__ SgdRule sgd_rule(const RoundDiv& den, int lr, int shift) {
+  SgdRule c;
+  c.den = den;
+  c.lr = lr;
+  c.shift = shift;
+  c.fast = den.d32 && shift >= 0 && shift <= 30;
+  c.sh = shift & 31;
+  c.bias = c.sh ? (1ll << (c.sh - 1)) : 0;
+  c.half32 = (uint32_t)den.half;
+  return c;
+}
+
+// What sgd_element asks its caller to store, and whether the reference's
+// checked arithmetic failed.
+enum : int { SGD_RES = 1, SGD_W = 2, SGD_BAD = 4 };
+
+// One element of apply_linear_weight_gradient_i64_to_i8 (train-core
+// lib.rs:386-465) with the residual carried (i8), or of
+// apply_embedding_accumulators_i64_to_i16 (nsrl-train/src/lib.rs:14457-14510):
+// the new residual and weight and which of them to store.
+__device__ __forceinline__ int sgd_element(bool i8, long long raw, long long r0, int prev, const SgdRule& c,
+                                           long long& res_out, int& w_out, unsigned& sat, unsigned& zero,
+                                           unsigned long long& l1) {
+  // the i8 rule skips a zero gradient, the embedding rule only with a zero residual
+  if (raw == 0 && (i8 || r0 == 0)) return 0;
+  const long long lo = i8 ? -128 : -32768, hi = i8 ? 127 : 32767;
+  if (c.fast && (unsigned long long)(raw + (1ll << 30)) < (1ull << 31) &&
+      (unsigned long long)(r0 + (1ll << 31)) < (1ull << 32)) {
+    // |raw| <= 2^30 and r0 an i32: |avg| <= 2^30, |product| < 2^62, so no
+    // step can overflow, the rounding shift needs no saturation and the new
+    // residual (|.| <= 2^(shift-1)) is exact in 32 bits
+    const int rr = (int)raw;
+    const uint32_t m = rr < 0 ? 0u - (uint32_t)rr : (uint32_t)rr;
+    const int q = (int)div32(m + c.half32, c.den);
+    const long long product = (long long)(rr < 0 ? -q : q) * c.lr + r0;
+    const long long scaled = (product + c.bias) >> c.sh;
+    const int next_res = (int)((uint32_t)product - ((uint32_t)scaled << c.sh));
+    zero += scaled == 0;
+    const long long un = (long long)prev - scaled;
+    const int cl = (int)(un < lo ? lo : (un > hi ? hi : un));
+    const bool clipped = (long long)cl != un;
+    sat += clipped;
+    res_out = (i8 && clipped) ? 0 : (long long)next_res;  // the i8 rule drops a saturated weight's residual
+    l1 += (unsigned long long)abs(cl - prev);
+    w_out = cl;
+    return SGD_RES | SGD_W;
+  }
+  long long avg, product;
+  if (!round_div(raw, c.den, avg)) return SGD_BAD;
+  if (avg == (long long)(int)avg) {
+    product = (long long)(int)avg * (long long)c.lr;  // |.| < 2^62: no overflow
+  } else if (mul_ovf(avg, (long long)c.lr, product)) {
+    return SGD_BAD;
+  }
+  if (add_ovf(product, r0, product)) return SGD_BAD;
+  const long long scaled = rhu64(product, (uint32_t)c.shift);
+  // product - (scaled << shift) is exact: |.| <= 2^(shift-1)
+  const long long next_res =
+      c.shift ? (long long)((unsigned long long)product - ((unsigned long long)scaled << c.shift)) : 0;
+  if (scaled == 0) ++zero;
+  int out = 0;
+  if (!i8) {  // the embedding rule stores its residual before the weight's check
+    res_out = next_res;
+    out = SGD_RES;
+  }
+  long long un;
+  if (add_ovf((long long)prev, -scaled, un)) return out | SGD_BAD;
+  const int cl = (int)(un < lo ? lo : (un > hi ? hi : un));
+  const bool clipped = (long long)cl != un;
+  if (clipped) ++sat;
+  if (i8) res_out = clipped ? 0 : next_res;
+  l1 += (unsigned long long)abs(cl - prev);
+  w_out = cl;
+  return SGD_RES | SGD_W;
+}
+
+// One thread's elements of an SGD tile: entries k * APPLY_THREADS (k <
+// APPLY_PER, k * APPLY_THREADS < rem) of the arrays from the given pointers.
+// The loads of APPLY_BATCH elements are issued before any of their
+// arithmetic, so each thread has that many independent loads in flight, and
+// every access is at a constant offset from pointers bumped once per batch.
+template <bool I8>
+__device__ __forceinline__ void sgd_tile(const long long* __restrict__ psum, long long* __restrict__ pres,
+                                         typename std::conditional<I8, int8_t, int16_t>::type* __restrict__ pw,
+                                         int rem, const SgdRule& rule, unsigned& sat, unsigned& zero,
+                                         unsigned long long& l1, bool& bad) {
+#pragma unroll 1
+  for (int j0 = 0; j0 < APPLY_PER; j0 += APPLY_BATCH) {
+    long long rv[APPLY_BATCH], qv[APPLY_BATCH];
+    int pv[APPLY_BATCH];
+#pragma unroll
+    for (int j = 0; j < APPLY_BATCH; ++j) {
+      rv[j] = 0;
+      qv[j] = 0;
+      pv[j] = 0;
+      if (j * APPLY_THREADS < rem) {
+        rv[j] = __ldcs(psum + j * APPLY_THREADS);
+        qv[j] = pres[j * APPLY_THREADS];
+        pv[j] = (int)pw[j * APPLY_THREADS];
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < APPLY_BATCH; ++j) {
+      if (j * APPLY_THREADS >= rem) continue;
+      long long nres;
+      int nw;
+      const int r = sgd_element(I8, rv[j], qv[j], pv[j], rule, nres, nw, sat, zero, l1);
+      bad |= (r & SGD_BAD) != 0;
+      if (r & SGD_RES) pres[j * APPLY_THREADS] = nres;
+      if (r & SGD_W) pw[j * APPLY_THREADS] = (typename std::conditional<I8, int8_t, int16_t>::type)nw;
+    }
+    psum += APPLY_BATCH * APPLY_THREADS;
+    pres += APPLY_BATCH * APPLY_THREADS;
+    pw += APPLY_BATCH * APPLY_THREADS;
+    rem -= APPLY_BATCH * APPLY_THREADS;
+  }
+}
+
+// The SGD rules over arrays, one element per thread (nsrl_selftest_sgd_apply).
+__global__ void sgd_apply_selftest_kernel(const long long* __restrict__ raw, long long* __restrict__ res, void* w,
+                                          int i8, long long n, long long count, int lr, int shift,
+                                          unsigned long long* stats, unsigned char* bad) {
+  const SgdRule rule = sgd_rule(round_div_by(count), lr, shift);
+  unsigned sat = 0, zero = 0;
+  unsigned long long l1 = 0;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const int prev = i8 ? (int)static_cast<int8_t*>(w)[i] : (int)static_cast<int16_t*>(w)[i];
+    long long nres;
+    int nw;
+    const int r = sgd_element(i8 != 0, raw[i], res[i], prev, rule, nres, nw, sat, zero, l1);
+    if (r & SGD_BAD) *bad = 1;
+    if (r & SGD_RES) res[i] = nres;
+    if (r & SGD_W) {
+      if (i8)
+        static_cast<int8_t*>(w)[i] = (int8_t)nw;
+      else
+        static_cast<int16_t*>(w)[i] = (int16_t)nw;
+    }
+  }
+  if (sat) atomicAdd(&stats[0], (unsigned long long)sat);
+  if (zero) atomicAdd(&stats[1], (unsigned long long)zero);
+  if (l1) atomicAdd(&stats[2], l1);
+}
+
 // One launch applies every parameter: each block takes apply tiles, finds the
 // tile's segment and runs that segment's rule on up to APPLY_TILE elements.
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(APPLY_THREADS, 3)
     apply_kernel(const ApplyTable* __restrict__ tab, const long long* __restrict__ sum,
                  const unsigned long long* __restrict__ counts, const int* decision, const int* shifts, int lr,
                  AdamRule ac, long long* __restrict__ res, long long* __restrict__ m1,
@@ -487,89 +667,59 @@ __global__ void __launch_bounds__(256)
                  unsigned long long* stats, nsrl_device_status* st) {
   if (*decision != DEC_APPLY) return;
   if (adam_step && blockIdx.x == 0 && threadIdx.x == 0) atomicAdd(adam_step, 1ull);  // once per batch
-  __shared__ int s_seg;
-  unsigned long long sat = 0, zero = 0, l1 = 0;
+  // The segment table, each segment's divider constants and shift are set
+  // up once per block in shared memory, so a tile's set-up reads no global
+  // memory and the block streams its tiles back to back.
+  __shared__ ApplySeg s_seg[MAX_SEGS];
+  __shared__ RoundDiv s_div[MAX_SEGS];
+  __shared__ int s_shift[MAX_SEGS];
+  __shared__ unsigned char s_state[MAX_SEGS];  // 0 apply, 1 nothing accumulated, 2 count out of range
+  const int nseg = tab->nseg, ntiles = tab->ntiles;
+  for (int i = threadIdx.x; i < nseg; i += blockDim.x) {
+    const ApplySeg g = tab->seg[i];
+    s_seg[i] = g;
+    const unsigned long long count = counts[g.count_idx];
+    s_state[i] = count == 0 ? 1 : (count > (unsigned long long)LLONG_MAX ? 2 : 0);
+    s_div[i] = round_div_by(s_state[i] ? 1 : (long long)count);
+    s_shift[i] = g.shift_class >= 0 ? shifts[g.shift_class] : 0;
+  }
+  __syncthreads();
+  unsigned sat = 0, zero = 0;  // per thread at most 16 per tile it takes
+  unsigned long long l1 = 0;
   bool bad = false;
-  const int ntiles = tab->ntiles;
   for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      int lo = 0, hi = tab->nseg - 1;  // last segment with tile0 <= t
-      while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (tab->seg[mid].tile0 <= t) lo = mid;
-        else hi = mid - 1;
-      }
-      s_seg = lo;
+    int si = 0, hi = nseg - 1;  // last segment with tile0 <= t
+    while (si < hi) {
+      const int mid = (si + hi + 1) >> 1;
+      if (s_seg[mid].tile0 <= t)
+        si = mid;
+      else
+        hi = mid - 1;
     }
-    __syncthreads();
-    const ApplySeg sg = tab->seg[s_seg];
-    const unsigned long long count = counts[sg.count_idx];
-    if (count == 0) continue;  // nothing accumulated: weights and state untouched
-    if (count > (unsigned long long)LLONG_MAX) {
+    const ApplySeg& sg = s_seg[si];
+    if (s_state[si] == 1) continue;  // nothing accumulated: weights and state untouched
+    if (s_state[si] == 2) {
       bad = true;
       continue;
     }
-    const RoundDiv den = round_div_by((long long)count);
+    const RoundDiv den = s_div[si];
     const long long e0 = (long long)(t - sg.tile0) * APPLY_TILE;
     const long long e1 = min(sg.len, e0 + APPLY_TILE);
-    const int shift = sg.shift_class >= 0 ? shifts[sg.shift_class] : 0;
-    for (long long e = e0 + threadIdx.x; e < e1; e += blockDim.x) {
-      const long long a = sg.off + e;
-      const long long raw = sum[a];
-      if (sg.kind == SEG_SGD_I8) {
-        // apply_linear_weight_gradient_i64_to_i8 (train-core lib.rs:386-465), residual carried
-        if (raw == 0) continue;
-        long long avg, product;
-        if (!round_div(raw, den, avg) || mul_ovf(avg, (long long)lr, product) || add_ovf(product, res[a], product)) {
-          bad = true;
-          continue;
-        }
-        const long long scaled = rhu64(product, (uint32_t)shift);
-        // product - (scaled << shift) is exact: |.| <= 2^(shift-1)
-        const long long next_res =
-            shift ? (long long)((unsigned long long)product - ((unsigned long long)scaled << shift)) : 0;
-        if (scaled == 0) ++zero;
-        int8_t* w = static_cast<int8_t*>(sg.w);
-        const int prev = w[e];
-        long long un;
-        if (add_ovf((long long)prev, -scaled, un)) {
-          bad = true;
-          continue;
-        }
-        const int cl = (int)sat_i8(un);
-        if ((long long)cl != un) {
-          ++sat;
-          res[a] = 0;
-        } else {
-          res[a] = next_res;
-        }
-        l1 += (unsigned long long)abs(cl - prev);
-        w[e] = (int8_t)cl;
-      } else if (sg.kind == SEG_SGD_EMB_I16) {
-        // apply_embedding_accumulators_i64_to_i16 (nsrl-train/src/lib.rs:14457-14510)
-        const long long r0 = res[a];
-        if (raw == 0 && r0 == 0) continue;
-        long long avg, product;
-        if (!round_div(raw, den, avg) || mul_ovf(avg, (long long)lr, product) || add_ovf(product, r0, product)) {
-          bad = true;
-          continue;
-        }
-        const long long scaled = rhu64(product, (uint32_t)shift);
-        res[a] = shift ? (long long)((unsigned long long)product - ((unsigned long long)scaled << shift)) : 0;
-        if (scaled == 0) ++zero;
-        int16_t* w = static_cast<int16_t*>(sg.w);
-        const int prev = w[e];
-        long long un;
-        if (add_ovf((long long)prev, -scaled, un)) {
-          bad = true;
-          continue;
-        }
-        const int cl = (int)sat_i16(un);
-        if ((long long)cl != un) ++sat;
-        l1 += (unsigned long long)abs(cl - prev);
-        w[e] = (int16_t)cl;
-      } else {
+    const int shift = s_shift[si];
+    if (sg.kind == SEG_SGD_I8 || sg.kind == SEG_SGD_EMB_I16) {
+      const SgdRule rule = sgd_rule(den, lr, shift);
+      const long long first = e0 + threadIdx.x;  // this thread's elements: first + k * APPLY_THREADS
+      const int rem = (int)(e1 - first);          // <= APPLY_TILE
+      if (sg.kind == SEG_SGD_I8)
+        sgd_tile<true>(sum + sg.off + first, res + sg.off + first, static_cast<int8_t*>(sg.w) + first, rem, rule,
+                       sat, zero, l1, bad);
+      else
+        sgd_tile<false>(sum + sg.off + first, res + sg.off + first, static_cast<int16_t*>(sg.w) + first, rem, rule,
+                        sat, zero, l1, bad);
+    } else {
+      for (long long e = e0 + threadIdx.x; e < e1; e += blockDim.x) {
+        const long long a = sg.off + e;
+        const long long raw = sum[a];
         // apply_integer_adam_accumulators_i64_to_i8 / _i16 (train-core lib.rs:469-593)
         const long long k = sg.state_off + e;
         long long g, f = m1[k], r = ares[k], delta;
@@ -612,8 +762,8 @@ __global__ void __launch_bounds__(256)
     l1 += __shfl_xor_sync(0xffffffffu, l1, o);
   }
   if ((threadIdx.x & 31) == 0) {
-    if (sat) atomicAdd(&stats[0], sat);
-    if (zero) atomicAdd(&stats[1], zero);
+    if (sat) atomicAdd(&stats[0], (unsigned long long)sat);
+    if (zero) atomicAdd(&stats[1], (unsigned long long)zero);
     if (l1) atomicAdd(&stats[2], l1);
   }
 }
@@ -664,6 +814,22 @@ size_t adam_len(const nsrl_train_model* m) {
 // v o [d][d], up gate [F][d], down [d][F], rms attention [d], rms mlp [d];
 // token embeddings [256][d]; positions [S][d].  Counts: head, 9 per layer,
 // embeddings.
+// Algorithmic bytes of one apply over the table: the i64 gradient sum read
+// once, then per kind the residual (SGD) or the three Adam state words read
+// and written, and the weight read and written.
+double apply_bytes(const ApplyTable& tab) {
+  double b = 0;
+  for (int i = 0; i < tab.nseg; ++i) {
+    const ApplySeg& g = tab.seg[i];
+    const int per = g.kind == SEG_SGD_I8 ? 8 + 16 + 2
+                    : g.kind == SEG_SGD_EMB_I16 ? 8 + 16 + 4
+                    : g.kind == SEG_ADAM_I8 ? 8 + 48 + 2
+                                            : 8 + 48 + 4;
+    b += (double)per * (double)g.len;
+  }
+  return b;
+}
+
 bool build_table(const nsrl_train_model* m, const nsrl_train_config* cfg, ApplyTable& tab) {
   const size_t d = m->d_model, F = m->hidden_dim, L = m->layers, S = m->seq_len;
   const size_t per_layer = 4 * d * d + 3 * F * d + 2 * d;
@@ -899,6 +1065,23 @@ nsrl_status nsrl_selftest_round_div(const long long* num, size_t n, long long de
   return NSRL_CUDA_ERROR;
 }
 
+nsrl_status nsrl_selftest_sgd_apply(const long long* sums, long long* residuals, void* weights, int weights_i8,
+                                    size_t n, unsigned long long count, int learning_rate, int shift,
+                                    unsigned long long* stats, unsigned char* bad, void* stream) {
+  if (!sums || !residuals || !weights || !stats || !bad || count == 0 || count > (unsigned long long)LLONG_MAX) {
+    set_error("nsrl_selftest_sgd_apply: NULL argument or count outside [1, 2^63)");
+    return NSRL_INVALID_SHAPE;
+  }
+  if (n == 0) return NSRL_OK;
+  const unsigned blocks = (unsigned)std::min<size_t>((n + 255) / 256, 148 * 8);
+  sgd_apply_selftest_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(
+      sums, residuals, weights, weights_i8, (long long)n, (long long)count, learning_rate, shift, stats, bad);
+  const cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) return NSRL_OK;
+  set_error("sgd apply selftest: %s", cudaGetErrorString(e));
+  return NSRL_CUDA_ERROR;
+}
+
 nsrl_status nsrl_merge_worker_parts_i64(const long long* parts, size_t workers, size_t checked_len, size_t len,
                                         long long* out, nsrl_device_status* status, void* stream) {
   if (!parts || !out || !status || workers == 0 || checked_len > len || workers > (size_t)INT32_MAX)
@@ -1017,10 +1200,10 @@ nsrl_status nsrl_train_dp_step(const nsrl_train_model* m, const uint8_t* context
                       (int)m->layers};
   const AdamRule arule{cfg->adam.learning_rate, cfg->adam.step_shift, cfg->adam.beta1_decay_shift,
                        cfg->adam.beta2_decay_shift, cfg->adam.epsilon};
-  const unsigned apply_blocks = (unsigned)std::max(1, std::min(tab.ntiles, 148 * 4));
+  const unsigned apply_blocks = (unsigned)std::max(1, std::min(tab.ntiles, 148 * 3));  // 3 resident per SM
   auto launch_apply = [&]() -> nsrl_status {
-    ProfScope prof("dp_apply", s, 0.0, 34.0 * (double)n_arena);
-    apply_kernel<<<apply_blocks, 256, 0, s>>>(dtab, sum, sum_counts, decision, shifts, cfg->learning_rate, arule,
+    ProfScope prof("dp_apply", s, 0.0, apply_bytes(tab));
+    apply_kernel<<<apply_blocks, APPLY_THREADS, 0, s>>>(dtab, sum, sum_counts, decision, shifts, cfg->learning_rate, arule,
                                               state->residuals, state->adam_first_moments,
                                               state->adam_second_moments, state->adam_update_residuals,
                                               adam ? state->adam_step : nullptr, stats3, status);

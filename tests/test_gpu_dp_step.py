@@ -163,10 +163,11 @@ def test_average_batch_movement(dtype, divisor):
 
 
 def test_apply_divider_matches_integer_division():
-    """The apply's divider (a double reciprocal of the count with one exact
-    integer correction below 2^52, integer division above) against Python's
-    exact round-half-away-from-zero division, at the edges: halves, the 2^52
-    boundary, i64 extremes, counts of 1, 3, 7, 2^31 - 1 and near 2^52."""
+    """The apply's divider (a 32-bit multiply-shift below 2^32, a double
+    reciprocal of the count with one exact integer correction below 2^52,
+    integer division above) against Python's exact round-half-away-from-zero
+    division, at the edges: halves, the 2^32 and 2^52 boundaries, i64
+    extremes, counts on both sides of 2^32 and 2^52."""
     import ctypes as C
     from nsrl_b200 import core
     T = _train()
@@ -184,9 +185,13 @@ def test_apply_divider_matches_integer_division():
         q = (m + half) // d
         return q if n >= 0 else -q
 
-    for den in (1, 2, 3, 7, 1000, (1 << 31) - 1, (1 << 52) - 1, 1 << 52, (1 << 60) + 7):
+    # dens on both sides of 2^32 (the 32-bit multiply-shift path) and 2^52 (the double path)
+    for den in (1, 2, 3, 7, 255, 256, 1000, 65537, (1 << 31) - 1, (1 << 32) - 1, 1 << 32, (1 << 32) + 1,
+                (1 << 52) - 1, 1 << 52, (1 << 60) + 7):
         nums = list(edge)
         nums += [k * den + den // 2 + o for k in (0, 1, 5, 12345) for o in (-1, 0, 1) if abs(k * den) < (1 << 62)]
+        nums += [(1 << 32) - 1 - den // 2 + o for o in (-1, 0, 1)] + [-((1 << 32) - 1 - den // 2) + o for o in (-1, 0, 1)]
+        nums += list(rng.integers(-(1 << 32), 1 << 32, 2000))
         nums += list(rng.integers(-(1 << 53), 1 << 53, 2000))
         nums += list(rng.integers(-(1 << 62), 1 << 62, 2000))
         a = np.array(nums, dtype=np.int64)
@@ -201,3 +206,94 @@ def test_apply_divider_matches_integer_division():
             assert (r is None) == (good[i] == 0), (n, den)
             if r is not None:
                 assert int(got[i]) == r, (n, den, int(got[i]), r)
+
+
+def _sgd_values(rng, n, big):
+    """Gradient sums and residuals on both sides of the fast path's limits
+    (|sum| <= 2^30, residual an i32), up to 2^40 when big."""
+    edge = [0, 1, -1, (1 << 30) - 1, 1 << 30, (1 << 30) + 1, -(1 << 30), -(1 << 30) - 1]
+    raw = rng.integers(-(1 << 24), 1 << 24, n)
+    raw[: len(edge)] = edge
+    raw[::11] = 0
+    if big:
+        raw[1::5] = rng.integers(-(1 << 40), 1 << 40, len(raw[1::5]))
+    res = rng.integers(-(1 << 12), 1 << 12, n)
+    res[::3] = 0
+    if big:
+        res[2::7] = rng.integers(-(1 << 40), 1 << 40, len(res[2::7]))
+        res[3::13] = [(1 << 31) - 1, 1 << 31, -(1 << 31), -(1 << 31) - 1] * (len(res[3::13]) // 4) + \
+            [1 << 31] * (len(res[3::13]) % 4)
+    return raw.astype(np.int64), res.astype(np.int64)
+
+
+@pytest.mark.parametrize("i8", [True, False])
+@pytest.mark.parametrize("count,lr,shift", [(1, 1, 0), (3, 1, 7), (256, 3, 12), (255, 1, 30), (7, 5, 31),
+                                            ((1 << 32) - 1, 1, 3), ((1 << 32) + 5, 1 << 20, 9), (9, 1, 45)])
+@pytest.mark.parametrize("big", [False, True])
+def test_sgd_apply_rule_matches_oracle(i8, count, lr, shift, big):
+    """The element rule of the data-parallel apply's SGD segments (its 32-bit
+    fast path and the checked 64-bit path) against the oracle's i8 apply with
+    the residual carried and its i16 embedding apply: residuals, weights and
+    the three statistics."""
+    import ctypes as C
+    from nsrl_b200 import core
+    T = _train()
+    L = T._lib_dp()
+    L.nsrl_selftest_sgd_apply.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_size_t, C.c_ulonglong,
+                                          C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]
+    n = 20000
+    rng = np.random.default_rng(count % 1000 + 31 * shift + 7 * lr + (5 if big else 0) + (1 if i8 else 0))
+    raw, res = _sgd_values(rng, n, big)
+    w = rng.integers(-128, 128, n).astype(np.int8) if i8 else rng.integers(-32768, 32768, n).astype(np.int16)
+    if i8:
+        ref = O.apply_linear_gradient_i64_to_i8(raw, res, w, count, lr, shift, True)
+        assert ref is not None
+        ref_res, ref_w, ref_stats = ref[1], ref[2], ref[4]
+    else:
+        ref_res, ref_w, st = res.copy(), w.copy(), np.zeros(3, np.uint64)
+        assert O.apply_embedding_gradient_i64_to_i16(raw.copy(), ref_res, ref_w, count, lr, shift, st)
+        ref_stats = [int(x) for x in st]
+    g_raw, g_res, g_w = (torch.from_numpy(a.copy()).cuda() for a in (raw, res, w))
+    stats = torch.zeros(3, dtype=torch.int64, device="cuda")
+    bad = torch.zeros(1, dtype=torch.uint8, device="cuda")
+    assert L.nsrl_selftest_sgd_apply(core._ptr(g_raw), core._ptr(g_res), core._ptr(g_w), int(i8), n, count, lr, shift,
+                                     core._ptr(stats), core._ptr(bad), core._stream()) == core.NSRL_OK
+    assert int(bad.item()) == 0
+    assert np.array_equal(g_res.cpu().numpy(), ref_res)
+    assert np.array_equal(g_w.cpu().numpy(), ref_w)
+    assert [int(x) for x in stats.cpu().numpy()] == ref_stats
+
+
+@pytest.mark.parametrize("i8", [True, False])
+@pytest.mark.parametrize("case", ["sum_min", "product", "residual_add"])
+def test_sgd_apply_rule_flags_overflow(i8, case):
+    """One element whose checked arithmetic fails among ordinary ones: the
+    oracle rejects the apply and the element rule reports it."""
+    import ctypes as C
+    from nsrl_b200 import core
+    T = _train()
+    L = T._lib_dp()
+    L.nsrl_selftest_sgd_apply.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_size_t, C.c_ulonglong,
+                                          C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]
+    n = 1000
+    rng = np.random.default_rng(3)
+    raw, res = _sgd_values(rng, n, False)
+    lr = 1
+    if case == "sum_min":
+        raw[500] = -(1 << 63)
+    elif case == "product":
+        raw[500], lr = (1 << 62) - 5, 4
+    else:
+        raw[500], res[500] = (1 << 62), (1 << 62)
+    w = rng.integers(-100, 100, n).astype(np.int8) if i8 else rng.integers(-1000, 1000, n).astype(np.int16)
+    if i8:
+        assert O.apply_linear_gradient_i64_to_i8(raw, res, w, 1, lr, 5, True) is None
+    else:
+        assert not O.apply_embedding_gradient_i64_to_i16(raw.copy(), res.copy(), w.copy(), 1, lr, 5,
+                                                         np.zeros(3, np.uint64))
+    g_raw, g_res, g_w = (torch.from_numpy(a.copy()).cuda() for a in (raw, res, w))
+    stats = torch.zeros(3, dtype=torch.int64, device="cuda")
+    bad = torch.zeros(1, dtype=torch.uint8, device="cuda")
+    assert L.nsrl_selftest_sgd_apply(core._ptr(g_raw), core._ptr(g_res), core._ptr(g_w), int(i8), n, 1, lr, 5,
+                                     core._ptr(stats), core._ptr(bad), core._stream()) == core.NSRL_OK
+    assert int(bad.item()) == 1
