@@ -200,8 +200,8 @@ __device__ __forceinline__ uint32_t shr_clamp(uint32_t x, uint32_t s) {
   return r;
 }
 
-__device__ __forceinline__ int max3i(int a, int b, int c) { return max(max(a, b), c); }
-__device__ __forceinline__ int min3i(int a, int b, int c) { return min(min(a, b), c); }
+__device__ __forceinline__ int max3i(int a, int b, int c) { return __vimax3_s32(a, b, c); }
+__device__ __forceinline__ int min3i(int a, int b, int c) { return __vimin3_s32(a, b, c); }
 __device__ __forceinline__ int max16(const int (&v)[16]) {
   const int a = max3i(v[0], v[1], v[2]), b = max3i(v[3], v[4], v[5]), c = max3i(v[6], v[7], v[8]);
   const int d = max3i(v[9], v[10], v[11]), e = max3i(v[12], v[13], v[14]);
@@ -211,11 +211,6 @@ __device__ __forceinline__ int min16(const int (&v)[16]) {
   const int a = min3i(v[0], v[1], v[2]), b = min3i(v[3], v[4], v[5]), c = min3i(v[6], v[7], v[8]);
   const int d = min3i(v[9], v[10], v[11]), e = min3i(v[12], v[13], v[14]);
   return min(min3i(a, b, c), min3i(d, e, v[15]));
-}
-__device__ __forceinline__ uint32_t sum16(const uint32_t (&v)[16]) {
-  const uint32_t a = v[0] + v[1] + v[2], b = v[3] + v[4] + v[5], c = v[6] + v[7] + v[8];
-  const uint32_t d = v[9] + v[10] + v[11], e = v[12] + v[13] + v[14];
-  return (a + b + c) + (d + e + v[15]);
 }
 
 // Pass 0 on one S tile of a warp (32 rows x 16 keys).  When every hh of the
@@ -243,6 +238,35 @@ __device__ __forceinline__ void tile_max(const uint32_t (&hh)[16], const uint32_
   } else {
     scores_max<FULL>(hh, mid, ll, nlive, mx32, mx64, mn64);
   }
+}
+
+// Pass 0 on one S tile of a warp whose rows all have L1(q_hi) <= 128, so
+// |hh| <= 128 * 128 and every raw value is an exact i32 without a range check.
+template <bool FULL>
+__device__ __forceinline__ void tile_max_bounded(const uint32_t (&hh)[16], const uint32_t (&mid)[16],
+                                                 const uint32_t (&ll)[16], int nlive, int& mx32) {
+  int r[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int raw = (int)(hh[i] * 65536u + mid[i] * 256u + ll[i]);
+    r[i] = (FULL || i < nlive) ? raw : INT_MIN;
+  }
+  mx32 = max(mx32, max16(r));
+}
+
+// Per 16-bit half min of two packed unsigned pairs.
+__device__ __forceinline__ uint32_t min_u16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("min.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// Sum of the absolute values of the 16 signed bytes of v.
+__device__ __forceinline__ uint32_t abs_sum16(const uint4 v) {
+  uint32_t s = __dp4a(__vabs4(v.x), 0x01010101u, 0u);  // __vabs4(-128) = 0x80: 128 as a byte sum term
+  s = __dp4a(__vabs4(v.y), 0x01010101u, s);
+  s = __dp4a(__vabs4(v.z), 0x01010101u, s);
+  return __dp4a(__vabs4(v.w), 0x01010101u, s);
 }
 
 // Pass-1 weights of a warp whose 32 rows all have exact i32 raw values
@@ -508,6 +532,23 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
     };
     auto live_keys = [&](int j) { return max(0, min(16, last_key - (j * KT + 16 * g) + 1)); };
 
+    // |hh| = |sum q_hi k_hi| <= L1(q_hi) * 128 for any key, so a warp whose
+    // rows all have L1(q_hi) <= 128 skips the per-tile range check of hh.
+    // (Head dim 16: the head's 16 bytes are the row's logical chunk 0.)
+    bool qbounded;
+    {
+      wait_bar(&ctl->q_full, 0, ctl, a.st);
+      uint32_t l1 = 0;
+      if (HDIM < 32) {
+        l1 = abs_sum16(*reinterpret_cast<const uint4*>(sm + OFF_Q + swz32_chunk((uint32_t)row, 0u)));
+      } else {
+#pragma unroll
+        for (int c = 0; c < Hd::ROW / 16; ++c)  // the swizzle permutes chunks within the row
+          l1 += abs_sum16(*reinterpret_cast<const uint4*>(sm + OFF_Q + row * Hd::ROW + 16 * c));
+      }
+      qbounded = __all_sync(FULLMASK, l1 <= 128u);
+    }
+
     // ---- pass 0: row max of raw = q.k ----
     // With head_dim 64 |256*mid + ll| <= B_MID (< 2^30), so raw is an exact
     // i32 whenever |hh| <= 16384 (mx32); other elements take an i64 path that
@@ -519,10 +560,17 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
       uint32_t hh[16], mid[16], ll[16];
       fetch_s((int)(it & 1), hh, mid, ll);
       const int nlive = live_keys(j);
-      if (__all_sync(FULLMASK, nlive == 16))
+      const bool full = __all_sync(FULLMASK, nlive == 16);
+      if (qbounded) {
+        if (full)
+          tile_max_bounded<true>(hh, mid, ll, nlive, mx32);
+        else
+          tile_max_bounded<false>(hh, mid, ll, nlive, mx32);
+      } else if (full) {
         tile_max<true>(hh, mid, ll, nlive, mx32, mx64, mn64);
-      else
+      } else {
         tile_max<false>(hh, mid, ll, nlive, mx32, mx64, mn64);
+      }
     }
     // Per-row constants of passes 1 and 2.
     uint32_t rawmax_lo = 0, cround = 0;
@@ -609,18 +657,21 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
       uint32_t hh[16], mid[16], ll[16], w[16];
       fetch_s((int)(it & 1), hh, mid, ll);
       weights(hh, mid, ll, live_keys(j), w);
-      rsum += sum16(w);
+      // weights are below 2^15: pairs packed as 16-bit halves for the store,
+      // and each pair added to the row sum by one dp2a (lo * 1 + hi * 1)
+      uint32_t wp[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        wp[i] = __byte_perm(w[2 * i], w[2 * i + 1], 0x5410);
+        rsum = __dp2a_lo(wp[i], 0x0101u, rsum);
+      }
       uint8_t* tb = wst + (j % 3) * (QT * 64);
       if (j >= 3) {
         if (lane == 0) bulk_wait_read<2>();
         __syncwarp();
       }
-      *reinterpret_cast<uint4*>(tb + c0) =
-          make_uint4(__byte_perm(w[0], w[1], 0x5410), __byte_perm(w[2], w[3], 0x5410),
-                     __byte_perm(w[4], w[5], 0x5410), __byte_perm(w[6], w[7], 0x5410));
-      *reinterpret_cast<uint4*>(tb + c1) =
-          make_uint4(__byte_perm(w[8], w[9], 0x5410), __byte_perm(w[10], w[11], 0x5410),
-                     __byte_perm(w[12], w[13], 0x5410), __byte_perm(w[14], w[15], 0x5410));
+      *reinterpret_cast<uint4*>(tb + c0) = make_uint4(wp[0], wp[1], wp[2], wp[3]);
+      *reinterpret_cast<uint4*>(tb + c1) = make_uint4(wp[4], wp[5], wp[6], wp[7]);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
@@ -662,13 +713,15 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
         w[2 * i] = wv[i] & 0xFFFFu;
         w[2 * i + 1] = wv[i] >> 16;
       }
-      // w * inv + 2^15 < 2^47 + 2^15, so the value shifted by 16 fits in 32 bits
+      // w <= sum(w) and inv <= 2^31 * (129/128) / sum(w), so rhu(w * inv, 16)
+      // <= 33025 < 2^16: two of them pack into 16-bit halves before the
+      // saturation to 32767, which is one packed min per pair
       uint32_t pw[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const uint32_t p0 = min((uint32_t)(((unsigned long long)w[2 * i] * inv + 32768ull) >> 16), 32767u);
-        const uint32_t p1 = min((uint32_t)(((unsigned long long)w[2 * i + 1] * inv + 32768ull) >> 16), 32767u);
-        pw[i] = __byte_perm(p0, p1, 0x5410);
+        const uint32_t p0 = (uint32_t)(((unsigned long long)w[2 * i] * inv + 32768ull) >> 16);
+        const uint32_t p1 = (uint32_t)(((unsigned long long)w[2 * i + 1] * inv + 32768ull) >> 16);
+        pw[i] = min_u16x2(__byte_perm(p0, p1, 0x5410), 0x7FFF7FFFu);
       }
       if (a.probs && row_live && key0 < S) {  // nsrl-train/src/lib.rs:15353-15418: the cached P
         uint4* dst = reinterpret_cast<uint4*>(a.probs + (((long long)b * a.H + h) * S + qi) * (long long)S + key0);
