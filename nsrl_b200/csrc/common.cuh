@@ -143,6 +143,23 @@ __device__ __forceinline__ int sat16(int v) {
   return (int)r;
 }
 
+// sat_i16(hi) in the upper 16 bits and sat_i16(lo) in the lower, one instruction.
+__device__ __forceinline__ uint32_t pack_sat16(int hi, int lo) {
+  uint32_t d;
+  asm("cvt.pack.sat.s16.s32 %0, %1, %2;" : "=r"(d) : "r"(hi), "r"(lo));
+  return d;
+}
+
+// rhu(p * m, 30) = (p * m + 2^29) >> 30 for a result inside i32 (|p * m| <
+// 2^61): one widening multiply-add and a funnel shift of its two words.
+__device__ __forceinline__ int rhu30_mul(int p, int m) {
+  long long t;
+  asm("mad.wide.s32 %0, %1, %2, %3;" : "=l"(t) : "r"(p), "r"(m), "l"(1ll << 29));
+  uint32_t r;
+  asm("shf.r.wrap.b32 %0, %1, %2, 30;" : "=r"(r) : "r"((uint32_t)t), "r"((uint32_t)(t >> 32)));
+  return (int)r;
+}
+
 // mlp.rs:150-170: hard-SiLU gate and the gated activation.  For an i16 gate
 // g, (g >> 2) + 16384 lies in [8192, 24575], so the clamp to [0, 32767] never
 // acts; |g * gate| and |up * silu| stay below 32768 * 24575 < 2^30, so

@@ -107,9 +107,17 @@ __global__ void __launch_bounds__(256, VPL >= 4 ? 2 : 3) rms_norm_reg_kernel(
   const int lane = threadIdx.x & 31;
   const long long warp0 = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const long long nwarps = (long long)gridDim.x * (blockDim.x >> 5);
-  uint4 gv[VPL];
+  int gs[VPL][8];  // this lane's gamma values, sign-extended once
 #pragma unroll
-  for (int v = 0; v < VPL; ++v) gv[v] = reinterpret_cast<const uint4*>(g)[v * 32 + lane];
+  for (int v = 0; v < VPL; ++v) {
+    const uint4 g4 = reinterpret_cast<const uint4*>(g)[v * 32 + lane];
+    const uint32_t gw[4] = {g4.x, g4.y, g4.z, g4.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      gs[v][2 * k] = (int)(int16_t)(gw[k] & 0xFFFFu);
+      gs[v][2 * k + 1] = (int)gw[k] >> 16;
+    }
+  }
   // rows of the group starting at r0 (a ragged last group re-reads the last row)
   auto load_group = [&](long long r0, uint4(&xv)[RPW][VPL]) {
 #pragma unroll
@@ -164,17 +172,16 @@ __global__ void __launch_bounds__(256, VPL >= 4 ? 2 : 3) rms_norm_reg_kernel(
 #pragma unroll
       for (int v = 0; v < VPL; ++v) {
         const uint32_t xw[4] = {xv[rr][v].x, xv[rr][v].y, xv[rr][v].z, xv[rr][v].w};
-        const uint32_t gw[4] = {gv[v].x, gv[v].y, gv[v].z, gv[v].w};
         uint32_t pk[4];
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          // sat_i16(rhu(x * g * inv, 30)) with |x * g| <= 2^30, 0 <= inv < 2^30
-          const int p0 = (int)(int16_t)(xw[k] & 0xFFFFu) * (int)(int16_t)(gw[k] & 0xFFFFu);
-          const int p1 = ((int)xw[k] >> 16) * ((int)gw[k] >> 16);
-          const int o0 = sat16((int)(((long long)p0 * inv + (1ll << 29)) >> 30));
-          const int o1 = sat16((int)(((long long)p1 * inv + (1ll << 29)) >> 30));
-          l1 += (unsigned)(abs(o0) + abs(o1));
-          pk[k] = __byte_perm((uint32_t)o0, (uint32_t)o1, 0x5410);
+          // sat_i16(rhu(x * g * inv, 30)) with |x * g| <= 2^30, 0 <= inv < 2^30,
+          // two values saturated and packed by one instruction; the row L1
+          // adds the packed pair's absolute values (|-32768| = 0x8000)
+          const int p0 = (int)(int16_t)(xw[k] & 0xFFFFu) * gs[v][2 * k];
+          const int p1 = ((int)xw[k] >> 16) * gs[v][2 * k + 1];
+          pk[k] = pack_sat16(rhu30_mul(p1, inv), rhu30_mul(p0, inv));
+          l1 = __dp2a_lo(__vabs2(pk[k]), 0x0101u, l1);
         }
         if (r < rows) {
           if (y) __stcs(reinterpret_cast<uint4*>(y + r * D) + v * 32 + lane, make_uint4(pk[0], pk[1], pk[2], pk[3]));
