@@ -1033,14 +1033,16 @@ cudaError_t launch_attention_backward_tc(const int16_t* q, const int16_t* k, con
       e = launch_split_causal(P, B * H, S, pth, ptl, s);
       if (e != cudaSuccess) return e;
     }
-    {
+    e = launch_attention_bwd_dl_tc(Planes{cth, ctl, nullptr, d}, vp, pp, lth, ltl, B, S, d, H, st, s);
+    if (e == cudaErrorNotSupported) {  // plane buffers the tensor maps cannot describe: the mma.sync kernel
+      (void)cudaGetLastError();
       DlArgs la{dC, (long long)ldc, vp.hi, vp.lo, (int)vp.ld, nullptr, (int)S, (int)H, nullptr, st, pp.hi, pp.lo, lth, ltl};
       ProfScope prof("attention_bwd_dl", s, 2.0 * (double)hd * pairs,
                      2.0 * 2.0 * (double)B * H * S * S + 4.0 * (double)B * S * d);
       attn_bwd_dl_kernel<64, true><<<dim3((unsigned)((S + BQ - 1) / BQ), (unsigned)H, (unsigned)B), 128, 0, s>>>(la);
       e = cudaGetLastError();
-      if (e != cudaSuccess) return e;
     }
+    if (e != cudaSuccess) return e;
     return launch_attention_kv_tc(Planes{lth, ltl, nullptr, S}, pp, qp, Planes{cth, ctl, nullptr, d}, B, S, d, H,
                                   planes ? nullptr : dk,
                                   planes ? nullptr : dv, planes ? planes[1] : GradPlanes{},

@@ -206,6 +206,14 @@ cudaError_t launch_attention_backward_tc(const int16_t* q, const int16_t* k, con
 // prescaled planes.
 bool attention_kv_tc_supported(size_t S, size_t d, size_t H);
 cudaError_t launch_split_causal(const int16_t* M, size_t BH, size_t S, int8_t* hi, uint8_t* lo, cudaStream_t s);
+// dL of the softmax-attention backward on the tensor cores (head_dim 64,
+// S % 16 == 0): dC and V as row-major planes [B*S][d], P as causal planes
+// [B*H][S][S]; dL written as causal planes [B*H][S][S] (zeros above the
+// diagonal up to the end of each row's 128-key block).  cudaErrorNotSupported
+// for other shapes.
+cudaError_t launch_attention_bwd_dl_tc(const Planes& cp, const Planes& vp, const Planes& pp, int8_t* l_hi,
+                                       uint8_t* l_lo, size_t B, size_t S, size_t d, size_t H,
+                                       nsrl_device_status* st, cudaStream_t s);
 cudaError_t launch_attention_kv_tc(const Planes& l, const Planes& p, const Planes& qp, const Planes& cp, size_t B,
                                    size_t S, size_t d, size_t H, int16_t* dk, int16_t* dv, const GradPlanes& gk,
                                    const GradPlanes& gv, nsrl_device_status* st, cudaStream_t s,

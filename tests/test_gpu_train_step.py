@@ -100,8 +100,11 @@ def test_rms_norm_backward(T, d, eps):
     assert sat == ref[2]
 
 
+# (40, 272, 128, 2): 240 query tiles of the tensor-core dL kernel, more than one per SM,
+# with S past a multiple of 128 and of 64
 @pytest.mark.parametrize("B,S,d,H", [(2, 33, 64, 4), (3, 64, 128, 2), (1, 200, 64, 1), (2, 48, 64, 4),
-                                     (1, 520, 128, 2), (2, 4, 64, 1), (2, 256, 256, 4), (1, 528, 128, 2)])
+                                     (1, 520, 128, 2), (2, 4, 64, 1), (2, 256, 256, 4), (1, 528, 128, 2),
+                                     (40, 272, 128, 2)])
 def test_attention_probabilities_and_backward(B, S, d, H):
     _, train = _core()
     rng = np.random.default_rng(B * S)
