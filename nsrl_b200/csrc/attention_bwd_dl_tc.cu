@@ -19,7 +19,7 @@
 // (sequence, head), the tiles with the most keys first.  18 warps:
 //   warp 0     TMA producer: the dC planes of an item (double-buffered), then
 //              per 64-key tile and pass the V planes (4-stage ring) and the P
-//              planes (3-stage ring)
+//              planes (5-stage ring)
 //   warp 1     TMEM allocator + MMA issuer: per tile eight K = 32 MMAs into
 //              one of two dP buffers of 3 x 64 columns
 //   warps 2-17 warp w owns query rows 32 (w % 4) .. +31 (its TMEM lane
@@ -41,7 +41,7 @@ constexpr int DKT = 64;   // keys per tile (MMA N)
 constexpr int DHD = 64;   // head dim (MMA K, two K = 32 steps)
 constexpr int DL_WARPS = 16;
 constexpr int DTHREADS = 64 + 32 * DL_WARPS;  // 576
-constexpr int VST = 4, PST = 3;                // V and P rings
+constexpr int VST = 4, PST = 5;                // V and P rings
 constexpr int PLANE_C = DQT * DHD;             // 8 KB: [128 rows][64 dims]
 constexpr int PLANE_V = DKT * DHD;             // 4 KB: [64 keys][64 dims]
 constexpr int PLANE_P = DQT * DKT;             // 8 KB: [128 rows][64 keys]
