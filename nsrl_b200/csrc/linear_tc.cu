@@ -53,6 +53,50 @@ struct TcMaps {
   CUtensorMap a_hi, a_lo, b[3];
 };
 
+// ---------------------------------------------------------------------------
+// Exact i32 prefix check (linear.rs:282-296): for rows where
+// |bias| + 127 * L1(x_row) can exceed i32::MAX, rescan every output in the
+// reference's order (bias first, then k = 0, 1, ...) with checked adds.
+// One warp per row; rows within the bound exit after one comparison.
+// ---------------------------------------------------------------------------
+struct CheckParams {
+  const int8_t* a_hi;
+  const uint8_t* a_lo;
+  const int16_t* a16;  // int16 A instead of the planes (row stride lda elements)
+  long long lda;
+  const unsigned long long* l1;
+  int M, K;
+  int nseg;
+  const int8_t* w[3];
+  const int32_t* bias[3];
+  int rows[3];
+  nsrl_device_status* st;
+};
+
+constexpr int PREFIX_CHECK_THREADS = 256;
+
+// Rescans row m of the linear in the reference's order (bias, then k = 0, 1,
+// ...): any i32 prefix outside the range flags the call (linear.rs:282-296).
+__device__ void prefix_rescan_row(const CheckParams& c, int m, int lane) {
+  const int8_t* ah = c.a16 ? nullptr : c.a_hi + (long long)m * c.lda;
+  const uint8_t* al = c.a16 ? nullptr : c.a_lo + (long long)m * c.lda;
+  const int16_t* a16 = c.a16 ? c.a16 + (long long)m * c.lda : nullptr;
+  for (int sg = 0; sg < c.nseg; ++sg) {
+    for (int n = lane; n < c.rows[sg]; n += 32) {
+      const int8_t* w = c.w[sg] + (long long)n * c.K;
+      int acc = c.bias[sg] ? c.bias[sg][n] : 0;
+      bool bad = false;
+      for (int k = 0; k < c.K && !bad; ++k) {
+        const int x = a16 ? (int)a16[k] : (int)ah[k] * 256 + (int)al[k];
+        long long t = (long long)acc + (long long)(x * (int)w[k]);
+        if (t < INT_MIN || t > INT_MAX) bad = true;
+        acc = (int)t;
+      }
+      if (bad) nsrl_flag(c.st, NSRL_FLAG_LINEAR_OVERFLOW);
+    }
+  }
+}
+
 struct TcParams {
   int M, K, N;  // N = output columns (GATED: hidden channels)
   int nseg, seg_rows;
@@ -76,6 +120,11 @@ struct TcParams {
   QkvRoute route;                   // QKV_VT: head-sharded destinations (route.nranks > 0)
   bool small_acc;                   // K * 127 * 32767 < 2^30: every accumulator is below 2^30
   bool wide;                        // i64 accumulator, requantize_i64_to_i16 (backward-input linears)
+  // The i32 prefix check, in the epilogue of each row block's first column
+  // tile (planes input with the rows' L1 given): rows past the L1 bound are
+  // rescanned there, one warp per row.
+  bool fuse_check;
+  CheckParams chk;
   nsrl_device_status* st;
 };
 
@@ -348,8 +397,12 @@ __global__ void __launch_bounds__(threads_for(A16), 1)
   uint32_t* tslot = reinterpret_cast<uint32_t*>(ready + STAGES);
   uint32_t* skip_flag = tslot + 1;
 
+  __shared__ unsigned long long s_maxb;  // max |bias| of the fused prefix check
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (threadIdx.x == 0) *skip_flag = timed_out(p.st) ? 1u : 0u;
+  if (threadIdx.x == 0) {
+    *skip_flag = timed_out(p.st) ? 1u : 0u;
+    s_maxb = 0ull;
+  }
   __syncthreads();
   if (*skip_flag) return;  // a wait of this call already timed out: do nothing
 
@@ -526,7 +579,16 @@ __global__ void __launch_bounds__(threads_for(A16), 1)
       if (sg == 1) ush1 = s0.right_shift;
       if (sg == 2) ush2 = s0.right_shift;
     }
-    uni = epilogue_all(uni);
+    if (p.fuse_check) {  // max |bias| over every segment, for the rows' prefix bound
+      long long mb = 0;
+      for (int sg = 0; sg < p.chk.nseg; ++sg)
+        if (p.chk.bias[sg])
+          for (int i = (int)threadIdx.x - 64; i < p.chk.rows[sg]; i += 32 * EPI_WARPS)
+            mb = max(mb, llabs((long long)p.chk.bias[sg][i]));
+      if (mb) atomicMax(&s_maxb, (unsigned long long)mb);
+    }
+    uni = epilogue_all(uni);  // a barrier of the epilogue warps: the maximum above is complete
+    const long long maxb = (long long)s_maxb;
     for (int t = blockIdx.x; t < p.tiles; t += gridDim.x, ++local) {
       const uint32_t buf = local & 1, use = local >> 1;
       const int m0 = (t / p.tiles_n) * BM, nt = t % p.tiles_n;
@@ -710,6 +772,14 @@ __global__ void __launch_bounds__(threads_for(A16), 1)
         }
       }
       if ((EPI == (int)Epi::PLANES || EPI == (int)Epi::GATED) && p.yl1 && row_ok && l1) atomicAdd(&p.yl1[r], l1);
+      if (p.fuse_check && nt == 0 && cg == 0) {
+        // The row block's prefix check, once (its first column tile): rows
+        // whose |bias| + 127 L1 bound passes i32::MAX are rescanned in the
+        // reference's order by the whole warp (rare).
+        const bool bad = row_ok && 127ll * (long long)p.chk.l1[r] + maxb > (long long)INT_MAX;
+        for (unsigned m = __ballot_sync(0xffffffffu, bad); m; m &= m - 1)
+          prefix_rescan_row(p.chk, m0 + q * 32 + (__ffs(m) - 1), lane);
+      }
     }
     if (EPI == (int)Epi::RESID) {
 #pragma unroll
@@ -813,50 +883,6 @@ __global__ void gemm_simt_kernel(const SimtParams s) {
     p.yh[(long long)m * p.ldp + n] = (int8_t)(v >> 8);
     p.yl[(long long)m * p.ldp + n] = (uint8_t)(v & 255);
     if (p.yl1) atomicAdd(&p.yl1[m], (unsigned long long)abs((int)v));
-  }
-}
-
-// ---------------------------------------------------------------------------
-// Exact i32 prefix check (linear.rs:282-296): for rows where
-// |bias| + 127 * L1(x_row) can exceed i32::MAX, rescan every output in the
-// reference's order (bias first, then k = 0, 1, ...) with checked adds.
-// One warp per row; rows within the bound exit after one comparison.
-// ---------------------------------------------------------------------------
-struct CheckParams {
-  const int8_t* a_hi;
-  const uint8_t* a_lo;
-  const int16_t* a16;  // int16 A instead of the planes (row stride lda elements)
-  long long lda;
-  const unsigned long long* l1;
-  int M, K;
-  int nseg;
-  const int8_t* w[3];
-  const int32_t* bias[3];
-  int rows[3];
-  nsrl_device_status* st;
-};
-
-constexpr int PREFIX_CHECK_THREADS = 256;
-
-// Rescans row m of the linear in the reference's order (bias, then k = 0, 1,
-// ...): any i32 prefix outside the range flags the call (linear.rs:282-296).
-__device__ void prefix_rescan_row(const CheckParams& c, int m, int lane) {
-  const int8_t* ah = c.a16 ? nullptr : c.a_hi + (long long)m * c.lda;
-  const uint8_t* al = c.a16 ? nullptr : c.a_lo + (long long)m * c.lda;
-  const int16_t* a16 = c.a16 ? c.a16 + (long long)m * c.lda : nullptr;
-  for (int sg = 0; sg < c.nseg; ++sg) {
-    for (int n = lane; n < c.rows[sg]; n += 32) {
-      const int8_t* w = c.w[sg] + (long long)n * c.K;
-      int acc = c.bias[sg] ? c.bias[sg][n] : 0;
-      bool bad = false;
-      for (int k = 0; k < c.K && !bad; ++k) {
-        const int x = a16 ? (int)a16[k] : (int)ah[k] * 256 + (int)al[k];
-        long long t = (long long)acc + (long long)(x * (int)w[k]);
-        if (t < INT_MIN || t > INT_MAX) bad = true;
-        acc = (int)t;
-      }
-      if (bad) nsrl_flag(c.st, NSRL_FLAG_LINEAR_OVERFLOW);
-    }
   }
 }
 
@@ -1069,6 +1095,26 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 
 bool tma_supported() { return encode_fn() != nullptr; }
 
+// The prefix check's view of a linear (its A, weights, biases and rows' L1).
+static CheckParams check_params(const GemmArgs& a) {
+  CheckParams c{};
+  c.a_hi = a.a_hi;
+  c.a_lo = a.a_lo;
+  c.a16 = a.a16;
+  c.lda = (long long)a.lda;
+  c.l1 = a.a_l1;
+  c.M = (int)a.M;
+  c.K = (int)a.K;
+  c.nseg = a.nseg;
+  for (int i = 0; i < a.nseg; ++i) {
+    c.w[i] = a.seg[i].w;
+    c.bias[i] = a.seg[i].bias;
+    c.rows[i] = (int)a.seg[i].rows;
+  }
+  c.st = a.st;
+  return c;
+}
+
 cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t stream) {
   const bool gated = a.epi == Epi::GATED;
   int N = 0;
@@ -1153,6 +1199,9 @@ cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t stream) {
       if (a16) return cudaErrorInvalidValue;
       tc = false;
     } else {
+      // planes input with the rows' L1: the prefix check runs in the GEMM's epilogue
+      p.fuse_check = need_check && !a16 && a.a_l1 != nullptr;
+      if (p.fuse_check) p.chk = check_params(a);
       p.tiles_n = gated ? (N + BN / 2 - 1) / (BN / 2) : (N + BN - 1) / BN;
       p.tiles = p.tiles_n * (int)((a.M + BM - 1) / BM);
       const int grid = std::min(p.tiles, sm_count());
@@ -1183,23 +1232,9 @@ cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t stream) {
 
   // The i32 prefix can only overflow when |bias| + K * 127 * 32767 > i32::MAX
   // (linear.rs:144-173); then rows outside the L1 bound are rescanned.
-  if (need_check) {
+  if (need_check && !(tc && p.fuse_check)) {
     if (!a.a_l1) return cudaErrorInvalidValue;
-    CheckParams c{};
-    c.a_hi = a.a_hi;
-    c.a_lo = a.a_lo;
-    c.a16 = a.a16;
-    c.lda = (long long)a.lda;
-    c.l1 = a.a_l1;
-    c.M = (int)a.M;
-    c.K = (int)a.K;
-    c.nseg = a.nseg;
-    for (int i = 0; i < a.nseg; ++i) {
-      c.w[i] = a.seg[i].w;
-      c.bias[i] = a.seg[i].bias;
-      c.rows[i] = (int)a.seg[i].rows;
-    }
-    c.st = a.st;
+    const CheckParams c = check_params(a);
     const unsigned blocks =
         (unsigned)std::min<size_t>((a.M + PREFIX_CHECK_THREADS - 1) / PREFIX_CHECK_THREADS, 148 * 8);
     ProfScope prof("linear_prefix_check", stream, 0.0, 8.0 * Mx);

@@ -75,19 +75,21 @@ def test_linear_identity_and_saturation(core):
     assert host(core.linear_i16_i8_i16_per_channel_checked(dev(x), g)).tolist() == [[32767, -32768]]
 
 
-def test_linear_rejects_final_overflow(core):
+@pytest.mark.parametrize("N", [1, 300])  # 300 outputs: the planes path, check fused into the GEMM
+def test_linear_rejects_final_overflow(core, N):
     """linear.rs:866-883: the sum leaves i32."""
-    w = np.full((1, 600), 127, np.int8)
-    o, g = lin_pair(core, w, 0, bias=[2**31 - 1])
+    w = np.full((N, 600), 127, np.int8)
+    o, g = lin_pair(core, w, 0, bias=[2**31 - 1] * N)
     x = np.full((1, 600), 32767, np.int16)
     assert O.linear(x, o) is None
     assert core.linear_i16_i8_i16_per_channel_checked(dev(x), g) is None
 
 
-def test_linear_rejects_prefix_overflow_with_fitting_total(core):
+@pytest.mark.parametrize("N", [3, 300])  # 300 outputs: the planes path, check fused into the GEMM
+def test_linear_rejects_prefix_overflow_with_fitting_total(core, N):
     """An i32 prefix overflows although the final sum fits: still `None` (checked_add per prefix)."""
     K = 1024
-    w = np.where(np.arange(K) < 600, 127, -127).astype(np.int8)[None, :].repeat(3, 0)
+    w = np.where(np.arange(K) < 600, 127, -127).astype(np.int8)[None, :].repeat(N, 0)
     w[1] = 1  # a row that never overflows
     x = np.full((2, K), 32767, np.int16)
     x[1] = 1
