@@ -19,8 +19,9 @@
 //   warp 0      TMA producer: A hi/lo planes + W tile per 128-wide K block,
 //               through a 4-stage shared-memory ring
 //   warp 1      TMEM allocator + MMA issuer (whole warp, one elected lane issues)
-//   warps 2..17 epilogue: TMEM -> registers -> requant -> global; four
-//               warps per TMEM lane quarter, 32 columns each
+//   warps 2..17 epilogue: TMEM -> registers -> requant -> global; two sets
+//               of eight taking alternate tiles (one accumulator buffer
+//               each), two warps per TMEM lane quarter, 64 columns each
 // The two accumulator pairs (hi, lo) of a 128 x 128 tile take 256 TMEM
 // columns; two tiles are in flight (512 columns) so that the epilogue of
 // tile i overlaps the MMAs of tile i+1.  Operand tiles are K-major with the
@@ -413,7 +414,7 @@ __global__ void __launch_bounds__(threads_for(A16), 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], EPI_WARPS);
+      mbar_init(&acc_empty[b], EPI_WARPS / 2);  // the set of eight warps that takes buffer b
     }
     if (A16)
       for (int s = 0; s < STAGES; ++s) mbar_init(&ready[s], CONV_WARPS);
@@ -555,12 +556,16 @@ __global__ void __launch_bounds__(threads_for(A16), 1)
       }
     }
   } else {
-    // Epilogue: warp w reads TMEM lanes [32*(w%4), 32*(w%4)+32) and owns
-    // column group cg = (w-2)/4 of the tile: columns [32*cg, 32*cg+32), or
-    // for the gated form up channels [16*cg, +16) with their gate channels.
+    // Epilogue: two sets of eight warps take alternate tiles (set s the
+    // tiles of accumulator buffer s), so that one set's accumulator loads
+    // and their latency overlap the other set's arithmetic.  Warp w reads
+    // TMEM lanes [32*(w%4), 32*(w%4)+32) and owns column groups cg = 2 cgs
+    // and 2 cgs + 1, cgs = ((w-2)/4) % 2, of its tiles: columns [32*cg,
+    // 32*cg+32), or for the gated form up channels [16*cg, +16) with their
+    // gate channels.
     const int q = warp & 3;
-    const int cg = (warp - 2) >> 2;
-    uint32_t local = 0;
+    const int set = (warp - 2) >> 3, cgs = ((warp - 2) >> 2) & 1;
+    uint32_t local = (uint32_t)set;
     unsigned long long sat = 0;
     // Every segment's scales uniform (multiplier 1, one shift, no bias)?  Then
     // the tiles take that shift and read no table: checked once per CTA by the
@@ -589,190 +594,202 @@ __global__ void __launch_bounds__(threads_for(A16), 1)
     }
     uni = epilogue_all(uni);  // a barrier of the epilogue warps: the maximum above is complete
     const long long maxb = (long long)s_maxb;
-    for (int t = blockIdx.x; t < p.tiles; t += gridDim.x, ++local) {
+    for (int t = blockIdx.x + set * (int)gridDim.x; t < p.tiles; t += 2 * (int)gridDim.x, local += 2) {
       const uint32_t buf = local & 1, use = local >> 1;
       const int m0 = (t / p.tiles_n) * BM, nt = t % p.tiles_n;
       const int r = m0 + q * 32 + lane;
       const bool row_ok = r < p.M;
       const uint32_t lrow = tmem + buf * ACC_COLS + ((uint32_t)(q * 32) << 16);
       unsigned long long l1 = 0;
-      if (EPI == (int)Epi::GATED) {
-        const int fb = nt * (BN / 2) + 16 * cg;
-        const int nvalid = max(0, min(16, p.N - fb));
-        const ColScale su =
-            uni ? uniform_scale(ush0) : load_scales(p.scales[0], p.bias[0], fb + (lane & 15), (lane & 15) < nvalid);
-        const ColScale sg =
-            uni ? uniform_scale(ush1) : load_scales(p.scales[1], p.bias[1], fb + (lane & 15), (lane & 15) < nvalid);
-        uint32_t hu[16], lu[16], hg[16], lg[16];
-        if (!mbar_wait(&acc_full[buf], use & 1, p.st)) break;
-        tc_fence_after();
-        tmem_ld16(lrow + 16 * cg, hu);
-        tmem_ld16(lrow + BN + 16 * cg, lu);
-        tmem_ld16(lrow + 64 + 16 * cg, hg);
-        tmem_ld16(lrow + BN + 64 + 16 * cg, lg);
-        tmem_wait_ld();
-        tc_fence_before();
-        if (lane == 0) mbar_arrive(&acc_empty[buf]);
-        int up[16], gt[16];
-        requant16(hu, lu, su, up, p.small_acc);
-        requant16(hg, lg, sg, gt, p.small_acc);
-        if (p.y && row_ok && nvalid > 0) {  // the up and gate values themselves (the training step's caches)
-          uint32_t ou[8], og[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            ou[i] = __byte_perm((uint32_t)up[2 * i], (uint32_t)up[2 * i + 1], 0x5410);
-            og[i] = __byte_perm((uint32_t)gt[2 * i], (uint32_t)gt[2 * i + 1], 0x5410);
+      bool stop = false;  // a wait of this call timed out
+#pragma unroll 1
+      for (int sub = 0; sub < 2; ++sub) {  // the warp's two column groups of the tile
+        const int cg = 2 * cgs + sub;
+        if (EPI == (int)Epi::GATED) {
+          const int fb = nt * (BN / 2) + 16 * cg;
+          const int nvalid = max(0, min(16, p.N - fb));
+          const ColScale su =
+              uni ? uniform_scale(ush0) : load_scales(p.scales[0], p.bias[0], fb + (lane & 15), (lane & 15) < nvalid);
+          const ColScale sg =
+              uni ? uniform_scale(ush1) : load_scales(p.scales[1], p.bias[1], fb + (lane & 15), (lane & 15) < nvalid);
+          uint32_t hu[16], lu[16], hg[16], lg[16];
+          if (sub == 0 && !mbar_wait(&acc_full[buf], use & 1, p.st)) {
+            stop = true;
+            break;
           }
-          const bool vok = ((p.ldy | fb) & 7) == 0;
-          store16_i16(p.y + (long long)r * p.ldy + fb, ou, nvalid, vok);
-          store16_i16(p.y2 + (long long)r * p.ldy + fb, og, nvalid, vok);
-        }
-        int act[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) act[i] = gated_act_i32(up[i], gt[i]);
-        unsigned a1 = 0;
-        if (nvalid == 16) {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) a1 += (unsigned)abs(act[i]);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) a1 += (i < nvalid) ? (unsigned)abs(act[i]) : 0u;
-        }
-        uint32_t o[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) o[i] = __byte_perm((uint32_t)act[2 * i], (uint32_t)act[2 * i + 1], 0x5410);
-        if (row_ok && nvalid > 0) {
-          const long long off = (long long)r * p.ldp + fb;
-          l1 += a1;
-          store16_planes_nol1(p.yh + off, p.yl + off, o, nvalid, ((p.ldp | fb) & 15) == 0);
-        }
-      } else {
-        const int nb = nt * BN;
-        const int sseg = (p.nseg == 3) ? nb / p.seg_rows : 0;
-        const int nloc = ((p.nseg == 3) ? nb % p.seg_rows : nb) + 32 * cg;
-        const int n = nb + 32 * cg;
-        const int nvalid = max(0, min(32, p.N - n));
-        const ColScale sc = uni ? uniform_scale(sseg == 0 ? ush0 : sseg == 1 ? ush1 : ush2)
-                                : load_scales(p.scales[sseg], p.bias[sseg], nloc + lane, lane < nvalid);
-        // The residual rows do not depend on the accumulator: fetch them first.
-        uint32_t s16[16];
-        const bool vec_skip = EPI == (int)Epi::RESID && ((p.ldskip | p.ldy | n) & 7) == 0 && nvalid == 32;  // both halves full
-        if (EPI == (int)Epi::RESID && row_ok && nvalid > 0) {
-          const int16_t* sk = p.skip + (long long)r * p.ldskip + n;
-          if (vec_skip) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const uint4 v = reinterpret_cast<const uint4*>(sk)[i];
-              s16[4 * i] = v.x;
-              s16[4 * i + 1] = v.y;
-              s16[4 * i + 2] = v.z;
-              s16[4 * i + 3] = v.w;
-            }
-          } else {
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const int a = (2 * i < nvalid) ? (int)sk[2 * i] : 0;
-              const int b = (2 * i + 1 < nvalid) ? (int)sk[2 * i + 1] : 0;
-              s16[i] = pack2(a, b);
-            }
-          }
-        }
-        if (!mbar_wait(&acc_full[buf], use & 1, p.st)) break;
-        tc_fence_after();
-        // All 32 columns come out of TMEM at once and the buffer is released
-        // before any arithmetic, so the next tile's MMAs overlap this
-        // epilogue; the columns are then finished in two halves of 16.  The
-        // residual form, which also holds the skip rows, and the int16-input
-        // form, which has fewer registers per thread, load and release half
-        // by half.
-        constexpr bool kOnce = EPI != (int)Epi::RESID && !A16;
-        uint32_t hq[2][16], lq[2][16];
-        if (kOnce) {
-          tmem_ld16(lrow + 32 * cg, hq[0]);
-          tmem_ld16(lrow + BN + 32 * cg, lq[0]);
-          tmem_ld16(lrow + 32 * cg + 16, hq[1]);
-          tmem_ld16(lrow + BN + 32 * cg + 16, lq[1]);
+          tc_fence_after();
+          tmem_ld16(lrow + 16 * cg, hu);
+          tmem_ld16(lrow + BN + 16 * cg, lu);
+          tmem_ld16(lrow + 64 + 16 * cg, hg);
+          tmem_ld16(lrow + BN + 64 + 16 * cg, lg);
           tmem_wait_ld();
           tc_fence_before();
-          if (lane == 0) mbar_arrive(&acc_empty[buf]);
-        }
-#pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          if (!kOnce) {
-            tmem_ld16(lrow + 32 * cg + 16 * hf, hq[hf]);
-            tmem_ld16(lrow + BN + 32 * cg + 16 * hf, lq[hf]);
-            tmem_wait_ld();
-            if (hf == 1) {
-              tc_fence_before();
-              if (lane == 0) mbar_arrive(&acc_empty[buf]);
-            }
-          }
-          const uint32_t(&h)[16] = hq[hf];
-          const uint32_t(&l)[16] = lq[hf];
-          const int nv = max(0, min(16, nvalid - 16 * hf));
-          const int nh = n + 16 * hf;
-          int v[16];
-          if (WIDE) {
-            bool bad = false;
-            requant_wide16(h, l, sc, v, bad, 16 * hf);
-            if (bad && row_ok && nv > 0) nsrl_flag(p.st, NSRL_FLAG_LINEAR_OVERFLOW);
-          } else {
-            requant_cols<16>(h, l, sc, v, p.small_acc, 16 * hf);
-          }
-          if (!row_ok || nv == 0) continue;
-          uint32_t o[8];
-          if (EPI == (int)Epi::RESID) {
+          if (sub == 1 && lane == 0) mbar_arrive(&acc_empty[buf]);  // both groups loaded
+          int up[16], gt[16];
+          requant16(hu, lu, su, up, p.small_acc);
+          requant16(hg, lg, sg, gt, p.small_acc);
+          if (p.y && row_ok && nvalid > 0) {  // the up and gate values themselves (the training step's caches)
+            uint32_t ou[8], og[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-              const uint32_t sk = s16[8 * hf + i];
-              const int a = (int)(int16_t)(sk & 0xFFFF) + v[2 * i];
-              const int b = (int)(int16_t)(sk >> 16) + v[2 * i + 1];
-              const int sa = clamp16(a), sb = clamp16(b);
-              if (2 * i < nv && sa != a) ++sat;
-              if (2 * i + 1 < nv && sb != b) ++sat;
-              o[i] = __byte_perm((uint32_t)sa, (uint32_t)sb, 0x5410);
+              ou[i] = __byte_perm((uint32_t)up[2 * i], (uint32_t)up[2 * i + 1], 0x5410);
+              og[i] = __byte_perm((uint32_t)gt[2 * i], (uint32_t)gt[2 * i + 1], 0x5410);
             }
-            store16_i16(p.y + (long long)r * p.ldy + nh, o, nv, vec_skip);
+            const bool vok = ((p.ldy | fb) & 7) == 0;
+            store16_i16(p.y + (long long)r * p.ldy + fb, ou, nvalid, vok);
+            store16_i16(p.y2 + (long long)r * p.ldy + fb, og, nvalid, vok);
+          }
+          int act[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) act[i] = gated_act_i32(up[i], gt[i]);
+          unsigned a1 = 0;
+          if (nvalid == 16) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) a1 += (unsigned)abs(act[i]);
           } else {
 #pragma unroll
-            for (int i = 0; i < 8; ++i) o[i] = __byte_perm((uint32_t)v[2 * i], (uint32_t)v[2 * i + 1], 0x5410);
-            if (EPI == (int)Epi::QKV_VT && p.route.nranks) {
-              qkv_route_store16(p, r, nh, v, o, nv);
-              continue;
-            }
-            if (EPI == (int)Epi::I16 || (EPI == (int)Epi::QKV_VT && p.y))  // QKV_VT: the training step's int16 cache
-              store16_i16(p.y + (long long)r * p.ldy + nh, o, nv, ((p.ldy | nh) & 7) == 0);
-            if (EPI == (int)Epi::I16) continue;
-            if (EPI == (int)Epi::QKV_VT && nh >= p.vt_col0) {
-              // v columns: byte stores into [b][h][dim][s]; the 32 lanes of the
-              // warp hold 32 consecutive positions, so each store instruction
-              // writes one contiguous 32-byte run per plane.  [b][h][dim][s] is
-              // contiguous over (h, dim): row (b, c) of the planes is
-              // b * H * hd + c for value column c.
-              const int b = r / p.vt_S, spos = r % p.vt_S;
-              const long long off0 = ((long long)b * (p.vt_H * p.vt_hd) + (nh - p.vt_col0)) * p.vt_S + spos;
+            for (int i = 0; i < 16; ++i) a1 += (i < nvalid) ? (unsigned)abs(act[i]) : 0u;
+          }
+          uint32_t o[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) o[i] = __byte_perm((uint32_t)act[2 * i], (uint32_t)act[2 * i + 1], 0x5410);
+          if (row_ok && nvalid > 0) {
+            const long long off = (long long)r * p.ldp + fb;
+            l1 += a1;
+            store16_planes_nol1(p.yh + off, p.yl + off, o, nvalid, ((p.ldp | fb) & 15) == 0);
+          }
+        } else {
+          const int nb = nt * BN;
+          const int sseg = (p.nseg == 3) ? nb / p.seg_rows : 0;
+          const int nloc = ((p.nseg == 3) ? nb % p.seg_rows : nb) + 32 * cg;
+          const int n = nb + 32 * cg;
+          const int nvalid = max(0, min(32, p.N - n));
+          const ColScale sc = uni ? uniform_scale(sseg == 0 ? ush0 : sseg == 1 ? ush1 : ush2)
+                                  : load_scales(p.scales[sseg], p.bias[sseg], nloc + lane, lane < nvalid);
+          // The residual rows do not depend on the accumulator: fetch them first.
+          uint32_t s16[16];
+          const bool vec_skip = EPI == (int)Epi::RESID && ((p.ldskip | p.ldy | n) & 7) == 0 && nvalid == 32;  // both halves full
+          if (EPI == (int)Epi::RESID && row_ok && nvalid > 0) {
+            const int16_t* sk = p.skip + (long long)r * p.ldskip + n;
+            if (vec_skip) {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const uint4 v = reinterpret_cast<const uint4*>(sk)[i];
+                s16[4 * i] = v.x;
+                s16[4 * i + 1] = v.y;
+                s16[4 * i + 2] = v.z;
+                s16[4 * i + 3] = v.w;
+              }
+            } else {
 #pragma unroll
               for (int i = 0; i < 16; ++i) {
-                if (i < nv) {
-                  const long long off = off0 + (long long)i * p.vt_S;
-                  p.vth[off] = (int8_t)(v[i] >> 8);
-                  p.vtl[off] = (uint8_t)(v[i] & 255);
-                }
+                const int a = (2 * i < nvalid) ? (int)sk[2 * i] : 0;
+                const int b = (2 * i + 1 < nvalid) ? (int)sk[2 * i + 1] : 0;
+                s16[i] = pack2(a, b);
               }
             }
-            if (EPI != (int)Epi::QKV_VT || nh < p.vt_col0 || p.v_rows) {
-              if (p.yl1) {
+          }
+          if (sub == 0 && !mbar_wait(&acc_full[buf], use & 1, p.st)) {
+            stop = true;
+            break;
+          }
+          tc_fence_after();
+          // All 32 columns come out of TMEM at once and the buffer is released
+          // before any arithmetic, so the next tile's MMAs overlap this
+          // epilogue; the columns are then finished in two halves of 16.  The
+          // residual form, which also holds the skip rows, and the int16-input
+          // form, which has fewer registers per thread, load and release half
+          // by half.
+          constexpr bool kOnce = EPI != (int)Epi::RESID && !A16;
+          uint32_t hq[2][16], lq[2][16];
+          if (kOnce) {
+            tmem_ld16(lrow + 32 * cg, hq[0]);
+            tmem_ld16(lrow + BN + 32 * cg, lq[0]);
+            tmem_ld16(lrow + 32 * cg + 16, hq[1]);
+            tmem_ld16(lrow + BN + 32 * cg + 16, lq[1]);
+            tmem_wait_ld();
+            tc_fence_before();
+            if (sub == 1 && lane == 0) mbar_arrive(&acc_empty[buf]);  // both groups loaded
+          }
 #pragma unroll
-                for (int i = 0; i < 16; ++i) l1 += (i < nv) ? (unsigned)abs(v[i]) : 0u;
+          for (int hf = 0; hf < 2; ++hf) {
+            if (!kOnce) {
+              tmem_ld16(lrow + 32 * cg + 16 * hf, hq[hf]);
+              tmem_ld16(lrow + BN + 32 * cg + 16 * hf, lq[hf]);
+              tmem_wait_ld();
+              if (hf == 1 && sub == 1) {  // both groups loaded
+                tc_fence_before();
+                if (lane == 0) mbar_arrive(&acc_empty[buf]);
               }
-              const long long off = (long long)r * p.ldp + nh;
-              store16_planes_nol1(p.yh + off, p.yl + off, o, nv, ((p.ldp | nh) & 15) == 0);
+            }
+            const uint32_t(&h)[16] = hq[hf];
+            const uint32_t(&l)[16] = lq[hf];
+            const int nv = max(0, min(16, nvalid - 16 * hf));
+            const int nh = n + 16 * hf;
+            int v[16];
+            if (WIDE) {
+              bool bad = false;
+              requant_wide16(h, l, sc, v, bad, 16 * hf);
+              if (bad && row_ok && nv > 0) nsrl_flag(p.st, NSRL_FLAG_LINEAR_OVERFLOW);
+            } else {
+              requant_cols<16>(h, l, sc, v, p.small_acc, 16 * hf);
+            }
+            if (!row_ok || nv == 0) continue;
+            uint32_t o[8];
+            if (EPI == (int)Epi::RESID) {
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const uint32_t sk = s16[8 * hf + i];
+                const int a = (int)(int16_t)(sk & 0xFFFF) + v[2 * i];
+                const int b = (int)(int16_t)(sk >> 16) + v[2 * i + 1];
+                const int sa = clamp16(a), sb = clamp16(b);
+                if (2 * i < nv && sa != a) ++sat;
+                if (2 * i + 1 < nv && sb != b) ++sat;
+                o[i] = __byte_perm((uint32_t)sa, (uint32_t)sb, 0x5410);
+              }
+              store16_i16(p.y + (long long)r * p.ldy + nh, o, nv, vec_skip);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 8; ++i) o[i] = __byte_perm((uint32_t)v[2 * i], (uint32_t)v[2 * i + 1], 0x5410);
+              if (EPI == (int)Epi::QKV_VT && p.route.nranks) {
+                qkv_route_store16(p, r, nh, v, o, nv);
+                continue;
+              }
+              if (EPI == (int)Epi::I16 || (EPI == (int)Epi::QKV_VT && p.y))  // QKV_VT: the training step's int16 cache
+                store16_i16(p.y + (long long)r * p.ldy + nh, o, nv, ((p.ldy | nh) & 7) == 0);
+              if (EPI == (int)Epi::I16) continue;
+              if (EPI == (int)Epi::QKV_VT && nh >= p.vt_col0) {
+                // v columns: byte stores into [b][h][dim][s]; the 32 lanes of the
+                // warp hold 32 consecutive positions, so each store instruction
+                // writes one contiguous 32-byte run per plane.  [b][h][dim][s] is
+                // contiguous over (h, dim): row (b, c) of the planes is
+                // b * H * hd + c for value column c.
+                const int b = r / p.vt_S, spos = r % p.vt_S;
+                const long long off0 = ((long long)b * (p.vt_H * p.vt_hd) + (nh - p.vt_col0)) * p.vt_S + spos;
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                  if (i < nv) {
+                    const long long off = off0 + (long long)i * p.vt_S;
+                    p.vth[off] = (int8_t)(v[i] >> 8);
+                    p.vtl[off] = (uint8_t)(v[i] & 255);
+                  }
+                }
+              }
+              if (EPI != (int)Epi::QKV_VT || nh < p.vt_col0 || p.v_rows) {
+                if (p.yl1) {
+#pragma unroll
+                  for (int i = 0; i < 16; ++i) l1 += (i < nv) ? (unsigned)abs(v[i]) : 0u;
+                }
+                const long long off = (long long)r * p.ldp + nh;
+                store16_planes_nol1(p.yh + off, p.yl + off, o, nv, ((p.ldp | nh) & 15) == 0);
+              }
             }
           }
         }
       }
+      if (stop) break;
       if ((EPI == (int)Epi::PLANES || EPI == (int)Epi::GATED) && p.yl1 && row_ok && l1) atomicAdd(&p.yl1[r], l1);
-      if (p.fuse_check && nt == 0 && cg == 0) {
+      if (p.fuse_check && nt == 0 && cgs == 0) {
         // The row block's prefix check, once (its first column tile): rows
         // whose |bias| + 127 L1 bound passes i32::MAX are rescanned in the
         // reference's order by the whole warp (rare).
