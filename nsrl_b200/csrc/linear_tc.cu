@@ -19,9 +19,10 @@
 //   warp 0      TMA producer: A hi/lo planes + W tile per 128-wide K block,
 //               through a 4-stage shared-memory ring
 //   warp 1      TMEM allocator + MMA issuer (whole warp, one elected lane issues)
-//   warps 2..17 epilogue: TMEM -> registers -> requant -> global; two sets
-//               of eight taking alternate tiles (one accumulator buffer
-//               each), two warps per TMEM lane quarter, 64 columns each
+//   warps 2..17 epilogue: TMEM -> registers -> requant -> global; four
+//               warps per TMEM lane quarter, 32 columns each (or, for the
+//               gated form without caches, two sets of eight taking
+//               alternate tiles, 64 columns each)
 // The two accumulator pairs (hi, lo) of a 128 x 128 tile take 256 TMEM
 // columns; two tiles are in flight (512 columns) so that the epilogue of
 // tile i overlaps the MMAs of tile i+1.  Operand tiles are K-major with the
@@ -385,9 +386,10 @@ __device__ __forceinline__ void store16_i16(int16_t* dst, const uint32_t (&o)[8]
 // 128-byte-swizzled layout, and only then hand the stage to the MMA.  The
 // separate split pass over A disappears; the i32 prefix check, where K or a
 // bias needs it, takes the rows' L1 from the int16 rows itself.
-template <int EPI, bool WIDE, bool A16>
+template <int EPI, bool WIDE, bool A16, int SETS>
 __global__ void __launch_bounds__(threads_for(A16), 1)
     gemm_tc_kernel(const __grid_constant__ TcMaps maps, const TcParams p) {
+  static_assert(SETS == 1 || SETS == 2, "one or two epilogue sets");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
@@ -414,7 +416,7 @@ __global__ void __launch_bounds__(threads_for(A16), 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], EPI_WARPS / 2);  // the set of eight warps that takes buffer b
+      mbar_init(&acc_empty[b], EPI_WARPS / SETS);  // the epilogue warps that take buffer b's tiles
     }
     if (A16)
       for (int s = 0; s < STAGES; ++s) mbar_init(&ready[s], CONV_WARPS);
@@ -556,15 +558,19 @@ __global__ void __launch_bounds__(threads_for(A16), 1)
       }
     }
   } else {
-    // Epilogue: two sets of eight warps take alternate tiles (set s the
-    // tiles of accumulator buffer s), so that one set's accumulator loads
-    // and their latency overlap the other set's arithmetic.  Warp w reads
-    // TMEM lanes [32*(w%4), 32*(w%4)+32) and owns column groups cg = 2 cgs
-    // and 2 cgs + 1, cgs = ((w-2)/4) % 2, of its tiles: columns [32*cg,
-    // 32*cg+32), or for the gated form up channels [16*cg, +16) with their
-    // gate channels.
+    // Epilogue: warp w reads TMEM lanes [32*(w%4), 32*(w%4)+32).  With one
+    // set (SETS = 1) all sixteen warps take every tile, warp w column group
+    // cg = (w-2)/4: columns [32*cg, 32*cg+32), or for the gated form up
+    // channels [16*cg, +16) with their gate channels.  With two sets, eight
+    // warps each take alternate tiles (set s the tiles of accumulator buffer
+    // s), so that one set's accumulator loads and their latency overlap the
+    // other set's arithmetic; warp w then owns column groups 2 cgs and
+    // 2 cgs + 1, cgs = ((w-2)/4) % 2.  Two sets hold more registers live and
+    // pay off where the epilogue has the fewest stores (the gated form
+    // without its int16 caches).
     const int q = warp & 3;
-    const int set = (warp - 2) >> 3, cgs = ((warp - 2) >> 2) & 1;
+    const int set = SETS == 2 ? (warp - 2) >> 3 : 0;
+    const int cg0 = SETS == 2 ? 2 * (((warp - 2) >> 2) & 1) : (warp - 2) >> 2;
     uint32_t local = (uint32_t)set;
     unsigned long long sat = 0;
     // Every segment's scales uniform (multiplier 1, one shift, no bias)?  Then
@@ -594,7 +600,7 @@ __global__ void __launch_bounds__(threads_for(A16), 1)
     }
     uni = epilogue_all(uni);  // a barrier of the epilogue warps: the maximum above is complete
     const long long maxb = (long long)s_maxb;
-    for (int t = blockIdx.x + set * (int)gridDim.x; t < p.tiles; t += 2 * (int)gridDim.x, local += 2) {
+    for (int t = blockIdx.x + set * (int)gridDim.x; t < p.tiles; t += SETS * (int)gridDim.x, local += SETS) {
       const uint32_t buf = local & 1, use = local >> 1;
       const int m0 = (t / p.tiles_n) * BM, nt = t % p.tiles_n;
       const int r = m0 + q * 32 + lane;
@@ -603,8 +609,8 @@ __global__ void __launch_bounds__(threads_for(A16), 1)
       unsigned long long l1 = 0;
       bool stop = false;  // a wait of this call timed out
 #pragma unroll 1
-      for (int sub = 0; sub < 2; ++sub) {  // the warp's two column groups of the tile
-        const int cg = 2 * cgs + sub;
+      for (int sub = 0; sub < SETS; ++sub) {  // the warp's column groups of the tile
+        const int cg = cg0 + sub;
         if (EPI == (int)Epi::GATED) {
           const int fb = nt * (BN / 2) + 16 * cg;
           const int nvalid = max(0, min(16, p.N - fb));
@@ -624,7 +630,7 @@ __global__ void __launch_bounds__(threads_for(A16), 1)
           tmem_ld16(lrow + BN + 64 + 16 * cg, lg);
           tmem_wait_ld();
           tc_fence_before();
-          if (sub == 1 && lane == 0) mbar_arrive(&acc_empty[buf]);  // both groups loaded
+          if (sub == SETS - 1 && lane == 0) mbar_arrive(&acc_empty[buf]);  // every group loaded
           int up[16], gt[16];
           requant16(hu, lu, su, up, p.small_acc);
           requant16(hg, lg, sg, gt, p.small_acc);
@@ -709,7 +715,7 @@ __global__ void __launch_bounds__(threads_for(A16), 1)
             tmem_ld16(lrow + BN + 32 * cg + 16, lq[1]);
             tmem_wait_ld();
             tc_fence_before();
-            if (sub == 1 && lane == 0) mbar_arrive(&acc_empty[buf]);  // both groups loaded
+            if (sub == SETS - 1 && lane == 0) mbar_arrive(&acc_empty[buf]);  // every group loaded
           }
 #pragma unroll
           for (int hf = 0; hf < 2; ++hf) {
@@ -717,7 +723,7 @@ __global__ void __launch_bounds__(threads_for(A16), 1)
               tmem_ld16(lrow + 32 * cg + 16 * hf, hq[hf]);
               tmem_ld16(lrow + BN + 32 * cg + 16 * hf, lq[hf]);
               tmem_wait_ld();
-              if (hf == 1 && sub == 1) {  // both groups loaded
+              if (hf == 1 && sub == SETS - 1) {  // every group loaded
                 tc_fence_before();
                 if (lane == 0) mbar_arrive(&acc_empty[buf]);
               }
@@ -789,7 +795,7 @@ __global__ void __launch_bounds__(threads_for(A16), 1)
       }
       if (stop) break;
       if ((EPI == (int)Epi::PLANES || EPI == (int)Epi::GATED) && p.yl1 && row_ok && l1) atomicAdd(&p.yl1[r], l1);
-      if (p.fuse_check && nt == 0 && cgs == 0) {
+      if (p.fuse_check && nt == 0 && cg0 == 0) {
         // The row block's prefix check, once (its first column tile): rows
         // whose |bias| + 127 L1 bound passes i32::MAX are rescanned in the
         // reference's order by the whole warp (rare).
@@ -1063,16 +1069,16 @@ bool make_map(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t rows, ui
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int EPI, bool WIDE, bool A16 = false>
+template <int EPI, bool WIDE, bool A16 = false, int SETS = 1>
 cudaError_t launch_tc(const TcMaps& maps, const TcParams& p, int grid, cudaStream_t stream) {
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<EPI, WIDE, A16>,
+    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<EPI, WIDE, A16, SETS>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  gemm_tc_kernel<EPI, WIDE, A16><<<grid, threads_for(A16), SMEM_BYTES, stream>>>(maps, p);
+  gemm_tc_kernel<EPI, WIDE, A16, SETS><<<grid, threads_for(A16), SMEM_BYTES, stream>>>(maps, p);
   return cudaGetLastError();
 }
 
@@ -1088,7 +1094,9 @@ cudaError_t launch_tc_epi(Epi epi, const TcMaps& maps, const TcParams& p, int gr
       return p.wide ? launch_tc<(int)Epi::RESID, true>(maps, p, grid, stream)
                     : launch_tc<(int)Epi::RESID, false>(maps, p, grid, stream);
     case Epi::GATED:  // the wide form takes neither of these (launch_gemm rejects it)
-      return launch_tc<(int)Epi::GATED, false>(maps, p, grid, stream);
+      // without the int16 caches (inference) the gated epilogue takes two sets
+      return p.y ? launch_tc<(int)Epi::GATED, false>(maps, p, grid, stream)
+                 : launch_tc<(int)Epi::GATED, false, false, 2>(maps, p, grid, stream);
     case Epi::QKV_VT:
       return launch_tc<(int)Epi::QKV_VT, false>(maps, p, grid, stream);
   }
