@@ -87,6 +87,7 @@ struct Maps {
   CUtensorMap p_hi, p_lo;  // P planes [B*H][S][S], 128 x 32-byte boxes (stores of the cached P)
   CUtensorMap w;           // weight scratch as bytes [rows][2 wstride], 128 x 64-byte boxes (last-pass loads)
   CUtensorMap ws;          // the same, 32 x 32-byte boxes: one softmax warp's weights of a tile (sum-pass stores)
+  CUtensorMap v_hi, v_lo;  // V rows [T][d] (the q|k|v planes' V columns), 32 keys x 64-byte boxes (vrow)
 };
 
 struct Args {
@@ -100,11 +101,19 @@ struct Args {
   int16_t* probs;    // optional P [B][H][S][S]: the visited key tiles only, zeros above the diagonal
   int pstore;        // write P as byte planes [B][H][S][S] (the same entries) through maps.p_hi / p_lo
   CtxRoute rt;       // head-sharded context destinations (rt.nranks > 0)
+  int vrow;          // head dim 64: the last pass reads V as row-major planes (an MN-major B operand)
   nsrl_device_status* st;
 };
 
 // Shared-memory descriptor, K-major, 64-byte swizzle: 8-row atoms of 512 B.
 __device__ __forceinline__ uint64_t sdesc_k64(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(512 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)4 << 61);
+}
+// Shared-memory descriptor of an MN-major tile of 64-byte rows (64 dims of
+// one key per row), 64-byte swizzle, 8-row groups 512 bytes apart: V rows as
+// the B operand of P V without a transposed copy.
+__device__ __forceinline__ uint64_t sdesc_mn64(uint32_t saddr) {
   return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(512 >> 4) << 32) |
          ((uint64_t)1 << 46) | ((uint64_t)4 << 61);
 }
@@ -381,10 +390,16 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
           if (pass < 2) {  // K rows j*32 .. +31 of this head
             tma_load_2d(stg, &maps.k_hi, &ctl->full[s], a.d + h * HDIM, row0 + j * KT);
             tma_load_2d(stg + PLANE_K, &maps.k_lo, &ctl->full[s], a.d + h * HDIM, row0 + j * KT);
-          } else {         // V^T: the head's dims x keys j*32 .. +31
-            const int vrow = (b * a.H + h) * HDIM;
-            tma_load_2d(stg, &maps.vt_hi, &ctl->full[s], j * KT, vrow);
-            tma_load_2d(stg + PLANE_V, &maps.vt_lo, &ctl->full[s], j * KT, vrow);
+          } else {
+            if (HDIM == 64 && a.vrow) {  // V rows: keys j*32 .. +31 x the head's 64 dims
+              // (keys past the sequence are the next one's rows: their P is 0)
+              tma_load_2d(stg, &maps.v_hi, &ctl->full[s], h * HDIM, row0 + j * KT);
+              tma_load_2d(stg + PLANE_V, &maps.v_lo, &ctl->full[s], h * HDIM, row0 + j * KT);
+            } else {  // V^T: the head's dims x keys j*32 .. +31
+              const int vrow = (b * a.H + h) * HDIM;
+              tma_load_2d(stg, &maps.vt_hi, &ctl->full[s], j * KT, vrow);
+              tma_load_2d(stg + PLANE_V, &maps.vt_lo, &ctl->full[s], j * KT, vrow);
+            }
             // the sum pass's weights of tile j, into ring slot j % WPF_N, once
             // the whole scratch block is written
             const int wb = j % WPF_N;
@@ -461,12 +476,16 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
         const uint32_t vh = smem_u32(sm + OFF_STAGE + s * STAGE_BYTES), vl = vh + PLANE_V;
         const uint32_t ph = smem_u32(sm + OFF_P + pb * 2 * PLANE_P), pl = ph + PLANE_P;
         const uint64_t aph = sdesc_k32(ph), apl = sdesc_k32(pl);
-        const uint64_t bvh = sdesc_k32(vh), bvl = sdesc_k32(vl);
+        // V^T tiles are K-major (32-byte rows of keys); V rows are an MN-major
+        // B operand (64-byte rows of dims), bit 16 of the instruction descriptor
+        const bool mn = HDIM == 64 && a.vrow;
+        const uint64_t bvh = mn ? sdesc_mn64(vh) : sdesc_k32(vh), bvl = mn ? sdesc_mn64(vl) : sdesc_k32(vl);
+        const uint32_t i_us = mn ? (pv_us | (1u << 16)) : pv_us, i_uu = mn ? (pv_uu | (1u << 16)) : pv_uu;
         const uint32_t acc = j > 0 ? 1u : 0u;
-        umma_i8_warp(tmem + O_HH, aph, bvh, pv_us, acc);
-        umma_i8_warp(tmem + O_MID, aph, bvl, pv_uu, acc);
-        umma_i8_warp(tmem + O_MID, apl, bvh, pv_us, 1u);
-        umma_i8_warp(tmem + O_LL, apl, bvl, pv_uu, acc);
+        umma_i8_warp(tmem + O_HH, aph, bvh, i_us, acc);
+        umma_i8_warp(tmem + O_MID, aph, bvl, i_uu, acc);
+        umma_i8_warp(tmem + O_MID, apl, bvh, i_us, 1u);
+        umma_i8_warp(tmem + O_LL, apl, bvl, i_uu, acc);
         umma_commit_warp(&ctl->p_empty[pb]);
         umma_commit_warp(&ctl->empty[s]);
         if (a.pstore && j > 0 && lane == 0) {  // the previous tile's store has read its P buffer
@@ -892,13 +911,15 @@ size_t attention_tc_scratch_bytes(size_t B, size_t S, size_t d, size_t H) {
 cudaError_t launch_attention_tc(const Planes& qkv, const VtPlanes& vt, size_t B, size_t S, size_t d, size_t H,
                                 bool causal, Planes ctx, int16_t* wscr, nsrl_device_status* st,
                                 cudaStream_t stream, int16_t* probs, const Planes* probs_planes,
-                                const CtxRoute* route) {
+                                const CtxRoute* route, bool v_rows) {
   if (!attention_tc_forward_supported(S, d, H) || encode_fn() == nullptr || wscr == nullptr)
     return cudaErrorNotSupported;
   const size_t hd = d / H;
   // head dim 16: the forward only (no P for a backward, no head-sharded routing)
   if (hd == 16 && (probs || probs_planes || (route && route->nranks))) return cudaErrorNotSupported;
   if (probs_planes && (!causal || probs_planes->ld != S)) return cudaErrorInvalidValue;
+  // V as row-major planes (the q|k|v planes' V columns): head dim 64, not routed
+  if (v_rows && (hd != 64 || (route && route->nranks))) return cudaErrorInvalidValue;
   if (route && route->nranks &&
       (route->tab == nullptr || route->s_loc <= 0 || S % (size_t)route->s_loc != 0 || probs || probs_planes))
     return cudaErrorInvalidValue;
@@ -913,8 +934,11 @@ cudaError_t launch_attention_tc(const Planes& qkv, const VtPlanes& vt, size_t B,
       make_map(&m.q_lo, qkv.lo, 2 * d, T, qkv.ld, hd == 64 ? 64 : 32, QT) &&
       make_map(&m.k_hi, qkv.hi, 2 * d, T, qkv.ld, hd == 64 ? 64 : 32, KT) &&
       make_map(&m.k_lo, qkv.lo, 2 * d, T, qkv.ld, hd == 64 ? 64 : 32, KT) &&
-      make_map(&m.vt_hi, vt.hi, S, B * H * hd, S, KT, (uint32_t)hd) &&
-      make_map(&m.vt_lo, vt.lo, S, B * H * hd, S, KT, (uint32_t)hd) &&
+      (v_rows || (make_map(&m.vt_hi, vt.hi, S, B * H * hd, S, KT, (uint32_t)hd) &&
+                  make_map(&m.vt_lo, vt.lo, S, B * H * hd, S, KT, (uint32_t)hd))) &&
+      // V rows of a head: 32 keys x 64 bytes (64-byte swizzle) from the V columns
+      (!v_rows || (make_map(&m.v_hi, qkv.hi + 2 * d, d, T, qkv.ld, 64, KT) &&
+                   make_map(&m.v_lo, qkv.lo + 2 * d, d, T, qkv.ld, 64, KT))) &&
       (!probs_planes || (make_p_map(&m.p_hi, probs_planes->hi, S, B * H) && make_p_map(&m.p_lo, probs_planes->lo, S, B * H))) &&
       make_map(&m.w, wscr, 2 * attention_tc_wstride(S), chunk_seqs(B, S, H) * H * ((S + QT - 1) / QT) * QT,
                2 * attention_tc_wstride(S), 64, QT) &&
@@ -925,6 +949,13 @@ cudaError_t launch_attention_tc(const Planes& qkv, const VtPlanes& vt, size_t B,
     m.p_hi = m.q_hi;  // unused
     m.p_lo = m.q_lo;
   }
+  if (v_rows) {
+    m.vt_hi = m.q_hi;  // unused
+    m.vt_lo = m.q_lo;
+  } else {
+    m.v_hi = m.q_hi;  // unused
+    m.v_lo = m.q_lo;
+  }
   Args a{};
   a.S = (int)S;
   a.d = (int)d;
@@ -934,6 +965,7 @@ cudaError_t launch_attention_tc(const Planes& qkv, const VtPlanes& vt, size_t B,
   a.ctx_lo = ctx.lo;
   a.ctx_l1 = ctx.l1;
   a.ldc = (long long)ctx.ld;
+  a.vrow = v_rows ? 1 : 0;
   a.probs = probs;
   a.pstore = probs_planes ? 1 : 0;
   if (route) a.rt = *route;

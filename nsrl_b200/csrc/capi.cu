@@ -143,6 +143,9 @@ nsrl_status attention_core(const Planes& xin, size_t B, size_t S, size_t d, size
                            nsrl_device_status* st, cudaStream_t stream) {
   const size_t T = B * S;
   const bool tc = vt.hi != nullptr && tma_supported();
+  // head dim 64: V stays in the q|k|v planes and the attention reads its rows
+  // (an MN-major operand); head dim 16 takes the transposed V planes
+  const bool v_rows = tc && d / H == 64;
   GemmArgs g{};
   g.a_hi = xin.hi;
   g.a_lo = xin.lo;
@@ -154,7 +157,7 @@ nsrl_status attention_core(const Planes& xin, size_t B, size_t S, size_t d, size
   g.seg[0] = seg_of(q);
   g.seg[1] = seg_of(k);
   g.seg[2] = seg_of(v);
-  g.epi = tc ? Epi::QKV_VT : Epi::PLANES;
+  g.epi = tc && !v_rows ? Epi::QKV_VT : Epi::PLANES;
   g.yp = qkv;
   g.vt = vt;
   g.st = st;
@@ -163,7 +166,9 @@ nsrl_status attention_core(const Planes& xin, size_t B, size_t S, size_t d, size
   if (!needs_l1(d, o)) ctx.l1 = nullptr;
   if (ctx.l1) NSRL_TRY(cudaMemsetAsync(ctx.l1, 0, T * sizeof(unsigned long long), stream), "memset");
   if (tc) {
-    NSRL_TRY(launch_attention_tc(qkv, vt, B, S, d, H, causal, ctx, vt.wscr, st, stream), "attention");
+    NSRL_TRY(launch_attention_tc(qkv, vt, B, S, d, H, causal, ctx, vt.wscr, st, stream, nullptr, nullptr, nullptr,
+                                 v_rows),
+             "attention");
   } else if (attention_prefill_native(d, H, S)) {
     NSRL_TRY(launch_attention(qkv, B, S, d, H, causal, ctx, st, stream), "attention");
   } else {

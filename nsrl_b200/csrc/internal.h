@@ -140,7 +140,8 @@ cudaError_t launch_attention(const Planes& qkv, size_t B, size_t S, size_t d, si
 cudaError_t launch_attention_tc(const Planes& qkv, const VtPlanes& vt, size_t B, size_t S, size_t d, size_t H,
                                 bool causal, Planes ctx, int16_t* wscr, nsrl_device_status* st,
                                 cudaStream_t stream, int16_t* probs = nullptr,
-                                const Planes* probs_planes = nullptr, const CtxRoute* route = nullptr);
+                                const Planes* probs_planes = nullptr, const CtxRoute* route = nullptr,
+                                bool v_rows = false);
 size_t attention_tc_wstride(size_t S);
 size_t attention_tc_scratch_bytes(size_t B, size_t S, size_t d, size_t H);
 // Shape rule of the tensor-core attention (head_dim 64, seq_len % 16 == 0,
