@@ -713,10 +713,12 @@ nsrl_status nsrl_train_windows(const nsrl_train_model* m, const uint8_t* context
     else
       TS_TRY(launch_split_planes(c.in, T, d, d, c.an, s), "split");
     // Q|K|V: with the tcgen05 attention, one GEMM writes the row-major q|k|v
-    // planes (cached for the backward) and the transposed V planes; the int16
-    // rows only when the backward cannot take the planes.
+    // planes (cached for the backward); at head dim 64 the attention reads V's
+    // rows from them, otherwise the GEMM also writes the transposed V planes.
+    // The int16 rows only when the backward cannot take the planes.
     const bool tc_attn = o.vt.hi && tma_supported() && attention_tc_supported(S, d, H);
     const bool planes_bwd = tc_attn && attention_kv_tc_supported(S, d, H);
+    const bool v_rows = planes_bwd && d / H == 64;
     {
       GemmArgs g{};
       g.a_hi = c.an.hi;
@@ -728,13 +730,15 @@ nsrl_status nsrl_train_windows(const nsrl_train_model* m, const uint8_t* context
       g.nseg = 3;
       for (int i = 0; i < 3; ++i)
         g.seg[i] = WeightSeg{ly.lin[i].weights, ly.lin[i].bias, ly.lin[i].scales, d};
-      g.epi = tc_attn ? Epi::QKV_VT : Epi::I16;
+      g.epi = !tc_attn ? Epi::I16 : v_rows ? Epi::PLANES : Epi::QKV_VT;
       g.y = planes_bwd ? nullptr : c.qkv;
       g.ldy = 3 * d;
       if (tc_attn) {
         g.yp = c.pqkv;
-        g.vt = o.vt;
-        g.v_rows = planes_bwd;
+        if (!v_rows) {
+          g.vt = o.vt;
+          g.v_rows = planes_bwd;
+        }
       }
       g.st = st;
       TS_TRY(launch_gemm(g, s), "qkv");
@@ -748,7 +752,8 @@ nsrl_status nsrl_train_windows(const nsrl_train_model* m, const uint8_t* context
       TS_TRY(cudaMemsetAsync(c.ctx.l1, 0, T * sizeof(unsigned long long), s), "memset");
       const Planes pv = p_cache_planes(c, W * H * S * S, S);
       const cudaError_t e = launch_attention_tc(c.pqkv, o.vt, W, S, d, H, true, c.ctx, o.vt.wscr, st, s,
-                                                planes_bwd ? nullptr : c.P, planes_bwd ? &pv : nullptr);
+                                                planes_bwd ? nullptr : c.P, planes_bwd ? &pv : nullptr, nullptr,
+                                                v_rows);
       // without the int16 q|k|v rows there is no other path
       if (e != cudaErrorNotSupported || planes_bwd) {
         TS_TRY(e, "attention");
