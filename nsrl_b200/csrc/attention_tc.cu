@@ -331,11 +331,7 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
   const int ntiles = (kend + KT - 1) / KT;
   const int wy = ((bl * a.H + h) * nq + qt) * QT;  // first row of this group's block of the weight scratch
 
-  if (threadIdx.x == 0) s_abort = timed_out(a.st) ? 1u : 0u;
   if (gtid == 0) ctl->abort = 0u;
-  __syncthreads();
-  if (s_abort) return;  // a wait of this call already timed out: the whole CTA skips its work
-
   if (warp == 0 && lane == 0) {
     mbar_init(&ctl->q_full, 1);
     for (int s = 0; s < ST; ++s) {
@@ -362,9 +358,18 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
     tmem_alloc(&s_tslot, TMEM_COLS);
     tmem_relinquish();
   }
+  // The prologue above touches no global memory: from here on the previous
+  // kernel's outputs (and the status it may have flagged) are visible.
+  griddep_wait();
+  if (threadIdx.x == 0) s_abort = timed_out(a.st) ? 1u : 0u;
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  griddep_launch();
+  if (s_abort) {  // a wait of this call already timed out: the whole CTA skips its work
+    if (gw == 1) tmem_dealloc(s_tslot, TMEM_COLS);
+    return;
+  }
   const uint32_t tmem = s_tslot + 256u * (uint32_t)grp;  // this group's 256 columns
   const int row0 = b * S;  // first token row of this sequence
 
@@ -987,11 +992,9 @@ cudaError_t launch_attention_tc(const Planes& qkv, const VtPlanes& vt, size_t B,
     a.b0 = (int)b0;
     a.nb = (int)std::min(chunk, B - b0);
     const dim3 grid((unsigned)H, (unsigned)((a.nb + GROUPS - 1) / GROUPS), (unsigned)((S + QT - 1) / QT));
-    if (hd == 16)
-      attention_tc_kernel<16><<<grid, THREADS, SMEM_BYTES, stream>>>(m, a);
-    else
-      attention_tc_kernel<64><<<grid, THREADS, SMEM_BYTES, stream>>>(m, a);
-    const cudaError_t e = cudaGetLastError();
+    cudaError_t e = hd == 16 ? launch_pdl(attention_tc_kernel<16>, grid, dim3(THREADS), SMEM_BYTES, stream, m, a)
+                             : launch_pdl(attention_tc_kernel<64>, grid, dim3(THREADS), SMEM_BYTES, stream, m, a);
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;

@@ -227,11 +227,13 @@ nsrl_status mlp_block(const int16_t* x, size_t T, size_t d, size_t F, const int1
   Planes gated = c.planes(T, F, true);
   if (!needs_l1(d, upp, gatep)) xn.l1 = nullptr;
   if (!needs_l1(F, downp)) gated.l1 = nullptr;
+  // cleared first, so that the norm, up/gate and down kernels follow one
+  // another directly (each may start its prologue while the previous drains)
+  if (gated.l1) NSRL_TRY(cudaMemsetAsync(gated.l1, 0, T * sizeof(unsigned long long), stream), "memset");
   if (gamma)
     NSRL_TRY(launch_rms_norm(x, T, d, gamma, eps, nullptr, xn, st, stream), "rms norm");
   else  // the mini transformer without RMS norm: the block reads x itself
     NSRL_TRY(launch_split_planes(x, T, d, d, xn, stream), "split");
-  if (gated.l1) NSRL_TRY(cudaMemsetAsync(gated.l1, 0, T * sizeof(unsigned long long), stream), "memset");
   GemmArgs g{};
   g.a_hi = xn.hi;
   g.a_lo = xn.lo;

@@ -402,13 +402,7 @@ __global__ void __launch_bounds__(threads_for(A16), 1)
 
   __shared__ unsigned long long s_maxb;  // max |bias| of the fused prefix check
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (threadIdx.x == 0) {
-    *skip_flag = timed_out(p.st) ? 1u : 0u;
-    s_maxb = 0ull;
-  }
-  __syncthreads();
-  if (*skip_flag) return;  // a wait of this call already timed out: do nothing
-
+  if (threadIdx.x == 0) s_maxb = 0ull;
   if (warp == 0 && lane == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
@@ -428,10 +422,19 @@ __global__ void __launch_bounds__(threads_for(A16), 1)
     tmem_alloc(tslot, TMEM_COLS);
     tmem_relinquish();
   }
+  // The prologue above touches no global memory: from here on the previous
+  // kernel's outputs (and the status it may have flagged) are visible.
+  griddep_wait();
+  if (threadIdx.x == 0) *skip_flag = timed_out(p.st) ? 1u : 0u;
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  griddep_launch();
   const uint32_t tmem = *tslot;
+  if (*skip_flag) {  // a wait of this call already timed out: do nothing
+    if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
+    return;
+  }
   const int nkb = (p.K + BK - 1) / BK;
 
   if (warp == 0) {
@@ -1078,8 +1081,9 @@ cudaError_t launch_tc(const TcMaps& maps, const TcParams& p, int grid, cudaStrea
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  gemm_tc_kernel<EPI, WIDE, A16, SETS><<<grid, threads_for(A16), SMEM_BYTES, stream>>>(maps, p);
-  return cudaGetLastError();
+  const cudaError_t e =
+      launch_pdl(gemm_tc_kernel<EPI, WIDE, A16, SETS>, dim3(grid), dim3(threads_for(A16)), SMEM_BYTES, stream, maps, p);
+  return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 cudaError_t launch_tc_epi(Epi epi, const TcMaps& maps, const TcParams& p, int grid, cudaStream_t stream) {

@@ -104,6 +104,8 @@ __global__ void __launch_bounds__(256, VPL >= 4 ? 2 : 3) rms_norm_reg_kernel(
     long long ldp, nsrl_device_status* st) {
   constexpr int D = 256 * VPL;
   constexpr int LOG2D = VPL == 1 ? 8 : (VPL == 2 ? 9 : 10);
+  griddep_wait();  // launched as a dependent: the previous kernel's rows (and gamma) are visible from here
+  griddep_launch();
   const int lane = threadIdx.x & 31;
   const long long warp0 = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const long long nwarps = (long long)gridDim.x * (blockDim.x >> 5);
@@ -216,16 +218,12 @@ cudaError_t launch_rms_norm(const int16_t* x, size_t rows, size_t d, const int16
     const size_t rpw = d == 256 ? 2 : 1;
     const size_t groups = (rows + rpw - 1) / rpw;
     const unsigned nb = (unsigned)std::min<size_t>((groups + 7) / 8, d == 1024 ? 148 * 2 : 148 * 3);
-#define NSRL_RMS_REG(VPL)                                                                                  \
-  rms_norm_reg_kernel<VPL, (VPL == 1 ? 2 : 1)><<<nb, 256, 0, stream>>>(x, (long long)rows, gamma, eps, y_i16,   \
-                                                                        yp.hi, yp.lo, yp.l1, (long long)yp.ld, st)
-    if (d == 256)
-      NSRL_RMS_REG(1);
-    else if (d == 512)
-      NSRL_RMS_REG(2);
-    else
-      NSRL_RMS_REG(4);
+#define NSRL_RMS_REG(VPL)                                                                                    \
+  launch_pdl(rms_norm_reg_kernel<VPL, (VPL == 1 ? 2 : 1)>, dim3(nb), dim3(256), 0, stream, x, (long long)rows, gamma, \
+             (unsigned long long)eps, y_i16, yp.hi, yp.lo, yp.l1, (long long)yp.ld, st)
+    const cudaError_t e = d == 256 ? NSRL_RMS_REG(1) : d == 512 ? NSRL_RMS_REG(2) : NSRL_RMS_REG(4);
 #undef NSRL_RMS_REG
+    if (e != cudaSuccess) return e;
   } else if (vec)
     rms_norm_kernel<true><<<blocks, 256, 0, stream>>>(x, (long long)rows, (int)d, 1.0 / (double)d, gamma, eps, y_i16,
                                                       yp.hi, yp.lo, yp.l1, (long long)yp.ld, st);
