@@ -162,9 +162,6 @@ __global__ void __launch_bounds__(DTHREADS, 1) attn_bwd_dl_tc_kernel(const __gri
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   DlCtl* ctl = reinterpret_cast<DlCtl*>(sm + OFF_BAR);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (threadIdx.x == 0) s_skip = timed_out(a.st) ? 1u : 0u;
-  __syncthreads();
-  if (s_skip) return;  // a wait of this call already timed out: do nothing
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(&ctl->c_full[i], 1);
@@ -187,10 +184,19 @@ __global__ void __launch_bounds__(DTHREADS, 1) attn_bwd_dl_tc_kernel(const __gri
     tmem_alloc(&ctl->tslot, DTMEM);
     tmem_relinquish();
   }
+  // The prologue above touches no global memory: from here on the previous
+  // kernel's outputs (and the status it may have flagged) are visible.
+  griddep_wait();
+  if (threadIdx.x == 0) s_skip = timed_out(a.st) ? 1u : 0u;
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  griddep_launch();
   const uint32_t tmem = ctl->tslot;
+  if (s_skip) {  // a wait of this call already timed out: do nothing
+    if (warp == 1) tmem_dealloc(tmem, DTMEM);
+    return;
+  }
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -470,7 +476,8 @@ cudaError_t launch_attention_bwd_dl_tc(const Planes& cp, const Planes& vp, const
   const double pairs = (double)B * (double)H * (double)S * (double)(S + 1) / 2.0;
   // algorithmic: dC . V twice (2 ops per MAC); P read twice and dL written (2 bytes each per entry)
   ProfScope prof("attention_bwd_dl", s, 2.0 * 2.0 * DHD * pairs, 3.0 * 2.0 * pairs + 4.0 * (double)B * S * d);
-  attn_bwd_dl_tc_kernel<<<grid, DTHREADS, DSMEM, s>>>(m, a);
+  const cudaError_t le = launch_pdl(attn_bwd_dl_tc_kernel, dim3(grid), dim3(DTHREADS), DSMEM, s, m, a);
+  if (le != cudaSuccess) return le;
   return cudaGetLastError();
 }
 

@@ -309,6 +309,8 @@ __global__ void __launch_bounds__(KTHREADS, 1) attn_kv_tc_kernel(const __grid_co
 // eight columns per thread and step; S % 8 == 0.
 __global__ void __launch_bounds__(256) split_causal_kernel(const int16_t* __restrict__ M, long long rows, int S,
                                                            int8_t* __restrict__ hi, uint8_t* __restrict__ lo) {
+  griddep_wait();  // launched as a dependent: the previous kernel's outputs are visible from here
+  griddep_launch();
   const long long rid = (long long)blockIdx.x * 4 + threadIdx.y;  // bh * S + t
   if (rid >= rows) return;
   const int c8 = S / 8;
@@ -381,7 +383,9 @@ cudaError_t launch_split_causal(const int16_t* M, size_t BH, size_t S, int8_t* h
   const size_t rows = BH * S;
   if (S % 8 != 0 || (rows + 3) / 4 > 0x7fffffffull) return cudaErrorInvalidValue;
   ProfScope prof("attention_bwd_split", s, 0.0, 2.0 * (double)BH * S * S);
-  split_causal_kernel<<<(unsigned)((rows + 3) / 4), dim3(64, 4), 0, s>>>(M, (long long)rows, (int)S, hi, lo);
+  const cudaError_t le =
+      launch_pdl(split_causal_kernel, dim3((unsigned)((rows + 3) / 4)), dim3(64, 4), 0, s, M, (long long)rows, (int)S, hi, lo);
+  if (le != cudaSuccess) return le;
   return cudaGetLastError();
 }
 

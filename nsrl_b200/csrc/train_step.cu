@@ -131,7 +131,8 @@ cudaError_t prescale_split(const int16_t* g, size_t M, size_t N, size_t ldg, con
   const long long n = (long long)M * (long long)N;
   ProfScope prof("prescale_split", s, 0.0, 4.0 * (double)n);
   if (N % 8 == 0 && ldg == N && out.ld == N && aligned_to(g, 16) && aligned_to(out.hi, 8) && aligned_to(out.lo, 8))
-    prescale_split_vec_kernel<<<blocks_for(n / 8, 148 * 32), 256, 0, s>>>(g, n / 8, (int)N, sc, out.hi, out.lo);
+    return launch_pdl(prescale_split_vec_kernel, dim3(blocks_for(n / 8, 148 * 32)), dim3(256), 0, s, g, n / 8, (int)N,
+                      sc, out.hi, out.lo);
   else
     prescale_split_kernel<<<blocks_for(n, 148 * 32), 256, 0, s>>>(g, (long long)M, (int)N, (long long)ldg, sc,
                                                                    out.hi, out.lo, (long long)out.ld);
@@ -228,9 +229,8 @@ cudaError_t rms_backward(const int16_t* x, size_t rows, size_t d, const int16_t*
   if (d == 256 && aligned_to(x, 16) && aligned_to(w, 16) && aligned_to(go, 16) &&
       aligned_to(res ? (const void*)res : (const void*)gi, 16) && aligned_to(res ? (void*)out : (void*)gi, 16)) {
     ProfScope prof("rms_backward", s, 0.0, (res ? 8.0 : 6.0) * (double)rows * (double)d);
-    rms_backward_vec_kernel<2><<<blocks_for((long long)(rows + 1) / 2 * 32, 148 * 8), 256, 0, s>>>(
-        x, (long long)rows, w, go, eps, gi, gw, sat, st, res, out, res_sat);
-    return cudaGetLastError();
+    return launch_pdl(rms_backward_vec_kernel<2>, dim3(blocks_for((long long)(rows + 1) / 2 * 32, 148 * 8)), dim3(256),
+                      0, s, x, (long long)rows, w, go, (unsigned long long)eps, gi, gw, sat, st, res, out, res_sat);
   }
   if (res) {
     const cudaError_t e = rms_backward(x, rows, d, w, go, eps, gi, gw, sat, st, s);
@@ -268,7 +268,8 @@ cudaError_t add_sat(const int16_t* a, const int16_t* b, size_t n, int16_t* out, 
                     cudaStream_t s) {
   ProfScope prof("add_saturating", s, 0.0, 6.0 * (double)n);
   if (n % 8 == 0 && aligned_to(a, 16) && aligned_to(b, 16) && aligned_to(out, 16))
-    add_sat_vec_kernel<<<blocks_for((long long)n / 8, 148 * 32), 256, 0, s>>>(a, b, (long long)n / 8, out, sat);
+    return launch_pdl(add_sat_vec_kernel, dim3(blocks_for((long long)n / 8, 148 * 32)), dim3(256), 0, s, a, b,
+                      (long long)n / 8, out, sat);
   else
     add_sat_kernel<<<blocks_for((long long)n), 256, 0, s>>>(a, b, (long long)n, out, sat);
   return cudaGetLastError();
@@ -843,10 +844,10 @@ nsrl_status nsrl_train_windows(const nsrl_train_model* m, const uint8_t* context
     {
       const long long n = (long long)T * F;
       ProfScope prof("gated_backward", s, 0.0, 14.0 * (double)n);
-      gated_backward_vec_kernel<<<blocks_for(n / 8, 148 * 32), 256, 0, s>>>(
-          o.gg, c.up, c.gate, n / 8, (int)F, ly.lin[4].scales, ly.lin[5].scales, nullptr, nullptr, paFn.hi, paFn.lo,
-          pbF.hi, pbF.lo);
-      TS_TRY(cudaGetLastError(), "gated backward");
+      TS_TRY(launch_pdl(gated_backward_vec_kernel, dim3(blocks_for(n / 8, 148 * 32)), dim3(256), 0, s, o.gg, c.up,
+                        c.gate, n / 8, (int)F, ly.lin[4].scales, ly.lin[5].scales, (int16_t*)nullptr,
+                        (int16_t*)nullptr, paFn.hi, paFn.lo, pbF.hi, pbF.lo),
+             "gated backward");
     }
     TS_TRY(bwd_gemm(paFn, T, F, c.wt[4], d, o.ident, o.gui, d, nullptr, nullptr, st, s), "up^T");
     TS_TRY(bwd_gemm(pbF, T, F, c.wt[5], d, o.ident, o.gmi, d, o.gui, mlp_sat, st, s), "gate^T");
@@ -889,7 +890,9 @@ nsrl_status nsrl_train_windows(const nsrl_train_model* m, const uint8_t* context
       const long long n = (long long)T * d;
       ProfScope prof("fanin", s, 0.0, 8.0 * (double)n);
       if (n % 8 == 0)  // carved buffers are 256-byte aligned
-        fanin3_vec_kernel<<<blocks_for(n / 8, 148 * 32), 256, 0, s>>>(o.gq, o.gk, o.gv, n / 8, o.gni, attn_sat);
+        TS_TRY(launch_pdl(fanin3_vec_kernel, dim3(blocks_for(n / 8, 148 * 32)), dim3(256), 0, s, o.gq, o.gk, o.gv,
+                          n / 8, o.gni, attn_sat),
+               "fanin");
       else
         fanin3_kernel<<<blocks_for(n), 256, 0, s>>>(o.gq, o.gk, o.gv, n, o.gni, attn_sat);
       TS_TRY(cudaGetLastError(), "fanin");

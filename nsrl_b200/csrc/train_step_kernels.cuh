@@ -115,6 +115,8 @@ __global__ void gated_backward_vec_kernel(const int16_t* __restrict__ gg, const 
                                           int16_t* __restrict__ ggate, int8_t* __restrict__ uh,
                                           uint8_t* __restrict__ ul, int8_t* __restrict__ gh,
                                           uint8_t* __restrict__ gl) {
+  griddep_wait();  // launched as a dependent: the previous kernel's outputs are visible from here
+  griddep_launch();
   int fcur = -1, s1[8], s2[8];  // the shifts of columns fcur .. +7
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
     int g[8], u[8], ga[8], ou[8], og[8], pu[8], pg[8];
@@ -155,6 +157,8 @@ __global__ void gated_backward_vec_kernel(const int16_t* __restrict__ gg, const 
 __global__ void prescale_split_vec_kernel(const int16_t* __restrict__ g, long long n8, int N,
                                           const nsrl_fixed_scale* __restrict__ sc, int8_t* __restrict__ hi,
                                           uint8_t* __restrict__ lo) {
+  griddep_wait();  // launched as a dependent: the previous kernel's outputs are visible from here
+  griddep_launch();
   // two words in flight per thread; each slot keeps the shifts of its
   // columns cur[k] .. +7 (the same every pass when the stride is a multiple of N)
   const long long stride = (long long)gridDim.x * blockDim.x;
@@ -187,6 +191,8 @@ __global__ void prescale_split_vec_kernel(const int16_t* __restrict__ g, long lo
 // add_sat_kernel / fanin3_kernel on eight elements per thread (n % 8 == 0).
 __global__ void add_sat_vec_kernel(const int16_t* __restrict__ a, const int16_t* __restrict__ b, long long n8,
                                    int16_t* __restrict__ out, unsigned long long* sat) {
+  griddep_wait();  // launched as a dependent: the previous kernel's outputs are visible from here
+  griddep_launch();
   unsigned long long c = 0;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
     int x[8], y[8], o[8];
@@ -207,6 +213,8 @@ __global__ void add_sat_vec_kernel(const int16_t* __restrict__ a, const int16_t*
 __global__ void fanin3_vec_kernel(const int16_t* __restrict__ a, const int16_t* __restrict__ b,
                                   const int16_t* __restrict__ c3, long long n8, int16_t* __restrict__ out,
                                   unsigned long long* sat) {
+  griddep_wait();  // launched as a dependent: the previous kernel's outputs are visible from here
+  griddep_launch();
   unsigned long long cnt = 0;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
     int x[8], y[8], z[8], o[8];
@@ -634,6 +642,8 @@ __global__ void __launch_bounds__(256) rms_backward_vec_kernel(
     const int16_t* __restrict__ x, long long rows, const int16_t* __restrict__ w, const int16_t* __restrict__ go,
     unsigned long long eps, int16_t* __restrict__ gi, long long* __restrict__ gw, unsigned long long* sat,
     nsrl_device_status* st, const int16_t* __restrict__ res, int16_t* __restrict__ out, unsigned long long* res_sat) {
+  griddep_wait();  // launched as a dependent: the previous kernel's outputs are visible from here
+  griddep_launch();
   constexpr int d = 256;
   const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
   int wv[8];

@@ -85,10 +85,6 @@ __global__ void __launch_bounds__(WTHREADS, 1) wgrad_tc_kernel(const __grid_cons
   uint32_t* skip_flag = tslot + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (threadIdx.x == 0) *skip_flag = timed_out(p.st) ? 1u : 0u;
-  __syncthreads();
-  if (*skip_flag) return;
-
   if (warp == 0 && lane == 0) {
     for (int s = 0; s < WSTAGES; ++s) {
       mbar_init(&full[s], 1);
@@ -106,10 +102,19 @@ __global__ void __launch_bounds__(WTHREADS, 1) wgrad_tc_kernel(const __grid_cons
     tmem_alloc(tslot, WTMEM);
     tmem_relinquish();
   }
+  // The prologue above touches no global memory: from here on the previous
+  // kernel's outputs (and the status it may have flagged) are visible.
+  griddep_wait();
+  if (threadIdx.x == 0) *skip_flag = timed_out(p.st) ? 1u : 0u;
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  griddep_launch();
   const uint32_t tmem = *tslot;
+  if (*skip_flag) {  // a wait of this call already timed out: do nothing
+    if (warp == 1) tmem_dealloc(tmem, WTMEM);
+    return;
+  }
 
   if (warp == 0) {
     if (lane == 0) {
@@ -310,7 +315,8 @@ cudaError_t launch_wgrad_tc(const int8_t* gh, const uint8_t* gl, size_t ldg, con
   const int grid = std::min(p.items, sms);
   ProfScope prof("accumulate_weight_grad_tc", s, 2.0 * (double)T * (double)N * (double)K,
                  2.0 * (double)T * (double)(N + K) + 16.0 * (double)N * (double)K * p.chunks);
-  wgrad_tc_kernel<<<grid, WTHREADS, WSMEM, s>>>(maps, p);
+  const cudaError_t le = launch_pdl(wgrad_tc_kernel, dim3(grid), dim3(WTHREADS), WSMEM, s, maps, p);
+  if (le != cudaSuccess) return le;
   return cudaGetLastError();
 }
 
