@@ -916,6 +916,8 @@ __global__ void gemm_simt_kernel(const SimtParams s) {
 // One thread per row tests that bound; the rows outside it (rare) are queued
 // in shared memory and rescanned exactly, one warp per row.
 __global__ void __launch_bounds__(PREFIX_CHECK_THREADS) prefix_check_kernel(const CheckParams c) {
+  griddep_wait();  // launched as a dependent: the previous kernel's outputs are visible from here
+  griddep_launch();
   __shared__ long long s_maxb;
   __shared__ int s_rows[PREFIX_CHECK_THREADS];
   __shared__ unsigned long long s_l1[PREFIX_CHECK_THREADS];  // int16 rows: their L1, computed here
@@ -968,6 +970,8 @@ __global__ void __launch_bounds__(PREFIX_CHECK_THREADS) prefix_check_kernel(cons
 // ---------------------------------------------------------------------------
 __global__ void split_planes_kernel(const int16_t* x, long long rows, int K, long long ldx, int8_t* hi, uint8_t* lo,
                                     unsigned long long* l1, long long ldp) {
+  griddep_wait();  // launched as a dependent: the previous kernel's outputs are visible from here
+  griddep_launch();
   const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
   for (long long r = (long long)blockIdx.x * warps + (threadIdx.x >> 5); r < rows; r += (long long)gridDim.x * warps) {
     const int16_t* xr = x + r * ldx;
@@ -987,6 +991,8 @@ __global__ void split_planes_kernel(const int16_t* x, long long rows, int K, lon
 // Vectorised split for K % 8 == 0 and 16-byte aligned rows: 8 elements per thread-step.
 __global__ void split_planes_vec_kernel(const int16_t* x, long long rows, int K, long long ldx, int8_t* hi,
                                         uint8_t* lo, unsigned long long* l1, long long ldp) {
+  griddep_wait();  // launched as a dependent: the previous kernel's outputs are visible from here
+  griddep_launch();
   const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
   for (long long r = (long long)blockIdx.x * warps + (threadIdx.x >> 5); r < rows; r += (long long)gridDim.x * warps) {
     const uint4* xr = reinterpret_cast<const uint4*>(x + r * ldx);
@@ -1015,6 +1021,8 @@ __global__ void split_planes_vec_kernel(const int16_t* x, long long rows, int K,
 
 __global__ void join_planes_kernel(const int8_t* hi, const uint8_t* lo, long long ldp, long long rows, int cols,
                                    int16_t* y, long long ldy) {
+  griddep_wait();  // launched as a dependent: the previous kernel's outputs are visible from here
+  griddep_launch();
   const long long n = rows * cols;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     long long r = i / cols;
@@ -1267,8 +1275,8 @@ cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t stream) {
     const unsigned blocks =
         (unsigned)std::min<size_t>((a.M + PREFIX_CHECK_THREADS - 1) / PREFIX_CHECK_THREADS, 148 * 8);
     ProfScope prof("linear_prefix_check", stream, 0.0, 8.0 * Mx);
-    prefix_check_kernel<<<blocks, PREFIX_CHECK_THREADS, 0, stream>>>(c);
-    err = cudaGetLastError();
+    err = launch_pdl(prefix_check_kernel, dim3(blocks), dim3(PREFIX_CHECK_THREADS), 0, stream, c);
+    if (err == cudaSuccess) err = cudaGetLastError();
   }
   return err;
 }
@@ -1277,14 +1285,12 @@ cudaError_t launch_split_planes(const int16_t* x, size_t rows, size_t K, size_t 
   if (rows == 0 || K == 0) return cudaSuccess;
   unsigned blocks = (unsigned)std::min<size_t>((rows + 7) / 8, 148 * 16);
   ProfScope prof("split_planes", stream, 0.0, 4.0 * rows * K + 8.0 * rows);
-  if (K % 8 == 0 && ldx % 8 == 0 && out.ld % 8 == 0 && aligned16(x) && (reinterpret_cast<uintptr_t>(out.hi) & 7) == 0 &&
-      (reinterpret_cast<uintptr_t>(out.lo) & 7) == 0)
-    split_planes_vec_kernel<<<blocks, 256, 0, stream>>>(x, (long long)rows, (int)K, (long long)ldx, out.hi, out.lo,
-                                                        out.l1, (long long)out.ld);
-  else
-    split_planes_kernel<<<blocks, 256, 0, stream>>>(x, (long long)rows, (int)K, (long long)ldx, out.hi, out.lo, out.l1,
-                                                    (long long)out.ld);
-  return cudaGetLastError();
+  const bool vec = K % 8 == 0 && ldx % 8 == 0 && out.ld % 8 == 0 && aligned16(x) &&
+                   (reinterpret_cast<uintptr_t>(out.hi) & 7) == 0 && (reinterpret_cast<uintptr_t>(out.lo) & 7) == 0;
+  const cudaError_t e = launch_pdl(vec ? split_planes_vec_kernel : split_planes_kernel, dim3(blocks), dim3(256), 0,
+                                   stream, x, (long long)rows, (int)K, (long long)ldx, out.hi, out.lo, out.l1,
+                                   (long long)out.ld);
+  return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 cudaError_t launch_join_planes(Planes in, size_t rows, size_t cols, int16_t* y, size_t ldy, cudaStream_t stream) {
@@ -1292,9 +1298,9 @@ cudaError_t launch_join_planes(Planes in, size_t rows, size_t cols, int16_t* y, 
   long long n = (long long)rows * cols;
   unsigned blocks = (unsigned)std::min<long long>((n + 255) / 256, 148 * 32);
   ProfScope prof("join_planes", stream, 0.0, 4.0 * (double)n);
-  join_planes_kernel<<<blocks, 256, 0, stream>>>(in.hi, in.lo, (long long)in.ld, (long long)rows, (int)cols, y,
-                                                 (long long)ldy);
-  return cudaGetLastError();
+  const cudaError_t e = launch_pdl(join_planes_kernel, dim3(blocks), dim3(256), 0, stream, (const int8_t*)in.hi,
+                                   (const uint8_t*)in.lo, (long long)in.ld, (long long)rows, (int)cols, y, (long long)ldy);
+  return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 }  // namespace nsrl
