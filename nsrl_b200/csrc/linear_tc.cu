@@ -637,14 +637,45 @@ __global__ void __launch_bounds__(threads_for(A16), 1)
           int up[16], gt[16];
           requant16(hu, lu, su, up, p.small_acc);
           requant16(hg, lg, sg, gt, p.small_acc);
-          if (p.y && row_ok && nvalid > 0) {  // the up and gate values themselves (the training step's caches)
+          // the up and gate values themselves (the training step's caches)
+          const bool vok = ((p.ldy | fb) & 7) == 0;
+          if (p.y && nvalid == 16 && vok) {
+            // Lanes 2i and 2i+1 swap halves, then each store instruction
+            // writes whole 32-byte runs (both halves of rows 2i, then of
+            // rows 2i+1) instead of one half of 32 rows.
+            uint32_t ou[8], og[8], xu[4], xg[4];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              ou[i] = __byte_perm((uint32_t)up[2 * i], (uint32_t)up[2 * i + 1], 0x5410);
+              og[i] = __byte_perm((uint32_t)gt[2 * i], (uint32_t)gt[2 * i + 1], 0x5410);
+            }
+            const bool odd = lane & 1;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              xu[k] = __shfl_xor_sync(0xffffffffu, odd ? ou[k] : ou[4 + k], 1);
+              xg[k] = __shfl_xor_sync(0xffffffffu, odd ? og[k] : og[4 + k], 1);
+            }
+            const int re = m0 + q * 32 + (lane & ~1);  // the pair's even row
+            const long long o1 = (long long)re * p.ldy + fb + (odd ? 8 : 0), o2 = o1 + p.ldy;
+            if (re < p.M) {
+              *reinterpret_cast<uint4*>(p.y + o1) =
+                  odd ? make_uint4(xu[0], xu[1], xu[2], xu[3]) : make_uint4(ou[0], ou[1], ou[2], ou[3]);
+              *reinterpret_cast<uint4*>(p.y2 + o1) =
+                  odd ? make_uint4(xg[0], xg[1], xg[2], xg[3]) : make_uint4(og[0], og[1], og[2], og[3]);
+            }
+            if (re + 1 < p.M) {
+              *reinterpret_cast<uint4*>(p.y + o2) =
+                  odd ? make_uint4(ou[4], ou[5], ou[6], ou[7]) : make_uint4(xu[0], xu[1], xu[2], xu[3]);
+              *reinterpret_cast<uint4*>(p.y2 + o2) =
+                  odd ? make_uint4(og[4], og[5], og[6], og[7]) : make_uint4(xg[0], xg[1], xg[2], xg[3]);
+            }
+          } else if (p.y && row_ok && nvalid > 0) {
             uint32_t ou[8], og[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
               ou[i] = __byte_perm((uint32_t)up[2 * i], (uint32_t)up[2 * i + 1], 0x5410);
               og[i] = __byte_perm((uint32_t)gt[2 * i], (uint32_t)gt[2 * i + 1], 0x5410);
             }
-            const bool vok = ((p.ldy | fb) & 7) == 0;
             store16_i16(p.y + (long long)r * p.ldy + fb, ou, nvalid, vok);
             store16_i16(p.y2 + (long long)r * p.ldy + fb, og, nvalid, vok);
           }
