@@ -378,6 +378,27 @@ __device__ __forceinline__ void store16_i16(int16_t* dst, const uint32_t (&o)[8]
   }
 }
 
+// Stores 16 int16 columns (o: 8 packed words) of this lane's row r at
+// base + r * ld + col as lane pairs: partners 2i and 2i+1 swap halves, so each
+// of the two store instructions writes whole 32-byte runs (rows 2i, then rows
+// 2i+1) instead of one 16-byte half of 32 rows.  Every lane of the warp calls
+// it (the swap is a shuffle); r has the parity of the lane, rows at or past M
+// are not written, and base + col, ld are 16-byte multiples.
+__device__ __forceinline__ void store16_i16_pairs(int16_t* base, long long ld, int r, int M, int col,
+                                                  const uint32_t (&o)[8], int lane) {
+  const bool odd = lane & 1;
+  uint32_t x[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) x[k] = __shfl_xor_sync(0xffffffffu, odd ? o[k] : o[4 + k], 1);
+  const int re = r & ~1;  // the pair's even row
+  const long long o1 = (long long)re * ld + col + (odd ? 8 : 0);
+  if (re < M)
+    *reinterpret_cast<uint4*>(base + o1) = odd ? make_uint4(x[0], x[1], x[2], x[3]) : make_uint4(o[0], o[1], o[2], o[3]);
+  if (re + 1 < M)
+    *reinterpret_cast<uint4*>(base + o1 + ld) =
+        odd ? make_uint4(o[4], o[5], o[6], o[7]) : make_uint4(x[0], x[1], x[2], x[3]);
+}
+
 // WIDE (= p.wide) is a template parameter so that each kernel holds only one
 // requantisation form: a smaller epilogue for the instruction cache.
 // A16: A is int16 [M][K] in global memory.  TMA loads each 128 x 128 int16
@@ -639,36 +660,15 @@ __global__ void __launch_bounds__(threads_for(A16), 1)
           requant16(hg, lg, sg, gt, p.small_acc);
           // the up and gate values themselves (the training step's caches)
           const bool vok = ((p.ldy | fb) & 7) == 0;
-          if (p.y && nvalid == 16 && vok) {
-            // Lanes 2i and 2i+1 swap halves, then each store instruction
-            // writes whole 32-byte runs (both halves of rows 2i, then of
-            // rows 2i+1) instead of one half of 32 rows.
-            uint32_t ou[8], og[8], xu[4], xg[4];
+          if (p.y && nvalid == 16 && vok) {  // whole 32-byte runs per store (lane pairs)
+            uint32_t ou[8], og[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
               ou[i] = __byte_perm((uint32_t)up[2 * i], (uint32_t)up[2 * i + 1], 0x5410);
               og[i] = __byte_perm((uint32_t)gt[2 * i], (uint32_t)gt[2 * i + 1], 0x5410);
             }
-            const bool odd = lane & 1;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              xu[k] = __shfl_xor_sync(0xffffffffu, odd ? ou[k] : ou[4 + k], 1);
-              xg[k] = __shfl_xor_sync(0xffffffffu, odd ? og[k] : og[4 + k], 1);
-            }
-            const int re = m0 + q * 32 + (lane & ~1);  // the pair's even row
-            const long long o1 = (long long)re * p.ldy + fb + (odd ? 8 : 0), o2 = o1 + p.ldy;
-            if (re < p.M) {
-              *reinterpret_cast<uint4*>(p.y + o1) =
-                  odd ? make_uint4(xu[0], xu[1], xu[2], xu[3]) : make_uint4(ou[0], ou[1], ou[2], ou[3]);
-              *reinterpret_cast<uint4*>(p.y2 + o1) =
-                  odd ? make_uint4(xg[0], xg[1], xg[2], xg[3]) : make_uint4(og[0], og[1], og[2], og[3]);
-            }
-            if (re + 1 < p.M) {
-              *reinterpret_cast<uint4*>(p.y + o2) =
-                  odd ? make_uint4(ou[4], ou[5], ou[6], ou[7]) : make_uint4(xu[0], xu[1], xu[2], xu[3]);
-              *reinterpret_cast<uint4*>(p.y2 + o2) =
-                  odd ? make_uint4(og[4], og[5], og[6], og[7]) : make_uint4(xg[0], xg[1], xg[2], xg[3]);
-            }
+            store16_i16_pairs(p.y, p.ldy, r, p.M, fb, ou, lane);
+            store16_i16_pairs(p.y2, p.ldy, r, p.M, fb, og, lane);
           } else if (p.y && row_ok && nvalid > 0) {
             uint32_t ou[8], og[8];
 #pragma unroll
@@ -774,7 +774,13 @@ __global__ void __launch_bounds__(threads_for(A16), 1)
             } else {
               requant_cols<16>(h, l, sc, v, p.small_acc, 16 * hf);
             }
-            if (!row_ok || nv == 0) continue;
+            // int16 outputs of whole 16-column runs go out as lane pairs
+            // (every lane takes part, valid row or not).  Not in the wide
+            // form (it spills with the swap and measured slower) nor the
+            // residual one (bound by its skip-row loads; no gain).
+            const bool pairs = !WIDE && (EPI == (int)Epi::I16 || (EPI == (int)Epi::QKV_VT && p.y && !p.route.nranks)) &&
+                               nv == 16 && ((p.ldy | nh) & 7) == 0;
+            if (!pairs && (!row_ok || nv == 0)) continue;
             uint32_t o[8];
             if (EPI == (int)Epi::RESID) {
 #pragma unroll
@@ -795,9 +801,13 @@ __global__ void __launch_bounds__(threads_for(A16), 1)
                 qkv_route_store16(p, r, nh, v, o, nv);
                 continue;
               }
-              if (EPI == (int)Epi::I16 || (EPI == (int)Epi::QKV_VT && p.y))  // QKV_VT: the training step's int16 cache
-                store16_i16(p.y + (long long)r * p.ldy + nh, o, nv, ((p.ldy | nh) & 7) == 0);
-              if (EPI == (int)Epi::I16) continue;
+              if (EPI == (int)Epi::I16 || (EPI == (int)Epi::QKV_VT && p.y)) {  // QKV_VT: the training step's int16 cache
+                if (pairs)
+                  store16_i16_pairs(p.y, p.ldy, r, p.M, nh, o, lane);
+                else
+                  store16_i16(p.y + (long long)r * p.ldy + nh, o, nv, ((p.ldy | nh) & 7) == 0);
+              }
+              if (EPI == (int)Epi::I16 || !row_ok) continue;
               if (EPI == (int)Epi::QKV_VT && nh >= p.vt_col0) {
                 // v columns: byte stores into [b][h][dim][s]; the 32 lanes of the
                 // warp hold 32 consecutive positions, so each store instruction
