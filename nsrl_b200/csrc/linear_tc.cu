@@ -378,25 +378,29 @@ __device__ __forceinline__ void store16_i16(int16_t* dst, const uint32_t (&o)[8]
   }
 }
 
-// Stores 16 int16 columns (o: 8 packed words) of this lane's row r at
-// base + r * ld + col as lane pairs: partners 2i and 2i+1 swap halves, so each
-// of the two store instructions writes whole 32-byte runs (rows 2i, then rows
-// 2i+1) instead of one 16-byte half of 32 rows.  Every lane of the warp calls
-// it (the swap is a shuffle); r has the parity of the lane, rows at or past M
-// are not written, and base + col, ld are 16-byte multiples.
-__device__ __forceinline__ void store16_i16_pairs(int16_t* base, long long ld, int r, int M, int col,
-                                                  const uint32_t (&o)[8], int lane) {
+// Stores 32 bytes (o: 8 words) of this lane's row r at base + r * ld as lane
+// pairs: partners 2i and 2i+1 swap halves, so each of the two store
+// instructions writes whole 32-byte runs (rows 2i, then rows 2i+1) instead of
+// one 16-byte half of 32 rows.  Every lane of the warp calls it (the swap is a
+// shuffle); r has the parity of the lane, rows at or past M are not written,
+// and base and ld (bytes) are 16-byte multiples.
+__device__ __forceinline__ void store32b_pairs(uint8_t* base, long long ld, int r, int M, const uint32_t (&o)[8],
+                                               int lane) {
   const bool odd = lane & 1;
   uint32_t x[4];
 #pragma unroll
   for (int k = 0; k < 4; ++k) x[k] = __shfl_xor_sync(0xffffffffu, odd ? o[k] : o[4 + k], 1);
   const int re = r & ~1;  // the pair's even row
-  const long long o1 = (long long)re * ld + col + (odd ? 8 : 0);
+  uint8_t* d = base + (long long)re * ld + (odd ? 16 : 0);
   if (re < M)
-    *reinterpret_cast<uint4*>(base + o1) = odd ? make_uint4(x[0], x[1], x[2], x[3]) : make_uint4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<uint4*>(d) = odd ? make_uint4(x[0], x[1], x[2], x[3]) : make_uint4(o[0], o[1], o[2], o[3]);
   if (re + 1 < M)
-    *reinterpret_cast<uint4*>(base + o1 + ld) =
-        odd ? make_uint4(o[4], o[5], o[6], o[7]) : make_uint4(x[0], x[1], x[2], x[3]);
+    *reinterpret_cast<uint4*>(d + ld) = odd ? make_uint4(o[4], o[5], o[6], o[7]) : make_uint4(x[0], x[1], x[2], x[3]);
+}
+// 16 int16 columns (o: 8 packed words) at base + r * ld + col, as above.
+__device__ __forceinline__ void store16_i16_pairs(int16_t* base, long long ld, int r, int M, int col,
+                                                  const uint32_t (&o)[8], int lane) {
+  store32b_pairs(reinterpret_cast<uint8_t*>(base + col), 2 * ld, r, M, o, lane);
 }
 
 // WIDE (= p.wide) is a template parameter so that each kernel holds only one
@@ -751,6 +755,7 @@ __global__ void __launch_bounds__(threads_for(A16), 1)
             tc_fence_before();
             if (sub == SETS - 1 && lane == 0) mbar_arrive(&acc_empty[buf]);  // every group loaded
           }
+          uint32_t ph0[4], pl0[4];  // planes: the first half's bytes, held for the paired stores
 #pragma unroll
           for (int hf = 0; hf < 2; ++hf) {
             if (!kOnce) {
@@ -780,6 +785,37 @@ __global__ void __launch_bounds__(threads_for(A16), 1)
             // residual one (bound by its skip-row loads; no gain).
             const bool pairs = !WIDE && (EPI == (int)Epi::I16 || (EPI == (int)Epi::QKV_VT && p.y && !p.route.nranks)) &&
                                nv == 16 && ((p.ldy | nh) & 7) == 0;
+            // planes: a lane's 32 columns are one 32-byte run per plane; the
+            // first half waits in registers for the second, then both go out
+            // as lane pairs
+            const bool ppairs = !WIDE && EPI == (int)Epi::PLANES && nvalid == 32 && ((p.ldp | n) & 15) == 0;
+            if (ppairs) {
+              uint32_t hw[4], lw[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const uint32_t a = __byte_perm((uint32_t)v[4 * i], (uint32_t)v[4 * i + 1], 0x5410);
+                const uint32_t b = __byte_perm((uint32_t)v[4 * i + 2], (uint32_t)v[4 * i + 3], 0x5410);
+                hw[i] = __byte_perm(a, b, 0x7531);
+                lw[i] = __byte_perm(a, b, 0x6420);
+              }
+              if (p.yl1 && row_ok) {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) l1 += (unsigned)abs(v[i]);
+              }
+              if (hf == 0) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  ph0[i] = hw[i];
+                  pl0[i] = lw[i];
+                }
+                continue;
+              }
+              const uint32_t hi8[8] = {ph0[0], ph0[1], ph0[2], ph0[3], hw[0], hw[1], hw[2], hw[3]};
+              const uint32_t lo8[8] = {pl0[0], pl0[1], pl0[2], pl0[3], lw[0], lw[1], lw[2], lw[3]};
+              store32b_pairs(reinterpret_cast<uint8_t*>(p.yh + n), p.ldp, r, p.M, hi8, lane);
+              store32b_pairs(p.yl + n, p.ldp, r, p.M, lo8, lane);
+              continue;
+            }
             if (!pairs && (!row_ok || nv == 0)) continue;
             uint32_t o[8];
             if (EPI == (int)Epi::RESID) {
