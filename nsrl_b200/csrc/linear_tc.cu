@@ -378,25 +378,6 @@ __device__ __forceinline__ void store16_i16(int16_t* dst, const uint32_t (&o)[8]
   }
 }
 
-// Stores 32 bytes (o: 8 words) of this lane's row r at base + r * ld as lane
-// pairs: partners 2i and 2i+1 swap halves, so each of the two store
-// instructions writes whole 32-byte runs (rows 2i, then rows 2i+1) instead of
-// one 16-byte half of 32 rows.  Every lane of the warp calls it (the swap is a
-// shuffle); r has the parity of the lane, rows at or past M are not written,
-// and base and ld (bytes) are 16-byte multiples.
-__device__ __forceinline__ void store32b_pairs(uint8_t* base, long long ld, int r, int M, const uint32_t (&o)[8],
-                                               int lane) {
-  const bool odd = lane & 1;
-  uint32_t x[4];
-#pragma unroll
-  for (int k = 0; k < 4; ++k) x[k] = __shfl_xor_sync(0xffffffffu, odd ? o[k] : o[4 + k], 1);
-  const int re = r & ~1;  // the pair's even row
-  uint8_t* d = base + (long long)re * ld + (odd ? 16 : 0);
-  if (re < M)
-    *reinterpret_cast<uint4*>(d) = odd ? make_uint4(x[0], x[1], x[2], x[3]) : make_uint4(o[0], o[1], o[2], o[3]);
-  if (re + 1 < M)
-    *reinterpret_cast<uint4*>(d + ld) = odd ? make_uint4(o[4], o[5], o[6], o[7]) : make_uint4(x[0], x[1], x[2], x[3]);
-}
 // 16 int16 columns (o: 8 packed words) at base + r * ld + col, as above.
 __device__ __forceinline__ void store16_i16_pairs(int16_t* base, long long ld, int r, int M, int col,
                                                   const uint32_t (&o)[8], int lane) {
