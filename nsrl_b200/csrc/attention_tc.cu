@@ -793,6 +793,12 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
       crow = (long long)b * a.rt.s_loc + (qi - own * a.rt.s_loc);
     }
     unsigned l1 = 0;
+    // Head dim 64, unrouted: a lane's 32 dims are one 32-byte run per plane;
+    // the first 16 wait in registers for the second, then both go out as
+    // lane pairs (every lane takes part, live row or not; qi has the lane's
+    // parity).
+    const bool pairs = HDIM == 64 && !a.rt.nranks && (a.ldc & 15) == 0;
+    uint32_t h0[4], l0[4];
 #pragma unroll
     for (int c = 0; c < 2; ++c) {  // dims [32g + 16c, +16) of the head's HDIM
       uint32_t oh[16], om[16], ol[16];
@@ -802,7 +808,7 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
       tmem_ld16(trow + O_MID + col, om);
       tmem_ld16(trow + O_LL + col, ol);
       tmem_wait_ld();
-      if (row_live) {
+      if (row_live || pairs) {
         uint32_t pk[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -810,7 +816,7 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
           const int t1 = (int)(oh[2 * i + 1] * 65536u + om[2 * i + 1] * 256u + ol[2 * i + 1]);
           const int v0 = max(-32768, min(32767, (t0 + 16384) >> 15));
           const int v1 = max(-32768, min(32767, (t1 + 16384) >> 15));
-          l1 += (unsigned)(abs(v0) + abs(v1));
+          if (row_live) l1 += (unsigned)(abs(v0) + abs(v1));
           pk[i] = __byte_perm((uint32_t)v0, (uint32_t)v1, 0x5410);
         }
         uint32_t hw[4], lw[4];
@@ -818,6 +824,22 @@ __global__ void __launch_bounds__(THREADS, 1) attention_tc_kernel(const __grid_c
         for (int k = 0; k < 4; ++k) {
           hw[k] = __byte_perm(pk[2 * k], pk[2 * k + 1], 0x7531);
           lw[k] = __byte_perm(pk[2 * k], pk[2 * k + 1], 0x6420);
+        }
+        if (pairs) {
+          if (c == 0) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              h0[k] = hw[k];
+              l0[k] = lw[k];
+            }
+            continue;
+          }
+          const uint32_t hi8[8] = {h0[0], h0[1], h0[2], h0[3], hw[0], hw[1], hw[2], hw[3]};
+          const uint32_t lo8[8] = {l0[0], l0[1], l0[2], l0[3], lw[0], lw[1], lw[2], lw[3]};
+          const long long base = (long long)row0 * a.ldc + h * HDIM + 32 * g;
+          store32b_pairs(reinterpret_cast<uint8_t*>(chi + base), a.ldc, qi, S, hi8, lane);
+          store32b_pairs(clo + base, a.ldc, qi, S, lo8, lane);
+          continue;
         }
         const long long off = crow * a.ldc + a.rt.col0 + h * HDIM + col;
         *reinterpret_cast<uint4*>(chi + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
