@@ -1162,7 +1162,7 @@ cudaError_t launch_tc_epi(Epi epi, const TcMaps& maps, const TcParams& p, int gr
                     : launch_tc<(int)Epi::PLANES, false>(maps, p, grid, stream);
     case Epi::RESID:
       return p.wide ? launch_tc<(int)Epi::RESID, true>(maps, p, grid, stream)
-                    : launch_tc<(int)Epi::RESID, false>(maps, p, grid, stream);
+                    : launch_tc<(int)Epi::RESID, false, false, 2>(maps, p, grid, stream);
     case Epi::GATED:  // the wide form takes neither of these (launch_gemm rejects it)
       // without the int16 caches (inference) the gated epilogue takes two sets
       return p.y ? launch_tc<(int)Epi::GATED, false>(maps, p, grid, stream)
