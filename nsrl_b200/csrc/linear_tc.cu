@@ -1156,7 +1156,7 @@ cudaError_t launch_tc_epi(Epi epi, const TcMaps& maps, const TcParams& p, int gr
   switch (epi) {
     case Epi::I16:
       return p.wide ? launch_tc<(int)Epi::I16, true>(maps, p, grid, stream)
-                    : launch_tc<(int)Epi::I16, false>(maps, p, grid, stream);
+                    : launch_tc<(int)Epi::I16, false, false, 2>(maps, p, grid, stream);
     case Epi::PLANES:
       return p.wide ? launch_tc<(int)Epi::PLANES, true>(maps, p, grid, stream)
                     : launch_tc<(int)Epi::PLANES, false>(maps, p, grid, stream);
