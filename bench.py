@@ -938,7 +938,7 @@ def main():
                                                                  "min(N, heads))")
     ap.add_argument("--shard-batch", type=int, default=BATCH, help="--case sharded: global batch (sequences)")
     ap.add_argument("--decode-batch", type=int, default=DEC_B)
-    ap.add_argument("--train-steps", type=int, default=3, help="timed steps of the training-step measurement")
+    ap.add_argument("--train-steps", type=int, default=10, help="timed steps of the training-step measurement")
     ap.add_argument("--train-windows", type=int, default=TR_BATCH,
                     help="--case train: windows per step (the measurement uses the global batch of 256)")
     args = ap.parse_args()
@@ -1076,7 +1076,7 @@ def main():
     train_out = None
     if not args.no_extras:
         hbm, tfl, src = peaks()
-        train_out = run_train(core, torch, dist, world, rank, steps=args.train_steps, warmup=2, flush=flush, hbm=hbm,
+        train_out = run_train(core, torch, dist, world, rank, steps=args.train_steps, warmup=3, flush=flush, hbm=hbm,
                               tfl=tfl, src=src, cpu_baseline=not args.no_cpu_baseline)
     if rank == 0:
         hbm, tfl, src = peaks()
